@@ -1,0 +1,239 @@
+"""ctypes binding of libcign_sm100.so (declared in include/cign_sm100.h).
+
+The library is built in-tree by ``python -m cign_b200.build`` (or
+``__graft_entry__.build()``).  There is no CPU fallback: every op of this
+package calls into this library and raises if it cannot be loaded.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libcign_sm100.so"
+
+CIGN_OK = 0
+ERR_NAMES = {
+    1: "invalid argument",
+    2: "null pointer",
+    3: "alignment",
+    4: "kernel launch failed",
+    5: "device wait timed out",
+    6: "unsupported shape",
+    7: "CUDA runtime error",
+}
+
+_LOCK = threading.Lock()
+_LIB = None
+_LOAD_ERROR = None
+
+
+class CsrF32(ctypes.Structure):
+    """Mirror of ``cign_csr_f32``."""
+
+    _fields_ = [
+        ("rows", c_int64),
+        ("cols", c_int64),
+        ("nnz", c_int64),
+        ("crow", c_void_p),
+        ("col", c_void_p),
+        ("val", c_void_p),
+    ]
+
+
+class SpmmPlanInfo(ctypes.Structure):
+    """Mirror of ``cign_spmm_plan_info``."""
+
+    _fields_ = [
+        ("rows", c_int64),
+        ("nnz", c_int64),
+        ("heavy_rows", c_int64),
+        ("heavy_rows_t", c_int64),
+        ("max_degree", c_int32),
+        ("max_degree_t", c_int32),
+        ("heavy_threshold", c_int32),
+        ("transpose_is_forward", c_int32),
+    ]
+
+
+_P = c_void_p  # any device pointer / opaque handle
+_PP = POINTER(c_void_p)  # host array of device pointers
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "cign_version": (c_int, []),
+    "cign_last_error": (c_char_p, []),
+    "cign_spmm_plan_create": (c_int, [POINTER(CsrF32), POINTER(CsrF32), POINTER(c_void_p)]),
+    "cign_spmm_plan_destroy": (c_int, [_P]),
+    "cign_spmm_plan_get_info": (c_int, [_P, POINTER(SpmmPlanInfo)]),
+    "cign_spmm": (c_int, [_P, c_int, _P, c_int64, _P, _P, _P]),
+    "cign_multihop_fwd": (c_int, [_P, c_int, _P, c_int64, _PP, _P]),
+    "cign_multihop_bwd": (c_int, [_P, c_int, _PP, c_int64, _P, _P, _P]),
+    "cign_gat_plan_create": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, POINTER(c_void_p)]),
+    "cign_gat_plan_destroy": (c_int, [_P]),
+    "cign_gat_plan_get_info": (c_int, [_P, POINTER(c_int64)]),
+    "cign_gat_fwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, c_float, c_float, c_uint64,
+                             _P, _P, _P, _P, _P]),
+    "cign_gat_bwd_workspace_bytes": (c_size_t, [_P, c_int32, c_int32]),
+    "cign_gat_bwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, c_float, c_float,
+                             c_uint64, _P, _P, _P, _P, _P, c_size_t, _P]),
+    "cign_gat_dropout_mask": (c_int, [c_int64, c_int32, c_float, c_uint64, _P, _P]),
+    "cign_attn_logits_fwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P]),
+    "cign_attn_logits_bwd_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
+    "cign_attn_logits_bwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
+                                     c_int32, _P, c_size_t, _P]),
+    "cign_head_mean_bias_silu_fwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P]),
+    "cign_head_mean_bias_silu_bwd_workspace_bytes": (c_size_t, [c_int64, c_int32]),
+    "cign_head_mean_bias_silu_bwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P,
+                                             c_size_t, _P]),
+    "cign_pack_fwd": (c_int, [c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, _P, _P, _PP,
+                              c_int64, _P, _P, _P]),
+    "cign_pack_bwd": (c_int, [c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, _P, _P, _P,
+                              _PP, c_int64, _P, _P, _P, _PP, c_int64, c_int32, _P, _P]),
+    "cign_dropout_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_float, c_uint64,
+                                    _P, _P, _P, _P]),
+    "cign_ln_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "cign_dropout_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, c_uint64, _P,
+                                    _P, _P, _P, c_size_t, _P]),
+    "cign_add_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, c_float, _P, _P, _P, _P]),
+    "cign_add_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                c_size_t, _P]),
+    "cign_gamma_residual_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_uint64, _P, _P]),
+    "cign_gamma_residual_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "cign_gamma_residual_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_uint64, _P, _P,
+                                        _P, c_size_t, _P]),
+    "cign_block_dropout_mask": (c_int, [c_int64, c_float, c_uint64, _P, _P]),
+}
+
+
+# Kernels launched by one call of each compute entry point (for launch
+# accounting); entries taking a hop count launch one kernel per hop.
+KERNELS_PER_CALL = {
+    "cign_spmm": 1, "cign_gat_fwd": 1, "cign_gat_bwd": 4, "cign_gat_dropout_mask": 1,
+    "cign_attn_logits_fwd": 1, "cign_attn_logits_bwd": 2, "cign_head_mean_bias_silu_fwd": 1,
+    "cign_head_mean_bias_silu_bwd": 3, "cign_pack_fwd": 1, "cign_pack_bwd": 1,
+    "cign_dropout_ln_fwd": 1, "cign_dropout_ln_bwd": 2, "cign_add_ln_fwd": 1,
+    "cign_add_ln_bwd": 2, "cign_gamma_residual_fwd": 1, "cign_gamma_residual_bwd": 2,
+    "cign_block_dropout_mask": 1,
+}
+PER_HOP = {"cign_multihop_fwd", "cign_multihop_bwd"}
+
+
+class _Counting:
+    """Proxy over the ctypes handle that counts kernel launches while
+    `counting` is on (one untimed step is enough: the step is deterministic
+    in its launch sequence)."""
+
+    def __init__(self, handle):
+        self._h = handle
+        self.counting = False
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._h, name)
+        if not self.counting or not name.startswith("cign_"):
+            return fn
+        def wrapped(*args):
+            rc = fn(*args)
+            if rc == 0:
+                if name in PER_HOP:
+                    self.launches += int(args[1])
+                else:
+                    self.launches += KERNELS_PER_CALL.get(name, 0)
+            return rc
+        return wrapped
+
+
+def load_library(path: Path | str | None = None):
+    """Load (once) and return the ctypes handle; raises if the .so is absent."""
+    global _LIB, _LOAD_ERROR
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        if _LOAD_ERROR is not None:
+            raise RuntimeError("libcign_sm100.so previously failed to load") from _LOAD_ERROR
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            err = FileNotFoundError(
+                f"{p} not found; build it with `python -m cign_b200.build` "
+                "(there is no CPU fallback)"
+            )
+            _LOAD_ERROR = err
+            raise err
+        try:
+            handle = ctypes.CDLL(str(p))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+        except Exception as exc:  # pragma: no cover - depends on the box
+            _LOAD_ERROR = exc
+            raise
+        _LIB = _Counting(handle)
+        return _LIB
+
+
+def last_error() -> str:
+    msg = load_library().cign_last_error()
+    return msg.decode("utf-8", "replace") if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    if rc != CIGN_OK:
+        kind = ERR_NAMES.get(rc, f"error {rc}")
+        raise RuntimeError(f"{what} failed ({kind}): {last_error()}")
+
+
+def require_cuda(what: str) -> None:
+    if not torch.cuda.is_available():
+        raise RuntimeError(f"{what} requires CUDA.")
+
+
+def ptr(t: torch.Tensor | None) -> c_void_p:
+    return c_void_p(0 if t is None else t.data_ptr())
+
+
+def ptr_array(ts) -> "ctypes.Array":
+    arr = (c_void_p * len(ts))()
+    for i, t in enumerate(ts):
+        arr[i] = 0 if t is None else t.data_ptr()
+    return arr
+
+
+def stream_of(t: torch.Tensor) -> c_void_p:
+    return c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def stream_on(device) -> c_void_p:
+    return c_void_p(torch.cuda.current_stream(torch.device(device)).cuda_stream)
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    """Caller-owned scratch (16-byte aligned by the caching allocator)."""
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+class DeviceGuard:
+    """Makes `device` current for the duration of a call (no-op if it is)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device):
+        self.idx = torch.device(device).index
+        self.prev = None
+
+    def __enter__(self):
+        if self.idx is not None:
+            cur = torch.cuda.current_device()
+            if cur != self.idx:
+                self.prev = cur
+                torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False

@@ -1,0 +1,174 @@
+"""Collapsed multi-head GAT core (drop-in for the reference's collapsed_gat).
+
+``collapsed_gat_mean_bias_silu(attn_row, attn_col, csr, csc, perm,
+negative_slope, in_feat, bias, attn_drop)`` computes, for destination row i,
+``SiLU(mean_h sum_j w_ijh in_feat[j,h,:] + bias)`` with
+``w = dropout(softmax_j(LeakyReLU(attn_row[i,h] + attn_col[j,h])))``
+(collapsed_gat.py:164-225; kernels collapsed_gat_ext/collapsed_gat_cuda.cu).
+Gradients flow to attn_row, attn_col, in_feat and bias; graph tensors get
+None (collapsed_gat.py:148-161).
+
+The dropout stream matches the reference bit for bit: per call the seed is
+``(initial_seed & (2^63-1)) + 0x9E3779B97F4A7C15 * (call_id + 1)`` modulo 2^63
+with a module-level call counter that does not advance when attn_drop == 0
+(collapsed_gat.py:201-211), and the keep bit of (CSR edge e, head h) is the
+splitmix64 Bernoulli of index e*H + h.  The mask is recomputed in backward
+rather than stored.  Unlike the reference kernel (H=6, C=256 only,
+collapsed_gat.cpp:67-68) any 1 <= H <= 64 and C >= 1 run natively.
+"""
+from __future__ import annotations
+
+import itertools
+
+import torch
+
+from . import _lib
+from .plans import gat_plan_for
+
+_EXT = None
+_EXT_ERROR = None
+_CALL_COUNTER = itertools.count()
+_MASK63 = (1 << 63) - 1
+MAX_HEADS = 64
+
+
+def _extension_name() -> str:
+    return "cign_sm100_collapsed_gat"
+
+
+def ensure_collapsed_gat_loaded(verbose: bool = False):
+    global _EXT, _EXT_ERROR
+    if _EXT is not None:
+        return _EXT
+    if _EXT_ERROR is not None:
+        raise RuntimeError("collapsed GAT extension previously failed to load") from _EXT_ERROR
+    if not torch.cuda.is_available():
+        raise RuntimeError("A3-v6 collapsed GAT requires CUDA")
+    try:
+        _EXT = _lib.load_library()
+    except Exception as exc:
+        _EXT_ERROR = exc
+        raise
+    return _EXT
+
+
+def gat_call_seed(attn_drop: float) -> int:
+    """Seed of the next call (advances the counter only when attn_drop > 0)."""
+    base_seed = int(torch.initial_seed()) & _MASK63
+    call_id = next(_CALL_COUNTER) if float(attn_drop) > 0.0 else -1
+    return 0 if call_id < 0 else (base_seed + 0x9E3779B97F4A7C15 * (call_id + 1)) & _MASK63
+
+
+def gat_forward_raw(plan, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed):
+    """Native forward; returns (out, pre, edge_max, edge_sum)."""
+    lib = ensure_collapsed_gat_loaded()
+    n, H, C = (int(s) for s in in_feat.shape)
+    out = torch.empty((n, C), dtype=torch.float32, device=in_feat.device)
+    pre = torch.empty_like(out)
+    emax = torch.empty((n, H), dtype=torch.float32, device=in_feat.device)
+    esum = torch.empty_like(emax)
+    with _lib.DeviceGuard(in_feat.device):
+        rc = lib.cign_gat_fwd(plan.handle, H, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
+                              _lib.ptr(in_feat), _lib.ptr(bias), float(negative_slope),
+                              float(attn_drop), int(seed) & ((1 << 64) - 1), _lib.ptr(out),
+                              _lib.ptr(pre), _lib.ptr(emax), _lib.ptr(esum), _lib.stream_of(in_feat))
+    _lib.check(rc, "cign_gat_fwd")
+    return out, pre, emax, esum
+
+
+def gat_backward_raw(plan, attn_row, attn_col, in_feat, pre, emax, esum, grad_y, negative_slope,
+                     attn_drop, seed):
+    """Native backward; returns (grad_feat, grad_attn_row, grad_attn_col, grad_bias)."""
+    lib = ensure_collapsed_gat_loaded()
+    n, H, C = (int(s) for s in in_feat.shape)
+    dev = in_feat.device
+    gfeat = torch.empty_like(in_feat)
+    grow = torch.empty((n, H), dtype=torch.float32, device=dev)
+    gcol = torch.empty_like(grow)
+    gbias = torch.empty((C,), dtype=torch.float32, device=dev)
+    nbytes = int(lib.cign_gat_bwd_workspace_bytes(plan.handle, H, C))
+    ws = _lib.workspace(nbytes, dev)
+    with _lib.DeviceGuard(dev):
+        rc = lib.cign_gat_bwd(plan.handle, H, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
+                              _lib.ptr(in_feat), _lib.ptr(pre), _lib.ptr(emax), _lib.ptr(esum),
+                              _lib.ptr(grad_y), float(negative_slope), float(attn_drop),
+                              int(seed) & ((1 << 64) - 1), _lib.ptr(gfeat), _lib.ptr(grow),
+                              _lib.ptr(gcol), _lib.ptr(gbias), _lib.ptr(ws), ws.numel(),
+                              _lib.stream_of(in_feat))
+    _lib.check(rc, "cign_gat_bwd")
+    return gfeat, grow, gcol, gbias
+
+
+def gat_dropout_mask(nnz: int, heads: int, attn_drop: float, seed: int, device) -> torch.Tensor:
+    """uint8 [nnz, H] keep-mask of one call (parity checks only)."""
+    lib = ensure_collapsed_gat_loaded()
+    mask = torch.empty((int(nnz), int(heads)), dtype=torch.uint8, device=device)
+    with _lib.DeviceGuard(device):
+        rc = lib.cign_gat_dropout_mask(int(nnz), int(heads), float(attn_drop),
+                                       int(seed) & ((1 << 64) - 1), _lib.ptr(mask),
+                                       _lib.stream_on(device))
+    _lib.check(rc, "cign_gat_dropout_mask")
+    return mask
+
+
+class _CollapsedGATFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, attn_row, attn_col, rowptr, col, colptr, row, perm, negative_slope, in_feat,
+                bias, attn_drop, seed):
+        ensure_collapsed_gat_loaded(False)
+        attn_row = attn_row.contiguous()
+        attn_col = attn_col.contiguous()
+        in_feat = in_feat.contiguous()
+        bias = bias.contiguous()
+        plan = gat_plan_for(rowptr, col, row, colptr, perm)
+        n, H, C = in_feat.shape
+        if tuple(attn_row.shape) != (n, H) or tuple(attn_col.shape) != (n, H):
+            raise RuntimeError("attn_row/attn_col must be [N,H] matching in_feat")
+        if bias.dim() != 1 or bias.size(0) != C:
+            raise RuntimeError("bias must be [C]")
+        if plan.n != n:
+            raise RuntimeError(f"graph has {plan.n} rows but in_feat has {n}")
+        out, pre, emax, esum = gat_forward_raw(plan, attn_row, attn_col, in_feat, bias,
+                                               negative_slope, attn_drop, seed)
+        ctx.save_for_backward(attn_row, attn_col, in_feat, pre, emax, esum)
+        ctx.plan = plan
+        ctx.negative_slope = float(negative_slope)
+        ctx.attn_drop = float(attn_drop)
+        ctx.seed = int(seed)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        attn_row, attn_col, in_feat, pre, emax, esum = ctx.saved_tensors
+        gfeat, grow, gcol, gbias = gat_backward_raw(
+            ctx.plan, attn_row, attn_col, in_feat, pre, emax, esum,
+            grad_y.to(torch.float32).contiguous(), ctx.negative_slope, ctx.attn_drop, ctx.seed)
+        return grow, gcol, None, None, None, None, None, None, gfeat, gbias, None, None
+
+
+def collapsed_gat_mean_bias_silu(
+    attn_row: torch.Tensor,
+    attn_col: torch.Tensor,
+    csr,
+    csc,
+    perm: torch.Tensor,
+    negative_slope: float,
+    in_feat: torch.Tensor,
+    bias: torch.Tensor,
+    attn_drop: float,
+) -> torch.Tensor:
+    if in_feat.dtype != torch.float32 or in_feat.device.type != "cuda":
+        raise TypeError("A3-v6 collapsed GAT requires CUDA float32 in_feat")
+    if bias is None:
+        raise ValueError("A3-v6 collapsed GAT currently requires bias=True")
+    if in_feat.dim() != 3:
+        raise ValueError(f"in_feat must be [N,H,C], got {tuple(in_feat.shape)}")
+    H = int(in_feat.size(1))
+    if not (1 <= H <= MAX_HEADS):
+        raise ValueError(f"collapsed GAT requires 1<=H<={MAX_HEADS}; got H={H}")
+    if not (0.0 <= float(attn_drop) < 1.0):
+        raise ValueError("attn_drop must be in [0,1)")
+    (rowptr, col), (row, colptr) = csr, csc
+    seed = gat_call_seed(attn_drop)
+    return _CollapsedGATFn.apply(attn_row, attn_col, rowptr, col, colptr, row, perm,
+                                 float(negative_slope), in_feat, bias, float(attn_drop), int(seed))

@@ -1,0 +1,546 @@
+// Block side ops for any hidden width D: dropout + LayerNorm, add +
+// LayerNorm, dropout + gamma-scaled residual, forward and backward.
+//
+// Reference: fused_block_ops.py (generic kernels, 1 <= D <= 256, inline
+// CUDA :15) and fused_block_ops_ext/fused_block_ops_cuda.cu (D = 256).
+// Semantics kept: dropout keep iff (splitmix64(seed ^ idx*0xD2B74407B1CE6E93)
+// >> 11) * 2^-53 >= p with idx = n*D + d and kept values scaled by 1/(1-p);
+// LayerNorm with biased variance, y = (q - mean) * rsqrt(var + eps) * w + b.
+//
+// A group of LPR lanes owns one row and holds it in registers (D <= the
+// group's register tile), so mean and variance are two in-register passes.
+// The dropout mask is recomputed from (seed, idx) in backward, never stored.
+// Parameter gradients (LN weight/bias, gamma) are accumulated per lane in
+// registers over a fixed chunk of rows, reduced across the CTA's groups in
+// shared memory in a fixed order, then summed over chunks by a second tiny
+// kernel: deterministic, no atomics.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace cign {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxGroups = 32;  // kThreads / smallest LPR (8)
+
+template <int VEC, int VPL, int LPR>
+struct RowCfg {
+  static constexpr int kGroups = kThreads / LPR;
+  static constexpr int kTile = LPR * VPL * VEC;
+};
+
+template <int LPR>
+__device__ __forceinline__ unsigned row_group_mask() {
+  return LPR == 32 ? kFullMask
+                   : (((1u << LPR) - 1u) << ((threadIdx.x & 31) / LPR * LPR));
+}
+template <int LPR>
+__device__ __forceinline__ float gsum(float v, unsigned gmask) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(gmask, v, o, LPR);
+  return v;
+}
+
+// Rows per chunk of the parameter-gradient reductions: a multiple of 32
+// (so every group layout divides it) giving at most ~4 chunks per SM.
+int64_t rows_per_chunk(int64_t n) {
+  const int64_t target = 592;
+  int64_t r = (n + target - 1) / target;
+  r = std::max<int64_t>(r, 32);
+  return (r + 31) / 32 * 32;
+}
+int64_t num_chunks(int64_t n) { return (n + rows_per_chunk(n) - 1) / rows_per_chunk(n); }
+
+// ---------------------------------------------------------------- forward
+// MODE 0: dropout-LN (x, seed, p);  MODE 1: add-LN (a + b).
+template <int MODE, int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+ln_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ x, const float* __restrict__ x2,
+              const float* __restrict__ w, const float* __restrict__ b, float p, float eps,
+              uint64_t seed, float* __restrict__ y, float* __restrict__ mean,
+              float* __restrict__ rstd) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = RowCfg<VEC, VPL, LPR>;
+  const int lig = threadIdx.x % LPR;
+  const unsigned gmask = row_group_mask<LPR>();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + threadIdx.x / LPR;
+  if (row >= n) return;
+  const float scale = p > 0.0f ? 1.0f / (1.0f - p) : 1.0f;
+  V q[VPL];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+    vzero(q[k]);
+    if (d < D) {
+      const V xv = ld_vec<VEC>(x + row * D + d);
+      if (MODE == 0) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const bool keep = block_keep(seed, static_cast<uint64_t>(row * D + d + j), p);
+          vel(q[k], j) = keep ? vel(xv, j) * scale : 0.0f;
+        }
+      } else {
+        const V x2v = ld_vec<VEC>(x2 + row * D + d);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) vel(q[k], j) = vel(xv, j) + vel(x2v, j);
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) s += vel(q[k], j);
+    }
+  }
+  const float mu = gsum<LPR>(s, gmask) / static_cast<float>(D);
+  float v = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+    if (d < D) {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float cdev = vel(q[k], j) - mu;
+        v += cdev * cdev;
+      }
+    }
+  }
+  const float rs = rsqrtf(gsum<LPR>(v, gmask) / static_cast<float>(D) + eps);
+  if (lig == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+    if (d < D) {
+      const V wv = ldg_vec<VEC>(w + d);
+      const V bv = ldg_vec<VEC>(b + d);
+      V o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) vel(o, j) = (vel(q[k], j) - mu) * rs * vel(wv, j) + vel(bv, j);
+      st_vec(y + row * D + d, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- backward
+// grad wrt the normalised input (dq) plus per-chunk partials of
+// sum(gy * xhat) and sum(gy) for the LN weight and bias.
+template <int MODE, int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
+              const float* __restrict__ x, const float* __restrict__ x2,
+              const float* __restrict__ w, const float* __restrict__ mean,
+              const float* __restrict__ rstd, float p, uint64_t seed,
+              float* __restrict__ gx, float* __restrict__ pw, float* __restrict__ pb) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = RowCfg<VEC, VPL, LPR>;
+  __shared__ float red[kThreads * VPL * VEC];  // per thread: VPL*VEC partials
+  const int lig = threadIdx.x % LPR;
+  const int group = threadIdx.x / LPR;
+  const unsigned gmask = row_group_mask<LPR>();
+  const float scale = p > 0.0f ? 1.0f / (1.0f - p) : 1.0f;
+  const float Df = static_cast<float>(D);
+  V aw[VPL], ab[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    vzero(aw[k]);
+    vzero(ab[k]);
+  }
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
+  const int64_t r1 = (r0 + rpc < n) ? (r0 + rpc) : n;
+  for (int64_t row = r0 + group; row < r1; row += Cfg::kGroups) {
+    const float mu = mean[row], rs = rstd[row];
+    V xh[VPL], dn[VPL];
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+      vzero(xh[k]);
+      vzero(dn[k]);
+      if (d < D) {
+        const V xv = ld_vec<VEC>(x + row * D + d);
+        const V gv = ld_vec<VEC>(gy + row * D + d);
+        const V wv = ldg_vec<VEC>(w + d);
+        V x2v;
+        if (MODE == 1) x2v = ld_vec<VEC>(x2 + row * D + d);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          float qv;
+          if (MODE == 0) {
+            const bool keep = block_keep(seed, static_cast<uint64_t>(row * D + d + j), p);
+            qv = keep ? vel(xv, j) * scale : 0.0f;
+          } else {
+            qv = vel(xv, j) + vel(x2v, j);
+          }
+          const float xhat = (qv - mu) * rs;
+          const float dnorm = vel(gv, j) * vel(wv, j);
+          vel(xh[k], j) = xhat;
+          vel(dn[k], j) = dnorm;
+          s1 += dnorm;
+          s2 += dnorm * xhat;
+          vel(aw[k], j) += vel(gv, j) * xhat;
+          vel(ab[k], j) += vel(gv, j);
+        }
+      }
+    }
+    s1 = gsum<LPR>(s1, gmask);
+    s2 = gsum<LPR>(s2, gmask);
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+      if (d < D) {
+        V o;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float dq = (rs / Df) * (Df * vel(dn[k], j) - s1 - vel(xh[k], j) * s2);
+          if (MODE == 0) {
+            const bool keep = block_keep(seed, static_cast<uint64_t>(row * D + d + j), p);
+            vel(o, j) = keep ? dq * scale : 0.0f;
+          } else {
+            vel(o, j) = dq;
+          }
+        }
+        st_vec(gx + row * D + d, o);
+      }
+    }
+  }
+  // Reduce the groups' column partials in a fixed order.
+  for (int pass = 0; pass < 2; ++pass) {
+    V(&acc)[VPL] = pass == 0 ? aw : ab;
+    float* out = pass == 0 ? pw : pb;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < VPL; ++k)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) red[(group * Cfg::kTile) + (lig + k * LPR) * VEC + j] = vel(acc[k], j);
+    __syncthreads();
+    for (int64_t d = threadIdx.x; d < D && d < Cfg::kTile; d += kThreads) {
+      float t = 0.0f;
+      for (int g = 0; g < Cfg::kGroups; ++g) t += red[g * Cfg::kTile + d];
+      out[static_cast<int64_t>(blockIdx.x) * D + d] = t;
+    }
+  }
+}
+
+__global__ void param_stage2_kernel(const float* __restrict__ pw, const float* __restrict__ pb,
+                                    int64_t chunks, int64_t D, float* __restrict__ gw,
+                                    float* __restrict__ gb) {
+  const int64_t d = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (d >= D) return;
+  float sw = 0.0f, sb = 0.0f;
+  for (int64_t k = 0; k < chunks; ++k) {
+    sw += pw[k * D + d];
+    if (pb != nullptr) sb += pb[k * D + d];
+  }
+  gw[d] = sw;
+  if (gb != nullptr) gb[d] = sb;
+}
+
+// y = h + gamma * dropout(g)
+template <int VEC>
+__global__ void gamma_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ h,
+                                 const float* __restrict__ g, const float* __restrict__ gamma,
+                                 float p, uint64_t seed, float* __restrict__ y) {
+  using V = typename VecT<VEC>::type;
+  const int64_t total = n * D / VEC;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const float scale = p > 0.0f ? 1.0f / (1.0f - p) : 1.0f;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const int64_t e = i * VEC;
+    const int64_t d = e % D;
+    const V hv = ld_vec<VEC>(h + e);
+    const V gv = ld_vec<VEC>(g + e);
+    const V gm = ldg_vec<VEC>(gamma + d);
+    V o;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const bool keep = block_keep(seed, static_cast<uint64_t>(e + j), p);
+      const float gd = keep ? vel(gv, j) * scale : 0.0f;
+      vel(o, j) = vel(hv, j) + vel(gm, j) * gd;
+    }
+    st_vec(y + e, o);
+  }
+}
+
+// grad_g = gy * gamma * m;  partial[chunk, d] = sum gy * g * m  (m = keep ? scale : 0)
+template <int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+gamma_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
+                 const float* __restrict__ g, const float* __restrict__ gamma, float p,
+                 uint64_t seed, float* __restrict__ gg, float* __restrict__ partial) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = RowCfg<VEC, VPL, LPR>;
+  __shared__ float red[kThreads * VPL * VEC];
+  const int lig = threadIdx.x % LPR;
+  const int group = threadIdx.x / LPR;
+  const float scale = p > 0.0f ? 1.0f / (1.0f - p) : 1.0f;
+  V acc[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) vzero(acc[k]);
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
+  const int64_t r1 = (r0 + rpc < n) ? (r0 + rpc) : n;
+  for (int64_t row = r0 + group; row < r1; row += Cfg::kGroups) {
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+      if (d < D) {
+        const V gyv = ld_vec<VEC>(gy + row * D + d);
+        const V gv = ld_vec<VEC>(g + row * D + d);
+        const V gm = ldg_vec<VEC>(gamma + d);
+        V o;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const bool keep = block_keep(seed, static_cast<uint64_t>(row * D + d + j), p);
+          const float m = keep ? scale : 0.0f;
+          vel(o, j) = vel(gyv, j) * vel(gm, j) * m;
+          vel(acc[k], j) += vel(gyv, j) * vel(gv, j) * m;
+        }
+        st_vec(gg + row * D + d, o);
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < VPL; ++k)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) red[(group * Cfg::kTile) + (lig + k * LPR) * VEC + j] = vel(acc[k], j);
+  __syncthreads();
+  for (int64_t d = threadIdx.x; d < D && d < Cfg::kTile; d += kThreads) {
+    float t = 0.0f;
+    for (int gi = 0; gi < Cfg::kGroups; ++gi) t += red[gi * Cfg::kTile + d];
+    partial[static_cast<int64_t>(blockIdx.x) * D + d] = t;
+  }
+}
+
+__global__ void block_mask_kernel(int64_t count, float p, uint64_t seed,
+                                  uint8_t* __restrict__ mask) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride)
+    mask[i] = block_keep(seed, static_cast<uint64_t>(i), p) ? 1 : 0;
+}
+
+// D must fit one group's register tile: D <= 1024 with float4, <= 256 scalar.
+#define CIGN_ROW_DISPATCH(VEC_, FV_, CALL)                                    \
+  do {                                                                        \
+    if ((FV_) <= 8) { constexpr int V_ = VEC_, P_ = 1, L_ = 8; CALL; }        \
+    else if ((FV_) <= 16) { constexpr int V_ = VEC_, P_ = 1, L_ = 16; CALL; } \
+    else if ((FV_) <= 32) { constexpr int V_ = VEC_, P_ = 1, L_ = 32; CALL; } \
+    else if ((FV_) <= 64) { constexpr int V_ = VEC_, P_ = 2, L_ = 32; CALL; } \
+    else if ((FV_) <= 128) { constexpr int V_ = VEC_, P_ = 4, L_ = 32; CALL; }\
+    else { constexpr int V_ = VEC_, P_ = 8, L_ = 32; CALL; }                  \
+  } while (0)
+
+int check_rows(int64_t n, int64_t D, bool v4, const char* name) {
+  CIGN_REQUIRE(n >= 0 && D >= 1, CIGN_ERR_INVALID_ARGUMENT, "%s: bad sizes", name);
+  CIGN_REQUIRE(D <= (v4 ? 1024 : 256), CIGN_ERR_UNSUPPORTED,
+               "%s: D=%lld exceeds the register-resident row limit (1024 for D%%4==0 with "
+               "16-byte aligned tensors, else 256)", name, (long long)D);
+  CIGN_REQUIRE(n < (1ll << 40), CIGN_ERR_UNSUPPORTED, "%s: too many rows", name);
+  return CIGN_OK;
+}
+
+template <int MODE, int VEC, int VPL, int LPR>
+int launch_ln_fwd(int64_t n, int64_t D, const float* x, const float* x2, const float* w,
+                  const float* b, float p, float eps, uint64_t seed, float* y, float* mean,
+                  float* rstd, cudaStream_t s) {
+  using Cfg = RowCfg<VEC, VPL, LPR>;
+  const int64_t grid = (n + Cfg::kGroups - 1) / Cfg::kGroups;
+  ln_fwd_kernel<MODE, VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      n, D, x, x2, w, b, p, eps, seed, y, mean, rstd);
+  CIGN_CHECK_LAUNCH("ln_fwd_kernel");
+  return CIGN_OK;
+}
+
+template <int MODE, int VEC, int VPL, int LPR>
+int launch_ln_bwd(int64_t n, int64_t D, const float* gy, const float* x, const float* x2,
+                  const float* w, const float* mean, const float* rstd, float p, uint64_t seed,
+                  float* gx, float* gw, float* gb, float* ws, cudaStream_t s) {
+  const int64_t rpc = rows_per_chunk(n);
+  const int64_t chunks = num_chunks(n);
+  float* pw = ws;
+  float* pb = ws + chunks * D;
+  ln_bwd_kernel<MODE, VEC, VPL, LPR><<<static_cast<unsigned>(chunks), kThreads, 0, s>>>(
+      n, D, rpc, gy, x, x2, w, mean, rstd, p, seed, gx, pw, pb);
+  CIGN_CHECK_LAUNCH("ln_bwd_kernel");
+  param_stage2_kernel<<<static_cast<unsigned>((D + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+      pw, pb, chunks, D, gw, gb);
+  CIGN_CHECK_LAUNCH("param_stage2_kernel");
+  return CIGN_OK;
+}
+
+template <int VEC, int VPL, int LPR>
+int launch_gamma_bwd(int64_t n, int64_t D, const float* gy, const float* g, const float* gamma,
+                     float p, uint64_t seed, float* gg, float* ggamma, float* ws,
+                     cudaStream_t s) {
+  const int64_t rpc = rows_per_chunk(n);
+  const int64_t chunks = num_chunks(n);
+  gamma_bwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(chunks), kThreads, 0, s>>>(
+      n, D, rpc, gy, g, gamma, p, seed, gg, ws);
+  CIGN_CHECK_LAUNCH("gamma_bwd_kernel");
+  param_stage2_kernel<<<static_cast<unsigned>((D + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+      ws, nullptr, chunks, D, ggamma, nullptr);
+  CIGN_CHECK_LAUNCH("param_stage2_kernel");
+  return CIGN_OK;
+}
+
+}  // namespace
+}  // namespace cign
+
+using namespace cign;
+
+extern "C" {
+
+int cign_dropout_ln_fwd(int64_t n, int64_t d, const float* x, const float* w, const float* b,
+                        float p, float eps, uint64_t seed, float* y, float* mean, float* rstd,
+                        cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y);
+  int rc = check_rows(n, d, v4, "dropout_ln_fwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(p >= 0.0f && p < 1.0f, CIGN_ERR_INVALID_ARGUMENT, "dropout_ln_fwd: p in [0,1)");
+  if (n == 0) return CIGN_OK;
+  CIGN_REQUIRE(x && w && b && y && mean && rstd, CIGN_ERR_NULL_POINTER, "dropout_ln_fwd: NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_ln_fwd<0, V_, P_, L_>(n, d, x, nullptr, w, b, p, eps, seed, y, mean, rstd, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_ln_fwd<0, V_, P_, L_>(n, d, x, nullptr, w, b, p, eps, seed, y, mean, rstd, s)));
+  return CIGN_OK;
+}
+
+size_t cign_ln_bwd_workspace_bytes(int64_t n, int64_t d) {
+  if (n <= 0) return 0;
+  return static_cast<size_t>(num_chunks(n)) * d * 2 * sizeof(float);
+}
+
+int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* x,
+                        const float* w, const float* mean, const float* rstd, float p,
+                        uint64_t seed, float* grad_x, float* grad_w, float* grad_b, void* ws,
+                        size_t ws_bytes, cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(grad_y) &&
+                  aligned16(grad_x);
+  int rc = check_rows(n, d, v4, "dropout_ln_bwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(grad_w && grad_b, CIGN_ERR_NULL_POINTER, "dropout_ln_bwd: NULL param grad");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_w, 0, d * sizeof(float), s), "memset");
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_b, 0, d * sizeof(float), s), "memset");
+    return CIGN_OK;
+  }
+  CIGN_REQUIRE(grad_y && x && w && mean && rstd && grad_x, CIGN_ERR_NULL_POINTER,
+               "dropout_ln_bwd: NULL");
+  CIGN_REQUIRE(ws && ws_bytes >= cign_ln_bwd_workspace_bytes(n, d), CIGN_ERR_INVALID_ARGUMENT,
+               "dropout_ln_bwd: workspace too small");
+  float* wsf = static_cast<float*>(ws);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s)));
+  return CIGN_OK;
+}
+
+int cign_add_ln_fwd(int64_t n, int64_t d, const float* a, const float* b, const float* w,
+                    const float* bias, float eps, float* y, float* mean, float* rstd,
+                    cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(w) &&
+                  aligned16(bias) && aligned16(y);
+  int rc = check_rows(n, d, v4, "add_ln_fwd");
+  if (rc) return rc;
+  if (n == 0) return CIGN_OK;
+  CIGN_REQUIRE(a && b && w && bias && y && mean && rstd, CIGN_ERR_NULL_POINTER, "add_ln_fwd: NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_ln_fwd<1, V_, P_, L_>(n, d, a, b, w, bias, 0.0f, eps, 0, y, mean, rstd, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_ln_fwd<1, V_, P_, L_>(n, d, a, b, w, bias, 0.0f, eps, 0, y, mean, rstd, s)));
+  return CIGN_OK;
+}
+
+int cign_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* a, const float* b,
+                    const float* w, const float* mean, const float* rstd, float* grad_z,
+                    float* grad_w, float* grad_b, void* ws, size_t ws_bytes,
+                    cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(w) &&
+                  aligned16(grad_y) && aligned16(grad_z);
+  int rc = check_rows(n, d, v4, "add_ln_bwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(grad_w && grad_b, CIGN_ERR_NULL_POINTER, "add_ln_bwd: NULL param grad");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_w, 0, d * sizeof(float), s), "memset");
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_b, 0, d * sizeof(float), s), "memset");
+    return CIGN_OK;
+  }
+  CIGN_REQUIRE(grad_y && a && b && w && mean && rstd && grad_z, CIGN_ERR_NULL_POINTER,
+               "add_ln_bwd: NULL");
+  CIGN_REQUIRE(ws && ws_bytes >= cign_ln_bwd_workspace_bytes(n, d), CIGN_ERR_INVALID_ARGUMENT,
+               "add_ln_bwd: workspace too small");
+  float* wsf = static_cast<float*>(ws);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_ln_bwd<1, V_, P_, L_>(n, d, grad_y, a, b, w, mean, rstd, 0.0f, 0, grad_z, grad_w, grad_b, wsf, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_ln_bwd<1, V_, P_, L_>(n, d, grad_y, a, b, w, mean, rstd, 0.0f, 0, grad_z, grad_w, grad_b, wsf, s)));
+  return CIGN_OK;
+}
+
+int cign_gamma_residual_fwd(int64_t n, int64_t d, const float* h, const float* g,
+                            const float* gamma, float p, uint64_t seed, float* y,
+                            cign_stream_t stream) {
+  CIGN_REQUIRE(n >= 0 && d >= 1, CIGN_ERR_INVALID_ARGUMENT, "gamma_residual_fwd: bad sizes");
+  CIGN_REQUIRE(p >= 0.0f && p < 1.0f, CIGN_ERR_INVALID_ARGUMENT, "gamma_residual_fwd: p in [0,1)");
+  if (n == 0) return CIGN_OK;
+  CIGN_REQUIRE(h && g && gamma && y, CIGN_ERR_NULL_POINTER, "gamma_residual_fwd: NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool v4 = d % 4 == 0 && aligned16(h) && aligned16(g) && aligned16(gamma) && aligned16(y);
+  const int64_t total = n * d / (v4 ? 4 : 1);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + kThreads - 1) / kThreads, 148ll * 16)));
+  if (v4) gamma_fwd_kernel<4><<<grid, kThreads, 0, s>>>(n, d, h, g, gamma, p, seed, y);
+  else gamma_fwd_kernel<1><<<grid, kThreads, 0, s>>>(n, d, h, g, gamma, p, seed, y);
+  CIGN_CHECK_LAUNCH("gamma_fwd_kernel");
+  return CIGN_OK;
+}
+
+size_t cign_gamma_residual_bwd_workspace_bytes(int64_t n, int64_t d) {
+  if (n <= 0) return 0;
+  return static_cast<size_t>(num_chunks(n)) * d * sizeof(float);
+}
+
+int cign_gamma_residual_bwd(int64_t n, int64_t d, const float* grad_y, const float* g,
+                            const float* gamma, float p, uint64_t seed, float* grad_g,
+                            float* grad_gamma, void* ws, size_t ws_bytes,
+                            cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(grad_y) && aligned16(g) && aligned16(gamma) &&
+                  aligned16(grad_g);
+  int rc = check_rows(n, d, v4, "gamma_residual_bwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(grad_gamma != nullptr, CIGN_ERR_NULL_POINTER, "gamma_residual_bwd: NULL grad_gamma");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_gamma, 0, d * sizeof(float), s), "memset");
+    return CIGN_OK;
+  }
+  CIGN_REQUIRE(grad_y && g && gamma && grad_g, CIGN_ERR_NULL_POINTER, "gamma_residual_bwd: NULL");
+  CIGN_REQUIRE(ws && ws_bytes >= cign_gamma_residual_bwd_workspace_bytes(n, d),
+               CIGN_ERR_INVALID_ARGUMENT, "gamma_residual_bwd: workspace too small");
+  float* wsf = static_cast<float*>(ws);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_gamma_bwd<V_, P_, L_>(n, d, grad_y, g, gamma, p, seed, grad_g, grad_gamma, wsf, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_gamma_bwd<V_, P_, L_>(n, d, grad_y, g, gamma, p, seed, grad_g, grad_gamma, wsf, s)));
+  return CIGN_OK;
+}
+
+int cign_block_dropout_mask(int64_t count, float p, uint64_t seed, uint8_t* mask,
+                            cign_stream_t stream) {
+  CIGN_REQUIRE(count >= 0, CIGN_ERR_INVALID_ARGUMENT, "block_dropout_mask: bad count");
+  if (count == 0) return CIGN_OK;
+  CIGN_REQUIRE(mask != nullptr, CIGN_ERR_NULL_POINTER, "block_dropout_mask: NULL mask");
+  const int grid = static_cast<int>(std::min<int64_t>((count + 255) / 256, 65535));
+  block_mask_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(count, p, seed, mask);
+  CIGN_CHECK_LAUNCH("block_mask_kernel");
+  return CIGN_OK;
+}
+
+}  // extern "C"

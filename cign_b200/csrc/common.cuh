@@ -1,0 +1,179 @@
+// Shared device/host helpers for the CIGN sm_100a kernels.
+//
+// Every entry point of libcign_sm100.so validates its arguments on the host,
+// launches on the caller's stream and returns an int status (0 = ok).  The
+// message for the last failure on the calling thread is kept in a
+// thread-local string readable through cign_last_error().
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+
+#include "../../include/cign_sm100.h"
+
+namespace cign {
+
+// ---------------------------------------------------------------- errors
+int set_error(int code, const char* fmt, ...);
+void clear_error();
+
+#define CIGN_REQUIRE(cond, code, ...)                                  \
+  do {                                                                  \
+    if (!(cond)) return ::cign::set_error((code), __VA_ARGS__);        \
+  } while (0)
+
+#define CIGN_CHECK_LAUNCH(what)                                               \
+  do {                                                                        \
+    cudaError_t _e = cudaGetLastError();                                      \
+    if (_e != cudaSuccess)                                                    \
+      return ::cign::set_error(CIGN_ERR_LAUNCH, "%s: %s", (what),             \
+                               cudaGetErrorString(_e));                       \
+  } while (0)
+
+#define CIGN_CHECK_CUDA(call, what)                                           \
+  do {                                                                        \
+    cudaError_t _e = (call);                                                  \
+    if (_e != cudaSuccess)                                                    \
+      return ::cign::set_error(CIGN_ERR_CUDA, "%s: %s", (what),               \
+                               cudaGetErrorString(_e));                       \
+  } while (0)
+
+inline bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Number of SMs of the current device (cached per device id).
+int sm_count();
+
+// Reads a device row-pointer array (int32 [rows+1]) to the host and returns
+// a device array (cudaMalloc'd; caller frees) of the rows whose length
+// exceeds `threshold`, sorted by length descending.  Used at plan time only.
+int build_heavy_list(const int32_t* ptr_dev, int64_t rows, int threshold,
+                     int32_t** heavy_out, int64_t* n_out,
+                     int32_t* max_len_out);
+
+// Deterministic two-stage column sums of a row-major [n, c] matrix
+// (reduce.cu).  `partial` holds colsum_chunks(n) * c floats.
+int64_t colsum_chunks(int64_t n);
+int colsum_f32(const float* a, int64_t n, int64_t c, float* partial,
+               float* out, cudaStream_t s);
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// ---------------------------------------------------------------- math
+// SiLU and its derivative written from their definitions:
+//   silu(x) = x * sigmoid(x),  silu'(x) = s * (1 + x * (1 - s)).
+__device__ __forceinline__ float sigmoid_f(float x) {
+  return 1.0f / (1.0f + expf(-x));
+}
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
+__device__ __forceinline__ float silu_grad_f(float x) {
+  const float s = sigmoid_f(x);
+  return s * (1.0f + x * (1.0f - s));
+}
+__device__ __forceinline__ float leaky_f(float x, float slope) {
+  return x > 0.0f ? x : x * slope;
+}
+
+// ---------------------------------------------------------------- RNG
+// splitmix64 finaliser (Steele, Lea, Flood 2014) -- the counter-based hash
+// both dropout streams of the reference use.  idx is hashed as
+// seed ^ (idx * 0xD2B74407B1CE6E93).
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+__host__ __device__ __forceinline__ uint64_t dropout_hash(uint64_t seed,
+                                                          uint64_t idx) {
+  return splitmix64(seed ^ (idx * 0xD2B74407B1CE6E93ull));
+}
+// GAT attention dropout (24-bit-free float uniform from the high 32 bits):
+// keep iff ((r >> 32) + 0.5) * 2^-32 > p.   (collapsed_gat_cuda.cu:42-45)
+__host__ __device__ __forceinline__ bool gat_keep(uint64_t seed, uint64_t idx,
+                                                  float p) {
+  const uint32_t hi = static_cast<uint32_t>(dropout_hash(seed, idx) >> 32);
+  const float u = (static_cast<float>(hi) + 0.5f) * 2.3283064365386963e-10f;
+  return u > p;
+}
+// Block-op dropout (53-bit double uniform): keep iff (r >> 11) * 2^-53 >= p.
+// (fused_block_ops.py:15, dropout_keep)
+__host__ __device__ __forceinline__ bool block_keep(uint64_t seed, uint64_t idx,
+                                                    float p) {
+  if (p <= 0.0f) return true;
+  const uint64_t r = dropout_hash(seed, idx);
+  const double u = static_cast<double>(r >> 11) * (1.0 / 9007199254740992.0);
+  return u >= static_cast<double>(p);
+}
+
+// ---------------------------------------------------------------- warp
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFullMask, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------- vectors
+template <int VEC> struct VecT;
+template <> struct VecT<1> { using type = float; };
+template <> struct VecT<4> { using type = float4; };
+
+template <int VEC>
+__device__ __forceinline__ typename VecT<VEC>::type ldg_vec(const float* p);
+template <>
+__device__ __forceinline__ float ldg_vec<1>(const float* p) { return __ldg(p); }
+template <>
+__device__ __forceinline__ float4 ldg_vec<4>(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+
+template <int VEC>
+__device__ __forceinline__ typename VecT<VEC>::type ld_vec(const float* p);
+template <>
+__device__ __forceinline__ float ld_vec<1>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float4 ld_vec<4>(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
+__device__ __forceinline__ void st_vec(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st_vec(float* p, float4 v) {
+  *reinterpret_cast<float4*>(p) = v;
+}
+
+// Element access on a vector held in registers.
+__device__ __forceinline__ float& vel(float& v, int) { return v; }
+__device__ __forceinline__ float& vel(float4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ float vel(const float& v, int) { return v; }
+__device__ __forceinline__ float vel(const float4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+__device__ __forceinline__ void vzero(float& v) { v = 0.0f; }
+__device__ __forceinline__ void vzero(float4& v) { v = make_float4(0.f, 0.f, 0.f, 0.f); }
+
+// acc += a * x
+__device__ __forceinline__ void vfma(float& acc, float a, float x) {
+  acc = fmaf(a, x, acc);
+}
+__device__ __forceinline__ void vfma(float4& acc, float a, const float4& x) {
+  acc.x = fmaf(a, x.x, acc.x);
+  acc.y = fmaf(a, x.y, acc.y);
+  acc.z = fmaf(a, x.z, acc.z);
+  acc.w = fmaf(a, x.w, acc.w);
+}
+__device__ __forceinline__ void vadd(float& acc, float x) { acc += x; }
+__device__ __forceinline__ void vadd(float4& acc, const float4& x) {
+  acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+}
+
+}  // namespace cign

@@ -1,0 +1,377 @@
+// Clifford interaction pack family (old/new interaction, tanh/none outer,
+// old/new alpha weighting, any hop count K <= 32), forward and backward.
+//
+// Reference kernels: fused_clifford_pack_ext/fused_clifford_pack_cuda.cu
+// (K=3 old interaction, :22-152), the generic-K inline kernels
+// (fused_clifford_pack.py:88-117; generic_engine/fused_clifford_cign_generic.py
+// :58-87) and the switch/CIGN packs (generic_engine/
+// fused_clifford_switch_pack_ext/fused_clifford_switch_pack_cuda.cu:22-368,
+// whose CIGN copy drops the tanh).
+//
+// One group of LPR lanes owns one node row; each lane keeps its slice of
+// H_norm/C_norm (and of the gradients) in registers while it walks the K
+// hops, so the backward needs no atomics: grad_H/grad_C are summed over k
+// in registers and grad_alpha[n,k] is one group reduction per hop.  The K
+// propagated tensors are read through a pointer list, so the caller's
+// per-hop outputs need no torch.stack copy.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace cign {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxK = 32;
+
+struct CPtrs { const float* p[kMaxK]; };
+struct MPtrs { float* p[kMaxK]; };
+
+template <int VEC, int VPL, int LPR>
+struct PackCfg {
+  static constexpr int kGroups = kThreads / LPR;
+  static constexpr int kTile = LPR * VPL * VEC;
+};
+
+template <int LPR>
+__device__ __forceinline__ unsigned pack_group_mask() {
+  return LPR == 32 ? kFullMask
+                   : (((1u << LPR) - 1u) << ((threadIdx.x & 31) / LPR * LPR));
+}
+
+// D/W of one channel and their partial derivatives w.r.t. b_hr and b_rh
+// (the reference's compute_dw, switch pack cu:22-58, plus the "old"
+// interaction of fused_clifford_pack_cuda.cu:40-46).
+struct DW {
+  float D, W, dD_hr, dD_rh, dW_hr, dW_rh;
+};
+__device__ __forceinline__ DW interact(float bhr, float brh, int interaction, int outer) {
+  DW r;
+  if (interaction == 0) {
+    r.D = silu_f(bhr);
+    r.W = bhr - brh;
+    r.dD_hr = silu_grad_f(bhr);
+    r.dD_rh = 0.0f;
+    r.dW_hr = 1.0f;
+    r.dW_rh = -1.0f;
+  } else {
+    const float sym = 0.5f * (bhr + brh);
+    const float anti = 0.5f * (bhr - brh);
+    r.D = silu_f(sym);
+    const float sd = 0.5f * silu_grad_f(sym);
+    r.dD_hr = sd;
+    r.dD_rh = sd;
+    float dw;
+    if (outer == 1) {
+      r.W = tanhf(anti);
+      dw = 1.0f - r.W * r.W;
+    } else {
+      r.W = anti;
+      dw = 1.0f;
+    }
+    r.dW_hr = 0.5f * dw;
+    r.dW_rh = -0.5f * dw;
+  }
+  return r;
+}
+// Forward-only variant (no derivatives).
+__device__ __forceinline__ void interact_fwd(float bhr, float brh, int interaction, int outer,
+                                             float& D, float& W) {
+  if (interaction == 0) {
+    D = silu_f(bhr);
+    W = bhr - brh;
+  } else {
+    D = silu_f(0.5f * (bhr + brh));
+    const float anti = 0.5f * (bhr - brh);
+    W = outer == 1 ? tanhf(anti) : anti;
+  }
+}
+
+template <int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+pack_fwd_kernel(int64_t n, int64_t D, int K, int interaction, int outer, int weighting,
+                const float* __restrict__ Hn, const float* __restrict__ Cn, CPtrs P,
+                int64_t ldp, const float* __restrict__ alpha, float* __restrict__ out) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = PackCfg<VEC, VPL, LPR>;
+  const int lig = threadIdx.x % LPR;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + threadIdx.x / LPR;
+  if (row >= n) return;
+  const int64_t ow = weighting == 0 ? 2 * D * K : 2 * D;
+  for (int64_t f0 = 0; f0 < D; f0 += Cfg::kTile) {
+    V h[VPL], c[VPL], accD[VPL], accW[VPL];
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t d = f0 + static_cast<int64_t>(lig + q * LPR) * VEC;
+      if (d < D) {
+        h[q] = ld_vec<VEC>(Hn + row * D + d);
+        c[q] = ld_vec<VEC>(Cn + row * D + d);
+      } else {
+        vzero(h[q]);
+        vzero(c[q]);
+      }
+      vzero(accD[q]);
+      vzero(accW[q]);
+    }
+    for (int k = 0; k < K; ++k) {
+      const float a = alpha != nullptr ? __ldg(alpha + row * K + k) : 1.0f;
+      const float* pk = P.p[k] + row * ldp;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t d = f0 + static_cast<int64_t>(lig + q * LPR) * VEC;
+        if (d >= D) continue;
+        const V th = ldg_vec<VEC>(pk + d);
+        const V tc = ldg_vec<VEC>(pk + D + d);
+        V ow_, od_;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          float Dv, Wv;
+          interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer,
+                       Dv, Wv);
+          vel(ow_, j) = a * Wv;
+          vel(od_, j) = a * Dv;
+        }
+        if (weighting == 0) {
+          float* o = out + row * ow + static_cast<int64_t>(k) * 2 * D + d;
+          st_vec(o, ow_);
+          st_vec(o + D, od_);
+        } else {
+          vadd(accD[q], od_);
+          vadd(accW[q], ow_);
+        }
+      }
+    }
+    if (weighting == 1) {
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t d = f0 + static_cast<int64_t>(lig + q * LPR) * VEC;
+        if (d < D) {
+          st_vec(out + row * ow + d, accD[q]);
+          st_vec(out + row * ow + D + d, accW[q]);
+        }
+      }
+    }
+  }
+}
+
+template <int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+pack_bwd_kernel(int64_t n, int64_t D, int K, int interaction, int outer, int weighting,
+                const float* __restrict__ GO, const float* __restrict__ Hn,
+                const float* __restrict__ Cn, CPtrs P, int64_t ldp,
+                const float* __restrict__ alpha, float* __restrict__ GH,
+                float* __restrict__ GC, MPtrs GP, int64_t ldgp, int accumulate_p,
+                float* __restrict__ GA) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = PackCfg<VEC, VPL, LPR>;
+  const int lig = threadIdx.x % LPR;
+  const unsigned gmask = pack_group_mask<LPR>();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + threadIdx.x / LPR;
+  if (row >= n) return;
+  const int64_t ow = weighting == 0 ? 2 * D * K : 2 * D;
+  for (int64_t f0 = 0; f0 < D; f0 += Cfg::kTile) {
+    V h[VPL], c[VPL], gh[VPL], gc[VPL], goD[VPL], goW[VPL];
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t d = f0 + static_cast<int64_t>(lig + q * LPR) * VEC;
+      vzero(gh[q]);
+      vzero(gc[q]);
+      if (d < D) {
+        h[q] = ld_vec<VEC>(Hn + row * D + d);
+        c[q] = ld_vec<VEC>(Cn + row * D + d);
+        if (weighting == 1) {
+          goD[q] = ld_vec<VEC>(GO + row * ow + d);
+          goW[q] = ld_vec<VEC>(GO + row * ow + D + d);
+        }
+      } else {
+        vzero(h[q]);
+        vzero(c[q]);
+        vzero(goD[q]);
+        vzero(goW[q]);
+      }
+    }
+    for (int k = 0; k < K; ++k) {
+      const float a = alpha != nullptr ? __ldg(alpha + row * K + k) : 1.0f;
+      const float* pk = P.p[k] + row * ldp;
+      float* gpk = GP.p[k] + row * ldgp;
+      float ga = 0.0f;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t d = f0 + static_cast<int64_t>(lig + q * LPR) * VEC;
+        if (d >= D) continue;
+        const V th = ldg_vec<VEC>(pk + d);
+        const V tc = ldg_vec<VEC>(pk + D + d);
+        V gW, gD;
+        if (weighting == 0) {
+          const float* go = GO + row * ow + static_cast<int64_t>(k) * 2 * D + d;
+          gW = ld_vec<VEC>(go);
+          gD = ld_vec<VEC>(go + D);
+        } else {
+          gW = goW[q];
+          gD = goD[q];
+        }
+        V gth, gtc;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float hv = vel(h[q], j), cv = vel(c[q], j);
+          const float thv = vel(th, j), tcv = vel(tc, j);
+          const DW r = interact(hv * tcv, cv * thv, interaction, outer);
+          const float gWo = vel(gW, j), gDo = vel(gD, j);
+          ga += gWo * r.W + gDo * r.D;
+          const float gWa = gWo * a, gDa = gDo * a;
+          const float gbhr = gDa * r.dD_hr + gWa * r.dW_hr;
+          const float gbrh = gDa * r.dD_rh + gWa * r.dW_rh;
+          vel(gh[q], j) += gbhr * tcv;
+          vel(gc[q], j) += gbrh * thv;
+          vel(gth, j) = gbrh * cv;
+          vel(gtc, j) = gbhr * hv;
+        }
+        if (accumulate_p) {
+          vadd(gth, ld_vec<VEC>(gpk + d));
+          vadd(gtc, ld_vec<VEC>(gpk + D + d));
+        }
+        st_vec(gpk + d, gth);
+        st_vec(gpk + D + d, gtc);
+      }
+      if (GA != nullptr) {
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) ga += __shfl_xor_sync(gmask, ga, o, LPR);
+        if (lig == 0) {
+          if (f0 == 0) GA[row * K + k] = ga;
+          else GA[row * K + k] += ga;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t d = f0 + static_cast<int64_t>(lig + q * LPR) * VEC;
+      if (d < D) {
+        st_vec(GH + row * D + d, gh[q]);
+        st_vec(GC + row * D + d, gc[q]);
+      }
+    }
+  }
+}
+
+#define CIGN_PACK_DISPATCH(VEC_, FV_, CALL)                                    \
+  do {                                                                         \
+    if ((FV_) <= 8) { constexpr int V_ = VEC_, P_ = 1, L_ = 8; CALL; }         \
+    else if ((FV_) <= 16) { constexpr int V_ = VEC_, P_ = 1, L_ = 16; CALL; }  \
+    else if ((FV_) <= 32) { constexpr int V_ = VEC_, P_ = 1, L_ = 32; CALL; }  \
+    else if ((FV_) <= 64) { constexpr int V_ = VEC_, P_ = 2, L_ = 32; CALL; }  \
+    else { constexpr int V_ = VEC_, P_ = 4, L_ = 32; CALL; }                   \
+  } while (0)
+
+// The backward keeps gh/gc/h/c/gradient tiles live across the hop loop; one
+// vector per lane (looping over D in 128-float tiles) keeps it near 80
+// registers, i.e. three resident CTAs per SM.
+#define CIGN_PACK_BWD_DISPATCH(VEC_, FV_, CALL)                                \
+  do {                                                                         \
+    if ((FV_) <= 8) { constexpr int V_ = VEC_, P_ = 1, L_ = 8; CALL; }         \
+    else if ((FV_) <= 16) { constexpr int V_ = VEC_, P_ = 1, L_ = 16; CALL; }  \
+    else { constexpr int V_ = VEC_, P_ = 1, L_ = 32; CALL; }                   \
+  } while (0)
+
+template <int VEC, int VPL, int LPR>
+int launch_fwd(int64_t n, int64_t D, int K, int inter, int outer, int weighting,
+               const float* H, const float* C, const CPtrs& P, int64_t ldp,
+               const float* alpha, float* out, cudaStream_t s) {
+  using Cfg = PackCfg<VEC, VPL, LPR>;
+  const int64_t grid = (n + Cfg::kGroups - 1) / Cfg::kGroups;
+  CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "pack_fwd: too many rows");
+  pack_fwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      n, D, K, inter, outer, weighting, H, C, P, ldp, alpha, out);
+  CIGN_CHECK_LAUNCH("pack_fwd_kernel");
+  return CIGN_OK;
+}
+
+template <int VEC, int VPL, int LPR>
+int launch_bwd(int64_t n, int64_t D, int K, int inter, int outer, int weighting,
+               const float* GO, const float* H, const float* C, const CPtrs& P, int64_t ldp,
+               const float* alpha, float* GH, float* GC, const MPtrs& GP, int64_t ldgp,
+               int acc, float* GA, cudaStream_t s) {
+  using Cfg = PackCfg<VEC, VPL, LPR>;
+  const int64_t grid = (n + Cfg::kGroups - 1) / Cfg::kGroups;
+  CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "pack_bwd: too many rows");
+  pack_bwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      n, D, K, inter, outer, weighting, GO, H, C, P, ldp, alpha, GH, GC, GP, ldgp, acc, GA);
+  CIGN_CHECK_LAUNCH("pack_bwd_kernel");
+  return CIGN_OK;
+}
+
+int check_modes(int64_t n, int64_t d, int k, int inter, int outer, int weighting,
+                const char* name) {
+  CIGN_REQUIRE(n >= 0 && d >= 1, CIGN_ERR_INVALID_ARGUMENT, "%s: bad sizes", name);
+  CIGN_REQUIRE(k >= 1 && k <= kMaxK, CIGN_ERR_UNSUPPORTED, "%s: hop count must be in [1, %d]",
+               name, kMaxK);
+  CIGN_REQUIRE(inter == 0 || inter == 1, CIGN_ERR_INVALID_ARGUMENT,
+               "%s: interaction must be 0 (old) or 1 (new)", name);
+  CIGN_REQUIRE(outer == 0 || outer == 1, CIGN_ERR_INVALID_ARGUMENT,
+               "%s: outer must be 0 (none) or 1 (tanh)", name);
+  CIGN_REQUIRE(weighting == 0 || weighting == 1, CIGN_ERR_INVALID_ARGUMENT,
+               "%s: weighting must be 0 (old) or 1 (new)", name);
+  return CIGN_OK;
+}
+
+}  // namespace
+}  // namespace cign
+
+using namespace cign;
+
+extern "C" {
+
+int cign_pack_fwd(int64_t n, int64_t d, int32_t k, int32_t interaction, int32_t outer,
+                  int32_t weighting, const float* H, const float* C, const float* const* P,
+                  int64_t ldp, const float* alpha, float* out, cign_stream_t stream) {
+  int rc = check_modes(n, d, k, interaction, outer, weighting, "pack_fwd");
+  if (rc) return rc;
+  if (n == 0) return CIGN_OK;
+  CIGN_REQUIRE(H && C && P && out, CIGN_ERR_NULL_POINTER, "pack_fwd: NULL argument");
+  CIGN_REQUIRE(ldp >= 2 * d, CIGN_ERR_INVALID_ARGUMENT, "pack_fwd: ldp < 2D");
+  CPtrs pl{};
+  bool v4 = d % 4 == 0 && ldp % 4 == 0 && aligned16(H) && aligned16(C) && aligned16(out);
+  for (int i = 0; i < k; ++i) {
+    CIGN_REQUIRE(P[i] != nullptr, CIGN_ERR_NULL_POINTER, "pack_fwd: P[%d] is NULL", i);
+    pl.p[i] = P[i];
+    v4 = v4 && aligned16(P[i]);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (v4) {
+    CIGN_PACK_DISPATCH(4, d / 4, return (launch_fwd<V_, P_, L_>(n, d, k, interaction, outer, weighting, H, C, pl, ldp, alpha, out, s)));
+  }
+  CIGN_PACK_DISPATCH(1, d, return (launch_fwd<V_, P_, L_>(n, d, k, interaction, outer, weighting, H, C, pl, ldp, alpha, out, s)));
+  return CIGN_OK;
+}
+
+int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction, int32_t outer,
+                  int32_t weighting, const float* grad_out, const float* H, const float* C,
+                  const float* const* P, int64_t ldp, const float* alpha, float* grad_H,
+                  float* grad_C, float* const* grad_P, int64_t ldgp, int32_t accumulate_p,
+                  float* grad_alpha, cign_stream_t stream) {
+  int rc = check_modes(n, d, k, interaction, outer, weighting, "pack_bwd");
+  if (rc) return rc;
+  if (n == 0) return CIGN_OK;
+  CIGN_REQUIRE(grad_out && H && C && P && grad_H && grad_C && grad_P, CIGN_ERR_NULL_POINTER,
+               "pack_bwd: NULL argument");
+  CIGN_REQUIRE(ldp >= 2 * d && ldgp >= 2 * d, CIGN_ERR_INVALID_ARGUMENT,
+               "pack_bwd: ldp/ldgp < 2D");
+  CPtrs pl{};
+  MPtrs gl{};
+  bool v4 = d % 4 == 0 && ldp % 4 == 0 && ldgp % 4 == 0 && aligned16(grad_out) &&
+            aligned16(H) && aligned16(C) && aligned16(grad_H) && aligned16(grad_C);
+  for (int i = 0; i < k; ++i) {
+    CIGN_REQUIRE(P[i] != nullptr && grad_P[i] != nullptr, CIGN_ERR_NULL_POINTER,
+                 "pack_bwd: P[%d]/grad_P[%d] is NULL", i, i);
+    pl.p[i] = P[i];
+    gl.p[i] = grad_P[i];
+    v4 = v4 && aligned16(P[i]) && aligned16(grad_P[i]);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (v4) {
+    CIGN_PACK_BWD_DISPATCH(4, d / 4, return (launch_bwd<V_, P_, L_>(n, d, k, interaction, outer, weighting, grad_out, H, C, pl, ldp, alpha, grad_H, grad_C, gl, ldgp, accumulate_p, grad_alpha, s)));
+  }
+  CIGN_PACK_BWD_DISPATCH(1, d, return (launch_bwd<V_, P_, L_>(n, d, k, interaction, outer, weighting, grad_out, H, C, pl, ldp, alpha, grad_H, grad_C, gl, ldgp, accumulate_p, grad_alpha, s)));
+  return CIGN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,444 @@
+// Fixed-CSR SpMM and the k-hop propagation recurrence (forward P^p X and the
+// transposed backward chain) for sm_100a.
+//
+// Design
+//   * Row-split gather SpMM.  A group of LPR lanes (LPR = 8/16/32) owns one
+//     output row and keeps the row's feature tile in registers (VPL vectors
+//     of VEC floats per lane).  Column ids / values of the row are read
+//     lane-parallel (coalesced) and broadcast with shuffles; each edge then
+//     costs LPR*VPL vector loads of the neighbour's feature row, issued two
+//     to four edges at a time for memory-level parallelism.
+//   * Power-law graphs have hub rows.  Rows with more than kHeavyThreshold
+//     non-zeros are listed at plan time (sorted by degree, descending) and
+//     processed first, one 256-thread CTA per row: its groups split the
+//     row's edges and combine their partial tiles through shared memory in a
+//     fixed order, so the result is deterministic and independent of timing.
+//   * The backward "+ g" of the hop chain is the SpMM epilogue (addend).
+//   * Reference: MultiHopCsrPlan (multihop_csr_ext/multihop_csr_pipeline_cuda.cu
+//     :113-322) drives three cuSPARSE SpMMs plus two add kernels per call.
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+
+struct cign_spmm_plan {
+  cign_csr_f32 p;
+  cign_csr_f32 pt;
+  bool pt_is_p;
+  int32_t* heavy_p;   // device [n_heavy_p]
+  int32_t* heavy_pt;  // device [n_heavy_pt] (aliases heavy_p when pt_is_p)
+  int64_t n_heavy_p;
+  int64_t n_heavy_pt;
+  int32_t max_deg_p;
+  int32_t max_deg_pt;
+  int device;
+};
+
+namespace cign {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kHeavyThreshold = 128;
+
+template <int VEC, int VPL, int LPR>
+struct SpmmCfg {
+  static constexpr int kGroups = kThreads / LPR;        // groups per CTA
+  static constexpr int kTile = LPR * VPL * VEC;         // floats per pass
+  static constexpr int kUnroll = VPL >= 4 ? 2 : 4;      // edges in flight
+};
+
+// acc[q] += sum over edges e in {start, start+step, ...} < e1 of
+//           val[e] * X[col[e], f0 + (lig + q*LPR)*VEC ...]
+// Edges are fetched LPR at a time (one per lane) and broadcast.
+template <int VEC, int VPL, int LPR>
+__device__ __forceinline__ void gather_edges(
+    const int* __restrict__ col, const float* __restrict__ val, int start,
+    int e1, int step, const float* __restrict__ X, int64_t F, int64_t f0,
+    int lig, unsigned gmask, typename VecT<VEC>::type (&acc)[VPL]) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = SpmmCfg<VEC, VPL, LPR>;
+  for (int base = start; base < e1; base += step) {
+    const int my = base + lig;
+    int c = 0;
+    float v = 0.0f;
+    if (my < e1) {
+      c = __ldg(col + my);
+      v = __ldg(val + my);
+    }
+    const int cnt = min(LPR, e1 - base);
+    int t = 0;
+    for (; t + Cfg::kUnroll <= cnt; t += Cfg::kUnroll) {
+      int cc[Cfg::kUnroll];
+      float vv[Cfg::kUnroll];
+#pragma unroll
+      for (int u = 0; u < Cfg::kUnroll; ++u) {
+        cc[u] = __shfl_sync(gmask, c, t + u, LPR);
+        vv[u] = __shfl_sync(gmask, v, t + u, LPR);
+      }
+      V xv[Cfg::kUnroll][VPL];
+#pragma unroll
+      for (int u = 0; u < Cfg::kUnroll; ++u) {
+        const float* xr = X + static_cast<int64_t>(cc[u]) * F + f0;
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) {
+          const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+          if (f0 + fi < F) xv[u][q] = ldg_vec<VEC>(xr + fi);
+          else vzero(xv[u][q]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < Cfg::kUnroll; ++u)
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) vfma(acc[q], vv[u], xv[u][q]);
+    }
+    for (; t < cnt; ++t) {
+      const int c0 = __shfl_sync(gmask, c, t, LPR);
+      const float v0 = __shfl_sync(gmask, v, t, LPR);
+      const float* xr = X + static_cast<int64_t>(c0) * F + f0;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+        if (f0 + fi < F) vfma(acc[q], v0, ldg_vec<VEC>(xr + fi));
+      }
+    }
+  }
+}
+
+template <int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+spmm_rows_kernel(int rows, const int* __restrict__ crow,
+                 const int* __restrict__ col, const float* __restrict__ val,
+                 const int* __restrict__ heavy_rows, int n_heavy,
+                 int heavy_threshold, const float* __restrict__ X, int64_t F,
+                 const float* __restrict__ addend, float* __restrict__ Y) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = SpmmCfg<VEC, VPL, LPR>;
+  const int lig = threadIdx.x % LPR;
+  const int group = threadIdx.x / LPR;
+  const unsigned gmask =
+      LPR == 32 ? kFullMask
+                : (((1u << LPR) - 1u) << ((threadIdx.x & 31) / LPR * LPR));
+
+  if (static_cast<int>(blockIdx.x) < n_heavy) {
+    // ---- one CTA per heavy row: all groups split the row's edges.
+    __shared__ float red[Cfg::kGroups * Cfg::kTile];
+    const int row = heavy_rows[blockIdx.x];
+    const int e0 = crow[row];
+    const int e1 = crow[row + 1];
+    for (int64_t f0 = 0; f0 < F; f0 += Cfg::kTile) {
+      V acc[VPL];
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) vzero(acc[q]);
+      gather_edges<VEC, VPL, LPR>(col, val, e0 + group * LPR, e1,
+                                  Cfg::kGroups * LPR, X, F, f0, lig, gmask,
+                                  acc);
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int fi = (lig + q * LPR) * VEC;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          red[group * Cfg::kTile + fi + j] = vel(acc[q], j);
+      }
+      __syncthreads();
+      for (int fi = threadIdx.x; fi < Cfg::kTile; fi += kThreads) {
+        if (f0 + fi < F) {
+          float s = 0.0f;
+          for (int g = 0; g < Cfg::kGroups; ++g) s += red[g * Cfg::kTile + fi];
+          const int64_t o = static_cast<int64_t>(row) * F + f0 + fi;
+          if (addend != nullptr) s += addend[o];
+          Y[o] = s;
+        }
+      }
+      __syncthreads();
+    }
+    return;
+  }
+
+  // ---- light rows: one group of LPR lanes per row.
+  const int64_t row64 =
+      static_cast<int64_t>(blockIdx.x - n_heavy) * Cfg::kGroups + group;
+  if (row64 >= rows) return;
+  const int row = static_cast<int>(row64);
+  const int e0 = crow[row];
+  const int e1 = crow[row + 1];
+  if (e1 - e0 > heavy_threshold) return;  // handled by a heavy CTA
+  for (int64_t f0 = 0; f0 < F; f0 += Cfg::kTile) {
+    V acc[VPL];
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) vzero(acc[q]);
+    gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask,
+                                acc);
+    float* yr = Y + row64 * F + f0;
+    const float* ar = addend != nullptr ? addend + row64 * F + f0 : nullptr;
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+      if (f0 + fi < F) {
+        if (ar != nullptr) vadd(acc[q], ld_vec<VEC>(ar + fi));
+        st_vec(yr + fi, acc[q]);
+      }
+    }
+  }
+}
+
+// Plan-time validation of a CSR: crow monotone with crow[0]=0, crow[rows]=nnz,
+// all columns in range.  Sets *bad to 1 on the first violation.
+__global__ void csr_validate_kernel(int64_t rows, int64_t cols, int64_t nnz,
+                                    const int* __restrict__ crow,
+                                    const int* __restrict__ col,
+                                    int* __restrict__ bad) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < rows; i += stride) {
+    if (crow[i] > crow[i + 1]) atomicExch(bad, 1);
+  }
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       e < nnz; e += stride) {
+    const int c = col[e];
+    if (c < 0 || c >= cols) atomicExch(bad, 1);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (crow[0] != 0 || static_cast<int64_t>(crow[rows]) != nnz)
+      atomicExch(bad, 1);
+  }
+}
+
+template <int VEC, int VPL, int LPR>
+int launch_spmm_cfg(const cign_csr_f32& m, const int32_t* heavy, int64_t n_heavy,
+                    const float* X, int64_t F, const float* addend, float* Y,
+                    cudaStream_t stream) {
+  using Cfg = SpmmCfg<VEC, VPL, LPR>;
+  const int64_t light_blocks = (m.rows + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = n_heavy + light_blocks;
+  if (grid == 0) return CIGN_OK;
+  CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "spmm: grid too large");
+  spmm_rows_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+      static_cast<int>(m.rows), m.crow, m.col, m.val, heavy,
+      static_cast<int>(n_heavy), kHeavyThreshold, X, F, addend, Y);
+  CIGN_CHECK_LAUNCH("spmm_rows_kernel");
+  return CIGN_OK;
+}
+
+template <int VEC>
+int launch_spmm_vec(const cign_csr_f32& m, const int32_t* heavy, int64_t n_heavy,
+                    const float* X, int64_t F, const float* addend, float* Y,
+                    cudaStream_t stream) {
+  const int64_t fv = F / VEC;  // vectors per row
+  if (fv <= 8) return launch_spmm_cfg<VEC, 1, 8>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  if (fv <= 16) return launch_spmm_cfg<VEC, 1, 16>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  if (fv <= 32) return launch_spmm_cfg<VEC, 1, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  if (fv <= 64) return launch_spmm_cfg<VEC, 2, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  if (fv <= 128) return launch_spmm_cfg<VEC, 4, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  return launch_spmm_cfg<VEC, 8, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
+}
+
+int run_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
+             int64_t F, const float* addend, float* Y, cudaStream_t stream) {
+  const bool use_t = transpose != 0 && !plan->pt_is_p;
+  const cign_csr_f32& m = use_t ? plan->pt : plan->p;
+  const int32_t* heavy = use_t ? plan->heavy_pt : plan->heavy_p;
+  const int64_t n_heavy = use_t ? plan->n_heavy_pt : plan->n_heavy_p;
+  const bool vec4 = (F % 4 == 0) && aligned16(X) && aligned16(Y) &&
+                    (addend == nullptr || aligned16(addend));
+  if (vec4) return launch_spmm_vec<4>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  return launch_spmm_vec<1>(m, heavy, n_heavy, X, F, addend, Y, stream);
+}
+
+int check_csr_args(const cign_csr_f32* m, const char* name) {
+  CIGN_REQUIRE(m != nullptr, CIGN_ERR_NULL_POINTER, "%s: csr is NULL", name);
+  CIGN_REQUIRE(m->rows >= 0 && m->cols >= 0 && m->nnz >= 0,
+               CIGN_ERR_INVALID_ARGUMENT, "%s: negative size", name);
+  CIGN_REQUIRE(m->rows < (1ll << 31) && m->cols < (1ll << 31) &&
+                   m->nnz < (1ll << 31),
+               CIGN_ERR_UNSUPPORTED, "%s: int32 CSR limits exceeded", name);
+  CIGN_REQUIRE(m->crow != nullptr, CIGN_ERR_NULL_POINTER, "%s: crow is NULL", name);
+  CIGN_REQUIRE(m->nnz == 0 || (m->col != nullptr && m->val != nullptr),
+               CIGN_ERR_NULL_POINTER, "%s: col/val is NULL", name);
+  return CIGN_OK;
+}
+
+// Validates the CSR on the device, then builds the heavy-row list (device
+// array owned by the plan).
+int build_heavy(const cign_csr_f32& m, int32_t** heavy_out, int64_t* n_out,
+                int32_t* max_deg_out) {
+  *heavy_out = nullptr;
+  *n_out = 0;
+  *max_deg_out = 0;
+  int* bad_d = nullptr;
+  CIGN_CHECK_CUDA(cudaMalloc(&bad_d, sizeof(int)), "plan: cudaMalloc");
+  cudaMemset(bad_d, 0, sizeof(int));
+  const int64_t work = std::max<int64_t>(std::max<int64_t>(m.rows, m.nnz), 1);
+  const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, 4096));
+  csr_validate_kernel<<<blocks, 256>>>(m.rows, m.cols, m.nnz, m.crow, m.col, bad_d);
+  cudaError_t le = cudaGetLastError();
+  int bad = 0;
+  cudaError_t ce = cudaMemcpy(&bad, bad_d, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(bad_d);
+  if (le != cudaSuccess || ce != cudaSuccess)
+    return set_error(CIGN_ERR_CUDA, "plan: csr validation failed: %s",
+                     cudaGetErrorString(le != cudaSuccess ? le : ce));
+  CIGN_REQUIRE(bad == 0, CIGN_ERR_INVALID_ARGUMENT,
+               "plan: malformed CSR (crow not monotone from 0 to nnz, or a "
+               "column index out of range)");
+  return build_heavy_list(m.crow, m.rows, kHeavyThreshold, heavy_out, n_out,
+                          max_deg_out);
+}
+
+int check_dense(const cign_spmm_plan* plan, const float* X, int64_t F,
+                const void* Y, const char* name) {
+  CIGN_REQUIRE(plan != nullptr, CIGN_ERR_NULL_POINTER, "%s: plan is NULL", name);
+  CIGN_REQUIRE(F > 0, CIGN_ERR_INVALID_ARGUMENT, "%s: F must be positive", name);
+  CIGN_REQUIRE(plan->p.rows == plan->p.cols, CIGN_ERR_INVALID_ARGUMENT,
+               "%s: operator must be square", name);
+  if (plan->p.rows > 0) {
+    CIGN_REQUIRE(X != nullptr && Y != nullptr, CIGN_ERR_NULL_POINTER,
+                 "%s: dense operand is NULL", name);
+  }
+  return CIGN_OK;
+}
+
+}  // namespace
+}  // namespace cign
+
+using namespace cign;
+
+extern "C" {
+
+int cign_spmm_plan_create(const cign_csr_f32* p, const cign_csr_f32* pt,
+                          cign_spmm_plan** out) {
+  CIGN_REQUIRE(out != nullptr, CIGN_ERR_NULL_POINTER, "plan_create: out is NULL");
+  *out = nullptr;
+  int rc = check_csr_args(p, "plan_create(P)");
+  if (rc) return rc;
+  const bool pt_is_p = pt == nullptr ||
+                       (pt->crow == p->crow && pt->col == p->col && pt->val == p->val);
+  if (!pt_is_p) {
+    rc = check_csr_args(pt, "plan_create(P^T)");
+    if (rc) return rc;
+    CIGN_REQUIRE(pt->rows == p->cols && pt->cols == p->rows && pt->nnz == p->nnz,
+                 CIGN_ERR_INVALID_ARGUMENT, "plan_create: P^T shape mismatch");
+  }
+  cign_spmm_plan* plan = new cign_spmm_plan();
+  plan->p = *p;
+  plan->pt = pt_is_p ? *p : *pt;
+  plan->pt_is_p = pt_is_p;
+  plan->heavy_p = plan->heavy_pt = nullptr;
+  cudaGetDevice(&plan->device);
+  rc = build_heavy(plan->p, &plan->heavy_p, &plan->n_heavy_p, &plan->max_deg_p);
+  if (rc == CIGN_OK && !pt_is_p)
+    rc = build_heavy(plan->pt, &plan->heavy_pt, &plan->n_heavy_pt, &plan->max_deg_pt);
+  if (rc != CIGN_OK) {
+    if (plan->heavy_p) cudaFree(plan->heavy_p);
+    if (plan->heavy_pt) cudaFree(plan->heavy_pt);
+    delete plan;
+    return rc;
+  }
+  if (pt_is_p) {
+    plan->heavy_pt = plan->heavy_p;
+    plan->n_heavy_pt = plan->n_heavy_p;
+    plan->max_deg_pt = plan->max_deg_p;
+  }
+  *out = plan;
+  clear_error();
+  return CIGN_OK;
+}
+
+int cign_spmm_plan_destroy(cign_spmm_plan* plan) {
+  if (plan == nullptr) return CIGN_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(plan->device);
+  if (plan->heavy_p) cudaFree(plan->heavy_p);
+  if (!plan->pt_is_p && plan->heavy_pt) cudaFree(plan->heavy_pt);
+  cudaSetDevice(prev);
+  delete plan;
+  return CIGN_OK;
+}
+
+int cign_spmm_plan_get_info(const cign_spmm_plan* plan, cign_spmm_plan_info* info) {
+  CIGN_REQUIRE(plan != nullptr && info != nullptr, CIGN_ERR_NULL_POINTER,
+               "plan_get_info: NULL argument");
+  info->rows = plan->p.rows;
+  info->nnz = plan->p.nnz;
+  info->heavy_rows = plan->n_heavy_p;
+  info->heavy_rows_t = plan->n_heavy_pt;
+  info->max_degree = plan->max_deg_p;
+  info->max_degree_t = plan->max_deg_pt;
+  info->heavy_threshold = kHeavyThreshold;
+  info->transpose_is_forward = plan->pt_is_p ? 1 : 0;
+  return CIGN_OK;
+}
+
+int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
+              int64_t F, const float* addend, float* Y, cign_stream_t stream) {
+  int rc = check_dense(plan, X, F, Y, "spmm");
+  if (rc) return rc;
+  CIGN_REQUIRE(X != Y || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
+               "spmm: Y must not alias X");
+  return run_spmm(plan, transpose, X, F, addend, Y,
+                  static_cast<cudaStream_t>(stream));
+}
+
+int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power, const float* X,
+                      int64_t F, float* const* Y, cign_stream_t stream) {
+  CIGN_REQUIRE(max_power >= 1, CIGN_ERR_INVALID_ARGUMENT,
+               "multihop_fwd: max_power must be >= 1");
+  CIGN_REQUIRE(Y != nullptr, CIGN_ERR_NULL_POINTER, "multihop_fwd: Y is NULL");
+  int rc = check_dense(plan, X, F, Y[0], "multihop_fwd");
+  if (rc) return rc;
+  for (int p = 0; p < max_power; ++p) {
+    CIGN_REQUIRE(Y[p] != nullptr || plan->p.rows == 0, CIGN_ERR_NULL_POINTER,
+                 "multihop_fwd: Y[%d] is NULL", p);
+    CIGN_REQUIRE(Y[p] != X || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
+                 "multihop_fwd: Y[%d] aliases X", p);
+    if (p > 0)
+      CIGN_REQUIRE(Y[p] != Y[p - 1] || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
+                   "multihop_fwd: Y[%d] aliases Y[%d]", p, p - 1);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float* src = X;
+  for (int p = 0; p < max_power; ++p) {
+    rc = run_spmm(plan, 0, src, F, nullptr, Y[p], s);
+    if (rc) return rc;
+    src = Y[p];
+  }
+  return CIGN_OK;
+}
+
+int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power,
+                      const float* const* G, int64_t F, float* GX, float* ws,
+                      cign_stream_t stream) {
+  CIGN_REQUIRE(max_power >= 1, CIGN_ERR_INVALID_ARGUMENT,
+               "multihop_bwd: max_power must be >= 1");
+  CIGN_REQUIRE(G != nullptr, CIGN_ERR_NULL_POINTER, "multihop_bwd: G is NULL");
+  int rc = check_dense(plan, GX, F, GX, "multihop_bwd");
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int top = 0;  // highest power (1-based) with a gradient
+  for (int p = max_power; p >= 1; --p)
+    if (G[p - 1] != nullptr) { top = p; break; }
+  const size_t bytes = static_cast<size_t>(plan->p.rows) * F * sizeof(float);
+  if (top == 0) {
+    if (bytes) CIGN_CHECK_CUDA(cudaMemsetAsync(GX, 0, bytes, s), "multihop_bwd: memset");
+    return CIGN_OK;
+  }
+  if (top >= 2)
+    CIGN_REQUIRE(ws != nullptr || plan->p.rows == 0, CIGN_ERR_NULL_POINTER,
+                 "multihop_bwd: ws is NULL");
+  for (int p = 0; p < max_power; ++p)
+    CIGN_REQUIRE(G[p] == nullptr || (G[p] != GX && G[p] != ws) || plan->p.rows == 0,
+                 CIGN_ERR_INVALID_ARGUMENT, "multihop_bwd: G[%d] aliases GX/ws", p);
+  // u_top = G[top-1];  u_p = P^T u_{p+1} + G[p-1]  (p = top-1 .. 1);
+  // GX = P^T u_1.  u_p lives in ws for odd p and in GX for even p, so the
+  // final SpMM reads ws and writes GX.
+  const float* u = G[top - 1];
+  for (int p = top - 1; p >= 1; --p) {
+    float* dst = (p & 1) ? ws : GX;
+    rc = run_spmm(plan, 1, u, F, G[p - 1], dst, s);
+    if (rc) return rc;
+    u = dst;
+  }
+  return run_spmm(plan, 1, u, F, nullptr, GX, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,212 @@
+"""Python owners of the native plan objects (cign_spmm_plan, cign_gat_plan).
+
+A plan keeps the int32 CSR tensors it was built from alive (the native plan
+only stores their device pointers) and is immutable after construction, so
+one plan may serve several streams.  Plans are built once per graph, before
+any timed work (the reference does the same in MultiHopCSR3GraphOperator /
+prepare_fused_gat_graph).
+"""
+from __future__ import annotations
+
+import ctypes
+from collections import OrderedDict
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+
+
+def _as_i32(t: torch.Tensor) -> torch.Tensor:
+    return t.to(dtype=torch.int32).contiguous()
+
+
+class SpmmPlan:
+    """Native SpMM plan over a square fixed operator P (and optionally P^T).
+
+    ``crow/col/val`` (and the ``*_t`` triple) are int32/int32/fp32 CUDA
+    tensors; when the transpose triple is None or bitwise equal to P's, the
+    transposed products reuse P (symmetric operator, the default for CIGN's
+    undirected normalised adjacency).
+    """
+
+    def __init__(self, crow, col, val, crow_t=None, col_t=None, val_t=None):
+        _lib.require_cuda("SpmmPlan")
+        self.lib = _lib.load_library()
+        self.device = crow.device
+        self.crow, self.col, self.val = _as_i32(crow), _as_i32(col), val.to(torch.float32).contiguous()
+        self.rows = int(self.crow.numel() - 1)
+        self.nnz = int(self.col.numel())
+        symmetric = crow_t is None
+        if not symmetric:
+            crow_t, col_t = _as_i32(crow_t), _as_i32(col_t)
+            val_t = val_t.to(torch.float32).contiguous()
+            symmetric = (
+                crow_t.numel() == self.crow.numel()
+                and col_t.numel() == self.col.numel()
+                and bool(torch.equal(crow_t, self.crow))
+                and bool(torch.equal(col_t, self.col))
+                and bool(torch.equal(val_t, self.val))
+            )
+        self.symmetric = symmetric
+        if symmetric:
+            self.crow_t, self.col_t, self.val_t = self.crow, self.col, self.val
+        else:
+            self.crow_t, self.col_t, self.val_t = crow_t, col_t, val_t
+        p = _lib.CsrF32(self.rows, self.rows, self.nnz, self.crow.data_ptr(), self.col.data_ptr(),
+                        self.val.data_ptr())
+        handle = ctypes.c_void_p()
+        with _lib.DeviceGuard(self.device):
+            if symmetric:
+                rc = self.lib.cign_spmm_plan_create(ctypes.byref(p), None, ctypes.byref(handle))
+            else:
+                pt = _lib.CsrF32(self.rows, self.rows, int(self.col_t.numel()), self.crow_t.data_ptr(),
+                                 self.col_t.data_ptr(), self.val_t.data_ptr())
+                rc = self.lib.cign_spmm_plan_create(ctypes.byref(p), ctypes.byref(pt),
+                                                    ctypes.byref(handle))
+        _lib.check(rc, "cign_spmm_plan_create")
+        self.handle = handle
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                self.lib.cign_spmm_plan_destroy(h)
+            except Exception:
+                pass
+            self.handle = None
+
+    def info(self) -> Dict[str, int]:
+        inf = _lib.SpmmPlanInfo()
+        _lib.check(self.lib.cign_spmm_plan_get_info(self.handle, ctypes.byref(inf)),
+                   "cign_spmm_plan_get_info")
+        return {name: int(getattr(inf, name)) for name, _ in _lib.SpmmPlanInfo._fields_}
+
+    # ---------------------------------------------------------------- ops
+    def _check_dense(self, x: torch.Tensor, what: str) -> torch.Tensor:
+        if x.device != self.device:
+            raise RuntimeError(f"{what}: tensor on {x.device}, plan on {self.device}")
+        if x.dim() != 2 or x.size(0) != self.rows:
+            raise ValueError(f"{what}: expected [{self.rows}, F], got {tuple(x.shape)}")
+        return x.to(torch.float32).contiguous()
+
+    def spmm(self, x: torch.Tensor, transpose: bool = False,
+             addend: Optional[torch.Tensor] = None) -> torch.Tensor:
+        x = self._check_dense(x, "spmm")
+        F = int(x.size(1))
+        y = torch.empty_like(x)
+        if addend is not None:
+            addend = self._check_dense(addend, "spmm addend")
+        with _lib.DeviceGuard(self.device):
+            rc = self.lib.cign_spmm(self.handle, 1 if transpose else 0, _lib.ptr(x), F,
+                                    _lib.ptr(addend), _lib.ptr(y), _lib.stream_of(x))
+        _lib.check(rc, "cign_spmm")
+        return y
+
+    def forward(self, x: torch.Tensor, max_power: int) -> List[torch.Tensor]:
+        """[P^1 x, ..., P^max_power x]."""
+        x = self._check_dense(x, "multihop forward")
+        ys = [torch.empty_like(x) for _ in range(int(max_power))]
+        arr = _lib.ptr_array(ys)
+        with _lib.DeviceGuard(self.device):
+            rc = self.lib.cign_multihop_fwd(self.handle, int(max_power), _lib.ptr(x),
+                                            int(x.size(1)), arr, _lib.stream_of(x))
+        _lib.check(rc, "cign_multihop_fwd")
+        return ys
+
+    def backward(self, grads: Sequence[Optional[torch.Tensor]], F: int) -> torch.Tensor:
+        """grads[p-1] = dL/d(P^p x) or None; returns dL/dx."""
+        ref = next((g for g in grads if g is not None), None)
+        if ref is None:
+            raise ValueError("multihop backward needs at least one gradient")
+        gs = [None if g is None else self._check_dense(g, "multihop grad") for g in grads]
+        gx = torch.empty((self.rows, int(F)), dtype=torch.float32, device=self.device)
+        ws = torch.empty_like(gx) if len(gs) >= 2 else None
+        arr = _lib.ptr_array(gs)
+        with _lib.DeviceGuard(self.device):
+            rc = self.lib.cign_multihop_bwd(self.handle, len(gs), arr, int(F), _lib.ptr(gx),
+                                            _lib.ptr(ws), _lib.stream_of(gx))
+        _lib.check(rc, "cign_multihop_bwd")
+        return gx
+
+
+class GatPlan:
+    """Native plan over the fixed GAT graph triple ((rowptr, col), (row, colptr), perm)."""
+
+    def __init__(self, rowptr, col, row, colptr, perm):
+        _lib.require_cuda("GatPlan")
+        self.lib = _lib.load_library()
+        self.device = rowptr.device
+        self.rowptr, self.col = _as_i32(rowptr), _as_i32(col)
+        self.row, self.colptr, self.perm = _as_i32(row), _as_i32(colptr), _as_i32(perm)
+        self.n = int(self.rowptr.numel() - 1)
+        self.nnz = int(self.col.numel())
+        if self.colptr.numel() != self.n + 1 or self.row.numel() != self.nnz or self.perm.numel() != self.nnz:
+            raise ValueError("GAT graph: CSR/CSC/perm sizes do not match")
+        handle = ctypes.c_void_p()
+        with _lib.DeviceGuard(self.device):
+            rc = self.lib.cign_gat_plan_create(self.n, self.nnz, _lib.ptr(self.rowptr), _lib.ptr(self.col),
+                                               _lib.ptr(self.colptr), _lib.ptr(self.row),
+                                               _lib.ptr(self.perm), ctypes.byref(handle))
+        _lib.check(rc, "cign_gat_plan_create")
+        self.handle = handle
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                self.lib.cign_gat_plan_destroy(h)
+            except Exception:
+                pass
+            self.handle = None
+
+    def info(self) -> Dict[str, int]:
+        arr = (ctypes.c_int64 * 6)()
+        _lib.check(self.lib.cign_gat_plan_get_info(self.handle, arr), "cign_gat_plan_get_info")
+        keys = ("n", "nnz", "heavy_rows", "heavy_cols", "max_row_len", "max_col_len")
+        return {k: int(v) for k, v in zip(keys, arr)}
+
+
+_CACHE_MAX = 16
+_GAT_PLANS: "OrderedDict[Tuple[int, ...], GatPlan]" = OrderedDict()
+_SPMM_PLANS: "OrderedDict[Tuple[int, ...], SpmmPlan]" = OrderedDict()
+
+
+def _cache_put(cache, key, plan):
+    cache[key] = plan
+    cache.move_to_end(key)
+    while len(cache) > _CACHE_MAX:
+        cache.popitem(last=False)
+
+
+def gat_plan_for(rowptr, col, row, colptr, perm) -> GatPlan:
+    """Plan cached by the graph tensors' identity (data pointers and sizes).
+
+    The cached plan keeps the caller's tensors alive, so their addresses
+    cannot be recycled for a different graph while the entry exists."""
+    key = (rowptr.data_ptr(), col.data_ptr(), row.data_ptr(), colptr.data_ptr(), perm.data_ptr(),
+           int(rowptr.numel()), int(col.numel()), int(rowptr.device.index or 0))
+    plan = _GAT_PLANS.get(key)
+    if plan is None:
+        plan = GatPlan(rowptr, col, row, colptr, perm)
+        plan._keepalive = (rowptr, col, row, colptr, perm)
+        _cache_put(_GAT_PLANS, key, plan)
+    return plan
+
+
+def spmm_plan_for(csr: torch.Tensor, csr_t: Optional[torch.Tensor]) -> SpmmPlan:
+    """Plan cached by the sparse CSR tensors' identity (FixedCSRSpMMFunction)."""
+    key = (csr.crow_indices().data_ptr(), csr.col_indices().data_ptr(), csr.values().data_ptr(),
+           0 if csr_t is None else csr_t.values().data_ptr(), int(csr._nnz()))
+    plan = _SPMM_PLANS.get(key)
+    if plan is None:
+        if csr_t is None:
+            plan = SpmmPlan(csr.crow_indices(), csr.col_indices(), csr.values())
+        else:
+            plan = SpmmPlan(csr.crow_indices(), csr.col_indices(), csr.values(),
+                            csr_t.crow_indices(), csr_t.col_indices(), csr_t.values())
+        # Keep the sparse tensors alive with the plan so the cache key (their
+        # storage addresses) cannot be reused by another tensor.
+        plan._keepalive = (csr, csr_t)
+        _cache_put(_SPMM_PLANS, key, plan)
+    return plan

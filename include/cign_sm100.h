@@ -1,0 +1,312 @@
+/*
+ * cign_sm100.h -- C ABI of libcign_sm100.so, the B200 (sm_100a) kernels of
+ * CIGN's sparse message-passing hot path.
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer unless stated otherwise;
+ *     pointer arrays (float* const* ...) are HOST arrays of device pointers.
+ *   - Dense matrices are row-major, fp32, contiguous, rows of the stated width.
+ *   - CSR indices are int32 (the reference converts to int32 before any
+ *     kernel: multihop_csr_pipeline.py:38-48, collapsed_gat.cpp:32-43).
+ *   - `stream` is a cudaStream_t passed as void*; 0 = legacy default stream.
+ *   - Every function returns CIGN_OK (0) or one of the CIGN_ERR_* codes; the
+ *     message of the last failure on the calling thread is returned by
+ *     cign_last_error().  Arguments are checked before anything is launched,
+ *     so an error return means nothing was enqueued.
+ *   - Kernels never allocate.  Scratch ("ws") is passed in by the caller,
+ *     sized by the matching *_workspace_bytes() query.
+ *   - Reductions are deterministic: repeated calls on the same inputs give
+ *     bitwise identical outputs (no floating-point atomics).
+ *
+ * Each entry point names the reference interface it replaces
+ * (rabbit-art/CIGN, path within that project:line).
+ */
+#ifndef CIGN_SM100_H
+#define CIGN_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define CIGN_API __attribute__((visibility("default")))
+#else
+#define CIGN_API
+#endif
+
+typedef void* cign_stream_t;
+
+enum {
+  CIGN_OK = 0,
+  CIGN_ERR_INVALID_ARGUMENT = 1, /* bad size / shape / mode value          */
+  CIGN_ERR_NULL_POINTER = 2,     /* required pointer is NULL               */
+  CIGN_ERR_ALIGNMENT = 3,        /* pointer not aligned as documented      */
+  CIGN_ERR_LAUNCH = 4,           /* kernel launch failed                   */
+  CIGN_ERR_TIMEOUT = 5,          /* a bounded device-side wait expired     */
+  CIGN_ERR_UNSUPPORTED = 6,      /* shape outside the supported range      */
+  CIGN_ERR_CUDA = 7              /* other CUDA runtime error               */
+};
+
+/* ------------------------------------------------------------------ misc */
+CIGN_API int cign_version(void);
+CIGN_API const char* cign_last_error(void);
+
+/* ------------------------------------------------------------------ CSR
+ * A fixed sparse graph operator in CSR form (device arrays).
+ * Replaces the CSR parts held by FixedCSRGraphOperator (model.py:134-159)
+ * and cloned to int32 by _csr_parts_int32 (multihop_csr_pipeline.py:38-48). */
+typedef struct cign_csr_f32 {
+  int64_t rows;
+  int64_t cols;
+  int64_t nnz;
+  const int32_t* crow; /* [rows+1], crow[0] = 0, non-decreasing */
+  const int32_t* col;  /* [nnz], 0 <= col < cols                */
+  const float* val;    /* [nnz]                                 */
+} cign_csr_f32;
+
+/* SpMM plan over P (and P^T).  Holds a device list of "heavy" rows that are
+ * processed one CTA per row; the CSR arrays themselves stay owned by the
+ * caller and must outlive the plan.  Immutable after creation: one plan may
+ * be used from several streams at once.
+ * Replaces MultiHopCsrPlan (multihop_csr_ext/multihop_csr_pipeline_cuda.cu:
+ * 113-322) and its Python owner MultiHopCSR3GraphOperator
+ * (multihop_csr_pipeline.py:89-140).  `pt` may be NULL when P is symmetric
+ * (or the caller only runs forward); the transposed entry points then use P.
+ * Synchronises the device once (reads crow to the host). */
+typedef struct cign_spmm_plan cign_spmm_plan;
+
+typedef struct cign_spmm_plan_info {
+  int64_t rows;
+  int64_t nnz;
+  int64_t heavy_rows;     /* rows of P processed one CTA per row          */
+  int64_t heavy_rows_t;   /* same for P^T                                  */
+  int32_t max_degree;
+  int32_t max_degree_t;
+  int32_t heavy_threshold;
+  int32_t transpose_is_forward; /* 1 when P^T calls reuse P              */
+} cign_spmm_plan_info;
+
+CIGN_API int cign_spmm_plan_create(const cign_csr_f32* p, const cign_csr_f32* pt,
+                          cign_spmm_plan** out);
+CIGN_API int cign_spmm_plan_destroy(cign_spmm_plan* plan);
+CIGN_API int cign_spmm_plan_get_info(const cign_spmm_plan* plan,
+                            cign_spmm_plan_info* info /* host */);
+
+/* Y = op(P) @ X (+ addend).  op = P (transpose=0) or P^T (transpose=1).
+ * X, Y, addend: [rows, F].  addend may be NULL.  Y must not alias X.
+ * Replaces FixedCSRSpMMFunction.forward/backward (model.py:106-131). */
+CIGN_API int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
+              int64_t F, const float* addend, float* Y, cign_stream_t stream);
+
+/* k-hop forward recurrence Y[p-1] = P^p X for p = 1..max_power.
+ * Y: host array of max_power device pointers, each [rows, F]; entries for
+ * powers the caller does not need still need a buffer (they are the
+ * recurrence state).
+ * Replaces MultiHopCsrPlan::forward3 (multihop_csr_pipeline_cuda.cu:287-297),
+ * GenericMultiHopCSRFunction.forward (multihop_csr_pipeline.py:233-246) and
+ * the hybrid native3 + tail path (multihop_csr_pipeline.py:214-230). */
+CIGN_API int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power,
+                      const float* X, int64_t F, float* const* Y,
+                      cign_stream_t stream);
+
+/* k-hop transposed backward: acc = 0; for p = max_power..1:
+ *   acc = P^T (acc + G[p-1]);   GX = acc.
+ * G: host array of max_power device pointers ([rows, F]) or NULL entries
+ * for powers that received no gradient.  ws: one [rows, F] fp32 buffer.
+ * The "+ G" is fused into the SpMM epilogue (one kernel per hop).
+ * Replaces MultiHopCsrPlan::backward3 (multihop_csr_pipeline_cuda.cu:299-321)
+ * and GenericMultiHopCSRFunction.backward (multihop_csr_pipeline.py:248-265).*/
+CIGN_API int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power,
+                      const float* const* G, int64_t F, float* GX, float* ws,
+                      cign_stream_t stream);
+
+/* ------------------------------------------------------------------ GAT
+ * Collapsed multi-head GAT (concat=False) over a fixed graph.
+ *
+ * Graph plan: destination-major CSR (rowptr [n+1], col [nnz]) and its CSC
+ * (colptr [n+1], row [nnz]) with perm[csc position] = CSR edge id -- the
+ * triple PyG's FusedGATConv.to_graph_format yields and the reference keeps
+ * in GraphCliffordNet.prepare_fused_gat_graph (generic_engine/model_cign.py:
+ * 1069-1158).  The plan validates the triple on the device, lists rows and
+ * columns with more than 128 edges (one CTA each) and keeps pointers to the
+ * caller's arrays, which must outlive it.  Synchronises the device once. */
+typedef struct cign_gat_plan cign_gat_plan;
+
+CIGN_API int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr,
+                         const int32_t* col, const int32_t* colptr,
+                         const int32_t* row, const int32_t* perm,
+                         cign_gat_plan** out);
+CIGN_API int cign_gat_plan_destroy(cign_gat_plan* plan);
+/* info (host, 6 entries): n, nnz, heavy rows, heavy columns, max row
+ * length, max column length. */
+CIGN_API int cign_gat_plan_get_info(const cign_gat_plan* plan, int64_t* info);
+
+/* Forward, for destination row i and head h:
+ *   e_ij = LeakyReLU(attn_row[i,h] + attn_col[j,h]),
+ *   w_ij = keep(e*H+h) * exp(e_ij - max_j e) / sum_j exp(e_ij - max_j e) / (1-p),
+ *   pre[i,:] = (1/H) sum_h sum_j w_ij in_feat[j,h,:] + bias,  out = SiLU(pre),
+ *   edge_max/edge_sum [N,H] = the row's max and exp-sum (saved for backward).
+ * keep(idx) is the splitmix64 Bernoulli of make_dropout_mask_kernel
+ * (collapsed_gat_cuda.cu:34-47), recomputed from (seed, idx), never stored.
+ * in_feat [N,H,C]; out, pre [N,C].  attn_drop in [0,1); 1 <= H <= 64.
+ * Replaces collapsed_gat_forward_cuda (collapsed_gat_ext/collapsed_gat_cuda.cu:
+ * 434-478) behind collapsed_gat_mean_bias_silu (collapsed_gat.py:164-225),
+ * without its H=6,C=256 restriction (collapsed_gat.cpp:67-68). */
+CIGN_API int cign_gat_fwd(const cign_gat_plan* plan, int32_t heads, int32_t channels,
+                 const float* attn_row, const float* attn_col,
+                 const float* in_feat, const float* bias, float negative_slope,
+                 float attn_drop, uint64_t seed, float* out, float* pre,
+                 float* edge_max, float* edge_sum, cign_stream_t stream);
+
+CIGN_API size_t cign_gat_bwd_workspace_bytes(const cign_gat_plan* plan, int32_t heads,
+                                    int32_t channels);
+
+/* Backward of cign_gat_fwd: grad_feat [N,H,C], grad_attn_row/col [N,H],
+ * grad_bias [C].  Deterministic: grad_attn_col is gathered over the CSC
+ * instead of the reference's atomicAdd scatter.
+ * Replaces collapsed_gat_backward_cuda (collapsed_gat_cuda.cu:480-545). */
+CIGN_API int cign_gat_bwd(const cign_gat_plan* plan, int32_t heads, int32_t channels,
+                 const float* attn_row, const float* attn_col,
+                 const float* in_feat, const float* pre, const float* edge_max,
+                 const float* edge_sum, const float* grad_y,
+                 float negative_slope, float attn_drop, uint64_t seed,
+                 float* grad_feat, float* grad_attn_row, float* grad_attn_col,
+                 float* grad_bias, void* ws, size_t ws_bytes,
+                 cign_stream_t stream);
+
+/* Materialise the GAT dropout keep-mask (uint8 [nnz*H], 1 = kept) exactly
+ * as make_dropout_mask_kernel (collapsed_gat_cuda.cu:34-47) does.  The
+ * forward/backward never need it; it exists for parity checks. */
+CIGN_API int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop,
+                          uint64_t seed, uint8_t* mask, cign_stream_t stream);
+
+/* ------------------------------------------------------------ side ops
+ * alpha_src[n,h] = sum_c x[n,h,c] att_src[h,c];  same for dst.
+ * Replaces attention_forward_cuda (fused_gat_sideops_cuda.cu:243-260). */
+CIGN_API int cign_attn_logits_fwd(int64_t n, int32_t heads, int32_t channels,
+                         const float* x, const float* att_src,
+                         const float* att_dst, float* alpha_src,
+                         float* alpha_dst, cign_stream_t stream);
+
+CIGN_API size_t cign_attn_logits_bwd_workspace_bytes(int64_t n, int32_t heads,
+                                            int32_t channels);
+
+/* grad_x = g_src (x) att_src + g_dst (x) att_dst;  grad_att_* = sum_n g x.
+ * accumulate != 0 adds into grad_x instead of overwriting it.
+ * Replaces attention_backward_cuda (fused_gat_sideops_cuda.cu:262-299). */
+CIGN_API int cign_attn_logits_bwd(int64_t n, int32_t heads, int32_t channels,
+                         const float* grad_src, const float* grad_dst,
+                         const float* x, const float* att_src,
+                         const float* att_dst, float* grad_x,
+                         float* grad_att_src, float* grad_att_dst,
+                         int32_t accumulate, void* ws, size_t ws_bytes,
+                         cign_stream_t stream);
+
+/* y = SiLU(mean_h out[n,h,:] + bias).  Replaces head_silu_forward_cuda
+ * (fused_gat_sideops_cuda.cu:301-316). */
+CIGN_API int cign_head_mean_bias_silu_fwd(int64_t n, int32_t heads, int32_t channels,
+                                 const float* out, const float* bias,
+                                 float* y, float* pre, cign_stream_t stream);
+
+CIGN_API size_t cign_head_mean_bias_silu_bwd_workspace_bytes(int64_t n,
+                                                    int32_t channels);
+
+/* Replaces head_silu_backward_cuda (fused_gat_sideops_cuda.cu:318-337). */
+CIGN_API int cign_head_mean_bias_silu_bwd(int64_t n, int32_t heads, int32_t channels,
+                                 const float* grad_y, const float* pre,
+                                 float* grad_out, float* grad_bias, void* ws,
+                                 size_t ws_bytes, cign_stream_t stream);
+
+/* ------------------------------------------------------------------ pack
+ * Clifford interaction pack.  For hop k with T_H = P_k[:, :D], T_C = P_k[:, D:]:
+ *   b_hr = H*T_C, b_rh = C*T_H
+ *   interaction 0 ("old"): D_k = SiLU(b_hr),           W_k = b_hr - b_rh
+ *   interaction 1 ("new"): D_k = SiLU((b_hr+b_rh)/2),  W_k = o((b_hr-b_rh)/2)
+ *     with outer o = identity (outer 0, "none") or tanh (outer 1)
+ *   weighting 0 ("old"): out[n, k*2D + d] = a_k W_k, out[n, k*2D + D + d] = a_k D_k
+ *   weighting 1 ("new"): out[n, d] = sum_k a_k D_k,  out[n, D + d] = sum_k a_k W_k
+ * P: host array of K device pointers, each [N, 2D] with row stride ldp floats.
+ * alpha: [N, K] or NULL (all ones).
+ * Replaces fused_pack_forward_kernel (fused_clifford_pack_ext/
+ * fused_clifford_pack_cuda.cu:22-56), the generic-K kernels
+ * (fused_clifford_pack.py:88-117, generic_engine/fused_clifford_cign_generic.py:
+ * 58-87) and the switch/CIGN packs (generic_engine/fused_clifford_switch_pack_ext/
+ * fused_clifford_switch_pack_cuda.cu:65-179). */
+CIGN_API int cign_pack_fwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
+                  int32_t outer, int32_t weighting, const float* H,
+                  const float* C, const float* const* P, int64_t ldp,
+                  const float* alpha, float* out, cign_stream_t stream);
+
+/* Backward: grad_H, grad_C [N,D]; grad_P: host array of K device pointers
+ * ([N,2D], stride ldgp); grad_alpha [N,K] or NULL.
+ * accumulate_p != 0 adds into grad_P instead of overwriting it.
+ * Replaces fused_pack_backward_main/alpha_kernel (fused_clifford_pack_cuda.cu:
+ * 58-152), the generic-K backward (fused_clifford_cign_generic.py:70-87) and
+ * backward_main/alpha_kernel (fused_clifford_switch_pack_cuda.cu:186-368). */
+CIGN_API int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
+                  int32_t outer, int32_t weighting, const float* grad_out,
+                  const float* H, const float* C, const float* const* P,
+                  int64_t ldp, const float* alpha, float* grad_H,
+                  float* grad_C, float* const* grad_P, int64_t ldgp,
+                  int32_t accumulate_p, float* grad_alpha,
+                  cign_stream_t stream);
+
+/* ------------------------------------------------------------ block ops
+ * Row LayerNorm over D with biased variance and rsqrt(var + eps); optional
+ * dropout (keep iff (splitmix64(seed ^ idx*0xD2B74407B1CE6E93) >> 11) * 2^-53
+ * >= p, idx = n*D + d) applied to x before the norm.  Masks are recomputed
+ * in backward from (seed, idx), never stored.
+ * Replaces the kernels of fused_block_ops.py:15 and fused_block_ops_ext/
+ * fused_block_ops_cuda.cu:45-322 without their D<=256 limit. */
+CIGN_API int cign_dropout_ln_fwd(int64_t n, int64_t d, const float* x, const float* w,
+                        const float* b, float p, float eps, uint64_t seed,
+                        float* y, float* mean, float* rstd,
+                        cign_stream_t stream);
+
+CIGN_API size_t cign_ln_bwd_workspace_bytes(int64_t n, int64_t d);
+
+CIGN_API int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y,
+                        const float* x, const float* w, const float* mean,
+                        const float* rstd, float p, uint64_t seed,
+                        float* grad_x, float* grad_w, float* grad_b, void* ws,
+                        size_t ws_bytes, cign_stream_t stream);
+
+/* y = LayerNorm(a + b). */
+CIGN_API int cign_add_ln_fwd(int64_t n, int64_t d, const float* a, const float* b,
+                    const float* w, const float* bias, float eps, float* y,
+                    float* mean, float* rstd, cign_stream_t stream);
+
+/* grad_z = d LN / d(a+b); the caller uses it for both a and b. */
+CIGN_API int cign_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* a,
+                    const float* b, const float* w, const float* mean,
+                    const float* rstd, float* grad_z, float* grad_w,
+                    float* grad_b, void* ws, size_t ws_bytes,
+                    cign_stream_t stream);
+
+/* y = h + gamma * dropout(g). */
+CIGN_API int cign_gamma_residual_fwd(int64_t n, int64_t d, const float* h,
+                            const float* g, const float* gamma, float p,
+                            uint64_t seed, float* y, cign_stream_t stream);
+
+CIGN_API size_t cign_gamma_residual_bwd_workspace_bytes(int64_t n, int64_t d);
+
+/* grad_g = grad_y * gamma * mask/(1-p);  grad_gamma = sum_n grad_y * g * mask/(1-p).
+ * (grad_h = grad_y is returned by the caller without a kernel.) */
+CIGN_API int cign_gamma_residual_bwd(int64_t n, int64_t d, const float* grad_y,
+                            const float* g, const float* gamma, float p,
+                            uint64_t seed, float* grad_g, float* grad_gamma,
+                            void* ws, size_t ws_bytes, cign_stream_t stream);
+
+/* Materialise the block-op dropout keep-mask (uint8 [count]) for indices
+ * 0..count-1, for parity checks only. */
+CIGN_API int cign_block_dropout_mask(int64_t count, float p, uint64_t seed,
+                            uint8_t* mask, cign_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CIGN_SM100_H */

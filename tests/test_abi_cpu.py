@@ -1,0 +1,67 @@
+"""The C-ABI library loads and exports every symbol include/cign_sm100.h
+declares; argument validation rejects bad input before touching the GPU.
+CPU only (no compute calls)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from cign_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "cign_sm100.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^CIGN_API\s+[\w\s\*]+?\b(cign_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load_library()
+    names = declared_symbols()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the Python binding covers every declared symbol
+    assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
+
+
+def test_version_and_error_text():
+    lib = _lib.load_library()
+    assert lib.cign_version() >= 1
+    out = ctypes.c_void_p()
+    rc = lib.cign_spmm_plan_create(None, None, ctypes.byref(out))
+    assert rc == 2  # CIGN_ERR_NULL_POINTER
+    assert "csr is NULL" in _lib.last_error()
+
+
+def test_invalid_arguments_rejected_before_launch():
+    lib = _lib.load_library()
+    # unknown pack modes / hop counts
+    assert lib.cign_pack_fwd(4, 8, 0, 1, 0, 0, None, None, None, 16, None, None, None) == 6
+    assert lib.cign_pack_fwd(4, 8, 2, 7, 0, 0, None, None, None, 16, None, None, None) == 1
+    # dropout probability out of range
+    assert lib.cign_dropout_ln_fwd(4, 8, None, None, None, 1.5, 1e-5, 0, None, None, None,
+                                   None) == 1
+    # D above the register-resident limit
+    assert lib.cign_add_ln_fwd(4, 4096, None, None, None, None, 1e-5, None, None, None,
+                               None) == 6
+    # GAT heads above the supported range
+    assert lib.cign_gat_fwd(ctypes.c_void_p(1), 65, 8, None, None, None, None, 0.2, 0.0, 0, None,
+                            None, None, None, None) == 6
+    assert "heads" in _lib.last_error()
+
+
+def test_python_api_requires_cuda_without_fallback():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("CUDA present")
+    from cign_b200 import collapsed_gat, fused_block_ops, multihop_csr_pipeline
+    with pytest.raises(RuntimeError):
+        multihop_csr_pipeline.ensure_multihop_csr_loaded()
+    with pytest.raises(RuntimeError):
+        collapsed_gat.ensure_collapsed_gat_loaded()
+    with pytest.raises(TypeError):
+        fused_block_ops.fused_add_layernorm(torch.zeros(2, 4), torch.zeros(2, 4), torch.ones(4),
+                                            torch.zeros(4), 1e-5)
