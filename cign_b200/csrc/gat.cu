@@ -756,7 +756,9 @@ __global__ void gat_validate_kernel(int64_t n, int64_t nnz,
   // CSC position e must belong to the column col[perm[e]]: checked by
   // comparing each column's range against the column ids of its edges.
   for (int64_t j = t0; j < n; j += stride) {
-    for (int pos = colptr[j]; pos < colptr[j + 1]; ++pos) {
+    const int lo = max(colptr[j], 0);
+    const int hi = min(static_cast<int64_t>(colptr[j + 1]), nnz);
+    for (int pos = lo; pos < hi; ++pos) {
       const int pe = perm[pos];
       if (pe >= 0 && pe < nnz && col[pe] != j) { atomicOr(bad, 64); break; }
     }
