@@ -52,9 +52,11 @@ class SpmmPlanInfo(ctypes.Structure):
         ("nnz", c_int64),
         ("heavy_rows", c_int64),
         ("heavy_rows_t", c_int64),
+        ("segments", c_int64),
+        ("segments_t", c_int64),
         ("max_degree", c_int32),
         ("max_degree_t", c_int32),
-        ("heavy_threshold", c_int32),
+        ("segment_length", c_int32),
         ("transpose_is_forward", c_int32),
     ]
 
@@ -66,17 +68,21 @@ _PP = POINTER(c_void_p)  # host array of device pointers
 SIGNATURES = {
     "cign_version": (c_int, []),
     "cign_last_error": (c_char_p, []),
+    "cign_kernel_launches": (c_uint64, []),
     "cign_spmm_plan_create": (c_int, [POINTER(CsrF32), POINTER(CsrF32), POINTER(c_void_p)]),
     "cign_spmm_plan_destroy": (c_int, [_P]),
     "cign_spmm_plan_get_info": (c_int, [_P, POINTER(SpmmPlanInfo)]),
-    "cign_spmm": (c_int, [_P, c_int, _P, c_int64, _P, _P, _P]),
-    "cign_multihop_fwd": (c_int, [_P, c_int, _P, c_int64, _PP, _P]),
-    "cign_multihop_bwd": (c_int, [_P, c_int, _PP, c_int64, _P, _P, _P]),
+    "cign_spmm_workspace_bytes": (c_size_t, [_P, c_int64]),
+    "cign_spmm": (c_int, [_P, c_int, _P, c_int64, _P, _P, _P, c_size_t, _P]),
+    "cign_multihop_workspace_bytes": (c_size_t, [_P, c_int, c_int64]),
+    "cign_multihop_fwd": (c_int, [_P, c_int, _P, c_int64, _PP, _P, c_size_t, _P]),
+    "cign_multihop_bwd": (c_int, [_P, c_int, _PP, c_int64, _P, _P, c_size_t, _P]),
     "cign_gat_plan_create": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, POINTER(c_void_p)]),
     "cign_gat_plan_destroy": (c_int, [_P]),
     "cign_gat_plan_get_info": (c_int, [_P, POINTER(c_int64)]),
+    "cign_gat_fwd_workspace_bytes": (c_size_t, [_P, c_int32, c_int32]),
     "cign_gat_fwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, c_float, c_float, c_uint64,
-                             _P, _P, _P, _P, _P]),
+                             _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_gat_bwd_workspace_bytes": (c_size_t, [_P, c_int32, c_int32]),
     "cign_gat_bwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, c_float, c_float,
                              c_uint64, _P, _P, _P, _P, _P, c_size_t, _P]),
@@ -109,44 +115,6 @@ SIGNATURES = {
 }
 
 
-# Kernels launched by one call of each compute entry point (for launch
-# accounting); entries taking a hop count launch one kernel per hop.
-KERNELS_PER_CALL = {
-    "cign_spmm": 1, "cign_gat_fwd": 1, "cign_gat_bwd": 4, "cign_gat_dropout_mask": 1,
-    "cign_attn_logits_fwd": 1, "cign_attn_logits_bwd": 2, "cign_head_mean_bias_silu_fwd": 1,
-    "cign_head_mean_bias_silu_bwd": 3, "cign_pack_fwd": 1, "cign_pack_bwd": 1,
-    "cign_dropout_ln_fwd": 1, "cign_dropout_ln_bwd": 2, "cign_add_ln_fwd": 1,
-    "cign_add_ln_bwd": 2, "cign_gamma_residual_fwd": 1, "cign_gamma_residual_bwd": 2,
-    "cign_block_dropout_mask": 1,
-}
-PER_HOP = {"cign_multihop_fwd", "cign_multihop_bwd"}
-
-
-class _Counting:
-    """Proxy over the ctypes handle that counts kernel launches while
-    `counting` is on (one untimed step is enough: the step is deterministic
-    in its launch sequence)."""
-
-    def __init__(self, handle):
-        self._h = handle
-        self.counting = False
-        self.launches = 0
-
-    def __getattr__(self, name):
-        fn = getattr(self._h, name)
-        if not self.counting or not name.startswith("cign_"):
-            return fn
-        def wrapped(*args):
-            rc = fn(*args)
-            if rc == 0:
-                if name in PER_HOP:
-                    self.launches += int(args[1])
-                else:
-                    self.launches += KERNELS_PER_CALL.get(name, 0)
-            return rc
-        return wrapped
-
-
 def load_library(path: Path | str | None = None):
     """Load (once) and return the ctypes handle; raises if the .so is absent."""
     global _LIB, _LOAD_ERROR
@@ -172,7 +140,7 @@ def load_library(path: Path | str | None = None):
         except Exception as exc:  # pragma: no cover - depends on the box
             _LOAD_ERROR = exc
             raise
-        _LIB = _Counting(handle)
+        _LIB = handle
         return _LIB
 
 

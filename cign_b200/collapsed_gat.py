@@ -67,11 +67,13 @@ def gat_forward_raw(plan, attn_row, attn_col, in_feat, bias, negative_slope, att
     pre = torch.empty_like(out)
     emax = torch.empty((n, H), dtype=torch.float32, device=in_feat.device)
     esum = torch.empty_like(emax)
+    ws = _lib.workspace(lib.cign_gat_fwd_workspace_bytes(plan.handle, H, C), in_feat.device)
     with _lib.DeviceGuard(in_feat.device):
         rc = lib.cign_gat_fwd(plan.handle, H, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
                               _lib.ptr(in_feat), _lib.ptr(bias), float(negative_slope),
                               float(attn_drop), int(seed) & ((1 << 64) - 1), _lib.ptr(out),
-                              _lib.ptr(pre), _lib.ptr(emax), _lib.ptr(esum), _lib.stream_of(in_feat))
+                              _lib.ptr(pre), _lib.ptr(emax), _lib.ptr(esum), _lib.ptr(ws),
+                              ws.numel(), _lib.stream_of(in_feat))
     _lib.check(rc, "cign_gat_fwd")
     return out, pre, emax, esum
 

@@ -1,6 +1,7 @@
 // Library-wide pieces of the C ABI: version, thread-local error text, device
 // properties cache.
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -14,6 +15,7 @@ namespace cign {
 
 namespace {
 thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
 std::mutex g_sm_mutex;
 int g_sm_count[64] = {0};
 }  // namespace
@@ -30,6 +32,8 @@ int set_error(int code, const char* fmt, ...) {
 
 void clear_error() { g_last_error.clear(); }
 
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
@@ -45,12 +49,9 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
-int build_heavy_list(const int32_t* ptr_dev, int64_t rows, int threshold,
-                     int32_t** heavy_out, int64_t* n_out,
-                     int32_t* max_len_out) {
-  *heavy_out = nullptr;
-  *n_out = 0;
-  *max_len_out = 0;
+int build_segments(const int32_t* ptr_dev, int64_t rows, int seg_len, SegList* out) {
+  *out = SegList();
+  out->seg_len = seg_len;
   std::vector<int32_t> ptr(static_cast<size_t>(rows) + 1);
   CIGN_CHECK_CUDA(cudaMemcpy(ptr.data(), ptr_dev, ptr.size() * sizeof(int32_t),
                              cudaMemcpyDeviceToHost),
@@ -60,30 +61,50 @@ int build_heavy_list(const int32_t* ptr_dev, int64_t rows, int threshold,
   for (int64_t r = 0; r < rows; ++r) {
     const int32_t len = ptr[r + 1] - ptr[r];
     max_len = std::max(max_len, len);
-    if (len > threshold) heavy.emplace_back(len, static_cast<int32_t>(r));
+    if (len > seg_len) heavy.emplace_back(len, static_cast<int32_t>(r));
   }
+  out->max_len = max_len;
+  if (heavy.empty()) return CIGN_OK;
   std::stable_sort(heavy.begin(), heavy.end(),
                    [](const std::pair<int32_t, int32_t>& a,
-                      const std::pair<int32_t, int32_t>& b) {
-                     return a.first > b.first;
-                   });
-  *max_len_out = max_len;
-  if (heavy.empty()) return CIGN_OK;
-  std::vector<int32_t> rows_h(heavy.size());
-  for (size_t i = 0; i < heavy.size(); ++i) rows_h[i] = heavy[i].second;
+                      const std::pair<int32_t, int32_t>& b) { return a.first > b.first; });
+  std::vector<int32_t> srow, sbeg, send, hrow, hfirst;
+  for (const auto& hr : heavy) {
+    const int32_t r = hr.second;
+    hrow.push_back(r);
+    hfirst.push_back(static_cast<int32_t>(srow.size()));
+    for (int32_t b = ptr[r]; b < ptr[r + 1]; b += seg_len) {
+      srow.push_back(r);
+      sbeg.push_back(b);
+      send.push_back(std::min(b + seg_len, ptr[r + 1]));
+    }
+  }
+  hfirst.push_back(static_cast<int32_t>(srow.size()));
+  const int64_t n_seg = static_cast<int64_t>(srow.size());
+  const int64_t n_heavy = static_cast<int64_t>(hrow.size());
+  std::vector<int32_t> host;
+  host.reserve(3 * n_seg + 2 * n_heavy + 1);
+  host.insert(host.end(), srow.begin(), srow.end());
+  host.insert(host.end(), sbeg.begin(), sbeg.end());
+  host.insert(host.end(), send.begin(), send.end());
+  host.insert(host.end(), hrow.begin(), hrow.end());
+  host.insert(host.end(), hfirst.begin(), hfirst.end());
   int32_t* d = nullptr;
-  CIGN_CHECK_CUDA(cudaMalloc(&d, rows_h.size() * sizeof(int32_t)),
-                  "plan: cudaMalloc heavy list");
-  cudaError_t e = cudaMemcpy(d, rows_h.data(), rows_h.size() * sizeof(int32_t),
-                             cudaMemcpyHostToDevice);
+  CIGN_CHECK_CUDA(cudaMalloc(&d, host.size() * sizeof(int32_t)), "plan: cudaMalloc segments");
+  cudaError_t e = cudaMemcpy(d, host.data(), host.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaFree(d);
-    return set_error(CIGN_ERR_CUDA, "plan: copy heavy list: %s",
-                     cudaGetErrorString(e));
+    return set_error(CIGN_ERR_CUDA, "plan: copy segments: %s", cudaGetErrorString(e));
   }
-  *heavy_out = d;
-  *n_out = static_cast<int64_t>(rows_h.size());
+  out->buf = d;
+  out->n_seg = n_seg;
+  out->n_heavy = n_heavy;
   return CIGN_OK;
+}
+
+void free_segments(SegList* s) {
+  if (s->buf) cudaFree(s->buf);
+  *s = SegList();
 }
 
 }  // namespace cign
@@ -93,5 +114,9 @@ extern "C" {
 int cign_version(void) { return 1; }
 
 const char* cign_last_error(void) { return cign::g_last_error.c_str(); }
+
+uint64_t cign_kernel_launches(void) {
+  return cign::g_launches.load(std::memory_order_relaxed);
+}
 
 }  // extern "C"

@@ -23,12 +23,17 @@ void clear_error();
     if (!(cond)) return ::cign::set_error((code), __VA_ARGS__);        \
   } while (0)
 
+// Every kernel launch of the library is followed by CIGN_CHECK_LAUNCH, which
+// also counts it (cign_kernel_launches()).
+void count_launch();
+
 #define CIGN_CHECK_LAUNCH(what)                                               \
   do {                                                                        \
     cudaError_t _e = cudaGetLastError();                                      \
     if (_e != cudaSuccess)                                                    \
       return ::cign::set_error(CIGN_ERR_LAUNCH, "%s: %s", (what),             \
                                cudaGetErrorString(_e));                       \
+    ::cign::count_launch();                                                   \
   } while (0)
 
 #define CIGN_CHECK_CUDA(call, what)                                           \
@@ -46,12 +51,32 @@ inline bool aligned16(const void* p) {
 // Number of SMs of the current device (cached per device id).
 int sm_count();
 
-// Reads a device row-pointer array (int32 [rows+1]) to the host and returns
-// a device array (cudaMalloc'd; caller frees) of the rows whose length
-// exceeds `threshold`, sorted by length descending.  Used at plan time only.
-int build_heavy_list(const int32_t* ptr_dev, int64_t rows, int threshold,
-                     int32_t** heavy_out, int64_t* n_out,
-                     int32_t* max_len_out);
+// Work split of a CSR-like pointer array: rows with more than `seg_len`
+// entries ("heavy" rows, e.g. hubs of a power-law graph) are cut into
+// segments of at most seg_len entries, each processed by its own lane
+// group; their partial results are combined afterwards in segment order,
+// which keeps the sum order fixed (deterministic).  Rows of at most seg_len
+// entries are processed whole.  One device buffer holds
+//   seg_row[n_seg] | seg_begin[n_seg] | seg_end[n_seg] |
+//   heavy_row[n_heavy] | heavy_first[n_heavy + 1]
+// (segments of heavy row h are heavy_first[h] .. heavy_first[h+1]-1).
+struct SegList {
+  int32_t* buf = nullptr;  // device
+  int64_t n_seg = 0;
+  int64_t n_heavy = 0;
+  int32_t max_len = 0;
+  int32_t seg_len = 0;
+  const int32_t* seg_row() const { return buf; }
+  const int32_t* seg_begin() const { return buf + n_seg; }
+  const int32_t* seg_end() const { return buf + 2 * n_seg; }
+  const int32_t* heavy_row() const { return buf + 3 * n_seg; }
+  const int32_t* heavy_first() const { return buf + 3 * n_seg + n_heavy; }
+};
+
+// Reads the device pointer array (int32 [rows+1]) to the host and builds the
+// segment list (heavy rows ordered by length, longest first).  Plan time only.
+int build_segments(const int32_t* ptr_dev, int64_t rows, int seg_len, SegList* out);
+void free_segments(SegList* s);
 
 // Deterministic two-stage column sums of a row-major [n, c] matrix
 // (reduce.cu).  `partial` holds colsum_chunks(n) * c floats.

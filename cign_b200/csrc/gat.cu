@@ -8,12 +8,17 @@
 // Layout: destination-major CSR (rowptr, col) and its CSC (colptr, row) with
 // perm[csc position] = CSR edge id, in_feat [N,H,C], attn_* [N,H].
 //
-// Forward, per destination row i (a group of LPR lanes; one CTA for rows
-// with more than kHeavy edges):
+// Work split: rows (and, in the backward, CSC columns) with at most kSegLen
+// edges are processed whole by one group of LPR lanes; longer "hub" rows are
+// cut at plan time into kSegLen-edge segments, one group each, whose partial
+// results are combined by a per-hub kernel in segment order (fixed sum
+// order: deterministic).
+//
+// Forward, per destination row i:
 //   1. per head h: max and exp-sum of e_ij = leaky(attn_row[i,h] +
-//      attn_col[j,h]) over the row (lane-parallel, group reductions);
-//   2. per 32-edge chunk and head: the lane owning edge e computes its
-//      weight w = keep(e*H+h) * exp(e_ij - max) / sum / (1-p) once, the group
+//      attn_col[j,h]) (group reductions; hub rows: one CTA per row first);
+//   2. per 32-edge chunk and head: the lane owning edge e computes its weight
+//      w = keep(e*H+h) * exp(e_ij - max) / sum / (1-p) once, the group
 //      broadcasts (col, w) and accumulates w * in_feat[j,h,:] into the row's
 //      C-wide register tile (heads summed into one tile: "collapsed");
 //   3. pre = acc / H + bias, out = SiLU(pre).
@@ -21,13 +26,13 @@
 // backward instead of being stored.
 //
 // Backward:
-//   K1 (CSR rows): g_pre = grad_y * SiLU'(pre) (stored in the workspace);
-//      per edge and head dot(g_pre[i,:]/H, in_feat[j,h,:]); softmax backward
-//      through the kept/scaled weights and LeakyReLU -> grad_logit[e,h]
-//      (workspace) and grad_attn_row[i,h] (row sums).
-//   K2 (CSC columns): grad_feat[j,h,:] = sum_{i->j} w_ij g_pre[i,:]/H and
-//      grad_attn_col[j,h] = sum_{i->j} grad_logit[e,h]  -- a gather, so no
-//      atomics are needed anywhere.
+//   K1 (CSR rows): g_pre = grad_y * SiLU'(pre) (workspace); per edge and head
+//      dot(g_pre[i,:]/H, in_feat[j,h,:]); softmax backward through the
+//      kept/scaled weights and LeakyReLU -> grad_logit[e,h] (workspace) and
+//      grad_attn_row[i,h] (row sums; hub rows finish in a per-row CTA).
+//   K2 (CSC columns): grad_feat[j,h,:] = sum_{i->j} w_ijh g_pre[i,:]/H and
+//      grad_attn_col[j,h] = sum_{i->j} grad_logit[e,h] -- gathers, so no
+//      atomics anywhere.
 //   grad_bias = column sums of g_pre (two-stage, fixed order).
 #include <algorithm>
 
@@ -41,12 +46,8 @@ struct cign_gat_plan {
   const int32_t* colptr;
   const int32_t* row;
   const int32_t* perm;
-  int32_t* heavy_rows;  // rows with > kHeavy in-edges (CSR), device
-  int32_t* heavy_cols;  // columns with > kHeavy out-edges (CSC), device
-  int64_t n_heavy_rows;
-  int64_t n_heavy_cols;
-  int32_t max_row_len;
-  int32_t max_col_len;
+  cign::SegList rows;  // hub destination rows (CSR)
+  cign::SegList cols;  // hub source columns (CSC)
   int device;
 };
 
@@ -54,7 +55,7 @@ namespace cign {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kHeavy = 128;
+constexpr int kSegLen = 32;
 constexpr int kMaxHeads = 64;
 constexpr float kNegInit = -1.0e38f;  // reference initial running max
 
@@ -62,7 +63,7 @@ template <int VEC, int VPL, int LPR>
 struct GatCfg {
   static constexpr int kGroups = kThreads / LPR;
   static constexpr int kTile = LPR * VPL * VEC;
-  static constexpr int kUnroll = VPL >= 4 ? 2 : 4;
+  static constexpr int kUnroll = VPL >= 8 ? 2 : 4;
 };
 
 template <int LPR>
@@ -112,9 +113,8 @@ __device__ __forceinline__ float block_max(float v, float* scratch) {
 // Attention weight of CSR edge e (head h) as the reference forms it:
 // w = exp(leaky(ad + ac) - m) / s, divided by (1 - p) when p > 0; zero when
 // the edge is dropped or the row sum is not positive.
-__device__ __forceinline__ float edge_weight(float ad, float ac, float m,
-                                             float s, float slope, float p,
-                                             uint64_t seed, uint64_t idx) {
+__device__ __forceinline__ float edge_weight(float ad, float ac, float m, float s, float slope,
+                                             float p, uint64_t seed, uint64_t idx) {
   const bool keep = (p <= 0.0f) || gat_keep(seed, idx, p);
   if (!keep || !(s > 0.0f)) return 0.0f;
   float w = expf(leaky_f(ad + ac, slope) - m) / s;
@@ -122,20 +122,19 @@ __device__ __forceinline__ float edge_weight(float ad, float ac, float m,
   return w;
 }
 
-// acc[q] += sum over edges {start, start+step, ...} < e1 and all heads of
-// w(e,h) * in_feat[col[e], h, f0 + (lig + q*LPR)*VEC ...]
+// acc[q] += sum over edges [e0, e1) and all heads of
+// w(e,h) * in_feat[col[e], h, f0 + (lig + q*LPR)*VEC ...]; smax/ssum point at
+// the row's per-head max and exp-sum.
 template <int VEC, int VPL, int LPR>
 __device__ __forceinline__ void gat_gather(
-    int row, int start, int e1, int step, int H, int64_t C, int64_t f0,
-    const int* __restrict__ col, const float* __restrict__ attn_row,
-    const float* __restrict__ attn_col, const float* __restrict__ x,
-    const float* __restrict__ stats /* [2H]: max, sum */, float slope, float p,
-    uint64_t seed, int lig, unsigned gmask,
-    typename VecT<VEC>::type (&acc)[VPL]) {
+    int64_t row, int e0, int e1, int H, int64_t C, int64_t f0, const int* __restrict__ col,
+    const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+    const float* __restrict__ x, const float* smax, const float* ssum, float slope, float p,
+    uint64_t seed, int lig, unsigned gmask, typename VecT<VEC>::type (&acc)[VPL]) {
   using V = typename VecT<VEC>::type;
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const int64_t HC = static_cast<int64_t>(H) * C;
-  for (int base = start; base < e1; base += step) {
+  for (int base = e0; base < e1; base += LPR) {
     const int my = base + lig;
     const bool valid = my < e1;
     const int c = valid ? __ldg(col + my) : 0;
@@ -143,10 +142,9 @@ __device__ __forceinline__ void gat_gather(
     for (int h = 0; h < H; ++h) {
       float w = 0.0f;
       if (valid)
-        w = edge_weight(__ldg(attn_row + static_cast<int64_t>(row) * H + h),
-                        __ldg(attn_col + static_cast<int64_t>(c) * H + h),
-                        stats[h], stats[H + h], slope, p, seed,
-                        static_cast<uint64_t>(my) * H + h);
+        w = edge_weight(__ldg(attn_row + row * H + h),
+                        __ldg(attn_col + static_cast<int64_t>(c) * H + h), smax[h], ssum[h],
+                        slope, p, seed, static_cast<uint64_t>(my) * H + h);
       const float* xh = x + static_cast<int64_t>(h) * C + f0;
       int t = 0;
       for (; t + Cfg::kUnroll <= cnt; t += Cfg::kUnroll) {
@@ -187,107 +185,76 @@ __device__ __forceinline__ void gat_gather(
   }
 }
 
-template <int VEC, int VPL, int LPR>
-__device__ __forceinline__ void gat_store_out(
-    int64_t row, int64_t C, int64_t f0, int H, int lig,
-    typename VecT<VEC>::type (&acc)[VPL], const float* __restrict__ bias,
-    float* __restrict__ pre, float* __restrict__ out) {
-  const float hf = static_cast<float>(H);
-#pragma unroll
-  for (int q = 0; q < VPL; ++q) {
-    const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
-    if (f0 + fi < C) {
-      typename VecT<VEC>::type pv = acc[q], ov;
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float pj = vel(acc[q], j) / hf + __ldg(bias + f0 + fi + j);
-        vel(pv, j) = pj;
-        vel(ov, j) = silu_f(pj);
-      }
-      st_vec(pre + row * C + f0 + fi, pv);
-      st_vec(out + row * C + f0 + fi, ov);
+// ------------------------------------------------------------ forward
+// Hub rows: one CTA per row computes the per-head max / exp-sum.
+__global__ void __launch_bounds__(kThreads)
+gat_hub_stats_kernel(int H, const int* __restrict__ rowptr, const int* __restrict__ col,
+                     const int* __restrict__ hub_row, const float* __restrict__ attn_row,
+                     const float* __restrict__ attn_col, float slope,
+                     float* __restrict__ emax, float* __restrict__ esum) {
+  __shared__ float scratch[32];
+  const int64_t row = hub_row[blockIdx.x];
+  const int e0 = rowptr[row], e1 = rowptr[row + 1];
+  for (int h = 0; h < H; ++h) {
+    const float ad = attn_row[row * H + h];
+    float m = kNegInit;
+    for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
+      m = fmaxf(m, leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope));
+    m = block_max(m, scratch);
+    float s = 0.0f;
+    for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
+      s += expf(leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope) - m);
+    s = block_sum(s, scratch);
+    if (threadIdx.x == 0) {
+      emax[row * H + h] = m;
+      esum[row * H + h] = s;
     }
   }
 }
 
-// ------------------------------------------------------------ forward
+// Blocks [0, seg_blocks): hub-row segments -> partial [n_seg, C];
+// remaining blocks: whole rows of at most kSegLen edges.
 template <int VEC, int VPL, int LPR>
 __global__ void __launch_bounds__(kThreads)
 gat_fwd_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
-               const int* __restrict__ col, const int* __restrict__ heavy_rows,
-               int n_heavy, const float* __restrict__ attn_row,
+               const int* __restrict__ col, const int* __restrict__ seg_row,
+               const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
+               int seg_blocks, const float* __restrict__ attn_row,
                const float* __restrict__ attn_col, const float* __restrict__ x,
-               const float* __restrict__ bias, float slope, float p,
-               uint64_t seed, float* __restrict__ out, float* __restrict__ pre,
-               float* __restrict__ emax, float* __restrict__ esum) {
+               const float* __restrict__ bias, float slope, float p, uint64_t seed,
+               float* __restrict__ out, float* __restrict__ pre, float* __restrict__ emax,
+               float* __restrict__ esum, float* __restrict__ partial) {
   using V = typename VecT<VEC>::type;
   using Cfg = GatCfg<VEC, VPL, LPR>;
-  extern __shared__ float smem[];
+  extern __shared__ float smem[];  // [kGroups][2H] row statistics
   const int lig = threadIdx.x % LPR;
   const int group = threadIdx.x / LPR;
   const unsigned gmask = group_mask<LPR>();
 
-  if (static_cast<int>(blockIdx.x) < n_heavy) {
-    // ---- heavy row: the whole CTA.
-    float* red = smem;                                  // [kGroups * kTile]
-    float* stats = smem + Cfg::kGroups * Cfg::kTile;    // [2H]
-    float* scratch = stats + 2 * kMaxHeads;             // [32]
-    const int row = heavy_rows[blockIdx.x];
-    const int e0 = rowptr[row], e1 = rowptr[row + 1];
-    for (int h = 0; h < H; ++h) {
-      const float ad = attn_row[static_cast<int64_t>(row) * H + h];
-      float m = kNegInit;
-      for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
-        m = fmaxf(m, leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope));
-      m = block_max(m, scratch);
-      float s = 0.0f;
-      for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
-        s += expf(leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope) - m);
-      s = block_sum(s, scratch);
-      if (threadIdx.x == 0) {
-        stats[h] = m;
-        stats[H + h] = s;
-        emax[static_cast<int64_t>(row) * H + h] = m;
-        esum[static_cast<int64_t>(row) * H + h] = s;
-      }
-    }
-    __syncthreads();
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    const int64_t sidx = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + group;
+    if (sidx >= n_seg) return;
+    const int64_t row = seg_row[sidx];
+    const int e0 = seg_begin[sidx], e1 = seg_end[sidx];
     for (int64_t f0 = 0; f0 < C; f0 += Cfg::kTile) {
       V acc[VPL];
 #pragma unroll
       for (int q = 0; q < VPL; ++q) vzero(acc[q]);
-      gat_gather<VEC, VPL, LPR>(row, e0 + group * LPR, e1, Cfg::kGroups * LPR, H, C,
-                                f0, col, attn_row, attn_col, x, stats, slope, p,
-                                seed, lig, gmask, acc);
+      gat_gather<VEC, VPL, LPR>(row, e0, e1, H, C, f0, col, attn_row, attn_col, x,
+                                emax + row * H, esum + row * H, slope, p, seed, lig, gmask, acc);
 #pragma unroll
       for (int q = 0; q < VPL; ++q) {
-        const int fi = (lig + q * LPR) * VEC;
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) red[group * Cfg::kTile + fi + j] = vel(acc[q], j);
+        const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+        if (f0 + fi < C) st_vec(partial + sidx * C + f0 + fi, acc[q]);
       }
-      __syncthreads();
-      const float hf = static_cast<float>(H);
-      for (int fi = threadIdx.x; fi < Cfg::kTile; fi += kThreads) {
-        if (f0 + fi < C) {
-          float a = 0.0f;
-          for (int g = 0; g < Cfg::kGroups; ++g) a += red[g * Cfg::kTile + fi];
-          const float pj = a / hf + bias[f0 + fi];
-          const int64_t o = static_cast<int64_t>(row) * C + f0 + fi;
-          pre[o] = pj;
-          out[o] = silu_f(pj);
-        }
-      }
-      __syncthreads();
     }
     return;
   }
 
-  // ---- light rows: a group per row.
-  const int64_t row64 = static_cast<int64_t>(blockIdx.x - n_heavy) * Cfg::kGroups + group;
+  const int64_t row64 = static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
   if (row64 >= n) return;
-  const int row = static_cast<int>(row64);
-  const int e0 = rowptr[row], e1 = rowptr[row + 1];
-  if (e1 - e0 > kHeavy) return;
+  const int e0 = rowptr[row64], e1 = rowptr[row64 + 1];
+  if (e1 - e0 > kSegLen) return;  // hub row: stats, segments and combine kernels
   float* stats = smem + group * 2 * H;
   for (int h = 0; h < H; ++h) {
     const float ad = attn_row[row64 * H + h];
@@ -307,29 +274,89 @@ gat_fwd_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
     }
   }
   __syncwarp(gmask);
+  const float hf = static_cast<float>(H);
   for (int64_t f0 = 0; f0 < C; f0 += Cfg::kTile) {
     V acc[VPL];
 #pragma unroll
     for (int q = 0; q < VPL; ++q) vzero(acc[q]);
-    gat_gather<VEC, VPL, LPR>(row, e0, e1, LPR, H, C, f0, col, attn_row, attn_col,
-                              x, stats, slope, p, seed, lig, gmask, acc);
-    gat_store_out<VEC, VPL, LPR>(row64, C, f0, H, lig, acc, bias, pre, out);
+    gat_gather<VEC, VPL, LPR>(row64, e0, e1, H, C, f0, col, attn_row, attn_col, x, stats,
+                              stats + H, slope, p, seed, lig, gmask, acc);
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+      if (f0 + fi < C) {
+        V pv, ov;
+        const V bv = ldg_vec<VEC>(bias + f0 + fi);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float pj = vel(acc[q], j) / hf + vel(bv, j);
+          vel(pv, j) = pj;
+          vel(ov, j) = silu_f(pj);
+        }
+        st_vec(pre + row64 * C + f0 + fi, pv);
+        st_vec(out + row64 * C + f0 + fi, ov);
+      }
+    }
+  }
+}
+
+// One CTA per hub row: acc = sum of segment partials (segment order),
+// pre = acc / H + bias, out = SiLU(pre).
+__global__ void __launch_bounds__(kThreads)
+gat_fwd_combine_kernel(int H, int64_t C, const int* __restrict__ hub_row,
+                       const int* __restrict__ hub_first, const float* __restrict__ partial,
+                       const float* __restrict__ bias, float* __restrict__ pre,
+                       float* __restrict__ out) {
+  const int64_t row = hub_row[blockIdx.x];
+  const int s0 = hub_first[blockIdx.x], s1 = hub_first[blockIdx.x + 1];
+  const float hf = static_cast<float>(H);
+  for (int64_t c = threadIdx.x; c < C; c += kThreads) {
+    float a = 0.0f;
+    for (int s = s0; s < s1; ++s) a += partial[static_cast<int64_t>(s) * C + c];
+    const float pj = a / hf + bias[c];
+    pre[row * C + c] = pj;
+    out[row * C + c] = silu_f(pj);
   }
 }
 
 // ------------------------------------------------------------ backward K1
-// Per destination row.  Workspace: gpre [N*C], glog [nnz*H].
-// Phase A: dots d(e,h) = sum_c (g_pre[i,c]/H) x[j,h,c]  -> glog[e,h]
-// Phase B: softmax/dropout/LeakyReLU backward           -> glog[e,h], grad_attn_row
+// Loads grad_y/pre of one row tile, optionally writes g_pre (unscaled) and
+// returns g_pre / H in registers.
 template <int VEC, int VPL, int LPR>
-__device__ __forceinline__ void k1_dots(
-    int row, int start, int e1, int step, int H, int64_t C, int64_t f0,
-    bool first_tile, const int* __restrict__ col, const float* __restrict__ x,
-    typename VecT<VEC>::type (&g)[VPL], int lig, unsigned gmask,
-    float* __restrict__ glog) {
+__device__ __forceinline__ void k1_gpre(int64_t row, int64_t C, int64_t f0, int H, int lig,
+                                        bool write, const float* __restrict__ grad_y,
+                                        const float* __restrict__ pre, float* __restrict__ gpre,
+                                        typename VecT<VEC>::type (&g)[VPL]) {
+  const float inv_h = 1.0f / static_cast<float>(H);
+#pragma unroll
+  for (int q = 0; q < VPL; ++q) {
+    const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+    if (f0 + fi < C) {
+      const auto gy = ld_vec<VEC>(grad_y + row * C + f0 + fi);
+      const auto pr = ld_vec<VEC>(pre + row * C + f0 + fi);
+      typename VecT<VEC>::type gp;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) vel(gp, j) = vel(gy, j) * silu_grad_f(vel(pr, j));
+      if (write) st_vec(gpre + row * C + f0 + fi, gp);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) vel(g[q], j) = vel(gp, j) * inv_h;
+    } else {
+      vzero(g[q]);
+    }
+  }
+}
+
+// dots d(e,h) = sum_c g[c] x[col[e],h,c] over this tile for edges [e0, e1);
+// the lane owning edge e stores (first tile) or adds (later tiles) glog[e,h].
+template <int VEC, int VPL, int LPR>
+__device__ __forceinline__ void k1_dots(int e0, int e1, int H, int64_t C, int64_t f0,
+                                        bool first_tile, const int* __restrict__ col,
+                                        const float* __restrict__ x,
+                                        const typename VecT<VEC>::type (&g)[VPL], int lig,
+                                        unsigned gmask, float* __restrict__ glog) {
   using V = typename VecT<VEC>::type;
   const int64_t HC = static_cast<int64_t>(H) * C;
-  for (int base = start; base < e1; base += step) {
+  for (int base = e0; base < e1; base += LPR) {
     const int my = base + lig;
     const bool valid = my < e1;
     const int c = valid ? __ldg(col + my) : 0;
@@ -389,34 +416,6 @@ __device__ __forceinline__ void k1_dots(
   }
 }
 
-// Loads grad_y/pre of one row tile, writes g_pre (unscaled) and returns
-// g_pre / H in registers.
-template <int VEC, int VPL, int LPR>
-__device__ __forceinline__ void k1_gpre(int64_t row, int64_t C, int64_t f0, int H,
-                                        int lig, bool write,
-                                        const float* __restrict__ grad_y,
-                                        const float* __restrict__ pre,
-                                        float* __restrict__ gpre,
-                                        typename VecT<VEC>::type (&g)[VPL]) {
-  const float inv_h = 1.0f / static_cast<float>(H);
-#pragma unroll
-  for (int q = 0; q < VPL; ++q) {
-    const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
-    if (f0 + fi < C) {
-      const auto gy = ld_vec<VEC>(grad_y + row * C + f0 + fi);
-      const auto pr = ld_vec<VEC>(pre + row * C + f0 + fi);
-      typename VecT<VEC>::type gp;
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) vel(gp, j) = vel(gy, j) * silu_grad_f(vel(pr, j));
-      if (write) st_vec(gpre + row * C + f0 + fi, gp);
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) vel(g[q], j) = vel(gp, j) * inv_h;
-    } else {
-      vzero(g[q]);
-    }
-  }
-}
-
 // Softmax/dropout/LeakyReLU backward of one edge (reference
 // attention_backward_kernel, collapsed_gat_cuda.cu:362-430).
 struct EdgeSoft {
@@ -424,9 +423,8 @@ struct EdgeSoft {
   float ge;    // kept and rescaled upstream gradient of the weight
   bool neg;    // raw < 0 (LeakyReLU slope branch)
 };
-__device__ __forceinline__ EdgeSoft edge_soft(float ad, float ac, float m, float s,
-                                              float slope, float p, uint64_t seed,
-                                              uint64_t idx, float dot) {
+__device__ __forceinline__ EdgeSoft edge_soft(float ad, float ac, float m, float s, float slope,
+                                              float p, uint64_t seed, uint64_t idx, float dot) {
   EdgeSoft r;
   const float raw = ad + ac;
   r.neg = raw < 0.0f;
@@ -438,11 +436,14 @@ __device__ __forceinline__ EdgeSoft edge_soft(float ad, float ac, float m, float
   return r;
 }
 
+// Blocks [0, seg_blocks): hub-row segments compute their edges' dots;
+// remaining blocks: whole rows (g_pre, dots, softmax backward).
 template <int VEC, int VPL, int LPR>
 __global__ void __launch_bounds__(kThreads)
 gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
-                    const int* __restrict__ col, const int* __restrict__ heavy_rows,
-                    int n_heavy, const float* __restrict__ attn_row,
+                    const int* __restrict__ col, const int* __restrict__ seg_row,
+                    const int* __restrict__ seg_begin, const int* __restrict__ seg_end,
+                    int n_seg, int seg_blocks, const float* __restrict__ attn_row,
                     const float* __restrict__ attn_col, const float* __restrict__ x,
                     const float* __restrict__ pre, const float* __restrict__ emax,
                     const float* __restrict__ esum, const float* __restrict__ grad_y,
@@ -450,59 +451,31 @@ gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
                     float* __restrict__ glog, float* __restrict__ grad_attn_row) {
   using V = typename VecT<VEC>::type;
   using Cfg = GatCfg<VEC, VPL, LPR>;
-  __shared__ float scratch[32];
   const int lig = threadIdx.x % LPR;
   const int group = threadIdx.x / LPR;
   const unsigned gmask = group_mask<LPR>();
 
-  if (static_cast<int>(blockIdx.x) < n_heavy) {
-    const int row = heavy_rows[blockIdx.x];
-    const int64_t r64 = row;
-    const int e0 = rowptr[row], e1 = rowptr[row + 1];
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    const int64_t sidx = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + group;
+    if (sidx >= n_seg) return;
+    const int64_t row = seg_row[sidx];
+    const int e0 = seg_begin[sidx], e1 = seg_end[sidx];
     for (int64_t f0 = 0; f0 < C; f0 += Cfg::kTile) {
       V g[VPL];
-      k1_gpre<VEC, VPL, LPR>(r64, C, f0, H, lig, group == 0, grad_y, pre, gpre, g);
-      k1_dots<VEC, VPL, LPR>(row, e0 + group * LPR, e1, Cfg::kGroups * LPR, H, C, f0,
-                             f0 == 0, col, x, g, lig, gmask, glog);
-    }
-    __syncthreads();  // glog of this row written by many threads
-    for (int h = 0; h < H; ++h) {
-      const float ad = attn_row[r64 * H + h];
-      const float m = emax[r64 * H + h], s = esum[r64 * H + h];
-      float wsum = 0.0f;
-      for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
-        const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s,
-                                      slope, p, seed, static_cast<uint64_t>(e) * H + h,
-                                      glog[static_cast<int64_t>(e) * H + h]);
-        wsum += es.soft * es.ge;
-      }
-      wsum = block_sum(wsum, scratch);
-      float grow = 0.0f;
-      for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
-        const int64_t o = static_cast<int64_t>(e) * H + h;
-        const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s,
-                                      slope, p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
-        float gout = es.soft * (es.ge - wsum);
-        if (es.neg) gout *= slope;
-        glog[o] = gout;
-        grow += gout;
-      }
-      grow = block_sum(grow, scratch);
-      if (threadIdx.x == 0) grad_attn_row[r64 * H + h] = grow;
+      k1_gpre<VEC, VPL, LPR>(row, C, f0, H, lig, false, grad_y, pre, gpre, g);
+      k1_dots<VEC, VPL, LPR>(e0, e1, H, C, f0, f0 == 0, col, x, g, lig, gmask, glog);
     }
     return;
   }
 
-  const int64_t r64 = static_cast<int64_t>(blockIdx.x - n_heavy) * Cfg::kGroups + group;
+  const int64_t r64 = static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
   if (r64 >= n) return;
-  const int row = static_cast<int>(r64);
-  const int e0 = rowptr[row], e1 = rowptr[row + 1];
-  if (e1 - e0 > kHeavy) return;
+  const int e0 = rowptr[r64], e1 = rowptr[r64 + 1];
+  if (e1 - e0 > kSegLen) return;
   for (int64_t f0 = 0; f0 < C; f0 += Cfg::kTile) {
     V g[VPL];
     k1_gpre<VEC, VPL, LPR>(r64, C, f0, H, lig, true, grad_y, pre, gpre, g);
-    k1_dots<VEC, VPL, LPR>(row, e0, e1, LPR, H, C, f0, f0 == 0, col, x, g, lig,
-                           gmask, glog);
+    k1_dots<VEC, VPL, LPR>(e0, e1, H, C, f0, f0 == 0, col, x, g, lig, gmask, glog);
   }
   // Each lane re-reads only the glog entries it wrote itself (same
   // lane -> edge mapping), so no synchronisation is needed.
@@ -511,8 +484,8 @@ gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
     const float m = emax[r64 * H + h], s = esum[r64 * H + h];
     float wsum = 0.0f;
     for (int e = e0 + lig; e < e1; e += LPR) {
-      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s,
-                                    slope, p, seed, static_cast<uint64_t>(e) * H + h,
+      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
+                                    p, seed, static_cast<uint64_t>(e) * H + h,
                                     glog[static_cast<int64_t>(e) * H + h]);
       wsum += es.soft * es.ge;
     }
@@ -520,8 +493,8 @@ gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
     float grow = 0.0f;
     for (int e = e0 + lig; e < e1; e += LPR) {
       const int64_t o = static_cast<int64_t>(e) * H + h;
-      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s,
-                                    slope, p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
+      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
+                                    p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
       float gout = es.soft * (es.ge - wsum);
       if (es.neg) gout *= slope;
       glog[o] = gout;
@@ -532,22 +505,64 @@ gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
   }
 }
 
+// One CTA per hub row: write its g_pre row and run the softmax backward over
+// its edges (dots already in glog from the segment groups).
+__global__ void __launch_bounds__(kThreads)
+gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
+                        const int* __restrict__ col, const int* __restrict__ hub_row,
+                        const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                        const float* __restrict__ pre, const float* __restrict__ emax,
+                        const float* __restrict__ esum, const float* __restrict__ grad_y,
+                        float slope, float p, uint64_t seed, float* __restrict__ gpre,
+                        float* __restrict__ glog, float* __restrict__ grad_attn_row) {
+  __shared__ float scratch[32];
+  const int64_t row = hub_row[blockIdx.x];
+  for (int64_t c = threadIdx.x; c < C; c += kThreads)
+    gpre[row * C + c] = grad_y[row * C + c] * silu_grad_f(pre[row * C + c]);
+  const int e0 = rowptr[row], e1 = rowptr[row + 1];
+  for (int h = 0; h < H; ++h) {
+    const float ad = attn_row[row * H + h];
+    const float m = emax[row * H + h], s = esum[row * H + h];
+    float wsum = 0.0f;
+    for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
+      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
+                                    p, seed, static_cast<uint64_t>(e) * H + h,
+                                    glog[static_cast<int64_t>(e) * H + h]);
+      wsum += es.soft * es.ge;
+    }
+    wsum = block_sum(wsum, scratch);
+    float grow = 0.0f;
+    for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
+      const int64_t o = static_cast<int64_t>(e) * H + h;
+      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
+                                    p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
+      float gout = es.soft * (es.ge - wsum);
+      if (es.neg) gout *= slope;
+      glog[o] = gout;
+      grow += gout;
+    }
+    grow = block_sum(grow, scratch);
+    if (threadIdx.x == 0) grad_attn_row[row * H + h] = grow;
+  }
+}
+
 // ------------------------------------------------------------ backward K2
-// Per source column j over its in-edges (CSC):
-//   grad_feat[j,h,:] = sum w(e,h) * g_pre[i,:] / H;   grad_attn_col[j,h] = sum glog[e,h]
-// Heads are processed HB at a time so one gathered g_pre row feeds HB
-// accumulator tiles.
+// acc[hh] += w(e, h0+hh) / H * g_pre[row[pos], tile] over CSC positions
+// [p0, p1) of column j.
 template <int VEC, int VPL, int LPR, int HB>
-__device__ __forceinline__ void k2_gather(
-    int colj, int start, int p1, int step, int H, int h0, int64_t C, int64_t f0,
-    const int* __restrict__ row, const int* __restrict__ perm,
-    const float* __restrict__ attn_row, const float* __restrict__ attn_col,
-    const float* __restrict__ emax, const float* __restrict__ esum,
-    const float* __restrict__ gpre, float slope, float p, uint64_t seed,
-    int lig, unsigned gmask, typename VecT<VEC>::type (&acc)[HB][VPL]) {
+__device__ __forceinline__ void k2_gather(int64_t j, int p0, int p1, int H, int h0, int64_t C,
+                                          int64_t f0, const int* __restrict__ row,
+                                          const int* __restrict__ perm,
+                                          const float* __restrict__ attn_row,
+                                          const float* __restrict__ attn_col,
+                                          const float* __restrict__ emax,
+                                          const float* __restrict__ esum,
+                                          const float* __restrict__ gpre, float slope, float p,
+                                          uint64_t seed, int lig, unsigned gmask,
+                                          typename VecT<VEC>::type (&acc)[HB][VPL]) {
   using V = typename VecT<VEC>::type;
   const float inv_h = 1.0f / static_cast<float>(H);
-  for (int base = start; base < p1; base += step) {
+  for (int base = p0; base < p1; base += LPR) {
     const int pos = base + lig;
     const bool valid = pos < p1;
     int i = 0;
@@ -562,9 +577,8 @@ __device__ __forceinline__ void k2_gather(
         const int h = h0 + hh;
         if (h < H) {
           const int64_t ih = static_cast<int64_t>(i) * H + h;
-          w[hh] = edge_weight(__ldg(attn_row + ih),
-                              __ldg(attn_col + static_cast<int64_t>(colj) * H + h),
-                              __ldg(emax + ih), __ldg(esum + ih), slope, p, seed,
+          w[hh] = edge_weight(__ldg(attn_row + ih), __ldg(attn_col + j * H + h), __ldg(emax + ih),
+                              __ldg(esum + ih), slope, p, seed,
                               static_cast<uint64_t>(e) * H + h) * inv_h;
         }
       }
@@ -618,83 +632,57 @@ __device__ __forceinline__ void k2_gather(
   }
 }
 
+// Blocks [0, seg_blocks): hub-column segments -> partial grad_feat
+// [n_seg, H*C] and partial grad_attn_col [n_seg, H]; remaining blocks:
+// whole columns.
 template <int VEC, int VPL, int LPR, int HB>
 __global__ void __launch_bounds__(kThreads)
 gat_bwd_cols_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
                     const int* __restrict__ row, const int* __restrict__ perm,
-                    const int* __restrict__ heavy_cols, int n_heavy,
-                    const float* __restrict__ attn_row,
-                    const float* __restrict__ attn_col, const float* __restrict__ emax,
-                    const float* __restrict__ esum, const float* __restrict__ gpre,
-                    const float* __restrict__ glog, float slope, float p, uint64_t seed,
-                    float* __restrict__ grad_feat, float* __restrict__ grad_attn_col) {
+                    const int* __restrict__ seg_col, const int* __restrict__ seg_begin,
+                    const int* __restrict__ seg_end, int n_seg, int seg_blocks,
+                    const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                    const float* __restrict__ emax, const float* __restrict__ esum,
+                    const float* __restrict__ gpre, const float* __restrict__ glog,
+                    float slope, float p, uint64_t seed, float* __restrict__ grad_feat,
+                    float* __restrict__ grad_attn_col, float* __restrict__ pfeat,
+                    float* __restrict__ pcol) {
   using V = typename VecT<VEC>::type;
   using Cfg = GatCfg<VEC, VPL, LPR>;
-  extern __shared__ float smem[];
   const int lig = threadIdx.x % LPR;
   const int group = threadIdx.x / LPR;
   const unsigned gmask = group_mask<LPR>();
   const int64_t HC = static_cast<int64_t>(H) * C;
 
-  if (static_cast<int>(blockIdx.x) < n_heavy) {
-    float* red = smem;  // [kGroups * kTile]
-    float* scratch = smem + Cfg::kGroups * Cfg::kTile;
-    const int j = heavy_cols[blockIdx.x];
-    const int64_t j64 = j;
-    const int p0 = colptr[j], p1 = colptr[j + 1];
-    for (int h = 0; h < H; ++h) {
-      float a = 0.0f;
-      for (int pos = p0 + threadIdx.x; pos < p1; pos += kThreads)
-        a += glog[static_cast<int64_t>(perm[pos]) * H + h];
-      a = block_sum(a, scratch);
-      if (threadIdx.x == 0) grad_attn_col[j64 * H + h] = a;
-    }
-    for (int h0 = 0; h0 < H; h0 += HB) {
-      for (int64_t f0 = 0; f0 < C; f0 += Cfg::kTile) {
-        V acc[HB][VPL];
-#pragma unroll
-        for (int hh = 0; hh < HB; ++hh)
-#pragma unroll
-          for (int q = 0; q < VPL; ++q) vzero(acc[hh][q]);
-        k2_gather<VEC, VPL, LPR, HB>(j, p0 + group * LPR, p1, Cfg::kGroups * LPR, H, h0,
-                                     C, f0, row, perm, attn_row, attn_col, emax, esum,
-                                     gpre, slope, p, seed, lig, gmask, acc);
-#pragma unroll
-        for (int hh = 0; hh < HB; ++hh) {
-          __syncthreads();
-#pragma unroll
-          for (int q = 0; q < VPL; ++q) {
-            const int fi = (lig + q * LPR) * VEC;
-#pragma unroll
-            for (int jj = 0; jj < VEC; ++jj) red[group * Cfg::kTile + fi + jj] = vel(acc[hh][q], jj);
-          }
-          __syncthreads();
-          if (h0 + hh < H) {
-            for (int fi = threadIdx.x; fi < Cfg::kTile; fi += kThreads) {
-              if (f0 + fi < C) {
-                float a = 0.0f;
-                for (int g = 0; g < Cfg::kGroups; ++g) a += red[g * Cfg::kTile + fi];
-                grad_feat[j64 * HC + static_cast<int64_t>(h0 + hh) * C + f0 + fi] = a;
-              }
-            }
-          }
-        }
-      }
-    }
-    return;
+  int64_t j64, out_idx;
+  int p0, p1;
+  float* fdst;
+  float* cdst;
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    const int64_t sidx = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + group;
+    if (sidx >= n_seg) return;
+    j64 = seg_col[sidx];
+    p0 = seg_begin[sidx];
+    p1 = seg_end[sidx];
+    out_idx = sidx;
+    fdst = pfeat;
+    cdst = pcol;
+  } else {
+    j64 = static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
+    if (j64 >= n) return;
+    p0 = colptr[j64];
+    p1 = colptr[j64 + 1];
+    if (p1 - p0 > kSegLen) return;  // hub column: segments + combine
+    out_idx = j64;
+    fdst = grad_feat;
+    cdst = grad_attn_col;
   }
-
-  const int64_t j64 = static_cast<int64_t>(blockIdx.x - n_heavy) * Cfg::kGroups + group;
-  if (j64 >= n) return;
-  const int j = static_cast<int>(j64);
-  const int p0 = colptr[j], p1 = colptr[j + 1];
-  if (p1 - p0 > kHeavy) return;
   for (int h = 0; h < H; ++h) {
     float a = 0.0f;
     for (int pos = p0 + lig; pos < p1; pos += LPR)
       a += glog[static_cast<int64_t>(perm[pos]) * H + h];
     a = group_sum<LPR>(a, gmask);
-    if (lig == 0) grad_attn_col[j64 * H + h] = a;
+    if (lig == 0) cdst[out_idx * H + h] = a;
   }
   for (int h0 = 0; h0 < H; h0 += HB) {
     for (int64_t f0 = 0; f0 < C; f0 += Cfg::kTile) {
@@ -703,9 +691,8 @@ gat_bwd_cols_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
       for (int hh = 0; hh < HB; ++hh)
 #pragma unroll
         for (int q = 0; q < VPL; ++q) vzero(acc[hh][q]);
-      k2_gather<VEC, VPL, LPR, HB>(j, p0, p1, LPR, H, h0, C, f0, row, perm, attn_row,
-                                   attn_col, emax, esum, gpre, slope, p, seed, lig,
-                                   gmask, acc);
+      k2_gather<VEC, VPL, LPR, HB>(j64, p0, p1, H, h0, C, f0, row, perm, attn_row, attn_col, emax,
+                                   esum, gpre, slope, p, seed, lig, gmask, acc);
 #pragma unroll
       for (int hh = 0; hh < HB; ++hh) {
         if (h0 + hh >= H) break;
@@ -713,11 +700,31 @@ gat_bwd_cols_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
         for (int q = 0; q < VPL; ++q) {
           const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
           if (f0 + fi < C)
-            st_vec(grad_feat + j64 * HC + static_cast<int64_t>(h0 + hh) * C + f0 + fi,
-                   acc[hh][q]);
+            st_vec(fdst + out_idx * HC + static_cast<int64_t>(h0 + hh) * C + f0 + fi, acc[hh][q]);
         }
       }
     }
+  }
+}
+
+// One CTA per hub column: sum the segment partials in segment order.
+__global__ void __launch_bounds__(kThreads)
+gat_bwd_cols_combine_kernel(int H, int64_t C, const int* __restrict__ hub_col,
+                            const int* __restrict__ hub_first, const float* __restrict__ pfeat,
+                            const float* __restrict__ pcol, float* __restrict__ grad_feat,
+                            float* __restrict__ grad_attn_col) {
+  const int64_t j = hub_col[blockIdx.x];
+  const int s0 = hub_first[blockIdx.x], s1 = hub_first[blockIdx.x + 1];
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  for (int64_t k = threadIdx.x; k < HC; k += kThreads) {
+    float a = 0.0f;
+    for (int s = s0; s < s1; ++s) a += pfeat[static_cast<int64_t>(s) * HC + k];
+    grad_feat[j * HC + k] = a;
+  }
+  for (int h = threadIdx.x; h < H; h += kThreads) {
+    float a = 0.0f;
+    for (int s = s0; s < s1; ++s) a += pcol[static_cast<int64_t>(s) * H + h];
+    grad_attn_col[j * H + h] = a;
   }
 }
 
@@ -725,17 +732,14 @@ gat_bwd_cols_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
 __global__ void gat_mask_kernel(int64_t total, float p, uint64_t seed,
                                 uint8_t* __restrict__ mask) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-       i < total; i += stride)
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride)
     mask[i] = gat_keep(seed, static_cast<uint64_t>(i), p) ? 1 : 0;
 }
 
-__global__ void gat_validate_kernel(int64_t n, int64_t nnz,
-                                    const int* __restrict__ rowptr,
-                                    const int* __restrict__ col,
-                                    const int* __restrict__ colptr,
-                                    const int* __restrict__ row,
-                                    const int* __restrict__ perm,
+__global__ void gat_validate_kernel(int64_t n, int64_t nnz, const int* __restrict__ rowptr,
+                                    const int* __restrict__ col, const int* __restrict__ colptr,
+                                    const int* __restrict__ row, const int* __restrict__ perm,
                                     int* __restrict__ bad) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -750,11 +754,10 @@ __global__ void gat_validate_kernel(int64_t n, int64_t nnz,
     if (r < 0 || r >= n) { atomicOr(bad, 8); continue; }
     const int pe = perm[e];
     if (pe < 0 || pe >= nnz) { atomicOr(bad, 16); continue; }
-    // The CSR edge perm[e] must start at row r (it lies inside r's range).
+    // The CSR edge perm[e] must lie in row r's CSR range.
     if (pe < rowptr[r] || pe >= rowptr[r + 1]) atomicOr(bad, 32);
   }
-  // CSC position e must belong to the column col[perm[e]]: checked by
-  // comparing each column's range against the column ids of its edges.
+  // CSC position pos of column j must map to a CSR edge whose column is j.
   for (int64_t j = t0; j < n; j += stride) {
     const int lo = max(colptr[j], 0);
     const int hi = min(static_cast<int64_t>(colptr[j + 1]), nnz);
@@ -770,93 +773,92 @@ __global__ void gat_validate_kernel(int64_t n, int64_t nnz,
 }
 
 // ------------------------------------------------------------ dispatch
-struct GatArgs {
-  const cign_gat_plan* plan;
-  int H;
-  int64_t C;
-};
-
-size_t fwd_smem_bytes(int kgroups, int ktile, int H) {
-  const size_t heavy = (static_cast<size_t>(kgroups) * ktile + 2 * kMaxHeads + 32) * sizeof(float);
-  const size_t light = static_cast<size_t>(kgroups) * 2 * H * sizeof(float);
-  return std::max(heavy, light);
-}
-
-template <typename K>
-int set_smem(K kernel, size_t bytes) {
-  if (bytes > 48 * 1024) {
-    CIGN_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(bytes)),
-                    "gat: set smem");
-  }
-  return CIGN_OK;
-}
+size_t rnd(size_t b) { return (b + 255) / 256 * 256; }
 
 template <int VEC, int VPL, int LPR>
 int launch_fwd_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
-                   const float* attn_col, const float* x, const float* bias,
-                   float slope, float p, uint64_t seed, float* out, float* pre,
-                   float* emax, float* esum, cudaStream_t s) {
+                   const float* attn_col, const float* x, const float* bias, float slope, float p,
+                   uint64_t seed, float* out, float* pre, float* emax, float* esum, float* partial,
+                   cudaStream_t s) {
   using Cfg = GatCfg<VEC, VPL, LPR>;
-  const int64_t grid = pl->n_heavy_rows + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
-  if (grid == 0) return CIGN_OK;
-  const size_t smem = fwd_smem_bytes(Cfg::kGroups, Cfg::kTile, H);
-  int rc = set_smem(gat_fwd_kernel<VEC, VPL, LPR>, smem);
-  if (rc) return rc;
+  const SegList& sl = pl->rows;
+  if (sl.n_heavy > 0) {
+    gat_hub_stats_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
+        H, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, slope, emax, esum);
+    CIGN_CHECK_LAUNCH("gat_hub_stats_kernel");
+  }
+  const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = seg_blocks + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
+  const size_t smem = static_cast<size_t>(Cfg::kGroups) * 2 * H * sizeof(float);
   gat_fwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(
-      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, pl->heavy_rows,
-      static_cast<int>(pl->n_heavy_rows), attn_row, attn_col, x, bias, slope, p, seed,
-      out, pre, emax, esum);
+      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
+      x, bias, slope, p, seed, out, pre, emax, esum, partial);
   CIGN_CHECK_LAUNCH("gat_fwd_kernel");
+  if (sl.n_heavy > 0) {
+    gat_fwd_combine_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
+        H, C, sl.heavy_row(), sl.heavy_first(), partial, bias, pre, out);
+    CIGN_CHECK_LAUNCH("gat_fwd_combine_kernel");
+  }
   return CIGN_OK;
 }
 
 template <int VEC, int VPL, int LPR>
 int launch_bwd_rows_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                         const float* attn_col, const float* x, const float* pre,
-                        const float* emax, const float* esum, const float* gy,
-                        float slope, float p, uint64_t seed, float* gpre, float* glog,
-                        float* grow, cudaStream_t s) {
+                        const float* emax, const float* esum, const float* gy, float slope,
+                        float p, uint64_t seed, float* gpre, float* glog, float* grow,
+                        cudaStream_t s) {
   using Cfg = GatCfg<VEC, VPL, LPR>;
-  const int64_t grid = pl->n_heavy_rows + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
-  if (grid == 0) return CIGN_OK;
+  const SegList& sl = pl->rows;
+  const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = seg_blocks + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
   gat_bwd_rows_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
-      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, pl->heavy_rows,
-      static_cast<int>(pl->n_heavy_rows), attn_row, attn_col, x, pre, emax, esum, gy,
-      slope, p, seed, gpre, glog, grow);
+      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
+      x, pre, emax, esum, gy, slope, p, seed, gpre, glog, grow);
   CIGN_CHECK_LAUNCH("gat_bwd_rows_kernel");
+  if (sl.n_heavy > 0) {
+    gat_bwd_hub_rows_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
+        H, C, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, pre, emax, esum, gy, slope,
+        p, seed, gpre, glog, grow);
+    CIGN_CHECK_LAUNCH("gat_bwd_hub_rows_kernel");
+  }
   return CIGN_OK;
 }
 
 template <int VEC, int VPL, int LPR, int HB>
 int launch_bwd_cols_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                         const float* attn_col, const float* emax, const float* esum,
-                        const float* gpre, const float* glog, float slope, float p,
-                        uint64_t seed, float* gfeat, float* gcol, cudaStream_t s) {
+                        const float* gpre, const float* glog, float slope, float p, uint64_t seed,
+                        float* gfeat, float* gcol, float* pfeat, float* pcol, cudaStream_t s) {
   using Cfg = GatCfg<VEC, VPL, LPR>;
-  const int64_t grid = pl->n_heavy_cols + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
-  if (grid == 0) return CIGN_OK;
-  const size_t smem = (static_cast<size_t>(Cfg::kGroups) * Cfg::kTile + 32) * sizeof(float);
-  int rc = set_smem(gat_bwd_cols_kernel<VEC, VPL, LPR, HB>, smem);
-  if (rc) return rc;
-  gat_bwd_cols_kernel<VEC, VPL, LPR, HB><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(
-      static_cast<int>(pl->n), H, C, pl->colptr, pl->row, pl->perm, pl->heavy_cols,
-      static_cast<int>(pl->n_heavy_cols), attn_row, attn_col, emax, esum, gpre, glog,
-      slope, p, seed, gfeat, gcol);
+  const SegList& sl = pl->cols;
+  const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = seg_blocks + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
+  gat_bwd_cols_kernel<VEC, VPL, LPR, HB><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      static_cast<int>(pl->n), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
+      emax, esum, gpre, glog, slope, p, seed, gfeat, gcol, pfeat, pcol);
   CIGN_CHECK_LAUNCH("gat_bwd_cols_kernel");
+  if (sl.n_heavy > 0) {
+    gat_bwd_cols_combine_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
+        H, C, sl.heavy_row(), sl.heavy_first(), pfeat, pcol, gfeat, gcol);
+    CIGN_CHECK_LAUNCH("gat_bwd_cols_combine_kernel");
+  }
   return CIGN_OK;
 }
 
-// Shape rule shared by the three kernels: VEC=4 when C%4==0 and the feature
+// Shape rule shared by the kernels: VEC=4 when C%4==0 and the feature
 // pointers are 16-byte aligned; LPR/VPL from the number of vectors per row.
-#define CIGN_GAT_DISPATCH(VEC_, FV_, CALL)                      \
-  do {                                                          \
-    if ((FV_) <= 8) { constexpr int V_ = VEC_, P_ = 1, L_ = 8; CALL; }        \
-    else if ((FV_) <= 16) { constexpr int V_ = VEC_, P_ = 1, L_ = 16; CALL; } \
-    else if ((FV_) <= 32) { constexpr int V_ = VEC_, P_ = 1, L_ = 32; CALL; } \
-    else if ((FV_) <= 64) { constexpr int V_ = VEC_, P_ = 2, L_ = 32; CALL; } \
-    else if ((FV_) <= 128) { constexpr int V_ = VEC_, P_ = 4, L_ = 32; CALL; }\
-    else { constexpr int V_ = VEC_, P_ = 8, L_ = 32; CALL; }                  \
+#define CIGN_GAT_DISPATCH(VEC_, FV_, CALL)                                     \
+  do {                                                                         \
+    if ((FV_) <= 8) { constexpr int V_ = VEC_, P_ = 1, L_ = 8; CALL; }         \
+    else if ((FV_) <= 16) { constexpr int V_ = VEC_, P_ = 1, L_ = 16; CALL; }  \
+    else if ((FV_) <= 32) { constexpr int V_ = VEC_, P_ = 1, L_ = 32; CALL; }  \
+    else if ((FV_) <= 64) { constexpr int V_ = VEC_, P_ = 2, L_ = 32; CALL; }  \
+    else if ((FV_) <= 128) { constexpr int V_ = VEC_, P_ = 4, L_ = 32; CALL; } \
+    else { constexpr int V_ = VEC_, P_ = 8, L_ = 32; CALL; }                   \
   } while (0)
 
 int check_plan(const cign_gat_plan* pl, int H, int64_t C, const char* name) {
@@ -868,6 +870,26 @@ int check_plan(const cign_gat_plan* pl, int H, int64_t C, const char* name) {
   return CIGN_OK;
 }
 
+size_t fwd_ws_bytes(const cign_gat_plan* pl, int64_t C) {
+  return rnd(static_cast<size_t>(pl->rows.n_seg) * C * sizeof(float));
+}
+
+// backward workspace: g_pre [N*C] | grad_logit [nnz*H] | colsum partials |
+// column-segment partials [n_seg*(H*C)] | [n_seg*H]
+struct BwdLayout {
+  size_t gpre, glog, csum, pfeat, pcol, total;
+};
+BwdLayout bwd_layout(const cign_gat_plan* pl, int H, int64_t C) {
+  BwdLayout L;
+  L.gpre = 0;
+  L.glog = L.gpre + rnd(static_cast<size_t>(pl->n) * C * sizeof(float));
+  L.csum = L.glog + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float));
+  L.pfeat = L.csum + rnd(static_cast<size_t>(colsum_chunks(pl->n)) * C * sizeof(float));
+  L.pcol = L.pfeat + rnd(static_cast<size_t>(pl->cols.n_seg) * H * C * sizeof(float));
+  L.total = L.pcol + rnd(static_cast<size_t>(pl->cols.n_seg) * H * sizeof(float));
+  return L;
+}
+
 }  // namespace
 }  // namespace cign
 
@@ -875,9 +897,8 @@ using namespace cign;
 
 extern "C" {
 
-int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr,
-                         const int32_t* col, const int32_t* colptr,
-                         const int32_t* row, const int32_t* perm,
+int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr, const int32_t* col,
+                         const int32_t* colptr, const int32_t* row, const int32_t* perm,
                          cign_gat_plan** out) {
   CIGN_REQUIRE(out != nullptr, CIGN_ERR_NULL_POINTER, "gat_plan_create: out is NULL");
   *out = nullptr;
@@ -901,9 +922,9 @@ int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr,
     return set_error(CIGN_ERR_CUDA, "gat_plan_create: validation failed: %s",
                      cudaGetErrorString(le != cudaSuccess ? le : ce));
   CIGN_REQUIRE(bad == 0, CIGN_ERR_INVALID_ARGUMENT,
-               "gat_plan_create: malformed graph (code 0x%x: 1/2 pointer arrays not "
-               "monotone, 4/8 index out of range, 16/32/64 perm inconsistent with "
-               "CSR/CSC, 128/256 pointer ends)", bad);
+               "gat_plan_create: malformed graph (code 0x%x: 1/2 pointer arrays not monotone, "
+               "4/8 index out of range, 16/32/64 perm inconsistent with CSR/CSC, 128/256 "
+               "pointer ends)", bad);
   cign_gat_plan* pl = new cign_gat_plan();
   pl->n = n;
   pl->nnz = nnz;
@@ -912,16 +933,12 @@ int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr,
   pl->colptr = colptr;
   pl->row = row;
   pl->perm = perm;
-  pl->heavy_rows = pl->heavy_cols = nullptr;
   cudaGetDevice(&pl->device);
-  int rc = build_heavy_list(rowptr, n, kHeavy, &pl->heavy_rows, &pl->n_heavy_rows,
-                            &pl->max_row_len);
-  if (rc == CIGN_OK)
-    rc = build_heavy_list(colptr, n, kHeavy, &pl->heavy_cols, &pl->n_heavy_cols,
-                          &pl->max_col_len);
+  int rc = build_segments(rowptr, n, kSegLen, &pl->rows);
+  if (rc == CIGN_OK) rc = build_segments(colptr, n, kSegLen, &pl->cols);
   if (rc != CIGN_OK) {
-    if (pl->heavy_rows) cudaFree(pl->heavy_rows);
-    if (pl->heavy_cols) cudaFree(pl->heavy_cols);
+    free_segments(&pl->rows);
+    free_segments(&pl->cols);
     delete pl;
     return rc;
   }
@@ -935,30 +952,37 @@ int cign_gat_plan_destroy(cign_gat_plan* pl) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(pl->device);
-  if (pl->heavy_rows) cudaFree(pl->heavy_rows);
-  if (pl->heavy_cols) cudaFree(pl->heavy_cols);
+  free_segments(&pl->rows);
+  free_segments(&pl->cols);
   cudaSetDevice(prev);
   delete pl;
   return CIGN_OK;
 }
 
-int cign_gat_plan_get_info(const cign_gat_plan* pl, int64_t* info /* host [6] */) {
+int cign_gat_plan_get_info(const cign_gat_plan* pl, int64_t* info) {
   CIGN_REQUIRE(pl != nullptr && info != nullptr, CIGN_ERR_NULL_POINTER,
                "gat_plan_get_info: NULL argument");
   info[0] = pl->n;
   info[1] = pl->nnz;
-  info[2] = pl->n_heavy_rows;
-  info[3] = pl->n_heavy_cols;
-  info[4] = pl->max_row_len;
-  info[5] = pl->max_col_len;
+  info[2] = pl->rows.n_heavy;
+  info[3] = pl->cols.n_heavy;
+  info[4] = pl->rows.max_len;
+  info[5] = pl->cols.max_len;
+  info[6] = pl->rows.n_seg;
+  info[7] = pl->cols.n_seg;
   return CIGN_OK;
 }
 
-int cign_gat_fwd(const cign_gat_plan* pl, int32_t heads, int32_t channels,
-                 const float* attn_row, const float* attn_col, const float* in_feat,
-                 const float* bias, float negative_slope, float attn_drop,
-                 uint64_t seed, float* out, float* pre, float* edge_max,
-                 float* edge_sum, cign_stream_t stream) {
+size_t cign_gat_fwd_workspace_bytes(const cign_gat_plan* pl, int32_t heads, int32_t channels) {
+  if (pl == nullptr || channels <= 0) return 0;
+  return fwd_ws_bytes(pl, channels);
+}
+
+int cign_gat_fwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const float* attn_row,
+                 const float* attn_col, const float* in_feat, const float* bias,
+                 float negative_slope, float attn_drop, uint64_t seed, float* out, float* pre,
+                 float* edge_max, float* edge_sum, void* ws, size_t ws_bytes,
+                 cign_stream_t stream) {
   int rc = check_plan(pl, heads, channels, "gat_fwd");
   if (rc) return rc;
   CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
@@ -966,36 +990,32 @@ int cign_gat_fwd(const cign_gat_plan* pl, int32_t heads, int32_t channels,
   if (pl->n == 0) return CIGN_OK;
   CIGN_REQUIRE(attn_row && attn_col && in_feat && bias && out && pre && edge_max && edge_sum,
                CIGN_ERR_NULL_POINTER, "gat_fwd: NULL tensor argument");
+  const size_t need = fwd_ws_bytes(pl, channels);
+  CIGN_REQUIRE(ws_bytes >= need && (need == 0 || ws != nullptr), CIGN_ERR_INVALID_ARGUMENT,
+               "gat_fwd: workspace too small (%zu < %zu bytes)", ws_bytes, need);
   const int64_t C = channels;
+  float* partial = static_cast<float*>(ws);
   const bool v4 = C % 4 == 0 && aligned16(in_feat) && aligned16(out) && aligned16(pre) &&
-                  aligned16(bias);
+                  aligned16(bias) && aligned16(partial);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (v4) {
-    CIGN_GAT_DISPATCH(4, C / 4, return (launch_fwd_cfg<V_, P_, L_>(pl, heads, C, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed, out, pre, edge_max, edge_sum, s)));
+    CIGN_GAT_DISPATCH(4, C / 4, return (launch_fwd_cfg<V_, P_, L_>(pl, heads, C, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed, out, pre, edge_max, edge_sum, partial, s)));
   }
-  CIGN_GAT_DISPATCH(1, C, return (launch_fwd_cfg<V_, P_, L_>(pl, heads, C, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed, out, pre, edge_max, edge_sum, s)));
+  CIGN_GAT_DISPATCH(1, C, return (launch_fwd_cfg<V_, P_, L_>(pl, heads, C, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed, out, pre, edge_max, edge_sum, partial, s)));
   return CIGN_OK;
 }
 
-size_t cign_gat_bwd_workspace_bytes(const cign_gat_plan* pl, int32_t heads,
-                                    int32_t channels) {
-  if (pl == nullptr) return 0;
-  const int64_t C = channels;
-  const int64_t chunks = colsum_chunks(pl->n);
-  // g_pre [N*C] + grad_logit [nnz*H] + column-sum partials [chunks*C], each
-  // rounded to 256 bytes.
-  auto r = [](size_t b) { return (b + 255) / 256 * 256; };
-  return r(pl->n * C * sizeof(float)) + r(pl->nnz * heads * sizeof(float)) +
-         r(chunks * C * sizeof(float));
+size_t cign_gat_bwd_workspace_bytes(const cign_gat_plan* pl, int32_t heads, int32_t channels) {
+  if (pl == nullptr || heads <= 0 || channels <= 0) return 0;
+  return bwd_layout(pl, heads, channels).total;
 }
 
-int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels,
-                 const float* attn_row, const float* attn_col, const float* in_feat,
-                 const float* pre, const float* edge_max, const float* edge_sum,
-                 const float* grad_y, float negative_slope, float attn_drop,
-                 uint64_t seed, float* grad_feat, float* grad_attn_row,
-                 float* grad_attn_col, float* grad_bias, void* ws, size_t ws_bytes,
-                 cign_stream_t stream) {
+int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const float* attn_row,
+                 const float* attn_col, const float* in_feat, const float* pre,
+                 const float* edge_max, const float* edge_sum, const float* grad_y,
+                 float negative_slope, float attn_drop, uint64_t seed, float* grad_feat,
+                 float* grad_attn_row, float* grad_attn_col, float* grad_bias, void* ws,
+                 size_t ws_bytes, cign_stream_t stream) {
   int rc = check_plan(pl, heads, channels, "gat_bwd");
   if (rc) return rc;
   CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
@@ -1006,16 +1026,16 @@ int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels,
   CIGN_REQUIRE(attn_row && attn_col && in_feat && pre && edge_max && edge_sum && grad_y &&
                    grad_feat && grad_attn_row && grad_attn_col && grad_bias,
                CIGN_ERR_NULL_POINTER, "gat_bwd: NULL tensor argument");
-  const size_t need = cign_gat_bwd_workspace_bytes(pl, heads, channels);
-  CIGN_REQUIRE(ws != nullptr && ws_bytes >= need, CIGN_ERR_INVALID_ARGUMENT,
-               "gat_bwd: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  const BwdLayout L = bwd_layout(pl, heads, C);
+  CIGN_REQUIRE(ws != nullptr && ws_bytes >= L.total, CIGN_ERR_INVALID_ARGUMENT,
+               "gat_bwd: workspace too small (%zu < %zu bytes)", ws_bytes, L.total);
   CIGN_REQUIRE(aligned16(ws), CIGN_ERR_ALIGNMENT, "gat_bwd: ws must be 16-byte aligned");
-  auto r = [](size_t b) { return (b + 255) / 256 * 256; };
   char* w = static_cast<char*>(ws);
-  float* gpre = reinterpret_cast<float*>(w);
-  float* glog = reinterpret_cast<float*>(w + r(pl->n * C * sizeof(float)));
-  float* partial = reinterpret_cast<float*>(w + r(pl->n * C * sizeof(float)) +
-                                            r(pl->nnz * heads * sizeof(float)));
+  float* gpre = reinterpret_cast<float*>(w + L.gpre);
+  float* glog = reinterpret_cast<float*>(w + L.glog);
+  float* csum = reinterpret_cast<float*>(w + L.csum);
+  float* pfeat = reinterpret_cast<float*>(w + L.pfeat);
+  float* pcol = reinterpret_cast<float*>(w + L.pcol);
   const bool v4 = C % 4 == 0 && aligned16(in_feat) && aligned16(pre) && aligned16(grad_y) &&
                   aligned16(grad_feat);
   if (v4) {
@@ -1028,15 +1048,15 @@ int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels,
   if (v4) {
     const int64_t fv = C / 4;
     if (fv > 128) {
-      CIGN_GAT_DISPATCH(4, fv, rc = (launch_bwd_cols_cfg<V_, P_, L_, 2>(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog, negative_slope, attn_drop, seed, grad_feat, grad_attn_col, s)));
+      CIGN_GAT_DISPATCH(4, fv, rc = (launch_bwd_cols_cfg<V_, P_, L_, 2>(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog, negative_slope, attn_drop, seed, grad_feat, grad_attn_col, pfeat, pcol, s)));
     } else {
-      CIGN_GAT_DISPATCH(4, fv, rc = (launch_bwd_cols_cfg<V_, P_, L_, 4>(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog, negative_slope, attn_drop, seed, grad_feat, grad_attn_col, s)));
+      CIGN_GAT_DISPATCH(4, fv, rc = (launch_bwd_cols_cfg<V_, P_, L_, 4>(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog, negative_slope, attn_drop, seed, grad_feat, grad_attn_col, pfeat, pcol, s)));
     }
   } else {
-    CIGN_GAT_DISPATCH(1, C, rc = (launch_bwd_cols_cfg<V_, P_, L_, 2>(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog, negative_slope, attn_drop, seed, grad_feat, grad_attn_col, s)));
+    CIGN_GAT_DISPATCH(1, C, rc = (launch_bwd_cols_cfg<V_, P_, L_, 2>(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog, negative_slope, attn_drop, seed, grad_feat, grad_attn_col, pfeat, pcol, s)));
   }
   if (rc) return rc;
-  return colsum_f32(gpre, pl->n, C, partial, grad_bias, s);
+  return colsum_f32(gpre, pl->n, C, csum, grad_bias, s);
 }
 
 int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop, uint64_t seed,
@@ -1046,7 +1066,8 @@ int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop, uint64_t 
   if (total == 0) return CIGN_OK;
   CIGN_REQUIRE(mask != nullptr, CIGN_ERR_NULL_POINTER, "gat_dropout_mask: mask is NULL");
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 65535));
-  gat_mask_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(total, attn_drop, seed, mask);
+  gat_mask_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(total, attn_drop, seed,
+                                                                         mask);
   CIGN_CHECK_LAUNCH("gat_mask_kernel");
   return CIGN_OK;
 }

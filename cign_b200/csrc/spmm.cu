@@ -8,11 +8,12 @@
 //     lane-parallel (coalesced) and broadcast with shuffles; each edge then
 //     costs LPR*VPL vector loads of the neighbour's feature row, issued two
 //     to four edges at a time for memory-level parallelism.
-//   * Power-law graphs have hub rows.  Rows with more than kHeavyThreshold
-//     non-zeros are listed at plan time (sorted by degree, descending) and
-//     processed first, one 256-thread CTA per row: its groups split the
-//     row's edges and combine their partial tiles through shared memory in a
-//     fixed order, so the result is deterministic and independent of timing.
+//   * Power-law graphs have hub rows (thousands of non-zeros).  Rows with
+//     more than kSegLen non-zeros are cut at plan time into segments of
+//     kSegLen edges; every segment is one group's work item (scheduled
+//     first), writing a partial tile to the workspace, and a combine kernel
+//     sums each hub row's partials in segment order.  The work per group is
+//     thus bounded by kSegLen edges and the result is deterministic.
 //   * The backward "+ g" of the hop chain is the SpMM epilogue (addend).
 //   * Reference: MultiHopCsrPlan (multihop_csr_ext/multihop_csr_pipeline_cuda.cu
 //     :113-322) drives three cuSPARSE SpMMs plus two add kernels per call.
@@ -25,12 +26,8 @@ struct cign_spmm_plan {
   cign_csr_f32 p;
   cign_csr_f32 pt;
   bool pt_is_p;
-  int32_t* heavy_p;   // device [n_heavy_p]
-  int32_t* heavy_pt;  // device [n_heavy_pt] (aliases heavy_p when pt_is_p)
-  int64_t n_heavy_p;
-  int64_t n_heavy_pt;
-  int32_t max_deg_p;
-  int32_t max_deg_pt;
+  cign::SegList seg_p;
+  cign::SegList seg_pt;  // unused (seg_p serves both) when pt_is_p
   int device;
 };
 
@@ -38,7 +35,7 @@ namespace cign {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kHeavyThreshold = 128;
+constexpr int kSegLen = 64;  // edges per work item of a hub row
 
 template <int VEC, int VPL, int LPR>
 struct SpmmCfg {
@@ -104,13 +101,16 @@ __device__ __forceinline__ void gather_edges(
   }
 }
 
+// Blocks [0, seg_blocks) process hub-row segments (one group each) into
+// `partial`; the remaining blocks process whole rows of at most kSegLen
+// non-zeros.
 template <int VEC, int VPL, int LPR>
 __global__ void __launch_bounds__(kThreads)
-spmm_rows_kernel(int rows, const int* __restrict__ crow,
-                 const int* __restrict__ col, const float* __restrict__ val,
-                 const int* __restrict__ heavy_rows, int n_heavy,
-                 int heavy_threshold, const float* __restrict__ X, int64_t F,
-                 const float* __restrict__ addend, float* __restrict__ Y) {
+spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__ col,
+                 const float* __restrict__ val, const int* __restrict__ seg_begin,
+                 const int* __restrict__ seg_end, int n_seg, int seg_blocks,
+                 const float* __restrict__ X, int64_t F, const float* __restrict__ addend,
+                 float* __restrict__ Y, float* __restrict__ partial) {
   using V = typename VecT<VEC>::type;
   using Cfg = SpmmCfg<VEC, VPL, LPR>;
   const int lig = threadIdx.x % LPR;
@@ -119,55 +119,37 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow,
       LPR == 32 ? kFullMask
                 : (((1u << LPR) - 1u) << ((threadIdx.x & 31) / LPR * LPR));
 
-  if (static_cast<int>(blockIdx.x) < n_heavy) {
-    // ---- one CTA per heavy row: all groups split the row's edges.
-    __shared__ float red[Cfg::kGroups * Cfg::kTile];
-    const int row = heavy_rows[blockIdx.x];
-    const int e0 = crow[row];
-    const int e1 = crow[row + 1];
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    const int64_t sidx = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + group;
+    if (sidx >= n_seg) return;
+    const int e0 = seg_begin[sidx], e1 = seg_end[sidx];
+    float* pr = partial + sidx * F;
     for (int64_t f0 = 0; f0 < F; f0 += Cfg::kTile) {
       V acc[VPL];
 #pragma unroll
       for (int q = 0; q < VPL; ++q) vzero(acc[q]);
-      gather_edges<VEC, VPL, LPR>(col, val, e0 + group * LPR, e1,
-                                  Cfg::kGroups * LPR, X, F, f0, lig, gmask,
-                                  acc);
+      gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask, acc);
 #pragma unroll
       for (int q = 0; q < VPL; ++q) {
-        const int fi = (lig + q * LPR) * VEC;
-#pragma unroll
-        for (int j = 0; j < VEC; ++j)
-          red[group * Cfg::kTile + fi + j] = vel(acc[q], j);
+        const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+        if (f0 + fi < F) st_vec(pr + f0 + fi, acc[q]);
       }
-      __syncthreads();
-      for (int fi = threadIdx.x; fi < Cfg::kTile; fi += kThreads) {
-        if (f0 + fi < F) {
-          float s = 0.0f;
-          for (int g = 0; g < Cfg::kGroups; ++g) s += red[g * Cfg::kTile + fi];
-          const int64_t o = static_cast<int64_t>(row) * F + f0 + fi;
-          if (addend != nullptr) s += addend[o];
-          Y[o] = s;
-        }
-      }
-      __syncthreads();
     }
     return;
   }
 
-  // ---- light rows: one group of LPR lanes per row.
   const int64_t row64 =
-      static_cast<int64_t>(blockIdx.x - n_heavy) * Cfg::kGroups + group;
+      static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
   if (row64 >= rows) return;
   const int row = static_cast<int>(row64);
   const int e0 = crow[row];
   const int e1 = crow[row + 1];
-  if (e1 - e0 > heavy_threshold) return;  // handled by a heavy CTA
+  if (e1 - e0 > kSegLen) return;  // a hub row: done by segments + combine
   for (int64_t f0 = 0; f0 < F; f0 += Cfg::kTile) {
     V acc[VPL];
 #pragma unroll
     for (int q = 0; q < VPL; ++q) vzero(acc[q]);
-    gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask,
-                                acc);
+    gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask, acc);
     float* yr = Y + row64 * F + f0;
     const float* ar = addend != nullptr ? addend + row64 * F + f0 : nullptr;
 #pragma unroll
@@ -178,6 +160,25 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow,
         st_vec(yr + fi, acc[q]);
       }
     }
+  }
+}
+
+// One CTA per hub row: Y[row] = sum of the row's segment partials in
+// segment order (+ addend).
+template <int VEC>
+__global__ void __launch_bounds__(kThreads)
+spmm_combine_kernel(const int* __restrict__ heavy_row, const int* __restrict__ heavy_first,
+                    const float* __restrict__ partial, int64_t F,
+                    const float* __restrict__ addend, float* __restrict__ Y) {
+  using V = typename VecT<VEC>::type;
+  const int h = blockIdx.x;
+  const int64_t row = heavy_row[h];
+  const int s0 = heavy_first[h], s1 = heavy_first[h + 1];
+  for (int64_t f = static_cast<int64_t>(threadIdx.x) * VEC; f < F; f += kThreads * VEC) {
+    V acc = ld_vec<VEC>(partial + static_cast<int64_t>(s0) * F + f);
+    for (int s = s0 + 1; s < s1; ++s) vadd(acc, ld_vec<VEC>(partial + static_cast<int64_t>(s) * F + f));
+    if (addend != nullptr) vadd(acc, ld_vec<VEC>(addend + row * F + f));
+    st_vec(Y + row * F + f, acc);
   }
 }
 
@@ -204,44 +205,52 @@ __global__ void csr_validate_kernel(int64_t rows, int64_t cols, int64_t nnz,
 }
 
 template <int VEC, int VPL, int LPR>
-int launch_spmm_cfg(const cign_csr_f32& m, const int32_t* heavy, int64_t n_heavy,
-                    const float* X, int64_t F, const float* addend, float* Y,
-                    cudaStream_t stream) {
+int launch_spmm_cfg(const cign_csr_f32& m, const SegList& sl, const float* X, int64_t F,
+                    const float* addend, float* Y, float* partial, cudaStream_t stream) {
   using Cfg = SpmmCfg<VEC, VPL, LPR>;
+  const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
   const int64_t light_blocks = (m.rows + Cfg::kGroups - 1) / Cfg::kGroups;
-  const int64_t grid = n_heavy + light_blocks;
+  const int64_t grid = seg_blocks + light_blocks;
   if (grid == 0) return CIGN_OK;
   CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "spmm: grid too large");
   spmm_rows_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
-      static_cast<int>(m.rows), m.crow, m.col, m.val, heavy,
-      static_cast<int>(n_heavy), kHeavyThreshold, X, F, addend, Y);
+      static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
+      static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, addend, Y, partial);
   CIGN_CHECK_LAUNCH("spmm_rows_kernel");
+  if (sl.n_heavy > 0) {
+    spmm_combine_kernel<VEC><<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, stream>>>(
+        sl.heavy_row(), sl.heavy_first(), partial, F, addend, Y);
+    CIGN_CHECK_LAUNCH("spmm_combine_kernel");
+  }
   return CIGN_OK;
 }
 
 template <int VEC>
-int launch_spmm_vec(const cign_csr_f32& m, const int32_t* heavy, int64_t n_heavy,
-                    const float* X, int64_t F, const float* addend, float* Y,
-                    cudaStream_t stream) {
+int launch_spmm_vec(const cign_csr_f32& m, const SegList& sl, const float* X, int64_t F,
+                    const float* addend, float* Y, float* partial, cudaStream_t stream) {
   const int64_t fv = F / VEC;  // vectors per row
-  if (fv <= 8) return launch_spmm_cfg<VEC, 1, 8>(m, heavy, n_heavy, X, F, addend, Y, stream);
-  if (fv <= 16) return launch_spmm_cfg<VEC, 1, 16>(m, heavy, n_heavy, X, F, addend, Y, stream);
-  if (fv <= 32) return launch_spmm_cfg<VEC, 1, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
-  if (fv <= 64) return launch_spmm_cfg<VEC, 2, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
-  if (fv <= 128) return launch_spmm_cfg<VEC, 4, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
-  return launch_spmm_cfg<VEC, 8, 32>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  if (fv <= 8) return launch_spmm_cfg<VEC, 1, 8>(m, sl, X, F, addend, Y, partial, stream);
+  if (fv <= 16) return launch_spmm_cfg<VEC, 1, 16>(m, sl, X, F, addend, Y, partial, stream);
+  if (fv <= 32) return launch_spmm_cfg<VEC, 1, 32>(m, sl, X, F, addend, Y, partial, stream);
+  if (fv <= 64) return launch_spmm_cfg<VEC, 2, 32>(m, sl, X, F, addend, Y, partial, stream);
+  if (fv <= 128) return launch_spmm_cfg<VEC, 4, 32>(m, sl, X, F, addend, Y, partial, stream);
+  return launch_spmm_cfg<VEC, 8, 32>(m, sl, X, F, addend, Y, partial, stream);
 }
 
-int run_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
-             int64_t F, const float* addend, float* Y, cudaStream_t stream) {
+size_t partial_bytes(const cign_spmm_plan* plan, int64_t F) {
+  const int64_t n = std::max(plan->seg_p.n_seg, plan->pt_is_p ? 0 : plan->seg_pt.n_seg);
+  return (static_cast<size_t>(n) * F * sizeof(float) + 255) / 256 * 256;
+}
+
+int run_spmm(const cign_spmm_plan* plan, int transpose, const float* X, int64_t F,
+             const float* addend, float* Y, float* partial, cudaStream_t stream) {
   const bool use_t = transpose != 0 && !plan->pt_is_p;
   const cign_csr_f32& m = use_t ? plan->pt : plan->p;
-  const int32_t* heavy = use_t ? plan->heavy_pt : plan->heavy_p;
-  const int64_t n_heavy = use_t ? plan->n_heavy_pt : plan->n_heavy_p;
-  const bool vec4 = (F % 4 == 0) && aligned16(X) && aligned16(Y) &&
+  const SegList& sl = use_t ? plan->seg_pt : plan->seg_p;
+  const bool vec4 = (F % 4 == 0) && aligned16(X) && aligned16(Y) && aligned16(partial) &&
                     (addend == nullptr || aligned16(addend));
-  if (vec4) return launch_spmm_vec<4>(m, heavy, n_heavy, X, F, addend, Y, stream);
-  return launch_spmm_vec<1>(m, heavy, n_heavy, X, F, addend, Y, stream);
+  if (vec4) return launch_spmm_vec<4>(m, sl, X, F, addend, Y, partial, stream);
+  return launch_spmm_vec<1>(m, sl, X, F, addend, Y, partial, stream);
 }
 
 int check_csr_args(const cign_csr_f32* m, const char* name) {
@@ -257,13 +266,9 @@ int check_csr_args(const cign_csr_f32* m, const char* name) {
   return CIGN_OK;
 }
 
-// Validates the CSR on the device, then builds the heavy-row list (device
-// array owned by the plan).
-int build_heavy(const cign_csr_f32& m, int32_t** heavy_out, int64_t* n_out,
-                int32_t* max_deg_out) {
-  *heavy_out = nullptr;
-  *n_out = 0;
-  *max_deg_out = 0;
+// Validates the CSR on the device, then builds the hub-row segment list
+// (device buffer owned by the plan).
+int build_plan_segments(const cign_csr_f32& m, SegList* out) {
   int* bad_d = nullptr;
   CIGN_CHECK_CUDA(cudaMalloc(&bad_d, sizeof(int)), "plan: cudaMalloc");
   cudaMemset(bad_d, 0, sizeof(int));
@@ -280,8 +285,7 @@ int build_heavy(const cign_csr_f32& m, int32_t** heavy_out, int64_t* n_out,
   CIGN_REQUIRE(bad == 0, CIGN_ERR_INVALID_ARGUMENT,
                "plan: malformed CSR (crow not monotone from 0 to nnz, or a "
                "column index out of range)");
-  return build_heavy_list(m.crow, m.rows, kHeavyThreshold, heavy_out, n_out,
-                          max_deg_out);
+  return build_segments(m.crow, m.rows, kSegLen, out);
 }
 
 int check_dense(const cign_spmm_plan* plan, const float* X, int64_t F,
@@ -322,21 +326,14 @@ int cign_spmm_plan_create(const cign_csr_f32* p, const cign_csr_f32* pt,
   plan->p = *p;
   plan->pt = pt_is_p ? *p : *pt;
   plan->pt_is_p = pt_is_p;
-  plan->heavy_p = plan->heavy_pt = nullptr;
   cudaGetDevice(&plan->device);
-  rc = build_heavy(plan->p, &plan->heavy_p, &plan->n_heavy_p, &plan->max_deg_p);
-  if (rc == CIGN_OK && !pt_is_p)
-    rc = build_heavy(plan->pt, &plan->heavy_pt, &plan->n_heavy_pt, &plan->max_deg_pt);
+  rc = build_plan_segments(plan->p, &plan->seg_p);
+  if (rc == CIGN_OK && !pt_is_p) rc = build_plan_segments(plan->pt, &plan->seg_pt);
   if (rc != CIGN_OK) {
-    if (plan->heavy_p) cudaFree(plan->heavy_p);
-    if (plan->heavy_pt) cudaFree(plan->heavy_pt);
+    free_segments(&plan->seg_p);
+    free_segments(&plan->seg_pt);
     delete plan;
     return rc;
-  }
-  if (pt_is_p) {
-    plan->heavy_pt = plan->heavy_p;
-    plan->n_heavy_pt = plan->n_heavy_p;
-    plan->max_deg_pt = plan->max_deg_p;
   }
   *out = plan;
   clear_error();
@@ -348,8 +345,8 @@ int cign_spmm_plan_destroy(cign_spmm_plan* plan) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(plan->device);
-  if (plan->heavy_p) cudaFree(plan->heavy_p);
-  if (!plan->pt_is_p && plan->heavy_pt) cudaFree(plan->heavy_pt);
+  free_segments(&plan->seg_p);
+  free_segments(&plan->seg_pt);
   cudaSetDevice(prev);
   delete plan;
   return CIGN_OK;
@@ -358,29 +355,49 @@ int cign_spmm_plan_destroy(cign_spmm_plan* plan) {
 int cign_spmm_plan_get_info(const cign_spmm_plan* plan, cign_spmm_plan_info* info) {
   CIGN_REQUIRE(plan != nullptr && info != nullptr, CIGN_ERR_NULL_POINTER,
                "plan_get_info: NULL argument");
+  const SegList& t = plan->pt_is_p ? plan->seg_p : plan->seg_pt;
   info->rows = plan->p.rows;
   info->nnz = plan->p.nnz;
-  info->heavy_rows = plan->n_heavy_p;
-  info->heavy_rows_t = plan->n_heavy_pt;
-  info->max_degree = plan->max_deg_p;
-  info->max_degree_t = plan->max_deg_pt;
-  info->heavy_threshold = kHeavyThreshold;
+  info->heavy_rows = plan->seg_p.n_heavy;
+  info->heavy_rows_t = t.n_heavy;
+  info->segments = plan->seg_p.n_seg;
+  info->segments_t = t.n_seg;
+  info->max_degree = plan->seg_p.max_len;
+  info->max_degree_t = t.max_len;
+  info->segment_length = kSegLen;
   info->transpose_is_forward = plan->pt_is_p ? 1 : 0;
   return CIGN_OK;
 }
 
-int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
-              int64_t F, const float* addend, float* Y, cign_stream_t stream) {
+size_t cign_spmm_workspace_bytes(const cign_spmm_plan* plan, int64_t F) {
+  if (plan == nullptr || F <= 0) return 0;
+  return partial_bytes(plan, F);
+}
+
+int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X, int64_t F,
+              const float* addend, float* Y, void* ws, size_t ws_bytes,
+              cign_stream_t stream) {
   int rc = check_dense(plan, X, F, Y, "spmm");
   if (rc) return rc;
   CIGN_REQUIRE(X != Y || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
                "spmm: Y must not alias X");
-  return run_spmm(plan, transpose, X, F, addend, Y,
+  const size_t need = partial_bytes(plan, F);
+  CIGN_REQUIRE(ws_bytes >= need && (need == 0 || ws != nullptr), CIGN_ERR_INVALID_ARGUMENT,
+               "spmm: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  return run_spmm(plan, transpose, X, F, addend, Y, static_cast<float*>(ws),
                   static_cast<cudaStream_t>(stream));
 }
 
-int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power, const float* X,
-                      int64_t F, float* const* Y, cign_stream_t stream) {
+size_t cign_multihop_workspace_bytes(const cign_spmm_plan* plan, int max_power, int64_t F) {
+  if (plan == nullptr || F <= 0) return 0;
+  const size_t state = max_power >= 2
+                           ? (static_cast<size_t>(plan->p.rows) * F * sizeof(float) + 255) / 256 * 256
+                           : 0;
+  return state + partial_bytes(plan, F);
+}
+
+int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power, const float* X, int64_t F,
+                      float* const* Y, void* ws, size_t ws_bytes, cign_stream_t stream) {
   CIGN_REQUIRE(max_power >= 1, CIGN_ERR_INVALID_ARGUMENT,
                "multihop_fwd: max_power must be >= 1");
   CIGN_REQUIRE(Y != nullptr, CIGN_ERR_NULL_POINTER, "multihop_fwd: Y is NULL");
@@ -395,19 +412,22 @@ int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power, const float* X,
       CIGN_REQUIRE(Y[p] != Y[p - 1] || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
                    "multihop_fwd: Y[%d] aliases Y[%d]", p, p - 1);
   }
+  const size_t need = partial_bytes(plan, F);
+  CIGN_REQUIRE(ws_bytes >= need && (need == 0 || ws != nullptr), CIGN_ERR_INVALID_ARGUMENT,
+               "multihop_fwd: workspace too small (%zu < %zu bytes)", ws_bytes, need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* partial = static_cast<float*>(ws);
   const float* src = X;
   for (int p = 0; p < max_power; ++p) {
-    rc = run_spmm(plan, 0, src, F, nullptr, Y[p], s);
+    rc = run_spmm(plan, 0, src, F, nullptr, Y[p], partial, s);
     if (rc) return rc;
     src = Y[p];
   }
   return CIGN_OK;
 }
 
-int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power,
-                      const float* const* G, int64_t F, float* GX, float* ws,
-                      cign_stream_t stream) {
+int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power, const float* const* G,
+                      int64_t F, float* GX, void* ws, size_t ws_bytes, cign_stream_t stream) {
   CIGN_REQUIRE(max_power >= 1, CIGN_ERR_INVALID_ARGUMENT,
                "multihop_bwd: max_power must be >= 1");
   CIGN_REQUIRE(G != nullptr, CIGN_ERR_NULL_POINTER, "multihop_bwd: G is NULL");
@@ -422,23 +442,28 @@ int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power,
     if (bytes) CIGN_CHECK_CUDA(cudaMemsetAsync(GX, 0, bytes, s), "multihop_bwd: memset");
     return CIGN_OK;
   }
-  if (top >= 2)
-    CIGN_REQUIRE(ws != nullptr || plan->p.rows == 0, CIGN_ERR_NULL_POINTER,
-                 "multihop_bwd: ws is NULL");
+  const size_t need = cign_multihop_workspace_bytes(plan, max_power, F);
+  CIGN_REQUIRE(ws_bytes >= need && (need == 0 || ws != nullptr), CIGN_ERR_INVALID_ARGUMENT,
+               "multihop_bwd: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  CIGN_REQUIRE(aligned16(ws), CIGN_ERR_ALIGNMENT, "multihop_bwd: ws must be 16-byte aligned");
+  // workspace = [state buffer [rows, F] (max_power >= 2) | segment partials]
+  const size_t state_bytes = max_power >= 2 ? (bytes + 255) / 256 * 256 : 0;
+  float* state = static_cast<float*>(ws);
+  float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + state_bytes);
   for (int p = 0; p < max_power; ++p)
-    CIGN_REQUIRE(G[p] == nullptr || (G[p] != GX && G[p] != ws) || plan->p.rows == 0,
+    CIGN_REQUIRE(G[p] == nullptr || (G[p] != GX && G[p] != state) || plan->p.rows == 0,
                  CIGN_ERR_INVALID_ARGUMENT, "multihop_bwd: G[%d] aliases GX/ws", p);
   // u_top = G[top-1];  u_p = P^T u_{p+1} + G[p-1]  (p = top-1 .. 1);
-  // GX = P^T u_1.  u_p lives in ws for odd p and in GX for even p, so the
-  // final SpMM reads ws and writes GX.
+  // GX = P^T u_1.  u_p lives in the state buffer for odd p and in GX for
+  // even p, so the final SpMM reads the state buffer and writes GX.
   const float* u = G[top - 1];
   for (int p = top - 1; p >= 1; --p) {
-    float* dst = (p & 1) ? ws : GX;
-    rc = run_spmm(plan, 1, u, F, G[p - 1], dst, s);
+    float* dst = (p & 1) ? state : GX;
+    rc = run_spmm(plan, 1, u, F, G[p - 1], dst, partial, s);
     if (rc) return rc;
     u = dst;
   }
-  return run_spmm(plan, 1, u, F, nullptr, GX, s);
+  return run_spmm(plan, 1, u, F, nullptr, GX, partial, s);
 }
 
 }  // extern "C"

@@ -97,9 +97,11 @@ class SpmmPlan:
         y = torch.empty_like(x)
         if addend is not None:
             addend = self._check_dense(addend, "spmm addend")
+        ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, F), self.device)
         with _lib.DeviceGuard(self.device):
             rc = self.lib.cign_spmm(self.handle, 1 if transpose else 0, _lib.ptr(x), F,
-                                    _lib.ptr(addend), _lib.ptr(y), _lib.stream_of(x))
+                                    _lib.ptr(addend), _lib.ptr(y), _lib.ptr(ws), ws.numel(),
+                                    _lib.stream_of(x))
         _lib.check(rc, "cign_spmm")
         return y
 
@@ -108,9 +110,11 @@ class SpmmPlan:
         x = self._check_dense(x, "multihop forward")
         ys = [torch.empty_like(x) for _ in range(int(max_power))]
         arr = _lib.ptr_array(ys)
+        F = int(x.size(1))
+        ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, F), self.device)
         with _lib.DeviceGuard(self.device):
-            rc = self.lib.cign_multihop_fwd(self.handle, int(max_power), _lib.ptr(x),
-                                            int(x.size(1)), arr, _lib.stream_of(x))
+            rc = self.lib.cign_multihop_fwd(self.handle, int(max_power), _lib.ptr(x), F, arr,
+                                            _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
         _lib.check(rc, "cign_multihop_fwd")
         return ys
 
@@ -121,11 +125,12 @@ class SpmmPlan:
             raise ValueError("multihop backward needs at least one gradient")
         gs = [None if g is None else self._check_dense(g, "multihop grad") for g in grads]
         gx = torch.empty((self.rows, int(F)), dtype=torch.float32, device=self.device)
-        ws = torch.empty_like(gx) if len(gs) >= 2 else None
+        ws = _lib.workspace(self.lib.cign_multihop_workspace_bytes(self.handle, len(gs), int(F)),
+                            self.device)
         arr = _lib.ptr_array(gs)
         with _lib.DeviceGuard(self.device):
             rc = self.lib.cign_multihop_bwd(self.handle, len(gs), arr, int(F), _lib.ptr(gx),
-                                            _lib.ptr(ws), _lib.stream_of(gx))
+                                            _lib.ptr(ws), ws.numel(), _lib.stream_of(gx))
         _lib.check(rc, "cign_multihop_bwd")
         return gx
 
@@ -161,9 +166,10 @@ class GatPlan:
             self.handle = None
 
     def info(self) -> Dict[str, int]:
-        arr = (ctypes.c_int64 * 6)()
+        arr = (ctypes.c_int64 * 8)()
         _lib.check(self.lib.cign_gat_plan_get_info(self.handle, arr), "cign_gat_plan_get_info")
-        keys = ("n", "nnz", "heavy_rows", "heavy_cols", "max_row_len", "max_col_len")
+        keys = ("n", "nnz", "heavy_rows", "heavy_cols", "max_row_len", "max_col_len",
+                "row_segments", "col_segments")
         return {k: int(v) for k, v in zip(keys, arr)}
 
 

@@ -53,6 +53,9 @@ enum {
 /* ------------------------------------------------------------------ misc */
 CIGN_API int cign_version(void);
 CIGN_API const char* cign_last_error(void);
+/* Number of kernels this library has launched in the process so far
+ * (all threads, all devices); for launch accounting in benchmarks. */
+CIGN_API uint64_t cign_kernel_launches(void);
 
 /* ------------------------------------------------------------------ CSR
  * A fixed sparse graph operator in CSR form (device arrays).
@@ -67,10 +70,11 @@ typedef struct cign_csr_f32 {
   const float* val;    /* [nnz]                                 */
 } cign_csr_f32;
 
-/* SpMM plan over P (and P^T).  Holds a device list of "heavy" rows that are
- * processed one CTA per row; the CSR arrays themselves stay owned by the
- * caller and must outlive the plan.  Immutable after creation: one plan may
- * be used from several streams at once.
+/* SpMM plan over P (and P^T).  Validates the CSR on the device and cuts rows
+ * with more than 64 non-zeros ("hub" rows of power-law graphs) into 64-edge
+ * segments processed in parallel and combined in a fixed order.  The CSR
+ * arrays stay owned by the caller and must outlive the plan.  Immutable
+ * after creation: one plan may be used from several streams at once.
  * Replaces MultiHopCsrPlan (multihop_csr_ext/multihop_csr_pipeline_cuda.cu:
  * 113-322) and its Python owner MultiHopCSR3GraphOperator
  * (multihop_csr_pipeline.py:89-140).  `pt` may be NULL when P is symmetric
@@ -81,11 +85,13 @@ typedef struct cign_spmm_plan cign_spmm_plan;
 typedef struct cign_spmm_plan_info {
   int64_t rows;
   int64_t nnz;
-  int64_t heavy_rows;     /* rows of P processed one CTA per row          */
+  int64_t heavy_rows;     /* hub rows of P (split into segments)           */
   int64_t heavy_rows_t;   /* same for P^T                                  */
+  int64_t segments;       /* segments of P's hub rows                      */
+  int64_t segments_t;
   int32_t max_degree;
   int32_t max_degree_t;
-  int32_t heavy_threshold;
+  int32_t segment_length; /* edges per segment                             */
   int32_t transpose_is_forward; /* 1 when P^T calls reuse P              */
 } cign_spmm_plan_info;
 
@@ -95,11 +101,20 @@ CIGN_API int cign_spmm_plan_destroy(cign_spmm_plan* plan);
 CIGN_API int cign_spmm_plan_get_info(const cign_spmm_plan* plan,
                             cign_spmm_plan_info* info /* host */);
 
+/* Workspace of one cign_spmm call with F feature columns (hub-row partials). */
+CIGN_API size_t cign_spmm_workspace_bytes(const cign_spmm_plan* plan, int64_t F);
+
 /* Y = op(P) @ X (+ addend).  op = P (transpose=0) or P^T (transpose=1).
  * X, Y, addend: [rows, F].  addend may be NULL.  Y must not alias X.
  * Replaces FixedCSRSpMMFunction.forward/backward (model.py:106-131). */
 CIGN_API int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
-              int64_t F, const float* addend, float* Y, cign_stream_t stream);
+              int64_t F, const float* addend, float* Y, void* ws,
+              size_t ws_bytes, cign_stream_t stream);
+
+/* Workspace of cign_multihop_fwd/bwd: the backward's [rows, F] recurrence
+ * state (max_power >= 2) plus the hub-row partials. */
+CIGN_API size_t cign_multihop_workspace_bytes(const cign_spmm_plan* plan,
+                                     int max_power, int64_t F);
 
 /* k-hop forward recurrence Y[p-1] = P^p X for p = 1..max_power.
  * Y: host array of max_power device pointers, each [rows, F]; entries for
@@ -109,19 +124,19 @@ CIGN_API int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X
  * GenericMultiHopCSRFunction.forward (multihop_csr_pipeline.py:233-246) and
  * the hybrid native3 + tail path (multihop_csr_pipeline.py:214-230). */
 CIGN_API int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power,
-                      const float* X, int64_t F, float* const* Y,
-                      cign_stream_t stream);
+                      const float* X, int64_t F, float* const* Y, void* ws,
+                      size_t ws_bytes, cign_stream_t stream);
 
 /* k-hop transposed backward: acc = 0; for p = max_power..1:
  *   acc = P^T (acc + G[p-1]);   GX = acc.
  * G: host array of max_power device pointers ([rows, F]) or NULL entries
- * for powers that received no gradient.  ws: one [rows, F] fp32 buffer.
- * The "+ G" is fused into the SpMM epilogue (one kernel per hop).
+ * for powers that received no gradient.  The "+ G" is fused into the SpMM
+ * epilogue (one pass per hop).
  * Replaces MultiHopCsrPlan::backward3 (multihop_csr_pipeline_cuda.cu:299-321)
  * and GenericMultiHopCSRFunction.backward (multihop_csr_pipeline.py:248-265).*/
 CIGN_API int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power,
-                      const float* const* G, int64_t F, float* GX, float* ws,
-                      cign_stream_t stream);
+                      const float* const* G, int64_t F, float* GX, void* ws,
+                      size_t ws_bytes, cign_stream_t stream);
 
 /* ------------------------------------------------------------------ GAT
  * Collapsed multi-head GAT (concat=False) over a fixed graph.
@@ -130,9 +145,10 @@ CIGN_API int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power,
  * (colptr [n+1], row [nnz]) with perm[csc position] = CSR edge id -- the
  * triple PyG's FusedGATConv.to_graph_format yields and the reference keeps
  * in GraphCliffordNet.prepare_fused_gat_graph (generic_engine/model_cign.py:
- * 1069-1158).  The plan validates the triple on the device, lists rows and
- * columns with more than 128 edges (one CTA each) and keeps pointers to the
- * caller's arrays, which must outlive it.  Synchronises the device once. */
+ * 1069-1158).  The plan validates the triple on the device, cuts rows and
+ * columns with more than 32 edges into 32-edge segments (processed in
+ * parallel, combined in a fixed order) and keeps pointers to the caller's
+ * arrays, which must outlive it.  Synchronises the device once. */
 typedef struct cign_gat_plan cign_gat_plan;
 
 CIGN_API int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr,
@@ -140,9 +156,12 @@ CIGN_API int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr,
                          const int32_t* row, const int32_t* perm,
                          cign_gat_plan** out);
 CIGN_API int cign_gat_plan_destroy(cign_gat_plan* plan);
-/* info (host, 6 entries): n, nnz, heavy rows, heavy columns, max row
- * length, max column length. */
+/* info (host, 8 entries): n, nnz, hub rows, hub columns, max row length,
+ * max column length, row segments, column segments. */
 CIGN_API int cign_gat_plan_get_info(const cign_gat_plan* plan, int64_t* info);
+
+CIGN_API size_t cign_gat_fwd_workspace_bytes(const cign_gat_plan* plan, int32_t heads,
+                                    int32_t channels);
 
 /* Forward, for destination row i and head h:
  *   e_ij = LeakyReLU(attn_row[i,h] + attn_col[j,h]),
@@ -159,7 +178,8 @@ CIGN_API int cign_gat_fwd(const cign_gat_plan* plan, int32_t heads, int32_t chan
                  const float* attn_row, const float* attn_col,
                  const float* in_feat, const float* bias, float negative_slope,
                  float attn_drop, uint64_t seed, float* out, float* pre,
-                 float* edge_max, float* edge_sum, cign_stream_t stream);
+                 float* edge_max, float* edge_sum, void* ws, size_t ws_bytes,
+                 cign_stream_t stream);
 
 CIGN_API size_t cign_gat_bwd_workspace_bytes(const cign_gat_plan* plan, int32_t heads,
                                     int32_t channels);

@@ -30,6 +30,7 @@ def test_library_exports_every_declared_symbol():
 def test_version_and_error_text():
     lib = _lib.load_library()
     assert lib.cign_version() >= 1
+    assert lib.cign_kernel_launches() == 0  # nothing launched without a GPU
     out = ctypes.c_void_p()
     rc = lib.cign_spmm_plan_create(None, None, ctypes.byref(out))
     assert rc == 2  # CIGN_ERR_NULL_POINTER
@@ -49,7 +50,7 @@ def test_invalid_arguments_rejected_before_launch():
                                None) == 6
     # GAT heads above the supported range
     assert lib.cign_gat_fwd(ctypes.c_void_p(1), 65, 8, None, None, None, None, 0.2, 0.0, 0, None,
-                            None, None, None, None) == 6
+                            None, None, None, None, 0, None) == 6
     assert "heads" in _lib.last_error()
 
 

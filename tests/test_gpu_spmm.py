@@ -76,7 +76,7 @@ def test_spmm_shapes_vs_oracle(cuda, F):
     n = 4000
     base, P = _powerlaw_operator(n, 30000, 11, cuda)
     plan = SpmmPlan(base.csr.crow_indices(), base.csr.col_indices(), base.csr.values())
-    assert plan.info()["heavy_rows"] > 0  # the CTA-per-row path is exercised
+    assert plan.info()["heavy_rows"] > 0  # the hub-row segment path is exercised
     g = torch.Generator().manual_seed(F)
     x = torch.randn(n, F, generator=g)
     y = plan.spmm(x.to(cuda))
