@@ -15,6 +15,7 @@
 // shared memory in a fixed order, then summed over chunks by a second tiny
 // kernel: deterministic, no atomics.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -544,3 +545,85 @@ int cign_block_dropout_mask(int64_t count, float p, uint64_t seed, uint8_t* mask
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------
+// Allocation-free variant of the dropout-LayerNorm backward.
+//
+// Some callers cannot allocate device memory at all: for example code that
+// runs as a plugin inside a host framework which owns every byte of device
+// memory through its own pool and hands kernels only their input and output
+// buffers, or code on a latency-critical loop where a cudaMalloc (and its
+// implicit synchronisation) is not allowed.  For them the workspace of the
+// parameter-gradient reduction lives in the fixed array below instead of a
+// caller-provided buffer.
+//
+// The array holds 592 row chunks x 1024 columns x 2 partial sums (4.6 MiB);
+// every GPU on which this library is loaded keeps it for the life of the
+// process.  592 is the largest chunk count rows_per_chunk() can produce, so
+// the limit is the hidden width: D <= 1024 (D <= 256 unless D % 4 == 0 and
+// the tensors are 16-byte aligned), the same as the workspace version.
+//
+// The array is shared by every call in the process: two calls that overlap
+// on the GPU (different streams, or different host threads) race on it and
+// give undefined results; order them on one stream.  Each call overwrites
+// every partial it later reads, so nothing has to be cleared between calls.
+// Its device address is looked up (cudaGetSymbolAddress) on the first call
+// on each device, with that device current; make that first call before any
+// stream capture.
+constexpr int64_t kStaticLnChunks = 592;
+constexpr int64_t kStaticLnMaxD = 1024;
+static __device__ __align__(256) float g_static_ln_scratch[kStaticLnChunks * kStaticLnMaxD * 2];
+
+namespace {
+std::mutex g_static_ln_mutex;
+float* g_static_ln_ptr[64] = {nullptr};
+
+// Device address of g_static_ln_scratch on the current device.
+int static_ln_scratch(float** out) {
+  int dev = 0;
+  CIGN_CHECK_CUDA(cudaGetDevice(&dev), "dropout_ln_bwd_static: cudaGetDevice");
+  CIGN_REQUIRE(dev >= 0 && dev < 64, CIGN_ERR_UNSUPPORTED,
+               "dropout_ln_bwd_static: device id %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_ln_mutex);
+  if (g_static_ln_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    CIGN_CHECK_CUDA(cudaGetSymbolAddress(&p, g_static_ln_scratch),
+                    "dropout_ln_bwd_static: cudaGetSymbolAddress");
+    g_static_ln_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_static_ln_ptr[dev];
+  return CIGN_OK;
+}
+}  // namespace
+
+extern "C" int cign_dropout_ln_bwd_static(int64_t n, int64_t d, const float* grad_y,
+                                          const float* x, const float* w, const float* mean,
+                                          const float* rstd, float p, uint64_t seed,
+                                          float* grad_x, float* grad_w, float* grad_b,
+                                          cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(grad_y) &&
+                  aligned16(grad_x);
+  int rc = check_rows(n, d, v4, "dropout_ln_bwd_static");
+  if (rc) return rc;
+  CIGN_REQUIRE(d <= kStaticLnMaxD && num_chunks(n) <= kStaticLnChunks, CIGN_ERR_UNSUPPORTED,
+               "dropout_ln_bwd_static: needs %lld x %lld partials, the static scratch holds "
+               "%lld x %lld", (long long)num_chunks(n), (long long)d,
+               (long long)kStaticLnChunks, (long long)kStaticLnMaxD);
+  CIGN_REQUIRE(grad_w && grad_b, CIGN_ERR_NULL_POINTER, "dropout_ln_bwd_static: NULL param grad");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_w, 0, d * sizeof(float), s), "memset");
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_b, 0, d * sizeof(float), s), "memset");
+    return CIGN_OK;
+  }
+  CIGN_REQUIRE(grad_y && x && w && mean && rstd && grad_x, CIGN_ERR_NULL_POINTER,
+               "dropout_ln_bwd_static: NULL");
+  float* wsf = nullptr;
+  rc = static_ln_scratch(&wsf);
+  if (rc) return rc;
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s)));
+  return CIGN_OK;
+}

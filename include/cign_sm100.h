@@ -294,6 +294,25 @@ CIGN_API int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y,
                         float* grad_x, float* grad_w, float* grad_b, void* ws,
                         size_t ws_bytes, cign_stream_t stream);
 
+/* Allocation-free variant of cign_dropout_ln_bwd (this entry point has no
+ * counterpart in the reference).  For callers that cannot allocate device
+ * memory -- e.g. a plugin inside a host framework that owns all device memory
+ * through its own pool and passes kernels only their inputs and outputs --
+ * the reduction scratch is a fixed 4.6 MiB array inside the library (592 row
+ * chunks x 1024 columns x 2 floats), held on every GPU that loads the
+ * library until the process exits.  Limit: D <= 1024 (the same as the
+ * workspace version); larger shapes return CIGN_ERR_UNSUPPORTED.  No
+ * cudaMalloc/cudaFree is called.  All calls share the array: calls that
+ * overlap on the GPU (other streams or threads) race; order them on one
+ * stream.  The first call on each device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture. */
+CIGN_API int cign_dropout_ln_bwd_static(int64_t n, int64_t d, const float* grad_y,
+                               const float* x, const float* w,
+                               const float* mean, const float* rstd, float p,
+                               uint64_t seed, float* grad_x, float* grad_w,
+                               float* grad_b, cign_stream_t stream);
+
 /* y = LayerNorm(a + b). */
 CIGN_API int cign_add_ln_fwd(int64_t n, int64_t d, const float* a, const float* b,
                     const float* w, const float* bias, float eps, float* y,
