@@ -223,20 +223,6 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
   }
 }
 
-__global__ void param_stage2_kernel(const float* __restrict__ pw, const float* __restrict__ pb,
-                                    int64_t chunks, int64_t D, float* __restrict__ gw,
-                                    float* __restrict__ gb) {
-  const int64_t d = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  if (d >= D) return;
-  float sw = 0.0f, sb = 0.0f;
-  for (int64_t k = 0; k < chunks; ++k) {
-    sw += pw[k * D + d];
-    if (pb != nullptr) sb += pb[k * D + d];
-  }
-  gw[d] = sw;
-  if (gb != nullptr) gb[d] = sb;
-}
-
 // y = h + gamma * dropout(g)
 template <int VEC>
 __global__ void gamma_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ h,
@@ -365,10 +351,7 @@ int launch_ln_bwd(int64_t n, int64_t D, const float* gy, const float* x, const f
   ln_bwd_kernel<MODE, VEC, VPL, LPR><<<static_cast<unsigned>(chunks), kThreads, 0, s>>>(
       n, D, rpc, gy, x, x2, w, mean, rstd, p, seed, gx, pw, pb);
   CIGN_CHECK_LAUNCH("ln_bwd_kernel");
-  param_stage2_kernel<<<static_cast<unsigned>((D + kThreads - 1) / kThreads), kThreads, 0, s>>>(
-      pw, pb, chunks, D, gw, gb);
-  CIGN_CHECK_LAUNCH("param_stage2_kernel");
-  return CIGN_OK;
+  return colsum_rows(pw, gw, pb, gb, chunks, D, D, s);
 }
 
 template <int VEC, int VPL, int LPR>
@@ -380,10 +363,7 @@ int launch_gamma_bwd(int64_t n, int64_t D, const float* gy, const float* g, cons
   gamma_bwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(chunks), kThreads, 0, s>>>(
       n, D, rpc, gy, g, gamma, p, seed, gg, ws);
   CIGN_CHECK_LAUNCH("gamma_bwd_kernel");
-  param_stage2_kernel<<<static_cast<unsigned>((D + kThreads - 1) / kThreads), kThreads, 0, s>>>(
-      ws, nullptr, chunks, D, ggamma, nullptr);
-  CIGN_CHECK_LAUNCH("param_stage2_kernel");
-  return CIGN_OK;
+  return colsum_rows(ws, ggamma, nullptr, nullptr, chunks, D, D, s);
 }
 
 }  // namespace

@@ -83,6 +83,11 @@ void free_segments(SegList* s);
 int64_t colsum_chunks(int64_t n);
 int colsum_f32(const float* a, int64_t n, int64_t c, float* partial,
                float* out, cudaStream_t s);
+// out_m[j] = sum over rows r of a_m[r * ld + j] (j < cols) for one or two
+// matrices (a1/out1 may be NULL), in a fixed order (reduce.cu).  Used as the
+// second stage of the chunked parameter-gradient reductions.
+int colsum_rows(const float* a0, float* out0, const float* a1, float* out1, int64_t rows,
+                int64_t cols, int64_t ld, cudaStream_t s);
 
 constexpr unsigned kFullMask = 0xffffffffu;
 
@@ -145,6 +150,84 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------- cp.async
+// 16-byte asynchronous global -> shared copies (LDGSTS, L1 bypass).  Each
+// thread waits only for its own groups, so a lane that reads back exactly
+// the bytes it copied needs no further synchronisation.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------- TMA ring
+// Bulk-copy (TMA, non-tensor) ring of shared-memory slots, one per warp.
+// Lane 0 arms a slot's mbarrier with the expected byte count and issues
+// cp.async.bulk copies (global -> shared, no multicast) that complete on it;
+// all lanes wait for the slot's phase, read it, and the slot is refilled
+// after a __syncwarp() and an async-proxy fence.  Waits are bounded: after
+// kWaitLimit polls the wait reports failure, the caller records a status
+// and drains, so a stuck copy can never hang the GPU.
+constexpr unsigned kWaitLimit = 1u << 20;
+constexpr int kStatusTimeout = 1;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
+          "r"(dst), "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait for `parity` on barrier `bar`; false after kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (unsigned i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// Persistent-kernel grid: resident CTAs per SM x SMs for `kernel`.
+template <typename K>
+int persistent_grid(K kernel, int threads, size_t smem) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  return per_sm * sm_count();
+}
+
 // ---------------------------------------------------------------- vectors
 template <int VEC> struct VecT;
 template <> struct VecT<1> { using type = float; };
@@ -199,6 +282,26 @@ __device__ __forceinline__ void vfma(float4& acc, float a, const float4& x) {
 __device__ __forceinline__ void vadd(float& acc, float x) { acc += x; }
 __device__ __forceinline__ void vadd(float4& acc, const float4& x) {
   acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+}
+
+// Sum of the vectors p[s * stride], s in [s0, s1), added strictly in s order
+// (deterministic); U independent loads are kept in flight.
+template <int VEC, int U = 8>
+__device__ __forceinline__ typename VecT<VEC>::type ordered_sum(const float* p, int64_t stride,
+                                                                int s0, int s1) {
+  using V = typename VecT<VEC>::type;
+  V acc;
+  vzero(acc);
+  int s = s0;
+  for (; s + U <= s1; s += U) {
+    V t[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) t[u] = ld_vec<VEC>(p + static_cast<int64_t>(s + u) * stride);
+#pragma unroll
+    for (int u = 0; u < U; ++u) vadd(acc, t[u]);
+  }
+  for (; s < s1; ++s) vadd(acc, ld_vec<VEC>(p + static_cast<int64_t>(s) * stride));
+  return acc;
 }
 
 }  // namespace cign

@@ -35,6 +35,10 @@
 //      atomics anywhere.
 //   grad_bias = column sums of g_pre (two-stage, fixed order).
 #include <algorithm>
+#include <initializer_list>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 
@@ -186,7 +190,7 @@ __device__ __forceinline__ void gat_gather(
 }
 
 // ------------------------------------------------------------ forward
-// Hub rows: one CTA per row computes the per-head max / exp-sum.
+// Hub rows: CTA (hub, head) computes that head's max / exp-sum of the row.
 __global__ void __launch_bounds__(kThreads)
 gat_hub_stats_kernel(int H, const int* __restrict__ rowptr, const int* __restrict__ col,
                      const int* __restrict__ hub_row, const float* __restrict__ attn_row,
@@ -194,21 +198,20 @@ gat_hub_stats_kernel(int H, const int* __restrict__ rowptr, const int* __restric
                      float* __restrict__ emax, float* __restrict__ esum) {
   __shared__ float scratch[32];
   const int64_t row = hub_row[blockIdx.x];
+  const int h = blockIdx.y;
   const int e0 = rowptr[row], e1 = rowptr[row + 1];
-  for (int h = 0; h < H; ++h) {
-    const float ad = attn_row[row * H + h];
-    float m = kNegInit;
-    for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
-      m = fmaxf(m, leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope));
-    m = block_max(m, scratch);
-    float s = 0.0f;
-    for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
-      s += expf(leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope) - m);
-    s = block_sum(s, scratch);
-    if (threadIdx.x == 0) {
-      emax[row * H + h] = m;
-      esum[row * H + h] = s;
-    }
+  const float ad = attn_row[row * H + h];
+  float m = kNegInit;
+  for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
+    m = fmaxf(m, leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope));
+  m = block_max(m, scratch);
+  float s = 0.0f;
+  for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
+    s += expf(leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope) - m);
+  s = block_sum(s, scratch);
+  if (threadIdx.x == 0) {
+    emax[row * H + h] = m;
+    esum[row * H + h] = s;
   }
 }
 
@@ -300,23 +303,33 @@ gat_fwd_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
   }
 }
 
-// One CTA per hub row: acc = sum of segment partials (segment order),
-// pre = acc / H + bias, out = SiLU(pre).
-__global__ void __launch_bounds__(kThreads)
+// Hub-row combine: acc = sum of the row's segment partials (segment order),
+// pre = acc / H + bias, out = SiLU(pre).  Block (hub, chunk) covers
+// kCombineThreads * VEC channels.
+constexpr int kCombineThreads = 64;
+
+template <int VEC>
+__global__ void __launch_bounds__(kCombineThreads)
 gat_fwd_combine_kernel(int H, int64_t C, const int* __restrict__ hub_row,
                        const int* __restrict__ hub_first, const float* __restrict__ partial,
                        const float* __restrict__ bias, float* __restrict__ pre,
                        float* __restrict__ out) {
+  using V = typename VecT<VEC>::type;
+  const int64_t c = (static_cast<int64_t>(blockIdx.y) * kCombineThreads + threadIdx.x) * VEC;
+  if (c >= C) return;
   const int64_t row = hub_row[blockIdx.x];
-  const int s0 = hub_first[blockIdx.x], s1 = hub_first[blockIdx.x + 1];
+  const V a = ordered_sum<VEC>(partial + c, C, hub_first[blockIdx.x], hub_first[blockIdx.x + 1]);
+  const V bv = ld_vec<VEC>(bias + c);
   const float hf = static_cast<float>(H);
-  for (int64_t c = threadIdx.x; c < C; c += kThreads) {
-    float a = 0.0f;
-    for (int s = s0; s < s1; ++s) a += partial[static_cast<int64_t>(s) * C + c];
-    const float pj = a / hf + bias[c];
-    pre[row * C + c] = pj;
-    out[row * C + c] = silu_f(pj);
+  V pv, ov;
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const float pj = vel(a, j) / hf + vel(bv, j);
+    vel(pv, j) = pj;
+    vel(ov, j) = silu_f(pj);
   }
+  st_vec(pre + row * C + c, pv);
+  st_vec(out + row * C + c, ov);
 }
 
 // ------------------------------------------------------------ backward K1
@@ -505,8 +518,9 @@ gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
   }
 }
 
-// One CTA per hub row: write its g_pre row and run the softmax backward over
-// its edges (dots already in glog from the segment groups).
+// Hub rows, CTA (hub, head): the softmax backward of that head over the
+// row's edges (dots already in glog from the segment groups); the head-0 CTA
+// also writes the row's g_pre.
 __global__ void __launch_bounds__(kThreads)
 gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
                         const int* __restrict__ col, const int* __restrict__ hub_row,
@@ -517,33 +531,34 @@ gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
                         float* __restrict__ glog, float* __restrict__ grad_attn_row) {
   __shared__ float scratch[32];
   const int64_t row = hub_row[blockIdx.x];
-  for (int64_t c = threadIdx.x; c < C; c += kThreads)
-    gpre[row * C + c] = grad_y[row * C + c] * silu_grad_f(pre[row * C + c]);
-  const int e0 = rowptr[row], e1 = rowptr[row + 1];
-  for (int h = 0; h < H; ++h) {
-    const float ad = attn_row[row * H + h];
-    const float m = emax[row * H + h], s = esum[row * H + h];
-    float wsum = 0.0f;
-    for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
-      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
-                                    p, seed, static_cast<uint64_t>(e) * H + h,
-                                    glog[static_cast<int64_t>(e) * H + h]);
-      wsum += es.soft * es.ge;
-    }
-    wsum = block_sum(wsum, scratch);
-    float grow = 0.0f;
-    for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
-      const int64_t o = static_cast<int64_t>(e) * H + h;
-      const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
-                                    p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
-      float gout = es.soft * (es.ge - wsum);
-      if (es.neg) gout *= slope;
-      glog[o] = gout;
-      grow += gout;
-    }
-    grow = block_sum(grow, scratch);
-    if (threadIdx.x == 0) grad_attn_row[row * H + h] = grow;
+  const int h = blockIdx.y;
+  if (h == 0) {
+    for (int64_t c = threadIdx.x; c < C; c += kThreads)
+      gpre[row * C + c] = grad_y[row * C + c] * silu_grad_f(pre[row * C + c]);
   }
+  const int e0 = rowptr[row], e1 = rowptr[row + 1];
+  const float ad = attn_row[row * H + h];
+  const float m = emax[row * H + h], s = esum[row * H + h];
+  float wsum = 0.0f;
+  for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
+    const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
+                                  p, seed, static_cast<uint64_t>(e) * H + h,
+                                  glog[static_cast<int64_t>(e) * H + h]);
+    wsum += es.soft * es.ge;
+  }
+  wsum = block_sum(wsum, scratch);
+  float grow = 0.0f;
+  for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
+    const int64_t o = static_cast<int64_t>(e) * H + h;
+    const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
+                                  p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
+    float gout = es.soft * (es.ge - wsum);
+    if (es.neg) gout *= slope;
+    glog[o] = gout;
+    grow += gout;
+  }
+  grow = block_sum(grow, scratch);
+  if (threadIdx.x == 0) grad_attn_row[row * H + h] = grow;
 }
 
 // ------------------------------------------------------------ backward K2
@@ -707,8 +722,11 @@ gat_bwd_cols_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
   }
 }
 
-// One CTA per hub column: sum the segment partials in segment order.
-__global__ void __launch_bounds__(kThreads)
+// Hub-column combine: grad_feat[j] / grad_attn_col[j] = sums of the
+// column's segment partials in segment order.  Block (hub, chunk) covers
+// kCombineThreads * VEC of the H*C features; chunk 0 also does the H logits.
+template <int VEC>
+__global__ void __launch_bounds__(kCombineThreads)
 gat_bwd_cols_combine_kernel(int H, int64_t C, const int* __restrict__ hub_col,
                             const int* __restrict__ hub_first, const float* __restrict__ pfeat,
                             const float* __restrict__ pcol, float* __restrict__ grad_feat,
@@ -716,15 +734,11 @@ gat_bwd_cols_combine_kernel(int H, int64_t C, const int* __restrict__ hub_col,
   const int64_t j = hub_col[blockIdx.x];
   const int s0 = hub_first[blockIdx.x], s1 = hub_first[blockIdx.x + 1];
   const int64_t HC = static_cast<int64_t>(H) * C;
-  for (int64_t k = threadIdx.x; k < HC; k += kThreads) {
-    float a = 0.0f;
-    for (int s = s0; s < s1; ++s) a += pfeat[static_cast<int64_t>(s) * HC + k];
-    grad_feat[j * HC + k] = a;
-  }
-  for (int h = threadIdx.x; h < H; h += kThreads) {
-    float a = 0.0f;
-    for (int s = s0; s < s1; ++s) a += pcol[static_cast<int64_t>(s) * H + h];
-    grad_attn_col[j * H + h] = a;
+  const int64_t k = (static_cast<int64_t>(blockIdx.y) * kCombineThreads + threadIdx.x) * VEC;
+  if (k < HC) st_vec(grad_feat + j * HC + k, ordered_sum<VEC>(pfeat + k, HC, s0, s1));
+  if (blockIdx.y == 0) {
+    for (int h = threadIdx.x; h < H; h += kCombineThreads)
+      grad_attn_col[j * H + h] = ordered_sum<1>(pcol + h, H, s0, s1);
   }
 }
 
@@ -772,6 +786,1047 @@ __global__ void gat_validate_kernel(int64_t n, int64_t nnz, const int* __restric
   }
 }
 
+
+// ====================================================================
+// Persistent cp.async ring kernels (C % 4 == 0, 16-byte aligned operands,
+// H <= kRingMaxH).  Work items (segments of hub rows/columns first, then
+// rows/columns of at most kSegLen edges, so every item has <= 32 edges:
+// one chunk) are taken from an atomic counter by whole warps.  For each
+// edge the warp streams the gathered feature tiles into a warp-private ring
+// of STAGES shared-memory slots with 16-byte cp.async copies, so STAGES
+// edges' rows are in flight per warp without holding registers; each lane
+// reads back only the float4 slots it copied itself.  The per-(edge, head)
+// softmax weights of the item are computed once by the edge-owner lanes and
+// kept in a warp-private shared array.  Sum orders are fixed (edge order
+// within an item, segment order in the combine kernels): deterministic.
+// ====================================================================
+constexpr int kRingThreads = 128;
+constexpr int kRingMaxH = 8;
+
+struct RingItem {
+  int64_t node;   // destination row (forward, K1) or source column (K2)
+  int e0, e1;     // edge range (CSR edges, or CSC positions for K2)
+  int seg;        // segment index, or -1 for a whole row/column
+};
+
+// Items [0, n_seg) are segments; [n_seg, n_seg + n) nodes.  Returns false
+// for a node that is a hub (handled by its segments).
+__device__ __forceinline__ bool ring_item(int it, int n_seg, const int* __restrict__ seg_node,
+                                          const int* __restrict__ seg_begin,
+                                          const int* __restrict__ seg_end,
+                                          const int* __restrict__ ptr, RingItem& r) {
+  if (it < n_seg) {
+    r.node = seg_node[it];
+    r.e0 = seg_begin[it];
+    r.e1 = seg_end[it];
+    r.seg = it;
+    return true;
+  }
+  r.node = it - n_seg;
+  r.e0 = ptr[r.node];
+  r.e1 = ptr[r.node + 1];
+  r.seg = -1;
+  return r.e1 - r.e0 <= kSegLen;
+}
+
+__device__ __forceinline__ int ring_next(int* counter, int lane) {
+  int it = 0;
+  if (lane == 0) it = atomicAdd(counter, 1);
+  return __shfl_sync(kFullMask, it, 0);
+}
+
+// Forward.  Items are (channel tile, item) pairs, tile-major.
+template <int STAGES>
+__global__ void __launch_bounds__(kRingThreads)
+gat_fwd_ring_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
+                    const int* __restrict__ col, const int* __restrict__ seg_row,
+                    const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
+                    const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                    const float* __restrict__ x, const float* __restrict__ bias, float slope,
+                    float p, uint64_t seed, float* __restrict__ out, float* __restrict__ pre,
+                    float* __restrict__ emax, float* __restrict__ esum,
+                    float* __restrict__ partial, int* __restrict__ counter) {
+  extern __shared__ float4 smem4[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int slot_f4 = H * 32;  // one 128-channel tile of every head
+  float4* ring = smem4 + warp * STAGES * slot_f4;
+  float* wsm = reinterpret_cast<float*>(smem4 + (kRingThreads / 32) * STAGES * slot_f4) +
+               warp * 32 * kRingMaxH;
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  const int per_tile = n_seg + n;
+  const int64_t n_tiles = (C + 127) / 128;
+  const int64_t total = n_tiles * per_tile;
+  const float hf = static_cast<float>(H);
+  for (;;) {
+    const int64_t item = ring_next(counter, lane);
+    if (item >= total) break;
+    const int64_t f0 = (item / per_tile) * 128;
+    RingItem r;
+    if (!ring_item(static_cast<int>(item % per_tile), n_seg, seg_row, seg_begin, seg_end, rowptr, r))
+      continue;
+    const int cnt = r.e1 - r.e0;
+    const int my = r.e0 + lane;
+    const int c = lane < cnt ? __ldg(col + my) : 0;
+    // per-(edge, head) weights of the item
+    for (int h = 0; h < H; ++h) {
+      const float ad = __ldg(attn_row + r.node * H + h);
+      const float ac = lane < cnt ? __ldg(attn_col + static_cast<int64_t>(c) * H + h) : 0.0f;
+      float m, s;
+      if (r.seg >= 0) {
+        m = emax[r.node * H + h];
+        s = esum[r.node * H + h];
+      } else {
+        const float e = lane < cnt ? leaky_f(ad + ac, slope) : kNegInit;
+        m = warp_max(e);
+        s = warp_sum(lane < cnt ? expf(e - m) : 0.0f);
+        if (lane == 0 && f0 == 0) {
+          emax[r.node * H + h] = m;
+          esum[r.node * H + h] = s;
+        }
+      }
+      wsm[lane * kRingMaxH + h] =
+          lane < cnt ? edge_weight(ad, ac, m, s, slope, p, seed, static_cast<uint64_t>(my) * H + h)
+                     : 0.0f;
+    }
+    __syncwarp();
+    const bool valid = f0 + lane * 4 < C;
+    const float* xt = x + f0 + lane * 4;
+    auto issue = [&](int k) {
+      if (k < cnt) {
+        const int ck = __shfl_sync(kFullMask, c, k);
+        float4* dst = ring + (k % STAGES) * slot_f4 + lane;
+        const float* src = xt + static_cast<int64_t>(ck) * HC;
+        if (valid)
+          for (int h = 0; h < H; ++h) cp_async16(dst + h * 32, src + static_cast<int64_t>(h) * C);
+      }
+      cp_async_commit();
+    };
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < STAGES; ++k) issue(k);
+    for (int k = 0; k < cnt; ++k) {
+      cp_async_wait<STAGES - 1>();
+      if (valid) {
+        const float4* slot = ring + (k % STAGES) * slot_f4 + lane;
+        for (int h = 0; h < H; ++h) vfma(acc, wsm[k * kRingMaxH + h], slot[h * 32]);
+      }
+      __syncwarp();
+      issue(k + STAGES);
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+    if (valid) {
+      const int64_t fi = f0 + lane * 4;
+      if (r.seg >= 0) {
+        st_vec(partial + static_cast<int64_t>(r.seg) * C + fi, acc);
+      } else {
+        const float4 bv = ldg_vec<4>(bias + fi);
+        float4 pv, ov;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float pj = vel(acc, j) / hf + vel(bv, j);
+          vel(pv, j) = pj;
+          vel(ov, j) = silu_f(pj);
+        }
+        st_vec(pre + r.node * C + fi, pv);
+        st_vec(out + r.node * C + fi, ov);
+      }
+    }
+  }
+}
+
+// Backward K1 (CSR rows): per item, per 128-channel tile, the dots of
+// g_pre[i]/H with every edge's x[j, h, tile]; the edge-owner lane
+// accumulates them over tiles.  Whole rows then run the softmax backward in
+// the warp; segments store their dots (the hub-row kernel finishes them).
+template <int STAGES>
+__global__ void __launch_bounds__(kRingThreads)
+gat_bwd_rows_ring_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
+                         const int* __restrict__ col, const int* __restrict__ seg_row,
+                         const int* __restrict__ seg_begin, const int* __restrict__ seg_end,
+                         int n_seg, const float* __restrict__ attn_row,
+                         const float* __restrict__ attn_col, const float* __restrict__ x,
+                         const float* __restrict__ pre, const float* __restrict__ emax,
+                         const float* __restrict__ esum, const float* __restrict__ grad_y,
+                         float slope, float p, uint64_t seed, float* __restrict__ gpre,
+                         float* __restrict__ glog, float* __restrict__ grad_attn_row,
+                         int* __restrict__ counter) {
+  extern __shared__ float4 smem4[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int slot_f4 = H * 32;
+  float4* ring = smem4 + warp * STAGES * slot_f4;
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  const int total = n_seg + n;
+  const float inv_h = 1.0f / static_cast<float>(H);
+  for (;;) {
+    const int it = ring_next(counter, lane);
+    if (it >= total) break;
+    RingItem r;
+    if (!ring_item(it, n_seg, seg_row, seg_begin, seg_end, rowptr, r)) continue;
+    const int cnt = r.e1 - r.e0;
+    const int my = r.e0 + lane;
+    const int c = lane < cnt ? __ldg(col + my) : 0;
+    float dacc[kRingMaxH];
+#pragma unroll
+    for (int h = 0; h < kRingMaxH; ++h) dacc[h] = 0.0f;
+    for (int64_t f0 = 0; f0 < C; f0 += 128) {
+      const int64_t fi = f0 + lane * 4;
+      const bool valid = fi < C;
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (valid) {
+        const float4 gy = ld_vec<4>(grad_y + r.node * C + fi);
+        const float4 pr = ld_vec<4>(pre + r.node * C + fi);
+        float4 gp;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vel(gp, j) = vel(gy, j) * silu_grad_f(vel(pr, j));
+        if (r.seg < 0) st_vec(gpre + r.node * C + fi, gp);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vel(g, j) = vel(gp, j) * inv_h;
+      }
+      const float* xt = x + fi;
+      auto issue = [&](int k) {
+        if (k < cnt) {
+          const int ck = __shfl_sync(kFullMask, c, k);
+          float4* dst = ring + (k % STAGES) * slot_f4 + lane;
+          const float* src = xt + static_cast<int64_t>(ck) * HC;
+          if (valid)
+            for (int h = 0; h < H; ++h) cp_async16(dst + h * 32, src + static_cast<int64_t>(h) * C);
+        }
+        cp_async_commit();
+      };
+#pragma unroll
+      for (int k = 0; k < STAGES; ++k) issue(k);
+      for (int k = 0; k < cnt; ++k) {
+        cp_async_wait<STAGES - 1>();
+        const float4* slot = ring + (k % STAGES) * slot_f4 + lane;
+#pragma unroll
+        for (int h = 0; h < kRingMaxH; ++h) {
+          if (h < H) {
+            float d = 0.0f;
+            if (valid) {
+              const float4 xv = slot[h * 32];
+              d = g.x * xv.x;
+              d = fmaf(g.y, xv.y, d);
+              d = fmaf(g.z, xv.z, d);
+              d = fmaf(g.w, xv.w, d);
+            }
+            d = warp_sum(d);
+            if (lane == k) dacc[h] += d;
+          }
+        }
+        __syncwarp();
+        issue(k + STAGES);
+      }
+      cp_async_wait<0>();
+      __syncwarp();
+    }
+    if (r.seg >= 0) {
+      if (lane < cnt) {
+#pragma unroll
+        for (int h = 0; h < kRingMaxH; ++h)
+          if (h < H) glog[static_cast<int64_t>(my) * H + h] = dacc[h];
+      }
+      continue;
+    }
+#pragma unroll
+    for (int h = 0; h < kRingMaxH; ++h) {
+      if (h >= H) break;
+      const float ad = attn_row[r.node * H + h];
+      const float m = emax[r.node * H + h], s = esum[r.node * H + h];
+      EdgeSoft es;
+      es.soft = 0.0f;
+      es.ge = 0.0f;
+      es.neg = false;
+      if (lane < cnt)
+        es = edge_soft(ad, attn_col[static_cast<int64_t>(c) * H + h], m, s, slope, p, seed,
+                       static_cast<uint64_t>(my) * H + h, dacc[h]);
+      const float wsum = warp_sum(es.soft * es.ge);
+      float gout = es.soft * (es.ge - wsum);
+      if (es.neg) gout *= slope;
+      if (lane < cnt) glog[static_cast<int64_t>(my) * H + h] = gout;
+      const float grow = warp_sum(lane < cnt ? gout : 0.0f);
+      if (lane == 0) grad_attn_row[r.node * H + h] = grow;
+    }
+  }
+}
+
+// Backward K2 (CSC columns): items are (256-channel tile, item) pairs,
+// tile-major.  grad_feat[j,h,tile] = sum_e w(e,h)/H g_pre[i_e, tile];
+// grad_attn_col[j,h] = sum_e grad_logit[e,h] (tile 0 only).
+template <int STAGES>
+__global__ void __launch_bounds__(kRingThreads)
+gat_bwd_cols_ring_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
+                         const int* __restrict__ row, const int* __restrict__ perm,
+                         const int* __restrict__ seg_col, const int* __restrict__ seg_begin,
+                         const int* __restrict__ seg_end, int n_seg,
+                         const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                         const float* __restrict__ emax, const float* __restrict__ esum,
+                         const float* __restrict__ gpre, const float* __restrict__ glog,
+                         float slope, float p, uint64_t seed, float* __restrict__ grad_feat,
+                         float* __restrict__ grad_attn_col, float* __restrict__ pfeat,
+                         float* __restrict__ pcol, int* __restrict__ counter) {
+  constexpr int VPL = 2;
+  extern __shared__ float4 smem4[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kSlot = 32 * VPL;
+  float4* ring = smem4 + warp * STAGES * kSlot;
+  float* wsm = reinterpret_cast<float*>(smem4 + (kRingThreads / 32) * STAGES * kSlot) +
+               warp * 32 * kRingMaxH;
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  const int per_tile = n_seg + n;
+  const int64_t n_tiles = (C + 4 * kSlot - 1) / (4 * kSlot);
+  const int64_t total = n_tiles * per_tile;
+  const float inv_h = 1.0f / static_cast<float>(H);
+  for (;;) {
+    const int64_t item = ring_next(counter, lane);
+    if (item >= total) break;
+    const int64_t f0 = (item / per_tile) * (4 * kSlot);
+    RingItem r;
+    if (!ring_item(static_cast<int>(item % per_tile), n_seg, seg_col, seg_begin, seg_end, colptr, r))
+      continue;
+    const int cnt = r.e1 - r.e0;
+    const int pos = r.e0 + lane;
+    int i = 0, e = 0;
+    if (lane < cnt) {
+      i = __ldg(row + pos);
+      e = __ldg(perm + pos);
+    }
+    for (int h = 0; h < H; ++h) {
+      float w = 0.0f;
+      if (lane < cnt) {
+        const int64_t ih = static_cast<int64_t>(i) * H + h;
+        w = edge_weight(__ldg(attn_row + ih), __ldg(attn_col + r.node * H + h), __ldg(emax + ih),
+                        __ldg(esum + ih), slope, p, seed, static_cast<uint64_t>(e) * H + h) * inv_h;
+      }
+      wsm[lane * kRingMaxH + h] = w;
+      if (f0 == 0) {
+        const float a = warp_sum(lane < cnt ? glog[static_cast<int64_t>(e) * H + h] : 0.0f);
+        if (lane == 0) {
+          if (r.seg >= 0) pcol[static_cast<int64_t>(r.seg) * H + h] = a;
+          else grad_attn_col[r.node * H + h] = a;
+        }
+      }
+    }
+    __syncwarp();
+    const float* gt = gpre + f0 + lane * 4;
+    auto issue = [&](int k) {
+      if (k < cnt) {
+        const int ik = __shfl_sync(kFullMask, i, k);
+        float4* dst = ring + (k % STAGES) * kSlot + lane;
+        const float* src = gt + static_cast<int64_t>(ik) * C;
+#pragma unroll
+        for (int q = 0; q < VPL; ++q)
+          if (f0 + (lane + q * 32) * 4 < C) cp_async16(dst + q * 32, src + q * 128);
+      }
+      cp_async_commit();
+    };
+    float4 acc[kRingMaxH][VPL];
+#pragma unroll
+    for (int h = 0; h < kRingMaxH; ++h)
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) acc[h][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < STAGES; ++k) issue(k);
+    for (int k = 0; k < cnt; ++k) {
+      cp_async_wait<STAGES - 1>();
+      const float4* slot = ring + (k % STAGES) * kSlot + lane;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        if (f0 + (lane + q * 32) * 4 < C) {
+          const float4 gv = slot[q * 32];
+#pragma unroll
+          for (int h = 0; h < kRingMaxH; ++h)
+            if (h < H) vfma(acc[h][q], wsm[k * kRingMaxH + h], gv);
+        }
+      }
+      __syncwarp();
+      issue(k + STAGES);
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+    float* dst = r.seg >= 0 ? pfeat + static_cast<int64_t>(r.seg) * HC : grad_feat + r.node * HC;
+#pragma unroll
+    for (int h = 0; h < kRingMaxH; ++h) {
+      if (h >= H) break;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t fi = f0 + (lane + q * 32) * 4;
+        if (fi < C) st_vec(dst + static_cast<int64_t>(h) * C + fi, acc[h][q]);
+      }
+    }
+  }
+}
+
+constexpr int kFwdStages = 6;
+constexpr int kK1Stages = 6;
+constexpr int kK2Stages = 8;
+
+// The kernel's dynamic shared-memory limit is raised to its largest use
+// (H = kRingMaxH) once; the persistent grid is sized for the actual use.
+template <typename K>
+int ring_grid(K kernel, size_t smem, size_t max_smem, int* cache) {
+  if (*cache == 0) {
+    CIGN_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(max_smem)),
+                    "gat: set smem");
+    *cache = persistent_grid(kernel, kRingThreads, smem);
+  }
+  return CIGN_OK;
+}
+
+size_t fwd_ring_smem(int H) {
+  return static_cast<size_t>(kRingThreads / 32) *
+         (static_cast<size_t>(kFwdStages) * H * 32 * 16 + 32 * kRingMaxH * sizeof(float));
+}
+size_t k1_ring_smem(int H) {
+  return static_cast<size_t>(kRingThreads / 32) * kK1Stages * H * 32 * 16;
+}
+size_t k2_ring_smem() {
+  return static_cast<size_t>(kRingThreads / 32) *
+         (static_cast<size_t>(kK2Stages) * 2 * 32 * 16 + 32 * kRingMaxH * sizeof(float));
+}
+
+// ------------------------------------------------------------ hub launches
+int launch_hub_stats(const cign_gat_plan* pl, int H, const float* attn_row, const float* attn_col,
+                     float slope, float* emax, float* esum, cudaStream_t s) {
+  const SegList& sl = pl->rows;
+  if (sl.n_heavy == 0) return CIGN_OK;
+  gat_hub_stats_kernel<<<dim3(static_cast<unsigned>(sl.n_heavy), H), kThreads, 0, s>>>(
+      H, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, slope, emax, esum);
+  CIGN_CHECK_LAUNCH("gat_hub_stats_kernel");
+  return CIGN_OK;
+}
+
+// Vector width of the combine kernels: 4 when every operand allows float4.
+bool combine_v4(int64_t n_feat, std::initializer_list<const void*> ptrs) {
+  if (n_feat % 4 != 0) return false;
+  for (const void* q : ptrs)
+    if (!aligned16(q)) return false;
+  return true;
+}
+
+unsigned combine_chunks(int64_t n_feat, int vec) {
+  const int64_t per_block = static_cast<int64_t>(kCombineThreads) * vec;
+  return static_cast<unsigned>((n_feat + per_block - 1) / per_block);
+}
+
+int launch_fwd_combine(const cign_gat_plan* pl, int H, int64_t C, const float* partial,
+                       const float* bias, float* pre, float* out, cudaStream_t s) {
+  const SegList& sl = pl->rows;
+  if (sl.n_heavy == 0) return CIGN_OK;
+  const bool v4 = combine_v4(C, {partial, bias, pre, out});
+  const dim3 grid(static_cast<unsigned>(sl.n_heavy), combine_chunks(C, v4 ? 4 : 1));
+  CIGN_REQUIRE(grid.y < 65536, CIGN_ERR_UNSUPPORTED, "gat: C too large for the hub combine");
+  if (v4)
+    gat_fwd_combine_kernel<4><<<grid, kCombineThreads, 0, s>>>(H, C, sl.heavy_row(),
+                                                               sl.heavy_first(), partial, bias, pre,
+                                                               out);
+  else
+    gat_fwd_combine_kernel<1><<<grid, kCombineThreads, 0, s>>>(H, C, sl.heavy_row(),
+                                                               sl.heavy_first(), partial, bias, pre,
+                                                               out);
+  CIGN_CHECK_LAUNCH("gat_fwd_combine_kernel");
+  return CIGN_OK;
+}
+
+int launch_bwd_hub_rows(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
+                        const float* attn_col, const float* pre, const float* emax,
+                        const float* esum, const float* gy, float slope, float p, uint64_t seed,
+                        float* gpre, float* glog, float* grow, cudaStream_t s) {
+  const SegList& sl = pl->rows;
+  if (sl.n_heavy == 0) return CIGN_OK;
+  gat_bwd_hub_rows_kernel<<<dim3(static_cast<unsigned>(sl.n_heavy), H), kThreads, 0, s>>>(
+      H, C, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, pre, emax, esum, gy, slope,
+      p, seed, gpre, glog, grow);
+  CIGN_CHECK_LAUNCH("gat_bwd_hub_rows_kernel");
+  return CIGN_OK;
+}
+
+int launch_bwd_cols_combine(const cign_gat_plan* pl, int H, int64_t C, const float* pfeat,
+                            const float* pcol, float* gfeat, float* gcol, cudaStream_t s) {
+  const SegList& sl = pl->cols;
+  if (sl.n_heavy == 0) return CIGN_OK;
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  const bool v4 = combine_v4(HC, {pfeat, gfeat});
+  const dim3 grid(static_cast<unsigned>(sl.n_heavy), combine_chunks(HC, v4 ? 4 : 1));
+  CIGN_REQUIRE(grid.y < 65536, CIGN_ERR_UNSUPPORTED, "gat: H*C too large for the hub combine");
+  if (v4)
+    gat_bwd_cols_combine_kernel<4><<<grid, kCombineThreads, 0, s>>>(
+        H, C, sl.heavy_row(), sl.heavy_first(), pfeat, pcol, gfeat, gcol);
+  else
+    gat_bwd_cols_combine_kernel<1><<<grid, kCombineThreads, 0, s>>>(
+        H, C, sl.heavy_row(), sl.heavy_first(), pfeat, pcol, gfeat, gcol);
+  CIGN_CHECK_LAUNCH("gat_bwd_cols_combine_kernel");
+  return CIGN_OK;
+}
+
+int launch_fwd_ring(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
+                    const float* attn_col, const float* x, const float* bias, float slope,
+                    float p, uint64_t seed, float* out, float* pre, float* emax, float* esum,
+                    float* partial, int* counter, cudaStream_t s) {
+  const SegList& sl = pl->rows;
+  {
+    const int rc = launch_hub_stats(pl, H, attn_row, attn_col, slope, emax, esum, s);
+    if (rc) return rc;
+  }
+  static thread_local int cache[64][kRingMaxH + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kernel = gat_fwd_ring_kernel<kFwdStages>;
+  const size_t smem = fwd_ring_smem(H);
+  int rc = ring_grid(kernel, smem, fwd_ring_smem(kRingMaxH), &cache[dev & 63][H]);
+  if (rc) return rc;
+  CIGN_CHECK_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), s), "gat: reset counter");
+  kernel<<<cache[dev & 63][H], kRingThreads, smem, s>>>(
+      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, x, bias, slope, p, seed, out,
+      pre, emax, esum, partial, counter);
+  CIGN_CHECK_LAUNCH("gat_fwd_ring_kernel");
+  return launch_fwd_combine(pl, H, C, partial, bias, pre, out, s);
+}
+
+int launch_bwd_rows_ring(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
+                         const float* attn_col, const float* x, const float* pre,
+                         const float* emax, const float* esum, const float* gy, float slope,
+                         float p, uint64_t seed, float* gpre, float* glog, float* grow,
+                         int* counter, cudaStream_t s) {
+  const SegList& sl = pl->rows;
+  static thread_local int cache[64][kRingMaxH + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kernel = gat_bwd_rows_ring_kernel<kK1Stages>;
+  const size_t smem = k1_ring_smem(H);
+  int rc = ring_grid(kernel, smem, k1_ring_smem(kRingMaxH), &cache[dev & 63][H]);
+  if (rc) return rc;
+  CIGN_CHECK_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), s), "gat: reset counter");
+  kernel<<<cache[dev & 63][H], kRingThreads, smem, s>>>(
+      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, x, pre, emax, esum, gy, slope,
+      p, seed, gpre, glog, grow, counter);
+  CIGN_CHECK_LAUNCH("gat_bwd_rows_ring_kernel");
+  {
+    const int rc = launch_bwd_hub_rows(pl, H, C, attn_row, attn_col, pre, emax, esum, gy, slope, p,
+                                       seed, gpre, glog, grow, s);
+    if (rc) return rc;
+  }
+  return CIGN_OK;
+}
+
+int launch_bwd_cols_ring(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
+                         const float* attn_col, const float* emax, const float* esum,
+                         const float* gpre, const float* glog, float slope, float p,
+                         uint64_t seed, float* gfeat, float* gcol, float* pfeat, float* pcol,
+                         int* counter, cudaStream_t s) {
+  const SegList& sl = pl->cols;
+  static thread_local int cache[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kernel = gat_bwd_cols_ring_kernel<kK2Stages>;
+  const size_t smem = k2_ring_smem();
+  int rc = ring_grid(kernel, smem, smem, &cache[dev & 63]);
+  if (rc) return rc;
+  CIGN_CHECK_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), s), "gat: reset counter");
+  kernel<<<cache[dev & 63], kRingThreads, smem, s>>>(
+      static_cast<int>(pl->n), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, emax, esum, gpre, glog, slope,
+      p, seed, gfeat, gcol, pfeat, pcol, counter);
+  CIGN_CHECK_LAUNCH("gat_bwd_cols_ring_kernel");
+  return launch_bwd_cols_combine(pl, H, C, pfeat, pcol, gfeat, gcol, s);
+}
+
+
+// ====================================================================
+// TMA-ring kernels (C % 4 == 0, 16-byte aligned operands, H <= kRingMaxH,
+// gathered row <= kTmaSlotMax bytes).  Same work items as the cp.async ring
+// kernels (every item has <= 32 edges), but each gathered row -- the whole
+// [H, C] block of x[j] in the forward and K1, the C-wide g_pre[i] row in K2
+// -- is ONE cp.async.bulk copy issued by lane 0 and completed on its slot's
+// mbarrier.  Waits are bounded; on expiry the warp records kStatusTimeout in
+// ctl[1], lets its in-flight copies land (bounded) and stops.
+// ====================================================================
+constexpr int kTmaWarps = 4;
+constexpr uint32_t kTmaSlotMax = 16384;
+
+struct TmaWarpRing {
+  float* slots;
+  uint64_t* bars;
+  float* wsm;
+  int stages;
+  int slot_floats;
+  uint32_t phase;
+};
+
+// smem layout: [slots of all warps][barriers of all warps][weights of all warps]
+__device__ __forceinline__ TmaWarpRing tma_ring_setup(unsigned char* smem, int stages,
+                                                      int slot_floats, int warp, int lane) {
+  TmaWarpRing r;
+  r.stages = stages;
+  r.slot_floats = slot_floats;
+  r.phase = 0;
+  const size_t slot_bytes_all = static_cast<size_t>(kTmaWarps) * stages * slot_floats * 4;
+  r.slots = reinterpret_cast<float*>(smem) + static_cast<size_t>(warp) * stages * slot_floats;
+  r.bars = reinterpret_cast<uint64_t*>(smem + slot_bytes_all) + warp * stages;
+  r.wsm = reinterpret_cast<float*>(smem + slot_bytes_all + kTmaWarps * stages * 8) +
+          warp * 32 * kRingMaxH;
+  if (lane == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(smem_u32(&r.bars[s]), 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  return r;
+}
+size_t tma_smem_bytes(int stages, int slot_floats) {
+  return static_cast<size_t>(kTmaWarps) *
+         (static_cast<size_t>(stages) * (slot_floats * 4 + 8) + 32 * kRingMaxH * 4);
+}
+int tma_stages(uint32_t slot_bytes, int target_bytes, int lo, int hi) {
+  return std::max(lo, std::min(hi, static_cast<int>(target_bytes / slot_bytes)));
+}
+
+// lane 0: arm slot k % stages and copy `bytes` from src into it
+__device__ __forceinline__ void tma_fill(TmaWarpRing& r, int k, const float* src, uint32_t bytes,
+                                         int lane) {
+  if (lane == 0) {
+    const int sl = k % r.stages;
+    const uint32_t bar = smem_u32(&r.bars[sl]);
+    mbar_expect_tx(bar, bytes);
+    bulk_g2s(smem_u32(r.slots + static_cast<size_t>(sl) * r.slot_floats), src, bytes, bar);
+  }
+}
+// all lanes: wait for slot k % stages; false (warp-uniform) on timeout
+__device__ __forceinline__ bool tma_take(TmaWarpRing& r, int k) {
+  const int sl = k % r.stages;
+  const bool got = mbar_wait(smem_u32(&r.bars[sl]), (r.phase >> sl) & 1u);
+  if (!__all_sync(kFullMask, got)) return false;
+  r.phase ^= 1u << sl;
+  return true;
+}
+// after the warp consumed slot k % stages: order its reads before a refill
+__device__ __forceinline__ void tma_release(int lane) {
+  __syncwarp();
+  if (lane == 0) fence_proxy_async();
+}
+// on failure: let fills [lo, hi) land (bounded) before the warp stops
+__device__ __forceinline__ void tma_drain(TmaWarpRing& r, int lo, int hi, int* status, int lane) {
+  if (lane == 0) atomicExch(status, kStatusTimeout);
+  for (int k = lo; k < hi; ++k) {
+    const int sl = k % r.stages;
+    mbar_wait(smem_u32(&r.bars[sl]), (r.phase >> sl) & 1u);
+    r.phase ^= 1u << sl;
+  }
+}
+
+// Forward: items are whole rows / hub segments.
+template <int VPL>
+__global__ void __launch_bounds__(kTmaWarps * 32)
+gat_fwd_tma_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
+                   const int* __restrict__ col, const int* __restrict__ seg_row,
+                   const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
+                   const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                   const float* __restrict__ x, const float* __restrict__ bias, float slope,
+                   float p, uint64_t seed, float* __restrict__ out, float* __restrict__ pre,
+                   float* __restrict__ emax, float* __restrict__ esum,
+                   float* __restrict__ partial, int stages, int* __restrict__ ctl) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  TmaWarpRing ring = tma_ring_setup(smem_raw, stages, static_cast<int>(HC), warp, lane);
+  const uint32_t bytes = static_cast<uint32_t>(HC * 4);
+  const int C4 = static_cast<int>(C / 4);
+  const int total = n_seg + n;
+  const float hf = static_cast<float>(H);
+  for (;;) {
+    const int it = ring_next(ctl, lane);
+    if (it >= total) break;
+    RingItem r;
+    if (!ring_item(it, n_seg, seg_row, seg_begin, seg_end, rowptr, r)) continue;
+    const int cnt = r.e1 - r.e0;
+    const int my = r.e0 + lane;
+    const int c = lane < cnt ? __ldg(col + my) : 0;
+    auto issue = [&](int k) {
+      if (k < cnt) {
+        const int ck = __shfl_sync(kFullMask, c, k);
+        tma_fill(ring, k, x + static_cast<int64_t>(ck) * HC, bytes, lane);
+      }
+    };
+    for (int k = 0; k < stages; ++k) issue(k);  // copies overlap the weight math
+    for (int h = 0; h < H; ++h) {
+      const float ad = __ldg(attn_row + r.node * H + h);
+      const float ac = lane < cnt ? __ldg(attn_col + static_cast<int64_t>(c) * H + h) : 0.0f;
+      float m, sm;
+      if (r.seg >= 0) {
+        m = emax[r.node * H + h];
+        sm = esum[r.node * H + h];
+      } else {
+        const float e = lane < cnt ? leaky_f(ad + ac, slope) : kNegInit;
+        m = warp_max(e);
+        sm = warp_sum(lane < cnt ? expf(e - m) : 0.0f);
+        if (lane == 0) {
+          emax[r.node * H + h] = m;
+          esum[r.node * H + h] = sm;
+        }
+      }
+      ring.wsm[lane * kRingMaxH + h] =
+          lane < cnt ? edge_weight(ad, ac, m, sm, slope, p, seed, static_cast<uint64_t>(my) * H + h)
+                     : 0.0f;
+    }
+    __syncwarp();
+    float4 acc[VPL];
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < cnt; ++k) {
+      if (!tma_take(ring, k)) {
+        tma_drain(ring, k, min(k + stages, cnt), ctl + 1, lane);
+        return;
+      }
+      const float4* slot = reinterpret_cast<const float4*>(ring.slots + static_cast<size_t>(k % stages) * HC);
+      for (int h = 0; h < H; ++h) {
+        const float w = ring.wsm[k * kRingMaxH + h];
+#pragma unroll
+        for (int q = 0; q < VPL; ++q)
+          if (lane + q * 32 < C4) vfma(acc[q], w, slot[h * C4 + lane + q * 32]);
+      }
+      tma_release(lane);
+      issue(k + stages);
+    }
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      if (lane + q * 32 >= C4) continue;
+      const int64_t fi = static_cast<int64_t>(lane + q * 32) * 4;
+      if (r.seg >= 0) {
+        st_vec(partial + static_cast<int64_t>(r.seg) * C + fi, acc[q]);
+      } else {
+        const float4 bv = ldg_vec<4>(bias + fi);
+        float4 pv, ov;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float pj = vel(acc[q], j) / hf + vel(bv, j);
+          vel(pv, j) = pj;
+          vel(ov, j) = silu_f(pj);
+        }
+        st_vec(pre + r.node * C + fi, pv);
+        st_vec(out + r.node * C + fi, ov);
+      }
+    }
+  }
+}
+
+// Backward K1 (CSR rows) on the TMA ring: dots of g_pre[i]/H with each
+// edge's x[j] block, then the softmax backward (whole rows) or the dots
+// stored for the hub-row kernel (segments).
+template <int VPL>
+__global__ void __launch_bounds__(kTmaWarps * 32)
+gat_bwd_rows_tma_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
+                        const int* __restrict__ col, const int* __restrict__ seg_row,
+                        const int* __restrict__ seg_begin, const int* __restrict__ seg_end,
+                        int n_seg, const float* __restrict__ attn_row,
+                        const float* __restrict__ attn_col, const float* __restrict__ x,
+                        const float* __restrict__ pre, const float* __restrict__ emax,
+                        const float* __restrict__ esum, const float* __restrict__ grad_y,
+                        float slope, float p, uint64_t seed, float* __restrict__ gpre,
+                        float* __restrict__ glog, float* __restrict__ grad_attn_row,
+                        int stages, int* __restrict__ ctl) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  TmaWarpRing ring = tma_ring_setup(smem_raw, stages, static_cast<int>(HC), warp, lane);
+  const uint32_t bytes = static_cast<uint32_t>(HC * 4);
+  const int C4 = static_cast<int>(C / 4);
+  const int total = n_seg + n;
+  const float inv_h = 1.0f / static_cast<float>(H);
+  for (;;) {
+    const int it = ring_next(ctl, lane);
+    if (it >= total) break;
+    RingItem r;
+    if (!ring_item(it, n_seg, seg_row, seg_begin, seg_end, rowptr, r)) continue;
+    const int cnt = r.e1 - r.e0;
+    const int my = r.e0 + lane;
+    const int c = lane < cnt ? __ldg(col + my) : 0;
+    auto issue = [&](int k) {
+      if (k < cnt) {
+        const int ck = __shfl_sync(kFullMask, c, k);
+        tma_fill(ring, k, x + static_cast<int64_t>(ck) * HC, bytes, lane);
+      }
+    };
+    for (int k = 0; k < stages; ++k) issue(k);
+    float4 g[VPL];
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      g[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (lane + q * 32 < C4) {
+        const int64_t fi = static_cast<int64_t>(lane + q * 32) * 4;
+        const float4 gy = ld_vec<4>(grad_y + r.node * C + fi);
+        const float4 pr = ld_vec<4>(pre + r.node * C + fi);
+        float4 gp;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vel(gp, j) = vel(gy, j) * silu_grad_f(vel(pr, j));
+        if (r.seg < 0) st_vec(gpre + r.node * C + fi, gp);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vel(g[q], j) = vel(gp, j) * inv_h;
+      }
+    }
+    float dacc[kRingMaxH];
+#pragma unroll
+    for (int h = 0; h < kRingMaxH; ++h) dacc[h] = 0.0f;
+    for (int k = 0; k < cnt; ++k) {
+      if (!tma_take(ring, k)) {
+        tma_drain(ring, k, min(k + stages, cnt), ctl + 1, lane);
+        return;
+      }
+      const float4* slot = reinterpret_cast<const float4*>(ring.slots + static_cast<size_t>(k % stages) * HC);
+#pragma unroll
+      for (int h = 0; h < kRingMaxH; ++h) {
+        if (h < H) {
+          float d = 0.0f;
+#pragma unroll
+          for (int q = 0; q < VPL; ++q) {
+            if (lane + q * 32 < C4) {
+              const float4 xv = slot[h * C4 + lane + q * 32];
+              d = fmaf(g[q].x, xv.x, d);
+              d = fmaf(g[q].y, xv.y, d);
+              d = fmaf(g[q].z, xv.z, d);
+              d = fmaf(g[q].w, xv.w, d);
+            }
+          }
+          d = warp_sum(d);
+          if (lane == k) dacc[h] = d;
+        }
+      }
+      tma_release(lane);
+      issue(k + stages);
+    }
+    if (r.seg >= 0) {
+      if (lane < cnt) {
+#pragma unroll
+        for (int h = 0; h < kRingMaxH; ++h)
+          if (h < H) glog[static_cast<int64_t>(my) * H + h] = dacc[h];
+      }
+      continue;
+    }
+#pragma unroll
+    for (int h = 0; h < kRingMaxH; ++h) {
+      if (h >= H) break;
+      const float ad = attn_row[r.node * H + h];
+      const float m = emax[r.node * H + h], s = esum[r.node * H + h];
+      EdgeSoft es;
+      es.soft = 0.0f;
+      es.ge = 0.0f;
+      es.neg = false;
+      if (lane < cnt)
+        es = edge_soft(ad, attn_col[static_cast<int64_t>(c) * H + h], m, s, slope, p, seed,
+                       static_cast<uint64_t>(my) * H + h, dacc[h]);
+      const float wsum = warp_sum(es.soft * es.ge);
+      float gout = es.soft * (es.ge - wsum);
+      if (es.neg) gout *= slope;
+      if (lane < cnt) glog[static_cast<int64_t>(my) * H + h] = gout;
+      const float grow = warp_sum(lane < cnt ? gout : 0.0f);
+      if (lane == 0) grad_attn_row[r.node * H + h] = grow;
+    }
+  }
+}
+
+// Backward K2 (CSC columns) on the TMA ring: g_pre[i] rows, heads in groups
+// of four accumulated in registers.
+template <int VPL>
+__global__ void __launch_bounds__(kTmaWarps * 32)
+gat_bwd_cols_tma_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
+                        const int* __restrict__ row, const int* __restrict__ perm,
+                        const int* __restrict__ seg_col, const int* __restrict__ seg_begin,
+                        const int* __restrict__ seg_end, int n_seg,
+                        const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                        const float* __restrict__ emax, const float* __restrict__ esum,
+                        const float* __restrict__ gpre, const float* __restrict__ glog,
+                        float slope, float p, uint64_t seed, float* __restrict__ grad_feat,
+                        float* __restrict__ grad_attn_col, float* __restrict__ pfeat,
+                        float* __restrict__ pcol, int stages, int* __restrict__ ctl) {
+  constexpr int HB = 4;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  TmaWarpRing ring = tma_ring_setup(smem_raw, stages, static_cast<int>(C), warp, lane);
+  const uint32_t bytes = static_cast<uint32_t>(C * 4);
+  const int C4 = static_cast<int>(C / 4);
+  const int64_t HC = static_cast<int64_t>(H) * C;
+  const int total = n_seg + n;
+  const float inv_h = 1.0f / static_cast<float>(H);
+  for (;;) {
+    const int it = ring_next(ctl, lane);
+    if (it >= total) break;
+    RingItem r;
+    if (!ring_item(it, n_seg, seg_col, seg_begin, seg_end, colptr, r)) continue;
+    const int cnt = r.e1 - r.e0;
+    const int pos = r.e0 + lane;
+    int i = 0, e = 0;
+    if (lane < cnt) {
+      i = __ldg(row + pos);
+      e = __ldg(perm + pos);
+    }
+    for (int h = 0; h < H; ++h) {
+      float w = 0.0f;
+      if (lane < cnt) {
+        const int64_t ih = static_cast<int64_t>(i) * H + h;
+        w = edge_weight(__ldg(attn_row + ih), __ldg(attn_col + r.node * H + h), __ldg(emax + ih),
+                        __ldg(esum + ih), slope, p, seed, static_cast<uint64_t>(e) * H + h) * inv_h;
+      }
+      ring.wsm[lane * kRingMaxH + h] = w;
+      const float a = warp_sum(lane < cnt ? glog[static_cast<int64_t>(e) * H + h] : 0.0f);
+      if (lane == 0) {
+        if (r.seg >= 0) pcol[static_cast<int64_t>(r.seg) * H + h] = a;
+        else grad_attn_col[r.node * H + h] = a;
+      }
+    }
+    __syncwarp();
+    float* dst = r.seg >= 0 ? pfeat + static_cast<int64_t>(r.seg) * HC : grad_feat + r.node * HC;
+    auto issue = [&](int k) {
+      if (k < cnt) {
+        const int ik = __shfl_sync(kFullMask, i, k);
+        tma_fill(ring, k, gpre + static_cast<int64_t>(ik) * C, bytes, lane);
+      }
+    };
+    for (int h0 = 0; h0 < H; h0 += HB) {
+      float4 acc[HB][VPL];
+#pragma unroll
+      for (int hh = 0; hh < HB; ++hh)
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) acc[hh][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < stages; ++k) issue(k);
+      for (int k = 0; k < cnt; ++k) {
+        if (!tma_take(ring, k)) {
+          tma_drain(ring, k, min(k + stages, cnt), ctl + 1, lane);
+          return;
+        }
+        const float4* slot = reinterpret_cast<const float4*>(ring.slots + static_cast<size_t>(k % stages) * C);
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) {
+          if (lane + q * 32 < C4) {
+            const float4 gv = slot[lane + q * 32];
+#pragma unroll
+            for (int hh = 0; hh < HB; ++hh)
+              if (h0 + hh < H) vfma(acc[hh][q], ring.wsm[k * kRingMaxH + h0 + hh], gv);
+          }
+        }
+        tma_release(lane);
+        issue(k + stages);
+      }
+#pragma unroll
+      for (int hh = 0; hh < HB; ++hh) {
+        if (h0 + hh >= H) break;
+#pragma unroll
+        for (int q = 0; q < VPL; ++q)
+          if (lane + q * 32 < C4)
+            st_vec(dst + static_cast<int64_t>(h0 + hh) * C + static_cast<int64_t>(lane + q * 32) * 4,
+                   acc[hh][q]);
+      }
+    }
+  }
+}
+
+// Persistent grid for `kernel` with `smem` bytes, cached per (device, smem);
+// the kernel's dynamic shared-memory limit is raised once per device.
+template <typename K>
+int tma_grid(K kernel, size_t smem, int* grid) {
+  static std::mutex mu;
+  static std::map<std::pair<int, size_t>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, smem});
+  if (it != cache.end()) {
+    *grid = it->second;
+    return CIGN_OK;
+  }
+  CIGN_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024),
+                  "gat: set smem");
+  *grid = persistent_grid(kernel, kTmaWarps * 32, smem);
+  cache[{dev, smem}] = *grid;
+  return CIGN_OK;
+}
+
+#define CIGN_TMA_VPL_DISPATCH(C4_, CALL)                        \
+  do {                                                          \
+    if ((C4_) <= 32) { constexpr int P_ = 1; CALL; }            \
+    else if ((C4_) <= 64) { constexpr int P_ = 2; CALL; }       \
+    else if ((C4_) <= 128) { constexpr int P_ = 4; CALL; }      \
+    else { constexpr int P_ = 8; CALL; }                        \
+  } while (0)
+
+template <int VPL>
+int launch_fwd_tma_vpl(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
+                       const float* attn_col, const float* x, const float* bias, float slope,
+                       float p, uint64_t seed, float* out, float* pre, float* emax, float* esum,
+                       float* partial, int* ctl, cudaStream_t s) {
+  const SegList& sl = pl->rows;
+  {
+    const int rc = launch_hub_stats(pl, H, attn_row, attn_col, slope, emax, esum, s);
+    if (rc) return rc;
+  }
+  const uint32_t slot_bytes = static_cast<uint32_t>(H * C * 4);
+  const int stages = tma_stages(slot_bytes, 24576, 2, 8);
+  const size_t smem = tma_smem_bytes(stages, static_cast<int>(H * C));
+  auto kernel = gat_fwd_tma_kernel<VPL>;
+  int grid = 0;
+  int rc = tma_grid(kernel, smem, &grid);
+  if (rc) return rc;
+  CIGN_CHECK_CUDA(cudaMemsetAsync(ctl, 0, 2 * sizeof(int), s), "gat: reset control");
+  kernel<<<grid, kTmaWarps * 32, smem, s>>>(
+      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, x, bias, slope, p, seed, out,
+      pre, emax, esum, partial, stages, ctl);
+  CIGN_CHECK_LAUNCH("gat_fwd_tma_kernel");
+  return launch_fwd_combine(pl, H, C, partial, bias, pre, out, s);
+}
+
+template <int VPL>
+int launch_bwd_rows_tma_vpl(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
+                            const float* attn_col, const float* x, const float* pre,
+                            const float* emax, const float* esum, const float* gy, float slope,
+                            float p, uint64_t seed, float* gpre, float* glog, float* grow,
+                            int* ctl, cudaStream_t s) {
+  const SegList& sl = pl->rows;
+  const uint32_t slot_bytes = static_cast<uint32_t>(H * C * 4);
+  const int stages = tma_stages(slot_bytes, 24576, 2, 8);
+  const size_t smem = tma_smem_bytes(stages, static_cast<int>(H * C));
+  auto kernel = gat_bwd_rows_tma_kernel<VPL>;
+  int grid = 0;
+  int rc = tma_grid(kernel, smem, &grid);
+  if (rc) return rc;
+  CIGN_CHECK_CUDA(cudaMemsetAsync(ctl, 0, 2 * sizeof(int), s), "gat: reset control");
+  kernel<<<grid, kTmaWarps * 32, smem, s>>>(
+      static_cast<int>(pl->n), H, C, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, x, pre, emax, esum, gy, slope,
+      p, seed, gpre, glog, grow, stages, ctl);
+  CIGN_CHECK_LAUNCH("gat_bwd_rows_tma_kernel");
+  {
+    const int rc = launch_bwd_hub_rows(pl, H, C, attn_row, attn_col, pre, emax, esum, gy, slope, p,
+                                       seed, gpre, glog, grow, s);
+    if (rc) return rc;
+  }
+  return CIGN_OK;
+}
+
+template <int VPL>
+int launch_bwd_cols_tma_vpl(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
+                            const float* attn_col, const float* emax, const float* esum,
+                            const float* gpre, const float* glog, float slope, float p,
+                            uint64_t seed, float* gfeat, float* gcol, float* pfeat, float* pcol,
+                            int* ctl, cudaStream_t s) {
+  const SegList& sl = pl->cols;
+  const uint32_t slot_bytes = static_cast<uint32_t>(C * 4);
+  const int stages = tma_stages(slot_bytes, 16384, 4, 8);
+  const size_t smem = tma_smem_bytes(stages, static_cast<int>(C));
+  auto kernel = gat_bwd_cols_tma_kernel<VPL>;
+  int grid = 0;
+  int rc = tma_grid(kernel, smem, &grid);
+  if (rc) return rc;
+  CIGN_CHECK_CUDA(cudaMemsetAsync(ctl, 0, 2 * sizeof(int), s), "gat: reset control");
+  kernel<<<grid, kTmaWarps * 32, smem, s>>>(
+      static_cast<int>(pl->n), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, emax, esum, gpre, glog, slope,
+      p, seed, gfeat, gcol, pfeat, pcol, stages, ctl);
+  CIGN_CHECK_LAUNCH("gat_bwd_cols_tma_kernel");
+  return launch_bwd_cols_combine(pl, H, C, pfeat, pcol, gfeat, gcol, s);
+}
+
 // ------------------------------------------------------------ dispatch
 size_t rnd(size_t b) { return (b + 255) / 256 * 256; }
 
@@ -782,10 +1837,9 @@ int launch_fwd_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_
                    cudaStream_t s) {
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const SegList& sl = pl->rows;
-  if (sl.n_heavy > 0) {
-    gat_hub_stats_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
-        H, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, slope, emax, esum);
-    CIGN_CHECK_LAUNCH("gat_hub_stats_kernel");
+  {
+    const int rc = launch_hub_stats(pl, H, attn_row, attn_col, slope, emax, esum, s);
+    if (rc) return rc;
   }
   const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
   const int64_t grid = seg_blocks + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
@@ -795,12 +1849,7 @@ int launch_fwd_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_
       sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
       x, bias, slope, p, seed, out, pre, emax, esum, partial);
   CIGN_CHECK_LAUNCH("gat_fwd_kernel");
-  if (sl.n_heavy > 0) {
-    gat_fwd_combine_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
-        H, C, sl.heavy_row(), sl.heavy_first(), partial, bias, pre, out);
-    CIGN_CHECK_LAUNCH("gat_fwd_combine_kernel");
-  }
-  return CIGN_OK;
+  return launch_fwd_combine(pl, H, C, partial, bias, pre, out, s);
 }
 
 template <int VEC, int VPL, int LPR>
@@ -818,11 +1867,10 @@ int launch_bwd_rows_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* 
       sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
       x, pre, emax, esum, gy, slope, p, seed, gpre, glog, grow);
   CIGN_CHECK_LAUNCH("gat_bwd_rows_kernel");
-  if (sl.n_heavy > 0) {
-    gat_bwd_hub_rows_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
-        H, C, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, pre, emax, esum, gy, slope,
-        p, seed, gpre, glog, grow);
-    CIGN_CHECK_LAUNCH("gat_bwd_hub_rows_kernel");
+  {
+    const int rc = launch_bwd_hub_rows(pl, H, C, attn_row, attn_col, pre, emax, esum, gy, slope, p,
+                                       seed, gpre, glog, grow, s);
+    if (rc) return rc;
   }
   return CIGN_OK;
 }
@@ -841,12 +1889,7 @@ int launch_bwd_cols_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* 
       sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
       emax, esum, gpre, glog, slope, p, seed, gfeat, gcol, pfeat, pcol);
   CIGN_CHECK_LAUNCH("gat_bwd_cols_kernel");
-  if (sl.n_heavy > 0) {
-    gat_bwd_cols_combine_kernel<<<static_cast<unsigned>(sl.n_heavy), kThreads, 0, s>>>(
-        H, C, sl.heavy_row(), sl.heavy_first(), pfeat, pcol, gfeat, gcol);
-    CIGN_CHECK_LAUNCH("gat_bwd_cols_combine_kernel");
-  }
-  return CIGN_OK;
+  return launch_bwd_cols_combine(pl, H, C, pfeat, pcol, gfeat, gcol, s);
 }
 
 // Shape rule shared by the kernels: VEC=4 when C%4==0 and the feature
@@ -870,14 +1913,15 @@ int check_plan(const cign_gat_plan* pl, int H, int64_t C, const char* name) {
   return CIGN_OK;
 }
 
+// forward workspace: hub-row partials [n_seg_rows * C] | work counter
 size_t fwd_ws_bytes(const cign_gat_plan* pl, int64_t C) {
-  return rnd(static_cast<size_t>(pl->rows.n_seg) * C * sizeof(float));
+  return rnd(static_cast<size_t>(pl->rows.n_seg) * C * sizeof(float)) + 256;
 }
 
 // backward workspace: g_pre [N*C] | grad_logit [nnz*H] | colsum partials |
 // column-segment partials [n_seg*(H*C)] | [n_seg*H]
 struct BwdLayout {
-  size_t gpre, glog, csum, pfeat, pcol, total;
+  size_t gpre, glog, csum, pfeat, pcol, counters, total;
 };
 BwdLayout bwd_layout(const cign_gat_plan* pl, int H, int64_t C) {
   BwdLayout L;
@@ -886,7 +1930,8 @@ BwdLayout bwd_layout(const cign_gat_plan* pl, int H, int64_t C) {
   L.csum = L.glog + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float));
   L.pfeat = L.csum + rnd(static_cast<size_t>(colsum_chunks(pl->n)) * C * sizeof(float));
   L.pcol = L.pfeat + rnd(static_cast<size_t>(pl->cols.n_seg) * H * C * sizeof(float));
-  L.total = L.pcol + rnd(static_cast<size_t>(pl->cols.n_seg) * H * sizeof(float));
+  L.counters = L.pcol + rnd(static_cast<size_t>(pl->cols.n_seg) * H * sizeof(float));
+  L.total = L.counters + 256;
   return L;
 }
 
@@ -998,6 +2043,17 @@ int cign_gat_fwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const
   const bool v4 = C % 4 == 0 && aligned16(in_feat) && aligned16(out) && aligned16(pre) &&
                   aligned16(bias) && aligned16(partial);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool tma_ok = v4 && heads <= kRingMaxH && C <= 1024 &&
+                      static_cast<uint64_t>(heads) * C * 4 <= kTmaSlotMax;
+  if (tma_ok) {
+    int* ctl = reinterpret_cast<int*>(static_cast<char*>(ws) + need - 256);
+    CIGN_TMA_VPL_DISPATCH(C / 4, return (launch_fwd_tma_vpl<P_>(pl, heads, C, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed, out, pre, edge_max, edge_sum, partial, ctl, s)));
+  }
+  if (v4 && heads <= kRingMaxH) {
+    int* counter = reinterpret_cast<int*>(static_cast<char*>(ws) + need - 256);
+    return launch_fwd_ring(pl, heads, C, attn_row, attn_col, in_feat, bias, negative_slope,
+                           attn_drop, seed, out, pre, edge_max, edge_sum, partial, counter, s);
+  }
   if (v4) {
     CIGN_GAT_DISPATCH(4, C / 4, return (launch_fwd_cfg<V_, P_, L_>(pl, heads, C, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed, out, pre, edge_max, edge_sum, partial, s)));
   }
@@ -1036,8 +2092,29 @@ int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const
   float* csum = reinterpret_cast<float*>(w + L.csum);
   float* pfeat = reinterpret_cast<float*>(w + L.pfeat);
   float* pcol = reinterpret_cast<float*>(w + L.pcol);
+  int* counters = reinterpret_cast<int*>(w + L.counters);
   const bool v4 = C % 4 == 0 && aligned16(in_feat) && aligned16(pre) && aligned16(grad_y) &&
                   aligned16(grad_feat);
+  const bool tma_ok = v4 && heads <= kRingMaxH && C <= 1024 &&
+                      static_cast<uint64_t>(heads) * C * 4 <= kTmaSlotMax;
+  if (tma_ok) {
+    CIGN_TMA_VPL_DISPATCH(C / 4, rc = (launch_bwd_rows_tma_vpl<P_>(pl, heads, C, attn_row, attn_col, in_feat, pre, edge_max, edge_sum, grad_y, negative_slope, attn_drop, seed, gpre, glog, grad_attn_row, counters, s)));
+    if (rc) return rc;
+    CIGN_TMA_VPL_DISPATCH(C / 4, rc = (launch_bwd_cols_tma_vpl<P_>(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog, negative_slope, attn_drop, seed, grad_feat, grad_attn_col, pfeat, pcol, counters + 2, s)));
+    if (rc) return rc;
+    return colsum_f32(gpre, pl->n, C, csum, grad_bias, s);
+  }
+  if (v4 && heads <= kRingMaxH) {
+    rc = launch_bwd_rows_ring(pl, heads, C, attn_row, attn_col, in_feat, pre, edge_max, edge_sum,
+                              grad_y, negative_slope, attn_drop, seed, gpre, glog, grad_attn_row,
+                              counters, s);
+    if (rc) return rc;
+    rc = launch_bwd_cols_ring(pl, heads, C, attn_row, attn_col, edge_max, edge_sum, gpre, glog,
+                              negative_slope, attn_drop, seed, grad_feat, grad_attn_col, pfeat,
+                              pcol, counters + 1, s);
+    if (rc) return rc;
+    return colsum_f32(gpre, pl->n, C, csum, grad_bias, s);
+  }
   if (v4) {
     CIGN_GAT_DISPATCH(4, C / 4, rc = (launch_bwd_rows_cfg<V_, P_, L_>(pl, heads, C, attn_row, attn_col, in_feat, pre, edge_max, edge_sum, grad_y, negative_slope, attn_drop, seed, gpre, glog, grad_attn_row, s)));
   } else {

@@ -12,6 +12,7 @@ namespace cign {
 namespace {
 
 constexpr int kColThreads = 256;
+constexpr int kSumWarps = 16;
 
 __global__ void colsum_stage1_kernel(const float* __restrict__ a, int64_t n,
                                      int64_t c, int64_t rows_per_chunk,
@@ -21,19 +22,36 @@ __global__ void colsum_stage1_kernel(const float* __restrict__ a, int64_t n,
   if (j >= c) return;
   const int64_t r0 = chunk * rows_per_chunk;
   const int64_t r1 = (r0 + rows_per_chunk < n) ? (r0 + rows_per_chunk) : n;
-  float s = 0.0f;
-  for (int64_t r = r0; r < r1; ++r) s += a[r * c + j];
-  partial[chunk * c + j] = s;
+  partial[chunk * c + j] = ordered_sum<1>(a + r0 * c + j, c, 0, static_cast<int>(r1 - r0));
 }
 
-__global__ void colsum_stage2_kernel(const float* __restrict__ partial,
-                                     int64_t chunks, int64_t c,
-                                     float* __restrict__ out) {
-  const int64_t j = static_cast<int64_t>(blockIdx.x) * kColThreads + threadIdx.x;
-  if (j >= c) return;
+// out_m[j] = sum over r in [0, rows) of a_m[r * ld + j] for j < cols, for the
+// matrix m = blockIdx.y (at most two: a0/out0 and a1/out1).  A block covers
+// 32 columns; warp w sums its contiguous share of rows in row order, then the
+// warp sums are added in warp order -- a fixed order, so runs are bitwise
+// repeatable.
+__global__ void __launch_bounds__(kSumWarps * 32)
+colsum_rows_kernel(const float* __restrict__ a0, float* __restrict__ out0,
+                   const float* __restrict__ a1, float* __restrict__ out1, int rows, int64_t cols,
+                   int64_t ld) {
+  __shared__ float part[kSumWarps][32];
+  const float* a = blockIdx.y == 0 ? a0 : a1;
+  float* out = blockIdx.y == 0 ? out0 : out1;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t j = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  const int rpw = (rows + kSumWarps - 1) / kSumWarps;
+  const int r0 = w * rpw;
+  const int r1 = r0 + rpw < rows ? r0 + rpw : rows;
   float s = 0.0f;
-  for (int64_t k = 0; k < chunks; ++k) s += partial[k * c + j];
-  out[j] = s;
+  if (j < cols && r0 < r1) s = ordered_sum<1>(a + j, ld, r0, r1);
+  part[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && j < cols) {
+    float t = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kSumWarps; ++k) t += part[k][lane];
+    out[j] = t;
+  }
 }
 
 }  // namespace
@@ -56,9 +74,19 @@ int colsum_f32(const float* a, int64_t n, int64_t c, float* partial, float* out,
   colsum_stage1_kernel<<<dim3(static_cast<unsigned>(chunks), static_cast<unsigned>(cblocks)),
                          kColThreads, 0, s>>>(a, n, c, 128, partial);
   CIGN_CHECK_LAUNCH("colsum_stage1_kernel");
-  colsum_stage2_kernel<<<static_cast<unsigned>(cblocks), kColThreads, 0, s>>>(partial, chunks,
-                                                                              c, out);
-  CIGN_CHECK_LAUNCH("colsum_stage2_kernel");
+  return colsum_rows(partial, out, nullptr, nullptr, chunks, c, c, s);
+}
+
+int colsum_rows(const float* a0, float* out0, const float* a1, float* out1, int64_t rows,
+                int64_t cols, int64_t ld, cudaStream_t s) {
+  if (cols == 0) return CIGN_OK;
+  CIGN_REQUIRE(rows > 0 && rows < (1ll << 31), CIGN_ERR_UNSUPPORTED, "colsum: bad row count");
+  const int64_t blocks = (cols + 31) / 32;
+  CIGN_REQUIRE(blocks < (1ll << 31), CIGN_ERR_UNSUPPORTED, "colsum: too many columns");
+  const dim3 grid(static_cast<unsigned>(blocks), a1 != nullptr ? 2u : 1u);
+  colsum_rows_kernel<<<grid, kSumWarps * 32, 0, s>>>(a0, out0, a1, out1, static_cast<int>(rows),
+                                                      cols, ld);
+  CIGN_CHECK_LAUNCH("colsum_rows_kernel");
   return CIGN_OK;
 }
 

@@ -92,21 +92,6 @@ attn_logits_bwd_kernel(int64_t n, int H, int64_t C, int64_t rows_per_chunk,
   st_vec(partial + (chunk * 2 + 1) * HC + col, pd);
 }
 
-__global__ void attn_param_stage2_kernel(const float* __restrict__ partial,
-                                         int64_t chunks, int64_t HC,
-                                         float* __restrict__ g_src,
-                                         float* __restrict__ g_dst) {
-  const int64_t j = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  if (j >= HC) return;
-  float s = 0.0f, d = 0.0f;
-  for (int64_t k = 0; k < chunks; ++k) {
-    s += partial[(k * 2 + 0) * HC + j];
-    d += partial[(k * 2 + 1) * HC + j];
-  }
-  g_src[j] = s;
-  g_dst[j] = d;
-}
-
 __global__ void head_silu_fwd_kernel(int64_t n, int H, int64_t C,
                                      const float* __restrict__ out,
                                      const float* __restrict__ bias,
@@ -229,10 +214,8 @@ int cign_attn_logits_bwd(int64_t n, int32_t heads, int32_t channels, const float
                                                         grad_dst, x, att_src, att_dst, grad_x,
                                                         accumulate, partial);
   CIGN_CHECK_LAUNCH("attn_logits_bwd_kernel");
-  attn_param_stage2_kernel<<<static_cast<unsigned>((HC + kThreads - 1) / kThreads), kThreads, 0,
-                             s>>>(partial, chunks, HC, grad_att_src, grad_att_dst);
-  CIGN_CHECK_LAUNCH("attn_param_stage2_kernel");
-  return CIGN_OK;
+  // partial rows alternate src, dst per chunk: two [chunks, HC] matrices with ld 2*HC
+  return colsum_rows(partial, grad_att_src, partial + HC, grad_att_dst, chunks, HC, 2 * HC, s);
 }
 
 int cign_head_mean_bias_silu_fwd(int64_t n, int32_t heads, int32_t channels,

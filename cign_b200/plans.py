@@ -21,6 +21,27 @@ def _as_i32(t: torch.Tensor) -> torch.Tensor:
     return t.to(dtype=torch.int32).contiguous()
 
 
+class HopTimer:
+    """Opt-in device timing of the k-hop calls: CUDA events recorded on the
+    launching stream around every cign_multihop_fwd / _bwd call while the
+    timer is installed (``SpmmPlan.hop_timer = HopTimer()``).  ``records`` holds
+    (kind, n_hops, n_addend_hops, F, start, end); read them after a
+    synchronize."""
+
+    def __init__(self):
+        self.records = []
+
+    def begin(self, stream):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        return ev
+
+    def end(self, stream, start, kind, n_hops, n_addend, F):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        self.records.append((kind, n_hops, n_addend, F, start, ev))
+
+
 class SpmmPlan:
     """Native SpMM plan over a square fixed operator P (and optionally P^T).
 
@@ -29,6 +50,8 @@ class SpmmPlan:
     transposed products reuse P (symmetric operator, the default for CIGN's
     undirected normalised adjacency).
     """
+
+    hop_timer: Optional[HopTimer] = None
 
     def __init__(self, crow, col, val, crow_t=None, col_t=None, val_t=None):
         _lib.require_cuda("SpmmPlan")
@@ -112,9 +135,14 @@ class SpmmPlan:
         arr = _lib.ptr_array(ys)
         F = int(x.size(1))
         ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, F), self.device)
+        timer = SpmmPlan.hop_timer
         with _lib.DeviceGuard(self.device):
+            stream = _lib.stream_of(x)
+            t0 = timer.begin(torch.cuda.current_stream(self.device)) if timer else None
             rc = self.lib.cign_multihop_fwd(self.handle, int(max_power), _lib.ptr(x), F, arr,
-                                            _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+                                            _lib.ptr(ws), ws.numel(), stream)
+            if timer:
+                timer.end(torch.cuda.current_stream(self.device), t0, "fwd", int(max_power), 0, F)
         _lib.check(rc, "cign_multihop_fwd")
         return ys
 
@@ -128,9 +156,16 @@ class SpmmPlan:
         ws = _lib.workspace(self.lib.cign_multihop_workspace_bytes(self.handle, len(gs), int(F)),
                             self.device)
         arr = _lib.ptr_array(gs)
+        timer = SpmmPlan.hop_timer
         with _lib.DeviceGuard(self.device):
+            stream = _lib.stream_of(gx)
+            t0 = timer.begin(torch.cuda.current_stream(self.device)) if timer else None
             rc = self.lib.cign_multihop_bwd(self.handle, len(gs), arr, int(F), _lib.ptr(gx),
-                                            _lib.ptr(ws), ws.numel(), _lib.stream_of(gx))
+                                            _lib.ptr(ws), ws.numel(), stream)
+            if timer:
+                # hop p (p = max..1) adds g_{p-1} when present: addend hops = grads[0..max-2]
+                n_add = sum(1 for g in gs[:-1] if g is not None)
+                timer.end(torch.cuda.current_stream(self.device), t0, "bwd", len(gs), n_add, int(F))
         _lib.check(rc, "cign_multihop_bwd")
         return gx
 
