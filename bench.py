@@ -245,7 +245,7 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device):
 
 
 def hop_roofline(timer, N, nnz, peak, peak_kind):
-    """Roofline of the dominant kernel, the k-hop SpMM (spmm_tma_kernel plus its
+    """Roofline of the dominant kernel, the k-hop SpMM (spmm_rows_kernel plus its
     hub-row combine; the largest share of the step's device time), from the
     CUDA events recorded around every k-hop call inside the timed steps."""
     t_ms = 0.0
@@ -272,7 +272,7 @@ def hop_roofline(timer, N, nnz, peak, peak_kind):
     if all(k in tr for k in ("fwd", "bwd_add", "bwd")):
         traffic = int((mix["fwd"] * tr["fwd"] + mix["bwd_add"] * tr["bwd_add"]
                        + mix["bwd"] * tr["bwd"]) / launches)
-    return {"bound": "hbm", "kernel": "spmm_hop (spmm_tma_kernel + hub combine), F=%d" % F,
+    return {"bound": "hbm", "kernel": "spmm_hop (spmm_rows_kernel + hub combine), F=%d" % F,
             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic,
             "algorithmic_bytes": int(alg / launches), "ms_per_launch": round(per_launch_s * 1e3, 4),

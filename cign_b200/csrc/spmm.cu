@@ -7,7 +7,13 @@
 //     of VEC floats per lane).  Column ids / values of the row are read
 //     lane-parallel (coalesced) and broadcast with shuffles; each edge then
 //     costs LPR*VPL vector loads of the neighbour's feature row, issued two
-//     to four edges at a time for memory-level parallelism.
+//     to four edges at a time for memory-level parallelism.  Rows wider than
+//     one tile are split over the grid's second dimension (one feature tile
+//     per block row), so the register footprint per lane, and with it the
+//     number of resident warps, stays that of a 256/512-float row.
+//     Measured on the cfg2 power-law graph this beat shared-memory staging
+//     (cp.async rings, and TMA bulk copies per neighbour row, whose per-copy
+//     cost put a ~95 us floor under every width) at every F.
 //   * Power-law graphs have hub rows (thousands of non-zeros).  Rows with
 //     more than kSegLen non-zeros are cut at plan time into segments of
 //     kSegLen edges; every segment is one group's work item (scheduled
@@ -124,7 +130,8 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
     if (sidx >= n_seg) return;
     const int e0 = seg_begin[sidx], e1 = seg_end[sidx];
     float* pr = partial + sidx * F;
-    for (int64_t f0 = 0; f0 < F; f0 += Cfg::kTile) {
+    for (int64_t f0 = static_cast<int64_t>(blockIdx.y) * Cfg::kTile; f0 < F;
+         f0 += static_cast<int64_t>(gridDim.y) * Cfg::kTile) {
       V acc[VPL];
 #pragma unroll
       for (int q = 0; q < VPL; ++q) vzero(acc[q]);
@@ -145,7 +152,8 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
   const int e0 = crow[row];
   const int e1 = crow[row + 1];
   if (e1 - e0 > kSegLen) return;  // a hub row: done by segments + combine
-  for (int64_t f0 = 0; f0 < F; f0 += Cfg::kTile) {
+  for (int64_t f0 = static_cast<int64_t>(blockIdx.y) * Cfg::kTile; f0 < F;
+       f0 += static_cast<int64_t>(gridDim.y) * Cfg::kTile) {
     V acc[VPL];
 #pragma unroll
     for (int q = 0; q < VPL; ++q) vzero(acc[q]);
@@ -197,228 +205,6 @@ int launch_spmm_combine(const SegList& sl, const float* partial, int64_t F, cons
   return CIGN_OK;
 }
 
-// Persistent ring kernel for F % 4 == 0 (16-byte aligned operands).
-// Work items are (feature tile, segment-or-row) pairs in tile-major order, so
-// at any time all warps gather from the same 256-column slice of X, which
-// stays resident in L2.  Every warp takes items from an atomic counter
-// (hub-row segments first within a tile, then whole rows), so no warp idles
-// while work remains.  For each item it walks the edges in chunks of 32
-// (col/val lane-parallel) and streams each neighbour's tile (32*VPL float4)
-// into a warp-private ring of STAGES shared-memory slots with cp.async:
-// STAGES edges are in flight per warp without holding registers.  Each lane
-// copies and later reads back only its own float4 slots, so a lane's
-// wait_group is all the synchronisation the data needs; __syncwarp() orders
-// a slot's reads before it is refilled.  Sum order per output element is the
-// edge order: results are deterministic and identical to the register
-// kernel's.
-template <int VPL, int STAGES>
-__global__ void __launch_bounds__(kThreads)
-spmm_ring_kernel(int rows, const int* __restrict__ crow, const int* __restrict__ col,
-                 const float* __restrict__ val, const int* __restrict__ seg_begin,
-                 const int* __restrict__ seg_end, int n_seg, const float* __restrict__ X,
-                 int64_t F, const float* __restrict__ addend, float* __restrict__ Y,
-                 float* __restrict__ partial, int* __restrict__ counter) {
-  extern __shared__ float4 ring_all[];
-  constexpr int kSlot = 32 * VPL;  // float4 per slot
-  constexpr int kTileF = 4 * kSlot;
-  const int lane = threadIdx.x & 31;
-  float4* ring = ring_all + (threadIdx.x >> 5) * STAGES * kSlot;
-  const int per_tile = n_seg + rows;
-  const int64_t n_tiles = (F + kTileF - 1) / kTileF;
-  const int64_t total = n_tiles * per_tile;
-  for (;;) {
-    int item32 = 0;
-    if (lane == 0) item32 = atomicAdd(counter, 1);
-    const int64_t item = __shfl_sync(kFullMask, item32, 0);
-    if (item >= total) break;
-    const int64_t f0 = (item / per_tile) * kTileF;
-    const int it = static_cast<int>(item % per_tile);
-    int e0, e1;
-    float* out;
-    const float* add = nullptr;
-    if (it < n_seg) {
-      e0 = seg_begin[it];
-      e1 = seg_end[it];
-      out = partial + static_cast<int64_t>(it) * F;
-    } else {
-      const int64_t row = it - n_seg;
-      e0 = crow[row];
-      e1 = crow[row + 1];
-      if (e1 - e0 > kSegLen) continue;  // hub row: done by its segments
-      out = Y + row * F;
-      if (addend != nullptr) add = addend + row * F;
-    }
-    float4 acc[VPL];
-#pragma unroll
-    for (int q = 0; q < VPL; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float* xt = X + f0 + static_cast<int64_t>(lane) * 4;
-    for (int base = e0; base < e1; base += 32) {
-      const int my = base + lane;
-      int c = 0;
-      float v = 0.0f;
-      if (my < e1) {
-        c = __ldg(col + my);
-        v = __ldg(val + my);
-      }
-      const int cnt = min(32, e1 - base);
-      auto issue = [&](int k) {
-        if (k < cnt) {
-          const int ck = __shfl_sync(kFullMask, c, k);
-          const float* src = xt + static_cast<int64_t>(ck) * F;
-          float4* dst = ring + (k % STAGES) * kSlot + lane;
-#pragma unroll
-          for (int q = 0; q < VPL; ++q)
-            if (f0 + (lane + q * 32) * 4 < F) cp_async16(dst + q * 32, src + q * 128);
-        }
-        cp_async_commit();
-      };
-#pragma unroll
-      for (int k = 0; k < STAGES; ++k) issue(k);
-      for (int k = 0; k < cnt; ++k) {
-        cp_async_wait<STAGES - 1>();
-        const float vk = __shfl_sync(kFullMask, v, k);
-        const float4* slot = ring + (k % STAGES) * kSlot + lane;
-#pragma unroll
-        for (int q = 0; q < VPL; ++q)
-          if (f0 + (lane + q * 32) * 4 < F) vfma(acc[q], vk, slot[q * 32]);
-        __syncwarp();
-        issue(k + STAGES);
-      }
-      cp_async_wait<0>();
-      __syncwarp();
-    }
-#pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int64_t fi = f0 + (lane + q * 32) * 4;
-      if (fi < F) {
-        if (add != nullptr) vadd(acc[q], ld_vec<4>(add + fi));
-        st_vec(out + fi, acc[q]);
-      }
-    }
-  }
-}
-
-// TMA-ring kernel (F % 4 == 0, 16-byte aligned operands): like the ring
-// kernel above, but each neighbour's feature tile (up to 1024 floats) is one
-// cp.async.bulk copy issued by lane 0 and completed on the slot's mbarrier,
-// so the per-edge instruction cost no longer scales with the tile size.
-// ctl[0] is the work counter, ctl[1] a status word set to kStatusTimeout if a
-// bounded mbarrier wait ever expires (the warp then drains and stops).
-constexpr int kTmaWarps = 4;
-
-template <int VPL>
-__global__ void __launch_bounds__(kTmaWarps * 32)
-spmm_tma_kernel(int rows, const int* __restrict__ crow, const int* __restrict__ col,
-                const float* __restrict__ val, const int* __restrict__ seg_begin,
-                const int* __restrict__ seg_end, int n_seg, const float* __restrict__ X,
-                int64_t F, const float* __restrict__ addend, float* __restrict__ Y,
-                float* __restrict__ partial, int stages, int* __restrict__ ctl) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  constexpr int kSlotF = 128 * VPL;  // floats per slot
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* slots = reinterpret_cast<float*>(smem_raw) + static_cast<size_t>(warp) * stages * kSlotF;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + static_cast<size_t>(kTmaWarps) * stages * kSlotF * 4) +
-                   warp * stages;
-  if (lane == 0) {
-    for (int s = 0; s < stages; ++s) mbar_init(smem_u32(&bars[s]), 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-  uint32_t phase = 0;
-  const int per_tile = n_seg + rows;
-  const int64_t n_tiles = (F + kSlotF - 1) / kSlotF;
-  const int64_t total = n_tiles * per_tile;
-  bool ok = true;
-  int pend_lo = 0, pend_hi = 0;  // fills issued but not consumed (on failure)
-  while (ok) {
-    int item32 = 0;
-    if (lane == 0) item32 = atomicAdd(ctl, 1);
-    const int64_t item = __shfl_sync(kFullMask, item32, 0);
-    if (item >= total) break;
-    const int64_t f0 = (item / per_tile) * kSlotF;
-    const int it = static_cast<int>(item % per_tile);
-    int e0, e1;
-    float* out;
-    const float* add = nullptr;
-    if (it < n_seg) {
-      e0 = seg_begin[it];
-      e1 = seg_end[it];
-      out = partial + static_cast<int64_t>(it) * F;
-    } else {
-      const int64_t row = it - n_seg;
-      e0 = crow[row];
-      e1 = crow[row + 1];
-      if (e1 - e0 > kSegLen) continue;  // hub row: done by its segments
-      out = Y + row * F;
-      if (addend != nullptr) add = addend + row * F;
-    }
-    const int64_t tile_f = (F - f0 < kSlotF) ? (F - f0) : kSlotF;
-    const uint32_t bytes = static_cast<uint32_t>(tile_f * 4);
-    float4 acc[VPL];
-#pragma unroll
-    for (int q = 0; q < VPL; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int base = e0; base < e1 && ok; base += 32) {
-      const int my = base + lane;
-      int c = 0;
-      float v = 0.0f;
-      if (my < e1) {
-        c = __ldg(col + my);
-        v = __ldg(val + my);
-      }
-      const int cnt = min(32, e1 - base);
-      auto issue = [&](int k) {
-        if (k < cnt) {
-          const int ck = __shfl_sync(kFullMask, c, k);
-          if (lane == 0) {
-            const int sl = k % stages;
-            const uint32_t bar = smem_u32(&bars[sl]);
-            mbar_expect_tx(bar, bytes);
-            bulk_g2s(smem_u32(slots + static_cast<size_t>(sl) * kSlotF), X + static_cast<int64_t>(ck) * F + f0,
-                     bytes, bar);
-          }
-        }
-      };
-      for (int k = 0; k < stages; ++k) issue(k);
-      for (int k = 0; k < cnt; ++k) {
-        const int sl = k % stages;
-        const bool got = mbar_wait(smem_u32(&bars[sl]), (phase >> sl) & 1u);
-        if (!__all_sync(kFullMask, got)) {
-          ok = false;
-          pend_lo = k;
-          pend_hi = min(k + stages, cnt);
-          break;
-        }
-        phase ^= 1u << sl;
-        const float vk = __shfl_sync(kFullMask, v, k);
-        const float4* slot = reinterpret_cast<const float4*>(slots + static_cast<size_t>(sl) * kSlotF);
-#pragma unroll
-        for (int q = 0; q < VPL; ++q)
-          if ((lane + q * 32) * 4 < tile_f) vfma(acc[q], vk, slot[lane + q * 32]);
-        __syncwarp();
-        if (lane == 0) fence_proxy_async();
-        issue(k + stages);
-      }
-    }
-    if (!ok) break;
-#pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int64_t fi = f0 + (lane + q * 32) * 4;
-      if (fi < F) {
-        if (add != nullptr) vadd(acc[q], ld_vec<4>(add + fi));
-        st_vec(out + fi, acc[q]);
-      }
-    }
-  }
-  if (!ok) {
-    if (lane == 0) atomicExch(ctl + 1, kStatusTimeout);
-    for (int k = pend_lo; k < pend_hi; ++k) {  // let in-flight copies land
-      const int sl = k % stages;
-      mbar_wait(smem_u32(&bars[sl]), (phase >> sl) & 1u);
-      phase ^= 1u << sl;
-    }
-  }
-}
-
 // Plan-time validation of a CSR: crow monotone with crow[0]=0, crow[rows]=nnz,
 // all columns in range.  Sets *bad to 1 on the first violation.
 __global__ void csr_validate_kernel(int64_t rows, int64_t cols, int64_t nnz,
@@ -450,7 +236,10 @@ int launch_spmm_cfg(const cign_csr_f32& m, const SegList& sl, const float* X, in
   const int64_t grid = seg_blocks + light_blocks;
   if (grid == 0) return CIGN_OK;
   CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "spmm: grid too large");
-  spmm_rows_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+  // one feature tile per block row of the grid (blocks stride over the rest)
+  const int64_t tiles = std::min<int64_t>((F + Cfg::kTile - 1) / Cfg::kTile, 65535);
+  spmm_rows_kernel<VEC, VPL, LPR><<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(tiles)),
+                                    kThreads, 0, stream>>>(
       static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
       static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, addend, Y, partial);
   CIGN_CHECK_LAUNCH("spmm_rows_kernel");
@@ -466,74 +255,14 @@ int launch_spmm_vec(const cign_csr_f32& m, const SegList& sl, const float* X, in
   if (fv <= 32) return launch_spmm_cfg<VEC, 1, 32>(m, sl, X, F, addend, Y, partial, stream);
   if (fv <= 64) return launch_spmm_cfg<VEC, 2, 32>(m, sl, X, F, addend, Y, partial, stream);
   if (fv <= 128) return launch_spmm_cfg<VEC, 4, 32>(m, sl, X, F, addend, Y, partial, stream);
+  // wider float4 rows: 256-float tiles over the grid's second dimension keep
+  // the register footprint (and so the warps in flight) of the narrow case
+  if (VEC == 4) return launch_spmm_cfg<VEC, 2, 32>(m, sl, X, F, addend, Y, partial, stream);
   return launch_spmm_cfg<VEC, 8, 32>(m, sl, X, F, addend, Y, partial, stream);
 }
 
-constexpr int kRingVPL = 2;     // 256-float feature tile per pass
-constexpr int kRingStages = 8;  // edges in flight per warp
-
-int launch_spmm_ring(const cign_csr_f32& m, const SegList& sl, const float* X, int64_t F,
-                     const float* addend, float* Y, float* partial, int* counter,
-                     cudaStream_t stream) {
-  auto kernel = spmm_ring_kernel<kRingVPL, kRingStages>;
-  const size_t smem = static_cast<size_t>(kThreads / 32) * kRingStages * 32 * kRingVPL * 16;
-  static thread_local int grid_cache[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int& grid = grid_cache[dev & 63];
-  if (grid == 0) {
-    CIGN_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)),
-                    "spmm: set smem");
-    grid = persistent_grid(kernel, kThreads, smem);
-  }
-  CIGN_CHECK_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), stream), "spmm: reset counter");
-  kernel<<<grid, kThreads, smem, stream>>>(static_cast<int>(m.rows), m.crow, m.col, m.val,
-                                           sl.seg_begin(), sl.seg_end(),
-                                           static_cast<int>(sl.n_seg), X, F, addend, Y, partial,
-                                           counter);
-  CIGN_CHECK_LAUNCH("spmm_ring_kernel");
-  return launch_spmm_combine<4>(sl, partial, F, addend, Y, stream);
-}
-
-template <int VPL>
-int launch_spmm_tma_vpl(const cign_csr_f32& m, const SegList& sl, const float* X, int64_t F,
-                        const float* addend, float* Y, float* partial, int* ctl,
-                        cudaStream_t stream) {
-  // ~16 KB of slots per warp, 3..8 stages
-  const int slot_bytes = 128 * VPL * 4;
-  const int stages = std::max(3, std::min(8, 16384 / slot_bytes));
-  const size_t smem = static_cast<size_t>(kTmaWarps) * stages * (slot_bytes + 8);
-  auto kernel = spmm_tma_kernel<VPL>;
-  static thread_local int grid_cache[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int& grid = grid_cache[dev & 63];
-  if (grid == 0) {
-    CIGN_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)),
-                    "spmm: set smem");
-    grid = persistent_grid(kernel, kTmaWarps * 32, smem);
-  }
-  CIGN_CHECK_CUDA(cudaMemsetAsync(ctl, 0, 2 * sizeof(int), stream), "spmm: reset control");
-  kernel<<<grid, kTmaWarps * 32, smem, stream>>>(static_cast<int>(m.rows), m.crow, m.col, m.val,
-                                                 sl.seg_begin(), sl.seg_end(),
-                                                 static_cast<int>(sl.n_seg), X, F, addend, Y,
-                                                 partial, stages, ctl);
-  CIGN_CHECK_LAUNCH("spmm_tma_kernel");
-  return launch_spmm_combine<4>(sl, partial, F, addend, Y, stream);
-}
-
-int launch_spmm_tma(const cign_csr_f32& m, const SegList& sl, const float* X, int64_t F,
-                    const float* addend, float* Y, float* partial, int* ctl,
-                    cudaStream_t stream) {
-  if (F <= 256) return launch_spmm_tma_vpl<2>(m, sl, X, F, addend, Y, partial, ctl, stream);
-  if (F <= 512) return launch_spmm_tma_vpl<4>(m, sl, X, F, addend, Y, partial, ctl, stream);
-  return launch_spmm_tma_vpl<8>(m, sl, X, F, addend, Y, partial, ctl, stream);
-}
-
-// Workspace of one SpMM: hub-row partials [n_seg, F] + the persistent
-// kernels' work counter and status word.
+// Workspace of one SpMM: hub-row partials [n_seg, F] (+ 256 bytes of
+// alignment slack).
 size_t partial_bytes(const cign_spmm_plan* plan, int64_t F) {
   const int64_t n = std::max(plan->seg_p.n_seg, plan->pt_is_p ? 0 : plan->seg_pt.n_seg);
   return (static_cast<size_t>(n) * F * sizeof(float) + 255) / 256 * 256 + 256;
@@ -546,12 +275,6 @@ int run_spmm(const cign_spmm_plan* plan, int transpose, const float* X, int64_t 
   const SegList& sl = use_t ? plan->seg_pt : plan->seg_p;
   const bool vec4 = (F % 4 == 0) && aligned16(X) && aligned16(Y) && aligned16(partial) &&
                     (addend == nullptr || aligned16(addend));
-  if (vec4 && F >= 128) {
-    const int64_t n = std::max(plan->seg_p.n_seg, plan->pt_is_p ? 0 : plan->seg_pt.n_seg);
-    int* counter = reinterpret_cast<int*>(
-        reinterpret_cast<char*>(partial) + (static_cast<size_t>(n) * F * sizeof(float) + 255) / 256 * 256);
-    return launch_spmm_tma(m, sl, X, F, addend, Y, partial, counter, stream);
-  }
   if (vec4) return launch_spmm_vec<4>(m, sl, X, F, addend, Y, partial, stream);
   return launch_spmm_vec<1>(m, sl, X, F, addend, Y, partial, stream);
 }
