@@ -174,3 +174,117 @@ def collapsed_gat_mean_bias_silu(
     seed = gat_call_seed(attn_drop)
     return _CollapsedGATFn.apply(attn_row, attn_col, rowptr, col, colptr, row, perm,
                                  float(negative_slope), in_feat, bias, float(attn_drop), int(seed))
+
+
+# ---------------------------------------------------------------- aggregate-first
+def gat_agg_forward_raw(plan, attn_row, attn_col, x, heads, negative_slope, attn_drop, seed):
+    """z [N,H,D] = per-head attention-weighted sums of x rows; returns (z, emax, esum)."""
+    lib = ensure_collapsed_gat_loaded()
+    n, D = (int(s) for s in x.shape)
+    H = int(heads)
+    z = torch.empty((n, H, D), dtype=torch.float32, device=x.device)
+    emax = torch.empty((n, H), dtype=torch.float32, device=x.device)
+    esum = torch.empty_like(emax)
+    ws = _lib.workspace(lib.cign_gat_agg_workspace_bytes(plan.handle, H, D, D), x.device)
+    with _lib.DeviceGuard(x.device):
+        rc = lib.cign_gat_agg_fwd(plan.handle, H, D, _lib.ptr(attn_row), _lib.ptr(attn_col),
+                                  _lib.ptr(x), float(negative_slope), float(attn_drop),
+                                  int(seed) & ((1 << 64) - 1), _lib.ptr(z), _lib.ptr(emax),
+                                  _lib.ptr(esum), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+    _lib.check(rc, "cign_gat_agg_fwd")
+    return z, emax, esum
+
+
+def gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z, grad_pre, negative_slope,
+                         attn_drop, seed):
+    """Returns (grad_feat [N,H,C], grad_attn_row [N,H], grad_attn_col [N,H])."""
+    lib = ensure_collapsed_gat_loaded()
+    n, D = (int(s) for s in x.shape)
+    H = int(emax.size(1))
+    C = int(grad_pre.size(1))
+    dev = x.device
+    gfeat = torch.empty((n, H, C), dtype=torch.float32, device=dev)
+    grow = torch.empty((n, H), dtype=torch.float32, device=dev)
+    gcol = torch.empty_like(grow)
+    ws = _lib.workspace(lib.cign_gat_agg_workspace_bytes(plan.handle, H, D, C), dev)
+    with _lib.DeviceGuard(dev):
+        rc = lib.cign_gat_agg_bwd(plan.handle, H, D, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
+                                  _lib.ptr(x), _lib.ptr(emax), _lib.ptr(esum), _lib.ptr(grad_z),
+                                  _lib.ptr(grad_pre), float(negative_slope), float(attn_drop),
+                                  int(seed) & ((1 << 64) - 1), _lib.ptr(gfeat), _lib.ptr(grow),
+                                  _lib.ptr(gcol), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+    _lib.check(rc, "cign_gat_agg_bwd")
+    return gfeat, grow, gcol
+
+
+def _head_projection(weight: torch.Tensor, heads: int) -> torch.Tensor:
+    """M [H*D, C] with M[(h,d), c] = W[h*C + c, d] / H, so that
+    z.view(N, H*D) @ M = (1/H) sum_h W_h z[:, h, :]."""
+    HC, D = weight.shape
+    C = HC // heads
+    return weight.view(heads, C, D).permute(0, 2, 1).reshape(heads * D, C) / heads
+
+
+class _AggregateFirstGATFn(torch.autograd.Function):
+    """SiLU(mean_h sum_j w_ijh (lin.weight_h x_j) + bias) computed as
+    SiLU(z.view(N, H*D) @ M + bias) with z = cign_gat_agg_fwd(x)."""
+
+    @staticmethod
+    def forward(ctx, x, attn_row, attn_col, weight, bias, plan, heads, negative_slope, attn_drop,
+                seed):
+        H = int(heads)
+        n, D = x.shape
+        z, emax, esum = gat_agg_forward_raw(plan, attn_row, attn_col, x, H, negative_slope,
+                                            attn_drop, seed)
+        M = _head_projection(weight, H)
+        pre = torch.addmm(bias, z.view(n, H * D), M)
+        ctx.save_for_backward(x, attn_row, attn_col, weight, z, pre, emax, esum)
+        ctx.plan, ctx.heads = plan, H
+        ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), int(seed)
+        return torch.nn.functional.silu(pre)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, attn_row, attn_col, weight, z, pre, emax, esum = ctx.saved_tensors
+        H = ctx.heads
+        n, D = x.shape
+        C = weight.size(0) // H
+        g_pre = torch.ops.aten.silu_backward(grad_out.contiguous(), pre)
+        grad_bias = g_pre.sum(0)
+        M = _head_projection(weight, H)
+        z2 = z.view(n, H * D)
+        grad_M = z2.t().mm(g_pre)                                   # [H*D, C]
+        grad_w = grad_M.view(H, D, C).permute(0, 2, 1).reshape(H * C, D) / H
+        grad_z = g_pre.mm(M.t())                                    # [N, H*D]
+        gfeat, grow, gcol = gat_agg_backward_raw(ctx.plan, attn_row, attn_col, x, emax, esum,
+                                                 grad_z, g_pre, ctx.negative_slope,
+                                                 ctx.attn_drop, ctx.seed)
+        grad_x = gfeat.view(n, H * C).mm(weight)                    # [N, D]
+        return grad_x, grow, gcol, grad_w, grad_bias, None, None, None, None, None
+
+
+def collapsed_gat_aggregate_first(x: torch.Tensor, attn_row: torch.Tensor, attn_col: torch.Tensor,
+                                  weight: torch.Tensor, bias: torch.Tensor, csr, csc,
+                                  perm: torch.Tensor, negative_slope: float,
+                                  attn_drop: float) -> torch.Tensor:
+    """collapsed_gat_mean_bias_silu(attn_row, attn_col, ..., in_feat=lin(x).view(N,H,C), bias)
+    evaluated aggregate-first: x [N,D] (16-byte aligned, D % 4 == 0), lin.weight
+    [H*C, D] (C % 4 == 0), attn_row = alpha_dst and attn_col = alpha_src [N,H].
+    Same dropout stream (call counter and keep bits) as the collapsed form."""
+    if x.dtype != torch.float32 or x.device.type != "cuda" or x.dim() != 2:
+        raise TypeError("aggregate-first GAT requires CUDA float32 x [N,D]")
+    H = int(attn_row.size(1))
+    if not (1 <= H <= MAX_HEADS):
+        raise ValueError(f"collapsed GAT requires 1<=H<={MAX_HEADS}; got H={H}")
+    if weight.dim() != 2 or weight.size(0) % H != 0 or weight.size(1) != x.size(1):
+        raise ValueError("weight must be [H*C, D]")
+    if not (0.0 <= float(attn_drop) < 1.0):
+        raise ValueError("attn_drop must be in [0,1)")
+    (rowptr, col), (row, colptr) = csr, csc
+    plan = gat_plan_for(rowptr, col, row, colptr, perm)
+    if plan.n != x.size(0):
+        raise RuntimeError(f"graph has {plan.n} rows but x has {x.size(0)}")
+    seed = gat_call_seed(attn_drop)
+    return _AggregateFirstGATFn.apply(x.contiguous(), attn_row.contiguous(), attn_col.contiguous(),
+                                      weight, bias, plan, H, float(negative_slope),
+                                      float(attn_drop), int(seed))

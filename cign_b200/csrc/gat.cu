@@ -532,7 +532,7 @@ gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
   __shared__ float scratch[32];
   const int64_t row = hub_row[blockIdx.x];
   const int h = blockIdx.y;
-  if (h == 0) {
+  if (h == 0 && grad_y != nullptr) {
     for (int64_t c = threadIdx.x; c < C; c += kThreads)
       gpre[row * C + c] = grad_y[row * C + c] * silu_grad_f(pre[row * C + c]);
   }
@@ -736,7 +736,7 @@ gat_bwd_cols_combine_kernel(int H, int64_t C, const int* __restrict__ hub_col,
   const int64_t HC = static_cast<int64_t>(H) * C;
   const int64_t k = (static_cast<int64_t>(blockIdx.y) * kCombineThreads + threadIdx.x) * VEC;
   if (k < HC) st_vec(grad_feat + j * HC + k, ordered_sum<VEC>(pfeat + k, HC, s0, s1));
-  if (blockIdx.y == 0) {
+  if (blockIdx.y == 0 && pcol != nullptr) {
     for (int h = threadIdx.x; h < H; h += kCombineThreads)
       grad_attn_col[j * H + h] = ordered_sum<1>(pcol + h, H, s0, s1);
   }
@@ -1242,9 +1242,18 @@ int launch_bwd_hub_rows(const cign_gat_plan* pl, int H, int64_t C, const float* 
   return CIGN_OK;
 }
 
+int launch_seg_combine(const SegList& sl, int H, int64_t C, const float* pfeat, const float* pcol,
+                       float* gfeat, float* gcol, cudaStream_t s);
+
 int launch_bwd_cols_combine(const cign_gat_plan* pl, int H, int64_t C, const float* pfeat,
                             const float* pcol, float* gfeat, float* gcol, cudaStream_t s) {
-  const SegList& sl = pl->cols;
+  return launch_seg_combine(pl->cols, H, C, pfeat, pcol, gfeat, gcol, s);
+}
+
+// out[target] = ordered sum of the target's segment partials ([n_seg, H*C]),
+// and, when pcol is not NULL, gcol[target] = the same over pcol ([n_seg, H]).
+int launch_seg_combine(const SegList& sl, int H, int64_t C, const float* pfeat, const float* pcol,
+                       float* gfeat, float* gcol, cudaStream_t s) {
   if (sl.n_heavy == 0) return CIGN_OK;
   const int64_t HC = static_cast<int64_t>(H) * C;
   const bool v4 = combine_v4(HC, {pfeat, gfeat});
@@ -1935,6 +1944,340 @@ BwdLayout bwd_layout(const cign_gat_plan* pl, int H, int64_t C) {
   return L;
 }
 
+// ------------------------------------------------------ aggregate-first form
+// GATConv's lin is linear, so per destination row i and head h
+//   sum_j w_ijh * (W_h X_j) = W_h (sum_j w_ijh X_j).
+// The aggregate-first kernels gather the layer input X [N, D] (one D-float
+// row per edge, shared by all heads) instead of lin's output [N, H, C], and
+// leave W to one dense GEMM afterwards:
+//   forward   Z[i,h,:] = sum_j w_ijh X[j,:]                  (gat_agg_kernel, CSR)
+//   backward  dots(e,h) = U[i,h,:] . X[j,:], U = dL/dZ        (gat_agg_dots_kernel, CSR)
+//             grad_feat[j,h,:] = sum_i w_ijh g_pre[i,:] / H   (gat_agg_kernel, CSC)
+// with the same weights w (logits, LeakyReLU, segment softmax, dropout
+// stream idx = e*H + h) as the collapsed kernels above.  Every work item --
+// a row (column) of at most kSegLen edges or one kSegLen-edge segment of a
+// hub -- is one warp whose lane k owns edge k, so per-edge quantities are
+// computed once per lane and broadcast with shuffles; feature tiles of
+// 128*VPL floats run over the grid's second dimension.
+
+constexpr int kAggHB = 4;  // heads per pass over a work item's edges
+
+template <int VPL>
+struct AggCfg {
+  static constexpr int kGroups = kThreads / 32;  // one warp per work item
+  static constexpr int kTile = 128 * VPL;        // floats per feature tile
+};
+
+// MODE 0 (forward, CSR rows of `ptr`/`idx`): out = Z [N, H, D] from X = src.
+//   Light rows compute their per-head max / exp-sum inline (written by the
+//   blockIdx.y == 0 tile); hub-row segments read them from emax/esum and
+//   write partials [n_seg, H, D].
+// MODE 1 (backward K2, CSC columns: ptr = colptr, idx = row, perm):
+//   out = grad_feat [N, H, D] from src = g_pre [N, D], scaled by 1/H; the
+//   y == 0 tile also sums glog over the column into gcol (hub segments:
+//   into pcol).
+template <int VPL, int MODE>
+__global__ void __launch_bounds__(kThreads)
+gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* __restrict__ idx,
+               const int* __restrict__ perm, const int* __restrict__ seg_row,
+               const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
+               int seg_blocks, const float* __restrict__ attn_row,
+               const float* __restrict__ attn_col, float* __restrict__ emax,
+               float* __restrict__ esum, const float* __restrict__ src, float slope, float p,
+               uint64_t seed, float* __restrict__ out, float* __restrict__ partial,
+               const float* __restrict__ glog, float* __restrict__ gcol,
+               float* __restrict__ pcol) {
+  using Cfg = AggCfg<VPL>;
+  const int lane = threadIdx.x & 31;
+  const int group = threadIdx.x >> 5;
+  const int64_t f0 = static_cast<int64_t>(blockIdx.y) * Cfg::kTile;
+  int64_t item, target;
+  int e0, e1;
+  bool seg;
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    item = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + group;
+    if (item >= n_seg) return;
+    target = seg_row[item];
+    e0 = seg_begin[item];
+    e1 = seg_end[item];
+    seg = true;
+  } else {
+    target = static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
+    if (target >= n) return;
+    e0 = ptr[target];
+    e1 = ptr[target + 1];
+    if (e1 - e0 > kSegLen) return;  // hub: done by its segments + combine
+    item = target;
+    seg = false;
+  }
+  const int k = e0 + lane;
+  const bool valid = k < e1;
+  const int cnt = e1 - e0;
+  int other = 0;     // MODE 0: source column j; MODE 1: destination row i
+  int64_t e = k;     // CSR edge id (dropout index)
+  if (valid) {
+    other = __ldg(idx + k);
+    if (MODE == 1) e = __ldg(perm + k);
+  }
+  const float scale = MODE == 1 ? 1.0f / static_cast<float>(H) : 1.0f;
+  const int64_t HD = static_cast<int64_t>(H) * D;
+  for (int h0 = 0; h0 < H; h0 += kAggHB) {
+    float w[kAggHB];
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh) {
+      const int h = h0 + hh;
+      w[hh] = 0.0f;
+      if (h >= H) continue;
+      if (MODE == 0) {
+        const float ad = __ldg(attn_row + target * H + h);
+        const float ac = valid ? __ldg(attn_col + static_cast<int64_t>(other) * H + h) : 0.0f;
+        float m, ssum;
+        if (seg) {
+          m = emax[target * H + h];
+          ssum = esum[target * H + h];
+        } else {
+          m = group_max<32>(valid ? fmaxf(kNegInit, leaky_f(ad + ac, slope)) : kNegInit, kFullMask);
+          ssum = group_sum<32>(valid ? expf(leaky_f(ad + ac, slope) - m) : 0.0f, kFullMask);
+          if (blockIdx.y == 0 && lane == 0) {
+            emax[target * H + h] = m;
+            esum[target * H + h] = ssum;
+          }
+        }
+        if (valid) w[hh] = edge_weight(ad, ac, m, ssum, slope, p, seed, static_cast<uint64_t>(e) * H + h);
+      } else {
+        if (valid) {
+          const int64_t ih = static_cast<int64_t>(other) * H + h;
+          w[hh] = edge_weight(__ldg(attn_row + ih), __ldg(attn_col + target * H + h), emax[ih],
+                              esum[ih], slope, p, seed, static_cast<uint64_t>(e) * H + h) * scale;
+        }
+        if (blockIdx.y == 0) {
+          const float gsum = group_sum<32>(valid ? glog[e * H + h] : 0.0f, kFullMask);
+          if (lane == 0) {
+            if (seg) pcol[item * H + h] = gsum;
+            else gcol[target * H + h] = gsum;
+          }
+        }
+      }
+    }
+    if (f0 >= D) continue;
+    float4 acc[kAggHB][VPL];
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh)
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) acc[hh][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int t = 0;
+    for (; t + 2 <= cnt; t += 2) {
+      const int c0 = __shfl_sync(kFullMask, other, t);
+      const int c1 = __shfl_sync(kFullMask, other, t + 1);
+      float4 x0[VPL], x1[VPL];
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+        if (fi < D) {
+          x0[q] = ldg_vec<4>(src + static_cast<int64_t>(c0) * D + fi);
+          x1[q] = ldg_vec<4>(src + static_cast<int64_t>(c1) * D + fi);
+        } else {
+          x0[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+          x1[q] = x0[q];
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) {
+        const float w0 = __shfl_sync(kFullMask, w[hh], t);
+        const float w1 = __shfl_sync(kFullMask, w[hh], t + 1);
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) {
+          vfma(acc[hh][q], w0, x0[q]);
+          vfma(acc[hh][q], w1, x1[q]);
+        }
+      }
+    }
+    if (t < cnt) {
+      const int c0 = __shfl_sync(kFullMask, other, t);
+      float4 x0[VPL];
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+        x0[q] = fi < D ? ldg_vec<4>(src + static_cast<int64_t>(c0) * D + fi)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) {
+        const float w0 = __shfl_sync(kFullMask, w[hh], t);
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) vfma(acc[hh][q], w0, x0[q]);
+      }
+    }
+    float* dst = seg ? partial + item * HD : out + target * HD;
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh) {
+      if (h0 + hh >= H) break;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+        if (fi < D) st_vec(dst + static_cast<int64_t>(h0 + hh) * D + fi, acc[hh][q]);
+      }
+    }
+  }
+}
+
+// Backward K1 of the aggregate-first form (CSR rows): dots(e,h) =
+// U[i,h,:] . X[j,:] over D in 256-float chunks (the row's U chunk in
+// registers, the neighbour's X chunk loaded once for all heads), reduced
+// across the warp; the lane owning edge e keeps its dots.  Light rows then
+// run the softmax/dropout/LeakyReLU backward in registers and write glog and
+// grad_attn_row; hub segments write their dots to glog for the hub-row kernel.
+__global__ void __launch_bounds__(kThreads)
+gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
+                    const int* __restrict__ col, const int* __restrict__ seg_row,
+                    const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
+                    int seg_blocks, const float* __restrict__ attn_row,
+                    const float* __restrict__ attn_col, const float* __restrict__ emax,
+                    const float* __restrict__ esum, const float* __restrict__ U,
+                    const float* __restrict__ X, float slope, float p, uint64_t seed,
+                    float* __restrict__ glog, float* __restrict__ grad_attn_row) {
+  constexpr int kChunk = 256;  // floats of D per pass: 2 float4 per lane
+  const int lane = threadIdx.x & 31;
+  const int group = threadIdx.x >> 5;
+  int64_t row;
+  int e0, e1;
+  bool seg;
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    const int64_t sidx = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + group;
+    if (sidx >= n_seg) return;
+    row = seg_row[sidx];
+    e0 = seg_begin[sidx];
+    e1 = seg_end[sidx];
+    seg = true;
+  } else {
+    row = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
+    if (row >= n) return;
+    e0 = rowptr[row];
+    e1 = rowptr[row + 1];
+    if (e1 - e0 > kSegLen) return;
+    seg = false;
+  }
+  const int k = e0 + lane;
+  const bool valid = k < e1;
+  const int cnt = e1 - e0;
+  const int c = valid ? __ldg(col + k) : 0;
+  const int64_t HD = static_cast<int64_t>(H) * D;
+  for (int h0 = 0; h0 < H; h0 += kAggHB) {
+    float mine[kAggHB];
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh) mine[hh] = 0.0f;
+    for (int64_t f0 = 0; f0 < D; f0 += kChunk) {
+      float4 u[kAggHB][2];
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+          u[hh][q] = (h0 + hh < H && fi < D)
+                         ? ld_vec<4>(U + row * HD + static_cast<int64_t>(h0 + hh) * D + fi)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      for (int t = 0; t < cnt; ++t) {
+        const int ct = __shfl_sync(kFullMask, c, t);
+        float4 x[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+          x[q] = fi < D ? ldg_vec<4>(X + static_cast<int64_t>(ct) * D + fi)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int hh = 0; hh < kAggHB; ++hh) {
+          float d = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            d = fmaf(u[hh][q].x, x[q].x, d);
+            d = fmaf(u[hh][q].y, x[q].y, d);
+            d = fmaf(u[hh][q].z, x[q].z, d);
+            d = fmaf(u[hh][q].w, x[q].w, d);
+          }
+          d = warp_sum(d);
+          if (lane == t) mine[hh] += d;
+        }
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh) {
+      const int h = h0 + hh;
+      if (h >= H) break;
+      const int64_t o = static_cast<int64_t>(k) * H + h;
+      if (seg) {
+        if (valid) glog[o] = mine[hh];
+        continue;
+      }
+      const float ad = attn_row[row * H + h];
+      const float m = emax[row * H + h], s = esum[row * H + h];
+      EdgeSoft es{0.0f, 0.0f, false};
+      if (valid)
+        es = edge_soft(ad, __ldg(attn_col + static_cast<int64_t>(c) * H + h), m, s, slope, p, seed,
+                       static_cast<uint64_t>(k) * H + h, mine[hh]);
+      const float wsum = group_sum<32>(valid ? es.soft * es.ge : 0.0f, kFullMask);
+      float gout = 0.0f;
+      if (valid) {
+        gout = es.soft * (es.ge - wsum);
+        if (es.neg) gout *= slope;
+        glog[o] = gout;
+      }
+      const float grow = group_sum<32>(gout, kFullMask);
+      if (lane == 0) grad_attn_row[row * H + h] = grow;
+    }
+  }
+}
+
+template <int VPL, int MODE>
+int launch_agg(const cign_gat_plan* pl, const SegList& sl, int H, int64_t D, const int* ptr,
+               const int* idx, const int* perm, const float* attn_row, const float* attn_col,
+               float* emax, float* esum, const float* src, float slope, float p, uint64_t seed,
+               float* out, float* partial, const float* glog, float* gcol, float* pcol,
+               cudaStream_t s) {
+  using Cfg = AggCfg<VPL>;
+  const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = seg_blocks + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t tiles = (D + Cfg::kTile - 1) / Cfg::kTile;
+  CIGN_REQUIRE(grid < (1ll << 31) && tiles < 65536, CIGN_ERR_UNSUPPORTED, "gat_agg: grid too large");
+  gat_agg_kernel<VPL, MODE><<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(tiles)),
+                              kThreads, 0, s>>>(
+      static_cast<int>(pl->n), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(), sl.seg_end(),
+      static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col, emax, esum,
+      src, slope, p, seed, out, partial, glog, gcol, pcol);
+  CIGN_CHECK_LAUNCH("gat_agg_kernel");
+  return launch_seg_combine(sl, H, D, partial, MODE == 1 ? pcol : nullptr, out,
+                            MODE == 1 ? gcol : nullptr, s);
+}
+
+// aggregate-first workspace: hub partials [max(n_seg rows, n_seg cols), H*D]
+// | column-hub logit partials [n_seg cols, H] | grad_logit [nnz, H]
+struct AggLayout {
+  size_t partial, pcol, glog, total;
+};
+AggLayout agg_layout(const cign_gat_plan* pl, int H, int64_t D, int64_t C) {
+  AggLayout L;
+  const size_t part = std::max(static_cast<size_t>(pl->rows.n_seg) * D,
+                               static_cast<size_t>(pl->cols.n_seg) * C);
+  L.partial = 0;
+  L.pcol = rnd(part * H * sizeof(float));
+  L.glog = L.pcol + rnd(static_cast<size_t>(pl->cols.n_seg) * H * sizeof(float));
+  L.total = L.glog + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float)) + 256;
+  return L;
+}
+
+int check_agg(const cign_gat_plan* pl, int H, int64_t D, std::initializer_list<const void*> ptrs,
+              const char* name) {
+  int rc = check_plan(pl, H, D, name);
+  if (rc) return rc;
+  CIGN_REQUIRE(D % 4 == 0, CIGN_ERR_UNSUPPORTED, "%s: D must be a multiple of 4", name);
+  for (const void* q : ptrs) {
+    CIGN_REQUIRE(q != nullptr, CIGN_ERR_NULL_POINTER, "%s: NULL tensor argument", name);
+    CIGN_REQUIRE(aligned16(q), CIGN_ERR_ALIGNMENT, "%s: tensors must be 16-byte aligned", name);
+  }
+  return CIGN_OK;
+}
+
 }  // namespace
 }  // namespace cign
 
@@ -2147,6 +2490,88 @@ int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop, uint64_t 
                                                                          mask);
   CIGN_CHECK_LAUNCH("gat_mask_kernel");
   return CIGN_OK;
+}
+
+size_t cign_gat_agg_workspace_bytes(const cign_gat_plan* pl, int32_t heads, int64_t dim,
+                                    int64_t channels) {
+  if (pl == nullptr || heads <= 0 || dim <= 0 || channels <= 0) return 0;
+  return agg_layout(pl, heads, dim, channels).total;
+}
+
+int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const float* attn_row,
+                     const float* attn_col, const float* x, float negative_slope, float attn_drop,
+                     uint64_t seed, float* z, float* edge_max, float* edge_sum, void* ws,
+                     size_t ws_bytes, cign_stream_t stream) {
+  int rc = check_agg(pl, heads, dim, {x, z, ws}, "gat_agg_fwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
+               "gat_agg_fwd: attn_drop must be in [0,1)");
+  CIGN_REQUIRE(attn_row && attn_col && edge_max && edge_sum, CIGN_ERR_NULL_POINTER,
+               "gat_agg_fwd: NULL tensor argument");
+  const AggLayout L = agg_layout(pl, heads, dim, dim);
+  CIGN_REQUIRE(ws_bytes >= L.total, CIGN_ERR_INVALID_ARGUMENT,
+               "gat_agg_fwd: workspace too small (%zu < %zu bytes)", ws_bytes, L.total);
+  if (pl->n == 0) return CIGN_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + L.partial);
+  rc = launch_hub_stats(pl, heads, attn_row, attn_col, negative_slope, edge_max, edge_sum, s);
+  if (rc) return rc;
+  if (dim <= 128)
+    return launch_agg<1, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
+                            attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
+                            partial, nullptr, nullptr, nullptr, s);
+  return launch_agg<2, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
+                          attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
+                          partial, nullptr, nullptr, nullptr, s);
+}
+
+int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_t channels,
+                     const float* attn_row, const float* attn_col, const float* x,
+                     const float* edge_max, const float* edge_sum, const float* grad_z,
+                     const float* grad_pre, float negative_slope, float attn_drop, uint64_t seed,
+                     float* grad_feat, float* grad_attn_row, float* grad_attn_col, void* ws,
+                     size_t ws_bytes, cign_stream_t stream) {
+  int rc = check_agg(pl, heads, dim, {x, grad_z, ws}, "gat_agg_bwd");
+  if (rc) return rc;
+  rc = check_agg(pl, heads, channels, {grad_pre, grad_feat}, "gat_agg_bwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
+               "gat_agg_bwd: attn_drop must be in [0,1)");
+  CIGN_REQUIRE(attn_row && attn_col && edge_max && edge_sum && grad_attn_row && grad_attn_col,
+               CIGN_ERR_NULL_POINTER, "gat_agg_bwd: NULL tensor argument");
+  const AggLayout L = agg_layout(pl, heads, dim, channels);
+  CIGN_REQUIRE(ws_bytes >= L.total, CIGN_ERR_INVALID_ARGUMENT,
+               "gat_agg_bwd: workspace too small (%zu < %zu bytes)", ws_bytes, L.total);
+  if (pl->n == 0) return CIGN_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* w = static_cast<char*>(ws);
+  float* partial = reinterpret_cast<float*>(w + L.partial);
+  float* pcol = reinterpret_cast<float*>(w + L.pcol);
+  float* glog = reinterpret_cast<float*>(w + L.glog);
+  // K1: dots U[i,h,:].X[j,:] and the softmax backward (rows)
+  const SegList& rs = pl->rows;
+  const int64_t seg_blocks = (rs.n_seg + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t grid = seg_blocks + (pl->n + kThreads / 32 - 1) / (kThreads / 32);
+  CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "gat_agg_bwd: grid too large");
+  gat_agg_dots_kernel<<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      static_cast<int>(pl->n), heads, dim, pl->rowptr, pl->col, rs.seg_row(), rs.seg_begin(),
+      rs.seg_end(), static_cast<int>(rs.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
+      edge_max, edge_sum, grad_z, x, negative_slope, attn_drop, seed, glog, grad_attn_row);
+  CIGN_CHECK_LAUNCH("gat_agg_dots_kernel");
+  rc = launch_bwd_hub_rows(pl, heads, channels, attn_row, attn_col, nullptr, edge_max, edge_sum,
+                           nullptr, negative_slope, attn_drop, seed, nullptr, glog, grad_attn_row,
+                           s);
+  if (rc) return rc;
+  // K2: grad_feat[j,h,:] = sum_i w g_pre[i,:] / H and grad_attn_col (columns)
+  float* emax = const_cast<float*>(edge_max);
+  float* esum = const_cast<float*>(edge_sum);
+  if (channels <= 128)
+    return launch_agg<1, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm,
+                            attn_row, attn_col, emax, esum, grad_pre, negative_slope, attn_drop,
+                            seed, grad_feat, partial, glog, grad_attn_col, pcol, s);
+  return launch_agg<2, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm, attn_row,
+                          attn_col, emax, esum, grad_pre, negative_slope, attn_drop, seed,
+                          grad_feat, partial, glog, grad_attn_col, pcol, s);
 }
 
 }  // extern "C"

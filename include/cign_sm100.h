@@ -203,6 +203,37 @@ CIGN_API int cign_gat_bwd(const cign_gat_plan* plan, int32_t heads, int32_t chan
 CIGN_API int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop,
                           uint64_t seed, uint8_t* mask, cign_stream_t stream);
 
+/* Aggregate-first form of the same layer.  GATConv's lin is linear, so with
+ * in_feat[j,h,:] = W_h x[j,:] (W = lin.weight viewed [H, C, D]):
+ *   sum_j w_ij in_feat[j,h,:] = W_h z[i,h,:],  z[i,h,:] = sum_j w_ij x[j,:].
+ * cign_gat_agg_fwd computes z [N,H,D] (and edge_max/edge_sum [N,H]) from the
+ * layer input x [N,D] with exactly the weights of cign_gat_fwd; the caller
+ * applies pre = z.view(N, H*D) @ M + bias with M[(h,d), c] = W_h[c,d] / H.
+ * Each edge then gathers one D-float row instead of H*C floats.
+ * cign_gat_agg_bwd: given grad_z = dL/dz [N,H,D] (= g_pre @ M^T) and
+ * grad_pre = dL/dpre [N,C], writes grad_attn_row/col [N,H] and
+ * grad_feat [N,H,C] = sum_i w_ij g_pre[i,:] / H (so dL/dx through the
+ * aggregation is grad_feat.view(N, H*C) @ lin.weight).
+ * x, z, grad_z, grad_pre, grad_feat and ws 16-byte aligned; D, C multiples
+ * of 4.  Same results as collapsed_gat_forward_cuda / _backward_cuda
+ * (collapsed_gat_cuda.cu:434-545) applied to lin(x), up to the order of
+ * the floating-point sums; it is the form the CIGN block calls
+ * (generic_engine/model_cign.py:551-567). */
+CIGN_API size_t cign_gat_agg_workspace_bytes(const cign_gat_plan* plan, int32_t heads,
+                                             int64_t dim, int64_t channels);
+CIGN_API int cign_gat_agg_fwd(const cign_gat_plan* plan, int32_t heads, int64_t dim,
+                              const float* attn_row, const float* attn_col, const float* x,
+                              float negative_slope, float attn_drop, uint64_t seed, float* z,
+                              float* edge_max, float* edge_sum, void* ws, size_t ws_bytes,
+                              cign_stream_t stream);
+CIGN_API int cign_gat_agg_bwd(const cign_gat_plan* plan, int32_t heads, int64_t dim,
+                              int64_t channels, const float* attn_row, const float* attn_col,
+                              const float* x, const float* edge_max, const float* edge_sum,
+                              const float* grad_z, const float* grad_pre, float negative_slope,
+                              float attn_drop, uint64_t seed, float* grad_feat,
+                              float* grad_attn_row, float* grad_attn_col, void* ws,
+                              size_t ws_bytes, cign_stream_t stream);
+
 /* ------------------------------------------------------------ side ops
  * alpha_src[n,h] = sum_c x[n,h,c] att_src[h,c];  same for dst.
  * Replaces attention_forward_cuda (fused_gat_sideops_cuda.cu:243-260). */
