@@ -171,22 +171,36 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
   }
 }
 
-// Hub-row combine: Y[row] = sum of the row's segment partials in segment
-// order (+ addend).  Block (hub, chunk) covers kCombineThreads * VEC columns
-// of one hub row, with several partial loads in flight per thread.
+// Hub-row combine: Y[row] = sum of the row's segment partials (+ addend).
+// Block (hub, chunk) covers kCombineThreads * VEC columns of one hub row; its
+// kCombineWays thread rows each sum a contiguous quarter of the segments in
+// order (several loads in flight), and the quarter sums are then added in
+// quarter order -- a fixed order, with a critical path a quarter as long.
 constexpr int kCombineThreads = 64;
+constexpr int kCombineWays = 4;
 
 template <int VEC>
-__global__ void __launch_bounds__(kCombineThreads)
+__global__ void __launch_bounds__(kCombineThreads * kCombineWays)
 spmm_combine_kernel(const int* __restrict__ heavy_row, const int* __restrict__ heavy_first,
                     const float* __restrict__ partial, int64_t F,
                     const float* __restrict__ addend, float* __restrict__ Y) {
   using V = typename VecT<VEC>::type;
+  __shared__ V part[kCombineWays - 1][kCombineThreads];
   const int h = blockIdx.x;
-  const int64_t f = (static_cast<int64_t>(blockIdx.y) * kCombineThreads + threadIdx.x) * VEC;
-  if (f >= F) return;
+  const int tx = threadIdx.x % kCombineThreads, way = threadIdx.x / kCombineThreads;
+  const int64_t f = (static_cast<int64_t>(blockIdx.y) * kCombineThreads + tx) * VEC;
+  const int s0 = heavy_first[h], s1 = heavy_first[h + 1];
+  const int per = (s1 - s0 + kCombineWays - 1) / kCombineWays;
+  const int a = min(s1, s0 + way * per), b = min(s1, a + per);
+  V acc;
+  vzero(acc);
+  if (f < F) acc = ordered_sum<VEC>(partial + f, F, a, b);
+  if (way > 0) part[way - 1][tx] = acc;
+  __syncthreads();
+  if (way > 0 || f >= F) return;
+#pragma unroll
+  for (int w = 0; w < kCombineWays - 1; ++w) vadd(acc, part[w][tx]);
   const int64_t row = heavy_row[h];
-  V acc = ordered_sum<VEC>(partial + f, F, heavy_first[h], heavy_first[h + 1]);
   if (addend != nullptr) vadd(acc, ld_vec<VEC>(addend + row * F + f));
   st_vec(Y + row * F + f, acc);
 }
@@ -199,8 +213,8 @@ int launch_spmm_combine(const SegList& sl, const float* partial, int64_t F, cons
   const int64_t chunks = (F / VEC * VEC + per_block - 1) / per_block;
   CIGN_REQUIRE(chunks < 65536, CIGN_ERR_UNSUPPORTED, "spmm: F too large for the hub combine");
   const dim3 grid(static_cast<unsigned>(sl.n_heavy), static_cast<unsigned>(chunks));
-  spmm_combine_kernel<VEC><<<grid, kCombineThreads, 0, stream>>>(sl.heavy_row(), sl.heavy_first(),
-                                                                 partial, F, addend, Y);
+  spmm_combine_kernel<VEC><<<grid, kCombineThreads * kCombineWays, 0, stream>>>(
+      sl.heavy_row(), sl.heavy_first(), partial, F, addend, Y);
   CIGN_CHECK_LAUNCH("spmm_combine_kernel");
   return CIGN_OK;
 }

@@ -21,7 +21,7 @@ outer nonlinearity "none"):
    the aggregation, so each edge gathers one D-float row, not heads*D.)
     C_norm = LN(C_gat + H_norm)                             fused_block_ops
     T^k    = P^k [H_norm | C_norm], k in order_set          multihop_csr_pipeline
-    alpha  = softmax(hop_gate_mlp([H+C | |H-C|]))           torch
+    alpha  = softmax(hop_gate_mlp([H+C | |H-C|]))           hop_gate (fused)
     G_raw  = Clifford pack(H_norm, C_norm, T, alpha)        fused_clifford_*
     H'     = H + gamma * dropout(proj(G_raw))               fused_block_ops
 Net (model_cign.py:1160-1212): dropout, dual input projection + SiLU, L
@@ -41,6 +41,7 @@ from .collapsed_gat import collapsed_gat_aggregate_first, collapsed_gat_mean_bia
 from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, fused_dropout_layernorm
 from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
+from .hop_gate import fused_hop_gate
 
 
 def _glorot_(t: torch.Tensor) -> None:
@@ -48,6 +49,20 @@ def _glorot_(t: torch.Tensor) -> None:
     a = math.sqrt(6.0 / (fan_in + fan_out))
     with torch.no_grad():
         t.uniform_(-a, a)
+
+
+def _linear_padded(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """F.linear with the output width padded to a multiple of 4 (zero rows of
+    weight/bias) and sliced back: a 5-wide output row is not 16-byte aligned,
+    which sends cuBLAS to slow unaligned kernels; the padded columns are
+    never read, so values and gradients equal F.linear's."""
+    k = weight.size(0)
+    pad = (-k) % 4
+    if pad == 0 or not x.is_cuda:
+        return F.linear(x, weight, bias)
+    w = F.pad(weight, (0, 0, 0, pad))
+    b = F.pad(bias, (0, pad))
+    return F.linear(x, w, b)[:, :k]
 
 
 class GATContext(nn.Module):
@@ -123,6 +138,9 @@ class GraphCliffordBlock(nn.Module):
         self.gamma = nn.Parameter(torch.full((hidden_dim,), float(init_gamma)))
 
     def compute_hop_gate(self, H_norm, C_norm):
+        if H_norm.size(1) % 4 == 0 and self.num_hops <= 8 and H_norm.is_cuda:
+            return fused_hop_gate(H_norm, C_norm, self.hop_gate_mlp.weight, self.hop_gate_mlp.bias,
+                                  self.alpha_score_mode).unsqueeze(-1)
         if self.alpha_score_mode == "old":
             gate_input = torch.cat([H_norm, C_norm], dim=-1)
         else:
@@ -206,7 +224,7 @@ class GraphCliffordNet(nn.Module):
             states.append(H)
         H_out = self.output_norm(torch.cat(states, dim=-1))
         H_out = F.dropout(H_out, p=self.dropout, training=self.training)
-        return self.classifier(H_out).float()
+        return _linear_padded(H_out, self.classifier.weight, self.classifier.bias).float()
 
 
 def build_model(in_dim: int, hidden_dim: int, out_dim: int, num_layers: int = 4,

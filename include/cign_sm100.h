@@ -305,6 +305,25 @@ CIGN_API int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
                   int32_t accumulate_p, float* grad_alpha,
                   cign_stream_t stream);
 
+/* ------------------------------------------------------------ hop gate
+ * alpha [N,K] = softmax_k(g @ W^T + b) with g = [H + C | |H - C|] (mode 1,
+ * alpha_score_mode "new") or [H | C] (mode 0, "old"); H, C [N,D], W [K,2D],
+ * b [K], 1 <= K <= 8, D a multiple of 4, H/C/W 16-byte aligned.  The gate
+ * input is never materialised and the linear runs in fp32.
+ * Replaces GraphCliffordBlock.compute_hop_gate (generic_engine/
+ * model_cign.py:721-749: torch.cat + abs + nn.Linear + softmax). */
+CIGN_API int cign_hop_gate_fwd(int64_t n, int64_t d, int32_t k, int32_t mode, const float* h,
+                               const float* c, const float* w, const float* b, float* alpha,
+                               cign_stream_t stream);
+CIGN_API size_t cign_hop_gate_bwd_workspace_bytes(int64_t n, int64_t d, int32_t k);
+/* Backward: grad_h, grad_c [N,D] (written), grad_w [K,2D], grad_b [K]
+ * (fixed-order sums: deterministic); sign(0) = 0 for |H - C|. */
+CIGN_API int cign_hop_gate_bwd(int64_t n, int64_t d, int32_t k, int32_t mode, const float* h,
+                               const float* c, const float* w, const float* alpha,
+                               const float* grad_alpha, float* grad_h, float* grad_c,
+                               float* grad_w, float* grad_b, void* ws, size_t ws_bytes,
+                               cign_stream_t stream);
+
 /* ------------------------------------------------------------ block ops
  * Row LayerNorm over D with biased variance and rsqrt(var + eps); optional
  * dropout (keep iff (splitmix64(seed ^ idx*0xD2B74407B1CE6E93) >> 11) * 2^-53
