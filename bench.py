@@ -139,7 +139,7 @@ def build_graph(cfg, device):
     return op, ((rp, c), (r, cp), perm), int(base.nnz), int(c.numel())
 
 
-def build_model_and_data(cfg, device, seed=0):
+def build_model_and_data(cfg, device, seed=0, capturable=False):
     from cign_b200 import synth
     from cign_b200.model_cign import build_model
     torch.manual_seed(seed)
@@ -147,16 +147,18 @@ def build_model_and_data(cfg, device, seed=0):
     model = build_model(in_dim=cfg.in_dim, hidden_dim=cfg.hidden_dim, out_dim=cfg.num_classes,
                         num_layers=cfg.layers, dropout=cfg.dropout, hop_scales=cfg.hops,
                         gat_heads=cfg.heads, gat_dropout=cfg.gat_dropout).to(device)
-    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5)
+    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5, capturable=capturable)
     return model, opt, x, y, train
 
 
-def train_step(model, opt, op, x, y, train_mask):
-    """optimizer.zero_grad -> forward -> CE(train) -> backward -> Adam.step
-    (generic_engine/train_cign.py:2103-2148)."""
-    opt.zero_grad()
+def train_step(model, opt, op, x, y, train_idx):
+    """optimizer.zero_grad -> forward -> CE(train rows) -> backward -> Adam.step
+    (generic_engine/train_cign.py:2103-2148).  The train rows are gathered by
+    a precomputed index (the same rows, in the same order, as the reference's
+    boolean mask, without its host synchronisation)."""
+    opt.zero_grad(set_to_none=True)
     logits = model(x, op)
-    loss = F.cross_entropy(logits[train_mask], y[train_mask])
+    loss = F.cross_entropy(logits.index_select(0, train_idx), y.index_select(0, train_idx))
     loss.backward()
     opt.step()
     return loss
@@ -343,6 +345,8 @@ def main():
     ap.add_argument("--workload", default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-nodes", type=int, default=6000)
+    ap.add_argument("--eager", action="store_true",
+                    help="launch every op from Python each step (default: replay one CUDA graph)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -399,16 +403,33 @@ def main():
     lib = _lib.load_library()
 
     op, gat_graph, nnz, nnz_g = build_graph(cfg, device)
-    model, opt, x_cpu, y_cpu, train_cpu = build_model_and_data(cfg, device, seed=rank)
+    use_graph = not args.eager
+    model, opt, x_cpu, y_cpu, train_cpu = build_model_and_data(cfg, device, seed=rank,
+                                                               capturable=use_graph)
     x = x_cpu.to(device)
     y = y_cpu.to(device)
-    train = train_cpu.to(device)
+    train_idx = train_cpu.to(device).nonzero().squeeze(1)
     model.prepare_fused_gat_graph(gat_graph)
     edge_passes = 2 * cfg.layers * len(cfg.hops) * nnz
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
 
-    for _ in range(args.warmup):
-        train_step(model, opt, op, x, y, train)
+    from cign_b200.plans import HopTimer, SpmmPlan
+    hop_timer = HopTimer()
+    step = lambda: train_step(model, opt, op, x, y, train_idx)  # noqa: E731
+    graphed = None
+    if use_graph:
+        from cign_b200.graph_step import GraphedStep
+
+        def install_timer():  # the captured step records its k-hop events
+            SpmmPlan.hop_timer = hop_timer
+
+        graphed = GraphedStep(step, device, warmup=args.warmup, before_capture=install_timer)
+        SpmmPlan.hop_timer = None
+        run_step = graphed
+    else:
+        for _ in range(args.warmup):
+            step()
+        run_step = step
     torch.cuda.synchronize()
     launches_before = int(lib.cign_kernel_launches())
 
@@ -419,19 +440,21 @@ def main():
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    from cign_b200.plans import HopTimer, SpmmPlan
-    hop_timer = HopTimer()
-    SpmmPlan.hop_timer = hop_timer  # CUDA events around every k-hop call, same stream
+    if not use_graph:
+        SpmmPlan.hop_timer = hop_timer  # CUDA events around every k-hop call, same stream
     sampler.start()
     for i in range(args.steps):
         flush.zero_()  # L2 flush between timed steps (outside the per-step events)
         starts[i].record(stream)
-        train_step(model, opt, op, x, y, train)
+        run_step()
         ends[i].record(stream)
     torch.cuda.synchronize()
     SpmmPlan.hop_timer = None
     clocks = sampler.stop()
-    timed_launches = int(lib.cign_kernel_launches()) - launches_before
+    # kernels launched per step: counted by the library while the graph was
+    # captured (one step), or over the timed eager steps
+    timed_launches = (graphed.native_launches * args.steps if use_graph
+                      else int(lib.cign_kernel_launches()) - launches_before)
     if dist is not None:
         dist.barrier()
     step_s = [s.elapsed_time(e) * 1e-3 for s, e in zip(starts, ends)]
@@ -446,7 +469,7 @@ def main():
     # end-to-end through the public API: features from pinned host memory,
     # loss read back every step.
     x_pin = x_cpu.pin_memory()
-    x_dev = torch.empty_like(x)
+    x_dev = x  # the step's static input buffer
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     loss_host = 0.0
@@ -456,7 +479,7 @@ def main():
     e_start.record(stream)
     for _ in range(args.steps):
         x_dev.copy_(x_pin, non_blocking=True)
-        loss = train_step(model, opt, op, x_dev, y, train)
+        loss = run_step()
         loss_host = float(loss.item())  # device -> host read of the step result
     e_end.record(stream)
     torch.cuda.synchronize()
@@ -473,6 +496,9 @@ def main():
         peak, peak_kind = load_peaks()
         kernels = kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device)
         roofline = hop_roofline(hop_timer, cfg.num_nodes, nnz, peak, peak_kind)
+        if roofline is not None and use_graph:
+            roofline["timing"] = ("CUDA events captured around every k-hop call inside the step "
+                                  "graph, read after the last timed replay")
         cpu_baseline = None
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample_config(cfg, args.cpu_sample_nodes)
@@ -493,6 +519,7 @@ def main():
                        "heads": cfg.heads, "layers": cfg.layers, "dropout": cfg.dropout,
                        "dense_gemm": "tf32 (cuBLAS via torch)",
                        "l2": "flushed between timed steps (256 MiB write)",
+                       "launch": "one CUDA graph per step" if use_graph else "eager",
                        "parallelism": f"replicas{world}" if world > 1 else "single"},
             "epoch_ms": round(ms_per_step, 4),
             "ms_per_step_median": round(statistics.median(step_s) * 1e3, 4),

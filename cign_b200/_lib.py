@@ -81,21 +81,22 @@ SIGNATURES = {
     "cign_gat_plan_destroy": (c_int, [_P]),
     "cign_gat_plan_get_info": (c_int, [_P, POINTER(c_int64)]),
     "cign_gat_fwd_workspace_bytes": (c_size_t, [_P, c_int32, c_int32]),
-    "cign_gat_fwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, c_float, c_float, c_uint64,
+    "cign_gat_fwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, c_float, c_float, c_uint64, _P,
                              _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_gat_bwd_workspace_bytes": (c_size_t, [_P, c_int32, c_int32]),
     "cign_gat_bwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, c_float, c_float,
-                             c_uint64, _P, _P, _P, _P, _P, c_size_t, _P]),
-    "cign_gat_dropout_mask": (c_int, [c_int64, c_int32, c_float, c_uint64, _P, _P]),
+                             c_uint64, _P, _P, _P, _P, _P, _P, c_size_t, _P]),
+    "cign_gat_dropout_mask": (c_int, [c_int64, c_int32, c_float, c_uint64, _P, _P, _P]),
+    "cign_seed_table_step": (c_int, [c_uint64, c_int32, _P, _P, c_int32, c_int32, _P, _P]),
     "cign_hop_gate_fwd": (c_int, [c_int64, c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P]),
     "cign_hop_gate_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int32]),
     "cign_hop_gate_bwd": (c_int, [c_int64, c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P,
                                   _P, _P, _P, c_size_t, _P]),
     "cign_gat_agg_workspace_bytes": (c_size_t, [_P, c_int32, c_int64, c_int64]),
-    "cign_gat_agg_fwd": (c_int, [_P, c_int32, c_int64, _P, _P, _P, c_float, c_float, c_uint64,
+    "cign_gat_agg_fwd": (c_int, [_P, c_int32, c_int64, _P, _P, _P, c_float, c_float, c_uint64, _P,
                                  _P, _P, _P, _P, c_size_t, _P]),
     "cign_gat_agg_bwd": (c_int, [_P, c_int32, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P,
-                                 c_float, c_float, c_uint64, _P, _P, _P, _P, c_size_t, _P]),
+                                 c_float, c_float, c_uint64, _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_attn_logits_fwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P]),
     "cign_attn_logits_bwd_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
     "cign_attn_logits_bwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
@@ -108,21 +109,21 @@ SIGNATURES = {
                               c_int64, _P, _P, _P]),
     "cign_pack_bwd": (c_int, [c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, _P, _P, _P,
                               _PP, c_int64, _P, _P, _P, _PP, c_int64, c_int32, _P, _P]),
-    "cign_dropout_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_float, c_uint64,
+    "cign_dropout_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_float, c_uint64, _P,
                                     _P, _P, _P, _P]),
     "cign_ln_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
-    "cign_dropout_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, c_uint64, _P,
+    "cign_dropout_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, c_uint64, _P, _P,
                                     _P, _P, _P, c_size_t, _P]),
     "cign_dropout_ln_bwd_static": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, c_uint64,
                                            _P, _P, _P, _P]),
     "cign_add_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, c_float, _P, _P, _P, _P]),
     "cign_add_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                 c_size_t, _P]),
-    "cign_gamma_residual_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_uint64, _P, _P]),
+    "cign_gamma_residual_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_uint64, _P, _P, _P]),
     "cign_gamma_residual_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
-    "cign_gamma_residual_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_uint64, _P, _P,
+    "cign_gamma_residual_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_uint64, _P, _P, _P,
                                         _P, c_size_t, _P]),
-    "cign_block_dropout_mask": (c_int, [c_int64, c_float, c_uint64, _P, _P]),
+    "cign_block_dropout_mask": (c_int, [c_int64, c_float, c_uint64, _P, _P, _P]),
 }
 
 
@@ -169,6 +170,16 @@ def check(rc: int, what: str) -> None:
 def require_cuda(what: str) -> None:
     if not torch.cuda.is_available():
         raise RuntimeError(f"{what} requires CUDA.")
+
+
+def seed_args(seed) -> tuple:
+    """(value, device pointer) of a dropout seed for the ABI's
+    `uint64_t seed, const uint64_t* seed_ptr` pair: a Python int is passed by
+    value; a one-element int64 CUDA tensor (a slot of a device seed table) is
+    passed by address and read by the kernel when it runs."""
+    if isinstance(seed, torch.Tensor):
+        return 0, c_void_p(seed.data_ptr())
+    return int(seed) & ((1 << 64) - 1), None
 
 
 def ptr(t: torch.Tensor | None) -> c_void_p:

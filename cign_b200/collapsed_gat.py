@@ -18,17 +18,14 @@ collapsed_gat.cpp:67-68) any 1 <= H <= 64 and C >= 1 run natively.
 """
 from __future__ import annotations
 
-import itertools
-
 import torch
 
-from . import _lib
+from . import _lib, seeds
 from .plans import gat_plan_for
 
 _EXT = None
 _EXT_ERROR = None
-_CALL_COUNTER = itertools.count()
-_MASK63 = (1 << 63) - 1
+_CALL_COUNTER = seeds.counter_iter(seeds.GAT)  # GAT call ids (shared with seeds.next_seed)
 MAX_HEADS = 64
 
 
@@ -52,11 +49,10 @@ def ensure_collapsed_gat_loaded(verbose: bool = False):
     return _EXT
 
 
-def gat_call_seed(attn_drop: float) -> int:
-    """Seed of the next call (advances the counter only when attn_drop > 0)."""
-    base_seed = int(torch.initial_seed()) & _MASK63
-    call_id = next(_CALL_COUNTER) if float(attn_drop) > 0.0 else -1
-    return 0 if call_id < 0 else (base_seed + 0x9E3779B97F4A7C15 * (call_id + 1)) & _MASK63
+def gat_call_seed(attn_drop: float):
+    """Seed of the next call (advances the counter only when attn_drop > 0):
+    an int, or a device seed slot while a seeds.DeviceSeedTable records."""
+    return seeds.next_seed(seeds.GAT, attn_drop)
 
 
 def gat_forward_raw(plan, attn_row, attn_col, in_feat, bias, negative_slope, attn_drop, seed):
@@ -71,7 +67,7 @@ def gat_forward_raw(plan, attn_row, attn_col, in_feat, bias, negative_slope, att
     with _lib.DeviceGuard(in_feat.device):
         rc = lib.cign_gat_fwd(plan.handle, H, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
                               _lib.ptr(in_feat), _lib.ptr(bias), float(negative_slope),
-                              float(attn_drop), int(seed) & ((1 << 64) - 1), _lib.ptr(out),
+                              float(attn_drop), *_lib.seed_args(seed), _lib.ptr(out),
                               _lib.ptr(pre), _lib.ptr(emax), _lib.ptr(esum), _lib.ptr(ws),
                               ws.numel(), _lib.stream_of(in_feat))
     _lib.check(rc, "cign_gat_fwd")
@@ -94,7 +90,7 @@ def gat_backward_raw(plan, attn_row, attn_col, in_feat, pre, emax, esum, grad_y,
         rc = lib.cign_gat_bwd(plan.handle, H, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
                               _lib.ptr(in_feat), _lib.ptr(pre), _lib.ptr(emax), _lib.ptr(esum),
                               _lib.ptr(grad_y), float(negative_slope), float(attn_drop),
-                              int(seed) & ((1 << 64) - 1), _lib.ptr(gfeat), _lib.ptr(grow),
+                              *_lib.seed_args(seed), _lib.ptr(gfeat), _lib.ptr(grow),
                               _lib.ptr(gcol), _lib.ptr(gbias), _lib.ptr(ws), ws.numel(),
                               _lib.stream_of(in_feat))
     _lib.check(rc, "cign_gat_bwd")
@@ -107,7 +103,7 @@ def gat_dropout_mask(nnz: int, heads: int, attn_drop: float, seed: int, device) 
     mask = torch.empty((int(nnz), int(heads)), dtype=torch.uint8, device=device)
     with _lib.DeviceGuard(device):
         rc = lib.cign_gat_dropout_mask(int(nnz), int(heads), float(attn_drop),
-                                       int(seed) & ((1 << 64) - 1), _lib.ptr(mask),
+                                       *_lib.seed_args(seed), _lib.ptr(mask),
                                        _lib.stream_on(device))
     _lib.check(rc, "cign_gat_dropout_mask")
     return mask
@@ -136,7 +132,7 @@ class _CollapsedGATFn(torch.autograd.Function):
         ctx.plan = plan
         ctx.negative_slope = float(negative_slope)
         ctx.attn_drop = float(attn_drop)
-        ctx.seed = int(seed)
+        ctx.seed = seed
         return out
 
     @staticmethod
@@ -173,7 +169,7 @@ def collapsed_gat_mean_bias_silu(
     (rowptr, col), (row, colptr) = csr, csc
     seed = gat_call_seed(attn_drop)
     return _CollapsedGATFn.apply(attn_row, attn_col, rowptr, col, colptr, row, perm,
-                                 float(negative_slope), in_feat, bias, float(attn_drop), int(seed))
+                                 float(negative_slope), in_feat, bias, float(attn_drop), seed)
 
 
 # ---------------------------------------------------------------- aggregate-first
@@ -189,7 +185,7 @@ def gat_agg_forward_raw(plan, attn_row, attn_col, x, heads, negative_slope, attn
     with _lib.DeviceGuard(x.device):
         rc = lib.cign_gat_agg_fwd(plan.handle, H, D, _lib.ptr(attn_row), _lib.ptr(attn_col),
                                   _lib.ptr(x), float(negative_slope), float(attn_drop),
-                                  int(seed) & ((1 << 64) - 1), _lib.ptr(z), _lib.ptr(emax),
+                                  *_lib.seed_args(seed), _lib.ptr(z), _lib.ptr(emax),
                                   _lib.ptr(esum), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
     _lib.check(rc, "cign_gat_agg_fwd")
     return z, emax, esum
@@ -211,7 +207,7 @@ def gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z, grad_p
         rc = lib.cign_gat_agg_bwd(plan.handle, H, D, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
                                   _lib.ptr(x), _lib.ptr(emax), _lib.ptr(esum), _lib.ptr(grad_z),
                                   _lib.ptr(grad_pre), float(negative_slope), float(attn_drop),
-                                  int(seed) & ((1 << 64) - 1), _lib.ptr(gfeat), _lib.ptr(grow),
+                                  *_lib.seed_args(seed), _lib.ptr(gfeat), _lib.ptr(grow),
                                   _lib.ptr(gcol), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
     _lib.check(rc, "cign_gat_agg_bwd")
     return gfeat, grow, gcol
@@ -240,7 +236,7 @@ class _AggregateFirstGATFn(torch.autograd.Function):
         pre = torch.addmm(bias, z.view(n, H * D), M)
         ctx.save_for_backward(x, attn_row, attn_col, weight, z, pre, emax, esum)
         ctx.plan, ctx.heads = plan, H
-        ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), int(seed)
+        ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), seed
         return torch.nn.functional.silu(pre)
 
     @staticmethod
@@ -287,4 +283,4 @@ def collapsed_gat_aggregate_first(x: torch.Tensor, attn_row: torch.Tensor, attn_
     seed = gat_call_seed(attn_drop)
     return _AggregateFirstGATFn.apply(x.contiguous(), attn_row.contiguous(), attn_col.contiguous(),
                                       weight, bias, plan, H, float(negative_slope),
-                                      float(attn_drop), int(seed))
+                                      float(attn_drop), seed)

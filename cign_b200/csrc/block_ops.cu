@@ -59,8 +59,9 @@ template <int MODE, int VEC, int VPL, int LPR>
 __global__ void __launch_bounds__(kThreads)
 ln_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ x, const float* __restrict__ x2,
               const float* __restrict__ w, const float* __restrict__ b, float p, float eps,
-              uint64_t seed, float* __restrict__ y, float* __restrict__ mean,
+              Seed seed_in, float* __restrict__ y, float* __restrict__ mean,
               float* __restrict__ rstd) {
+  const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   using Cfg = RowCfg<VEC, VPL, LPR>;
   const int lig = threadIdx.x % LPR;
@@ -131,8 +132,9 @@ __global__ void __launch_bounds__(kThreads)
 ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
               const float* __restrict__ x, const float* __restrict__ x2,
               const float* __restrict__ w, const float* __restrict__ mean,
-              const float* __restrict__ rstd, float p, uint64_t seed,
+              const float* __restrict__ rstd, float p, Seed seed_in,
               float* __restrict__ gx, float* __restrict__ pw, float* __restrict__ pb) {
+  const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   using Cfg = RowCfg<VEC, VPL, LPR>;
   __shared__ float red[kThreads * VPL * VEC];  // per thread: VPL*VEC partials
@@ -227,7 +229,8 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
 template <int VEC>
 __global__ void gamma_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ h,
                                  const float* __restrict__ g, const float* __restrict__ gamma,
-                                 float p, uint64_t seed, float* __restrict__ y) {
+                                 float p, Seed seed_in, float* __restrict__ y) {
+  const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   const int64_t total = n * D / VEC;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -255,7 +258,8 @@ template <int VEC, int VPL, int LPR>
 __global__ void __launch_bounds__(kThreads)
 gamma_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
                  const float* __restrict__ g, const float* __restrict__ gamma, float p,
-                 uint64_t seed, float* __restrict__ gg, float* __restrict__ partial) {
+                 Seed seed_in, float* __restrict__ gg, float* __restrict__ partial) {
+  const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   using Cfg = RowCfg<VEC, VPL, LPR>;
   __shared__ float red[kThreads * VPL * VEC];
@@ -300,8 +304,9 @@ gamma_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy
   }
 }
 
-__global__ void block_mask_kernel(int64_t count, float p, uint64_t seed,
+__global__ void block_mask_kernel(int64_t count, float p, Seed seed_in,
                                   uint8_t* __restrict__ mask) {
+  const uint64_t seed = seed_in;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
        i += stride)
@@ -330,7 +335,7 @@ int check_rows(int64_t n, int64_t D, bool v4, const char* name) {
 
 template <int MODE, int VEC, int VPL, int LPR>
 int launch_ln_fwd(int64_t n, int64_t D, const float* x, const float* x2, const float* w,
-                  const float* b, float p, float eps, uint64_t seed, float* y, float* mean,
+                  const float* b, float p, float eps, Seed seed, float* y, float* mean,
                   float* rstd, cudaStream_t s) {
   using Cfg = RowCfg<VEC, VPL, LPR>;
   const int64_t grid = (n + Cfg::kGroups - 1) / Cfg::kGroups;
@@ -342,7 +347,7 @@ int launch_ln_fwd(int64_t n, int64_t D, const float* x, const float* x2, const f
 
 template <int MODE, int VEC, int VPL, int LPR>
 int launch_ln_bwd(int64_t n, int64_t D, const float* gy, const float* x, const float* x2,
-                  const float* w, const float* mean, const float* rstd, float p, uint64_t seed,
+                  const float* w, const float* mean, const float* rstd, float p, Seed seed,
                   float* gx, float* gw, float* gb, float* ws, cudaStream_t s) {
   const int64_t rpc = rows_per_chunk(n);
   const int64_t chunks = num_chunks(n);
@@ -356,7 +361,7 @@ int launch_ln_bwd(int64_t n, int64_t D, const float* gy, const float* x, const f
 
 template <int VEC, int VPL, int LPR>
 int launch_gamma_bwd(int64_t n, int64_t D, const float* gy, const float* g, const float* gamma,
-                     float p, uint64_t seed, float* gg, float* ggamma, float* ws,
+                     float p, Seed seed, float* gg, float* ggamma, float* ws,
                      cudaStream_t s) {
   const int64_t rpc = rows_per_chunk(n);
   const int64_t chunks = num_chunks(n);
@@ -374,8 +379,10 @@ using namespace cign;
 extern "C" {
 
 int cign_dropout_ln_fwd(int64_t n, int64_t d, const float* x, const float* w, const float* b,
-                        float p, float eps, uint64_t seed, float* y, float* mean, float* rstd,
+                        float p, float eps, uint64_t seed_value, const uint64_t* seed_ptr,
+                        float* y, float* mean, float* rstd,
                         cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   const bool v4 = d % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y);
   int rc = check_rows(n, d, v4, "dropout_ln_fwd");
   if (rc) return rc;
@@ -397,8 +404,10 @@ size_t cign_ln_bwd_workspace_bytes(int64_t n, int64_t d) {
 
 int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* x,
                         const float* w, const float* mean, const float* rstd, float p,
-                        uint64_t seed, float* grad_x, float* grad_w, float* grad_b, void* ws,
+                        uint64_t seed_value, const uint64_t* seed_ptr,
+                        float* grad_x, float* grad_w, float* grad_b, void* ws,
                         size_t ws_bytes, cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   const bool v4 = d % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(grad_y) &&
                   aligned16(grad_x);
   int rc = check_rows(n, d, v4, "dropout_ln_bwd");
@@ -467,8 +476,10 @@ int cign_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* a, c
 }
 
 int cign_gamma_residual_fwd(int64_t n, int64_t d, const float* h, const float* g,
-                            const float* gamma, float p, uint64_t seed, float* y,
+                            const float* gamma, float p, uint64_t seed_value, const uint64_t* seed_ptr,
+                            float* y,
                             cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   CIGN_REQUIRE(n >= 0 && d >= 1, CIGN_ERR_INVALID_ARGUMENT, "gamma_residual_fwd: bad sizes");
   CIGN_REQUIRE(p >= 0.0f && p < 1.0f, CIGN_ERR_INVALID_ARGUMENT, "gamma_residual_fwd: p in [0,1)");
   if (n == 0) return CIGN_OK;
@@ -489,9 +500,11 @@ size_t cign_gamma_residual_bwd_workspace_bytes(int64_t n, int64_t d) {
 }
 
 int cign_gamma_residual_bwd(int64_t n, int64_t d, const float* grad_y, const float* g,
-                            const float* gamma, float p, uint64_t seed, float* grad_g,
+                            const float* gamma, float p, uint64_t seed_value, const uint64_t* seed_ptr,
+                            float* grad_g,
                             float* grad_gamma, void* ws, size_t ws_bytes,
                             cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   const bool v4 = d % 4 == 0 && aligned16(grad_y) && aligned16(g) && aligned16(gamma) &&
                   aligned16(grad_g);
   int rc = check_rows(n, d, v4, "gamma_residual_bwd");
@@ -513,8 +526,10 @@ int cign_gamma_residual_bwd(int64_t n, int64_t d, const float* grad_y, const flo
   return CIGN_OK;
 }
 
-int cign_block_dropout_mask(int64_t count, float p, uint64_t seed, uint8_t* mask,
+int cign_block_dropout_mask(int64_t count, float p, uint64_t seed_value, const uint64_t* seed_ptr,
+                            uint8_t* mask,
                             cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   CIGN_REQUIRE(count >= 0, CIGN_ERR_INVALID_ARGUMENT, "block_dropout_mask: bad count");
   if (count == 0) return CIGN_OK;
   CIGN_REQUIRE(mask != nullptr, CIGN_ERR_NULL_POINTER, "block_dropout_mask: NULL mask");

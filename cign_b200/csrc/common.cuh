@@ -107,6 +107,18 @@ __device__ __forceinline__ float leaky_f(float x, float slope) {
 }
 
 // ---------------------------------------------------------------- RNG
+// Dropout seed of one call: a value, or (ptr != NULL) the value stored in
+// device memory at ptr -- read by the kernel, so a captured CUDA graph can
+// draw a new seed on every replay.  Kernels convert it once on entry.
+struct Seed {
+  uint64_t value = 0;
+  const uint64_t* ptr = nullptr;
+  Seed() = default;
+  Seed(uint64_t v) : value(v) {}  // NOLINT: implicit on purpose (plain seeds)
+  Seed(uint64_t v, const uint64_t* p) : value(v), ptr(p) {}
+  __device__ __forceinline__ operator uint64_t() const { return ptr != nullptr ? *ptr : value; }
+};
+
 // splitmix64 finaliser (Steele, Lea, Flood 2014) -- the counter-based hash
 // both dropout streams of the reference use.  idx is hashed as
 // seed ^ (idx * 0xD2B74407B1CE6E93).

@@ -224,9 +224,10 @@ gat_fwd_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
                const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
                int seg_blocks, const float* __restrict__ attn_row,
                const float* __restrict__ attn_col, const float* __restrict__ x,
-               const float* __restrict__ bias, float slope, float p, uint64_t seed,
+               const float* __restrict__ bias, float slope, float p, Seed seed_in,
                float* __restrict__ out, float* __restrict__ pre, float* __restrict__ emax,
                float* __restrict__ esum, float* __restrict__ partial) {
+  const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   using Cfg = GatCfg<VEC, VPL, LPR>;
   extern __shared__ float smem[];  // [kGroups][2H] row statistics
@@ -460,8 +461,9 @@ gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
                     const float* __restrict__ attn_col, const float* __restrict__ x,
                     const float* __restrict__ pre, const float* __restrict__ emax,
                     const float* __restrict__ esum, const float* __restrict__ grad_y,
-                    float slope, float p, uint64_t seed, float* __restrict__ gpre,
+                    float slope, float p, Seed seed_in, float* __restrict__ gpre,
                     float* __restrict__ glog, float* __restrict__ grad_attn_row) {
+  const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const int lig = threadIdx.x % LPR;
@@ -527,8 +529,9 @@ gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
                         const float* __restrict__ attn_row, const float* __restrict__ attn_col,
                         const float* __restrict__ pre, const float* __restrict__ emax,
                         const float* __restrict__ esum, const float* __restrict__ grad_y,
-                        float slope, float p, uint64_t seed, float* __restrict__ gpre,
+                        float slope, float p, Seed seed_in, float* __restrict__ gpre,
                         float* __restrict__ glog, float* __restrict__ grad_attn_row) {
+  const uint64_t seed = seed_in;
   __shared__ float scratch[32];
   const int64_t row = hub_row[blockIdx.x];
   const int h = blockIdx.y;
@@ -659,9 +662,10 @@ gat_bwd_cols_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
                     const float* __restrict__ attn_row, const float* __restrict__ attn_col,
                     const float* __restrict__ emax, const float* __restrict__ esum,
                     const float* __restrict__ gpre, const float* __restrict__ glog,
-                    float slope, float p, uint64_t seed, float* __restrict__ grad_feat,
+                    float slope, float p, Seed seed_in, float* __restrict__ grad_feat,
                     float* __restrict__ grad_attn_col, float* __restrict__ pfeat,
                     float* __restrict__ pcol) {
+  const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const int lig = threadIdx.x % LPR;
@@ -743,8 +747,9 @@ gat_bwd_cols_combine_kernel(int H, int64_t C, const int* __restrict__ hub_col,
 }
 
 // ------------------------------------------------------------ misc kernels
-__global__ void gat_mask_kernel(int64_t total, float p, uint64_t seed,
+__global__ void gat_mask_kernel(int64_t total, float p, Seed seed_in,
                                 uint8_t* __restrict__ mask) {
+  const uint64_t seed = seed_in;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += stride)
@@ -843,9 +848,10 @@ gat_fwd_ring_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
                     const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
                     const float* __restrict__ attn_row, const float* __restrict__ attn_col,
                     const float* __restrict__ x, const float* __restrict__ bias, float slope,
-                    float p, uint64_t seed, float* __restrict__ out, float* __restrict__ pre,
+                    float p, Seed seed_in, float* __restrict__ out, float* __restrict__ pre,
                     float* __restrict__ emax, float* __restrict__ esum,
                     float* __restrict__ partial, int* __restrict__ counter) {
+  const uint64_t seed = seed_in;
   extern __shared__ float4 smem4[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int slot_f4 = H * 32;  // one 128-channel tile of every head
@@ -948,9 +954,10 @@ gat_bwd_rows_ring_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr
                          const float* __restrict__ attn_col, const float* __restrict__ x,
                          const float* __restrict__ pre, const float* __restrict__ emax,
                          const float* __restrict__ esum, const float* __restrict__ grad_y,
-                         float slope, float p, uint64_t seed, float* __restrict__ gpre,
+                         float slope, float p, Seed seed_in, float* __restrict__ gpre,
                          float* __restrict__ glog, float* __restrict__ grad_attn_row,
                          int* __restrict__ counter) {
+  const uint64_t seed = seed_in;
   extern __shared__ float4 smem4[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int slot_f4 = H * 32;
@@ -1062,9 +1069,10 @@ gat_bwd_cols_ring_kernel(int n, int H, int64_t C, const int* __restrict__ colptr
                          const float* __restrict__ attn_row, const float* __restrict__ attn_col,
                          const float* __restrict__ emax, const float* __restrict__ esum,
                          const float* __restrict__ gpre, const float* __restrict__ glog,
-                         float slope, float p, uint64_t seed, float* __restrict__ grad_feat,
+                         float slope, float p, Seed seed_in, float* __restrict__ grad_feat,
                          float* __restrict__ grad_attn_col, float* __restrict__ pfeat,
                          float* __restrict__ pcol, int* __restrict__ counter) {
+  const uint64_t seed = seed_in;
   constexpr int VPL = 2;
   extern __shared__ float4 smem4[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1231,7 +1239,7 @@ int launch_fwd_combine(const cign_gat_plan* pl, int H, int64_t C, const float* p
 
 int launch_bwd_hub_rows(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                         const float* attn_col, const float* pre, const float* emax,
-                        const float* esum, const float* gy, float slope, float p, uint64_t seed,
+                        const float* esum, const float* gy, float slope, float p, Seed seed,
                         float* gpre, float* glog, float* grow, cudaStream_t s) {
   const SegList& sl = pl->rows;
   if (sl.n_heavy == 0) return CIGN_OK;
@@ -1271,7 +1279,7 @@ int launch_seg_combine(const SegList& sl, int H, int64_t C, const float* pfeat, 
 
 int launch_fwd_ring(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                     const float* attn_col, const float* x, const float* bias, float slope,
-                    float p, uint64_t seed, float* out, float* pre, float* emax, float* esum,
+                    float p, Seed seed, float* out, float* pre, float* emax, float* esum,
                     float* partial, int* counter, cudaStream_t s) {
   const SegList& sl = pl->rows;
   {
@@ -1297,7 +1305,7 @@ int launch_fwd_ring(const cign_gat_plan* pl, int H, int64_t C, const float* attn
 int launch_bwd_rows_ring(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                          const float* attn_col, const float* x, const float* pre,
                          const float* emax, const float* esum, const float* gy, float slope,
-                         float p, uint64_t seed, float* gpre, float* glog, float* grow,
+                         float p, Seed seed, float* gpre, float* glog, float* grow,
                          int* counter, cudaStream_t s) {
   const SegList& sl = pl->rows;
   static thread_local int cache[64][kRingMaxH + 1] = {};
@@ -1324,7 +1332,7 @@ int launch_bwd_rows_ring(const cign_gat_plan* pl, int H, int64_t C, const float*
 int launch_bwd_cols_ring(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                          const float* attn_col, const float* emax, const float* esum,
                          const float* gpre, const float* glog, float slope, float p,
-                         uint64_t seed, float* gfeat, float* gcol, float* pfeat, float* pcol,
+                         Seed seed, float* gfeat, float* gcol, float* pfeat, float* pcol,
                          int* counter, cudaStream_t s) {
   const SegList& sl = pl->cols;
   static thread_local int cache[64] = {};
@@ -1433,9 +1441,10 @@ gat_fwd_tma_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
                    const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
                    const float* __restrict__ attn_row, const float* __restrict__ attn_col,
                    const float* __restrict__ x, const float* __restrict__ bias, float slope,
-                   float p, uint64_t seed, float* __restrict__ out, float* __restrict__ pre,
+                   float p, Seed seed_in, float* __restrict__ out, float* __restrict__ pre,
                    float* __restrict__ emax, float* __restrict__ esum,
                    float* __restrict__ partial, int stages, int* __restrict__ ctl) {
+  const uint64_t seed = seed_in;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t HC = static_cast<int64_t>(H) * C;
@@ -1532,9 +1541,10 @@ gat_bwd_rows_tma_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
                         const float* __restrict__ attn_col, const float* __restrict__ x,
                         const float* __restrict__ pre, const float* __restrict__ emax,
                         const float* __restrict__ esum, const float* __restrict__ grad_y,
-                        float slope, float p, uint64_t seed, float* __restrict__ gpre,
+                        float slope, float p, Seed seed_in, float* __restrict__ gpre,
                         float* __restrict__ glog, float* __restrict__ grad_attn_row,
                         int stages, int* __restrict__ ctl) {
+  const uint64_t seed = seed_in;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t HC = static_cast<int64_t>(H) * C;
@@ -1645,9 +1655,10 @@ gat_bwd_cols_tma_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
                         const float* __restrict__ attn_row, const float* __restrict__ attn_col,
                         const float* __restrict__ emax, const float* __restrict__ esum,
                         const float* __restrict__ gpre, const float* __restrict__ glog,
-                        float slope, float p, uint64_t seed, float* __restrict__ grad_feat,
+                        float slope, float p, Seed seed_in, float* __restrict__ grad_feat,
                         float* __restrict__ grad_attn_col, float* __restrict__ pfeat,
                         float* __restrict__ pcol, int stages, int* __restrict__ ctl) {
+  const uint64_t seed = seed_in;
   constexpr int HB = 4;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1762,7 +1773,7 @@ int tma_grid(K kernel, size_t smem, int* grid) {
 template <int VPL>
 int launch_fwd_tma_vpl(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                        const float* attn_col, const float* x, const float* bias, float slope,
-                       float p, uint64_t seed, float* out, float* pre, float* emax, float* esum,
+                       float p, Seed seed, float* out, float* pre, float* emax, float* esum,
                        float* partial, int* ctl, cudaStream_t s) {
   const SegList& sl = pl->rows;
   {
@@ -1789,7 +1800,7 @@ template <int VPL>
 int launch_bwd_rows_tma_vpl(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                             const float* attn_col, const float* x, const float* pre,
                             const float* emax, const float* esum, const float* gy, float slope,
-                            float p, uint64_t seed, float* gpre, float* glog, float* grow,
+                            float p, Seed seed, float* gpre, float* glog, float* grow,
                             int* ctl, cudaStream_t s) {
   const SegList& sl = pl->rows;
   const uint32_t slot_bytes = static_cast<uint32_t>(H * C * 4);
@@ -1817,7 +1828,7 @@ template <int VPL>
 int launch_bwd_cols_tma_vpl(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                             const float* attn_col, const float* emax, const float* esum,
                             const float* gpre, const float* glog, float slope, float p,
-                            uint64_t seed, float* gfeat, float* gcol, float* pfeat, float* pcol,
+                            Seed seed, float* gfeat, float* gcol, float* pfeat, float* pcol,
                             int* ctl, cudaStream_t s) {
   const SegList& sl = pl->cols;
   const uint32_t slot_bytes = static_cast<uint32_t>(C * 4);
@@ -1842,7 +1853,7 @@ size_t rnd(size_t b) { return (b + 255) / 256 * 256; }
 template <int VEC, int VPL, int LPR>
 int launch_fwd_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                    const float* attn_col, const float* x, const float* bias, float slope, float p,
-                   uint64_t seed, float* out, float* pre, float* emax, float* esum, float* partial,
+                   Seed seed, float* out, float* pre, float* emax, float* esum, float* partial,
                    cudaStream_t s) {
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const SegList& sl = pl->rows;
@@ -1865,7 +1876,7 @@ template <int VEC, int VPL, int LPR>
 int launch_bwd_rows_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                         const float* attn_col, const float* x, const float* pre,
                         const float* emax, const float* esum, const float* gy, float slope,
-                        float p, uint64_t seed, float* gpre, float* glog, float* grow,
+                        float p, Seed seed, float* gpre, float* glog, float* grow,
                         cudaStream_t s) {
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const SegList& sl = pl->rows;
@@ -1887,7 +1898,7 @@ int launch_bwd_rows_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* 
 template <int VEC, int VPL, int LPR, int HB>
 int launch_bwd_cols_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* attn_row,
                         const float* attn_col, const float* emax, const float* esum,
-                        const float* gpre, const float* glog, float slope, float p, uint64_t seed,
+                        const float* gpre, const float* glog, float slope, float p, Seed seed,
                         float* gfeat, float* gcol, float* pfeat, float* pcol, cudaStream_t s) {
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const SegList& sl = pl->cols;
@@ -1984,9 +1995,10 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
                int seg_blocks, const float* __restrict__ attn_row,
                const float* __restrict__ attn_col, float* __restrict__ emax,
                float* __restrict__ esum, const float* __restrict__ src, float slope, float p,
-               uint64_t seed, float* __restrict__ out, float* __restrict__ partial,
+               Seed seed_in, float* __restrict__ out, float* __restrict__ partial,
                const float* __restrict__ glog, float* __restrict__ gcol,
                float* __restrict__ pcol) {
+  const uint64_t seed = seed_in;
   using Cfg = AggCfg<VPL>;
   const int lane = threadIdx.x & 31;
   const int group = threadIdx.x >> 5;
@@ -2134,8 +2146,9 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
                     int seg_blocks, const float* __restrict__ attn_row,
                     const float* __restrict__ attn_col, const float* __restrict__ emax,
                     const float* __restrict__ esum, const float* __restrict__ U,
-                    const float* __restrict__ X, float slope, float p, uint64_t seed,
+                    const float* __restrict__ X, float slope, float p, Seed seed_in,
                     float* __restrict__ glog, float* __restrict__ grad_attn_row) {
+  const uint64_t seed = seed_in;
   constexpr int kChunk = 256;  // floats of D per pass: 2 float4 per lane
   const int lane = threadIdx.x & 31;
   const int group = threadIdx.x >> 5;
@@ -2232,7 +2245,7 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
 template <int VPL, int MODE>
 int launch_agg(const cign_gat_plan* pl, const SegList& sl, int H, int64_t D, const int* ptr,
                const int* idx, const int* perm, const float* attn_row, const float* attn_col,
-               float* emax, float* esum, const float* src, float slope, float p, uint64_t seed,
+               float* emax, float* esum, const float* src, float slope, float p, Seed seed,
                float* out, float* partial, const float* glog, float* gcol, float* pcol,
                cudaStream_t s) {
   using Cfg = AggCfg<VPL>;
@@ -2368,9 +2381,11 @@ size_t cign_gat_fwd_workspace_bytes(const cign_gat_plan* pl, int32_t heads, int3
 
 int cign_gat_fwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const float* attn_row,
                  const float* attn_col, const float* in_feat, const float* bias,
-                 float negative_slope, float attn_drop, uint64_t seed, float* out, float* pre,
+                 float negative_slope, float attn_drop, uint64_t seed_value, const uint64_t* seed_ptr,
+                 float* out, float* pre,
                  float* edge_max, float* edge_sum, void* ws, size_t ws_bytes,
                  cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   int rc = check_plan(pl, heads, channels, "gat_fwd");
   if (rc) return rc;
   CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
@@ -2412,9 +2427,11 @@ size_t cign_gat_bwd_workspace_bytes(const cign_gat_plan* pl, int32_t heads, int3
 int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const float* attn_row,
                  const float* attn_col, const float* in_feat, const float* pre,
                  const float* edge_max, const float* edge_sum, const float* grad_y,
-                 float negative_slope, float attn_drop, uint64_t seed, float* grad_feat,
+                 float negative_slope, float attn_drop, uint64_t seed_value, const uint64_t* seed_ptr,
+                 float* grad_feat,
                  float* grad_attn_row, float* grad_attn_col, float* grad_bias, void* ws,
                  size_t ws_bytes, cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   int rc = check_plan(pl, heads, channels, "gat_bwd");
   if (rc) return rc;
   CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
@@ -2479,8 +2496,9 @@ int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const
   return colsum_f32(gpre, pl->n, C, csum, grad_bias, s);
 }
 
-int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop, uint64_t seed,
+int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop, uint64_t seed_value, const uint64_t* seed_ptr,
                           uint8_t* mask, cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   CIGN_REQUIRE(nnz >= 0 && heads >= 1, CIGN_ERR_INVALID_ARGUMENT, "gat_dropout_mask: bad sizes");
   const int64_t total = nnz * heads;
   if (total == 0) return CIGN_OK;
@@ -2500,8 +2518,10 @@ size_t cign_gat_agg_workspace_bytes(const cign_gat_plan* pl, int32_t heads, int6
 
 int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const float* attn_row,
                      const float* attn_col, const float* x, float negative_slope, float attn_drop,
-                     uint64_t seed, float* z, float* edge_max, float* edge_sum, void* ws,
+                     uint64_t seed_value, const uint64_t* seed_ptr,
+                     float* z, float* edge_max, float* edge_sum, void* ws,
                      size_t ws_bytes, cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   int rc = check_agg(pl, heads, dim, {x, z, ws}, "gat_agg_fwd");
   if (rc) return rc;
   CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
@@ -2528,9 +2548,10 @@ int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const 
 int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_t channels,
                      const float* attn_row, const float* attn_col, const float* x,
                      const float* edge_max, const float* edge_sum, const float* grad_z,
-                     const float* grad_pre, float negative_slope, float attn_drop, uint64_t seed,
+                     const float* grad_pre, float negative_slope, float attn_drop, uint64_t seed_value, const uint64_t* seed_ptr,
                      float* grad_feat, float* grad_attn_row, float* grad_attn_col, void* ws,
                      size_t ws_bytes, cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
   int rc = check_agg(pl, heads, dim, {x, grad_z, ws}, "gat_agg_bwd");
   if (rc) return rc;
   rc = check_agg(pl, heads, channels, {grad_pre, grad_feat}, "gat_agg_bwd");

@@ -17,16 +17,13 @@ natively; the reference's generic kernels stop at D = 256 (:104).
 """
 from __future__ import annotations
 
-import itertools
-
 import torch
 
-from . import _lib
+from . import _lib, seeds
 
 _EXT = None
 _EXT_ERROR = None
-_CALL_COUNTER = itertools.count()
-_MASK63 = (1 << 63) - 1
+_CALL_COUNTER = seeds.counter_iter(seeds.BLOCK)  # block-op call ids (shared with seeds.next_seed)
 MAX_D = 1024
 
 
@@ -50,12 +47,10 @@ def ensure_fused_block_ops_loaded(verbose: bool = False):
     return _EXT
 
 
-def _next_seed(tag: int, dropout_p: float) -> int:
-    if float(dropout_p) <= 0.0:
-        return 0
-    base = int(torch.initial_seed()) & _MASK63
-    call = next(_CALL_COUNTER) + 1
-    return (base + 0x9E3779B97F4A7C15 * call + 0xD2B74407B1CE6E93 * int(tag)) & _MASK63
+def _next_seed(tag: int, dropout_p: float):
+    """Seed of the next block-op call: an int, or a device seed slot while a
+    seeds.DeviceSeedTable records."""
+    return seeds.next_seed(seeds.BLOCK, dropout_p, tag)
 
 
 # ------------------------------------------------------------------ raw ops
@@ -67,8 +62,8 @@ def dropout_ln_forward(x, w, b, p, eps, seed):
     rstd = torch.empty_like(mean)
     with _lib.DeviceGuard(x.device):
         rc = lib.cign_dropout_ln_fwd(n, D, _lib.ptr(x), _lib.ptr(w), _lib.ptr(b), float(p), float(eps),
-                                     int(seed), _lib.ptr(y), _lib.ptr(mean), _lib.ptr(rstd),
-                                     _lib.stream_of(x))
+                                     *_lib.seed_args(seed), _lib.ptr(y), _lib.ptr(mean),
+                                     _lib.ptr(rstd), _lib.stream_of(x))
     _lib.check(rc, "cign_dropout_ln_fwd")
     return y, mean, rstd
 
@@ -82,8 +77,9 @@ def dropout_ln_backward(gy, x, w, mean, rstd, p, seed):
     ws = _lib.workspace(lib.cign_ln_bwd_workspace_bytes(n, D), x.device)
     with _lib.DeviceGuard(x.device):
         rc = lib.cign_dropout_ln_bwd(n, D, _lib.ptr(gy), _lib.ptr(x), _lib.ptr(w), _lib.ptr(mean),
-                                     _lib.ptr(rstd), float(p), int(seed), _lib.ptr(gx), _lib.ptr(gw),
-                                     _lib.ptr(gb), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+                                     _lib.ptr(rstd), float(p), *_lib.seed_args(seed), _lib.ptr(gx),
+                                     _lib.ptr(gw), _lib.ptr(gb), _lib.ptr(ws), ws.numel(),
+                                     _lib.stream_of(x))
     _lib.check(rc, "cign_dropout_ln_bwd")
     return gx, gw, gb
 
@@ -123,7 +119,7 @@ def gamma_residual_forward(h, g, gamma, p, seed):
     y = torch.empty_like(h)
     with _lib.DeviceGuard(h.device):
         rc = lib.cign_gamma_residual_fwd(n, D, _lib.ptr(h), _lib.ptr(g), _lib.ptr(gamma), float(p),
-                                         int(seed), _lib.ptr(y), _lib.stream_of(h))
+                                         *_lib.seed_args(seed), _lib.ptr(y), _lib.stream_of(h))
     _lib.check(rc, "cign_gamma_residual_fwd")
     return y
 
@@ -136,8 +132,8 @@ def gamma_residual_backward(gy, g, gamma, p, seed):
     ws = _lib.workspace(lib.cign_gamma_residual_bwd_workspace_bytes(n, D), g.device)
     with _lib.DeviceGuard(g.device):
         rc = lib.cign_gamma_residual_bwd(n, D, _lib.ptr(gy), _lib.ptr(g), _lib.ptr(gamma), float(p),
-                                         int(seed), _lib.ptr(gg), _lib.ptr(ggamma), _lib.ptr(ws),
-                                         ws.numel(), _lib.stream_of(g))
+                                         *_lib.seed_args(seed), _lib.ptr(gg), _lib.ptr(ggamma),
+                                         _lib.ptr(ws), ws.numel(), _lib.stream_of(g))
     _lib.check(rc, "cign_gamma_residual_bwd")
     return gg, ggamma
 
@@ -147,8 +143,8 @@ def block_dropout_mask(count: int, p: float, seed: int, device) -> torch.Tensor:
     lib = ensure_fused_block_ops_loaded()
     mask = torch.empty((int(count),), dtype=torch.uint8, device=device)
     with _lib.DeviceGuard(device):
-        rc = lib.cign_block_dropout_mask(int(count), float(p), int(seed), _lib.ptr(mask),
-                                         _lib.stream_on(device))
+        rc = lib.cign_block_dropout_mask(int(count), float(p), *_lib.seed_args(seed),
+                                         _lib.ptr(mask), _lib.stream_on(device))
     _lib.check(rc, "cign_block_dropout_mask")
     return mask
 
@@ -162,7 +158,7 @@ class _DropoutLayerNormFn(torch.autograd.Function):
         y, mean, rstd = dropout_ln_forward(x, weight, bias.contiguous(), dropout_p, eps, seed)
         ctx.save_for_backward(x, weight, mean, rstd)
         ctx.dropout_p = float(dropout_p)
-        ctx.seed = int(seed)
+        ctx.seed = seed
         return y
 
     @staticmethod
@@ -198,7 +194,7 @@ class _DropoutGammaResidualFn(torch.autograd.Function):
         y = gamma_residual_forward(h.contiguous(), g, gamma, dropout_p, seed)
         ctx.save_for_backward(g, gamma)
         ctx.dropout_p = float(dropout_p)
-        ctx.seed = int(seed)
+        ctx.seed = seed
         return y
 
     @staticmethod

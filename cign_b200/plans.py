@@ -26,20 +26,24 @@ class HopTimer:
     launching stream around every cign_multihop_fwd / _bwd call while the
     timer is installed (``SpmmPlan.hop_timer = HopTimer()``).  ``records`` holds
     (kind, n_hops, n_addend_hops, F, start, end); read them after a
-    synchronize."""
+    synchronize.  Inside a CUDA-graph capture the events become event-record
+    nodes of the graph, so after a replay they hold that replay's times."""
 
     def __init__(self):
         self.records = []
 
-    def begin(self, stream):
-        ev = torch.cuda.Event(enable_timing=True)
+    @staticmethod
+    def _event(stream):
+        ev = torch.cuda.Event(enable_timing=True,
+                              external=torch.cuda.is_current_stream_capturing())
         ev.record(stream)
         return ev
 
+    def begin(self, stream):
+        return self._event(stream)
+
     def end(self, stream, start, kind, n_hops, n_addend, F):
-        ev = torch.cuda.Event(enable_timing=True)
-        ev.record(stream)
-        self.records.append((kind, n_hops, n_addend, F, start, ev))
+        self.records.append((kind, n_hops, n_addend, F, start, self._event(stream)))
 
 
 class SpmmPlan:

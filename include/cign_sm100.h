@@ -17,6 +17,10 @@
  *     sized by the matching *_workspace_bytes() query.
  *   - Reductions are deterministic: repeated calls on the same inputs give
  *     bitwise identical outputs (no floating-point atomics).
+ *   - Dropout entry points take `uint64_t seed, const uint64_t* seed_ptr`:
+ *     with seed_ptr == NULL the seed is `seed`; otherwise it is the value at
+ *     the device address seed_ptr when the kernel runs (so a captured CUDA
+ *     graph can draw a fresh seed on every replay).
  *
  * Each entry point names the reference interface it replaces
  * (rabbit-art/CIGN, path within that project:line).
@@ -177,7 +181,8 @@ CIGN_API size_t cign_gat_fwd_workspace_bytes(const cign_gat_plan* plan, int32_t 
 CIGN_API int cign_gat_fwd(const cign_gat_plan* plan, int32_t heads, int32_t channels,
                  const float* attn_row, const float* attn_col,
                  const float* in_feat, const float* bias, float negative_slope,
-                 float attn_drop, uint64_t seed, float* out, float* pre,
+                 float attn_drop, uint64_t seed,
+                              const uint64_t* seed_ptr, float* out, float* pre,
                  float* edge_max, float* edge_sum, void* ws, size_t ws_bytes,
                  cign_stream_t stream);
 
@@ -193,6 +198,7 @@ CIGN_API int cign_gat_bwd(const cign_gat_plan* plan, int32_t heads, int32_t chan
                  const float* in_feat, const float* pre, const float* edge_max,
                  const float* edge_sum, const float* grad_y,
                  float negative_slope, float attn_drop, uint64_t seed,
+                              const uint64_t* seed_ptr,
                  float* grad_feat, float* grad_attn_row, float* grad_attn_col,
                  float* grad_bias, void* ws, size_t ws_bytes,
                  cign_stream_t stream);
@@ -201,7 +207,8 @@ CIGN_API int cign_gat_bwd(const cign_gat_plan* plan, int32_t heads, int32_t chan
  * as make_dropout_mask_kernel (collapsed_gat_cuda.cu:34-47) does.  The
  * forward/backward never need it; it exists for parity checks. */
 CIGN_API int cign_gat_dropout_mask(int64_t nnz, int32_t heads, float attn_drop,
-                          uint64_t seed, uint8_t* mask, cign_stream_t stream);
+                          uint64_t seed,
+                              const uint64_t* seed_ptr, uint8_t* mask, cign_stream_t stream);
 
 /* Aggregate-first form of the same layer.  GATConv's lin is linear, so with
  * in_feat[j,h,:] = W_h x[j,:] (W = lin.weight viewed [H, C, D]):
@@ -223,14 +230,16 @@ CIGN_API size_t cign_gat_agg_workspace_bytes(const cign_gat_plan* plan, int32_t 
                                              int64_t dim, int64_t channels);
 CIGN_API int cign_gat_agg_fwd(const cign_gat_plan* plan, int32_t heads, int64_t dim,
                               const float* attn_row, const float* attn_col, const float* x,
-                              float negative_slope, float attn_drop, uint64_t seed, float* z,
+                              float negative_slope, float attn_drop, uint64_t seed,
+                              const uint64_t* seed_ptr, float* z,
                               float* edge_max, float* edge_sum, void* ws, size_t ws_bytes,
                               cign_stream_t stream);
 CIGN_API int cign_gat_agg_bwd(const cign_gat_plan* plan, int32_t heads, int64_t dim,
                               int64_t channels, const float* attn_row, const float* attn_col,
                               const float* x, const float* edge_max, const float* edge_sum,
                               const float* grad_z, const float* grad_pre, float negative_slope,
-                              float attn_drop, uint64_t seed, float* grad_feat,
+                              float attn_drop, uint64_t seed,
+                              const uint64_t* seed_ptr, float* grad_feat,
                               float* grad_attn_row, float* grad_attn_col, void* ws,
                               size_t ws_bytes, cign_stream_t stream);
 
@@ -305,6 +314,20 @@ CIGN_API int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
                   int32_t accumulate_p, float* grad_alpha,
                   cign_stream_t stream);
 
+/* ------------------------------------------------------------ seed table
+ * Device-side dropout seed streams for CUDA-graph training steps.  For slot
+ * i < n_slots with layout[3i..3i+2] = (kind, tag, offset):
+ *   kind 0 (GAT):   table[i] = (base + 0x9E3779B97F4A7C15 * (counters[0] + offset + 1)) mod 2^63
+ *   kind 1 (block): table[i] = (base + 0x9E3779B97F4A7C15 * (counters[1] + offset + 1)
+ *                               + 0xD2B74407B1CE6E93 * tag) mod 2^63
+ * then counters[0] += n_gat, counters[1] += n_block -- the per-call seeds of
+ * collapsed_gat.py:201-211 and fused_block_ops.py:46-50 with the call
+ * counters kept on the device.  layout, counters (int64 [2]) and table
+ * (uint64 [n_slots]) are device arrays; n_slots <= 4096. */
+CIGN_API int cign_seed_table_step(uint64_t base, int32_t n_slots, const int32_t* layout,
+                                  int64_t* counters, int32_t n_gat, int32_t n_block,
+                                  uint64_t* table, cign_stream_t stream);
+
 /* ------------------------------------------------------------ hop gate
  * alpha [N,K] = softmax_k(g @ W^T + b) with g = [H + C | |H - C|] (mode 1,
  * alpha_score_mode "new") or [H | C] (mode 0, "old"); H, C [N,D], W [K,2D],
@@ -333,6 +356,7 @@ CIGN_API int cign_hop_gate_bwd(int64_t n, int64_t d, int32_t k, int32_t mode, co
  * fused_block_ops_cuda.cu:45-322 without their D<=256 limit. */
 CIGN_API int cign_dropout_ln_fwd(int64_t n, int64_t d, const float* x, const float* w,
                         const float* b, float p, float eps, uint64_t seed,
+                              const uint64_t* seed_ptr,
                         float* y, float* mean, float* rstd,
                         cign_stream_t stream);
 
@@ -341,6 +365,7 @@ CIGN_API size_t cign_ln_bwd_workspace_bytes(int64_t n, int64_t d);
 CIGN_API int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y,
                         const float* x, const float* w, const float* mean,
                         const float* rstd, float p, uint64_t seed,
+                              const uint64_t* seed_ptr,
                         float* grad_x, float* grad_w, float* grad_b, void* ws,
                         size_t ws_bytes, cign_stream_t stream);
 
@@ -378,7 +403,8 @@ CIGN_API int cign_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const fl
 /* y = h + gamma * dropout(g). */
 CIGN_API int cign_gamma_residual_fwd(int64_t n, int64_t d, const float* h,
                             const float* g, const float* gamma, float p,
-                            uint64_t seed, float* y, cign_stream_t stream);
+                            uint64_t seed,
+                              const uint64_t* seed_ptr, float* y, cign_stream_t stream);
 
 CIGN_API size_t cign_gamma_residual_bwd_workspace_bytes(int64_t n, int64_t d);
 
@@ -386,12 +412,14 @@ CIGN_API size_t cign_gamma_residual_bwd_workspace_bytes(int64_t n, int64_t d);
  * (grad_h = grad_y is returned by the caller without a kernel.) */
 CIGN_API int cign_gamma_residual_bwd(int64_t n, int64_t d, const float* grad_y,
                             const float* g, const float* gamma, float p,
-                            uint64_t seed, float* grad_g, float* grad_gamma,
+                            uint64_t seed,
+                              const uint64_t* seed_ptr, float* grad_g, float* grad_gamma,
                             void* ws, size_t ws_bytes, cign_stream_t stream);
 
 /* Materialise the block-op dropout keep-mask (uint8 [count]) for indices
  * 0..count-1, for parity checks only. */
 CIGN_API int cign_block_dropout_mask(int64_t count, float p, uint64_t seed,
+                              const uint64_t* seed_ptr,
                             uint8_t* mask, cign_stream_t stream);
 
 #ifdef __cplusplus

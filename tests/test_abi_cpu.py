@@ -44,13 +44,13 @@ def test_invalid_arguments_rejected_before_launch():
     assert lib.cign_pack_fwd(4, 8, 2, 7, 0, 0, None, None, None, 16, None, None, None) == 1
     # dropout probability out of range
     assert lib.cign_dropout_ln_fwd(4, 8, None, None, None, 1.5, 1e-5, 0, None, None, None,
-                                   None) == 1
+                                   None, None) == 1
     # D above the register-resident limit
     assert lib.cign_add_ln_fwd(4, 4096, None, None, None, None, 1e-5, None, None, None,
                                None) == 6
     # GAT heads above the supported range
     assert lib.cign_gat_fwd(ctypes.c_void_p(1), 65, 8, None, None, None, None, 0.2, 0.0, 0, None,
-                            None, None, None, None, 0, None) == 6
+                            None, None, None, None, None, 0, None) == 6
     assert "heads" in _lib.last_error()
 
 

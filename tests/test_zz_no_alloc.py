@@ -37,7 +37,8 @@ def _workspace_version(lib, n, d, x, w, gy, mean, rstd, p, seed, stream):
     ws = torch.empty(max(int(lib.cign_ln_bwd_workspace_bytes(n, d)), 16), dtype=torch.uint8,
                      device=x.device)
     rc = lib.cign_dropout_ln_bwd(n, d, _lib.ptr(gy), _lib.ptr(x), _lib.ptr(w), _lib.ptr(mean),
-                                 _lib.ptr(rstd), p, seed, _lib.ptr(gx), _lib.ptr(gw), _lib.ptr(gb),
+                                 _lib.ptr(rstd), p, seed, None, _lib.ptr(gx), _lib.ptr(gw),
+                                 _lib.ptr(gb),
                                  _lib.ptr(ws), ws.numel(), stream)
     _lib.check(rc, "cign_dropout_ln_bwd")
     return gx, gw, gb
