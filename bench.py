@@ -283,6 +283,133 @@ def hop_roofline(timer, N, nnz, peak, peak_kind):
             "timing": "CUDA events around every k-hop call in the timed steps, on the launching stream"}
 
 
+# ------------------------------------------------------- partitioned (N > 1)
+def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
+    """Weak scaling: a power-law graph of world x cfg2 size (same generator,
+    degree law and per-node widths) is row-partitioned over the ranks, so
+    each rank trains a cfg2-sized row range; halo rows move over NCCL once
+    per hop and per GAT layer; parameter gradients are summed with one
+    all-reduce per step."""
+    from dataclasses import replace
+
+    import torch.distributed as dist
+
+    from cign_b200 import _lib, synth
+    from cign_b200.distributed import allreduce_gradients, partition_graph
+    from cign_b200.graph_operator import (build_sparse_normalized_adjacency,
+                                          prepare_fixed_csr_operator, prepare_gat_edge_index,
+                                          to_graph_format)
+    from cign_b200.model_cign import build_model
+
+    torch.backends.cuda.matmul.allow_tf32 = True
+    lib = _lib.load_library()
+    gcfg = replace(cfg, name=f"{cfg.name}_x{world}", num_nodes=cfg.num_nodes * world,
+                   num_edges=cfg.num_edges * world)
+    n = gcfg.num_nodes
+    edge = synth.make_edges(gcfg).to(device)
+    ei, adj = build_sparse_normalized_adjacency(edge, n)
+    base = prepare_fixed_csr_operator(adj)
+    (rp, c), _, _ = to_graph_format(prepare_gat_edge_index(ei, n).flip(0), n)
+    bounds, hplan, exch, dop, dgat = partition_graph(base.csr, rp, c, world, rank, device)
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    nnz = int(base.nnz)
+    x_all, y_all, train_all, _, _ = synth.make_features(gcfg)
+    torch.manual_seed(0)  # identical parameters on every rank
+    model = build_model(in_dim=cfg.in_dim, hidden_dim=cfg.hidden_dim, out_dim=cfg.num_classes,
+                        num_layers=cfg.layers, dropout=cfg.dropout, hop_scales=cfg.hops,
+                        gat_heads=cfg.heads, gat_dropout=cfg.gat_dropout).to(device)
+    model.prepare_fused_gat_graph(dgat)
+    torch.manual_seed(1000 + rank)  # independent dropout streams per rank
+    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5)
+    x_cpu = x_all[r0:r1].contiguous()
+    x = x_cpu.to(device)
+    y = y_all[r0:r1].to(device)
+    train_global = int(train_all.sum())
+    mine = train_all[r0:r1].nonzero().squeeze(1).to(device)
+    edge_passes = 2 * cfg.layers * len(cfg.hops) * nnz  # whole graph, all ranks
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    params = list(model.parameters())
+
+    def step(xin):
+        opt.zero_grad(set_to_none=True)
+        logits = model(xin, dop)
+        loss = F.cross_entropy(logits.index_select(0, mine), y.index_select(0, mine),
+                               reduction="sum") / train_global
+        loss.backward()
+        allreduce_gradients(params)
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    launches_before = int(lib.cign_kernel_launches())
+    stream = torch.cuda.current_stream(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step(x)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    launches = int(lib.cign_kernel_launches()) - launches_before
+    total_s = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) * 1e-3
+    t = torch.tensor([total_s], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_s = float(t.item())
+
+    x_pin = x_cpu.pin_memory()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        x.copy_(x_pin, non_blocking=True)
+        loss_host = float(step(x).item())
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) * 1e-3], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_s = float(t.item())
+    halo = torch.tensor([hplan.n_halo], device=device, dtype=torch.float64)
+    dist.all_reduce(halo)
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        result = {
+            "metric": metric,
+            "value": round(edge_passes * args.steps / total_s / 1e9, 4), "unit": "GTEPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_s / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": gcfg.name, "nodes": n, "directed_edges": gcfg.num_edges,
+                       "nnz_P": nnz, "nodes_per_gpu": n // world, "in_dim": cfg.in_dim,
+                       "hidden": cfg.hidden_dim, "hops": list(cfg.hops), "heads": cfg.heads,
+                       "layers": cfg.layers, "dropout": cfg.dropout,
+                       "parallelism": f"row-partition x{world}",
+                       "exchange": "NCCL P2P halo rows per hop and per GAT layer; one "
+                                   "gradient all-reduce per step",
+                       "halo_rows_total": int(halo.item()),
+                       "l2": "flushed between timed steps (256 MiB write)", "launch": "eager"},
+            "e2e": {"value": round(edge_passes * args.steps / e2e_s / 1e9, 4), "unit": "GTEPS",
+                    "h2d_bytes_per_step": int(x_cpu.numel() * 4), "d2h_bytes_per_step": 4,
+                    "ms_per_step": round(e2e_s / args.steps * 1e3, 4)},
+            "gpu_launches": launches,
+            "roofline": None, "cpu_baseline": None, "clocks": clocks,
+            "peak_hbm_gbs": peak, "peak_kind": peak_kind,
+            "final_loss": round(loss_host, 5),
+        }
+        print(json.dumps(result), flush=True)
+    dist.barrier()
+    return 0
+
+
 # ------------------------------------------------------------------ CPU arm
 def cpu_sample_config(cfg, sample_nodes):
     from dataclasses import replace
@@ -396,6 +523,10 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
+        try:
+            return run_partitioned(args, cfg, metric, world, rank, local_rank, device)
+        finally:
+            dist.destroy_process_group()
     torch.backends.cuda.matmul.allow_tf32 = True
     torch.backends.cudnn.allow_tf32 = True
 

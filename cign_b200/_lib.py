@@ -78,6 +78,8 @@ SIGNATURES = {
     "cign_multihop_fwd": (c_int, [_P, c_int, _P, c_int64, _PP, _P, c_size_t, _P]),
     "cign_multihop_bwd": (c_int, [_P, c_int, _PP, c_int64, _P, _P, c_size_t, _P]),
     "cign_gat_plan_create": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, POINTER(c_void_p)]),
+    "cign_gat_plan_create_rect": (c_int, [c_int64, c_int64, c_int64, _P, _P, _P, _P, _P,
+                                          POINTER(c_void_p)]),
     "cign_gat_plan_destroy": (c_int, [_P]),
     "cign_gat_plan_get_info": (c_int, [_P, POINTER(c_int64)]),
     "cign_gat_fwd_workspace_bytes": (c_size_t, [_P, c_int32, c_int32]),

@@ -176,7 +176,8 @@ def collapsed_gat_mean_bias_silu(
 def gat_agg_forward_raw(plan, attn_row, attn_col, x, heads, negative_slope, attn_drop, seed):
     """z [N,H,D] = per-head attention-weighted sums of x rows; returns (z, emax, esum)."""
     lib = ensure_collapsed_gat_loaded()
-    n, D = (int(s) for s in x.shape)
+    D = int(x.size(1))
+    n = int(plan.n)  # destination rows (x has plan.n_cols rows)
     H = int(heads)
     z = torch.empty((n, H, D), dtype=torch.float32, device=x.device)
     emax = torch.empty((n, H), dtype=torch.float32, device=x.device)
@@ -195,13 +196,14 @@ def gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z, grad_p
                          attn_drop, seed):
     """Returns (grad_feat [N,H,C], grad_attn_row [N,H], grad_attn_col [N,H])."""
     lib = ensure_collapsed_gat_loaded()
-    n, D = (int(s) for s in x.shape)
+    n_cols, D = (int(s) for s in x.shape)
+    n = int(plan.n)
     H = int(emax.size(1))
     C = int(grad_pre.size(1))
     dev = x.device
-    gfeat = torch.empty((n, H, C), dtype=torch.float32, device=dev)
+    gfeat = torch.empty((n_cols, H, C), dtype=torch.float32, device=dev)
     grow = torch.empty((n, H), dtype=torch.float32, device=dev)
-    gcol = torch.empty_like(grow)
+    gcol = torch.empty((n_cols, H), dtype=torch.float32, device=dev)
     ws = _lib.workspace(lib.cign_gat_agg_workspace_bytes(plan.handle, H, D, C), dev)
     with _lib.DeviceGuard(dev):
         rc = lib.cign_gat_agg_bwd(plan.handle, H, D, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
@@ -229,7 +231,7 @@ class _AggregateFirstGATFn(torch.autograd.Function):
     def forward(ctx, x, attn_row, attn_col, weight, bias, plan, heads, negative_slope, attn_drop,
                 seed):
         H = int(heads)
-        n, D = x.shape
+        n, D = int(plan.n), int(x.size(1))
         z, emax, esum = gat_agg_forward_raw(plan, attn_row, attn_col, x, H, negative_slope,
                                             attn_drop, seed)
         M = _head_projection(weight, H)
@@ -243,7 +245,8 @@ class _AggregateFirstGATFn(torch.autograd.Function):
     def backward(ctx, grad_out):
         x, attn_row, attn_col, weight, z, pre, emax, esum = ctx.saved_tensors
         H = ctx.heads
-        n, D = x.shape
+        n, D = int(z.size(0)), int(x.size(1))
+        n_cols = int(x.size(0))
         C = weight.size(0) // H
         g_pre = torch.ops.aten.silu_backward(grad_out.contiguous(), pre)
         grad_bias = g_pre.sum(0)
@@ -255,7 +258,7 @@ class _AggregateFirstGATFn(torch.autograd.Function):
         gfeat, grow, gcol = gat_agg_backward_raw(ctx.plan, attn_row, attn_col, x, emax, esum,
                                                  grad_z, g_pre, ctx.negative_slope,
                                                  ctx.attn_drop, ctx.seed)
-        grad_x = gfeat.view(n, H * C).mm(weight)                    # [N, D]
+        grad_x = gfeat.view(n_cols, H * C).mm(weight)               # [N_cols, D]
         return grad_x, grow, gcol, grad_w, grad_bias, None, None, None, None, None
 
 
@@ -278,8 +281,9 @@ def collapsed_gat_aggregate_first(x: torch.Tensor, attn_row: torch.Tensor, attn_
         raise ValueError("attn_drop must be in [0,1)")
     (rowptr, col), (row, colptr) = csr, csc
     plan = gat_plan_for(rowptr, col, row, colptr, perm)
-    if plan.n != x.size(0):
-        raise RuntimeError(f"graph has {plan.n} rows but x has {x.size(0)}")
+    if plan.n_cols != x.size(0) or attn_row.size(0) != plan.n or attn_col.size(0) != plan.n_cols:
+        raise RuntimeError(f"graph is {plan.n} x {plan.n_cols} but x has {x.size(0)} rows, "
+                           f"attn_row {attn_row.size(0)}, attn_col {attn_col.size(0)}")
     seed = gat_call_seed(attn_drop)
     return _AggregateFirstGATFn.apply(x.contiguous(), attn_row.contiguous(), attn_col.contiguous(),
                                       weight, bias, plan, H, float(negative_slope),

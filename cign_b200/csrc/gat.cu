@@ -43,7 +43,8 @@
 #include "common.cuh"
 
 struct cign_gat_plan {
-  int64_t n;
+  int64_t n;       // destination rows (CSR rows)
+  int64_t n_cols;  // source columns (CSC columns); == n for a square graph
   int64_t nnz;
   const int32_t* rowptr;
   const int32_t* col;
@@ -756,19 +757,20 @@ __global__ void gat_mask_kernel(int64_t total, float p, Seed seed_in,
     mask[i] = gat_keep(seed, static_cast<uint64_t>(i), p) ? 1 : 0;
 }
 
-__global__ void gat_validate_kernel(int64_t n, int64_t nnz, const int* __restrict__ rowptr,
+__global__ void gat_validate_kernel(int64_t n, int64_t n_cols, int64_t nnz,
+                                    const int* __restrict__ rowptr,
                                     const int* __restrict__ col, const int* __restrict__ colptr,
                                     const int* __restrict__ row, const int* __restrict__ perm,
                                     int* __restrict__ bad) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (int64_t i = t0; i < n; i += stride) {
+  for (int64_t i = t0; i < n; i += stride)
     if (rowptr[i] > rowptr[i + 1]) atomicOr(bad, 1);
+  for (int64_t i = t0; i < n_cols; i += stride)
     if (colptr[i] > colptr[i + 1]) atomicOr(bad, 2);
-  }
   for (int64_t e = t0; e < nnz; e += stride) {
     const int c = col[e];
-    if (c < 0 || c >= n) atomicOr(bad, 4);
+    if (c < 0 || c >= n_cols) atomicOr(bad, 4);
     const int r = row[e];
     if (r < 0 || r >= n) { atomicOr(bad, 8); continue; }
     const int pe = perm[e];
@@ -777,7 +779,7 @@ __global__ void gat_validate_kernel(int64_t n, int64_t nnz, const int* __restric
     if (pe < rowptr[r] || pe >= rowptr[r + 1]) atomicOr(bad, 32);
   }
   // CSC position pos of column j must map to a CSR edge whose column is j.
-  for (int64_t j = t0; j < n; j += stride) {
+  for (int64_t j = t0; j < n_cols; j += stride) {
     const int lo = max(colptr[j], 0);
     const int hi = min(static_cast<int64_t>(colptr[j + 1]), nnz);
     for (int pos = lo; pos < hi; ++pos) {
@@ -787,7 +789,7 @@ __global__ void gat_validate_kernel(int64_t n, int64_t nnz, const int* __restric
   }
   if (t0 == 0) {
     if (rowptr[0] != 0 || rowptr[n] != nnz) atomicOr(bad, 128);
-    if (colptr[0] != 0 || colptr[n] != nnz) atomicOr(bad, 256);
+    if (colptr[0] != 0 || colptr[n_cols] != nnz) atomicOr(bad, 256);
   }
 }
 
@@ -1344,7 +1346,7 @@ int launch_bwd_cols_ring(const cign_gat_plan* pl, int H, int64_t C, const float*
   if (rc) return rc;
   CIGN_CHECK_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), s), "gat: reset counter");
   kernel<<<cache[dev & 63], kRingThreads, smem, s>>>(
-      static_cast<int>(pl->n), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
+      static_cast<int>(pl->n_cols), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
       sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, emax, esum, gpre, glog, slope,
       p, seed, gfeat, gcol, pfeat, pcol, counter);
   CIGN_CHECK_LAUNCH("gat_bwd_cols_ring_kernel");
@@ -1840,7 +1842,7 @@ int launch_bwd_cols_tma_vpl(const cign_gat_plan* pl, int H, int64_t C, const flo
   if (rc) return rc;
   CIGN_CHECK_CUDA(cudaMemsetAsync(ctl, 0, 2 * sizeof(int), s), "gat: reset control");
   kernel<<<grid, kTmaWarps * 32, smem, s>>>(
-      static_cast<int>(pl->n), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
+      static_cast<int>(pl->n_cols), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
       sl.seg_end(), static_cast<int>(sl.n_seg), attn_row, attn_col, emax, esum, gpre, glog, slope,
       p, seed, gfeat, gcol, pfeat, pcol, stages, ctl);
   CIGN_CHECK_LAUNCH("gat_bwd_cols_tma_kernel");
@@ -1903,9 +1905,9 @@ int launch_bwd_cols_cfg(const cign_gat_plan* pl, int H, int64_t C, const float* 
   using Cfg = GatCfg<VEC, VPL, LPR>;
   const SegList& sl = pl->cols;
   const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
-  const int64_t grid = seg_blocks + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = seg_blocks + (pl->n_cols + Cfg::kGroups - 1) / Cfg::kGroups;
   gat_bwd_cols_kernel<VEC, VPL, LPR, HB><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
-      static_cast<int>(pl->n), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
+      static_cast<int>(pl->n_cols), H, C, pl->colptr, pl->row, pl->perm, sl.seg_row(), sl.seg_begin(),
       sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
       emax, esum, gpre, glog, slope, p, seed, gfeat, gcol, pfeat, pcol);
   CIGN_CHECK_LAUNCH("gat_bwd_cols_kernel");
@@ -2249,13 +2251,14 @@ int launch_agg(const cign_gat_plan* pl, const SegList& sl, int H, int64_t D, con
                float* out, float* partial, const float* glog, float* gcol, float* pcol,
                cudaStream_t s) {
   using Cfg = AggCfg<VPL>;
+  const int64_t targets = MODE == 0 ? pl->n : pl->n_cols;
   const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
-  const int64_t grid = seg_blocks + (pl->n + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = seg_blocks + (targets + Cfg::kGroups - 1) / Cfg::kGroups;
   const int64_t tiles = (D + Cfg::kTile - 1) / Cfg::kTile;
   CIGN_REQUIRE(grid < (1ll << 31) && tiles < 65536, CIGN_ERR_UNSUPPORTED, "gat_agg: grid too large");
   gat_agg_kernel<VPL, MODE><<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(tiles)),
                               kThreads, 0, s>>>(
-      static_cast<int>(pl->n), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(), sl.seg_end(),
+      static_cast<int>(targets), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(), sl.seg_end(),
       static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col, emax, esum,
       src, slope, p, seed, out, partial, glog, gcol, pcol);
   CIGN_CHECK_LAUNCH("gat_agg_kernel");
@@ -2301,9 +2304,16 @@ extern "C" {
 int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr, const int32_t* col,
                          const int32_t* colptr, const int32_t* row, const int32_t* perm,
                          cign_gat_plan** out) {
+  return cign_gat_plan_create_rect(n, n, nnz, rowptr, col, colptr, row, perm, out);
+}
+
+int cign_gat_plan_create_rect(int64_t n, int64_t n_cols, int64_t nnz, const int32_t* rowptr,
+                              const int32_t* col, const int32_t* colptr, const int32_t* row,
+                              const int32_t* perm, cign_gat_plan** out) {
   CIGN_REQUIRE(out != nullptr, CIGN_ERR_NULL_POINTER, "gat_plan_create: out is NULL");
   *out = nullptr;
-  CIGN_REQUIRE(n >= 0 && nnz >= 0 && n < (1ll << 31) && nnz < (1ll << 31),
+  CIGN_REQUIRE(n >= 0 && n_cols >= 0 && nnz >= 0 && n < (1ll << 31) && n_cols < (1ll << 31) &&
+                   nnz < (1ll << 31),
                CIGN_ERR_INVALID_ARGUMENT, "gat_plan_create: bad sizes");
   CIGN_REQUIRE(rowptr != nullptr && colptr != nullptr, CIGN_ERR_NULL_POINTER,
                "gat_plan_create: rowptr/colptr is NULL");
@@ -2312,9 +2322,9 @@ int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr, const in
   int* bad_d = nullptr;
   CIGN_CHECK_CUDA(cudaMalloc(&bad_d, sizeof(int)), "gat_plan_create: cudaMalloc");
   cudaMemset(bad_d, 0, sizeof(int));
-  const int64_t work = std::max<int64_t>(std::max<int64_t>(n, nnz), 1);
+  const int64_t work = std::max<int64_t>(std::max<int64_t>(std::max(n, n_cols), nnz), 1);
   const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, 4096));
-  gat_validate_kernel<<<blocks, 256>>>(n, nnz, rowptr, col, colptr, row, perm, bad_d);
+  gat_validate_kernel<<<blocks, 256>>>(n, n_cols, nnz, rowptr, col, colptr, row, perm, bad_d);
   cudaError_t le = cudaGetLastError();
   int bad = 0;
   cudaError_t ce = cudaMemcpy(&bad, bad_d, sizeof(int), cudaMemcpyDeviceToHost);
@@ -2328,6 +2338,7 @@ int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr, const in
                "pointer ends)", bad);
   cign_gat_plan* pl = new cign_gat_plan();
   pl->n = n;
+  pl->n_cols = n_cols;
   pl->nnz = nnz;
   pl->rowptr = rowptr;
   pl->col = col;
@@ -2336,7 +2347,7 @@ int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr, const in
   pl->perm = perm;
   cudaGetDevice(&pl->device);
   int rc = build_segments(rowptr, n, kSegLen, &pl->rows);
-  if (rc == CIGN_OK) rc = build_segments(colptr, n, kSegLen, &pl->cols);
+  if (rc == CIGN_OK) rc = build_segments(colptr, n_cols, kSegLen, &pl->cols);
   if (rc != CIGN_OK) {
     free_segments(&pl->rows);
     free_segments(&pl->cols);
@@ -2388,6 +2399,8 @@ int cign_gat_fwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const
   const Seed seed{seed_value, seed_ptr};
   int rc = check_plan(pl, heads, channels, "gat_fwd");
   if (rc) return rc;
+  CIGN_REQUIRE(pl->n == pl->n_cols, CIGN_ERR_UNSUPPORTED,
+               "gat_fwd: needs a square graph (rectangular plans: cign_gat_agg_*)");
   CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
                "gat_fwd: attn_drop must be in [0,1)");
   if (pl->n == 0) return CIGN_OK;
@@ -2434,6 +2447,8 @@ int cign_gat_bwd(const cign_gat_plan* pl, int32_t heads, int32_t channels, const
   const Seed seed{seed_value, seed_ptr};
   int rc = check_plan(pl, heads, channels, "gat_bwd");
   if (rc) return rc;
+  CIGN_REQUIRE(pl->n == pl->n_cols, CIGN_ERR_UNSUPPORTED,
+               "gat_bwd: needs a square graph (rectangular plans: cign_gat_agg_*)");
   CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
                "gat_bwd: attn_drop must be in [0,1)");
   const int64_t C = channels;

@@ -329,12 +329,12 @@ int build_plan_segments(const cign_csr_f32& m, SegList* out) {
 }
 
 int check_dense(const cign_spmm_plan* plan, const float* X, int64_t F,
-                const void* Y, const char* name) {
+                const void* Y, const char* name, bool square = true) {
   CIGN_REQUIRE(plan != nullptr, CIGN_ERR_NULL_POINTER, "%s: plan is NULL", name);
   CIGN_REQUIRE(F > 0, CIGN_ERR_INVALID_ARGUMENT, "%s: F must be positive", name);
-  CIGN_REQUIRE(plan->p.rows == plan->p.cols, CIGN_ERR_INVALID_ARGUMENT,
+  CIGN_REQUIRE(!square || plan->p.rows == plan->p.cols, CIGN_ERR_INVALID_ARGUMENT,
                "%s: operator must be square", name);
-  if (plan->p.rows > 0) {
+  if (plan->p.rows > 0 || plan->p.cols > 0) {
     CIGN_REQUIRE(X != nullptr && Y != nullptr, CIGN_ERR_NULL_POINTER,
                  "%s: dense operand is NULL", name);
   }
@@ -417,8 +417,11 @@ size_t cign_spmm_workspace_bytes(const cign_spmm_plan* plan, int64_t F) {
 int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X, int64_t F,
               const float* addend, float* Y, void* ws, size_t ws_bytes,
               cign_stream_t stream) {
-  int rc = check_dense(plan, X, F, Y, "spmm");
+  int rc = check_dense(plan, X, F, Y, "spmm", false);
   if (rc) return rc;
+  CIGN_REQUIRE(!(transpose && plan->pt_is_p && plan->p.rows != plan->p.cols),
+               CIGN_ERR_INVALID_ARGUMENT,
+               "spmm: a rectangular P needs its transpose at plan creation");
   CIGN_REQUIRE(X != Y || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
                "spmm: Y must not alias X");
   const size_t need = partial_bytes(plan, F);

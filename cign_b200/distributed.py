@@ -1,0 +1,345 @@
+"""Row-partitioned CIGN over several GPUs (one process per GPU).
+
+Partition (the multi-GPU plan of the reference's hot path: contiguous row
+ranges, halo rows exchanged once per hop).  Rank r owns the destination rows
+[bounds[r], bounds[r+1]) of every node tensor; the ranges are balanced by
+rows + non-zeros of the operator.  The rank's row block of P (and of the GAT
+graph, which has the same sparsity pattern as A + I) references columns
+outside its range: those "halo" rows are numbered after the rank's own rows,
+sorted by global id (so grouped by owner rank), giving the "extended" index
+space [own rows | halo rows].
+
+HaloExchange.gather(x_own) -> x_ext fills the halo rows from their owners
+(batched NCCL point-to-point sends/receives; gloo on CPU for tests); its
+autograd backward sends the halo rows' gradients back to their owners,
+which add them to their own rows in a fixed order (peer by peer, unique
+indices per peer), so the sum order is deterministic.
+
+On top of it:
+  * DistMultiHop: per hop, gather the halo rows of the current state, then
+    the local row-block SpMM (cign_spmm on a rectangular plan whose
+    transpose serves the backward);
+  * DistGatGraph: the aggregate-first collapsed GAT on a rectangular plan
+    (destination rows = own rows, source columns = extended rows).
+Every other op of the CIGN block is row-local.  Parameter gradients are
+summed over ranks with one all-reduce (allreduce_gradients).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Sequence
+
+import torch
+import torch.distributed as dist
+
+from .plans import SpmmPlan
+
+
+def partition_rows(crow: torch.Tensor, world: int) -> List[int]:
+    """Contiguous row ranges [b[r], b[r+1]) balancing rows + non-zeros."""
+    crow = crow.to(torch.int64).cpu()
+    n = crow.numel() - 1
+    nnz = int(crow[-1])
+    work = crow + torch.arange(n + 1, dtype=torch.int64)  # events up to each row start
+    total = n + nnz
+    bounds = [0]
+    for r in range(1, world):
+        t = (r * total) // world
+        b = int(torch.searchsorted(work, torch.tensor(t), right=False))
+        bounds.append(max(bounds[-1], min(b, n)))
+    bounds.append(n)
+    return bounds
+
+
+class HaloPlan:
+    """Index bookkeeping of one rank (computed identically on every rank from
+    the global CSR; no communication)."""
+
+    def __init__(self, crow: torch.Tensor, col: torch.Tensor, bounds: Sequence[int], rank: int):
+        crow = crow.to(torch.int64).cpu()
+        col = col.to(torch.int64).cpu()
+        self.bounds = list(bounds)
+        self.rank = rank
+        self.world = len(bounds) - 1
+        r0, r1 = self.bounds[rank], self.bounds[rank + 1]
+        self.r0, self.r1 = r0, r1
+        self.n_own = r1 - r0
+        block = col[int(crow[r0]):int(crow[r1])]
+        outside = block[(block < r0) | (block >= r1)]
+        self.halo = torch.unique(outside)  # sorted global ids
+        self.n_halo = int(self.halo.numel())
+        b = torch.tensor(self.bounds, dtype=torch.int64)
+        owner = torch.searchsorted(b, self.halo, right=True) - 1
+        self.recv_counts = [int((owner == p).sum()) for p in range(self.world)]
+        self.send_idx: List[torch.Tensor] = []
+        self.send_counts: List[int] = []
+        for p in range(self.world):
+            if p == rank:
+                self.send_idx.append(torch.zeros(0, dtype=torch.int64))
+                self.send_counts.append(0)
+                continue
+            p0, p1 = self.bounds[p], self.bounds[p + 1]
+            pc = col[int(crow[p0]):int(crow[p1])]
+            need = torch.unique(pc[(pc >= r0) & (pc < r1)]) - r0
+            self.send_idx.append(need)
+            self.send_counts.append(int(need.numel()))
+
+    def to_ext(self, cols: torch.Tensor) -> torch.Tensor:
+        """Global column ids -> extended ids ([own rows | halo rows])."""
+        cols = cols.to(torch.int64).cpu()
+        own = (cols >= self.r0) & (cols < self.r1)
+        ext = torch.empty_like(cols)
+        ext[own] = cols[own] - self.r0
+        pos = torch.searchsorted(self.halo, cols[~own])
+        if pos.numel() and (pos.max() >= self.n_halo or not torch.equal(self.halo[pos], cols[~own])):
+            raise ValueError("column outside this rank's halo")
+        ext[~own] = self.n_own + pos
+        return ext
+
+
+class TorchP2P:
+    """Point-to-point transport over torch.distributed (NCCL between GPUs,
+    gloo on CPU): one batched group of sends and receives per exchange."""
+
+    def __init__(self, group=None):
+        self.group = group
+
+    def exchange(self, sends: Dict[int, torch.Tensor], recvs: Dict[int, torch.Tensor]) -> None:
+        ops = []
+        for p in sorted(set(sends) | set(recvs)):
+            if p in sends:
+                ops.append(dist.P2POp(dist.isend, sends[p], p, self.group))
+            if p in recvs:
+                ops.append(dist.P2POp(dist.irecv, recvs[p], p, self.group))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+
+
+class StagedGlooP2P:
+    """Point-to-point transport staged through host memory over a gloo
+    group: for ranks that cannot use NCCL between them (e.g. several
+    processes sharing one GPU in tests).  Slower than TorchP2P."""
+
+    def __init__(self, group=None):
+        self.group = group
+
+    def exchange(self, sends: Dict[int, torch.Tensor], recvs: Dict[int, torch.Tensor]) -> None:
+        host_recv = {p: torch.empty(t.shape, dtype=t.dtype) for p, t in recvs.items()}
+        ops = []
+        for p in sorted(set(sends) | set(recvs)):
+            if p in sends:
+                ops.append(dist.P2POp(dist.isend, sends[p].detach().cpu(), p, self.group))
+            if p in recvs:
+                ops.append(dist.P2POp(dist.irecv, host_recv[p], p, self.group))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        for p, t in recvs.items():
+            t.copy_(host_recv[p])
+
+
+class LoopbackTransport:
+    """In-process transport between ranks run as threads of one process (all
+    on one device and stream): rank r's send to p is a copy queued for p.
+    For tests of the partitioned path on a single GPU."""
+
+    def __init__(self, world: int):
+        import queue
+        self.world = world
+        self.boxes = {(a, b): queue.Queue() for a in range(world) for b in range(world)}
+
+    def endpoint(self, rank: int) -> "LoopbackTransport._Endpoint":
+        return LoopbackTransport._Endpoint(self, rank)
+
+    class _Endpoint:
+        def __init__(self, hub, rank):
+            self.hub, self.rank = hub, rank
+
+        def exchange(self, sends, recvs):
+            for p, t in sends.items():
+                self.hub.boxes[(self.rank, p)].put(t.clone())
+            for p, t in recvs.items():
+                t.copy_(self.hub.boxes[(p, self.rank)].get(timeout=120))
+
+
+class HaloExchange:
+    def __init__(self, plan: HaloPlan, device, transport=None):
+        self.plan = plan
+        self.device = torch.device(device)
+        self.transport = transport if transport is not None else TorchP2P()
+        self.n_own, self.n_halo = plan.n_own, plan.n_halo
+        self.send_idx = [t.to(self.device) for t in plan.send_idx]
+        self.send_all = (torch.cat(self.send_idx) if plan.world > 1
+                         else torch.zeros(0, dtype=torch.int64, device=self.device))
+        self.send_off = _offsets(plan.send_counts)
+        self.recv_off = _offsets(plan.recv_counts)
+
+    def _exchange(self, sends: Dict[int, torch.Tensor], recvs: Dict[int, torch.Tensor]) -> None:
+        self.transport.exchange(sends, recvs)
+
+    def gather(self, x_own: torch.Tensor) -> torch.Tensor:
+        """x_ext [n_own + n_halo, F]: own rows, then the halo rows from their owners."""
+        F = x_own.size(1)
+        x_ext = torch.empty((self.n_own + self.n_halo, F), dtype=x_own.dtype, device=x_own.device)
+        x_ext[:self.n_own].copy_(x_own)
+        send = x_own.index_select(0, self.send_all) if self.send_all.numel() else None
+        sends, recvs = {}, {}
+        for p in range(self.plan.world):
+            if self.plan.send_counts[p]:
+                sends[p] = send[self.send_off[p]:self.send_off[p] + self.plan.send_counts[p]]
+            if self.plan.recv_counts[p]:
+                a = self.n_own + self.recv_off[p]
+                recvs[p] = x_ext[a:a + self.plan.recv_counts[p]]
+        self._exchange(sends, recvs)
+        return x_ext
+
+    def scatter_add(self, g_ext: torch.Tensor) -> torch.Tensor:
+        """Backward of gather: own rows' gradient plus the gradients other
+        ranks computed for them (added peer by peer)."""
+        g_ext = g_ext.contiguous()
+        F = g_ext.size(1)
+        g_own = g_ext[:self.n_own].clone()
+        recv = torch.empty((int(self.send_all.numel()), F), dtype=g_ext.dtype, device=g_ext.device)
+        sends, recvs = {}, {}
+        for p in range(self.plan.world):
+            if self.plan.recv_counts[p]:
+                a = self.n_own + self.recv_off[p]
+                sends[p] = g_ext[a:a + self.plan.recv_counts[p]]
+            if self.plan.send_counts[p]:
+                recvs[p] = recv[self.send_off[p]:self.send_off[p] + self.plan.send_counts[p]]
+        self._exchange(sends, recvs)
+        for p in range(self.plan.world):
+            if self.plan.send_counts[p]:
+                g_own.index_add_(0, self.send_idx[p], recvs[p])
+        return g_own
+
+
+def _offsets(counts: Sequence[int]) -> List[int]:
+    out, acc = [], 0
+    for c in counts:
+        out.append(acc)
+        acc += int(c)
+    return out
+
+
+class _HaloFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_own, exchange):
+        ctx.exchange = exchange
+        return exchange.gather(x_own.contiguous())
+
+    @staticmethod
+    def backward(ctx, g_ext):
+        return ctx.exchange.scatter_add(g_ext), None
+
+
+def halo_gather(x_own: torch.Tensor, exchange: HaloExchange) -> torch.Tensor:
+    return _HaloFn.apply(x_own, exchange)
+
+
+def _local_block(crow, col, val, plan: HaloPlan):
+    """Rows [r0, r1) of a global CSR with extended column ids (edge order kept)."""
+    crow = crow.to(torch.int64).cpu()
+    a, b = int(crow[plan.r0]), int(crow[plan.r1])
+    lcrow = crow[plan.r0:plan.r1 + 1] - a
+    lcol = plan.to_ext(col[a:b])
+    lval = None if val is None else val[a:b].cpu()
+    return lcrow, lcol, lval
+
+
+class _LocalSpmmFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_ext, plan: SpmmPlan):
+        ctx.plan = plan
+        return plan.spmm(x_ext.contiguous())
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.plan.spmm(g.contiguous(), transpose=True), None
+
+
+class DistMultiHop:
+    """k-hop propagation P^p x over the row-partitioned operator."""
+
+    def __init__(self, csr_global: torch.Tensor, plan: HaloPlan, exchange: HaloExchange):
+        crow = csr_global.crow_indices().cpu()
+        col = csr_global.col_indices().cpu()
+        val = csr_global.values().cpu()
+        lcrow, lcol, lval = _local_block(crow, col, val, plan)
+        n_own, n_ext = plan.n_own, plan.n_own + plan.n_halo
+        rows = torch.repeat_interleave(torch.arange(n_own), lcrow[1:] - lcrow[:-1])
+        t = torch.sparse_coo_tensor(torch.stack([lcol, rows]), lval, (n_ext, n_own)).coalesce()
+        tc = t.to_sparse_csr()
+        dev = exchange.device
+        self.plan = SpmmPlan(lcrow.to(dev), lcol.to(dev), lval.to(dev),
+                             tc.crow_indices().to(dev), tc.col_indices().to(dev),
+                             tc.values().to(dev), cols=n_ext)
+        self.exchange = exchange
+        self.nnz_local = int(lcol.numel())
+
+    def powers(self, x_own: torch.Tensor, powers: Sequence[int]) -> Dict[int, torch.Tensor]:
+        wanted = sorted(set(int(p) for p in powers))
+        out: Dict[int, torch.Tensor] = {}
+        if 0 in wanted:
+            out[0] = x_own
+        cur = x_own
+        for p in range(1, wanted[-1] + 1):
+            cur = _LocalSpmmFn.apply(halo_gather(cur, self.exchange), self.plan)
+            if p in wanted:
+                out[p] = cur
+        return out
+
+
+class DistGatGraph:
+    """The rank's block of the GAT graph ((rowptr, col), (row, colptr), perm)
+    over extended columns, with the halo exchange that fills them."""
+
+    def __init__(self, rowptr_g: torch.Tensor, col_g: torch.Tensor, plan: HaloPlan,
+                 exchange: HaloExchange):
+        lcrow, lcol, _ = _local_block(rowptr_g, col_g, None, plan)
+        n_own, n_ext = plan.n_own, plan.n_own + plan.n_halo
+        nnz = int(lcol.numel())
+        rows = torch.repeat_interleave(torch.arange(n_own), lcrow[1:] - lcrow[:-1])
+        # CSC over extended columns; perm[csc position] = local CSR edge id
+        order = torch.argsort(lcol * max(n_own, 1) + rows, stable=True)
+        row_csc = rows[order]
+        counts = torch.bincount(lcol, minlength=n_ext)
+        colptr = torch.zeros(n_ext + 1, dtype=torch.int64)
+        colptr[1:] = torch.cumsum(counts, 0)
+        dev = exchange.device
+        i32 = lambda t: t.to(torch.int32).to(dev)  # noqa: E731
+        self.csr = (i32(lcrow), i32(lcol))
+        self.csc = (i32(row_csc), i32(colptr))
+        self.perm = i32(order)
+        self.exchange = exchange
+        self.n_own, self.n_ext, self.nnz = n_own, n_ext, nnz
+
+    def halo(self, x_own: torch.Tensor) -> torch.Tensor:
+        return halo_gather(x_own, self.exchange)
+
+
+def partition_graph(csr_global: torch.Tensor, gat_rowptr: torch.Tensor, gat_col: torch.Tensor,
+                    world: int, rank: int, device, transport=None):
+    """Everything one rank needs: (bounds, HaloPlan, HaloExchange, DistMultiHop,
+    DistGatGraph).  csr_global: P as a sparse CSR tensor; gat_rowptr/gat_col:
+    the destination-major CSR of the GAT graph (same sparsity pattern)."""
+    bounds = partition_rows(csr_global.crow_indices(), world)
+    plan = HaloPlan(csr_global.crow_indices(), csr_global.col_indices(), bounds, rank)
+    exchange = HaloExchange(plan, device, transport)
+    op = DistMultiHop(csr_global, plan, exchange)
+    gat = DistGatGraph(gat_rowptr, gat_col, plan, exchange)
+    return bounds, plan, exchange, op, gat
+
+
+def allreduce_gradients(params, group=None) -> None:
+    """Sum every parameter's gradient over the ranks (one flat all-reduce)."""
+    grads = [p.grad for p in params if p.grad is not None]
+    if not grads:
+        return
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat, group=group)
+    off = 0
+    for g in grads:
+        n = g.numel()
+        g.copy_(flat[off:off + n].view_as(g))
+        off += n

@@ -125,6 +125,9 @@ def selected_sparse_powers(operator, X: torch.Tensor, powers):
     outputs = {}
     if 0 in requested:
         outputs[0] = X
+    if hasattr(operator, "powers") and callable(operator.powers):
+        # a row-partitioned operator (cign_b200.distributed.DistMultiHop)
+        return operator.powers(X, sorted(requested))
     if isinstance(operator, MultiHopCSR3GraphOperator) and requested == {1, 2, 3}:
         y1, y2, y3 = multihop_csr3(operator, X)
         outputs[1], outputs[2], outputs[3] = y1, y2, y3

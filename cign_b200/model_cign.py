@@ -91,19 +91,28 @@ class GATContext(nn.Module):
 
     def forward(self, x: torch.Tensor, gat_graph) -> torch.Tensor:
         H, C = self.heads, self.out_channels
-        csr, csc, perm = gat_graph
         drop = self.dropout if self.training else 0.0
+        partitioned = hasattr(gat_graph, "halo")  # cign_b200.distributed.DistGatGraph
+        if partitioned:
+            csr, csc, perm = gat_graph.csr, gat_graph.csc, gat_graph.perm
+            x_src = gat_graph.halo(x)  # own rows, then the halo rows from their owners
+        else:
+            csr, csc, perm = gat_graph
+            x_src = x
         if self.aggregate_first and x.size(1) % 4 == 0 and C % 4 == 0:
             # lin is linear: aggregate x per head, apply lin.weight afterwards.
             # alpha_src[n,h] = <W_h x_n, att_src[h]> = <x_n, W_h^T att_src[h]>.
             Wv = self.lin.weight.view(H, C, -1)
             V = torch.cat([torch.einsum("hcd,hc->hd", Wv, self.att_src[0]),
                            torch.einsum("hcd,hc->hd", Wv, self.att_dst[0])], 0)
-            alpha = x.matmul(V.t())
-            a_src, a_dst = alpha[:, :H].contiguous(), alpha[:, H:].contiguous()
+            alpha = x_src.matmul(V.t())
+            a_src = alpha[:, :H].contiguous()
+            a_dst = alpha[:x.size(0), H:].contiguous()
             return collapsed_gat_aggregate_first(
-                x, attn_row=a_dst, attn_col=a_src, weight=self.lin.weight, bias=self.bias,
+                x_src, attn_row=a_dst, attn_col=a_src, weight=self.lin.weight, bias=self.bias,
                 csr=csr, csc=csc, perm=perm, negative_slope=self.negative_slope, attn_drop=drop)
+        if partitioned:
+            raise NotImplementedError("a partitioned graph needs the aggregate-first GAT form")
         xh = self.lin(x).view(-1, H, C)
         a_src, a_dst = fused_attention_logits(xh, self.att_src, self.att_dst)
         return collapsed_gat_mean_bias_silu(

@@ -57,15 +57,19 @@ class SpmmPlan:
 
     hop_timer: Optional[HopTimer] = None
 
-    def __init__(self, crow, col, val, crow_t=None, col_t=None, val_t=None):
+    def __init__(self, crow, col, val, crow_t=None, col_t=None, val_t=None,
+                 cols: Optional[int] = None):
         _lib.require_cuda("SpmmPlan")
         self.lib = _lib.load_library()
         self.device = crow.device
         self.crow, self.col, self.val = _as_i32(crow), _as_i32(col), val.to(torch.float32).contiguous()
         self.rows = int(self.crow.numel() - 1)
+        self.cols = self.rows if cols is None else int(cols)
         self.nnz = int(self.col.numel())
+        if self.cols != self.rows and crow_t is None:
+            raise ValueError("a rectangular operator needs its transpose (crow_t, col_t, val_t)")
         symmetric = crow_t is None
-        if not symmetric:
+        if not symmetric and self.cols == self.rows:
             crow_t, col_t = _as_i32(crow_t), _as_i32(col_t)
             val_t = val_t.to(torch.float32).contiguous()
             symmetric = (
@@ -75,19 +79,22 @@ class SpmmPlan:
                 and bool(torch.equal(col_t, self.col))
                 and bool(torch.equal(val_t, self.val))
             )
+        elif not symmetric:
+            crow_t, col_t = _as_i32(crow_t), _as_i32(col_t)
+            val_t = val_t.to(torch.float32).contiguous()
         self.symmetric = symmetric
         if symmetric:
             self.crow_t, self.col_t, self.val_t = self.crow, self.col, self.val
         else:
             self.crow_t, self.col_t, self.val_t = crow_t, col_t, val_t
-        p = _lib.CsrF32(self.rows, self.rows, self.nnz, self.crow.data_ptr(), self.col.data_ptr(),
+        p = _lib.CsrF32(self.rows, self.cols, self.nnz, self.crow.data_ptr(), self.col.data_ptr(),
                         self.val.data_ptr())
         handle = ctypes.c_void_p()
         with _lib.DeviceGuard(self.device):
             if symmetric:
                 rc = self.lib.cign_spmm_plan_create(ctypes.byref(p), None, ctypes.byref(handle))
             else:
-                pt = _lib.CsrF32(self.rows, self.rows, int(self.col_t.numel()), self.crow_t.data_ptr(),
+                pt = _lib.CsrF32(self.cols, self.rows, int(self.col_t.numel()), self.crow_t.data_ptr(),
                                  self.col_t.data_ptr(), self.val_t.data_ptr())
                 rc = self.lib.cign_spmm_plan_create(ctypes.byref(p), ctypes.byref(pt),
                                                     ctypes.byref(handle))
@@ -110,20 +117,22 @@ class SpmmPlan:
         return {name: int(getattr(inf, name)) for name, _ in _lib.SpmmPlanInfo._fields_}
 
     # ---------------------------------------------------------------- ops
-    def _check_dense(self, x: torch.Tensor, what: str) -> torch.Tensor:
+    def _check_dense(self, x: torch.Tensor, what: str, rows: Optional[int] = None) -> torch.Tensor:
+        rows = self.rows if rows is None else int(rows)
         if x.device != self.device:
             raise RuntimeError(f"{what}: tensor on {x.device}, plan on {self.device}")
-        if x.dim() != 2 or x.size(0) != self.rows:
-            raise ValueError(f"{what}: expected [{self.rows}, F], got {tuple(x.shape)}")
+        if x.dim() != 2 or x.size(0) != rows:
+            raise ValueError(f"{what}: expected [{rows}, F], got {tuple(x.shape)}")
         return x.to(torch.float32).contiguous()
 
     def spmm(self, x: torch.Tensor, transpose: bool = False,
              addend: Optional[torch.Tensor] = None) -> torch.Tensor:
-        x = self._check_dense(x, "spmm")
+        x = self._check_dense(x, "spmm", self.rows if transpose else self.cols)
         F = int(x.size(1))
-        y = torch.empty_like(x)
+        y = torch.empty((self.cols if transpose else self.rows, F), dtype=torch.float32,
+                        device=x.device)
         if addend is not None:
-            addend = self._check_dense(addend, "spmm addend")
+            addend = self._check_dense(addend, "spmm addend", int(y.size(0)))
         ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, F), self.device)
         with _lib.DeviceGuard(self.device):
             rc = self.lib.cign_spmm(self.handle, 1 if transpose else 0, _lib.ptr(x), F,
@@ -184,14 +193,15 @@ class GatPlan:
         self.rowptr, self.col = _as_i32(rowptr), _as_i32(col)
         self.row, self.colptr, self.perm = _as_i32(row), _as_i32(colptr), _as_i32(perm)
         self.n = int(self.rowptr.numel() - 1)
+        self.n_cols = int(self.colptr.numel() - 1)
         self.nnz = int(self.col.numel())
-        if self.colptr.numel() != self.n + 1 or self.row.numel() != self.nnz or self.perm.numel() != self.nnz:
+        if self.row.numel() != self.nnz or self.perm.numel() != self.nnz:
             raise ValueError("GAT graph: CSR/CSC/perm sizes do not match")
         handle = ctypes.c_void_p()
         with _lib.DeviceGuard(self.device):
-            rc = self.lib.cign_gat_plan_create(self.n, self.nnz, _lib.ptr(self.rowptr), _lib.ptr(self.col),
-                                               _lib.ptr(self.colptr), _lib.ptr(self.row),
-                                               _lib.ptr(self.perm), ctypes.byref(handle))
+            rc = self.lib.cign_gat_plan_create_rect(
+                self.n, self.n_cols, self.nnz, _lib.ptr(self.rowptr), _lib.ptr(self.col),
+                _lib.ptr(self.colptr), _lib.ptr(self.row), _lib.ptr(self.perm), ctypes.byref(handle))
         _lib.check(rc, "cign_gat_plan_create")
         self.handle = handle
 

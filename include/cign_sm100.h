@@ -109,7 +109,10 @@ CIGN_API int cign_spmm_plan_get_info(const cign_spmm_plan* plan,
 CIGN_API size_t cign_spmm_workspace_bytes(const cign_spmm_plan* plan, int64_t F);
 
 /* Y = op(P) @ X (+ addend).  op = P (transpose=0) or P^T (transpose=1).
- * X, Y, addend: [rows, F].  addend may be NULL.  Y must not alias X.
+ * X: [cols of op(P), F]; Y, addend: [rows of op(P), F].  P may be
+ * rectangular (a row block of a partitioned operator); its transposed
+ * product then needs `pt` at plan creation.  addend may be NULL.  Y must not
+ * alias X.
  * Replaces FixedCSRSpMMFunction.forward/backward (model.py:106-131). */
 CIGN_API int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
               int64_t F, const float* addend, float* Y, void* ws,
@@ -159,6 +162,14 @@ CIGN_API int cign_gat_plan_create(int64_t n, int64_t nnz, const int32_t* rowptr,
                          const int32_t* col, const int32_t* colptr,
                          const int32_t* row, const int32_t* perm,
                          cign_gat_plan** out);
+/* Rectangular form: destination rows 0..n_rows-1 (rowptr [n_rows+1]) and
+ * source columns 0..n_cols-1 (colptr [n_cols+1]) -- e.g. the row block of a
+ * partitioned graph whose columns index local rows plus halo rows.  Only the
+ * cign_gat_agg_* entry points accept n_rows != n_cols. */
+CIGN_API int cign_gat_plan_create_rect(int64_t n_rows, int64_t n_cols, int64_t nnz,
+                                       const int32_t* rowptr, const int32_t* col,
+                                       const int32_t* colptr, const int32_t* row,
+                                       const int32_t* perm, cign_gat_plan** out);
 CIGN_API int cign_gat_plan_destroy(cign_gat_plan* plan);
 /* info (host, 8 entries): n, nnz, hub rows, hub columns, max row length,
  * max column length, row segments, column segments. */
