@@ -246,7 +246,7 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device):
     return out
 
 
-def hop_roofline(timer, N, nnz, peak, peak_kind):
+def hop_roofline(timer, N, nnz, peak, peak_kind, with_traffic=True):
     """Roofline of the dominant kernel, the k-hop SpMM (spmm_rows_kernel plus its
     hub-row combine; the largest share of the step's device time), from the
     CUDA events recorded around every k-hop call inside the timed steps."""
@@ -255,7 +255,7 @@ def hop_roofline(timer, N, nnz, peak, peak_kind):
     alg = 0
     mix = {"fwd": 0, "bwd_add": 0, "bwd": 0}
     F = None
-    for kind, n_hops, n_add, F, start, end in timer.records:
+    for kind, n_hops, n_add, F, start, end, rows, rec_nnz in timer.records:
         t_ms += start.elapsed_time(end)
         launches += n_hops
         if kind == "fwd":
@@ -263,13 +263,15 @@ def hop_roofline(timer, N, nnz, peak, peak_kind):
         else:
             mix["bwd_add"] += n_add
             mix["bwd"] += n_hops - n_add
-        alg += (n_hops - n_add) * algorithmic_bytes("spmm", N, nnz, F=F)
-        alg += n_add * algorithmic_bytes("spmm_add", N, nnz, F=F)
+        Nr = N if rows is None else rows
+        Zr = nnz if rec_nnz is None else rec_nnz
+        alg += (n_hops - n_add) * algorithmic_bytes("spmm", Nr, Zr, F=F)
+        alg += n_add * algorithmic_bytes("spmm_add", Nr, Zr, F=F)
     if launches == 0:
         return None
     per_launch_s = t_ms * 1e-3 / launches
     achieved = alg / launches / per_launch_s / 1e9
-    tr = load_traffic().get("spmm_hop", {})
+    tr = load_traffic().get("spmm_hop", {}) if with_traffic else {}
     traffic = None
     if all(k in tr for k in ("fwd", "bwd_add", "bwd")):
         traffic = int((mix["fwd"] * tr["fwd"] + mix["bwd_add"] * tr["bwd_add"]
@@ -348,8 +350,11 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     sampler = ClockSampler(local_rank)
+    from cign_b200.plans import HopTimer, SpmmPlan
+    hop_timer = HopTimer()
     dist.barrier()
     torch.cuda.synchronize()
+    SpmmPlan.hop_timer = hop_timer  # events around every local row-block SpMM
     sampler.start()
     for i in range(args.steps):
         flush.zero_()
@@ -357,9 +362,11 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
         step(x)
         ends[i].record(stream)
     torch.cuda.synchronize()
+    SpmmPlan.hop_timer = None
     clocks = sampler.stop()
     launches = int(lib.cign_kernel_launches()) - launches_before
-    total_s = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) * 1e-3
+    step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    total_s = sum(step_ms) * 1e-3
     t = torch.tensor([total_s], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_s = float(t.item())
@@ -401,8 +408,10 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                     "h2d_bytes_per_step": int(x_cpu.numel() * 4), "d2h_bytes_per_step": 4,
                     "ms_per_step": round(e2e_s / args.steps * 1e3, 4)},
             "gpu_launches": launches,
-            "roofline": None, "cpu_baseline": None, "clocks": clocks,
-            "peak_hbm_gbs": peak, "peak_kind": peak_kind,
+            "step_ms_rank0": [round(v, 3) for v in step_ms],
+            "roofline": hop_roofline(hop_timer, hplan.n_own, dop.nnz_local, peak, peak_kind,
+                                     with_traffic=False),
+            "cpu_baseline": None, "clocks": clocks,
             "final_loss": round(loss_host, 5),
         }
         print(json.dumps(result), flush=True)

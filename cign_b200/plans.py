@@ -42,8 +42,8 @@ class HopTimer:
     def begin(self, stream):
         return self._event(stream)
 
-    def end(self, stream, start, kind, n_hops, n_addend, F):
-        self.records.append((kind, n_hops, n_addend, F, start, self._event(stream)))
+    def end(self, stream, start, kind, n_hops, n_addend, F, rows=None, nnz=None):
+        self.records.append((kind, n_hops, n_addend, F, start, self._event(stream), rows, nnz))
 
 
 class SpmmPlan:
@@ -134,10 +134,15 @@ class SpmmPlan:
         if addend is not None:
             addend = self._check_dense(addend, "spmm addend", int(y.size(0)))
         ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, F), self.device)
+        timer = SpmmPlan.hop_timer
         with _lib.DeviceGuard(self.device):
+            t0 = timer.begin(torch.cuda.current_stream(self.device)) if timer else None
             rc = self.lib.cign_spmm(self.handle, 1 if transpose else 0, _lib.ptr(x), F,
                                     _lib.ptr(addend), _lib.ptr(y), _lib.ptr(ws), ws.numel(),
                                     _lib.stream_of(x))
+            if timer:
+                timer.end(torch.cuda.current_stream(self.device), t0, "bwd" if transpose else "fwd",
+                          1, 0 if addend is None else 1, F, rows=int(y.size(0)), nnz=self.nnz)
         _lib.check(rc, "cign_spmm")
         return y
 
