@@ -2192,27 +2192,59 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
                          ? ld_vec<4>(U + row * HD + static_cast<int64_t>(h0 + hh) * D + fi)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-      for (int t = 0; t < cnt; ++t) {
-        const int ct = __shfl_sync(kFullMask, c, t);
-        float4 x[2];
+      // 4 edges per pass: their X loads are in flight together, and the 16
+      // (edge, head) partial dots are reduced across the warp by a transposed
+      // butterfly (each level halves the values a lane carries), leaving the
+      // total of value m = 4*edge + head on lanes 2m and 2m+1.
+      for (int t0 = 0; t0 < cnt; t0 += 4) {
+        float4 x[4][2];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
-          x[q] = fi < D ? ldg_vec<4>(X + static_cast<int64_t>(ct) * D + fi)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int hh = 0; hh < kAggHB; ++hh) {
-          float d = 0.0f;
+        for (int e4 = 0; e4 < 4; ++e4) {
+          const int t = t0 + e4;
+          const int ct = __shfl_sync(kFullMask, c, t < 32 ? t : 31);
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
-            d = fmaf(u[hh][q].x, x[q].x, d);
-            d = fmaf(u[hh][q].y, x[q].y, d);
-            d = fmaf(u[hh][q].z, x[q].z, d);
-            d = fmaf(u[hh][q].w, x[q].w, d);
+            const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+            x[e4][q] = (t < cnt && fi < D) ? ldg_vec<4>(X + static_cast<int64_t>(ct) * D + fi)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
           }
-          d = warp_sum(d);
-          if (lane == t) mine[hh] += d;
+        }
+        float v[16];
+#pragma unroll
+        for (int e4 = 0; e4 < 4; ++e4)
+#pragma unroll
+          for (int hh = 0; hh < kAggHB; ++hh) {
+            float d = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              d = fmaf(u[hh][q].x, x[e4][q].x, d);
+              d = fmaf(u[hh][q].y, x[e4][q].y, d);
+              d = fmaf(u[hh][q].z, x[e4][q].z, d);
+              d = fmaf(u[hh][q].w, x[e4][q].w, d);
+            }
+            v[e4 * 4 + hh] = d;
+          }
+#pragma unroll
+        for (int level = 0; level < 4; ++level) {
+          const int half = 8 >> level;                 // values kept after this level
+          const int off = 16 >> level;                 // lane distance
+          const bool upper = (lane & off) != 0;
+#pragma unroll
+          for (int j = 0; j < half; ++j) {
+            const float keep = upper ? v[j + half] : v[j];
+            const float send = upper ? v[j] : v[j + half];
+            v[j] = keep + __shfl_xor_sync(kFullMask, send, off);
+          }
+        }
+        const float tot = v[0] + __shfl_xor_sync(kFullMask, v[0], 1);
+        // lane t0 + e4 (the edge's owner) collects its 4 heads
+        const int e_mine = lane - t0;
+        const bool owner = e_mine >= 0 && e_mine < 4;
+#pragma unroll
+        for (int hh = 0; hh < kAggHB; ++hh) {
+          const int src = 2 * ((owner ? e_mine : 0) * 4 + hh);
+          const float d = __shfl_sync(kFullMask, tot, src);
+          if (owner) mine[hh] += d;
         }
       }
     }
