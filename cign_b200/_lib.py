@@ -89,11 +89,13 @@ SIGNATURES = {
     "cign_gat_bwd": (c_int, [_P, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, c_float, c_float,
                              c_uint64, _P, _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_gat_dropout_mask": (c_int, [c_int64, c_int32, c_float, c_uint64, _P, _P, _P]),
+    "cign_colsum_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "cign_colsum_f32": (c_int, [c_int64, c_int64, _P, _P, _P, c_size_t, _P]),
     "cign_seed_table_step": (c_int, [c_uint64, c_int32, _P, _P, c_int32, c_int32, _P, _P]),
     "cign_hop_gate_fwd": (c_int, [c_int64, c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P]),
     "cign_hop_gate_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int32]),
     "cign_hop_gate_bwd": (c_int, [c_int64, c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P,
-                                  _P, _P, _P, c_size_t, _P]),
+                                  _P, _P, c_int32, _P, _P, c_int64, _P, c_size_t, _P]),
     "cign_gat_agg_workspace_bytes": (c_size_t, [_P, c_int32, c_int64, c_int64]),
     "cign_gat_agg_fwd": (c_int, [_P, c_int32, c_int64, _P, _P, _P, c_float, c_float, c_uint64, _P,
                                  _P, _P, _P, _P, c_size_t, _P]),

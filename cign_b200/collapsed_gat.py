@@ -215,6 +215,35 @@ def gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z, grad_p
     return gfeat, grow, gcol
 
 
+def _bias_silu(lin: torch.Tensor, bias: torch.Tensor):
+    """(SiLU(lin + bias), lin + bias) in one pass (cign_head_mean_bias_silu_fwd, 1 head)."""
+    lib = ensure_collapsed_gat_loaded()
+    n, C = (int(s) for s in lin.shape)
+    out = torch.empty_like(lin)
+    pre = torch.empty_like(lin)
+    with _lib.DeviceGuard(lin.device):
+        rc = lib.cign_head_mean_bias_silu_fwd(n, 1, C, _lib.ptr(lin), _lib.ptr(bias.contiguous()),
+                                              _lib.ptr(out), _lib.ptr(pre), _lib.stream_of(lin))
+    _lib.check(rc, "cign_head_mean_bias_silu_fwd")
+    return out, pre
+
+
+def _bias_silu_backward(grad_out: torch.Tensor, pre: torch.Tensor):
+    """(g_pre = grad_out * SiLU'(pre), fixed-order column sums of g_pre)."""
+    lib = ensure_collapsed_gat_loaded()
+    grad_out = grad_out.to(torch.float32).contiguous()
+    n, C = (int(s) for s in pre.shape)
+    g_pre = torch.empty_like(pre)
+    g_bias = torch.empty((C,), dtype=torch.float32, device=pre.device)
+    ws = _lib.workspace(lib.cign_head_mean_bias_silu_bwd_workspace_bytes(n, C), pre.device)
+    with _lib.DeviceGuard(pre.device):
+        rc = lib.cign_head_mean_bias_silu_bwd(n, 1, C, _lib.ptr(grad_out), _lib.ptr(pre),
+                                              _lib.ptr(g_pre), _lib.ptr(g_bias), _lib.ptr(ws),
+                                              ws.numel(), _lib.stream_of(pre))
+    _lib.check(rc, "cign_head_mean_bias_silu_bwd")
+    return g_pre, g_bias
+
+
 def _head_projection(weight: torch.Tensor, heads: int) -> torch.Tensor:
     """M [H*D, C] with M[(h,d), c] = W[h*C + c, d] / H, so that
     z.view(N, H*D) @ M = (1/H) sum_h W_h z[:, h, :]."""
@@ -235,11 +264,12 @@ class _AggregateFirstGATFn(torch.autograd.Function):
         z, emax, esum = gat_agg_forward_raw(plan, attn_row, attn_col, x, H, negative_slope,
                                             attn_drop, seed)
         M = _head_projection(weight, H)
-        pre = torch.addmm(bias, z.view(n, H * D), M)
+        lin = z.view(n, H * D).mm(M)
+        out, pre = _bias_silu(lin, bias)
         ctx.save_for_backward(x, attn_row, attn_col, weight, z, pre, emax, esum)
         ctx.plan, ctx.heads = plan, H
         ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), seed
-        return torch.nn.functional.silu(pre)
+        return out
 
     @staticmethod
     def backward(ctx, grad_out):
@@ -248,8 +278,7 @@ class _AggregateFirstGATFn(torch.autograd.Function):
         n, D = int(z.size(0)), int(x.size(1))
         n_cols = int(x.size(0))
         C = weight.size(0) // H
-        g_pre = torch.ops.aten.silu_backward(grad_out.contiguous(), pre)
-        grad_bias = g_pre.sum(0)
+        g_pre, grad_bias = _bias_silu_backward(grad_out, pre)
         M = _head_projection(weight, H)
         z2 = z.view(n, H * D)
         grad_M = z2.t().mm(g_pre)                                   # [H*D, C]

@@ -91,8 +91,9 @@ __global__ void __launch_bounds__(kThreads)
 hop_gate_bwd_kernel(int64_t n, int64_t D, int64_t rpc, int mode, const float* __restrict__ H,
                     const float* __restrict__ C, const float* __restrict__ W,
                     const float* __restrict__ alpha, const float* __restrict__ g_alpha,
-                    float* __restrict__ gH, float* __restrict__ gC, float* __restrict__ pw,
-                    float* __restrict__ pb) {
+                    float* __restrict__ gH, float* __restrict__ gC, int accumulate,
+                    const float* __restrict__ add_h, const float* __restrict__ add_c,
+                    int64_t add_ld, float* __restrict__ pw, float* __restrict__ pb) {
   __shared__ float4 red[kThreads / 32][2][32];
   __shared__ float redb[kThreads / 32][K];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -154,8 +155,18 @@ hop_gate_bwd_kernel(int64_t n, int64_t D, int64_t rpc, int mode, const float* __
       oh = gi0;
       oc = gi1;
     }
-    st_vec(gH + row * D + c, oh);
-    st_vec(gC + row * D + c, oc);
+    // existing gradient first, then the extra addend, then this op's part
+    float4 th = make_float4(0.f, 0.f, 0.f, 0.f), tc = th;
+    if (accumulate) {
+      th = ld_vec<4>(gH + row * D + c);
+      tc = ld_vec<4>(gC + row * D + c);
+    }
+    if (add_h != nullptr) vadd(th, ld_vec<4>(add_h + row * add_ld + c));
+    if (add_c != nullptr) vadd(tc, ld_vec<4>(add_c + row * add_ld + c));
+    vadd(th, oh);
+    vadd(tc, oc);
+    st_vec(gH + row * D + c, th);
+    st_vec(gC + row * D + c, tc);
   }
   // fixed-order reduction of the warps' parameter partials, one k at a time
 #pragma unroll
@@ -247,10 +258,15 @@ size_t cign_hop_gate_bwd_workspace_bytes(int64_t n, int64_t d, int32_t k) {
 
 int cign_hop_gate_bwd(int64_t n, int64_t d, int32_t k, int32_t mode, const float* h,
                       const float* c, const float* w, const float* alpha, const float* grad_alpha,
-                      float* grad_h, float* grad_c, float* grad_w, float* grad_b, void* ws,
-                      size_t ws_bytes, cign_stream_t stream) {
+                      float* grad_h, float* grad_c, float* grad_w, float* grad_b,
+                      int32_t accumulate, const float* add_h, const float* add_c, int64_t add_ld,
+                      void* ws, size_t ws_bytes, cign_stream_t stream) {
   int rc = check_hg(n, d, k, mode, {h, c, w, grad_h, grad_c, ws}, "hop_gate_bwd");
   if (rc) return rc;
+  CIGN_REQUIRE((add_h == nullptr && add_c == nullptr) ||
+                   (add_ld >= d && add_ld % 4 == 0 && (add_h == nullptr || aligned16(add_h)) &&
+                    (add_c == nullptr || aligned16(add_c))),
+               CIGN_ERR_ALIGNMENT, "hop_gate_bwd: addends need 16-byte rows (add_ld % 4 == 0)");
   CIGN_REQUIRE(grad_w != nullptr && grad_b != nullptr, CIGN_ERR_NULL_POINTER,
                "hop_gate_bwd: NULL parameter gradient");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -274,7 +290,8 @@ int cign_hop_gate_bwd(int64_t n, int64_t d, int32_t k, int32_t mode, const float
                                        rnd256(static_cast<size_t>(ch) * k * 2 * d * sizeof(float)));
   const dim3 grid(static_cast<unsigned>(ch), static_cast<unsigned>(tiles));
   CIGN_HG_K_DISPATCH(k, (hop_gate_bwd_kernel<K_><<<grid, kThreads, 0, s>>>(
-                            n, d, rpc, mode, h, c, w, alpha, grad_alpha, grad_h, grad_c, pw, pb)));
+                            n, d, rpc, mode, h, c, w, alpha, grad_alpha, grad_h, grad_c,
+                            accumulate, add_h, add_c, add_ld, pw, pb)));
   CIGN_CHECK_LAUNCH("hop_gate_bwd_kernel");
   rc = colsum_rows(pw, grad_w, nullptr, nullptr, ch, static_cast<int64_t>(k) * 2 * d,
                    static_cast<int64_t>(k) * 2 * d, s);

@@ -91,3 +91,26 @@ int colsum_rows(const float* a0, float* out0, const float* a1, float* out1, int6
 }
 
 }  // namespace cign
+
+using namespace cign;
+
+extern "C" {
+
+size_t cign_colsum_workspace_bytes(int64_t n, int64_t c) {
+  if (n <= 0 || c <= 0) return 0;
+  return static_cast<size_t>(colsum_chunks(n)) * c * sizeof(float);
+}
+
+int cign_colsum_f32(int64_t n, int64_t c, const float* a, float* out, void* ws, size_t ws_bytes,
+                    cign_stream_t stream) {
+  CIGN_REQUIRE(n >= 0 && c >= 0, CIGN_ERR_INVALID_ARGUMENT, "colsum: negative size");
+  if (c == 0) return CIGN_OK;
+  CIGN_REQUIRE(out != nullptr && (n == 0 || a != nullptr), CIGN_ERR_NULL_POINTER,
+               "colsum: NULL argument");
+  const size_t need = cign_colsum_workspace_bytes(n, c);
+  CIGN_REQUIRE(ws_bytes >= need && (need == 0 || ws != nullptr), CIGN_ERR_INVALID_ARGUMENT,
+               "colsum: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  return colsum_f32(a, n, c, static_cast<float*>(ws), out, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -123,7 +123,7 @@ __global__ void head_silu_bwd_kernel(int64_t n, int H, int64_t C,
        i += stride) {
     const int64_t r = i / C, c = i - r * C;
     const float gp = gy[i] * silu_grad_f(pre[i]);
-    gpre[i] = gp;
+    if (gpre != nullptr) gpre[i] = gp;
     const float g = gp / hf;
     float* go = grad_out + r * H * C + c;
     for (int h = 0; h < H; ++h) go[static_cast<int64_t>(h) * C] = g;
@@ -259,10 +259,11 @@ int cign_head_mean_bias_silu_bwd(int64_t n, int32_t heads, int32_t channels,
   float* gpre = static_cast<float*>(ws);
   float* partial = reinterpret_cast<float*>(
       static_cast<char*>(ws) + (static_cast<size_t>(n) * channels * sizeof(float) + 255) / 256 * 256);
-  head_silu_bwd_kernel<<<grid_1d(n * channels), kThreads, 0, s>>>(n, heads, channels, grad_y, pre,
-                                                                  grad_out, gpre);
+  // one head: grad_out is g_pre itself, so the column sums read it directly
+  head_silu_bwd_kernel<<<grid_1d(n * channels), kThreads, 0, s>>>(
+      n, heads, channels, grad_y, pre, grad_out, heads == 1 ? nullptr : gpre);
   CIGN_CHECK_LAUNCH("head_silu_bwd_kernel");
-  return colsum_f32(gpre, n, channels, partial, grad_bias, s);
+  return colsum_f32(heads == 1 ? grad_out : gpre, n, channels, partial, grad_bias, s);
 }
 
 }  // extern "C"

@@ -15,6 +15,38 @@ from . import _lib
 MAX_HOPS = 8
 
 
+def hop_gate_forward_raw(h, c, weight, bias, mode: int) -> torch.Tensor:
+    """alpha [N, K] (cign_hop_gate_fwd)."""
+    lib = _lib.load_library()
+    n, d = h.shape
+    k = int(weight.size(0))
+    alpha = torch.empty((n, k), dtype=torch.float32, device=h.device)
+    with _lib.DeviceGuard(h.device):
+        rc = lib.cign_hop_gate_fwd(n, d, k, int(mode), _lib.ptr(h), _lib.ptr(c), _lib.ptr(weight),
+                                   _lib.ptr(bias), _lib.ptr(alpha), _lib.stream_of(h))
+    _lib.check(rc, "cign_hop_gate_fwd")
+    return alpha
+
+
+def hop_gate_backward_raw(h, c, weight, alpha, grad_alpha, mode: int, grad_h, grad_c,
+                          accumulate: bool = False, add_h=None, add_c=None, add_ld: int = 0):
+    """Writes grad_h/grad_c (see cign_hop_gate_bwd); returns (grad_w, grad_b)."""
+    lib = _lib.load_library()
+    n, d = h.shape
+    k = int(weight.size(0))
+    gw = torch.empty_like(weight)
+    gb = torch.empty((k,), dtype=torch.float32, device=h.device)
+    ws = _lib.workspace(lib.cign_hop_gate_bwd_workspace_bytes(n, d, k), h.device)
+    with _lib.DeviceGuard(h.device):
+        rc = lib.cign_hop_gate_bwd(n, d, k, int(mode), _lib.ptr(h), _lib.ptr(c), _lib.ptr(weight),
+                                   _lib.ptr(alpha), _lib.ptr(grad_alpha.contiguous()),
+                                   _lib.ptr(grad_h), _lib.ptr(grad_c), _lib.ptr(gw), _lib.ptr(gb),
+                                   1 if accumulate else 0, add_h, add_c, int(add_ld),
+                                   _lib.ptr(ws), ws.numel(), _lib.stream_of(h))
+    _lib.check(rc, "cign_hop_gate_bwd")
+    return gw, gb
+
+
 class _HopGateFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, c, weight, bias, mode):
@@ -46,8 +78,8 @@ class _HopGateFn(torch.autograd.Function):
             rc = lib.cign_hop_gate_bwd(n, d, k, ctx.mode, _lib.ptr(h), _lib.ptr(c),
                                        _lib.ptr(weight), _lib.ptr(alpha),
                                        _lib.ptr(grad_alpha.contiguous()), _lib.ptr(gh),
-                                       _lib.ptr(gc), _lib.ptr(gw), _lib.ptr(gb), _lib.ptr(ws),
-                                       ws.numel(), _lib.stream_of(h))
+                                       _lib.ptr(gc), _lib.ptr(gw), _lib.ptr(gb), 0, None, None, 0,
+                                       _lib.ptr(ws), ws.numel(), _lib.stream_of(h))
         _lib.check(rc, "cign_hop_gate_bwd")
         return gh, gc, gw, gb, None
 

@@ -41,7 +41,9 @@ from .collapsed_gat import collapsed_gat_aggregate_first, collapsed_gat_mean_bia
 from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, fused_dropout_layernorm
 from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
+from .block_fused import native_spmm_plan, propagate_gate_pack
 from .hop_gate import fused_hop_gate
+from .linear import linear
 
 
 def _glorot_(t: torch.Tensor) -> None:
@@ -162,6 +164,17 @@ class GraphCliffordBlock(nn.Module):
         C_gat = self.context_gat(H_norm, gat_graph)
         C_norm = fused_add_layernorm(C_gat, H_norm, self.c_norm.weight, self.c_norm.bias,
                                      self.c_norm.eps)
+        plan = native_spmm_plan(graph_operator)
+        if (plan is not None and self.interaction_mode == "new" and self.outer_nonlinearity == "none"
+                and self.alpha_weighting_mode == "old" and self.alpha_score_mode in ("new", "old")
+                and H_norm.size(1) % 4 == 0 and self.num_hops <= 8
+                and len(set(self.order_set)) == self.num_hops and min(self.order_set) >= 1):
+            # propagation + hop gate + pack as one node (gradients merged in-kernel)
+            G_raw = propagate_gate_pack(H_norm, C_norm, self.hop_gate_mlp.weight,
+                                        self.hop_gate_mlp.bias, plan, self.order_set,
+                                        self.alpha_score_mode)
+            G_feat = linear(G_raw, self.proj.weight, self.proj.bias)
+            return fused_dropout_gamma_residual(H, G_feat, self.gamma, p)
         HC = torch.cat([H_norm, C_norm], dim=-1)
         propagated = selected_sparse_powers(graph_operator, HC, self.order_set)
         hop_gate = self.compute_hop_gate(H_norm, C_norm)
@@ -185,7 +198,7 @@ class GraphCliffordBlock(nn.Module):
             from .fused_clifford_switch_pack import fused_clifford_switch_pack
             G_raw = fused_clifford_switch_pack(H_norm, C_norm, props, hop_gate, "new",
                                                self.alpha_weighting_mode)
-        G_feat = self.proj(G_raw)
+        G_feat = linear(G_raw, self.proj.weight, self.proj.bias)
         return fused_dropout_gamma_residual(H, G_feat, self.gamma, p)
 
 
@@ -225,8 +238,9 @@ class GraphCliffordNet(nn.Module):
             raise RuntimeError("call prepare_fused_gat_graph(...) once before training")
         x = x.float()
         H_in = F.dropout(x, p=self.dropout, training=self.training)
-        H = self.input_act(self.input_proj_0(H_in)) + self.input_eta * self.input_act(
-            self.input_proj_1(H_in))
+        H = self.input_act(linear(H_in, self.input_proj_0.weight, self.input_proj_0.bias)) + \
+            self.input_eta * self.input_act(linear(H_in, self.input_proj_1.weight,
+                                                   self.input_proj_1.bias))
         states = [H]
         for block in self.blocks:
             H = block(H, graph_operator, self._gat_graph)

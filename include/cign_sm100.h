@@ -325,6 +325,16 @@ CIGN_API int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
                   int32_t accumulate_p, float* grad_alpha,
                   cign_stream_t stream);
 
+/* ------------------------------------------------------------ column sum
+ * out[j] = sum_i a[i, j] for a row-major [n, c] matrix, in a fixed order
+ * (two stages: fixed 128-row chunks, then the chunk partials) -- the bias
+ * gradient of a linear layer, which the reference leaves to autograd's
+ * grad.sum(0) (e.g. the proj and input linears, generic_engine/
+ * model_cign.py:700-704).  ws: cign_colsum_workspace_bytes(n, c) bytes. */
+CIGN_API size_t cign_colsum_workspace_bytes(int64_t n, int64_t c);
+CIGN_API int cign_colsum_f32(int64_t n, int64_t c, const float* a, float* out, void* ws,
+                             size_t ws_bytes, cign_stream_t stream);
+
 /* ------------------------------------------------------------ seed table
  * Device-side dropout seed streams for CUDA-graph training steps.  For slot
  * i < n_slots with layout[3i..3i+2] = (kind, tag, offset):
@@ -350,13 +360,17 @@ CIGN_API int cign_hop_gate_fwd(int64_t n, int64_t d, int32_t k, int32_t mode, co
                                const float* c, const float* w, const float* b, float* alpha,
                                cign_stream_t stream);
 CIGN_API size_t cign_hop_gate_bwd_workspace_bytes(int64_t n, int64_t d, int32_t k);
-/* Backward: grad_h, grad_c [N,D] (written), grad_w [K,2D], grad_b [K]
- * (fixed-order sums: deterministic); sign(0) = 0 for |H - C|. */
+/* Backward: grad_h, grad_c [N,D], grad_w [K,2D], grad_b [K] (fixed-order
+ * sums: deterministic); sign(0) = 0 for |H - C|.  grad_h/grad_c receive
+ * (accumulate ? their current value : 0) + add_h/add_c rows (row stride
+ * add_ld floats; either may be NULL) + this op's gradient, so callers can
+ * merge the other consumers' gradients of H and C into the same pass. */
 CIGN_API int cign_hop_gate_bwd(int64_t n, int64_t d, int32_t k, int32_t mode, const float* h,
                                const float* c, const float* w, const float* alpha,
                                const float* grad_alpha, float* grad_h, float* grad_c,
-                               float* grad_w, float* grad_b, void* ws, size_t ws_bytes,
-                               cign_stream_t stream);
+                               float* grad_w, float* grad_b, int32_t accumulate,
+                               const float* add_h, const float* add_c, int64_t add_ld, void* ws,
+                               size_t ws_bytes, cign_stream_t stream);
 
 /* ------------------------------------------------------------ block ops
  * Row LayerNorm over D with biased variance and rsqrt(var + eps); optional
