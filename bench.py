@@ -312,7 +312,8 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     ei, adj = build_sparse_normalized_adjacency(edge, n)
     base = prepare_fixed_csr_operator(adj)
     (rp, c), _, _ = to_graph_format(prepare_gat_edge_index(ei, n).flip(0), n)
-    bounds, hplan, exch, dop, dgat = partition_graph(base.csr, rp, c, world, rank, device)
+    bounds, hplan, exch, dop, dgat = partition_graph(
+        base.csr, rp, c, world, rank, device, transport=None if args.exchange == "nccl" else "peer")
     r0, r1 = bounds[rank], bounds[rank + 1]
     nnz = int(base.nnz)
     x_all, y_all, train_all, _, _ = synth.make_features(gcfg)
@@ -333,6 +334,7 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     params = list(model.parameters())
 
     def step(xin):
+        exch.begin_step()
         opt.zero_grad(set_to_none=True)
         logits = model(xin, dop)
         loss = F.cross_entropy(logits.index_select(0, mine), y.index_select(0, mine),
@@ -387,6 +389,8 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     e2e_s = float(t.item())
     halo = torch.tensor([hplan.n_halo], device=device, dtype=torch.float64)
     dist.all_reduce(halo)
+    if hasattr(exch, "close"):
+        exch.close()
     if rank == 0:
         peak, peak_kind = load_peaks()
         result = {
@@ -400,8 +404,11 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                        "hidden": cfg.hidden_dim, "hops": list(cfg.hops), "heads": cfg.heads,
                        "layers": cfg.layers, "dropout": cfg.dropout,
                        "parallelism": f"row-partition x{world}",
-                       "exchange": "NCCL P2P halo rows per hop and per GAT layer; one "
-                                   "gradient all-reduce per step",
+                       "exchange": ("halo rows per hop and per GAT layer: " +
+                                    ("NCCL point-to-point" if args.exchange == "nccl" else
+                                     "stored into the peers' IPC-mapped buffers over NVLink "
+                                     "(cign_halo_push)") +
+                                    "; one gradient all-reduce per step"),
                        "halo_rows_total": int(halo.item()),
                        "l2": "flushed between timed steps (256 MiB write)", "launch": "eager"},
             "e2e": {"value": round(edge_passes * args.steps / e2e_s / 1e9, 4), "unit": "GTEPS",
@@ -481,6 +488,8 @@ def main():
     ap.add_argument("--workload", default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-nodes", type=int, default=6000)
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="halo exchange of the multi-GPU run")
     ap.add_argument("--eager", action="store_true",
                     help="launch every op from Python each step (default: replay one CUDA graph)")
     args = ap.parse_args()

@@ -177,6 +177,10 @@ class HaloExchange:
     def _exchange(self, sends: Dict[int, torch.Tensor], recvs: Dict[int, torch.Tensor]) -> None:
         self.transport.exchange(sends, recvs)
 
+    def begin_step(self) -> None:
+        """Called at the start of every training step (buffer bookkeeping of
+        exchanges that keep per-step buffers; nothing to do here)."""
+
     def gather(self, x_own: torch.Tensor) -> torch.Tensor:
         """x_ext [n_own + n_halo, F]: own rows, then the halo rows from their owners."""
         F = x_own.size(1)
@@ -212,6 +216,146 @@ class HaloExchange:
             if self.plan.send_counts[p]:
                 g_own.index_add_(0, self.send_idx[p], recvs[p])
         return g_own
+
+
+class _DeviceArray:
+    """Zero-copy torch view of a raw device allocation (CUDA array interface)."""
+
+    def __init__(self, ptr: int, shape, device: torch.device):
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": tuple(shape),
+                                         "typestr": "<f4", "strides": None, "version": 3}
+        self.device = device
+
+
+class PeerHaloExchange(HaloExchange):
+    """Halo exchange over NVLink peer memory instead of NCCL point-to-point.
+
+    Every exchange of a step gets its own buffers (allocated on first use with
+    cudaMalloc, shared with the peers through CUDA IPC): for a gather, the
+    extended tensor [own rows | halo rows] into whose halo part the owners
+    store their rows with cign_halo_push; for a scatter_add, the buffer into
+    which the peers store the gradients of the rows this rank sent them.
+    One collective after each push orders the stores before any rank reads.
+    Buffers are reused by the same exchange of the next step; the
+    gradient all-reduce that ends every step orders those writes after the
+    previous step's reads.  Call begin_step() at the start of every step.
+    """
+
+    def __init__(self, plan: HaloPlan, device, group=None):
+        super().__init__(plan, device, TorchP2P(group))
+        from . import _lib
+        self.lib = _lib.load_library()
+        self._lib = _lib
+        self.group = group
+        w = plan.world
+        # every rank's counts, so each rank can address its slots on the peers
+        mine = torch.tensor([plan.n_own] + plan.recv_counts + plan.send_counts,
+                            dtype=torch.int64, device=self.device)
+        allc = [torch.empty_like(mine) for _ in range(w)]
+        dist.all_gather(allc, mine, group=group)
+        allc = [t.cpu().tolist() for t in allc]
+        self.n_own_of = [a[0] for a in allc]
+        self.recv_off_of = [_offsets(a[1:1 + w]) for a in allc]
+        self.send_off_of = [_offsets(a[1 + w:1 + 2 * w]) for a in allc]
+        self.send_begin = torch.tensor(_offsets(plan.send_counts) + [sum(plan.send_counts)],
+                                       dtype=torch.int64, device=self.device)
+        self.recv_begin = torch.tensor(_offsets(plan.recv_counts) + [sum(plan.recv_counts)],
+                                       dtype=torch.int64, device=self.device)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._slots: List[dict] = []
+        self._call = 0
+
+    def begin_step(self) -> None:
+        self._call = 0
+
+    def _alloc_shared(self, rows: int, F: int):
+        """A [rows, F] fp32 buffer of this rank and the base pointers of every
+        rank's buffer of the same slot (all ranks allocate together)."""
+        nbytes = max(int(rows) * int(F) * 4, 16)
+        ptr = self._lib.c_void_p()
+        self._lib.check(self.lib.cign_device_alloc(nbytes, self._lib.ctypes.byref(ptr)),
+                        "cign_device_alloc")
+        handle = (self._lib.ctypes.c_ubyte * 64)()
+        self._lib.check(self.lib.cign_ipc_handle(ptr, handle), "cign_ipc_handle")
+        mine = torch.tensor(list(handle), dtype=torch.uint8, device=self.device)
+        allh = [torch.empty_like(mine) for _ in range(self.plan.world)]
+        dist.all_gather(allh, mine, group=self.group)
+        bases = []
+        for r, h in enumerate(allh):
+            if r == self.plan.rank:
+                bases.append(ptr.value)
+                continue
+            hb = (self._lib.ctypes.c_ubyte * 64)(*h.cpu().tolist())
+            q = self._lib.c_void_p()
+            self._lib.check(self.lib.cign_ipc_open(hb, self._lib.ctypes.byref(q)), "cign_ipc_open")
+            bases.append(q.value)
+        view = torch.as_tensor(_DeviceArray(ptr.value, (rows, F), self.device), device=self.device)
+        return ptr, view, bases
+
+    def _slot(self, kind: str, F: int) -> dict:
+        i = self._call
+        self._call += 1
+        if i < len(self._slots):
+            slot = self._slots[i]
+            if slot["kind"] != kind or slot["F"] != F:
+                raise RuntimeError("exchange sequence changed between steps")
+            return slot
+        me, w = self.plan.rank, self.plan.world
+        if kind == "gather":
+            ptr, view, bases = self._alloc_shared(self.n_own + self.n_halo, F)
+            dst = [bases[p] + (self.n_own_of[p] + self.recv_off_of[p][me]) * F * 4
+                   for p in range(w)]
+        else:  # scatter: peers store gradients of the rows this rank sent them
+            ptr, view, bases = self._alloc_shared(int(self.send_all.numel()), F)
+            dst = [bases[p] + self.send_off_of[p][me] * F * 4 for p in range(w)]
+        slot = {"kind": kind, "F": F, "ptr": ptr, "view": view, "bases": bases,
+                "dst": torch.tensor(dst, dtype=torch.int64, device=self.device)}
+        self._slots.append(slot)
+        return slot
+
+    def _push(self, src, F, idx, begin, dst, total):
+        rc = self.lib.cign_halo_push(self.plan.world, self._lib.ptr(src), F,
+                                     self._lib.ptr(idx) if idx is not None else None,
+                                     self._lib.ptr(begin), self._lib.ptr(dst), int(total),
+                                     self._lib.stream_of(src))
+        self._lib.check(rc, "cign_halo_push")
+        dist.all_reduce(self._flag, group=self.group)  # all stores done before any read
+
+    def gather(self, x_own: torch.Tensor) -> torch.Tensor:
+        x_own = x_own.contiguous()
+        F = int(x_own.size(1))
+        slot = self._slot("gather", F)
+        x_ext = slot["view"]
+        x_ext[:self.n_own].copy_(x_own)
+        self._push(x_own, F, self.send_all, self.send_begin, slot["dst"],
+                   int(self.send_all.numel()))
+        return x_ext
+
+    def scatter_add(self, g_ext: torch.Tensor) -> torch.Tensor:
+        g_ext = g_ext.contiguous()
+        F = int(g_ext.size(1))
+        slot = self._slot("scatter", F)
+        g_own = g_ext[:self.n_own].clone()
+        self._push(g_ext[self.n_own:], F, None, self.recv_begin, slot["dst"], self.n_halo)
+        recv = slot["view"]
+        for p in range(self.plan.world):
+            c = self.plan.send_counts[p]
+            if c:
+                g_own.index_add_(0, self.send_idx[p], recv[self.send_off[p]:self.send_off[p] + c])
+        return g_own
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after the last step)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for slot in self._slots:
+            for r, b in enumerate(slot["bases"]):
+                if r != self.plan.rank:
+                    self.lib.cign_ipc_close(self._lib.c_void_p(b))
+        dist.barrier(group=self.group)
+        for slot in self._slots:
+            self.lib.cign_device_free(slot["ptr"])
+        self._slots = []
 
 
 def _offsets(counts: Sequence[int]) -> List[int]:
@@ -322,10 +466,15 @@ def partition_graph(csr_global: torch.Tensor, gat_rowptr: torch.Tensor, gat_col:
                     world: int, rank: int, device, transport=None):
     """Everything one rank needs: (bounds, HaloPlan, HaloExchange, DistMultiHop,
     DistGatGraph).  csr_global: P as a sparse CSR tensor; gat_rowptr/gat_col:
-    the destination-major CSR of the GAT graph (same sparsity pattern)."""
+    the destination-major CSR of the GAT graph (same sparsity pattern).
+    transport: None (NCCL point-to-point), "peer" (NVLink peer-memory stores,
+    PeerHaloExchange), or a transport object (TorchP2P, StagedGlooP2P, ...)."""
     bounds = partition_rows(csr_global.crow_indices(), world)
     plan = HaloPlan(csr_global.crow_indices(), csr_global.col_indices(), bounds, rank)
-    exchange = HaloExchange(plan, device, transport)
+    if transport == "peer":
+        exchange = PeerHaloExchange(plan, device)
+    else:
+        exchange = HaloExchange(plan, device, transport)
     op = DistMultiHop(csr_global, plan, exchange)
     gat = DistGatGraph(gat_rowptr, gat_col, plan, exchange)
     return bounds, plan, exchange, op, gat

@@ -325,6 +325,30 @@ CIGN_API int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
                   int32_t accumulate_p, float* grad_alpha,
                   cign_stream_t stream);
 
+/* ------------------------------------------------------------ peer memory
+ * Halo exchange of the row-partitioned path over NVLink peer memory
+ * (the reference trains on one GPU: these entry points have no reference
+ * counterpart).
+ * cign_device_alloc/free: plain cudaMalloc'd buffers whose CUDA IPC handles
+ * (CIGN_IPC_HANDLE_BYTES bytes, cign_ipc_handle) other processes map with
+ * cign_ipc_open (peer access enabled lazily) and unmap with cign_ipc_close.
+ * cign_halo_push: for flat row k < total of the send list (peer p owns rows
+ * peer_begin[p] .. peer_begin[p+1]-1; peer_begin is a device array of
+ * n_peers+1 entries), copy row idx[k] of src (row k when idx is NULL) to
+ * peer_dst[p] + (k - peer_begin[p]) * F -- peer_dst is a device array of
+ * n_peers (usually IPC-mapped) pointers.  F % 4 == 0, 16-byte aligned rows.
+ * The copies are ordinary stores; order them against the readers with a
+ * collective (or event) after the launch. */
+#define CIGN_IPC_HANDLE_BYTES 64
+CIGN_API int cign_device_alloc(size_t bytes, void** ptr);
+CIGN_API int cign_device_free(void* ptr);
+CIGN_API int cign_ipc_handle(const void* ptr, void* handle);
+CIGN_API int cign_ipc_open(const void* handle, void** ptr);
+CIGN_API int cign_ipc_close(void* ptr);
+CIGN_API int cign_halo_push(int32_t n_peers, const float* src, int64_t F, const int64_t* idx,
+                            const int64_t* peer_begin, float* const* peer_dst, int64_t total,
+                            cign_stream_t stream);
+
 /* ------------------------------------------------------------ column sum
  * out[j] = sum_i a[i, j] for a row-major [n, c] matrix, in a fixed order
  * (two stages: fixed 128-row chunks, then the chunk partials) -- the bias
