@@ -287,11 +287,13 @@ def hop_roofline(timer, N, nnz, peak, peak_kind, with_traffic=True):
 
 # ------------------------------------------------------- partitioned (N > 1)
 def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
-    """Weak scaling: a power-law graph of world x cfg2 size (same generator,
-    degree law and per-node widths) is row-partitioned over the ranks, so
-    each rank trains a cfg2-sized row range; halo rows move over NCCL once
-    per hop and per GAT layer; parameter gradients are summed with one
-    all-reduce per step."""
+    """cfg2 (the default) scales weakly: a power-law graph of world x cfg2
+    size (same generator, degree law and per-node widths) is row-partitioned
+    over the ranks, so each rank trains a cfg2-sized row range.  Other
+    workloads (e.g. cfg4, the 2.45M-node RMAT graph) scale strongly: the
+    same graph is partitioned over more ranks.  Halo rows move once per hop
+    and per GAT layer; parameter gradients are summed with one all-reduce
+    per step."""
     from dataclasses import replace
 
     import torch.distributed as dist
@@ -305,8 +307,9 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
 
     torch.backends.cuda.matmul.allow_tf32 = True
     lib = _lib.load_library()
-    gcfg = replace(cfg, name=f"{cfg.name}_x{world}", num_nodes=cfg.num_nodes * world,
-                   num_edges=cfg.num_edges * world)
+    weak = args.workload == "cfg2"
+    gcfg = (replace(cfg, name=f"{cfg.name}_x{world}", num_nodes=cfg.num_nodes * world,
+                    num_edges=cfg.num_edges * world) if weak else cfg)
     n = gcfg.num_nodes
     edge = synth.make_edges(gcfg).to(device)
     ei, adj = build_sparse_normalized_adjacency(edge, n)
@@ -323,7 +326,8 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                         gat_heads=cfg.heads, gat_dropout=cfg.gat_dropout).to(device)
     model.prepare_fused_gat_graph(dgat)
     torch.manual_seed(1000 + rank)  # independent dropout streams per rank
-    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5)
+    use_graph = not args.eager
+    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5, capturable=use_graph)
     x_cpu = x_all[r0:r1].contiguous()
     x = x_cpu.to(device)
     y = y_all[r0:r1].to(device)
@@ -344,29 +348,44 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
         opt.step()
         return loss
 
-    for _ in range(args.warmup):
-        step(x)
+    from cign_b200.plans import HopTimer, SpmmPlan
+    hop_timer = HopTimer()
+    graphed = None
+    if use_graph:
+        from cign_b200.graph_step import GraphedStep
+
+        def install_timer():  # the captured step records its local SpMM events
+            SpmmPlan.hop_timer = hop_timer
+
+        graphed = GraphedStep(lambda: step(x), device, warmup=args.warmup,
+                              before_capture=install_timer)
+        SpmmPlan.hop_timer = None
+        run_step = lambda xin: graphed()  # noqa: E731  (x is the graph's static input)
+    else:
+        for _ in range(args.warmup):
+            step(x)
+        run_step = step
     torch.cuda.synchronize()
     launches_before = int(lib.cign_kernel_launches())
     stream = torch.cuda.current_stream(device)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     sampler = ClockSampler(local_rank)
-    from cign_b200.plans import HopTimer, SpmmPlan
-    hop_timer = HopTimer()
     dist.barrier()
     torch.cuda.synchronize()
-    SpmmPlan.hop_timer = hop_timer  # events around every local row-block SpMM
+    if not use_graph:
+        SpmmPlan.hop_timer = hop_timer  # events around every local row-block SpMM
     sampler.start()
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
-        step(x)
+        run_step(x)
         ends[i].record(stream)
     torch.cuda.synchronize()
     SpmmPlan.hop_timer = None
     clocks = sampler.stop()
-    launches = int(lib.cign_kernel_launches()) - launches_before
+    launches = (graphed.native_launches * args.steps if use_graph
+                else int(lib.cign_kernel_launches()) - launches_before)
     step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
     total_s = sum(step_ms) * 1e-3
     t = torch.tensor([total_s], device=device, dtype=torch.float64)
@@ -381,7 +400,7 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     e0.record(stream)
     for _ in range(args.steps):
         x.copy_(x_pin, non_blocking=True)
-        loss_host = float(step(x).item())
+        loss_host = float(run_step(x).item())
     e1.record(stream)
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) * 1e-3], device=device, dtype=torch.float64)
@@ -389,6 +408,9 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     e2e_s = float(t.item())
     halo = torch.tensor([hplan.n_halo], device=device, dtype=torch.float64)
     dist.all_reduce(halo)
+    if graphed is not None:
+        del graphed  # release the graph (it holds collectives) before the buffers go
+        torch.cuda.synchronize()
     if hasattr(exch, "close"):
         exch.close()
     if rank == 0:
@@ -398,7 +420,8 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
             "value": round(edge_passes * args.steps / total_s / 1e9, 4), "unit": "GTEPS",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(total_s / args.steps * 1e3, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
             "config": {"workload": gcfg.name, "nodes": n, "directed_edges": gcfg.num_edges,
                        "nnz_P": nnz, "nodes_per_gpu": n // world, "in_dim": cfg.in_dim,
                        "hidden": cfg.hidden_dim, "hops": list(cfg.hops), "heads": cfg.heads,
@@ -410,7 +433,8 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                                      "(cign_halo_push)") +
                                     "; one gradient all-reduce per step"),
                        "halo_rows_total": int(halo.item()),
-                       "l2": "flushed between timed steps (256 MiB write)", "launch": "eager"},
+                       "l2": "flushed between timed steps (256 MiB write)",
+                       "launch": "one CUDA graph per step" if use_graph else "eager"},
             "e2e": {"value": round(edge_passes * args.steps / e2e_s / 1e9, 4), "unit": "GTEPS",
                     "h2d_bytes_per_step": int(x_cpu.numel() * 4), "d2h_bytes_per_step": 4,
                     "ms_per_step": round(e2e_s / args.steps * 1e3, 4)},
