@@ -129,7 +129,7 @@ def build_graph(cfg, device):
                                           prepare_fixed_csr_operator, prepare_gat_edge_index,
                                           to_graph_format)
     from cign_b200.multihop_csr_pipeline import prepare_multihop_csr_operator
-    edge = synth.make_edges(cfg).to(device)
+    edge = synth.make_edges(cfg, device=device).to(device)
     n = cfg.num_nodes
     ei, adj = build_sparse_normalized_adjacency(edge, n)
     base = prepare_fixed_csr_operator(adj)
@@ -311,7 +311,7 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     gcfg = (replace(cfg, name=f"{cfg.name}_x{world}", num_nodes=cfg.num_nodes * world,
                     num_edges=cfg.num_edges * world) if weak else cfg)
     n = gcfg.num_nodes
-    edge = synth.make_edges(gcfg).to(device)
+    edge = synth.make_edges(gcfg, device=device).to(device)
     ei, adj = build_sparse_normalized_adjacency(edge, n)
     base = prepare_fixed_csr_operator(adj)
     (rp, c), _, _ = to_graph_format(prepare_gat_edge_index(ei, n).flip(0), n)
@@ -450,6 +450,93 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     return 0
 
 
+# ------------------------------------------------------------------ sweep
+def run_sweep(args, device):
+    """isolated kernel sweep on the cfg2 graph.  One JSON line per
+    case: k-hop SpMM (hops 1..8, F in {64, 128, 512}; forward chain and its
+    transposed backward) next to cuSPARSE (torch.sparse.mm, the library the
+    reference's MultiHopCsrPlan calls); the collapsed GAT layer with 1/4/8
+    heads (aggregate-first form, forward + backward, and the drop-in form);
+    the Clifford pack and its proj mix GEMM at 8 and 16 blades with the
+    contraction in TF32 and in FP32.  Device times from CUDA events."""
+    from cign_b200 import _pack, collapsed_gat, synth
+    from cign_b200.plans import gat_plan_for
+    cfg = synth.CONFIGS["cfg2"]
+    op, gat_graph, nnz, nnz_g = build_graph(cfg, device)
+    plan = op.plan.spmm
+    N = cfg.num_nodes
+    stream = torch.cuda.current_stream(device)
+    g = torch.Generator(device=device).manual_seed(3)
+    csr = op.base.csr if hasattr(op, "base") else None
+
+    def emit(d):
+        d.update({"sweep": "configs[2]", "graph": cfg.name, "nodes": N, "nnz_P": nnz})
+        print(json.dumps(d), flush=True)
+
+    for F in (64, 128, 512):
+        X = torch.randn(N, F, device=device, generator=g)
+        for K in range(1, 9):
+            t_f = time_launches(lambda: plan.forward(X, K), 5, stream)
+            gs = [torch.randn(N, F, device=device, generator=g) for _ in range(K)]
+            t_b = time_launches(lambda: plan.backward(gs, F), 5, stream)
+            line = {"op": "multihop_spmm", "F": F, "hops": K,
+                    "fwd_ms": round(t_f * 1e3, 4), "bwd_ms": round(t_b * 1e3, 4),
+                    "gteps": round(2 * K * nnz / (t_f + t_b) / 1e9, 3)}
+            if csr is not None:
+                def cus():
+                    y = X
+                    for _ in range(K):
+                        y = torch.sparse.mm(csr, y)
+                    return y
+                line["cusparse_fwd_ms"] = round(time_launches(cus, 5, stream) * 1e3, 4)
+            emit(line)
+    (rp, c), (r, cp), perm = gat_graph
+    gplan = gat_plan_for(rp, c, r, cp, perm)
+    D = cfg.hidden_dim
+    for H in (1, 4, 8):
+        x = torch.randn(N, D, device=device, generator=g)
+        a = torch.randn(N, H, device=device, generator=g)
+        z, emax, esum = collapsed_gat.gat_agg_forward_raw(gplan, a, a, x, H, 0.2, 0.5, 7)
+        U = torch.randn(N, H * D, device=device, generator=g)
+        gp = torch.randn(N, D, device=device, generator=g)
+        t_af = time_launches(lambda: collapsed_gat.gat_agg_forward_raw(gplan, a, a, x, H, 0.2, 0.5, 7),
+                             5, stream)
+        t_ab = time_launches(lambda: collapsed_gat.gat_agg_backward_raw(
+            gplan, a, a, x, emax, esum, U, gp, 0.2, 0.5, 7), 5, stream)
+        xin = torch.randn(N, H, D, device=device, generator=g)
+        bias = torch.zeros(D, device=device)
+        t_cf = time_launches(lambda: collapsed_gat.gat_forward_raw(gplan, a, a, xin, bias, 0.2, 0.5, 7),
+                             5, stream)
+        out, pre, em2, es2 = collapsed_gat.gat_forward_raw(gplan, a, a, xin, bias, 0.2, 0.5, 7)
+        t_cb = time_launches(lambda: collapsed_gat.gat_backward_raw(
+            gplan, a, a, xin, pre, em2, es2, gp, 0.2, 0.5, 7), 5, stream)
+        emit({"op": "collapsed_gat", "heads": H, "channels": D,
+              "aggregate_first_fwd_ms": round(t_af * 1e3, 4),
+              "aggregate_first_bwd_ms": round(t_ab * 1e3, 4),
+              "drop_in_fwd_ms": round(t_cf * 1e3, 4), "drop_in_bwd_ms": round(t_cb * 1e3, 4)})
+    K = 3
+    for blades in (8, 16):
+        Dp = 64 * blades
+        Hn = torch.randn(N, Dp, device=device, generator=g)
+        Cn = torch.randn(N, Dp, device=device, generator=g)
+        props = [torch.randn(N, 2 * Dp, device=device, generator=g) for _ in range(K)]
+        alpha = torch.softmax(torch.randn(N, K, device=device, generator=g), -1)
+        W = torch.randn(Dp, 2 * K * Dp, device=device, generator=g) / (2 * K * Dp) ** 0.5
+        t_pf = time_launches(lambda: _pack.pack_forward(Hn, Cn, props, alpha, 1, 0, 0), 5, stream)
+        G = _pack.pack_forward(Hn, Cn, props, alpha, 1, 0, 0)
+        line = {"op": "clifford_pack_mix", "blades": blades, "D": Dp, "hops": K,
+                "pack_fwd_ms": round(t_pf * 1e3, 4)}
+        for name, tf32 in (("tf32", True), ("fp32", False)):
+            prev = torch.backends.cuda.matmul.allow_tf32
+            torch.backends.cuda.matmul.allow_tf32 = tf32
+            t_mm = time_launches(lambda: G.mm(W.t()), 5, stream)
+            torch.backends.cuda.matmul.allow_tf32 = prev
+            line[f"mix_{name}_ms"] = round(t_mm * 1e3, 4)
+            line[f"mix_{name}_tflops"] = round(2 * N * 2 * K * Dp * Dp / t_mm / 1e12, 1)
+        emit(line)
+    return 0
+
+
 # ------------------------------------------------------------------ CPU arm
 def cpu_sample_config(cfg, sample_nodes):
     from dataclasses import replace
@@ -512,6 +599,9 @@ def main():
     ap.add_argument("--workload", default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-nodes", type=int, default=6000)
+    ap.add_argument("--sweep", action="store_true",
+                    help="configs[2] isolated kernel sweep (one JSON line per case) instead of "
+                         "the training-step benchmark")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="halo exchange of the multi-GPU run")
     ap.add_argument("--eager", action="store_true",
@@ -574,6 +664,8 @@ def main():
 
     from cign_b200 import _lib
     lib = _lib.load_library()
+    if args.sweep:
+        return run_sweep(args, device)
 
     op, gat_graph, nnz, nnz_g = build_graph(cfg, device)
     use_graph = not args.eager
