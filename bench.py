@@ -20,9 +20,13 @@ pinned host memory and the loss read back every step.
 in oracle/, run on all host cores) on a bounded sample of the workload (the
 same graph family at a smaller N); there is no GPU in that arm.
 
-With --gpus N > 1 (torchrun, NCCL) every rank runs an independent replica of
-the workload (weak scaling, no data-path collective); `value` is the sum of
-the ranks' edge-passes over the slowest rank's time.
+With --gpus N > 1 (torchrun, NCCL) the graph is row-partitioned over the
+ranks with a halo exchange per hop and per GAT layer and one gradient
+all-reduce per step: cfg2 scales weakly (an N x cfg2 graph, a cfg2-sized row
+range per rank), other workloads (--workload cfg4, the 2.45M-node RMAT
+graph) strongly.  `value` is the whole job's edge-passes over the slowest
+rank's time.  Workloads above GRAPH_CAPTURE_MAX_NODES nodes run eagerly;
+smaller ones replay each step as one CUDA graph (--eager to opt out).
 """
 from __future__ import annotations
 
@@ -46,6 +50,7 @@ PEAKS_PATH = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_PATH = ROOT / "profiles" / "traffic.json"
 FALLBACK_HBM_GBS = 6650.0
 L2_FLUSH_BYTES = 256 << 20
+GRAPH_CAPTURE_MAX_NODES = 1_000_000  # larger workloads run eagerly
 
 
 # ------------------------------------------------------------------ helpers
@@ -176,6 +181,14 @@ def algorithmic_bytes(kind, N, nnz, F=0, H=0, C=0, K=0, D=0, nnz_g=0):
     if kind == "gat_bwd":
         return (8 * (N + 1) + 12 * nnz_g + 8 * N * H + 4 * N * H * C + 8 * N * C + 8 * N * H
                 + 4 * N * H * C + 8 * N * H + 4 * C)
+    if kind == "gat_agg_fwd":
+        return 4 * (N + 1) + 4 * nnz_g + 8 * N * H + 4 * N * D + 4 * N * H * D + 8 * N * H
+    if kind == "gat_agg_bwd":
+        return (8 * (N + 1) + 12 * nnz_g + 24 * N * H + 4 * N * D + 4 * N * H * D + 4 * N * C
+                + 4 * N * H * C)
+    if kind == "pack_proj":  # G written for the backward (keep_g)
+        return (8 * N * D + 8 * K * N * D + 4 * N * K + 8 * K * N * D + 4 * C * 2 * K * D
+                + 4 * N * C + 4 * C)
     if kind == "pack_fwd":
         return 8 * N * D + 8 * K * N * D + 4 * N * K + 8 * K * N * D
     if kind == "pack_bwd":
@@ -212,15 +225,17 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device):
     t_spmm_add = time_launches(lambda: plan.spmm(X, transpose=True, addend=G), 20, stream)
     (rp, c), (r, cp), perm = gat_graph
     gplan = gat_plan_for(rp, c, r, cp, perm)
-    xin = torch.randn(N, H, D, device=device, generator=g)
+    x = torch.randn(N, D, device=device, generator=g)
     a = torch.randn(N, H, device=device, generator=g)
-    bias = torch.zeros(D, device=device)
-    fwd = lambda: collapsed_gat.gat_forward_raw(gplan, a, a, xin, bias, 0.2, cfg.gat_dropout, 7)
+    fwd = lambda: collapsed_gat.gat_agg_forward_raw(gplan, a, a, x, H, 0.2, cfg.gat_dropout, 7)
     t_gat_fwd = time_launches(fwd, 10, stream)
-    out, pre, emax, esum = fwd()
-    gy = torch.randn(N, D, device=device, generator=g)
-    t_gat_bwd = time_launches(lambda: collapsed_gat.gat_backward_raw(
-        gplan, a, a, xin, pre, emax, esum, gy, 0.2, cfg.gat_dropout, 7), 10, stream)
+    z, emax, esum = fwd()
+    del z
+    gz = torch.randn(N, H * D, device=device, generator=g)
+    gpre = torch.randn(N, D, device=device, generator=g)
+    t_gat_bwd = time_launches(lambda: collapsed_gat.gat_agg_backward_raw(
+        gplan, a, a, x, emax, esum, gz, gpre, 0.2, cfg.gat_dropout, 7), 10, stream)
+    del gz, gpre
     Hn = torch.randn(N, D, device=device, generator=g)
     Cn = torch.randn(N, D, device=device, generator=g)
     props = [torch.randn(N, 2 * D, device=device, generator=g) for _ in range(K)]
@@ -229,11 +244,22 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device):
     go = torch.randn(N, 2 * K * D, device=device, generator=g)
     t_pack_b = time_launches(lambda: _pack.pack_backward(go, Hn, Cn, props, alpha, 1, 0, 0, True),
                              20, stream)
+    del go
+    Wp = torch.randn(D, 2 * K * D, device=device, generator=g) / (2 * K * D) ** 0.5
+    bp = torch.zeros(D, device=device)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    t_pp = time_launches(lambda: _pack.pack_proj_forward(Hn, Cn, props, alpha, Wp, bp, True), 20,
+                         stream)
+    torch.backends.cuda.matmul.allow_tf32 = prev
     rows = {
         "spmm_fwd_hop": (t_spmm, L * K, algorithmic_bytes("spmm", N, nnz, F=Fw)),
         "spmm_bwd_hop_fused_add": (t_spmm_add, L * K, algorithmic_bytes("spmm_add", N, nnz, F=Fw)),
-        "gat_fwd": (t_gat_fwd, L, algorithmic_bytes("gat_fwd", N, nnz, H=H, C=D, nnz_g=nnz_g)),
-        "gat_bwd": (t_gat_bwd, L, algorithmic_bytes("gat_bwd", N, nnz, H=H, C=D, nnz_g=nnz_g)),
+        "gat_agg_fwd": (t_gat_fwd, L, algorithmic_bytes("gat_agg_fwd", N, nnz, H=H, D=D,
+                                                        nnz_g=nnz_g)),
+        "gat_agg_bwd": (t_gat_bwd, L, algorithmic_bytes("gat_agg_bwd", N, nnz, H=H, C=D, D=D,
+                                                        nnz_g=nnz_g)),
+        "pack_proj_tcgen05_fwd": (t_pp, L, algorithmic_bytes("pack_proj", N, nnz, K=K, D=D, C=D)),
         "pack_fwd": (t_pack_f, L, algorithmic_bytes("pack_fwd", N, nnz, K=K, D=D)),
         "pack_bwd": (t_pack_b, L, algorithmic_bytes("pack_bwd", N, nnz, K=K, D=D)),
     }
@@ -533,6 +559,15 @@ def run_sweep(args, device):
             torch.backends.cuda.matmul.allow_tf32 = prev
             line[f"mix_{name}_ms"] = round(t_mm * 1e3, 4)
             line[f"mix_{name}_tflops"] = round(2 * N * 2 * K * Dp * Dp / t_mm / 1e12, 1)
+        if _pack.pack_proj_supported(Dp, K, Dp):
+            # pack + mix as one tcgen05 GEMM with the pack as its A-operand prologue
+            bias = torch.zeros(Dp, device=device)
+            for keep in (False, True):
+                t_pp = time_launches(lambda: _pack.pack_proj_forward(
+                    Hn, Cn, props, alpha, W, bias, keep), 5, stream)
+                key = "pack_mix_tcgen05" + ("_with_g" if keep else "")
+                line[f"{key}_ms"] = round(t_pp * 1e3, 4)
+                line[f"{key}_tflops"] = round(2 * N * 2 * K * Dp * Dp / t_pp / 1e12, 1)
         emit(line)
     return 0
 
@@ -617,6 +652,10 @@ def main():
     from cign_b200 import synth
     cfg = synth.CONFIGS[args.workload]
     metric = "CIGN fwd+bwd train-step GTEPS (SpMM edge-passes/s)"
+    if cfg.num_nodes > GRAPH_CAPTURE_MAX_NODES:
+        # launch overhead is negligible at this size, and a captured step would
+        # hold a second copy of the activations in the graph's private pool
+        args.eager = True
 
     if args.impl == "reference":
         # CPU reference arm: rank 0 only; other ranks exit without work.
@@ -782,7 +821,8 @@ def main():
     result = None
     if rank == 0:
         peak, peak_kind = load_peaks()
-        kernels = kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device)
+        kernels = (kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device)
+                   if cfg.num_nodes <= GRAPH_CAPTURE_MAX_NODES else None)
         roofline = hop_roofline(hop_timer, cfg.num_nodes, nnz, peak, peak_kind)
         if roofline is not None and use_graph:
             roofline["timing"] = ("CUDA events captured around every k-hop call inside the step "

@@ -32,6 +32,52 @@ def pack_forward(H, C, props: Sequence[torch.Tensor], alpha: Optional[torch.Tens
     return out
 
 
+def pack_proj_supported(D: int, K: int, dout: int) -> bool:
+    """Shapes the tcgen05 pack + proj GEMM (cign_pack_proj_gemm_tf32) takes."""
+    return D % 32 == 0 and 1 <= K <= 8 and dout % 32 == 0 and 32 <= dout <= 512
+
+
+def pack_proj_call(H, C, props: Sequence[torch.Tensor], alpha: torch.Tensor,
+                   weight: torch.Tensor, bias: torch.Tensor, keep_g: bool):
+    """(out, G or None, workspace) of one cign_pack_proj_gemm_tf32 call; the
+    workspace holds the device status word that pack_proj_status reads."""
+    lib = _lib.load_library()
+    n, D = (int(s) for s in H.shape)
+    K = len(props)
+    dout = int(weight.size(0))
+    weight = weight.contiguous()
+    out = torch.empty((n, dout), dtype=torch.float32, device=H.device)
+    G = torch.empty((n, 2 * K * D), dtype=torch.float32, device=H.device) if keep_g else None
+    ws = _lib.workspace(lib.cign_pack_proj_workspace_bytes(D, K, dout), H.device)
+    with _lib.DeviceGuard(H.device):
+        rc = lib.cign_pack_proj_gemm_tf32(n, D, K, dout, _lib.ptr(H), _lib.ptr(C),
+                                          _lib.ptr_array(props), 2 * D, _lib.ptr(alpha),
+                                          _lib.ptr(weight), _lib.ptr(bias.contiguous()),
+                                          _lib.ptr(out), _lib.ptr(G), _lib.ptr(ws), ws.numel(),
+                                          _lib.stream_of(H))
+    _lib.check(rc, "cign_pack_proj_gemm_tf32")
+    return out, G, ws
+
+
+def pack_proj_forward(H, C, props: Sequence[torch.Tensor], alpha: torch.Tensor,
+                      weight: torch.Tensor, bias: torch.Tensor, keep_g: bool):
+    """(G @ weight.T + bias, G or None) for G = pack(H, C, props, alpha) with the
+    production switches (interaction "new", outer none, weighting "old"),
+    G never stored unless keep_g; TF32 tensor-core products, fp32 sums."""
+    out, G, _ = pack_proj_call(H, C, props, alpha, weight, bias, keep_g)
+    return out, G
+
+
+def pack_proj_status(ws: torch.Tensor, D: int, K: int, dout: int) -> None:
+    """Raise if a bounded device-side wait of the call that used `ws` expired
+    (synchronises the current stream)."""
+    lib = _lib.load_library()
+    with _lib.DeviceGuard(ws.device):
+        rc = lib.cign_pack_proj_status(_lib.ptr(ws), int(D), int(K), int(dout),
+                                       _lib.stream_of(ws))
+    _lib.check(rc, "cign_pack_proj_status")
+
+
 def pack_backward(grad_out, H, C, props, alpha, interaction, outer, weighting, need_alpha: bool):
     lib = _lib.load_library()
     n, D = (int(s) for s in H.shape)

@@ -23,11 +23,14 @@ import torch
 
 from . import _lib, _pack
 from .hop_gate import hop_gate_backward_raw, hop_gate_forward_raw
+from .linear import _weight_grad, colsum
 from .multihop_csr_pipeline import (GenericMultiHopCSRGraphOperator,
                                     HybridNative3TailCSRGraphOperator, MultiHopCSR3GraphOperator)
 from .plans import SpmmPlan, spmm_plan_for
 
 PACK_MODES = (1, 0, 0)  # interaction "new", outer none, weighting "old"
+# pack + proj on the tcgen05 pack-prologue GEMM when TF32 matmuls are allowed
+USE_TCGEN05_PACK_PROJ = True
 
 
 def native_spmm_plan(operator) -> Optional[SpmmPlan]:
@@ -48,9 +51,7 @@ class _PropagateGatePackFn(torch.autograd.Function):
         H = H.contiguous()
         C = C.contiguous()
         D = H.size(1)
-        max_power = max(order_set)
-        ys = plan.forward(torch.cat([H, C], 1), max_power)
-        props = [ys[p - 1] for p in order_set]
+        props = _propagate(H, C, plan, order_set)
         alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
         G = _pack.pack_forward(H, C, props, alpha, *PACK_MODES)
         ctx.save_for_backward(H, C, gate_w, alpha, *props)
@@ -60,18 +61,82 @@ class _PropagateGatePackFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gG):
         H, C, gate_w, alpha, *props = ctx.saved_tensors
-        D = ctx.D
-        gH, gC, gP, gA = _pack.pack_backward(gG.contiguous(), H, C, props, alpha, *PACK_MODES,
-                                             need_alpha=True)
-        grads = [None] * max(ctx.order_set)
-        for p, g in zip(ctx.order_set, gP):
-            grads[p - 1] = g
-        gHC = ctx.plan.backward(grads, 2 * D)  # dL/d[H | C] through the propagation
-        add_c = _lib.c_void_p(gHC.data_ptr() + D * gHC.element_size())  # right half
-        gw, gb = hop_gate_backward_raw(H, C, gate_w, alpha, gA, ctx.gate_mode, gH, gC,
-                                       accumulate=True, add_h=_lib.ptr(gHC), add_c=add_c,
-                                       add_ld=2 * D)
+        gH, gC, gw, gb = _gate_pack_backward(ctx, gG, H, C, gate_w, alpha, props)
         return gH, gC, gw, gb, None, None, None
+
+
+def _propagate(H, C, plan, order_set):
+    ys = plan.forward(torch.cat([H, C], 1), max(order_set))
+    return [ys[p - 1] for p in order_set]
+
+
+def _gate_pack_backward(ctx, gG, H, C, gate_w, alpha, props):
+    """pack backward -> transposed k-hop propagation -> hop-gate backward, the
+    last one adding the pack's and the propagation's gradients into
+    (grad H_norm, grad C_norm) in the same pass."""
+    D = ctx.D
+    gH, gC, gP, gA = _pack.pack_backward(gG.contiguous(), H, C, props, alpha, *PACK_MODES,
+                                         need_alpha=True)
+    grads = [None] * max(ctx.order_set)
+    for p, g in zip(ctx.order_set, gP):
+        grads[p - 1] = g
+    del gP
+    gHC = ctx.plan.backward(grads, 2 * D)  # dL/d[H | C] through the propagation
+    del grads
+    add_c = _lib.c_void_p(gHC.data_ptr() + D * gHC.element_size())  # right half
+    gw, gb = hop_gate_backward_raw(H, C, gate_w, alpha, gA, ctx.gate_mode, gH, gC,
+                                   accumulate=True, add_h=_lib.ptr(gHC), add_c=add_c,
+                                   add_ld=2 * D)
+    return gH, gC, gw, gb
+
+
+class _PropagateGatePackProjFn(torch.autograd.Function):
+    """The same node followed by the block's proj linear layer.
+
+    With TF32 matmuls allowed (torch.backends.cuda.matmul.allow_tf32) and
+    supported shapes, pack and proj run as one tcgen05 GEMM whose A operand
+    is the pack, evaluated tile by tile in shared memory
+    (cign_pack_proj_gemm_tf32); otherwise as the pack kernel and an fp32
+    addmm.  keep_g=False (graphs where G_raw [N, 2KD] is too large to keep)
+    stores no G_raw: the backward recomputes it (one pack pass, bit-identical)
+    for the proj weight gradient."""
+
+    @staticmethod
+    def forward(ctx, H, C, gate_w, gate_b, proj_w, proj_b, plan, order_set, gate_mode, keep_g):
+        H = H.contiguous()
+        C = C.contiguous()
+        props = _propagate(H, C, plan, order_set)
+        alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
+        D, K = H.size(1), len(props)
+        if (USE_TCGEN05_PACK_PROJ and torch.backends.cuda.matmul.allow_tf32
+                and _pack.pack_proj_supported(D, K, proj_w.size(0))):
+            out, G = _pack.pack_proj_forward(H, C, props, alpha, proj_w, proj_b, keep_g)
+        else:
+            G = _pack.pack_forward(H, C, props, alpha, *PACK_MODES)
+            out = torch.addmm(proj_b, G, proj_w.t())
+            if not keep_g:
+                G = None
+        saved = [H, C, gate_w, alpha, proj_w, *props]
+        ctx.keep_g = G is not None
+        if ctx.keep_g:
+            saved.append(G)
+        ctx.save_for_backward(*saved)
+        ctx.plan, ctx.order_set, ctx.gate_mode, ctx.D = plan, tuple(order_set), gate_mode, D
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        H, C, gate_w, alpha, proj_w, *rest = ctx.saved_tensors
+        K = len(ctx.order_set)
+        props = rest[:K]
+        g = g.contiguous()
+        G = rest[K] if ctx.keep_g else _pack.pack_forward(H, C, props, alpha, *PACK_MODES)
+        g_proj_w = _weight_grad(g, G)
+        del G
+        g_proj_b = colsum(g)
+        gG = g.mm(proj_w)
+        gH, gC, gw, gb = _gate_pack_backward(ctx, gG, H, C, gate_w, alpha, props)
+        return gH, gC, gw, gb, g_proj_w, g_proj_b, None, None, None, None
 
 
 def propagate_gate_pack(H_norm: torch.Tensor, C_norm: torch.Tensor, gate_w: torch.Tensor,
@@ -82,3 +147,16 @@ def propagate_gate_pack(H_norm: torch.Tensor, C_norm: torch.Tensor, gate_w: torc
         raise ValueError("order_set must hold distinct positive hop counts")
     return _PropagateGatePackFn.apply(H_norm, C_norm, gate_w, gate_b, plan, order,
                                       1 if score_mode == "new" else 0)
+
+
+def propagate_gate_pack_proj(H_norm: torch.Tensor, C_norm: torch.Tensor, gate_w: torch.Tensor,
+                             gate_b: torch.Tensor, plan: SpmmPlan, order_set: Sequence[int],
+                             score_mode: str, proj_w: torch.Tensor, proj_b: torch.Tensor,
+                             keep_g: bool = True) -> torch.Tensor:
+    """linear(propagate_gate_pack(...), proj_w, proj_b) as one node; keep_g=False
+    recomputes G_raw in the backward instead of keeping it."""
+    order = tuple(int(p) for p in order_set)
+    if len(set(order)) != len(order) or min(order) < 1:
+        raise ValueError("order_set must hold distinct positive hop counts")
+    return _PropagateGatePackProjFn.apply(H_norm, C_norm, gate_w, gate_b, proj_w, proj_b, plan,
+                                          order, 1 if score_mode == "new" else 0, bool(keep_g))

@@ -254,7 +254,11 @@ def _head_projection(weight: torch.Tensor, heads: int) -> torch.Tensor:
 
 class _AggregateFirstGATFn(torch.autograd.Function):
     """SiLU(mean_h sum_j w_ijh (lin.weight_h x_j) + bias) computed as
-    SiLU(z.view(N, H*D) @ M + bias) with z = cign_gat_agg_fwd(x)."""
+    SiLU(z.view(N, H*D) @ M + bias) with z = cign_gat_agg_fwd(x).
+
+    z is not kept for the backward: the weight gradient sum_i z_i^T g_pre_i
+    equals sum_j gfeat_j^T x_j (gfeat = the gradient of lin(x).view(N,H,C),
+    which the backward kernels produce anyway), so only x is saved."""
 
     @staticmethod
     def forward(ctx, x, attn_row, attn_col, weight, bias, plan, heads, negative_slope, attn_drop,
@@ -265,29 +269,29 @@ class _AggregateFirstGATFn(torch.autograd.Function):
                                             attn_drop, seed)
         M = _head_projection(weight, H)
         lin = z.view(n, H * D).mm(M)
+        del z
         out, pre = _bias_silu(lin, bias)
-        ctx.save_for_backward(x, attn_row, attn_col, weight, z, pre, emax, esum)
+        ctx.save_for_backward(x, attn_row, attn_col, weight, pre, emax, esum)
         ctx.plan, ctx.heads = plan, H
         ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), seed
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        x, attn_row, attn_col, weight, z, pre, emax, esum = ctx.saved_tensors
+        x, attn_row, attn_col, weight, pre, emax, esum = ctx.saved_tensors
         H = ctx.heads
-        n, D = int(z.size(0)), int(x.size(1))
         n_cols = int(x.size(0))
         C = weight.size(0) // H
         g_pre, grad_bias = _bias_silu_backward(grad_out, pre)
         M = _head_projection(weight, H)
-        z2 = z.view(n, H * D)
-        grad_M = z2.t().mm(g_pre)                                   # [H*D, C]
-        grad_w = grad_M.view(H, D, C).permute(0, 2, 1).reshape(H * C, D) / H
         grad_z = g_pre.mm(M.t())                                    # [N, H*D]
         gfeat, grow, gcol = gat_agg_backward_raw(ctx.plan, attn_row, attn_col, x, emax, esum,
                                                  grad_z, g_pre, ctx.negative_slope,
                                                  ctx.attn_drop, ctx.seed)
-        grad_x = gfeat.view(n_cols, H * C).mm(weight)               # [N_cols, D]
+        del grad_z
+        gfeat2 = gfeat.view(n_cols, H * C)
+        grad_w = gfeat2.t().mm(x)                                   # [H*C, D]
+        grad_x = gfeat2.mm(weight)                                  # [N_cols, D]
         return grad_x, grow, gcol, grad_w, grad_bias, None, None, None, None, None
 
 

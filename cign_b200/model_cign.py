@@ -41,7 +41,7 @@ from .collapsed_gat import collapsed_gat_aggregate_first, collapsed_gat_mean_bia
 from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, fused_dropout_layernorm
 from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
-from .block_fused import native_spmm_plan, propagate_gate_pack
+from .block_fused import native_spmm_plan, propagate_gate_pack_proj
 from .hop_gate import fused_hop_gate
 from .linear import linear
 
@@ -148,6 +148,16 @@ class GraphCliffordBlock(nn.Module):
         self.hop_gate_mlp = nn.Linear(2 * hidden_dim, self.num_hops, bias=True)
         self.gamma = nn.Parameter(torch.full((hidden_dim,), float(init_gamma)))
 
+    # G_raw [N, 2*K*D] at or above this size is recomputed in the backward
+    # instead of being kept (None: decide by size; True/False: always/never)
+    recompute_pack = None
+    RECOMPUTE_PACK_BYTES = 4 << 30
+
+    def _recompute_pack(self, H_norm) -> bool:
+        if self.recompute_pack is not None:
+            return bool(self.recompute_pack)
+        return H_norm.size(0) * 2 * self.num_hops * self.hidden_dim * 4 >= self.RECOMPUTE_PACK_BYTES
+
     def compute_hop_gate(self, H_norm, C_norm):
         if H_norm.size(1) % 4 == 0 and self.num_hops <= 8 and H_norm.is_cuda:
             return fused_hop_gate(H_norm, C_norm, self.hop_gate_mlp.weight, self.hop_gate_mlp.bias,
@@ -170,10 +180,10 @@ class GraphCliffordBlock(nn.Module):
                 and H_norm.size(1) % 4 == 0 and self.num_hops <= 8
                 and len(set(self.order_set)) == self.num_hops and min(self.order_set) >= 1):
             # propagation + hop gate + pack as one node (gradients merged in-kernel)
-            G_raw = propagate_gate_pack(H_norm, C_norm, self.hop_gate_mlp.weight,
-                                        self.hop_gate_mlp.bias, plan, self.order_set,
-                                        self.alpha_score_mode)
-            G_feat = linear(G_raw, self.proj.weight, self.proj.bias)
+            args = (H_norm, C_norm, self.hop_gate_mlp.weight, self.hop_gate_mlp.bias, plan,
+                    self.order_set, self.alpha_score_mode)
+            G_feat = propagate_gate_pack_proj(*args, self.proj.weight, self.proj.bias,
+                                              keep_g=not self._recompute_pack(H_norm))
             return fused_dropout_gamma_residual(H, G_feat, self.gamma, p)
         HC = torch.cat([H_norm, C_norm], dim=-1)
         propagated = selected_sparse_powers(graph_operator, HC, self.order_set)

@@ -325,6 +325,28 @@ CIGN_API int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
                   int32_t accumulate_p, float* grad_alpha,
                   cign_stream_t stream);
 
+/* ------------------------------------------------------- pack + proj GEMM
+ * out[n,:] = G[n,:] @ W^T + bias with G = pack(H, C, P_1..P_K, alpha) in the
+ * production switches (interaction "new", outer none, weighting "old"),
+ * on tcgen05 tensor cores in TF32 with fp32 accumulation.  Replaces the
+ * pack call (fused_clifford_switch_pack(..., "new", "old"),
+ * generic_engine/model_cign.py:869-876) followed by the proj linear layer
+ * (model_cign.py:927-929).  W is [dout, 2*K*d] row-major, bias [dout]; P as in
+ * cign_pack_fwd (ldp >= 2d, 16-byte aligned rows).  G is never stored unless
+ * g_out is non-NULL ([n, 2*K*d], written exactly as cign_pack_fwd writes it).
+ * Requires d % 32 == 0, 1 <= K <= 8, dout % 32 == 0 and dout <= 512.
+ * The workspace holds W re-laid out for the MMA plus a status word that
+ * cign_pack_proj_status reads (CIGN_ERR_TIMEOUT if a bounded device-side
+ * wait expired; it synchronises `stream`). */
+CIGN_API size_t cign_pack_proj_workspace_bytes(int64_t d, int32_t k, int64_t dout);
+CIGN_API int cign_pack_proj_gemm_tf32(int64_t n, int64_t d, int32_t k, int64_t dout,
+                             const float* H, const float* C, const float* const* P,
+                             int64_t ldp, const float* alpha, const float* W,
+                             const float* bias, float* out, float* g_out, void* ws,
+                             size_t ws_bytes, cign_stream_t stream);
+CIGN_API int cign_pack_proj_status(const void* ws, int64_t d, int32_t k, int64_t dout,
+                          cign_stream_t stream);
+
 /* ------------------------------------------------------------ peer memory
  * Halo exchange of the row-partitioned path over NVLink peer memory
  * (the reference trains on one GPU: these entry points have no reference
