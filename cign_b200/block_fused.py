@@ -30,7 +30,8 @@ from .plans import SpmmPlan, spmm_plan_for
 
 PACK_MODES = (1, 0, 0)  # interaction "new", outer none, weighting "old"
 # pack + proj on the tcgen05 pack-prologue GEMM when TF32 matmuls are allowed
-USE_TCGEN05_PACK_PROJ = True
+# (off by default: at cfg2 it is not yet faster than the pack kernel + cuBLAS)
+USE_TCGEN05_PACK_PROJ = False
 
 
 def native_spmm_plan(operator) -> Optional[SpmmPlan]:

@@ -16,9 +16,10 @@ which add them to their own rows in a fixed order (peer by peer, unique
 indices per peer), so the sum order is deterministic.
 
 On top of it:
-  * DistMultiHop: per hop, gather the halo rows of the current state, then
-    the local row-block SpMM (cign_spmm on a rectangular plan whose
-    transpose serves the backward);
+  * DistMultiHop: per hop, the SpMM of the rank's row block split by column
+    owner -- own columns (square plan) and halo columns (rectangular plan,
+    transposes for the backward) -- with the halo rows of the current state
+    pushed by their owners while the own-column part runs;
   * DistGatGraph: the aggregate-first collapsed GAT on a rectangular plan
     (destination rows = own rows, source columns = extended rows).
 Every other op of the CIGN block is row-local.  Parameter gradients are
@@ -197,6 +198,45 @@ class HaloExchange:
         self._exchange(sends, recvs)
         return x_ext
 
+    def gather_halo(self, x_own: torch.Tensor):
+        """Start filling the halo rows only: returns (halo [n_halo, F], event).
+        The caller's stream must wait for `event` (None: already complete)
+        before reading halo."""
+        F = x_own.size(1)
+        halo = torch.empty((self.n_halo, F), dtype=x_own.dtype, device=x_own.device)
+        send = x_own.index_select(0, self.send_all) if self.send_all.numel() else None
+        sends, recvs = {}, {}
+        for p in range(self.plan.world):
+            if self.plan.send_counts[p]:
+                sends[p] = send[self.send_off[p]:self.send_off[p] + self.plan.send_counts[p]]
+            if self.plan.recv_counts[p]:
+                recvs[p] = halo[self.recv_off[p]:self.recv_off[p] + self.plan.recv_counts[p]]
+        self._exchange(sends, recvs)
+        return halo, None
+
+    def return_halo(self, g_halo: torch.Tensor):
+        """Start sending the halo rows' gradients [n_halo, F] back to their
+        owners: returns (recv [sum(send_counts), F], event) for add_returned."""
+        g_halo = g_halo.contiguous()
+        F = g_halo.size(1)
+        recv = torch.empty((int(self.send_all.numel()), F), dtype=g_halo.dtype,
+                           device=g_halo.device)
+        sends, recvs = {}, {}
+        for p in range(self.plan.world):
+            if self.plan.recv_counts[p]:
+                sends[p] = g_halo[self.recv_off[p]:self.recv_off[p] + self.plan.recv_counts[p]]
+            if self.plan.send_counts[p]:
+                recvs[p] = recv[self.send_off[p]:self.send_off[p] + self.plan.send_counts[p]]
+        self._exchange(sends, recvs)
+        return recv, None
+
+    def add_returned(self, g_own: torch.Tensor, recv: torch.Tensor) -> None:
+        """g_own += the gradients the peers returned (peer by peer, fixed order)."""
+        for p in range(self.plan.world):
+            c = self.plan.send_counts[p]
+            if c:
+                g_own.index_add_(0, self.send_idx[p], recv[self.send_off[p]:self.send_off[p] + c])
+
     def scatter_add(self, g_ext: torch.Tensor) -> torch.Tensor:
         """Backward of gather: own rows' gradient plus the gradients other
         ranks computed for them (added peer by peer)."""
@@ -264,6 +304,7 @@ class PeerHaloExchange(HaloExchange):
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._slots: List[dict] = []
         self._call = 0
+        self._stream = None  # side stream of the asynchronous pushes
 
     def begin_step(self) -> None:
         self._call = 0
@@ -305,6 +346,9 @@ class PeerHaloExchange(HaloExchange):
             ptr, view, bases = self._alloc_shared(self.n_own + self.n_halo, F)
             dst = [bases[p] + (self.n_own_of[p] + self.recv_off_of[p][me]) * F * 4
                    for p in range(w)]
+        elif kind == "halo":  # the halo rows only
+            ptr, view, bases = self._alloc_shared(self.n_halo, F)
+            dst = [bases[p] + self.recv_off_of[p][me] * F * 4 for p in range(w)]
         else:  # scatter: peers store gradients of the rows this rank sent them
             ptr, view, bases = self._alloc_shared(int(self.send_all.numel()), F)
             dst = [bases[p] + self.send_off_of[p][me] * F * 4 for p in range(w)]
@@ -320,6 +364,38 @@ class PeerHaloExchange(HaloExchange):
                                      self._lib.stream_of(src))
         self._lib.check(rc, "cign_halo_push")
         dist.all_reduce(self._flag, group=self.group)  # all stores done before any read
+
+    def _side(self):
+        if self._stream is None:
+            self._stream = torch.cuda.Stream(self.device)
+        return self._stream
+
+    def _push_async(self, src, F, idx, begin, dst, total):
+        """The push and its ordering collective on the side stream, after the
+        current stream's work so far; returns the event that ends them."""
+        cur = torch.cuda.current_stream(self.device)
+        side = self._side()
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            self._push(src, F, idx, begin, dst, total)
+            ev = torch.cuda.Event()
+            ev.record(side)
+        return ev
+
+    def gather_halo(self, x_own: torch.Tensor):
+        x_own = x_own.contiguous()
+        F = int(x_own.size(1))
+        slot = self._slot("halo", F)
+        ev = self._push_async(x_own, F, self.send_all, self.send_begin, slot["dst"],
+                              int(self.send_all.numel()))
+        return slot["view"], ev
+
+    def return_halo(self, g_halo: torch.Tensor):
+        g_halo = g_halo.contiguous()
+        F = int(g_halo.size(1))
+        slot = self._slot("scatter", F)
+        ev = self._push_async(g_halo, F, None, self.recv_begin, slot["dst"], self.n_halo)
+        return slot["view"], ev
 
     def gather(self, x_own: torch.Tensor) -> torch.Tensor:
         x_own = x_own.contiguous()
@@ -391,33 +467,68 @@ def _local_block(crow, col, val, plan: HaloPlan):
     return lcrow, lcol, lval
 
 
-class _LocalSpmmFn(torch.autograd.Function):
+def _csr_plan(rows_of_edges, cols, vals, n_rows: int, n_cols: int, dev) -> SpmmPlan:
+    """SpmmPlan of the [n_rows, n_cols] operator given as COO edges (row-major
+    order kept), with its transpose for the backward."""
+    counts = torch.bincount(rows_of_edges, minlength=n_rows)
+    crow = torch.zeros(n_rows + 1, dtype=torch.int64)
+    crow[1:] = torch.cumsum(counts, 0)
+    t = torch.sparse_coo_tensor(torch.stack([cols, rows_of_edges]), vals,
+                                (n_cols, n_rows)).coalesce().to_sparse_csr()
+    return SpmmPlan(crow.to(dev), cols.to(dev), vals.to(dev), t.crow_indices().to(dev),
+                    t.col_indices().to(dev), t.values().to(dev), cols=n_cols)
+
+
+class _DistHopFn(torch.autograd.Function):
+    """One hop y = P_r x over the rank's row block, split by column owner:
+    y = P_own x_own + P_halo halo(x).  The halo push runs on a side stream
+    while P_own x_own is computed; the backward returns P_halo^T g to the
+    owners the same way while P_own^T g is computed."""
+
     @staticmethod
-    def forward(ctx, x_ext, plan: SpmmPlan):
-        ctx.plan = plan
-        return plan.spmm(x_ext.contiguous())
+    def forward(ctx, x_own, hop: "DistMultiHop"):
+        ctx.hop = hop
+        x_own = x_own.contiguous()
+        halo, ev = hop.exchange.gather_halo(x_own)
+        y = hop.own.spmm(x_own)
+        if hop.halo is None:
+            return y
+        if ev is not None:
+            torch.cuda.current_stream(x_own.device).wait_event(ev)
+        return hop.halo.spmm(halo, addend=y)
 
     @staticmethod
     def backward(ctx, g):
-        return ctx.plan.spmm(g.contiguous(), transpose=True), None
+        hop = ctx.hop
+        g = g.contiguous()
+        if hop.halo is None:
+            return hop.own.spmm(g, transpose=True), None
+        g_halo = hop.halo.spmm(g, transpose=True)
+        recv, ev = hop.exchange.return_halo(g_halo)
+        g_own = hop.own.spmm(g, transpose=True)
+        if ev is not None:
+            torch.cuda.current_stream(g.device).wait_event(ev)
+        hop.exchange.add_returned(g_own, recv)
+        return g_own, None
 
 
 class DistMultiHop:
-    """k-hop propagation P^p x over the row-partitioned operator."""
+    """k-hop propagation P^p x over the row-partitioned operator; each hop
+    overlaps the halo exchange with the own-column part of the SpMM."""
 
     def __init__(self, csr_global: torch.Tensor, plan: HaloPlan, exchange: HaloExchange):
         crow = csr_global.crow_indices().cpu()
         col = csr_global.col_indices().cpu()
         val = csr_global.values().cpu()
         lcrow, lcol, lval = _local_block(crow, col, val, plan)
-        n_own, n_ext = plan.n_own, plan.n_own + plan.n_halo
+        n_own = plan.n_own
         rows = torch.repeat_interleave(torch.arange(n_own), lcrow[1:] - lcrow[:-1])
-        t = torch.sparse_coo_tensor(torch.stack([lcol, rows]), lval, (n_ext, n_own)).coalesce()
-        tc = t.to_sparse_csr()
         dev = exchange.device
-        self.plan = SpmmPlan(lcrow.to(dev), lcol.to(dev), lval.to(dev),
-                             tc.crow_indices().to(dev), tc.col_indices().to(dev),
-                             tc.values().to(dev), cols=n_ext)
+        own = lcol < n_own
+        self.own = _csr_plan(rows[own], lcol[own], lval[own], n_own, n_own, dev)
+        hal = ~own
+        self.halo = (_csr_plan(rows[hal], lcol[hal] - n_own, lval[hal], n_own, plan.n_halo, dev)
+                     if plan.n_halo else None)
         self.exchange = exchange
         self.nnz_local = int(lcol.numel())
 
@@ -428,7 +539,7 @@ class DistMultiHop:
             out[0] = x_own
         cur = x_own
         for p in range(1, wanted[-1] + 1):
-            cur = _LocalSpmmFn.apply(halo_gather(cur, self.exchange), self.plan)
+            cur = _DistHopFn.apply(cur, self)
             if p in wanted:
                 out[p] = cur
         return out

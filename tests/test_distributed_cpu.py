@@ -92,6 +92,13 @@ def _exchange_worker(rank, world, port, errors):
             want[p.r0:p.r1] += Gs[r][:p.n_own]
             want.index_add_(0, p.halo, Gs[r][p.n_own:])
         assert torch.allclose(x_own.grad, want[me.r0:me.r1], atol=1e-6)
+        # the split hop's path: halo rows only, gradients returned to owners
+        halo, ev = ex.gather_halo(X[me.r0:me.r1].contiguous())
+        assert ev is None and torch.equal(halo, X[me.halo])
+        recv, _ = ex.return_halo(Gs[rank][me.n_own:])
+        g_own = Gs[rank][:me.n_own].clone()
+        ex.add_returned(g_own, recv)
+        assert torch.allclose(g_own, want[me.r0:me.r1], atol=1e-6)
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:  # pragma: no cover - reported to the parent

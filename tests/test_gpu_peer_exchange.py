@@ -1,7 +1,9 @@
 """PeerHaloExchange (halo rows stored into the peers' IPC-mapped buffers by
 cign_halo_push) against the NCCL point-to-point exchange: the same extended
-tensors forward and the same gathered gradients backward, over three steps
-(buffers reused per step).  Needs 2 GPUs; skipped otherwise."""
+tensors forward and the same gathered gradients backward, and the same
+halo rows / returned gradients through the asynchronous halo-only path
+(side-stream pushes), over three steps (buffers reused per step).  Needs 2
+GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -55,6 +57,19 @@ def _worker(rank, world, port, errors):
                 (er * w).sum().backward()
                 (ep * w).sum().backward()
                 assert torch.equal(xr.grad, xp.grad), f"scatter F={F} step={step}"
+                # halo rows only, pushed on the side stream (the split hop's path)
+                hr, _ = ref.gather_halo(x)
+                hp, ev = peer.gather_halo(x)
+                torch.cuda.current_stream(dev).wait_event(ev)
+                assert torch.equal(hr, hp), f"gather_halo F={F} step={step}"
+                gh = torch.randn(plan.n_halo, F, device=dev, generator=g)
+                rr, _ = ref.return_halo(gh)
+                rp, ev = peer.return_halo(gh)
+                torch.cuda.current_stream(dev).wait_event(ev)
+                a, c = x.clone(), x.clone()
+                ref.add_returned(a, rr)
+                peer.add_returned(c, rp)
+                assert torch.equal(a, c), f"return_halo F={F} step={step}"
         peer.close()
         dist.barrier()
         dist.destroy_process_group()
