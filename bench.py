@@ -499,7 +499,8 @@ def run_sweep(args, device):
         d.update({"sweep": "configs[2]", "graph": cfg.name, "nodes": N, "nnz_P": nnz})
         print(json.dumps(d), flush=True)
 
-    for F in (64, 128, 512):
+    ops = set(args.sweep_ops.split(",")) if args.sweep_ops else {"spmm", "gat", "pack"}
+    for F in ((64, 128, 512) if "spmm" in ops else ()):
         X = torch.randn(N, F, device=device, generator=g)
         for K in range(1, 9):
             t_f = time_launches(lambda: plan.forward(X, K), 5, stream)
@@ -519,7 +520,7 @@ def run_sweep(args, device):
     (rp, c), (r, cp), perm = gat_graph
     gplan = gat_plan_for(rp, c, r, cp, perm)
     D = cfg.hidden_dim
-    for H in (1, 4, 8):
+    for H in ((1, 4, 8) if "gat" in ops else ()):
         x = torch.randn(N, D, device=device, generator=g)
         a = torch.randn(N, H, device=device, generator=g)
         z, emax, esum = collapsed_gat.gat_agg_forward_raw(gplan, a, a, x, H, 0.2, 0.5, 7)
@@ -541,7 +542,7 @@ def run_sweep(args, device):
               "aggregate_first_bwd_ms": round(t_ab * 1e3, 4),
               "drop_in_fwd_ms": round(t_cf * 1e3, 4), "drop_in_bwd_ms": round(t_cb * 1e3, 4)})
     K = 3
-    for blades in (8, 16):
+    for blades in ((8, 16) if "pack" in ops else ()):
         Dp = 64 * blades
         Hn = torch.randn(N, Dp, device=device, generator=g)
         Cn = torch.randn(N, Dp, device=device, generator=g)
@@ -637,6 +638,8 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="configs[2] isolated kernel sweep (one JSON line per case) instead of "
                          "the training-step benchmark")
+    ap.add_argument("--sweep-ops", default="",
+                    help="comma-separated subset of the sweep: spmm,gat,pack (default all)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="halo exchange of the multi-GPU run")
     ap.add_argument("--eager", action="store_true",

@@ -29,9 +29,11 @@ from .multihop_csr_pipeline import (GenericMultiHopCSRGraphOperator,
 from .plans import SpmmPlan, spmm_plan_for
 
 PACK_MODES = (1, 0, 0)  # interaction "new", outer none, weighting "old"
-# pack + proj on the tcgen05 pack-prologue GEMM when TF32 matmuls are allowed
-# (off by default: at cfg2 it is not yet faster than the pack kernel + cuBLAS)
-USE_TCGEN05_PACK_PROJ = False
+# pack + proj on the tcgen05 pack-prologue GEMM (TF32 matmuls allowed):
+# None = when G_raw is not kept (large graphs: no G write at all, and many
+# row tiles per SM); True/False = always/never.  When G_raw is kept, writing
+# it from the GEMM costs more than the separate pack kernel's write.
+USE_TCGEN05_PACK_PROJ = None
 
 
 def native_spmm_plan(operator) -> Optional[SpmmPlan]:
@@ -109,7 +111,8 @@ class _PropagateGatePackProjFn(torch.autograd.Function):
         props = _propagate(H, C, plan, order_set)
         alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
         D, K = H.size(1), len(props)
-        if (USE_TCGEN05_PACK_PROJ and torch.backends.cuda.matmul.allow_tf32
+        fused = (not keep_g) if USE_TCGEN05_PACK_PROJ is None else USE_TCGEN05_PACK_PROJ
+        if (fused and torch.backends.cuda.matmul.allow_tf32
                 and _pack.pack_proj_supported(D, K, proj_w.size(0))):
             out, G = _pack.pack_proj_forward(H, C, props, alpha, proj_w, proj_b, keep_g)
         else:

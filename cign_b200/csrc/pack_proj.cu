@@ -9,6 +9,9 @@
 // separate cuBLAS GEMM on it; here G is produced tile by tile straight into
 // shared memory as the MMA's A operand and never round-trips through HBM
 // (optionally it is also written out once, for the proj weight gradient).
+// The pack is evaluated with the hardware exponential (values within ~1e-6
+// relative of cign_pack_fwd's), since it only feeds TF32 products and the
+// TF32-tolerance weight gradient.
 //
 // One CTA owns 128 node rows and the whole output width (Dout <= 512 fp32
 // accumulator columns of tensor memory).  Warp roles:
@@ -19,10 +22,11 @@
 //   warp 1      allocates tensor memory; one lane issues tcgen05.mma
 //               (kind::tf32, M=128, N<=256 per instruction) and releases ring
 //               slots with tcgen05.commit;
-//   warps 2-9   read H/C/P rows with 16-byte loads, evaluate the pack for
-//               32 channels x K hops, round to TF32 and store the A tiles in
-//               the swizzled layout; afterwards they drain the accumulator
-//               (tcgen05.ld), add the bias and store the output rows.
+//   warps 2-17  (4 threads per row, 8 channels each) read H/C/P rows with
+//               16-byte loads, evaluate the pack for 32 channels x K hops,
+//               round to TF32 and store the A tiles in the swizzled layout;
+//               afterwards they drain the accumulator (tcgen05.ld), add the
+//               bias and store the output rows.
 // Every wait on an mbarrier is bounded (kWaitLimit polls, or earlier once
 // another role gave up); on expiry the CTA records kStatusTimeout in the
 // status word, stops producing, lets issued copies and MMAs complete
@@ -35,14 +39,14 @@
 namespace cign {
 namespace {
 
-constexpr int kPPThreads = 320;      // 10 warps
-constexpr int kPPProducers = 256;    // warps 2..9
+constexpr int kPPThreads = 576;      // 18 warps
+constexpr int kPPProducers = 512;    // warps 2..17
 constexpr int kPPRows = 128;         // rows per CTA (MMA M)
 constexpr int kPPBK = 32;            // fp32 k-elements per k-block (128 bytes per row)
-constexpr int kPPAStages = 4;
+constexpr int kPPAStages = 3;
 constexpr int kPPMaxK = 8;
 constexpr uint32_t kATileBytes = kPPRows * kPPBK * 4;  // 16 KB
-constexpr size_t kPPSmemBudget = 200 * 1024;
+constexpr size_t kPPSmemBudget = 208 * 1024;
 
 struct PPtrs { const float* p[kPPMaxK]; };
 
@@ -134,6 +138,17 @@ __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t
          (col & 3u) * 4u;
 }
 
+// The production interaction ("new", outer none) with the SiLU from the
+// hardware exponential and fast division: the values feed a TF32 product
+// (operands rounded to 2^-11 relative), so their ~1e-6 relative error is
+// immaterial, and the shorter dependency chain keeps the few producer warps
+// per scheduler ahead of the tensor core.
+__device__ __forceinline__ void interact_fwd_fast(float bhr, float brh, float& D, float& W) {
+  const float sym = 0.5f * (bhr + brh);
+  D = __fdividef(sym, 1.0f + __expf(-sym));
+  W = 0.5f * (bhr - brh);
+}
+
 // wait on `bar` for `parity`, bounded; gives up early once *abort is set
 __device__ __forceinline__ bool pp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
   for (unsigned i = 0; i < kWaitLimit; ++i) {
@@ -168,11 +183,10 @@ __global__ void pack_proj_prepare_w(const float* __restrict__ w, int64_t dout, i
   }
 }
 
-struct PPSmem {
-  uint32_t a_ring;   // kPPAStages x 16 KB
-  uint32_t b_ring;   // b_stages x dout*128 B
-  uint32_t bars;     // a_full[4] a_empty[4] b_full[S] b_empty[S] acc_full
-};
+// W ring entries hold one 256-row chunk of a k-block (32 KB at 32 columns):
+// finer than whole k-blocks (Dout x 128 B), so more of W is in flight.
+constexpr int kPPChunkRows = 256;
+constexpr uint32_t kBEntryBytes = kPPChunkRows * kPPBK * 4;  // 32 KB
 
 __global__ void __launch_bounds__(kPPThreads, 1)
 pack_proj_kernel(int64_t n, int64_t D, int K, int64_t dout, const float* __restrict__ H,
@@ -184,14 +198,14 @@ pack_proj_kernel(int64_t n, int64_t D, int K, int64_t dout, const float* __restr
   extern __shared__ __align__(1024) unsigned char pp_smem_raw[];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
+  __shared__ const float* hop_ptr_sh[kPPMaxK];
   // 1024-byte aligned operand rings (the swizzle pattern is address based)
   const uint32_t raw = smem_u32(pp_smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* base_ptr = pp_smem_raw + (base - raw);
-  const uint32_t b_tile = static_cast<uint32_t>(dout) * 128u;
   const uint32_t a_ring = base;
   const uint32_t b_ring = a_ring + kPPAStages * kATileBytes;
-  const uint32_t bars = b_ring + b_stages * b_tile;
+  const uint32_t bars = b_ring + b_stages * kBEntryBytes;
   auto a_full = [&](int s) { return bars + 8u * s; };
   auto a_empty = [&](int s) { return bars + 8u * (kPPAStages + s); };
   auto b_full = [&](int s) { return bars + 8u * (2 * kPPAStages + s); };
@@ -204,8 +218,12 @@ pack_proj_kernel(int64_t n, int64_t D, int K, int64_t dout, const float* __restr
   const int64_t kdim = 2 * K * D;
   const int n_db = static_cast<int>(D / kPPBK);
   const int n_blocks = n_db * K * 2;  // k-blocks in production order (db, hop, half)
+  const int n_chunks = static_cast<int>((dout + kPPChunkRows - 1) / kPPChunkRows);
   volatile int* abort = &abort_sh;
 
+#pragma unroll
+  for (int i = 0; i < kPPMaxK; ++i)
+    if (threadIdx.x == i) hop_ptr_sh[i] = P.p[i];
   if (threadIdx.x == 0) {
     abort_sh = 0;
     for (int s = 0; s < kPPAStages; ++s) {
@@ -229,57 +247,69 @@ pack_proj_kernel(int64_t n, int64_t D, int K, int64_t dout, const float* __restr
   const uint32_t tmem = tmem_base_sh;
 
   if (warp == 0) {
-    // ------------------------------------------------ W k-block stream
+    // ------------------------------------------------ W chunk stream
     if (lane == 0) {
+      const int n_entries = n_blocks * n_chunks;
       int issued = 0;
-      for (int b = 0; b < n_blocks; ++b) {
-        const int s = b % b_stages;
-        const int u = b / b_stages;
+      for (int e = 0; e < n_entries; ++e) {
+        const int s = e % b_stages;
+        const int u = e / b_stages;
         if (u > 0 && !pp_wait(b_empty(s), (u - 1) & 1, abort)) {
           pp_fail(abort, status);
           break;
         }
         if (*abort) break;
+        const int b = e / n_chunks;
+        const int c = e % n_chunks;
         const int db = b / (2 * K);
         const int hop = (b / 2) % K;
         const int half = b & 1;
         const int64_t kb = (static_cast<int64_t>(hop) * 2 * D + half * D) / kPPBK + db;
-        mbar_expect_tx(b_full(s), b_tile);
-        bulk_g2s(b_ring + s * b_tile, wt + kb * dout * kPPBK, b_tile, b_full(s));
+        const int64_t r0 = static_cast<int64_t>(c) * kPPChunkRows;
+        const uint32_t bytes =
+            static_cast<uint32_t>((dout - r0 < kPPChunkRows ? dout - r0 : kPPChunkRows) * 128);
+        mbar_expect_tx(b_full(s), bytes);
+        bulk_g2s(b_ring + s * kBEntryBytes, wt + (kb * dout + r0) * kPPBK, bytes, b_full(s));
         ++issued;
       }
       // let the last copy of every slot land before the CTA can exit (a
       // plain bounded wait: it must not give up early on abort)
-      for (int b = max(0, issued - b_stages); b < issued; ++b)
-        mbar_wait(b_full(b % b_stages), (b / b_stages) & 1);
+      for (int e = max(0, issued - b_stages); e < issued; ++e)
+        mbar_wait(b_full(e % b_stages), (e / b_stages) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issue
     if (lane == 0) {
-      for (int b = 0; b < n_blocks; ++b) {
+      bool ok = true;
+      for (int b = 0; b < n_blocks && ok; ++b) {
         const int sa = b % kPPAStages, ua = b / kPPAStages;
-        const int sb = b % b_stages, ub = b / b_stages;
-        if (!pp_wait(a_full(sa), ua & 1, abort) || !pp_wait(b_full(sb), ub & 1, abort)) {
+        if (!pp_wait(a_full(sa), ua & 1, abort)) {
           pp_fail(abort, status);
           break;
         }
-        tc_fence_after();
         const uint32_t a_addr = a_ring + sa * kATileBytes;
-        const uint32_t b_addr = b_ring + sb * b_tile;
-        for (int64_t n0 = 0; n0 < dout; n0 += 256) {
-          const uint32_t nn = static_cast<uint32_t>(dout - n0 < 256 ? dout - n0 : 256);
+        for (int c = 0; c < n_chunks; ++c) {
+          const int e = b * n_chunks + c;
+          const int sb = e % b_stages, ub = e / b_stages;
+          if (!pp_wait(b_full(sb), ub & 1, abort)) {
+            pp_fail(abort, status);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int64_t n0 = static_cast<int64_t>(c) * kPPChunkRows;
+          const uint32_t nn = static_cast<uint32_t>(dout - n0 < kPPChunkRows ? dout - n0
+                                                                             : kPPChunkRows);
           const uint32_t idesc = tf32_idesc(nn);
+          const uint32_t b_addr = b_ring + sb * kBEntryBytes;
 #pragma unroll
           for (int kk = 0; kk < kPPBK / 8; ++kk) {
-            const uint64_t ad = sw128_kmajor_desc(a_addr + kk * 32);
-            const uint64_t bd = sw128_kmajor_desc(b_addr + static_cast<uint32_t>(n0) * 128u +
-                                                  kk * 32);
-            umma_tf32(tmem + static_cast<uint32_t>(n0), ad, bd, idesc,
-                      (b > 0 || kk > 0) ? 1u : 0u);
+            umma_tf32(tmem + static_cast<uint32_t>(n0), sw128_kmajor_desc(a_addr + kk * 32),
+                      sw128_kmajor_desc(b_addr + kk * 32), idesc, (b > 0 || kk > 0) ? 1u : 0u);
           }
+          umma_commit(b_empty(sb));
         }
-        umma_commit(a_empty(sa));
-        umma_commit(b_empty(sb));
+        if (ok) umma_commit(a_empty(sa));
       }
       umma_commit(acc_full);
       // every MMA issued above completes before tensor memory is freed
@@ -287,77 +317,93 @@ pack_proj_kernel(int64_t n, int64_t D, int K, int64_t dout, const float* __restr
     }
   } else {
     // ------------------------------------------------ pack producers
+    // Steps walk (d-block, hop); the next step's P rows are loaded while the
+    // current step is evaluated and stored.
     const int t = threadIdx.x - 64;
-    const int r = t >> 1;          // tile row
-    const int hf = t & 1;          // which 16 of the 32 channels
+    const int r = t >> 2;          // tile row
+    const int hf = t & 3;          // which 8 of the 32 channels
     const int64_t row = row0 + r;
     const bool valid = row < n;
-    const float* hrow = H + row * D;
-    const float* crow = C + row * D;
-    for (int db = 0; db < n_db && !*abort; ++db) {
-      const int64_t d0 = static_cast<int64_t>(db) * kPPBK + hf * 16;
-      float4 h4[4], c4[4];
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int n_steps = n_db * K;
+    float4 h4[2], c4[2], th[2], tc[2];
+    float a;
+    auto load_hc = [&](int db, float4 (&hh)[2], float4 (&cc)[2]) {
+      const int64_t d0 = static_cast<int64_t>(db) * kPPBK + hf * 8;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        h4[q] = valid ? __ldg(reinterpret_cast<const float4*>(hrow + d0) + q)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-        c4[q] = valid ? __ldg(reinterpret_cast<const float4*>(crow + d0) + q)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < 2; ++q) {
+        hh[q] = valid ? __ldg(reinterpret_cast<const float4*>(H + row * D + d0) + q) : zero;
+        cc[q] = valid ? __ldg(reinterpret_cast<const float4*>(C + row * D + d0) + q) : zero;
       }
-      for (int hop = 0; hop < K; ++hop) {
-        const float* prow = P.p[hop] + row * ldp;
-        float4 th[4], tc[4];
-        const float a = valid ? __ldg(alpha + row * K + hop) : 0.0f;
+    };
+    auto load_p = [&](int db, int hop, float4 (&pth)[2], float4 (&ptc)[2], float& pa) {
+      const int64_t d0 = static_cast<int64_t>(db) * kPPBK + hf * 8;
+      const float* prow = hop_ptr_sh[hop] + row * ldp;
+      pa = valid ? __ldg(alpha + row * K + hop) : 0.0f;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          th[q] = valid ? __ldg(reinterpret_cast<const float4*>(prow + d0) + q)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-          tc[q] = valid ? __ldg(reinterpret_cast<const float4*>(prow + D + d0) + q)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < 2; ++q) {
+        pth[q] = valid ? __ldg(reinterpret_cast<const float4*>(prow + d0) + q) : zero;
+        ptc[q] = valid ? __ldg(reinterpret_cast<const float4*>(prow + D + d0) + q) : zero;
+      }
+    };
+    load_hc(0, h4, c4);
+    load_p(0, 0, th, tc, a);
+    for (int step = 0; step < n_steps && !*abort; ++step) {
+      const int db = step / K;
+      const int hop = step % K;
+      float4 nth[2], ntc[2];
+      float na = 0.0f;
+      const bool more = step + 1 < n_steps;
+      const bool new_db = more && (step + 1) % K == 0;
+      if (more) load_p((step + 1) / K, (step + 1) % K, nth, ntc, na);
+      const int64_t d0 = static_cast<int64_t>(db) * kPPBK + hf * 8;
+      // both A slots of this step (W half, D half) must be free
+      const int b0 = step * 2;
+      const int s0 = b0 % kPPAStages, s1 = (b0 + 1) % kPPAStages;
+      const int u0 = b0 / kPPAStages, u1 = (b0 + 1) / kPPAStages;
+      if ((u0 > 0 && !pp_wait(a_empty(s0), (u0 - 1) & 1, abort)) ||
+          (u1 > 0 && !pp_wait(a_empty(s1), (u1 - 1) & 1, abort))) {
+        pp_fail(abort, status);
+        break;
+      }
+      unsigned char* tile0 = base_ptr + s0 * kATileBytes;
+      unsigned char* tile1 = base_ptr + s1 * kATileBytes;
+      float* g = (g_out != nullptr && valid)
+                     ? g_out + row * kdim + static_cast<int64_t>(hop) * 2 * D + d0
+                     : nullptr;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float4 wv, dv;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float Dv, Wv;
+          interact_fwd_fast(vel(h4[q], j) * vel(tc[q], j), vel(c4[q], j) * vel(th[q], j), Dv,
+                            Wv);
+          vel(wv, j) = a * Wv;
+          vel(dv, j) = a * Dv;
         }
-        float4 wv[4], dv[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float Dv, Wv;
-            interact_fwd(vel(h4[q], j) * vel(tc[q], j), vel(c4[q], j) * vel(th[q], j), 1, 0, Dv,
-                         Wv);
-            vel(wv[q], j) = a * Wv;
-            vel(dv[q], j) = a * Dv;
-          }
+        if (g != nullptr) {
+          reinterpret_cast<float4*>(g)[q] = wv;
+          reinterpret_cast<float4*>(g + D)[q] = dv;
         }
-        if (g_out != nullptr && valid) {
-          float* g = g_out + row * kdim + static_cast<int64_t>(hop) * 2 * D + d0;
+        const uint32_t off = sw128_offset(r, hf * 8 + q * 4);
+        *reinterpret_cast<float4*>(tile0 + off) =
+            make_float4(to_tf32(wv.x), to_tf32(wv.y), to_tf32(wv.z), to_tf32(wv.w));
+        *reinterpret_cast<float4*>(tile1 + off) =
+            make_float4(to_tf32(dv.x), to_tf32(dv.y), to_tf32(dv.z), to_tf32(dv.w));
+      }
+      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+      mbar_arrive(a_full(s0));
+      mbar_arrive(a_full(s1));
+      if (more) {
+        // H/C rows of the next d-block go into the registers just freed
+        if (new_db) load_hc(db + 1, h4, c4);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            reinterpret_cast<float4*>(g)[q] = wv[q];
-            reinterpret_cast<float4*>(g + D)[q] = dv[q];
-          }
+        for (int q = 0; q < 2; ++q) {
+          th[q] = nth[q];
+          tc[q] = ntc[q];
         }
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int b = (db * K + hop) * 2 + half;
-          const int s = b % kPPAStages;
-          const int u = b / kPPAStages;
-          if (u > 0 && !pp_wait(a_empty(s), (u - 1) & 1, abort)) {
-            pp_fail(abort, status);
-            break;
-          }
-          unsigned char* tile = base_ptr + s * kATileBytes;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float4 v = half == 0 ? wv[q] : dv[q];
-            v.x = to_tf32(v.x);
-            v.y = to_tf32(v.y);
-            v.z = to_tf32(v.z);
-            v.w = to_tf32(v.w);
-            *reinterpret_cast<float4*>(tile + sw128_offset(r, hf * 16 + q * 4)) = v;
-          }
-          fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
-          mbar_arrive(a_full(s));
-        }
-        if (*abort) break;
+        a = na;
       }
     }
     // ------------------------------------------------ epilogue
@@ -367,9 +413,9 @@ pack_proj_kernel(int64_t n, int64_t D, int K, int64_t dout, const float* __restr
     // warp-uniform decision: tcgen05.ld is a .sync.aligned warp instruction
     if (__all_sync(kFullMask, ok && !*abort)) {
       const int q = warp & 3;                  // TMEM lane quarter of this warp
-      const int cg = (warp - 2) >> 2;          // 0: warps 2-5, 1: warps 6-9
+      const int cg = (warp - 2) >> 2;          // column group 0..3 (warps 2-5, 6-9, ...)
       const int64_t orow = row0 + q * 32 + lane;
-      for (int64_t c0 = cg * 32; c0 < dout; c0 += 64) {
+      for (int64_t c0 = cg * 32; c0 < dout; c0 += 128) {
         uint32_t v[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0), v);
         tmem_ld_wait();
@@ -399,14 +445,13 @@ pack_proj_kernel(int64_t n, int64_t D, int K, int64_t dout, const float* __restr
 size_t pp_wt_bytes(int64_t dout, int64_t kdim) {
   return (static_cast<size_t>(dout) * kdim * 4 + 1023) / 1024 * 1024;
 }
-int pp_b_stages(int64_t dout) {
-  const size_t b_tile = static_cast<size_t>(dout) * 128;
+int pp_b_stages() {
   const size_t room = kPPSmemBudget - kPPAStages * kATileBytes;
-  return static_cast<int>(std::max<size_t>(2, std::min<size_t>(6, room / b_tile)));
+  return static_cast<int>(std::min<size_t>(8, room / kBEntryBytes));
 }
-size_t pp_smem_bytes(int64_t dout, int b_stages) {
+size_t pp_smem_bytes(int b_stages) {
   return 1024 /* alignment slack */ + kPPAStages * kATileBytes +
-         static_cast<size_t>(b_stages) * dout * 128 + 8 * (2 * kPPAStages + 2 * b_stages + 1);
+         static_cast<size_t>(b_stages) * kBEntryBytes + 8 * (2 * kPPAStages + 2 * b_stages + 1);
 }
 
 }  // namespace
@@ -465,8 +510,8 @@ int cign_pack_proj_gemm_tf32(int64_t n, int64_t d, int32_t k, int64_t dout, cons
     pack_proj_prepare_w<<<blocks, 256, 0, s>>>(w, dout, kdim, wt);
     CIGN_CHECK_LAUNCH("pack_proj_prepare_w");
   }
-  const int b_stages = pp_b_stages(dout);
-  const size_t smem = pp_smem_bytes(dout, b_stages);
+  const int b_stages = pp_b_stages();
+  const size_t smem = pp_smem_bytes(b_stages);
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(dout)) cols <<= 1;
   {
