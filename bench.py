@@ -638,6 +638,9 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="configs[2] isolated kernel sweep (one JSON line per case) instead of "
                          "the training-step benchmark")
+    ap.add_argument("--pack-proj", choices=["auto", "fused", "separate"], default="auto",
+                    help="block pack + proj: tcgen05 pack-prologue GEMM (fused), pack kernel + "
+                         "cuBLAS (separate), or fused only when G_raw is recomputed (auto)")
     ap.add_argument("--sweep-ops", default="",
                     help="comma-separated subset of the sweep: spmm,gat,pack (default all)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
@@ -655,6 +658,9 @@ def main():
     from cign_b200 import synth
     cfg = synth.CONFIGS[args.workload]
     metric = "CIGN fwd+bwd train-step GTEPS (SpMM edge-passes/s)"
+    from cign_b200 import block_fused
+    block_fused.USE_TCGEN05_PACK_PROJ = {"auto": None, "fused": True,
+                                         "separate": False}[args.pack_proj]
     if cfg.num_nodes > GRAPH_CAPTURE_MAX_NODES:
         # launch overhead is negligible at this size, and a captured step would
         # hold a second copy of the activations in the graph's private pool
@@ -849,6 +855,7 @@ def main():
                        "hidden": cfg.hidden_dim, "channels_x_blades": "64x8", "hops": list(cfg.hops),
                        "heads": cfg.heads, "layers": cfg.layers, "dropout": cfg.dropout,
                        "dense_gemm": "tf32 (cuBLAS via torch)",
+                       "pack_proj": args.pack_proj,
                        "l2": "flushed between timed steps (256 MiB write)",
                        "launch": "one CUDA graph per step" if use_graph else "eager",
                        "parallelism": f"replicas{world}" if world > 1 else "single"},
