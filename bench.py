@@ -399,8 +399,11 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     sampler = ClockSampler(local_rank)
     dist.barrier()
     torch.cuda.synchronize()
+    push_timer = []
     if not use_graph:
         SpmmPlan.hop_timer = hop_timer  # events around every local row-block SpMM
+        if hasattr(exch, "timer"):
+            exch.timer = push_timer  # events around every halo push + its barrier
     sampler.start()
     for i in range(args.steps):
         flush.zero_()
@@ -409,6 +412,11 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
         ends[i].record(stream)
     torch.cuda.synchronize()
     SpmmPlan.hop_timer = None
+    if hasattr(exch, "timer"):
+        exch.timer = None
+    exchange_ms = (sum(a.elapsed_time(b) for a, b, _ in push_timer) / args.steps
+                   if push_timer else None)
+    exchange_bytes = sum(nb for _, _, nb in push_timer) / args.steps if push_timer else None
     clocks = sampler.stop()
     launches = (graphed.native_launches * args.steps if use_graph
                 else int(lib.cign_kernel_launches()) - launches_before)
@@ -433,7 +441,9 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_s = float(t.item())
     halo = torch.tensor([hplan.n_halo], device=device, dtype=torch.float64)
+    halo_max = halo.clone()
     dist.all_reduce(halo)
+    dist.all_reduce(halo_max, op=dist.ReduceOp.MAX)
     if graphed is not None:
         del graphed  # release the graph (it holds collectives) before the buffers go
         torch.cuda.synchronize()
@@ -459,6 +469,7 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                                      "(cign_halo_push)") +
                                     "; one gradient all-reduce per step"),
                        "halo_rows_total": int(halo.item()),
+                       "halo_rows_max_per_rank": int(halo_max.item()),
                        "l2": "flushed between timed steps (256 MiB write)",
                        "launch": "one CUDA graph per step" if use_graph else "eager"},
             "e2e": {"value": round(edge_passes * args.steps / e2e_s / 1e9, 4), "unit": "GTEPS",
@@ -466,6 +477,13 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                     "ms_per_step": round(e2e_s / args.steps * 1e3, 4)},
             "gpu_launches": launches,
             "step_ms_rank0": [round(v, 3) for v in step_ms],
+            "halo_push_rank0": (None if exchange_ms is None else {
+                "ms_per_step": round(exchange_ms, 3),
+                "bytes_per_step": int(exchange_bytes),
+                "gbs": round(exchange_bytes / (exchange_ms * 1e-3) / 1e9, 1),
+                "timing": "CUDA events around each halo push kernel and its ordering "
+                          "all-reduce (side stream for the k-hop pushes, which overlap "
+                          "the own-column SpMM)"}),
             "roofline": hop_roofline(hop_timer, hplan.n_own, dop.nnz_local, peak, peak_kind,
                                      with_traffic=False),
             "cpu_baseline": None, "clocks": clocks,

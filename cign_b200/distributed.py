@@ -305,6 +305,9 @@ class PeerHaloExchange(HaloExchange):
         self._slots: List[dict] = []
         self._call = 0
         self._stream = None  # side stream of the asynchronous pushes
+        # list to collect (start, end, bytes sent) of every push + ordering
+        # collective, or None (set by benchmarks; not used under graph capture)
+        self.timer = None
 
     def begin_step(self) -> None:
         self._call = 0
@@ -314,8 +317,20 @@ class PeerHaloExchange(HaloExchange):
         rank's buffer of the same slot (all ranks allocate together)."""
         nbytes = max(int(rows) * int(F) * 4, 16)
         ptr = self._lib.c_void_p()
-        self._lib.check(self.lib.cign_device_alloc(nbytes, self._lib.ctypes.byref(ptr)),
-                        "cign_device_alloc")
+        rc = self.lib.cign_device_alloc(nbytes, self._lib.ctypes.byref(ptr))
+        if rc != 0:  # memory cached by torch's allocator: release it and retry once
+            torch.cuda.synchronize(self.device)
+            torch.cuda.empty_cache()
+            rc = self.lib.cign_device_alloc(nbytes, self._lib.ctypes.byref(ptr))
+        # every rank learns whether all allocations succeeded before any of
+        # them waits in the handle exchange
+        ok = torch.tensor([1.0 if rc == 0 else 0.0], device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if float(ok.item()) < 1.0:
+            if rc == 0:
+                self.lib.cign_device_free(ptr)
+            raise RuntimeError(f"peer halo buffer of {nbytes} bytes: cudaMalloc failed on "
+                               f"{'this' if rc != 0 else 'another'} rank (out of device memory)")
         handle = (self._lib.ctypes.c_ubyte * 64)()
         self._lib.check(self.lib.cign_ipc_handle(ptr, handle), "cign_ipc_handle")
         mine = torch.tensor(list(handle), dtype=torch.uint8, device=self.device)
@@ -358,12 +373,20 @@ class PeerHaloExchange(HaloExchange):
         return slot
 
     def _push(self, src, F, idx, begin, dst, total):
+        stream = torch.cuda.current_stream(self.device)
+        if self.timer is not None:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
         rc = self.lib.cign_halo_push(self.plan.world, self._lib.ptr(src), F,
                                      self._lib.ptr(idx) if idx is not None else None,
                                      self._lib.ptr(begin), self._lib.ptr(dst), int(total),
                                      self._lib.stream_of(src))
         self._lib.check(rc, "cign_halo_push")
         dist.all_reduce(self._flag, group=self.group)  # all stores done before any read
+        if self.timer is not None:
+            t1 = torch.cuda.Event(enable_timing=True)
+            t1.record(stream)
+            self.timer.append((t0, t1, int(total) * int(F) * 4))
 
     def _side(self):
         if self._stream is None:
