@@ -414,9 +414,14 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     SpmmPlan.hop_timer = None
     if hasattr(exch, "timer"):
         exch.timer = None
-    exchange_ms = (sum(a.elapsed_time(b) for a, b, _ in push_timer) / args.steps
-                   if push_timer else None)
-    exchange_bytes = sum(nb for _, _, nb in push_timer) / args.steps if push_timer else None
+    # per rank: push-kernel ms, barrier-wait ms, bytes sent (per step)
+    mine = torch.tensor([sum(a.elapsed_time(b) for a, b, _, _ in push_timer) / args.steps,
+                         sum(b.elapsed_time(c) for _, b, c, _ in push_timer) / args.steps,
+                         sum(nb for _, _, _, nb in push_timer) / args.steps],
+                        device=device, dtype=torch.float64)
+    per_rank = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(per_rank, mine)
+    push_stats = [t.tolist() for t in per_rank] if push_timer else None
     clocks = sampler.stop()
     launches = (graphed.native_launches * args.steps if use_graph
                 else int(lib.cign_kernel_launches()) - launches_before)
@@ -477,13 +482,14 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                     "ms_per_step": round(e2e_s / args.steps * 1e3, 4)},
             "gpu_launches": launches,
             "step_ms_rank0": [round(v, 3) for v in step_ms],
-            "halo_push_rank0": (None if exchange_ms is None else {
-                "ms_per_step": round(exchange_ms, 3),
-                "bytes_per_step": int(exchange_bytes),
-                "gbs": round(exchange_bytes / (exchange_ms * 1e-3) / 1e9, 1),
-                "timing": "CUDA events around each halo push kernel and its ordering "
-                          "all-reduce (side stream for the k-hop pushes, which overlap "
-                          "the own-column SpMM)"}),
+            "halo_push_per_rank": (None if push_stats is None else {
+                "push_ms_per_step": [round(v[0], 2) for v in push_stats],
+                "barrier_wait_ms_per_step": [round(v[1], 2) for v in push_stats],
+                "bytes_sent_per_step": [int(v[2]) for v in push_stats],
+                "push_gbs": [round(v[2] / max(v[0], 1e-9) * 1e-6, 1) for v in push_stats],
+                "timing": "CUDA events around each halo push kernel (push) and its ordering "
+                          "all-reduce (barrier wait: includes waiting for slower ranks); the "
+                          "k-hop pushes run on a side stream beside the own-column SpMM"}),
             "roofline": hop_roofline(hop_timer, hplan.n_own, dop.nnz_local, peak, peak_kind,
                                      with_traffic=False),
             "cpu_baseline": None, "clocks": clocks,

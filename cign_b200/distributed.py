@@ -305,8 +305,9 @@ class PeerHaloExchange(HaloExchange):
         self._slots: List[dict] = []
         self._call = 0
         self._stream = None  # side stream of the asynchronous pushes
-        # list to collect (start, end, bytes sent) of every push + ordering
-        # collective, or None (set by benchmarks; not used under graph capture)
+        # list to collect (start, push done, barrier done, bytes sent) of every
+        # push and its ordering collective, or None (set by benchmarks; not
+        # used under graph capture)
         self.timer = None
 
     def begin_step(self) -> None:
@@ -382,11 +383,14 @@ class PeerHaloExchange(HaloExchange):
                                      self._lib.ptr(begin), self._lib.ptr(dst), int(total),
                                      self._lib.stream_of(src))
         self._lib.check(rc, "cign_halo_push")
-        dist.all_reduce(self._flag, group=self.group)  # all stores done before any read
         if self.timer is not None:
             t1 = torch.cuda.Event(enable_timing=True)
             t1.record(stream)
-            self.timer.append((t0, t1, int(total) * int(F) * 4))
+        dist.all_reduce(self._flag, group=self.group)  # all stores done before any read
+        if self.timer is not None:
+            t2 = torch.cuda.Event(enable_timing=True)
+            t2.record(stream)
+            self.timer.append((t0, t1, t2, int(total) * int(F) * 4))
 
     def _side(self):
         if self._stream is None:
