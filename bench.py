@@ -415,12 +415,12 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     if hasattr(exch, "timer"):
         exch.timer = None
     # per rank: push-kernel ms, barrier-wait ms, bytes sent (per step)
-    mine = torch.tensor([sum(a.elapsed_time(b) for a, b, _, _ in push_timer) / args.steps,
-                         sum(b.elapsed_time(c) for _, b, c, _ in push_timer) / args.steps,
-                         sum(nb for _, _, _, nb in push_timer) / args.steps],
-                        device=device, dtype=torch.float64)
-    per_rank = [torch.empty_like(mine) for _ in range(world)]
-    dist.all_gather(per_rank, mine)
+    push_mine = torch.tensor([sum(a.elapsed_time(b) for a, b, _, _ in push_timer) / args.steps,
+                              sum(b.elapsed_time(c) for _, b, c, _ in push_timer) / args.steps,
+                              sum(nb for _, _, _, nb in push_timer) / args.steps],
+                             device=device, dtype=torch.float64)
+    per_rank = [torch.empty_like(push_mine) for _ in range(world)]
+    dist.all_gather(per_rank, push_mine)
     push_stats = [t.tolist() for t in per_rank] if push_timer else None
     clocks = sampler.stop()
     launches = (graphed.native_launches * args.steps if use_graph
