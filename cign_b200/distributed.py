@@ -35,13 +35,22 @@ import torch.distributed as dist
 from .plans import SpmmPlan
 
 
-def partition_rows(crow: torch.Tensor, world: int) -> List[int]:
-    """Contiguous row ranges [b[r], b[r+1]) balancing rows + non-zeros."""
+# Cost of an own row relative to a non-zero in the partition balance.  On the
+# 2.45M-node RMAT graph at 8 ranks, a rank's step time grew by ~150 ns per own
+# row (the row-wise ops, GEMMs and the per-row fixed cost of the gathers) and
+# ~5 ns per non-zero, so rows are weighted 30x.
+ROW_WEIGHT = 30
+
+
+def partition_rows(crow: torch.Tensor, world: int, row_weight: int = 1) -> List[int]:
+    """Contiguous row ranges [b[r], b[r+1]) balancing row_weight * rows +
+    non-zeros."""
     crow = crow.to(torch.int64).cpu()
     n = crow.numel() - 1
     nnz = int(crow[-1])
-    work = crow + torch.arange(n + 1, dtype=torch.int64)  # events up to each row start
-    total = n + nnz
+    # work before each row start
+    work = crow + int(row_weight) * torch.arange(n + 1, dtype=torch.int64)
+    total = int(row_weight) * n + nnz
     bounds = [0]
     for r in range(1, world):
         t = (r * total) // world
@@ -601,13 +610,14 @@ class DistGatGraph:
 
 
 def partition_graph(csr_global: torch.Tensor, gat_rowptr: torch.Tensor, gat_col: torch.Tensor,
-                    world: int, rank: int, device, transport=None):
+                    world: int, rank: int, device, transport=None, row_weight: int = ROW_WEIGHT):
     """Everything one rank needs: (bounds, HaloPlan, HaloExchange, DistMultiHop,
     DistGatGraph).  csr_global: P as a sparse CSR tensor; gat_rowptr/gat_col:
     the destination-major CSR of the GAT graph (same sparsity pattern).
     transport: None (NCCL point-to-point), "peer" (NVLink peer-memory stores,
-    PeerHaloExchange), or a transport object (TorchP2P, StagedGlooP2P, ...)."""
-    bounds = partition_rows(csr_global.crow_indices(), world)
+    PeerHaloExchange), or a transport object (TorchP2P, StagedGlooP2P, ...).
+    row_weight: cost of an own row in units of one non-zero (partition_rows)."""
+    bounds = partition_rows(csr_global.crow_indices(), world, row_weight)
     plan = HaloPlan(csr_global.crow_indices(), csr_global.col_indices(), bounds, rank)
     if transport == "peer":
         exchange = PeerHaloExchange(plan, device)

@@ -22,16 +22,20 @@ def _global_csr(n=700, e=5000, seed=3):
     return adj.coalesce().to_sparse_csr()
 
 
-def test_partition_balances_rows_plus_nnz():
+@pytest.mark.parametrize("row_weight", [1, 30])
+def test_partition_balances_rows_plus_nnz(row_weight):
+    """Ranges balance row_weight * rows + non-zeros to within one row's work."""
     P = _global_csr()
     crow = P.crow_indices()
     n, nnz = crow.numel() - 1, int(crow[-1])
+    total = row_weight * n + nnz
     for world in (1, 2, 3, 8):
-        b = partition_rows(crow, world)
+        b = partition_rows(crow, world, row_weight)
         assert b[0] == 0 and b[-1] == n and all(x <= y for x, y in zip(b, b[1:]))
-        work = [(b[r + 1] - b[r]) + int(crow[b[r + 1]] - crow[b[r]]) for r in range(world)]
-        assert sum(work) == n + nnz
-        assert max(work) <= (n + nnz) / world + int((crow[1:] - crow[:-1]).max()) + 1
+        work = [row_weight * (b[r + 1] - b[r]) + int(crow[b[r + 1]] - crow[b[r]])
+                for r in range(world)]
+        assert sum(work) == total
+        assert max(work) <= total / world + int((crow[1:] - crow[:-1]).max()) + row_weight
 
 
 def test_halo_plans_agree_between_ranks():
