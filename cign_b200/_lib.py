@@ -117,6 +117,10 @@ SIGNATURES = {
                                              c_size_t, _P]),
     "cign_pack_fwd": (c_int, [c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, _P, _P, _PP,
                               c_int64, _P, _P, _P]),
+    "cign_jk_ln_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "cign_jk_ln_fwd": (c_int, [c_int64, c_int32, c_int64, _PP, _P, _P, c_float, _P, _P, _P, _P]),
+    "cign_jk_ln_bwd": (c_int, [c_int64, c_int32, c_int64, _P, _PP, _P, _P, _P, _PP, _P, _P, _P,
+                               c_size_t, _P]),
     "cign_pack_proj_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int64]),
     "cign_pack_proj_gemm_tf32": (c_int, [c_int64, c_int64, c_int32, c_int64, _P, _P, _PP, c_int64,
                                          _P, _P, _P, _P, _P, _P, c_size_t, _P]),

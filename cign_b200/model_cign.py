@@ -42,6 +42,7 @@ from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, 
 from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
 from .block_fused import native_spmm_plan, propagate_gate_pack_proj
+from .jk_norm import jk_layer_norm, jk_norm_supported
 from .hop_gate import fused_hop_gate
 from .linear import linear
 
@@ -255,7 +256,11 @@ class GraphCliffordNet(nn.Module):
         for block in self.blocks:
             H = block(H, graph_operator, self._gat_graph)
             states.append(H)
-        H_out = self.output_norm(torch.cat(states, dim=-1))
+        if jk_norm_supported(states):  # LayerNorm of the cat, without the cat
+            H_out = jk_layer_norm(states, self.output_norm.weight, self.output_norm.bias,
+                                  self.output_norm.eps)
+        else:
+            H_out = self.output_norm(torch.cat(states, dim=-1))
         H_out = F.dropout(H_out, p=self.dropout, training=self.training)
         return _linear_padded(H_out, self.classifier.weight, self.classifier.bias).float()
 

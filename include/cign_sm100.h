@@ -325,6 +325,25 @@ CIGN_API int cign_pack_bwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
                   int32_t accumulate_p, float* grad_alpha,
                   cign_stream_t stream);
 
+/* ---------------------------------------------------- JK output LayerNorm
+ * y = LayerNorm([seg_0 | seg_1 | ... | seg_{S-1}]) over rows of
+ * D = S * seg_width <= 2048 floats (biased variance), reading the S segment
+ * tensors [n, seg_width] directly instead of their concatenation; mean and
+ * rstd [n] are saved for the backward.  Replaces
+ * output_norm(torch.cat(states, dim=-1)) of GraphCliffordNet
+ * (generic_engine/model_cign.py:1195-1201).  segs / grad_segs: host arrays
+ * of S device pointers; seg_width % 4 == 0, 16-byte aligned rows.  The
+ * backward writes the per-segment input gradients and the LayerNorm weight
+ * and bias gradients (fixed-order sums over rows). */
+CIGN_API size_t cign_jk_ln_workspace_bytes(int64_t n, int64_t d);
+CIGN_API int cign_jk_ln_fwd(int64_t n, int32_t n_seg, int64_t seg_width,
+                   const float* const* segs, const float* w, const float* b, float eps,
+                   float* y, float* mean, float* rstd, cign_stream_t stream);
+CIGN_API int cign_jk_ln_bwd(int64_t n, int32_t n_seg, int64_t seg_width, const float* grad_y,
+                   const float* const* segs, const float* w, const float* mean,
+                   const float* rstd, float* const* grad_segs, float* grad_w,
+                   float* grad_b, void* ws, size_t ws_bytes, cign_stream_t stream);
+
 /* ------------------------------------------------------- pack + proj GEMM
  * out[n,:] = G[n,:] @ W^T + bias with G = pack(H, C, P_1..P_K, alpha) in the
  * production switches (interaction "new", outer none, weighting "old"),
