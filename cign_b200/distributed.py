@@ -36,10 +36,11 @@ from .plans import SpmmPlan
 
 
 # Cost of an own row relative to a non-zero in the partition balance.  On the
-# 2.45M-node RMAT graph at 8 ranks, a rank's step time grew by ~150 ns per own
-# row (the row-wise ops, GEMMs and the per-row fixed cost of the gathers) and
-# ~5 ns per non-zero, so rows are weighted 30x.
-ROW_WEIGHT = 30
+# 2.45M-node RMAT graph at 8 ranks (two partitions measured), a rank's busy
+# time per step fitted 159 ns per own row (the row-wise ops, the GEMMs and
+# the per-row fixed cost of the gathers) + 3.2 ns per non-zero + 34 ms, so a
+# row weighs 50 non-zeros.
+ROW_WEIGHT = 50
 
 
 def partition_rows(crow: torch.Tensor, world: int, row_weight: int = 1) -> List[int]:

@@ -52,6 +52,21 @@ def test_invalid_arguments_rejected_before_launch():
     assert lib.cign_gat_fwd(ctypes.c_void_p(1), 65, 8, None, None, None, None, 0.2, 0.0, 0, None,
                             None, None, None, None, None, 0, None) == 6
     assert "heads" in _lib.last_error()
+    # pack + proj GEMM: D not a multiple of 32, Dout above the 512 TMEM columns,
+    # more hops than the kernel's pointer table
+    ws = ctypes.c_void_p(16)
+    assert lib.cign_pack_proj_gemm_tf32(128, 48, 2, 64, None, None, None, 96, None, None, None,
+                                        None, None, ws, 1 << 20, None) == 6
+    assert "multiple of 32" in _lib.last_error()
+    assert lib.cign_pack_proj_gemm_tf32(128, 64, 2, 1024, None, None, None, 128, None, None,
+                                        None, None, None, ws, 1 << 30, None) == 6
+    assert lib.cign_pack_proj_gemm_tf32(128, 64, 9, 64, None, None, None, 128, None, None, None,
+                                        None, None, ws, 1 << 30, None) == 6
+    assert lib.cign_pack_proj_workspace_bytes(512, 3, 512) >= 512 * 3072 * 4
+    # JK LayerNorm: row wider than 2048 floats, too many segments
+    assert lib.cign_jk_ln_fwd(4, 3, 1024, None, None, None, 1e-5, None, None, None, None) == 6
+    assert lib.cign_jk_ln_fwd(4, 9, 64, None, None, None, 1e-5, None, None, None, None) == 6
+    assert lib.cign_jk_ln_workspace_bytes(1000, 1536) == 2 * 16 * 1536 * 4
 
 
 def test_python_api_requires_cuda_without_fallback():
