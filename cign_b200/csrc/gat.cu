@@ -2587,6 +2587,11 @@ int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const 
     return launch_agg<1, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
                             attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
                             partial, nullptr, nullptr, nullptr, s);
+  if (dim > 256)  // one 512-float tile per row: each edge weight computed once (9% faster
+                  // than two 256-float tiles at D=512; the backward K2 keeps two tiles)
+    return launch_agg<4, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
+                            attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
+                            partial, nullptr, nullptr, nullptr, s);
   return launch_agg<2, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
                           attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
                           partial, nullptr, nullptr, nullptr, s);
