@@ -8,7 +8,7 @@
 // registers as float4 chunks; chunk c of the row is float4 (c mod W/4) of
 // segment c div (W/4).  Mean and variance are two in-register passes.
 // Backward: one warp per row forms grad_x = rstd * (g*w - mean(g*w) -
-// xhat * mean(g*w*xhat)) and writes it back per segment; the parameter
+// xhat * mean(g*w*xhat)) in two passes and writes it back per segment; the parameter
 // gradients sum g*xhat and g over rows in fixed-size row chunks (one thread
 // per float4 column), then over chunks with colsum_rows: fixed order, no
 // atomics.
@@ -80,6 +80,9 @@ jk_ln_fwd_kernel(int64_t n, int64_t W, int64_t D, SegPtrs segs, const float* __r
   }
 }
 
+// Two passes over the row: the first forms the row sums of g*w and g*w*xhat,
+// the second reloads x, g, w (L1 hits) and writes grad_x, so a lane holds no
+// row arrays and the kernel keeps enough warps resident to cover the loads.
 template <int NCH>
 __global__ void __launch_bounds__(kJkThreads)
 jk_ln_bwd_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy, SegPtrs segs,
@@ -91,39 +94,40 @@ jk_ln_bwd_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy, 
   const int64_t wq = W / 4;
   const int64_t dq = D / 4;
   const float mu = mean[row], rs = rstd[row];
-  float4 xh[NCH], dn[NCH];
   float s1 = 0.0f, s2 = 0.0f;
-#pragma unroll
+#pragma unroll 4
   for (int k = 0; k < NCH; ++k) {
     const int64_t c = lane + 32 * k;
-    xh[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    dn[k] = xh[k];
     if (c < dq) {
       const int seg = static_cast<int>(c / wq);
       const float4 xv =
           __ldg(reinterpret_cast<const float4*>(segs.p[seg] + row * W) + (c - seg * wq));
       const float4 gv = __ldg(reinterpret_cast<const float4*>(gy + row * D) + c);
       const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + c);
-      xh[k] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
-      dn[k] = make_float4(gv.x * wv.x, gv.y * wv.y, gv.z * wv.z, gv.w * wv.w);
-      s1 += (dn[k].x + dn[k].y) + (dn[k].z + dn[k].w);
-      s2 += (dn[k].x * xh[k].x + dn[k].y * xh[k].y) + (dn[k].z * xh[k].z + dn[k].w * xh[k].w);
+      const float d0 = gv.x * wv.x, d1 = gv.y * wv.y, d2 = gv.z * wv.z, d3 = gv.w * wv.w;
+      s1 += (d0 + d1) + (d2 + d3);
+      s2 += (d0 * ((xv.x - mu) * rs) + d1 * ((xv.y - mu) * rs)) +
+            (d2 * ((xv.z - mu) * rs) + d3 * ((xv.w - mu) * rs));
     }
   }
   const float Df = static_cast<float>(D);
   s1 = warp_sum(s1);
   s2 = warp_sum(s2);
   const float f = rs / Df;
-#pragma unroll
+#pragma unroll 4
   for (int k = 0; k < NCH; ++k) {
     const int64_t c = lane + 32 * k;
     if (c < dq) {
       const int seg = static_cast<int>(c / wq);
+      const float4 xv =
+          __ldg(reinterpret_cast<const float4*>(segs.p[seg] + row * W) + (c - seg * wq));
+      const float4 gv = __ldg(reinterpret_cast<const float4*>(gy + row * D) + c);
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + c);
       float4 o;
-      o.x = f * (Df * dn[k].x - s1 - xh[k].x * s2);
-      o.y = f * (Df * dn[k].y - s1 - xh[k].y * s2);
-      o.z = f * (Df * dn[k].z - s1 - xh[k].z * s2);
-      o.w = f * (Df * dn[k].w - s1 - xh[k].w * s2);
+      o.x = f * (Df * (gv.x * wv.x) - s1 - ((xv.x - mu) * rs) * s2);
+      o.y = f * (Df * (gv.y * wv.y) - s1 - ((xv.y - mu) * rs) * s2);
+      o.z = f * (Df * (gv.z * wv.z) - s1 - ((xv.z - mu) * rs) * s2);
+      o.w = f * (Df * (gv.w * wv.w) - s1 - ((xv.w - mu) * rs) * s2);
       reinterpret_cast<float4*>(gsegs.p[seg] + row * W)[c - seg * wq] = o;
     }
   }
