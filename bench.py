@@ -152,12 +152,14 @@ def build_model_and_data(cfg, device, seed=0, capturable=False):
     model = build_model(in_dim=cfg.in_dim, hidden_dim=cfg.hidden_dim, out_dim=cfg.num_classes,
                         num_layers=cfg.layers, dropout=cfg.dropout, hop_scales=cfg.hops,
                         gat_heads=cfg.heads, gat_dropout=cfg.gat_dropout).to(device)
-    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5, capturable=capturable)
+    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5, capturable=capturable,
+                           fused=True)
     return model, opt, x, y, train
 
 
 def train_step(model, opt, op, x, y, train_idx):
-    """optimizer.zero_grad -> forward -> CE(train rows) -> backward -> Adam.step
+    """optimizer.zero_grad -> forward -> CE(train rows) -> backward -> Adam.step (torch's
+    fused Adam)
     (generic_engine/train_cign.py:2103-2148).  The train rows are gathered by
     a precomputed index (the same rows, in the same order, as the reference's
     boolean mask, without its host synchronisation)."""
@@ -353,7 +355,8 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     model.prepare_fused_gat_graph(dgat)
     torch.manual_seed(1000 + rank)  # independent dropout streams per rank
     use_graph = not args.eager
-    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5, capturable=use_graph)
+    opt = torch.optim.Adam(model.parameters(), lr=0.003, weight_decay=1e-5, capturable=use_graph,
+                           fused=True)
     x_cpu = x_all[r0:r1].contiguous()
     x = x_cpu.to(device)
     y = y_all[r0:r1].to(device)
