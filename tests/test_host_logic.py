@@ -1,0 +1,69 @@
+"""Host-side logic that needs no GPU: dropout seed streams, shape gates of
+the fused kernels, the graph-capture policy of the bench.
+
+The seed formulas are restated from the reference (collapsed_gat.py:204-211
+for GAT calls, fused_block_ops.py:46-50 for block-op calls) and checked
+against cign_b200.seeds, including the rule that p == 0 calls neither get a
+seed nor advance the stream."""
+import pytest
+import torch
+
+from cign_b200 import _pack, seeds
+from cign_b200.jk_norm import jk_norm_supported
+
+MASK63 = (1 << 63) - 1
+
+
+def reference_gat_seed(base, call_id):
+    return (base + 0x9E3779B97F4A7C15 * (call_id + 1)) & MASK63
+
+
+def reference_block_seed(base, call_1based, tag):
+    return (base + 0x9E3779B97F4A7C15 * call_1based + 0xD2B74407B1CE6E93 * int(tag)) & MASK63
+
+
+@pytest.fixture()
+def fresh_counters():
+    saved = seeds.host_counters()
+    seeds.set_host_counters(0, 0)
+    yield
+    seeds.set_host_counters(*saved)
+
+
+def test_seed_streams_follow_reference_formulas(fresh_counters):
+    torch.manual_seed(1234567)
+    base = int(torch.initial_seed()) & MASK63
+    got_gat = [seeds.next_seed(seeds.GAT, 0.3) for _ in range(3)]
+    assert got_gat == [reference_gat_seed(base, c) for c in range(3)]
+    got_block = [seeds.next_seed(seeds.BLOCK, 0.5, tag) for tag in (1, 2, 1)]
+    assert got_block == [reference_block_seed(base, c + 1, t)
+                         for c, t in zip(range(3), (1, 2, 1))]
+
+
+def test_zero_probability_does_not_advance(fresh_counters):
+    torch.manual_seed(7)
+    base = int(torch.initial_seed()) & MASK63
+    assert seeds.next_seed(seeds.GAT, 0.0) == 0
+    assert seeds.next_seed(seeds.BLOCK, 0.0, 3) == 0
+    assert seeds.host_counters() == (0, 0)
+    assert seeds.next_seed(seeds.GAT, 0.1) == reference_gat_seed(base, 0)
+
+
+@pytest.mark.parametrize("D,K,dout,ok", [(512, 3, 512, True), (32, 1, 32, True),
+                                         (48, 2, 64, False), (512, 9, 512, False),
+                                         (512, 3, 1024, False), (512, 3, 48, False)])
+def test_pack_proj_shape_gate(D, K, dout, ok):
+    assert _pack.pack_proj_supported(D, K, dout) is ok
+
+
+def test_jk_norm_gate_needs_cuda_fp32_equal_widths():
+    cpu = [torch.zeros(4, 8) for _ in range(3)]
+    assert not jk_norm_supported(cpu)  # CPU tensors: the torch path is used
+    assert not jk_norm_supported([])
+
+
+def test_graph_capture_policy():
+    import bench
+    from cign_b200 import synth
+    assert synth.CONFIGS["cfg2"].num_nodes <= bench.GRAPH_CAPTURE_MAX_NODES
+    assert synth.CONFIGS["cfg4"].num_nodes > bench.GRAPH_CAPTURE_MAX_NODES
