@@ -528,19 +528,20 @@ class _DistHopFn(torch.autograd.Function):
         x_own = x_own.contiguous()
         halo, ev = hop.exchange.gather_halo(x_own)
         y = hop.own.spmm(x_own)
-        if hop.halo is None:
-            return y
         if ev is not None:
             torch.cuda.current_stream(x_own.device).wait_event(ev)
+        if hop.halo is None:
+            return y
         return hop.halo.spmm(halo, addend=y)
 
     @staticmethod
     def backward(ctx, g):
         hop = ctx.hop
         g = g.contiguous()
-        if hop.halo is None:
-            return hop.own.spmm(g, transpose=True), None
-        g_halo = hop.halo.spmm(g, transpose=True)
+        # a rank without halo columns returns nothing but still takes the
+        # exchange's steps (its collective) like every other rank
+        g_halo = (g.new_zeros((0, g.size(1))) if hop.halo is None
+                  else hop.halo.spmm(g, transpose=True))
         recv, ev = hop.exchange.return_halo(g_halo)
         g_own = hop.own.spmm(g, transpose=True)
         if ev is not None:

@@ -10,9 +10,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from cign_b200 import synth
-from cign_b200.distributed import (HaloExchange, HaloPlan, _local_block, halo_gather,
-                                   partition_rows)
+from cign_b200 import distributed, synth
+from cign_b200.distributed import (DistMultiHop, HaloExchange, HaloPlan, _local_block,
+                                   halo_gather, partition_rows)
 from cign_b200.graph_operator import build_sparse_normalized_adjacency
 
 
@@ -116,6 +116,109 @@ def test_halo_exchange_gloo(world):
     errors = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_exchange_worker, args=(r, world, port, errors)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    msgs = []
+    while not errors.empty():
+        msgs.append(errors.get())
+    assert not msgs, msgs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+class _CpuPlan:
+    """CPU stand-in for the native SpmmPlan of a partitioned block (the
+    host logic around it is what these tests cover)."""
+
+    def __init__(self, rows, cols, vals, n_rows, n_cols, dev):
+        self.A = torch.sparse_coo_tensor(torch.stack([rows, cols]), vals,
+                                         (n_rows, n_cols)).coalesce()
+
+    def spmm(self, x, transpose=False, addend=None):
+        y = torch.sparse.mm(self.A.t() if transpose else self.A, x)
+        return y if addend is None else y + addend
+
+
+class _RecordingExchange(HaloExchange):
+    """The base exchange, recording the sequence of exchange steps."""
+
+    def __init__(self, plan):
+        super().__init__(plan, "cpu")
+        self.calls = []
+
+    def gather_halo(self, x_own):
+        self.calls.append("gather_halo")
+        return super().gather_halo(x_own)
+
+    def return_halo(self, g_halo):
+        self.calls.append("return_halo")
+        return super().return_halo(g_halo)
+
+    def add_returned(self, g_own, recv):
+        self.calls.append("add_returned")
+        super().add_returned(g_own, recv)
+
+
+def _two_component_csr():
+    """Nodes 0-399 and 400-599 form two unconnected graphs."""
+    a = synth.powerlaw_graph(400, 3000, seed=4)
+    b = synth.powerlaw_graph(200, 1500, seed=5) + 400
+    _, adj = build_sparse_normalized_adjacency(torch.cat([a, b], dim=1), 600)
+    return adj.coalesce().to_sparse_csr()
+
+
+def _khop_worker(rank, world, port, errors):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        distributed._csr_plan = _CpuPlan  # CPU stand-in for the native plans
+        P = _two_component_csr()
+        bounds = [0, 200, 400, 600]  # rank 2 owns the second graph: no halo columns
+        me = HaloPlan(P.crow_indices(), P.col_indices(), bounds, rank)
+        assert (me.n_halo == 0) == (rank == 2)
+        ex = _RecordingExchange(me)
+        hop = DistMultiHop(P, me, ex)
+        gen = torch.Generator().manual_seed(21)
+        X = torch.randn(600, 4, generator=gen)
+        Gs = {p: torch.randn(600, 4, generator=gen) for p in (1, 2, 3)}
+        x_own = X[me.r0:me.r1].clone().requires_grad_(True)
+        outs = hop.powers(x_own, (1, 2, 3))
+        loss = sum((outs[p] * Gs[p][me.r0:me.r1]).sum() for p in (1, 2, 3))
+        loss.backward()
+        Y, want_grad, Pt = X, torch.zeros(600, 4), P.t()
+        for p in (1, 2, 3):
+            Y = P @ Y
+            assert torch.allclose(outs[p].detach(), Y[me.r0:me.r1], atol=1e-5), p
+            g = Gs[p]
+            for _ in range(p):
+                g = Pt @ g
+            want_grad += g
+        assert torch.allclose(x_own.grad, want_grad[me.r0:me.r1], atol=1e-5)
+        # every rank took the same exchange steps in the same order
+        seqs = [None] * world
+        dist.all_gather_object(seqs, ex.calls)
+        assert all(q == seqs[0] for q in seqs), seqs
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # pragma: no cover - reported to the parent
+        errors.put(f"rank {rank}: {exc!r}")
+        raise
+
+
+def test_partitioned_khop_with_a_halo_free_rank_gloo():
+    """k-hop forward and backward over three ranks, one of which has no halo
+    columns: results equal the global P^p X and its gradient, and all ranks
+    take the same sequence of exchange steps (one collective each on the
+    peer-memory transport)."""
+    ctx = mp.get_context("spawn")
+    errors = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_khop_worker, args=(r, 3, port, errors)) for r in range(3)]
     for p in procs:
         p.start()
     for p in procs:
