@@ -611,8 +611,6 @@ def cpu_sample_config(cfg, sample_nodes):
 def run_cpu_oracle(cfg, steps, warmup, budget_s=None):
     """The reference's torch path restated in oracle/ (CPU, all host threads)
     on one sampled graph of the workload's family; returns (GTEPS, s/step)."""
-    import numpy as np
-
     from cign_b200 import synth
     from oracle import graph as og
     from oracle import ops

@@ -12,7 +12,6 @@ from __future__ import annotations
 
 import torch
 
-from . import _lib
 from .multihop_csr_pipeline import (
     GenericMultiHopCSRGraphOperator,
     HybridNative3TailCSRGraphOperator,

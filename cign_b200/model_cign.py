@@ -30,7 +30,6 @@ blocks, JK concat, LayerNorm, dropout, classifier.
 from __future__ import annotations
 
 import math
-from typing import Optional, Sequence
 
 import torch
 import torch.nn as nn

@@ -15,8 +15,6 @@ reference), so parity tests run with dropout 0.
 """
 from __future__ import annotations
 
-import math
-
 import torch
 import torch.nn as nn
 import torch.nn.functional as F

@@ -9,7 +9,6 @@ from __future__ import annotations
 
 from typing import Dict, Optional, Sequence
 
-import numpy as np
 import torch
 import torch.nn.functional as F
 

@@ -5,7 +5,6 @@ suite runs with `-m "not gpu"`).  GPU tests never skip silently when the
 native library is missing: they fail, because the product path has no
 CPU fallback.
 """
-import os
 import sys
 from pathlib import Path
 

@@ -1,5 +1,4 @@
 """Comparison helpers shared by the GPU parity tests."""
-import numpy as np
 import torch
 
 

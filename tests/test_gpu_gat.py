@@ -9,7 +9,6 @@ from cign_b200.collapsed_gat import collapsed_gat_mean_bias_silu, gat_dropout_ma
 from cign_b200.fused_gat_sideops import fused_attention_logits, fused_head_mean_bias_silu
 from cign_b200.graph_operator import prepare_gat_edge_index, to_graph_format
 from cign_b200.plans import gat_plan_for
-from oracle import graph as og
 from oracle import ops, rng
 from tests.helpers import assert_parity
 

@@ -2,7 +2,6 @@
 reference model's own outputs and parameter gradients (golden, produced by
 generic_engine/model_cign.py with every fused switch off), at the
 reference's thresholds (validate_cign_acceleration.py:53-57)."""
-import numpy as np
 import pytest
 import torch
 

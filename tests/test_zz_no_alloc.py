@@ -9,8 +9,6 @@ reduction scratch is a fixed array inside the library instead of a buffer
 the caller passes.  This file is named so that pytest collects it last; it
 also passes on its own in a fresh process.
 """
-import ctypes
-
 import pytest
 import torch
 
