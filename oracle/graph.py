@@ -3,7 +3,7 @@
 * ``normalized_adjacency``: generic_engine/train_cign.py:1558-1589
   (to_undirected -> add self loops -> degree over `col`, clamp(min=1),
   w = d^-1/2[row] * d^-1/2[col] in fp32 -> coalesce, duplicates summed).
-* ``csr_of`` / ``csr_transpose``: prepare_fixed_csr_operator, model.py:162-199
+* ``csr_of`` / ``csr_transpose``: prepare_fixed_csr_operator, model.py:149-186
   (coalesce = sort by (row, col) and sum duplicates; P^T by flipping the
   indices and coalescing again).
 * ``gat_graph``: prepare_gat_edge_index (train_cign.py:1759-1771) followed by
@@ -19,6 +19,9 @@ import numpy as np
 
 
 def to_undirected(edge_index: np.ndarray, n: int) -> np.ndarray:
+    """Both directions of every edge, deduplicated and sorted by (row, col): the
+    to_undirected step of build_sparse_normalized_adjacency
+    (generic_engine/train_cign.py:1558-1589)."""
     row = np.asarray(edge_index[0], dtype=np.int64)
     col = np.asarray(edge_index[1], dtype=np.int64)
     key = np.unique(np.concatenate([row * n + col, col * n + row]))
@@ -26,7 +29,8 @@ def to_undirected(edge_index: np.ndarray, n: int) -> np.ndarray:
 
 
 def coalesce(row, col, val, n_rows: int, n_cols: int):
-    """Sort by (row, col) and sum duplicate entries (torch COO coalesce)."""
+    """Sort by (row, col) and sum duplicate entries: torch COO coalesce, as
+    prepare_fixed_csr_operator applies it (model.py:161-163, 176-183)."""
     key = np.asarray(row, np.int64) * n_cols + np.asarray(col, np.int64)
     order = np.argsort(key, kind="stable")
     key = key[order]
@@ -38,7 +42,8 @@ def coalesce(row, col, val, n_rows: int, n_cols: int):
 
 def normalized_adjacency(edge_index: np.ndarray, n: int, use_undirected: bool = True,
                          add_self_loop: bool = True):
-    """Coalesced COO (row, col, val fp32) of D^-1/2 (A + I) D^-1/2."""
+    """Coalesced COO (row, col, val fp32) of D^-1/2 (A + I) D^-1/2
+    (generic_engine/train_cign.py:1558-1589)."""
     ei = to_undirected(edge_index, n) if use_undirected else np.asarray(edge_index, np.int64)
     if add_self_loop:
         loops = np.arange(n, dtype=np.int64)
@@ -52,19 +57,22 @@ def normalized_adjacency(edge_index: np.ndarray, n: int, use_undirected: bool = 
 
 
 def csr_of(row, col, val, n_rows: int):
-    """CSR arrays (crow int64 [n_rows+1], col int64, val) of a coalesced COO."""
+    """CSR arrays (crow int64 [n_rows+1], col int64, val) of a coalesced COO:
+    the to_sparse_csr conversion of prepare_fixed_csr_operator (model.py:149-186)."""
     crow = np.zeros(n_rows + 1, dtype=np.int64)
     np.cumsum(np.bincount(np.asarray(row, np.int64), minlength=n_rows), out=crow[1:])
     return crow, np.asarray(col, np.int64), np.asarray(val)
 
 
 def csr_transpose(row, col, val, n: int):
-    """CSR of P^T: flip the indices and coalesce (model.py:186-197)."""
+    """CSR of P^T: flip the indices and coalesce (model.py:176-186)."""
     r, c, v = coalesce(col, row, val, n, n)
     return csr_of(r, c, v, n)
 
 
 def prepare_gat_edge_index(edge_index: np.ndarray, n: int) -> np.ndarray:
+    """Remove self-loops, then add exactly one per node
+    (generic_engine/train_cign.py:1759-1771)."""
     ei = np.asarray(edge_index, np.int64)
     ei = ei[:, ei[0] != ei[1]]
     loops = np.arange(n, dtype=np.int64)

@@ -23,6 +23,9 @@ from . import ops, rng
 
 
 class OracleGAT(nn.Module):
+    """GATConv(concat=False) + bias + SiLU on the collapsed-GAT restatement
+    (CompatibleCollapsedFusedGATConv.forward, generic_engine/model_cign.py:524-570)."""
+
     def __init__(self, in_channels, out_channels, heads, dropout, negative_slope=0.2):
         super().__init__()
         self.heads, self.out_channels = heads, out_channels
@@ -43,6 +46,9 @@ class OracleGAT(nn.Module):
 
 
 class OracleBlock(nn.Module):
+    """GraphCliffordBlock with every fused switch off
+    (generic_engine/model_cign.py:573-937)."""
+
     def __init__(self, hidden_dim, order_set, dropout, gat_heads, gat_dropout, init_gamma=0.49):
         super().__init__()
         self.hidden_dim = hidden_dim
@@ -74,6 +80,9 @@ class OracleBlock(nn.Module):
 
 
 class OracleCIGN(nn.Module):
+    """GraphCliffordNet: dual input projection, blocks, JK concat, LayerNorm,
+    classifier (generic_engine/model_cign.py:943-1215)."""
+
     def __init__(self, in_dim, hidden_dim, out_dim, num_layers, order_set, dropout, gat_heads,
                  gat_dropout, init_gamma=0.49, init_input_eta=0.1):
         super().__init__()

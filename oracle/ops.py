@@ -17,6 +17,8 @@ from . import rng
 
 # --------------------------------------------------------------------- SpMM
 def csr_tensor(crow, col, val, n_rows: int, n_cols: int) -> torch.Tensor:
+    """CSR(P) as a torch CPU tensor, the form prepare_fixed_csr_operator
+    caches (model.py:149-186)."""
     return torch.sparse_csr_tensor(torch.as_tensor(crow, dtype=torch.int64),
                                    torch.as_tensor(col, dtype=torch.int64),
                                    torch.as_tensor(val, dtype=torch.float32),
@@ -24,7 +26,8 @@ def csr_tensor(crow, col, val, n_rows: int, n_cols: int) -> torch.Tensor:
 
 
 class _FixedSpMM(torch.autograd.Function):
-    """Y = P X, grad_X = P^T grad_Y (model.py:106-131, CPU torch.sparse.mm)."""
+    """Y = P X, grad_X = P^T grad_Y: FixedCSRSpMMFunction (model.py:57-106),
+    with CPU torch.sparse.mm."""
 
     @staticmethod
     def forward(ctx, x, P, PT):
@@ -37,6 +40,7 @@ class _FixedSpMM(torch.autograd.Function):
 
 
 def spmm(P, PT, x):
+    """fixed_sparse_mm: one application of P (model.py:189-192)."""
     return _FixedSpMM.apply(x, P, PT)
 
 
@@ -127,7 +131,7 @@ def head_mean_bias_silu(out, bias):
 # --------------------------------------------------------------------- pack
 def pack(H, C, props: Sequence[torch.Tensor], alpha: Optional[torch.Tensor], interaction: str,
          outer: str, weighting: str):
-    """Clifford pack family: validate_a3.py:219-230 (old interaction),
+    """Clifford pack family: validate_a3.py:8-19 legacy_pack (old interaction),
     validate_cign_switch_pack.py:17-50 (tanh switch) and
     validate_cign_acceleration.py:10-18 (CIGN, no outer nonlinearity)."""
     Ds, Ws = [], []
@@ -169,6 +173,8 @@ def dropout_layernorm(x, w, b, p: float, eps: float, seed: int):
 
 
 def add_layernorm(a, b, w, bias, eps: float):
+    """LN(a + b) (generic_engine/validate_a3v8.py:29; fused_add_layernorm,
+    fused_block_ops.py:112)."""
     return F.layer_norm(a + b, (a.size(1),), w, bias, eps)
 
 

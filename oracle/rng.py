@@ -22,6 +22,7 @@ MASK63 = (1 << 63) - 1
 
 
 def splitmix64(x) -> np.ndarray:
+    """The splitmix64 finaliser (collapsed_gat_cuda.cu:27-32), elementwise on uint64."""
     x = np.asarray(x, dtype=np.uint64)
     with np.errstate(over="ignore"):
         x = x + GOLDEN
@@ -37,7 +38,8 @@ def _hash(seed: int, count: int) -> np.ndarray:
 
 
 def gat_keep_mask(seed: int, count: int, p: float) -> np.ndarray:
-    """bool [count]: the attention keep-mask (p <= 0 keeps everything)."""
+    """bool [count]: the attention keep-mask (collapsed_gat_cuda.cu:34-47);
+    p <= 0 keeps everything."""
     if float(p) <= 0.0:
         return np.ones(int(count), dtype=bool)
     hi = (_hash(seed, count) >> np.uint64(32)).astype(np.uint32)
@@ -46,7 +48,8 @@ def gat_keep_mask(seed: int, count: int, p: float) -> np.ndarray:
 
 
 def block_keep_mask(seed: int, count: int, p: float) -> np.ndarray:
-    """bool [count]: the block-op keep-mask."""
+    """bool [count]: the block-op keep-mask (dropout_keep of
+    fused_block_ops.py:15)."""
     if float(p) <= 0.0:
         return np.ones(int(count), dtype=bool)
     r = _hash(seed, count) >> np.uint64(11)
