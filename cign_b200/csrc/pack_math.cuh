@@ -8,7 +8,7 @@ namespace cign {
 
 // D/W of one channel and their partial derivatives w.r.t. b_hr and b_rh
 // (the reference's compute_dw, switch pack cu:22-58, plus the "old"
-// interaction of fused_clifford_pack_cuda.cu:40-46).
+// interaction of fused_clifford_pack_cuda.cu:47-49).
 struct DW {
   float D, W, dD_hr, dD_rh, dW_hr, dW_rh;
 };

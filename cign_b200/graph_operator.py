@@ -24,7 +24,7 @@ from .plans import spmm_plan_for
 
 
 class FixedCSRSpMMFunction(torch.autograd.Function):
-    """Y = P X; grad_X = P^T grad_Y (model.py:106-131), on the native SpMM."""
+    """Y = P X; grad_X = P^T grad_Y (model.py:57-106), on the native SpMM."""
 
     @staticmethod
     def forward(ctx, X: torch.Tensor, operator_csr: torch.Tensor, operator_t_csr: torch.Tensor):
@@ -52,7 +52,7 @@ class FixedCSRSpMMFunction(torch.autograd.Function):
 
 
 class FixedCSRGraphOperator:
-    """Immutable cache holding CSR(P) and CSR(P^T) (model.py:134-159)."""
+    """Immutable cache holding CSR(P) and CSR(P^T) (model.py:109-146)."""
 
     __slots__ = ("csr", "csr_t", "shape", "nnz", "dtype", "device", "info")
 
@@ -85,7 +85,7 @@ def _clone_csr_storage(csr: torch.Tensor) -> torch.Tensor:
 
 @torch.no_grad()
 def prepare_fixed_csr_operator(operator: torch.Tensor) -> FixedCSRGraphOperator:
-    """COO/CSR operator -> cached CSR(P), CSR(P^T) (model.py:162-199)."""
+    """COO/CSR operator -> cached CSR(P), CSR(P^T) (model.py:149-186)."""
     if not isinstance(operator, torch.Tensor):
         raise TypeError(f"operator must be a torch.Tensor, got {type(operator)!r}")
     if operator.dim() != 2 or operator.size(0) != operator.size(1):
@@ -182,7 +182,7 @@ def build_sparse_normalized_adjacency(edge_index: torch.Tensor, num_nodes: int,
 
 @torch.no_grad()
 def prepare_gat_edge_index(edge_index: torch.Tensor, num_nodes: int) -> torch.Tensor:
-    """Remove self-loops, then add exactly one per node (train_cign.py:1759-1771)."""
+    """Remove self-loops, then add exactly one per node (generic_engine/train_cign.py:1759-1771)."""
     mask = edge_index[0] != edge_index[1]
     ei = edge_index[:, mask]
     loops = torch.arange(num_nodes, device=edge_index.device, dtype=edge_index.dtype)
@@ -198,7 +198,7 @@ def to_graph_format(edge_index_dst_src: torch.Tensor, num_nodes: int):
     * perm[csc position] = CSR edge id.
 
     This is the convention the reference's GAT kernels read
-    (collapsed_gat_cuda.cu:227-248, model_cign.py:1121-1145); the PyG helper it
+    (collapsed_gat_cuda.cu:227-248, generic_engine/model_cign.py:1117-1146); the PyG helper it
     obtains it from is not vendored, so the order is defined here.
     Returns ((rowptr, col), (row, colptr), perm), all int32 and contiguous.
     """

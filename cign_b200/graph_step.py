@@ -1,6 +1,6 @@
 """A whole training step captured in one CUDA graph.
 
-The reference runs every step eagerly from Python (train_cign.py:2103-2148),
+The reference runs every step eagerly from Python (generic_engine/train_cign.py:2103-2148),
 which costs several milliseconds of host time per step at cfg2 scale -- more
 than the device needs.  :class:`GraphedStep` runs a step function a few
 times eagerly (on a side stream, so lazy initialisation happens outside the

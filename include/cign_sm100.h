@@ -63,7 +63,7 @@ CIGN_API uint64_t cign_kernel_launches(void);
 
 /* ------------------------------------------------------------------ CSR
  * A fixed sparse graph operator in CSR form (device arrays).
- * Replaces the CSR parts held by FixedCSRGraphOperator (model.py:134-159)
+ * Replaces the CSR parts held by FixedCSRGraphOperator (model.py:109-146)
  * and cloned to int32 by _csr_parts_int32 (multihop_csr_pipeline.py:38-48). */
 typedef struct cign_csr_f32 {
   int64_t rows;
@@ -113,7 +113,7 @@ CIGN_API size_t cign_spmm_workspace_bytes(const cign_spmm_plan* plan, int64_t F)
  * rectangular (a row block of a partitioned operator); its transposed
  * product then needs `pt` at plan creation.  addend may be NULL.  Y must not
  * alias X.
- * Replaces FixedCSRSpMMFunction.forward/backward (model.py:106-131). */
+ * Replaces FixedCSRSpMMFunction.forward/backward (model.py:57-106). */
 CIGN_API int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X,
               int64_t F, const float* addend, float* Y, void* ws,
               size_t ws_bytes, cign_stream_t stream);

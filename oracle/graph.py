@@ -6,9 +6,9 @@
 * ``csr_of`` / ``csr_transpose``: prepare_fixed_csr_operator, model.py:149-186
   (coalesce = sort by (row, col) and sum duplicates; P^T by flipping the
   indices and coalescing again).
-* ``gat_graph``: prepare_gat_edge_index (train_cign.py:1759-1771) followed by
+* ``gat_graph``: prepare_gat_edge_index (generic_engine/train_cign.py:1759-1771) followed by
   the destination-major CSR/CSC/perm layout read by the reference's GAT
-  kernels (collapsed_gat_cuda.cu:227-248; model_cign.py:1121-1145).
+  kernels (collapsed_gat_cuda.cu:227-248; generic_engine/model_cign.py:1117-1146).
 
 The fp32 products are evaluated in float32 exactly as torch does, so the
 values are bit-identical to the reference's, not merely close.
@@ -81,7 +81,7 @@ def prepare_gat_edge_index(edge_index: np.ndarray, n: int) -> np.ndarray:
 
 def gat_graph(edge_index_src_dst: np.ndarray, n: int):
     """((rowptr, col), (row, colptr), perm) for a PyG-style source->target edge
-    list: rows are destinations (edge_index.flip(0), model_cign.py:1121),
+    list: rows are destinations (edge_index.flip(0), generic_engine/model_cign.py:1118),
     CSR sorted by (row, col) keeping duplicates, CSC a stable re-sort by
     column, perm[csc position] = CSR edge id."""
     dst = np.asarray(edge_index_src_dst[1], np.int64)
