@@ -67,3 +67,23 @@ def test_graph_capture_policy():
     from cign_b200 import synth
     assert synth.CONFIGS["cfg2"].num_nodes <= bench.GRAPH_CAPTURE_MAX_NODES
     assert synth.CONFIGS["cfg4"].num_nodes > bench.GRAPH_CAPTURE_MAX_NODES
+
+
+def test_algorithmic_bytes_at_cfg2_shapes():
+    """Roofline numerators (compulsory HBM bytes per launch: every tensor read
+    or written once) at cfg2's shapes, N=24,492, nnz=390,042, D=512, F=2D,
+    H=4, K=3; the figures of the per-kernel bandwidth table in profiles/."""
+    import bench
+    N, nnz, D, H, K = 24492, 390042, 512, 4, 3
+    F = 2 * D
+    ab = bench.algorithmic_bytes
+    # SpMM pass: crow, col + val, X read, Y written (+ the fused addend)
+    assert ab("spmm", N, nnz, F=F) == 4 * (N + 1) + 8 * nnz + 8 * N * F == 203_856_772
+    assert ab("spmm_add", N, nnz, F=F) == 304_176_004
+    assert ab("gat_agg_fwd", N, nnz, H=H, D=D, nnz_g=nnz) == 254_023_708
+    assert ab("gat_agg_bwd", N, nnz, H=H, D=D, C=D, nnz_g=nnz) == 508_823_840
+    assert ab("pack_fwd", N, nnz, D=D, K=K) == 702_528_528
+    assert ab("pack_bwd", N, nnz, D=D, K=K) == 1_104_099_360
+    assert ab("pack_proj", N, nnz, D=D, K=K, C=D) == 758_981_648
+    with pytest.raises(ValueError):
+        ab("unknown", N, nnz)
