@@ -105,17 +105,25 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        rows = []
         try:
-            for line in Path(self.path).read_text().splitlines():
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+            lines = Path(self.path).read_text().splitlines()
         finally:
             try:
                 os.unlink(self.path)
             except OSError:
                 pass
+        return self.summarize(lines)
+
+    @staticmethod
+    def summarize(lines):
+        """{sm_mhz: median, sm_max_mhz, reasons: throttle reasons seen Active,
+        samples} of `nvidia-smi --query-gpu=QUERY --format=csv,noheader,nounits`
+        lines, or None without samples."""
+        rows = []
+        for line in lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]

@@ -87,3 +87,22 @@ def test_algorithmic_bytes_at_cfg2_shapes():
     assert ab("pack_proj", N, nnz, D=D, K=K, C=D) == 758_981_648
     with pytest.raises(ValueError):
         ab("unknown", N, nnz)
+
+
+def test_clock_summary_of_nvidia_smi_samples():
+    """The bench's clock record from `nvidia-smi --query-gpu` CSV lines (a
+    fake sample: no GPU, no NVML): median SM clock under load, the max clock,
+    and every throttle reason seen Active."""
+    import bench
+    lines = [
+        "0, 1965, 1965, 650.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "0, 1800, 1965, 990.3, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, 1845, 1965, 995.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "garbage line",
+    ]
+    got = bench.ClockSampler.summarize(lines)
+    assert got == {"sm_mhz": 1845.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
+                   "samples": 3}
+    hot = lines[:1] + ["0, 1200, 1965, 700.0, 0x48, Active, Not Active, Active, Not Active"]
+    assert bench.ClockSampler.summarize(hot)["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+    assert bench.ClockSampler.summarize([]) is None
