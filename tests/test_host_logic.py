@@ -106,3 +106,32 @@ def test_clock_summary_of_nvidia_smi_samples():
     hot = lines[:1] + ["0, 1200, 1965, 700.0, 0x48, Active, Not Active, Active, Not Active"]
     assert bench.ClockSampler.summarize(hot)["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
     assert bench.ClockSampler.summarize([]) is None
+
+
+def test_hop_roofline_from_recorded_events():
+    """The bench's `roofline` object from k-hop timer records (fake CUDA
+    events): algorithmic bytes per launch over the measured time per launch."""
+    import bench
+
+    class _Ev:
+        def __init__(self, ms):
+            self.ms = ms
+
+        def elapsed_time(self, end):
+            return end.ms - self.ms
+
+    class _Timer:
+        records = [("fwd", 3, 0, 1024, _Ev(0.0), _Ev(0.6), None, None),
+                   ("bwd", 3, 2, 1024, _Ev(1.0), _Ev(1.9), None, None)]
+
+    N, nnz, F = 24492, 390042, 1024
+    r = bench.hop_roofline(_Timer(), N, nnz, 6449.7, "measured", with_traffic=False)
+    alg = 4 * bench.algorithmic_bytes("spmm", N, nnz, F=F) + 2 * bench.algorithmic_bytes(
+        "spmm_add", N, nnz, F=F)
+    assert r["launches_timed"] == 6 and r["launch_mix"] == {"fwd": 3, "bwd_add": 2, "bwd": 1}
+    assert r["algorithmic_bytes"] == int(alg / 6)
+    assert abs(r["ms_per_launch"] - 1.5 / 6) < 1e-9
+    assert abs(r["achieved"] - alg / 1.5e-3 / 1e9) < 0.1
+    assert abs(r["frac"] - r["achieved"] / 6449.7) < 1e-4
+    assert r["traffic"] is None and r["bound"] == "hbm" and r["unit"] == "GB/s"
+    assert bench.hop_roofline(type("T", (), {"records": []})(), N, nnz, 1.0, "x") is None
