@@ -81,3 +81,45 @@ def test_python_api_requires_cuda_without_fallback():
     with pytest.raises(TypeError):
         fused_block_ops.fused_add_layernorm(torch.zeros(2, 4), torch.zeros(2, 4), torch.ones(4),
                                             torch.zeros(4), 1e-5)
+
+
+def test_python_api_raises_the_reference_exception_types():
+    """Bad inputs raise what the reference raises, before any launch:
+    multihop_csr_pipeline.py:38-48, 94-101, 171; collapsed_gat.py:184-187;
+    fused_gat_sideops.py:96; fused_clifford_pack.py:29;
+    fused_block_ops.py:102-104."""
+    import torch
+    from cign_b200 import collapsed_gat, fused_block_ops, fused_clifford_pack, fused_gat_sideops
+    from cign_b200 import multihop_csr_pipeline as mh
+    if torch.cuda.is_available():
+        pytest.skip("CUDA present: the device checks would pass")
+    csr = torch.eye(4).to_sparse_csr()
+
+    class Base:  # a prepared FixedCSRGraphOperator as the reference expects it
+        shape, nnz = (4, 4), 4
+
+    Base.csr = Base.csr_t = csr
+    with pytest.raises(TypeError):
+        mh._csr_parts_int32(torch.eye(4))
+    with pytest.raises(RuntimeError):
+        mh._csr_parts_int32(csr)
+    with pytest.raises(ValueError):
+        mh.MultiHopCSR3GraphOperator(Base(), dense_cols=0)
+    with pytest.raises(ValueError):
+        mh.MultiHopCSR3GraphOperator(Base(), dense_cols=8, algorithm=5)
+    with pytest.raises(TypeError):
+        mh.MultiHopCSR3GraphOperator(object(), dense_cols=8)
+    with pytest.raises(ValueError):
+        mh.prepare_multihop_csr_operator(Base(), 8, powers=())
+    x = torch.zeros(4, 2, 3)
+    with pytest.raises(TypeError):
+        collapsed_gat.collapsed_gat_mean_bias_silu(torch.zeros(4, 2), torch.zeros(4, 2), None,
+                                                   None, None, 0.2, x, torch.zeros(3), 0.0)
+    with pytest.raises(TypeError):
+        fused_gat_sideops.fused_attention_logits(x, torch.zeros(1, 2, 3), torch.zeros(1, 2, 3))
+    with pytest.raises(RuntimeError):
+        fused_clifford_pack.fused_clifford_pack(torch.zeros(4, 8), torch.zeros(4, 8),
+                                                [torch.zeros(4, 16)] * 3, None)
+    with pytest.raises(TypeError):
+        fused_block_ops.fused_dropout_layernorm(torch.zeros(4, 8), torch.ones(8), torch.zeros(8),
+                                                0.1, 1e-5)
