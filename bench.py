@@ -610,7 +610,12 @@ def run_sweep(args, device):
 
 # ------------------------------------------------------------------ CPU arm
 def cpu_sample_config(cfg, sample_nodes):
+    """The CPU arm's bounded sample of a workload: the same generator and
+    average degree on min(sample_nodes, N) nodes (the whole workload when it
+    is that small already)."""
     from dataclasses import replace
+    if sample_nodes >= cfg.num_nodes:
+        return cfg
     scale = sample_nodes / cfg.num_nodes
     return replace(cfg, name=cfg.name + f"_sample{sample_nodes}", num_nodes=sample_nodes,
                    num_edges=int(round(cfg.num_edges * scale)))
@@ -676,6 +681,8 @@ def main():
                          "cuBLAS (separate), or fused only when G_raw is recomputed (auto)")
     ap.add_argument("--sweep-ops", default="",
                     help="comma-separated subset of the sweep: spmm,gat,pack (default all)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the workload's number of CIGN blocks (0: the config's)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="halo exchange of the multi-GPU run")
     ap.add_argument("--eager", action="store_true",
@@ -690,6 +697,9 @@ def main():
 
     from cign_b200 import synth
     cfg = synth.CONFIGS[args.workload]
+    if args.layers > 0:
+        from dataclasses import replace as dc_replace
+        cfg = dc_replace(cfg, layers=args.layers)
     metric = "CIGN fwd+bwd train-step GTEPS (SpMM edge-passes/s)"
     from cign_b200 import block_fused
     block_fused.USE_TCGEN05_PACK_PROJ = {"auto": None, "fused": True,

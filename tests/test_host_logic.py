@@ -135,3 +135,15 @@ def test_hop_roofline_from_recorded_events():
     assert abs(r["frac"] - r["achieved"] / 6449.7) < 1e-4
     assert r["traffic"] is None and r["bound"] == "hbm" and r["unit"] == "GB/s"
     assert bench.hop_roofline(type("T", (), {"records": []})(), N, nnz, 1.0, "x") is None
+
+
+def test_cpu_sample_is_never_larger_than_the_workload():
+    import bench
+    from cign_b200 import synth
+    cfg1, cfg2 = synth.CONFIGS["cfg1"], synth.CONFIGS["cfg2"]
+    assert bench.cpu_sample_config(cfg1, 6000) is cfg1
+    s = bench.cpu_sample_config(cfg2, 6000)
+    assert s.num_nodes == 6000 and s.name == "cfg2_powerlaw24492_sample6000"
+    assert s.num_edges == round(cfg2.num_edges * 6000 / cfg2.num_nodes)
+    assert (s.hidden_dim, s.hops, s.heads, s.layers) == (cfg2.hidden_dim, cfg2.hops, cfg2.heads,
+                                                         cfg2.layers)
