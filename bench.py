@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload ("cfg2"): full CIGN forward + backward +
+Workload ("cfg2", the headline configuration): full CIGN forward + backward +
 Adam step, fp32 (TF32 dense GEMMs as the reference's default), on a seeded
 synthetic power-law graph (N=24,492, 186,100 directed edges, exponent 2.5),
 features [N,300] ~ N(0,1), 5 uniform classes, hidden 512 (= 64 channels x 8

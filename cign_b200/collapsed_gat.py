@@ -18,6 +18,8 @@ collapsed_gat.cpp:67-68) any 1 <= H <= 64 and C >= 1 run natively.
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from . import _lib, seeds
@@ -293,6 +295,66 @@ class _AggregateFirstGATFn(torch.autograd.Function):
         grad_w = gfeat2.t().mm(x)                                   # [H*C, D]
         grad_x = gfeat2.mm(weight)                                  # [N_cols, D]
         return grad_x, grow, gcol, grad_w, grad_bias, None, None, None, None, None
+
+
+@contextlib.contextmanager
+def _full_fp32_matmul():
+    """cuBLAS in full fp32 inside the block (TF32 off), the caller's setting after."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        yield
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+class _LogitsThroughWeightFn(torch.autograd.Function):
+    """alpha [N, 2H] = x @ V^T, V = [W_h^T att_src[h] ; W_h^T att_dst[h]]: the
+    attention logits of lin(x) (the attention-logit side op on
+    lin(x).view(N, H, C), fused_gat_sideops.py:50-71) without forming lin(x).
+
+    Always full fp32, whatever the TF32 setting: the parameter gradients of
+    att_src / att_dst are sums over every node of terms that largely cancel,
+    and TF32-rounded operands there cost percent-level relative error; the
+    products are N*D*2H multiply-adds, a negligible share of the step."""
+
+    @staticmethod
+    def forward(ctx, x, weight, att_src, att_dst, heads):
+        H = int(heads)
+        HC, D = (int(s) for s in weight.shape)
+        C = HC // H
+        Wv = weight.view(H, C, D)
+        V = torch.cat([(Wv * att_src.reshape(H, C, 1)).sum(1),
+                       (Wv * att_dst.reshape(H, C, 1)).sum(1)], 0)           # [2H, D]
+        with _full_fp32_matmul():
+            alpha = x.mm(V.t())
+        ctx.save_for_backward(x, weight, att_src, att_dst, V)
+        ctx.heads = H
+        return alpha
+
+    @staticmethod
+    def backward(ctx, g):
+        x, weight, att_src, att_dst, V = ctx.saved_tensors
+        H = ctx.heads
+        HC, D = (int(s) for s in weight.shape)
+        C = HC // H
+        g = g.contiguous()
+        with _full_fp32_matmul():
+            gx = g.mm(V) if ctx.needs_input_grad[0] else None
+            gV = g.t().mm(x)                                                 # [2H, D]
+        gVs, gVd = gV[:H].reshape(H, 1, D), gV[H:].reshape(H, 1, D)
+        Wv = weight.view(H, C, D)
+        gW = (att_src.reshape(H, C, 1) * gVs + att_dst.reshape(H, C, 1) * gVd).reshape(HC, D)
+        gas = (Wv * gVs).sum(2).reshape(att_src.shape)
+        gad = (Wv * gVd).sum(2).reshape(att_dst.shape)
+        return gx, gW, gas, gad, None
+
+
+def attention_logits_through_weight(x: torch.Tensor, weight: torch.Tensor, att_src: torch.Tensor,
+                                    att_dst: torch.Tensor, heads: int) -> torch.Tensor:
+    """[alpha_src | alpha_dst] [N, 2H] of lin(x).view(N, H, C) with
+    lin.weight = weight [H*C, D] and att_* [1, H, C], in full fp32."""
+    return _LogitsThroughWeightFn.apply(x.contiguous(), weight, att_src, att_dst, int(heads))
 
 
 def collapsed_gat_aggregate_first(x: torch.Tensor, attn_row: torch.Tensor, attn_col: torch.Tensor,

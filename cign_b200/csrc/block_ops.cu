@@ -45,8 +45,11 @@ __device__ __forceinline__ float gsum(float v, unsigned gmask) {
 
 // Rows per chunk of the parameter-gradient reductions: a multiple of 32
 // (so every group layout divides it) giving at most ~4 chunks per SM.
+// Row chunks of the parameter-gradient reduction: at most this many (four
+// per SM), each a multiple of 32 rows.
+constexpr int64_t kLnChunkTarget = 592;
 int64_t rows_per_chunk(int64_t n) {
-  const int64_t target = 592;
+  const int64_t target = kLnChunkTarget;
   int64_t r = (n + target - 1) / target;
   r = std::max<int64_t>(r, 32);
   return (r + 31) / 32 * 32;
@@ -564,9 +567,13 @@ int cign_block_dropout_mask(int64_t count, float p, uint64_t seed_value, const u
 // every partial it later reads, so nothing has to be cleared between calls.
 // Its device address is looked up (cudaGetSymbolAddress) on the first call
 // on each device, with that device current; make that first call before any
-// stream capture.
+// stream capture.  The dropout seed is a host value only (no device seed
+// slot, unlike cign_dropout_ln_bwd): a captured graph that replays this call
+// replays the same mask.
 constexpr int64_t kStaticLnChunks = 592;
 constexpr int64_t kStaticLnMaxD = 1024;
+static_assert(kStaticLnChunks == kLnChunkTarget,
+              "the static scratch must hold the largest chunk count rows_per_chunk() gives");
 static __device__ __align__(256) float g_static_ln_scratch[kStaticLnChunks * kStaticLnMaxD * 2];
 
 namespace {

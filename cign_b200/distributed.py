@@ -320,8 +320,18 @@ class PeerHaloExchange(HaloExchange):
         # used under graph capture)
         self.timer = None
 
-    def begin_step(self) -> None:
+    def begin_step(self, order_with_previous_step: bool = False) -> None:
+        """Start a step: the exchanges of this step reuse the previous step's
+        buffers, in the same order.  A peer's push of this step overwrites a
+        buffer this rank read in the previous step, so some collective must
+        separate the two steps on every rank.  A training step has one (the
+        gradient all-reduce at its end); a caller without one -- e.g. forward
+        passes only, for evaluation -- passes order_with_previous_step=True,
+        which adds a one-element all-reduce on the current stream here.  Every
+        rank must pass the same value."""
         self._call = 0
+        if order_with_previous_step:
+            dist.all_reduce(self._flag, group=self.group)
 
     def _alloc_shared(self, rows: int, F: int):
         """A [rows, F] fp32 buffer of this rank and the base pointers of every

@@ -36,7 +36,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import fused_clifford_cign_generic, fused_clifford_cign_pack, fused_clifford_pack
-from .collapsed_gat import collapsed_gat_aggregate_first, collapsed_gat_mean_bias_silu
+from .collapsed_gat import (attention_logits_through_weight, collapsed_gat_aggregate_first,
+                            collapsed_gat_mean_bias_silu)
 from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, fused_dropout_layernorm
 from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
@@ -104,10 +105,8 @@ class GATContext(nn.Module):
         if self.aggregate_first and x.size(1) % 4 == 0 and C % 4 == 0:
             # lin is linear: aggregate x per head, apply lin.weight afterwards.
             # alpha_src[n,h] = <W_h x_n, att_src[h]> = <x_n, W_h^T att_src[h]>.
-            Wv = self.lin.weight.view(H, C, -1)
-            V = torch.cat([torch.einsum("hcd,hc->hd", Wv, self.att_src[0]),
-                           torch.einsum("hcd,hc->hd", Wv, self.att_dst[0])], 0)
-            alpha = x_src.matmul(V.t())
+            alpha = attention_logits_through_weight(x_src, self.lin.weight, self.att_src,
+                                                    self.att_dst, H)
             a_src = alpha[:, :H].contiguous()
             a_dst = alpha[:x.size(0), H:].contiguous()
             return collapsed_gat_aggregate_first(

@@ -166,8 +166,8 @@ class WorkloadConfig:
     avg_degree: float = 8.0
 
 
-# The BASELINE.json configurations that a single GPU runs (cfg2 is the
-# headline bench; cfg1 is the CPU-runnable case; cfg4 the large graph).
+# The benchmark configurations that a single GPU runs (cfg2 is the headline
+# training step; cfg1 the CPU-runnable case; cfg4 the large RMAT graph).
 CONFIGS = {
     "cfg1": WorkloadConfig("cfg1_er2000", 2000, 8000, "er", 64, 5, 64, (1, 2), 4, 2, 0.5, 0.5,
                            seed=0, avg_degree=8.0),

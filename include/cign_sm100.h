@@ -471,7 +471,9 @@ CIGN_API int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y,
  * overlap on the GPU (other streams or threads) race; order them on one
  * stream.  The first call on each device looks up the array's device
  * address with that device current; make that first call before any stream
- * capture. */
+ * capture.  The dropout seed is a host value only (there is no device seed
+ * slot): a captured graph replaying this call applies the same mask on every
+ * replay. */
 CIGN_API int cign_dropout_ln_bwd_static(int64_t n, int64_t d, const float* grad_y,
                                const float* x, const float* w,
                                const float* mean, const float* rstd, float p,

@@ -99,16 +99,18 @@ class OracleCIGN(nn.Module):
         self.classifier = nn.Linear(final_dim, out_dim, bias=True)
         self.calls = 0
 
-    def forward(self, x, P, PT, gat_graph, initial_seed: int = 0):
+    def forward(self, x, P, PT, gat_graph, initial_seed: int = 0, gat_call0: int = 0,
+                block_call0: int = 0):
         """Seeds follow the reference's per-call counters: one GAT counter and
         one shared block-op counter (tags 1 and 2), advanced only when the
-        corresponding dropout is active."""
+        corresponding dropout is active.  gat_call0 / block_call0 are the
+        counters' values before this forward (0 for a fresh process)."""
         x = x.float()
         H_in = F.dropout(x, p=self.dropout, training=self.training)
         H = F.silu(self.input_proj_0(H_in)) + self.input_eta * F.silu(self.input_proj_1(H_in))
         states = [H]
-        gat_call = 0
-        block_call = 0
+        gat_call = int(gat_call0)
+        block_call = int(block_call0)
         for blk in self.blocks:
             p = blk.dropout if self.training else 0.0
             gp = blk.context_gat.dropout if self.training else 0.0

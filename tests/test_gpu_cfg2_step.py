@@ -1,0 +1,189 @@
+"""The benchmarked configuration end to end: one cfg2 training step exactly as
+bench.py runs it (N=24,492 power-law graph, D=512, K=3, H=4, L=2, dropout
+0.5 everywhere including attention dropout, graph-captured step with fused
+Adam) against the CPU oracle on the same seeds, and the on-device graph
+preparation against the oracle's index arrays.
+
+Dropout masks: the native ops draw their masks from the reference's
+splitmix64 streams, which the oracle restates bit for bit, so the seeds of
+the replayed step (the host call counters after the warm-up steps) are
+handed to the oracle.  The two net-level dropouts (input and JK output,
+torch's F.dropout in both the reference and this model) are replaced in both
+models by one fixed, seeded mask per tensor shape, so the CPU and the GPU
+apply the same masks.
+
+Tolerances: with TF32 off, the reference's own model thresholds
+(validate_cign_acceleration.py:53-57: outputs rtol 2e-4 / atol 2e-5,
+gradients rtol 5e-4 / atol 5e-5) elementwise.  With TF32 on (the bench's
+setting, and the reference's default, train_cign.py:755-768): logits and
+loss within 2e-3 relative (rel-L2).  Parameter gradients within 2e-3, or,
+where TF32 itself moves a gradient further than that, no further from the
+fp32 oracle than the reference's own order of computation under TF32 moves
+it (x 1.5): lin(x) as a TF32 GEMM, the attention logits and the collapsed
+GAT in fp32 (CompatibleCollapsedFusedGATConv.forward, model_cign.py:524-570),
+i.e. this model with GATContext.aggregate_first off, same parameters and
+seeds.  The GAT parameters' gradients are sums over all nodes of nearly
+cancelling terms (the softmax backward), so TF32-rounded operands anywhere
+upstream move them by about 1e-2 in either order.
+"""
+import copy
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import bench
+from cign_b200 import seeds, synth
+from cign_b200.graph_operator import (build_sparse_normalized_adjacency,
+                                      prepare_fixed_csr_operator, prepare_gat_edge_index,
+                                      to_graph_format)
+from cign_b200.graph_step import GraphedStep
+from oracle import graph as og
+from oracle import ops
+from oracle.model import OracleCIGN
+from tests.helpers import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+CFG = synth.CONFIGS["cfg2"]
+
+
+class _FixedDropout:
+    """F.dropout stand-in: one fixed keep-mask per tensor shape, on either device."""
+
+    def __init__(self, shapes, device, p):
+        g = torch.Generator().manual_seed(1234)
+        self.cpu = {s: torch.rand(s, generator=g) >= p for s in shapes}
+        self.dev = {s: m.to(device) for s, m in self.cpu.items()}
+
+    def __call__(self, x, p=0.5, training=True, inplace=False):
+        if not training or p == 0.0:
+            return x
+        masks = self.dev if x.is_cuda else self.cpu
+        return x * masks[tuple(x.shape)].to(x.dtype) * (1.0 / (1.0 - p))
+
+
+def _oracle_graph(edge_cpu, n):
+    r, c, v = og.normalized_adjacency(edge_cpu.numpy(), n)
+    P = ops.csr_tensor(*og.csr_of(r, c, v, n), n, n)
+    PT = ops.csr_tensor(*og.csr_transpose(r, c, v, n), n, n)
+    ei = og.to_undirected(edge_cpu.numpy(), n)
+    loops = np.arange(n)
+    ei = np.concatenate([ei, np.stack([loops, loops])], axis=1)
+    gat = og.gat_graph(og.prepare_gat_edge_index(ei, n), n)
+    return P, PT, gat
+
+
+@pytest.mark.parametrize("tf32", [False, True], ids=["tf32_off", "tf32_on"])
+def test_cfg2_graphed_training_step_vs_oracle(cuda, monkeypatch, tf32):
+    n = CFG.num_nodes
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = tf32
+    fixed = _FixedDropout([(n, CFG.in_dim), (n, CFG.hidden_dim * (CFG.layers + 1))], cuda,
+                          CFG.dropout)
+    monkeypatch.setattr(torch.nn.functional, "dropout", fixed)
+    try:
+        op, gat_graph, nnz, nnz_g = bench.build_graph(CFG, cuda)
+        model, opt, x_cpu, y_cpu, train_cpu = bench.build_model_and_data(CFG, cuda, seed=0,
+                                                                         capturable=True)
+        assert model.blocks[0].dropout == 0.5 and model.blocks[0].context_gat.dropout == 0.5
+        x, y = x_cpu.to(cuda), y_cpu.to(cuda)
+        idx = train_cpu.to(cuda).nonzero().squeeze(1)
+        model.prepare_fused_gat_graph(gat_graph)
+        held = {}
+
+        def step():
+            opt.zero_grad(set_to_none=True)
+            logits = model(x, op)
+            held["logits"] = logits
+            loss = F.cross_entropy(logits.index_select(0, idx), y.index_select(0, idx))
+            loss.backward()
+            opt.step()
+            return loss
+
+        seeds.set_host_counters(0, 0)
+        graphed = GraphedStep(step, cuda, warmup=3)
+        gat_call0, block_call0 = seeds.host_counters()  # the first replay's dropout calls
+        assert (gat_call0, block_call0) == (3 * CFG.layers, 3 * 2 * CFG.layers)
+        state = {k: v.detach().cpu().clone() for k, v in model.state_dict().items()}
+        twin = copy.deepcopy(model) if tf32 else None
+        loss = float(graphed().detach())
+        torch.cuda.synchronize()
+        graphed.finish()
+        logits = held["logits"].detach().cpu()
+        grads = {k: p.grad.detach().cpu().clone() for k, p in model.named_parameters()}
+        if tf32:  # the reference's order of computation, same parameters and seeds
+            for blk in twin.blocks:
+                blk.context_gat.aggregate_first = False
+            twin.zero_grad(set_to_none=True)
+            seeds.set_host_counters(gat_call0, block_call0)
+            out = twin(x, op)
+            F.cross_entropy(out.index_select(0, idx), y.index_select(0, idx)).backward()
+            ref_order = {k: p.grad.detach().cpu().clone() for k, p in twin.named_parameters()}
+            del twin, out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+    oracle = OracleCIGN(CFG.in_dim, CFG.hidden_dim, CFG.num_classes, CFG.layers, CFG.hops,
+                        CFG.dropout, CFG.heads, CFG.gat_dropout)
+    oracle.load_state_dict(state)
+    oracle.train()
+    P, PT, gat = _oracle_graph(synth.make_edges(CFG), n)
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    ref_logits = oracle(x_cpu, P, PT, gat, initial_seed=0, gat_call0=gat_call0,
+                        block_call0=block_call0)
+    train = train_cpu.nonzero().squeeze(1)
+    ref_loss = F.cross_entropy(ref_logits[train], y_cpu[train])
+    ref_loss.backward()
+
+    if tf32:
+        errs = {name: (rel_l2(grads[name], q.grad), rel_l2(ref_order[name], q.grad))
+                for name, q in oracle.named_parameters()}
+        report = "; ".join(f"{k} {a:.2e} (reference order {b:.2e})"
+                           for k, (a, b) in sorted(errs.items(), key=lambda kv: -kv[1][0]))
+        assert rel_l2(logits, ref_logits) <= 2e-3, (rel_l2(logits, ref_logits), report)
+        assert abs(loss - float(ref_loss)) <= 2e-3 * abs(float(ref_loss)), report
+        bad = {k: a for k, (a, b) in errs.items() if a > max(2e-3, 1.5 * b)}
+        assert not bad, report
+    else:
+        torch.testing.assert_close(logits, ref_logits.detach(), rtol=2e-4, atol=2e-5)
+        assert abs(loss - float(ref_loss)) <= 2e-4 * abs(float(ref_loss))
+        for name, q in oracle.named_parameters():
+            torch.testing.assert_close(grads[name], q.grad, rtol=5e-4, atol=5e-5, msg=name)
+
+
+@pytest.mark.parametrize("workload", ["cfg2", "rmat"])
+def test_graph_preparation_on_device_vs_oracle(cuda, workload):
+    """build_sparse_normalized_adjacency, prepare_fixed_csr_operator,
+    prepare_gat_edge_index and to_graph_format run on the GPU (as bench.py
+    runs them): CSR(P), CSR(Pᵀ), the GAT CSR/CSC/perm equal the oracle's
+    index arrays bit for bit.  The fp32 operator values agree within 5 ulp
+    (relative 6e-7): the device evaluates deg^-1/2 with CUDA's single-precision
+    power / reciprocal square root (up to 2 ulp each), the CPU (and the
+    oracle) as a correctly rounded 1/sqrt."""
+    if workload == "cfg2":
+        n, edge = CFG.num_nodes, synth.make_edges(CFG)
+    else:
+        n = 200_000
+        edge = synth.rmat_graph(n, 2_000_000, seed=3)
+    ei, adj = build_sparse_normalized_adjacency(edge.to(cuda), n)
+    base = prepare_fixed_csr_operator(adj)
+    (rp, c), (r, cp), perm = to_graph_format(prepare_gat_edge_index(ei, n).flip(0), n)
+    ro, co, vo = og.normalized_adjacency(edge.numpy(), n)
+    crow, col, val = og.csr_of(ro, co, vo, n)
+    np.testing.assert_array_equal(base.csr.crow_indices().cpu().numpy(), crow)
+    np.testing.assert_array_equal(base.csr.col_indices().cpu().numpy(), col)
+    np.testing.assert_allclose(base.csr.values().cpu().numpy(), val, rtol=6e-7, atol=0)
+    crow_t, col_t, val_t = og.csr_transpose(ro, co, vo, n)
+    np.testing.assert_array_equal(base.csr_t.crow_indices().cpu().numpy(), crow_t)
+    np.testing.assert_array_equal(base.csr_t.col_indices().cpu().numpy(), col_t)
+    np.testing.assert_allclose(base.csr_t.values().cpu().numpy(), val_t, rtol=6e-7, atol=0)
+    (rp_o, c_o), (r_o, cp_o), perm_o = og.gat_graph(
+        og.prepare_gat_edge_index(ei.cpu().numpy(), n), n)
+    for name, a, b in (("rowptr", rp, rp_o), ("col", c, c_o), ("row", r, r_o),
+                       ("colptr", cp, cp_o), ("perm", perm, perm_o)):
+        np.testing.assert_array_equal(a.cpu().numpy(), b, err_msg=name)
+    # the edge list the device used is the oracle's undirected list plus self loops
+    ei_o = og.to_undirected(edge.numpy(), n)
+    np.testing.assert_array_equal(ei.cpu().numpy()[:, :ei_o.shape[1]], ei_o)

@@ -72,7 +72,7 @@ def test_graph_capture_policy():
 def test_algorithmic_bytes_at_cfg2_shapes():
     """Roofline numerators (compulsory HBM bytes per launch: every tensor read
     or written once) at cfg2's shapes, N=24,492, nnz=390,042, D=512, F=2D,
-    H=4, K=3; the figures of the per-kernel bandwidth table in profiles/."""
+    H=4, K=3."""
     import bench
     N, nnz, D, H, K = 24492, 390042, 512, 4, 3
     F = 2 * D

@@ -68,6 +68,45 @@ def test_static_scratch_matches_workspace_version(cuda, n, d, p):
             assert_parity(a, e, what=f"{name} n={n} d={d} call={call}")
 
 
+def test_static_scratch_allocates_nothing(cuda):
+    """Around a call of the static entry point neither torch's allocator nor
+    the device's free memory changes (inputs and outputs exist beforehand;
+    the device address of the scratch is looked up before the measurement)."""
+    lib = _lib.load_library()
+    stream = _lib.stream_on(cuda)
+    n, d, p, seed = 24492, 512, 0.5, 99
+    x, w, gy, mean, rstd = _inputs(n, d, cuda, seed=5)
+    gx, gw, gb = torch.empty_like(x), torch.empty(d, device=cuda), torch.empty(d, device=cuda)
+
+    def call():
+        rc = lib.cign_dropout_ln_bwd_static(n, d, _lib.ptr(gy), _lib.ptr(x), _lib.ptr(w),
+                                            _lib.ptr(mean), _lib.ptr(rstd), p, seed,
+                                            _lib.ptr(gx), _lib.ptr(gw), _lib.ptr(gb), stream)
+        _lib.check(rc, "cign_dropout_ln_bwd_static")
+
+    call()  # first call on this device: symbol lookup
+    torch.cuda.synchronize()
+    stats0 = torch.cuda.memory_stats(cuda)["allocation.all.current"]
+    free0, _ = torch.cuda.mem_get_info(cuda)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_stats(cuda)["allocation.all.current"] == stats0
+    assert torch.cuda.mem_get_info(cuda)[0] == free0
+
+
+def test_static_scratch_zero_rows(cuda):
+    """n = 0: the parameter gradients are zeros (no rows contribute)."""
+    lib = _lib.load_library()
+    gw = torch.full((64,), 7.0, device=cuda)
+    gb = torch.full((64,), 7.0, device=cuda)
+    rc = lib.cign_dropout_ln_bwd_static(0, 64, None, None, None, None, None, 0.0, 0, None,
+                                        _lib.ptr(gw), _lib.ptr(gb), _lib.stream_on(cuda))
+    _lib.check(rc, "cign_dropout_ln_bwd_static")
+    torch.cuda.synchronize()
+    assert bool((gw == 0).all()) and bool((gb == 0).all())
+
+
 def test_static_scratch_rejects_oversize(cuda):
     lib = _lib.load_library()
     rc = lib.cign_dropout_ln_bwd_static(8, 2048, None, None, None, None, None, 0.0, 0, None, None,
