@@ -17,8 +17,13 @@ is the same step through the public API with the features copied from
 pinned host memory and the loss read back every step.
 
 --impl reference times the reference's own CPU path (its torch ops restated
-in oracle/, run on all host cores) on a bounded sample of the workload (the
-same graph family at a smaller N); there is no GPU in that arm.
+in oracle/, run on all host cores) on the same workload graph, whole, for up
+to --steps steps within --cpu-budget-s seconds; there is no GPU in that arm.
+The cpu_baseline object of the GPU arm is the same runner for 3 steps.
+
+roofline.epoch_frac = T_roof / ms_per_step, T_roof = sum over every kernel of
+the step (step_roofline_items) of max(compulsory bytes / HBM peak, FLOPs /
+TF32 peak).
 
 With --gpus N > 1 (torchrun, NCCL) the graph is row-partitioned over the
 ranks with a halo exchange per hop and per GAT layer and one gradient
@@ -64,6 +69,120 @@ def load_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+FALLBACK_BF16_SUSTAINED_TFLOPS = 1400.0
+
+
+def load_tf32_peak():
+    """Dense TF32 tensor-core peak (TFLOP/s) for kernels inside a long step:
+    the measured sustained cuBLAS bf16 rate halved (TF32 issues at half the
+    bf16 rate on sm_100), else the fallback figure halved."""
+    if PEAKS_PATH.exists():
+        try:
+            d = json.loads(PEAKS_PATH.read_text())
+            return float(d["bf16_tflops_sustained"]) / 2.0, "measured bf16 sustained / 2"
+        except Exception:
+            pass
+    return FALLBACK_BF16_SUSTAINED_TFLOPS / 2.0, "fallback bf16 sustained / 2"
+
+
+def step_roofline_items(cfg, nnz, nnz_g):
+    """Every kernel of one training step of the model as this repository runs
+    it (forward, CE loss, backward, fused Adam), with its compulsory HBM bytes
+    (each tensor it touches read or written once) and its FLOPs (GEMMs only;
+    the other kernels have arithmetic intensity < 1 flop/byte).  Returns a
+    list of (name, launches per step, bytes per launch, flops per launch)."""
+    N, D, H, K, L = cfg.num_nodes, cfg.hidden_dim, cfg.heads, len(cfg.hops), cfg.layers
+    I, Cls, F2 = cfg.in_dim, cfg.num_classes, 2 * cfg.hidden_dim
+    S = L + 1                                         # JK states
+    HD = H * D
+    gemm = lambda m, n, k: (4 * (m * k + k * n + m * n), 2 * m * n * k)  # noqa: E731
+    it = []
+
+    def add(name, count, nbytes, flops=0):
+        it.append((name, count, int(nbytes), int(flops)))
+
+    # forward, net input
+    add("input dropout", 1, 9 * N * I)
+    add("input projections (GEMM)", 2, *gemm(N, D, I))
+    add("input SiLU mix", 1, 12 * N * D)
+    # forward, per block
+    add("dropout-LN fwd", L, 8 * N * D + 8 * N)
+    add("GAT logits (fp32 GEMM)", L, *gemm(N, 2 * H, D))
+    add("GAT aggregate fwd", L, algorithmic_bytes("gat_agg_fwd", N, nnz, H=H, D=D, nnz_g=nnz_g))
+    add("GAT z.M (GEMM)", L, *gemm(N, D, HD))
+    add("GAT bias+SiLU fwd", L, 12 * N * D)
+    add("add-LN fwd", L, 12 * N * D + 8 * N)
+    add("[H|C] concat", L, 16 * N * D)
+    add("k-hop SpMM fwd hop", L * K, algorithmic_bytes("spmm", N, nnz, F=F2))
+    add("hop gate fwd", L, 8 * N * D + 4 * N * K)
+    add("pack fwd", L, algorithmic_bytes("pack_fwd", N, nnz, K=K, D=D))
+    add("proj (GEMM)", L, *gemm(N, D, 2 * K * D))
+    add("dropout-gamma-residual fwd", L, 12 * N * D)
+    # forward, net output and loss
+    add("JK LayerNorm fwd", 1, 8 * N * S * D + 8 * N)
+    add("output dropout", 1, 9 * N * S * D)
+    add("classifier (GEMM)", 1, *gemm(N, Cls, S * D))
+    add("cross-entropy fwd+bwd", 1, 12 * N * Cls)
+    # backward, net output
+    add("classifier dgrad (GEMM)", 1, *gemm(N, S * D, Cls))
+    add("classifier wgrad (GEMM)", 1, *gemm(Cls, S * D, N))
+    add("output dropout bwd", 1, 9 * N * S * D)
+    add("JK LayerNorm bwd (+ parameter pass)", 1, 20 * N * S * D + 8 * N)
+    # backward, per block
+    add("block-state gradient sums", 2 * L, 12 * N * D)
+    add("dropout-gamma-residual bwd", L, 12 * N * D)
+    add("proj dgrad (GEMM)", L, *gemm(N, 2 * K * D, D))
+    add("proj wgrad (GEMM)", L, *gemm(D, 2 * K * D, N))
+    add("proj bias colsum", L, 4 * N * D)
+    add("pack bwd", L, algorithmic_bytes("pack_bwd", N, nnz, K=K, D=D))
+    add("k-hop SpMM bwd hop (+g fused)", L * (K - 1), algorithmic_bytes("spmm_add", N, nnz, F=F2))
+    add("k-hop SpMM bwd hop", L, algorithmic_bytes("spmm", N, nnz, F=F2))
+    add("hop gate bwd (+ gradient adds)", L, 24 * N * D + 8 * N * K)
+    add("add-LN bwd", L, 16 * N * D + 8 * N)
+    add("GAT bias+SiLU bwd", L, 12 * N * D)
+    add("GAT grad z (GEMM)", L, *gemm(N, HD, D))
+    add("GAT aggregate bwd", L, algorithmic_bytes("gat_agg_bwd", N, nnz, H=H, C=D, D=D,
+                                                   nnz_g=nnz_g))
+    add("GAT lin wgrad (GEMM)", L, *gemm(HD, D, N))
+    add("GAT input dgrad (GEMM)", L, *gemm(N, D, HD))
+    add("GAT logits bwd (fp32 GEMMs)", L, 2 * gemm(N, D, 2 * H)[0], 2 * gemm(N, D, 2 * H)[1])
+    add("H_norm gradient sums", 3 * L, 12 * N * D)
+    add("dropout-LN bwd", L, 12 * N * D + 8 * N)
+    # backward, net input
+    add("input SiLU mix bwd", 1, 20 * N * D)
+    add("input projections wgrad (GEMM)", 2, *gemm(D, I, N))
+    add("input projections bias colsum", 2, 4 * N * D)
+    # optimizer: fused Adam reads param, grad, exp_avg, exp_avg_sq, writes three
+    params = (2 * (I * D + D) + 1 + L * (4 * D + HD * D + 2 * H * D + D + 2 * K * D * D + D
+                                     + 2 * D * K + K + D) + 2 * S * D + S * D * Cls + Cls)
+    add("Adam (fused)", 1, 28 * params)
+    return it
+
+
+def step_roofline(cfg, nnz, nnz_g, ms_per_step, hbm_gbs, tf32_tflops):
+    """T_roof = sum over the step's kernels of max(bytes / HBM peak, flops /
+    TF32 peak); frac = T_roof / measured step time."""
+    items = step_roofline_items(cfg, nnz, nnz_g)
+    t_roof = 0.0
+    t_hbm = 0.0
+    t_tc = 0.0
+    tot_b = tot_f = 0
+    for _, count, nbytes, flops in items:
+        tb = nbytes / (hbm_gbs * 1e9)
+        tf = flops / (tf32_tflops * 1e12)
+        t_roof += count * max(tb, tf)
+        t_hbm += count * tb
+        t_tc += count * tf
+        tot_b += count * nbytes
+        tot_f += count * flops
+    return {"t_roof_ms": round(t_roof * 1e3, 4), "epoch_frac": round(t_roof * 1e3 / ms_per_step, 4),
+            "step_bytes": int(tot_b), "step_tf32_flops": int(tot_f),
+            "hbm_bound_ms": round(t_hbm * 1e3, 4), "tensor_bound_ms": round(t_tc * 1e3, 4),
+            "kernels_modelled": len(items),
+            "launches_modelled": int(sum(c for _, c, _, _ in items)),
+            "peaks": {"hbm_gbs": hbm_gbs, "tf32_tflops": round(tf32_tflops, 1)}}
+
+
 def load_traffic():
     if TRAFFIC_PATH.exists():
         try:
@@ -78,28 +197,50 @@ class ClockSampler:
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,"
+             "timestamp")
+    INTERVAL_MS = 20
 
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
         self.path = None
+        self.windows = []
 
     def start(self):
+        """Start sampling and wait (up to 5 s) until the first sample is written,
+        so that the timed region that follows is covered."""
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                 "--format=csv,noheader,nounits", "-lms", str(self.INTERVAL_MS), "-f", self.path],
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 5.0:
+            try:
+                if Path(self.path).stat().st_size > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.01)
+
+    def begin(self):
+        """Host time at the start of a timed region (pair with end())."""
+        self.windows.append([time.time(), None])
+
+    def end(self):
+        if self.windows:
+            self.windows[-1][1] = time.time()
 
     def stop(self):
         if self.proc is None:
             return None
-        time.sleep(0.25)
+        time.sleep(2.0 * self.INTERVAL_MS / 1e3)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -112,7 +253,27 @@ class ClockSampler:
                 os.unlink(self.path)
             except OSError:
                 pass
-        return self.summarize(lines)
+        return self.summarize(self.in_windows(lines, self.windows))
+
+    @staticmethod
+    def in_windows(lines, windows):
+        """The samples whose timestamp (last column, local time) falls inside one
+        of the [begin, end] host-time windows; all samples when none carries a
+        readable timestamp or no window was marked."""
+        import datetime
+        if not windows:
+            return lines
+        kept, stamped = [], 0
+        for line in lines:
+            parts = [p.strip() for p in line.split(",")]
+            try:
+                ts = datetime.datetime.strptime(parts[-1], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except (ValueError, IndexError):
+                continue
+            stamped += 1
+            if any(b <= ts <= (e if e is not None else ts) for b, e in windows):
+                kept.append(line)
+        return kept if stamped else lines
 
     @staticmethod
     def summarize(lines):
@@ -219,9 +380,10 @@ def time_launches(fn, reps, stream):
     return start.elapsed_time(end) / reps * 1e-3  # seconds per call
 
 
-def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device):
+def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device, pack_proj_in_step=False):
     """Per-op device time (CUDA events on the launching stream) of the native
-    kernels on the workload's own shapes, with launches per training step."""
+    kernels on the workload's own shapes, with launches per training step
+    (0 for a kernel timed here that the step does not launch)."""
     from cign_b200 import _pack, collapsed_gat
     from cign_b200.plans import gat_plan_for
     N, D, H, K, L = cfg.num_nodes, cfg.hidden_dim, cfg.heads, len(cfg.hops), cfg.layers
@@ -269,7 +431,8 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device):
                                                         nnz_g=nnz_g)),
         "gat_agg_bwd": (t_gat_bwd, L, algorithmic_bytes("gat_agg_bwd", N, nnz, H=H, C=D, D=D,
                                                         nnz_g=nnz_g)),
-        "pack_proj_tcgen05_fwd": (t_pp, L, algorithmic_bytes("pack_proj", N, nnz, K=K, D=D, C=D)),
+        "pack_proj_tcgen05_fwd": (t_pp, L if pack_proj_in_step else 0,
+                                  algorithmic_bytes("pack_proj", N, nnz, K=K, D=D, C=D)),
         "pack_fwd": (t_pack_f, L, algorithmic_bytes("pack_fwd", N, nnz, K=K, D=D)),
         "pack_bwd": (t_pack_b, L, algorithmic_bytes("pack_bwd", N, nnz, K=K, D=D)),
     }
@@ -279,6 +442,9 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device):
                      "ms_per_step": round(t * per_step * 1e3, 4),
                      "algorithmic_bytes": int(nbytes),
                      "achieved_gbs": round(nbytes / t / 1e9, 1)}
+    if not pack_proj_in_step:
+        out["pack_proj_tcgen05_fwd"]["note"] = ("not launched by this step: with G_raw kept for "
+                                                "the backward the pack kernel + cuBLAS run instead")
     return out
 
 
@@ -416,12 +582,14 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
         if hasattr(exch, "timer"):
             exch.timer = push_timer  # events around every halo push + its barrier
     sampler.start()
+    sampler.begin()
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
         run_step(x)
         ends[i].record(stream)
     torch.cuda.synchronize()
+    sampler.end()
     SpmmPlan.hop_timer = None
     if hasattr(exch, "timer"):
         exch.timer = None
@@ -672,7 +840,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-nodes", type=int, default=6000)
+    ap.add_argument("--cpu-sample-nodes", type=int, default=0,
+                    help="nodes of the CPU arms' graph (0: the whole workload graph)")
+    ap.add_argument("--cpu-budget-s", type=float, default=240.0,
+                    help="the reference arm stops timing after this many seconds")
     ap.add_argument("--sweep", action="store_true",
                     help="configs[2] isolated kernel sweep (one JSON line per case) instead of "
                          "the training-step benchmark")
@@ -713,22 +884,24 @@ def main():
         # CPU reference arm: rank 0 only; other ranks exit without work.
         if rank != 0:
             return 0
-        sample = cpu_sample_config(cfg, args.cpu_sample_nodes)
-        steps = max(1, min(args.steps, 5))
-        gteps, t, done, nnz = run_cpu_oracle(sample, steps, 1, budget_s=150.0)
+        sample = cpu_sample_config(cfg, args.cpu_sample_nodes or cfg.num_nodes)
+        gteps, t, done, nnz = run_cpu_oracle(sample, max(1, args.steps), 1,
+                                             budget_s=args.cpu_budget_s)
         cores = os.cpu_count() or 1
         line = {
             "impl": "reference", "metric": metric, "value": round(gteps, 6), "unit": "GTEPS",
             "n_gpus": args.gpus, "steps": done, "warmup": 1, "ms_per_step": round(t * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": sample.name, "nodes": sample.num_nodes, "nnz": nnz,
+            "config": {"workload": sample.name, "nodes": sample.num_nodes, "nnz_P": nnz,
                        "hidden": cfg.hidden_dim, "hops": list(cfg.hops), "heads": cfg.heads,
-                       "layers": cfg.layers, "note": "reference torch path on CPU (oracle/ restatement)"},
+                       "layers": cfg.layers, "dropout": cfg.dropout,
+                       "note": "the reference's torch training step on the host CPU "
+                               "(oracle/ restatement, all host threads)"},
             "cpu_baseline": {"value": round(gteps, 6), "unit": "GTEPS", "cores": cores,
                              "kind": "port",
-                             "sample": f"one full train step on the {sample.name} graph "
-                                       f"(N={sample.num_nodes}, same family/degree/widths)"},
+                             "sample": f"{done} full training step(s) (median) on the whole "
+                                       f"{sample.name} graph (N={sample.num_nodes}, nnz={nnz})"},
             "e2e": {"value": round(gteps, 6), "unit": "GTEPS", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }
@@ -767,6 +940,9 @@ def main():
     train_idx = train_cpu.to(device).nonzero().squeeze(1)
     model.prepare_fused_gat_graph(gat_graph)
     edge_passes = 2 * cfg.layers * len(cfg.hops) * nnz
+    # GAT edge passes: per layer one forward pass and three backward passes
+    # (edge logits, softmax backward, transposed aggregation) over nnz_g x H
+    gat_edge_passes = cfg.layers * nnz_g * cfg.heads * 4
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
 
     from cign_b200.plans import HopTimer, SpmmPlan
@@ -799,14 +975,15 @@ def main():
     if not use_graph:
         SpmmPlan.hop_timer = hop_timer  # CUDA events around every k-hop call, same stream
     sampler.start()
+    sampler.begin()
     for i in range(args.steps):
         flush.zero_()  # L2 flush between timed steps (outside the per-step events)
         starts[i].record(stream)
         run_step()
         ends[i].record(stream)
     torch.cuda.synchronize()
+    sampler.end()
     SpmmPlan.hop_timer = None
-    clocks = sampler.stop()
     # kernels launched per step: counted by the library while the graph was
     # captured (one step), or over the timed eager steps
     timed_launches = (graphed.native_launches * args.steps if use_graph
@@ -847,6 +1024,7 @@ def main():
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
+    sampler.begin()
     e_start.record(stream)
     copy_stream.wait_event(e_start)
     stage(0)
@@ -861,6 +1039,8 @@ def main():
         loss_pin[i:i + 1].copy_(loss.detach().reshape(1), non_blocking=True)  # D2H of the result
     e_end.record(stream)
     torch.cuda.synchronize()
+    sampler.end()
+    clocks = sampler.stop()  # samples inside the two timed regions
     loss_host = float(loss_pin[-1])
     e2e_s = e_start.elapsed_time(e_end) * 1e-3
     if dist is not None:
@@ -873,20 +1053,31 @@ def main():
     result = None
     if rank == 0:
         peak, peak_kind = load_peaks()
-        kernels = (kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device)
+        blk = model.blocks[0]
+        keep_g = not blk._recompute_pack(torch.empty(cfg.num_nodes, 0))
+        pp_in_step = ((not keep_g) if block_fused.USE_TCGEN05_PACK_PROJ is None
+                      else bool(block_fused.USE_TCGEN05_PACK_PROJ))
+        kernels = (kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device, pp_in_step)
                    if cfg.num_nodes <= GRAPH_CAPTURE_MAX_NODES else None)
         roofline = hop_roofline(hop_timer, cfg.num_nodes, nnz, peak, peak_kind)
+        tf32_peak, tf32_kind = load_tf32_peak()
+        step_roof = step_roofline(cfg, nnz, nnz_g, ms_per_step, peak, tf32_peak)
+        step_roof["peaks"]["kind"] = f"HBM {peak_kind}; TF32 {tf32_kind}"
+        if roofline is not None:
+            roofline["epoch_frac"] = step_roof["epoch_frac"]
+            roofline["epoch"] = step_roof
         if roofline is not None and use_graph:
             roofline["timing"] = ("CUDA events captured around every k-hop call inside the step "
                                   "graph, read after the last timed replay")
         cpu_baseline = None
         if world == 1 and not args.no_cpu_baseline:
-            sample = cpu_sample_config(cfg, args.cpu_sample_nodes)
+            sample = cpu_sample_config(cfg, args.cpu_sample_nodes or cfg.num_nodes)
             gteps_cpu, t_cpu, done, nnz_s = run_cpu_oracle(sample, 3, 1, budget_s=60.0)
             cpu_baseline = {"value": round(gteps_cpu, 6), "unit": "GTEPS",
                             "cores": os.cpu_count() or 1, "kind": "port",
-                            "sample": f"{done} full train step(s) of the oracle model on the "
-                                      f"{sample.name} graph (N={sample.num_nodes}, nnz={nnz_s})",
+                            "sample": f"{done} full training step(s) (median) of the oracle "
+                                      f"model on the whole {sample.name} graph "
+                                      f"(N={sample.num_nodes}, nnz={nnz_s})",
                             "s_per_step": round(t_cpu, 3)}
         result = {
             "metric": metric, "value": round(value, 4), "unit": "GTEPS", "n_gpus": world,
@@ -903,6 +1094,8 @@ def main():
                        "launch": "one CUDA graph per step" if use_graph else "eager",
                        "parallelism": f"replicas{world}" if world > 1 else "single"},
             "epoch_ms": round(ms_per_step, 4),
+            "gat_gteps": round(gat_edge_passes * world * args.steps / total_s / 1e9, 4),
+            "gat_edge_passes_per_step": int(gat_edge_passes * world),
             "ms_per_step_median": round(statistics.median(step_s) * 1e3, 4),
             "e2e": {"value": round(e2e_value, 4), "unit": "GTEPS",
                     "h2d_bytes_per_step": int(x.numel() * 4), "d2h_bytes_per_step": 4,

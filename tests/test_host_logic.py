@@ -108,6 +108,25 @@ def test_clock_summary_of_nvidia_smi_samples():
     assert bench.ClockSampler.summarize([]) is None
 
 
+def test_clock_samples_inside_timed_windows():
+    """Only samples stamped inside a marked [begin, end] window count; lines
+    without a timestamp keep the old behaviour (all samples)."""
+    import datetime
+
+    import bench
+
+    def stamp(t):
+        return datetime.datetime.fromtimestamp(t).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+    base = 1_800_000_000.0
+    lines = [f"0, {mhz}, 1965, 900.0, 0x0, Not Active, Not Active, Not Active, Not Active, "
+             f"{stamp(base + dt)}" for mhz, dt in ((345, 0.0), (1965, 1.0), (1950, 1.1), (345, 3.0))]
+    kept = bench.ClockSampler.in_windows(lines, [[base + 0.5, base + 1.5]])
+    assert bench.ClockSampler.summarize(kept) == {"sm_mhz": 1957.5, "sm_max_mhz": 1965.0,
+                                                  "reasons": [], "samples": 2}
+    unstamped = [ln.rsplit(",", 1)[0] for ln in lines]
+    assert bench.ClockSampler.in_windows(unstamped, [[base, base + 1]]) == unstamped
+
+
 def test_hop_roofline_from_recorded_events():
     """The bench's `roofline` object from k-hop timer records (fake CUDA
     events): algorithmic bytes per launch over the measured time per launch."""
@@ -147,3 +166,25 @@ def test_cpu_sample_is_never_larger_than_the_workload():
     assert s.num_edges == round(cfg2.num_edges * 6000 / cfg2.num_nodes)
     assert (s.hidden_dim, s.hops, s.heads, s.layers) == (cfg2.hidden_dim, cfg2.hops, cfg2.heads,
                                                          cfg2.layers)
+
+
+def test_step_roofline_model_at_cfg2():
+    """The whole-step roofline: every modelled kernel counted once per launch,
+    T_roof = sum of max(bytes / HBM, flops / TF32) and frac = T_roof / step."""
+    import bench
+    from cign_b200 import synth
+    cfg = synth.CONFIGS["cfg2"]
+    items = bench.step_roofline_items(cfg, 390042, 390042)
+    names = [n for n, _, _, _ in items]
+    assert len(names) == len(set(names))
+    counts = dict((n, c) for n, c, _, _ in items)
+    assert counts["k-hop SpMM fwd hop"] == 6
+    assert counts["k-hop SpMM bwd hop (+g fused)"] + counts["k-hop SpMM bwd hop"] == 6
+    flops = dict((n, f) for n, _, _, f in items)
+    N, D, K = 24492, 512, 3
+    assert flops["proj (GEMM)"] == 2 * N * D * 2 * K * D
+    r = bench.step_roofline(cfg, 390042, 390042, 10.0, 6452.5, 700.0)
+    manual = sum(c * max(b / 6452.5e9, f / 700e12) for _, c, b, f in items) * 1e3
+    assert abs(r["t_roof_ms"] - round(manual, 4)) < 1e-3
+    assert abs(r["epoch_frac"] - round(manual / 10.0, 4)) < 1e-4
+    assert r["hbm_bound_ms"] <= r["t_roof_ms"] <= r["hbm_bound_ms"] + r["tensor_bound_ms"]
