@@ -10,7 +10,7 @@
 //     to four edges at a time for memory-level parallelism.  Rows wider than
 //     one tile are split over the grid's second dimension (one feature tile
 //     per block row), so the register footprint per lane, and with it the
-//     number of resident warps, stays that of a 256/512-float row.
+//     number of resident warps, stays that of a 256-float row.
 //     Measured on the cfg2 power-law graph this beat shared-memory staging
 //     (cp.async rings, and TMA bulk copies per neighbour row, whose per-copy
 //     cost put a ~95 us floor under every width) at every F.
@@ -125,22 +125,21 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
       LPR == 32 ? kFullMask
                 : (((1u << LPR) - 1u) << ((threadIdx.x & 31) / LPR * LPR));
 
+  // one feature tile per block row of the grid (gridDim.y * kTile >= F)
+  const int64_t f0 = static_cast<int64_t>(blockIdx.y) * Cfg::kTile;
+  V acc[VPL];
+#pragma unroll
+  for (int q = 0; q < VPL; ++q) vzero(acc[q]);
   if (static_cast<int>(blockIdx.x) < seg_blocks) {
     const int64_t sidx = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + group;
     if (sidx >= n_seg) return;
-    const int e0 = seg_begin[sidx], e1 = seg_end[sidx];
+    gather_edges<VEC, VPL, LPR>(col, val, seg_begin[sidx], seg_end[sidx], LPR, X, F, f0, lig,
+                                gmask, acc);
     float* pr = partial + sidx * F;
-    for (int64_t f0 = static_cast<int64_t>(blockIdx.y) * Cfg::kTile; f0 < F;
-         f0 += static_cast<int64_t>(gridDim.y) * Cfg::kTile) {
-      V acc[VPL];
 #pragma unroll
-      for (int q = 0; q < VPL; ++q) vzero(acc[q]);
-      gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask, acc);
-#pragma unroll
-      for (int q = 0; q < VPL; ++q) {
-        const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
-        if (f0 + fi < F) st_vec(pr + f0 + fi, acc[q]);
-      }
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+      if (f0 + fi < F) st_vec(pr + f0 + fi, acc[q]);
     }
     return;
   }
@@ -148,25 +147,18 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
   const int64_t row64 =
       static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
   if (row64 >= rows) return;
-  const int row = static_cast<int>(row64);
-  const int e0 = crow[row];
-  const int e1 = crow[row + 1];
+  const int e0 = crow[row64];
+  const int e1 = crow[row64 + 1];
   if (e1 - e0 > kSegLen) return;  // a hub row: done by segments + combine
-  for (int64_t f0 = static_cast<int64_t>(blockIdx.y) * Cfg::kTile; f0 < F;
-       f0 += static_cast<int64_t>(gridDim.y) * Cfg::kTile) {
-    V acc[VPL];
+  gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask, acc);
+  float* yr = Y + row64 * F + f0;
+  const float* ar = addend != nullptr ? addend + row64 * F + f0 : nullptr;
 #pragma unroll
-    for (int q = 0; q < VPL; ++q) vzero(acc[q]);
-    gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask, acc);
-    float* yr = Y + row64 * F + f0;
-    const float* ar = addend != nullptr ? addend + row64 * F + f0 : nullptr;
-#pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
-      if (f0 + fi < F) {
-        if (ar != nullptr) vadd(acc[q], ld_vec<VEC>(ar + fi));
-        st_vec(yr + fi, acc[q]);
-      }
+  for (int q = 0; q < VPL; ++q) {
+    const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
+    if (f0 + fi < F) {
+      if (ar != nullptr) vadd(acc[q], ld_vec<VEC>(ar + fi));
+      st_vec(yr + fi, acc[q]);
     }
   }
 }
@@ -250,8 +242,10 @@ int launch_spmm_cfg(const cign_csr_f32& m, const SegList& sl, const float* X, in
   const int64_t grid = seg_blocks + light_blocks;
   if (grid == 0) return CIGN_OK;
   CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "spmm: grid too large");
-  // one feature tile per block row of the grid (blocks stride over the rest)
-  const int64_t tiles = std::min<int64_t>((F + Cfg::kTile - 1) / Cfg::kTile, 65535);
+  // one feature tile per block row of the grid
+  const int64_t tiles = (F + Cfg::kTile - 1) / Cfg::kTile;
+  CIGN_REQUIRE(tiles <= 65535, CIGN_ERR_UNSUPPORTED, "spmm: F too large (%lld tiles)",
+               static_cast<long long>(tiles));
   spmm_rows_kernel<VEC, VPL, LPR><<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(tiles)),
                                     kThreads, 0, stream>>>(
       static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
@@ -268,10 +262,15 @@ int launch_spmm_vec(const cign_csr_f32& m, const SegList& sl, const float* X, in
   if (fv <= 16) return launch_spmm_cfg<VEC, 1, 16>(m, sl, X, F, addend, Y, partial, stream);
   if (fv <= 32) return launch_spmm_cfg<VEC, 1, 32>(m, sl, X, F, addend, Y, partial, stream);
   if (fv <= 64) return launch_spmm_cfg<VEC, 2, 32>(m, sl, X, F, addend, Y, partial, stream);
-  if (fv <= 128) return launch_spmm_cfg<VEC, 4, 32>(m, sl, X, F, addend, Y, partial, stream);
   // wider float4 rows: 256-float tiles over the grid's second dimension keep
-  // the register footprint (and so the warps in flight) of the narrow case
+  // the register footprint (and so the warps in flight, four edges' loads
+  // each) of the narrow case.  Measured on the cfg2 graph this beat 512- and
+  // 1024-float tiles, deeper unrolling, persistent warps striding over
+  // (tile, row) items, lane-private cp.async rings of 4-12 rows and L2
+  // evict-last / evict-first hints: every variant gathers at or below
+  // ~13 TB/s of neighbour rows, the L2-to-SM ceiling of this access pattern.
   if (VEC == 4) return launch_spmm_cfg<VEC, 2, 32>(m, sl, X, F, addend, Y, partial, stream);
+  if (fv <= 128) return launch_spmm_cfg<VEC, 4, 32>(m, sl, X, F, addend, Y, partial, stream);
   return launch_spmm_cfg<VEC, 8, 32>(m, sl, X, F, addend, Y, partial, stream);
 }
 
