@@ -110,8 +110,7 @@ def step_roofline_items(cfg, nnz, nnz_g):
     add("GAT logits (fp32 GEMM)", L, *gemm(N, 2 * H, D))
     add("GAT aggregate fwd", L, algorithmic_bytes("gat_agg_fwd", N, nnz, H=H, D=D, nnz_g=nnz_g))
     add("GAT z.M (GEMM)", L, *gemm(N, D, HD))
-    add("GAT bias+SiLU fwd", L, 12 * N * D)
-    add("add-LN fwd", L, 12 * N * D + 8 * N)
+    add("GAT bias+SiLU + add-LN fwd", L, 16 * N * D + 8 * N)
     add("[H|C] concat", L, 16 * N * D)
     add("k-hop SpMM fwd hop", L * K, algorithmic_bytes("spmm", N, nnz, F=F2))
     add("hop gate fwd", L, 8 * N * D + 4 * N * K)
@@ -138,8 +137,7 @@ def step_roofline_items(cfg, nnz, nnz_g):
     add("k-hop SpMM bwd hop (+g fused)", L * (K - 1), algorithmic_bytes("spmm_add", N, nnz, F=F2))
     add("k-hop SpMM bwd hop", L, algorithmic_bytes("spmm", N, nnz, F=F2))
     add("hop gate bwd (+ gradient adds)", L, 24 * N * D + 8 * N * K)
-    add("add-LN bwd", L, 16 * N * D + 8 * N)
-    add("GAT bias+SiLU bwd", L, 12 * N * D)
+    add("GAT bias+SiLU + add-LN bwd (+ parameter sums)", L, 20 * N * D + 8 * N)
     add("GAT grad z (GEMM)", L, *gemm(N, HD, D))
     add("GAT aggregate bwd", L, algorithmic_bytes("gat_agg_bwd", N, nnz, H=H, C=D, D=D,
                                                    nnz_g=nnz_g))

@@ -254,16 +254,17 @@ def _head_projection(weight: torch.Tensor, heads: int) -> torch.Tensor:
     return weight.view(heads, C, D).permute(0, 2, 1).reshape(heads * D, C) / heads
 
 
-class _AggregateFirstGATFn(torch.autograd.Function):
-    """SiLU(mean_h sum_j w_ijh (lin.weight_h x_j) + bias) computed as
-    SiLU(z.view(N, H*D) @ M + bias) with z = cign_gat_agg_fwd(x).
+class _AggregateFirstLinFn(torch.autograd.Function):
+    """lin = mean_h sum_j w_ijh (lin.weight_h x_j), computed as z.view(N, H*D) @ M
+    with z = cign_gat_agg_fwd(x): the collapsed GAT's head-mean output before
+    its bias (collapsed_gat_cuda.cu:52-174 with in_feat = lin(x)).
 
-    z is not kept for the backward: the weight gradient sum_i z_i^T g_pre_i
+    z is not kept for the backward: the weight gradient sum_i z_i^T g_i
     equals sum_j gfeat_j^T x_j (gfeat = the gradient of lin(x).view(N,H,C),
     which the backward kernels produce anyway), so only x is saved."""
 
     @staticmethod
-    def forward(ctx, x, attn_row, attn_col, weight, bias, plan, heads, negative_slope, attn_drop,
+    def forward(ctx, x, attn_row, attn_col, weight, plan, heads, negative_slope, attn_drop,
                 seed):
         H = int(heads)
         n, D = int(plan.n), int(x.size(1))
@@ -272,19 +273,18 @@ class _AggregateFirstGATFn(torch.autograd.Function):
         M = _head_projection(weight, H)
         lin = z.view(n, H * D).mm(M)
         del z
-        out, pre = _bias_silu(lin, bias)
-        ctx.save_for_backward(x, attn_row, attn_col, weight, pre, emax, esum)
+        ctx.save_for_backward(x, attn_row, attn_col, weight, emax, esum)
         ctx.plan, ctx.heads = plan, H
         ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), seed
-        return out
+        return lin
 
     @staticmethod
-    def backward(ctx, grad_out):
-        x, attn_row, attn_col, weight, pre, emax, esum = ctx.saved_tensors
+    def backward(ctx, g_lin):
+        x, attn_row, attn_col, weight, emax, esum = ctx.saved_tensors
         H = ctx.heads
         n_cols = int(x.size(0))
         C = weight.size(0) // H
-        g_pre, grad_bias = _bias_silu_backward(grad_out, pre)
+        g_pre = g_lin.contiguous()
         M = _head_projection(weight, H)
         grad_z = g_pre.mm(M.t())                                    # [N, H*D]
         gfeat, grow, gcol = gat_agg_backward_raw(ctx.plan, attn_row, attn_col, x, emax, esum,
@@ -294,7 +294,97 @@ class _AggregateFirstGATFn(torch.autograd.Function):
         gfeat2 = gfeat.view(n_cols, H * C)
         grad_w = gfeat2.t().mm(x)                                   # [H*C, D]
         grad_x = gfeat2.mm(weight)                                  # [N_cols, D]
-        return grad_x, grow, gcol, grad_w, grad_bias, None, None, None, None, None
+        return grad_x, grow, gcol, grad_w, None, None, None, None, None
+
+
+class _BiasSiLUFn(torch.autograd.Function):
+    """SiLU(lin + bias) (the collapsed GAT's epilogue, collapsed_gat_cuda.cu:167-173)."""
+
+    @staticmethod
+    def forward(ctx, lin, bias):
+        out, pre = _bias_silu(lin, bias)
+        ctx.save_for_backward(pre)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        (pre,) = ctx.saved_tensors
+        g_pre, grad_bias = _bias_silu_backward(grad_out, pre)
+        return g_pre, grad_bias
+
+
+def aggregate_first_with_plan(x, attn_row, attn_col, weight, bias, plan, heads, negative_slope,
+                              attn_drop, seed):
+    """SiLU(lin + bias) of the aggregate-first GAT on an existing plan (the
+    body of collapsed_gat_aggregate_first, for callers holding a plan)."""
+    lin = _AggregateFirstLinFn.apply(x, attn_row, attn_col, weight, plan, heads, negative_slope,
+                                     attn_drop, seed)
+    return _BiasSiLUFn.apply(lin, bias)
+
+
+def silu_add_ln_forward(lin, bias, h, weight, ln_bias, eps):
+    """(y, pre, mean, rstd) of cign_silu_add_ln_fwd."""
+    lib = ensure_collapsed_gat_loaded()
+    n, D = (int(v) for v in lin.shape)
+    y = torch.empty_like(lin)
+    pre = torch.empty_like(lin)
+    mean = torch.empty((n,), dtype=torch.float32, device=lin.device)
+    rstd = torch.empty_like(mean)
+    with _lib.DeviceGuard(lin.device):
+        rc = lib.cign_silu_add_ln_fwd(n, D, _lib.ptr(lin), _lib.ptr(bias), _lib.ptr(h),
+                                      _lib.ptr(weight), _lib.ptr(ln_bias), float(eps),
+                                      _lib.ptr(pre), _lib.ptr(y), _lib.ptr(mean), _lib.ptr(rstd),
+                                      _lib.stream_of(lin))
+    _lib.check(rc, "cign_silu_add_ln_fwd")
+    return y, pre, mean, rstd
+
+
+def silu_add_ln_backward(grad_y, pre, h, weight, mean, rstd):
+    """(grad_z, grad_pre, grad_w, grad_b, grad_bias) of cign_silu_add_ln_bwd."""
+    lib = ensure_collapsed_gat_loaded()
+    n, D = (int(v) for v in pre.shape)
+    gz = torch.empty_like(pre)
+    gpre = torch.empty_like(pre)
+    gw = torch.empty((D,), dtype=torch.float32, device=pre.device)
+    gb = torch.empty_like(gw)
+    gbias = torch.empty_like(gw)
+    ws = _lib.workspace(lib.cign_silu_add_ln_bwd_workspace_bytes(n, D), pre.device)
+    with _lib.DeviceGuard(pre.device):
+        rc = lib.cign_silu_add_ln_bwd(n, D, _lib.ptr(grad_y), _lib.ptr(pre), _lib.ptr(h),
+                                      _lib.ptr(weight), _lib.ptr(mean), _lib.ptr(rstd),
+                                      _lib.ptr(gz), _lib.ptr(gpre), _lib.ptr(gw), _lib.ptr(gb),
+                                      _lib.ptr(gbias), _lib.ptr(ws), ws.numel(),
+                                      _lib.stream_of(pre))
+    _lib.check(rc, "cign_silu_add_ln_bwd")
+    return gz, gpre, gw, gb, gbias
+
+
+class _SiLUAddLayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, lin, bias, h, weight, ln_bias, eps):
+        lin, h = lin.contiguous(), h.contiguous()
+        y, pre, mean, rstd = silu_add_ln_forward(lin, bias, h, weight, ln_bias, eps)
+        ctx.save_for_backward(pre, h, weight, mean, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        pre, h, weight, mean, rstd = ctx.saved_tensors
+        gz, gpre, gw, gb, gbias = silu_add_ln_backward(grad_y.contiguous(), pre, h, weight, mean,
+                                                       rstd)
+        return gpre, gbias, gz, gw, gb, None
+
+
+def gat_silu_add_layernorm(lin: torch.Tensor, bias: torch.Tensor, h: torch.Tensor,
+                           weight: torch.Tensor, ln_bias: torch.Tensor,
+                           eps: float) -> torch.Tensor:
+    """LayerNorm(SiLU(lin + bias) + h) with LayerNorm weight/ln_bias: the GAT
+    layer's bias + SiLU epilogue and the block's add-LayerNorm
+    (model_cign.py:767-787) as one op, forward and backward.  lin is the GAT's
+    head-mean output before its bias (collapsed_gat_aggregate_first_lin)."""
+    if lin.dim() != 2 or h.shape != lin.shape:
+        raise ValueError("lin and h must both be [N, D]")
+    return _SiLUAddLayerNormFn.apply(lin, bias, h, weight, ln_bias, float(eps))
 
 
 @contextlib.contextmanager
@@ -380,6 +470,33 @@ def collapsed_gat_aggregate_first(x: torch.Tensor, attn_row: torch.Tensor, attn_
         raise RuntimeError(f"graph is {plan.n} x {plan.n_cols} but x has {x.size(0)} rows, "
                            f"attn_row {attn_row.size(0)}, attn_col {attn_col.size(0)}")
     seed = gat_call_seed(attn_drop)
-    return _AggregateFirstGATFn.apply(x.contiguous(), attn_row.contiguous(), attn_col.contiguous(),
-                                      weight, bias, plan, H, float(negative_slope),
-                                      float(attn_drop), seed)
+    return aggregate_first_with_plan(x.contiguous(), attn_row.contiguous(), attn_col.contiguous(),
+                                     weight, bias, plan, H, float(negative_slope),
+                                     float(attn_drop), seed)
+
+
+def collapsed_gat_aggregate_first_lin(x: torch.Tensor, attn_row: torch.Tensor,
+                                      attn_col: torch.Tensor, weight: torch.Tensor, csr, csc,
+                                      perm: torch.Tensor, negative_slope: float,
+                                      attn_drop: float) -> torch.Tensor:
+    """The head-mean output of collapsed_gat_aggregate_first before its bias and
+    SiLU ([N, C]); pair it with gat_silu_add_layernorm.  Same arguments,
+    checks and dropout stream."""
+    if x.dtype != torch.float32 or x.device.type != "cuda" or x.dim() != 2:
+        raise TypeError("aggregate-first GAT requires CUDA float32 x [N,D]")
+    H = int(attn_row.size(1))
+    if not (1 <= H <= MAX_HEADS):
+        raise ValueError(f"collapsed GAT requires 1<=H<={MAX_HEADS}; got H={H}")
+    if weight.dim() != 2 or weight.size(0) % H != 0 or weight.size(1) != x.size(1):
+        raise ValueError("weight must be [H*C, D]")
+    if not (0.0 <= float(attn_drop) < 1.0):
+        raise ValueError("attn_drop must be in [0,1)")
+    (rowptr, col), (row, colptr) = csr, csc
+    plan = gat_plan_for(rowptr, col, row, colptr, perm)
+    if plan.n_cols != x.size(0) or attn_row.size(0) != plan.n or attn_col.size(0) != plan.n_cols:
+        raise RuntimeError(f"graph is {plan.n} x {plan.n_cols} but x has {x.size(0)} rows, "
+                           f"attn_row {attn_row.size(0)}, attn_col {attn_col.size(0)}")
+    seed = gat_call_seed(attn_drop)
+    return _AggregateFirstLinFn.apply(x.contiguous(), attn_row.contiguous(),
+                                      attn_col.contiguous(), weight, plan, H,
+                                      float(negative_slope), float(attn_drop), seed)

@@ -307,6 +307,173 @@ gamma_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy
   }
 }
 
+// ------------------------------------------------ GAT epilogue + add-LN
+// The GAT layer's side ops and the block's add-LayerNorm in one pass over
+// the row (model_cign.py:767-787 with the collapsed GAT's bias + SiLU,
+// collapsed_gat_cuda.cu:167-173, and fused_add_layernorm):
+//   pre = lin + bias;  c = SiLU(pre);  y = LayerNorm(c + h) * w + b.
+// `lin` is the head-mean GAT output before its bias (the aggregate-first
+// form's z @ M).  Writes pre (for the SiLU backward), y, mean and rstd; the
+// SiLU output itself is never stored.  The formulas of
+// cign_head_mean_bias_silu_fwd (one head) followed by cign_add_ln_fwd.
+template <int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+silu_add_ln_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ lin,
+                       const float* __restrict__ bias, const float* __restrict__ h,
+                       const float* __restrict__ w, const float* __restrict__ b, float eps,
+                       float* __restrict__ pre_out, float* __restrict__ y,
+                       float* __restrict__ mean, float* __restrict__ rstd) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = RowCfg<VEC, VPL, LPR>;
+  const int lig = threadIdx.x % LPR;
+  const unsigned gmask = row_group_mask<LPR>();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + threadIdx.x / LPR;
+  if (row >= n) return;
+  V q[VPL];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+    vzero(q[k]);
+    if (d < D) {
+      const V lv = ld_vec<VEC>(lin + row * D + d);
+      const V bv = ldg_vec<VEC>(bias + d);
+      const V hv = ld_vec<VEC>(h + row * D + d);
+      V pv;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        vel(pv, j) = vel(lv, j) + vel(bv, j);
+        vel(q[k], j) = silu_f(vel(pv, j)) + vel(hv, j);
+        s += vel(q[k], j);
+      }
+      st_vec(pre_out + row * D + d, pv);
+    }
+  }
+  const float mu = gsum<LPR>(s, gmask) / static_cast<float>(D);
+  float v = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+    if (d < D) {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float cdev = vel(q[k], j) - mu;
+        v += cdev * cdev;
+      }
+    }
+  }
+  const float rs = rsqrtf(gsum<LPR>(v, gmask) / static_cast<float>(D) + eps);
+  if (lig == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+    if (d < D) {
+      const V wv = ldg_vec<VEC>(w + d);
+      const V bv = ldg_vec<VEC>(b + d);
+      V o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) vel(o, j) = (vel(q[k], j) - mu) * rs * vel(wv, j) + vel(bv, j);
+      st_vec(y + row * D + d, o);
+    }
+  }
+}
+
+// Backward of silu_add_ln_fwd: grad_z = dLN/d(c + h) (the gradient of h, and
+// of the SiLU output c), grad_pre = grad_z * SiLU'(pre) (the gradient of lin),
+// and per-chunk partials of sum(gy * xhat), sum(gy) (LN weight and bias) and
+// sum(grad_pre) (the GAT bias), reduced in a fixed order like ln_bwd_kernel.
+template <int VEC, int VPL, int LPR>
+__global__ void __launch_bounds__(kThreads)
+silu_add_ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
+                       const float* __restrict__ pre, const float* __restrict__ h,
+                       const float* __restrict__ w, const float* __restrict__ mean,
+                       const float* __restrict__ rstd, float* __restrict__ gz,
+                       float* __restrict__ gpre, float* __restrict__ pw,
+                       float* __restrict__ pb, float* __restrict__ pbias) {
+  using V = typename VecT<VEC>::type;
+  using Cfg = RowCfg<VEC, VPL, LPR>;
+  __shared__ float red[kThreads * VPL * VEC];
+  const int lig = threadIdx.x % LPR;
+  const int group = threadIdx.x / LPR;
+  const unsigned gmask = row_group_mask<LPR>();
+  const float Df = static_cast<float>(D);
+  V aw[VPL], ab[VPL], ag[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    vzero(aw[k]);
+    vzero(ab[k]);
+    vzero(ag[k]);
+  }
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
+  const int64_t r1 = (r0 + rpc < n) ? (r0 + rpc) : n;
+  for (int64_t row = r0 + group; row < r1; row += Cfg::kGroups) {
+    const float mu = mean[row], rs = rstd[row];
+    V xh[VPL], dn[VPL], pv[VPL];
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+      vzero(xh[k]);
+      vzero(dn[k]);
+      vzero(pv[k]);
+      if (d < D) {
+        pv[k] = ld_vec<VEC>(pre + row * D + d);
+        const V hv = ld_vec<VEC>(h + row * D + d);
+        const V gv = ld_vec<VEC>(gy + row * D + d);
+        const V wv = ldg_vec<VEC>(w + d);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float qv = silu_f(vel(pv[k], j)) + vel(hv, j);
+          const float xhat = (qv - mu) * rs;
+          const float dnorm = vel(gv, j) * vel(wv, j);
+          vel(xh[k], j) = xhat;
+          vel(dn[k], j) = dnorm;
+          s1 += dnorm;
+          s2 += dnorm * xhat;
+          vel(aw[k], j) += vel(gv, j) * xhat;
+          vel(ab[k], j) += vel(gv, j);
+        }
+      }
+    }
+    s1 = gsum<LPR>(s1, gmask);
+    s2 = gsum<LPR>(s2, gmask);
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
+      if (d < D) {
+        V oz, op;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float dq = (rs / Df) * (Df * vel(dn[k], j) - s1 - vel(xh[k], j) * s2);
+          vel(oz, j) = dq;
+          vel(op, j) = dq * silu_grad_f(vel(pv[k], j));
+          vel(ag[k], j) += vel(op, j);
+        }
+        st_vec(gz + row * D + d, oz);
+        st_vec(gpre + row * D + d, op);
+      }
+    }
+  }
+  for (int pass = 0; pass < 3; ++pass) {
+    V(&acc)[VPL] = pass == 0 ? aw : (pass == 1 ? ab : ag);
+    float* out = pass == 0 ? pw : (pass == 1 ? pb : pbias);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < VPL; ++k)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) red[(group * Cfg::kTile) + (lig + k * LPR) * VEC + j] = vel(acc[k], j);
+    __syncthreads();
+    for (int64_t d = threadIdx.x; d < D && d < Cfg::kTile; d += kThreads) {
+      float t = 0.0f;
+      for (int g = 0; g < Cfg::kGroups; ++g) t += red[g * Cfg::kTile + d];
+      out[static_cast<int64_t>(blockIdx.x) * D + d] = t;
+    }
+  }
+}
+
 __global__ void block_mask_kernel(int64_t count, float p, Seed seed_in,
                                   uint8_t* __restrict__ mask) {
   const uint64_t seed = seed_in;
@@ -360,6 +527,36 @@ int launch_ln_bwd(int64_t n, int64_t D, const float* gy, const float* x, const f
       n, D, rpc, gy, x, x2, w, mean, rstd, p, seed, gx, pw, pb);
   CIGN_CHECK_LAUNCH("ln_bwd_kernel");
   return colsum_rows(pw, gw, pb, gb, chunks, D, D, s);
+}
+
+template <int VEC, int VPL, int LPR>
+int launch_silu_add_ln_fwd(int64_t n, int64_t D, const float* lin, const float* bias,
+                           const float* h, const float* w, const float* b, float eps, float* pre,
+                           float* y, float* mean, float* rstd, cudaStream_t s) {
+  using Cfg = RowCfg<VEC, VPL, LPR>;
+  const int64_t grid = (n + Cfg::kGroups - 1) / Cfg::kGroups;
+  silu_add_ln_fwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      n, D, lin, bias, h, w, b, eps, pre, y, mean, rstd);
+  CIGN_CHECK_LAUNCH("silu_add_ln_fwd_kernel");
+  return CIGN_OK;
+}
+
+template <int VEC, int VPL, int LPR>
+int launch_silu_add_ln_bwd(int64_t n, int64_t D, const float* gy, const float* pre,
+                           const float* h, const float* w, const float* mean, const float* rstd,
+                           float* gz, float* gpre, float* gw, float* gb, float* gbias, float* ws,
+                           cudaStream_t s) {
+  const int64_t rpc = rows_per_chunk(n);
+  const int64_t chunks = num_chunks(n);
+  float* pw = ws;
+  float* pb = ws + chunks * D;
+  float* pbias = ws + 2 * chunks * D;
+  silu_add_ln_bwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(chunks), kThreads, 0, s>>>(
+      n, D, rpc, gy, pre, h, w, mean, rstd, gz, gpre, pw, pb, pbias);
+  CIGN_CHECK_LAUNCH("silu_add_ln_bwd_kernel");
+  int rc = colsum_rows(pw, gw, pb, gb, chunks, D, D, s);
+  if (rc) return rc;
+  return colsum_rows(pbias, gbias, nullptr, nullptr, chunks, D, D, s);
 }
 
 template <int VEC, int VPL, int LPR>
@@ -526,6 +723,58 @@ int cign_gamma_residual_bwd(int64_t n, int64_t d, const float* grad_y, const flo
     CIGN_ROW_DISPATCH(4, d / 4, return (launch_gamma_bwd<V_, P_, L_>(n, d, grad_y, g, gamma, p, seed, grad_g, grad_gamma, wsf, s)));
   }
   CIGN_ROW_DISPATCH(1, d, return (launch_gamma_bwd<V_, P_, L_>(n, d, grad_y, g, gamma, p, seed, grad_g, grad_gamma, wsf, s)));
+  return CIGN_OK;
+}
+
+int cign_silu_add_ln_fwd(int64_t n, int64_t d, const float* lin, const float* bias,
+                         const float* h, const float* w, const float* b, float eps, float* pre,
+                         float* y, float* mean, float* rstd, cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(lin) && aligned16(bias) && aligned16(h) &&
+                  aligned16(w) && aligned16(b) && aligned16(pre) && aligned16(y);
+  int rc = check_rows(n, d, v4, "silu_add_ln_fwd");
+  if (rc) return rc;
+  if (n == 0) return CIGN_OK;
+  CIGN_REQUIRE(lin && bias && h && w && b && pre && y && mean && rstd, CIGN_ERR_NULL_POINTER,
+               "silu_add_ln_fwd: NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_silu_add_ln_fwd<V_, P_, L_>(n, d, lin, bias, h, w, b, eps, pre, y, mean, rstd, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_silu_add_ln_fwd<V_, P_, L_>(n, d, lin, bias, h, w, b, eps, pre, y, mean, rstd, s)));
+  return CIGN_OK;
+}
+
+size_t cign_silu_add_ln_bwd_workspace_bytes(int64_t n, int64_t d) {
+  if (n <= 0) return 0;
+  return static_cast<size_t>(num_chunks(n)) * d * 3 * sizeof(float);
+}
+
+int cign_silu_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* pre,
+                         const float* h, const float* w, const float* mean, const float* rstd,
+                         float* grad_z, float* grad_pre, float* grad_w, float* grad_b,
+                         float* grad_bias, void* ws, size_t ws_bytes, cign_stream_t stream) {
+  const bool v4 = d % 4 == 0 && aligned16(grad_y) && aligned16(pre) && aligned16(h) &&
+                  aligned16(w) && aligned16(grad_z) && aligned16(grad_pre);
+  int rc = check_rows(n, d, v4, "silu_add_ln_bwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(grad_w && grad_b && grad_bias, CIGN_ERR_NULL_POINTER,
+               "silu_add_ln_bwd: NULL parameter gradient");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_w, 0, d * sizeof(float), s), "memset");
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_b, 0, d * sizeof(float), s), "memset");
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_bias, 0, d * sizeof(float), s), "memset");
+    return CIGN_OK;
+  }
+  CIGN_REQUIRE(grad_y && pre && h && w && mean && rstd && grad_z && grad_pre,
+               CIGN_ERR_NULL_POINTER, "silu_add_ln_bwd: NULL");
+  CIGN_REQUIRE(ws != nullptr && ws_bytes >= cign_silu_add_ln_bwd_workspace_bytes(n, d),
+               CIGN_ERR_INVALID_ARGUMENT, "silu_add_ln_bwd: workspace too small");
+  float* wsf = static_cast<float*>(ws);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_silu_add_ln_bwd<V_, P_, L_>(n, d, grad_y, pre, h, w, mean, rstd, grad_z, grad_pre, grad_w, grad_b, grad_bias, wsf, s)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_silu_add_ln_bwd<V_, P_, L_>(n, d, grad_y, pre, h, w, mean, rstd, grad_z, grad_pre, grad_w, grad_b, grad_bias, wsf, s)));
   return CIGN_OK;
 }
 

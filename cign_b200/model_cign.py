@@ -15,11 +15,13 @@ outer nonlinearity "none"):
     x      = lin(H_norm).view(N, heads, D)                  cuBLAS (TF32)
     a_s, a_d = attention logits(x)                          fused_gat_sideops
     C_gat  = SiLU(mean_h GAT(x) + bias)                     collapsed_gat
-  (GATContext evaluates the three GAT lines aggregate-first by default:
-   a = H_norm @ (W_h^T att)^T, z_h = GAT-weighted sums of H_norm rows,
-   C_gat = SiLU(z @ M + bias) -- the same function with lin applied after
-   the aggregation, so each edge gathers one D-float row, not heads*D.)
     C_norm = LN(C_gat + H_norm)                             fused_block_ops
+  (GATContext evaluates the GAT aggregate-first by default:
+   a = H_norm @ (W_h^T att)^T, z_h = GAT-weighted sums of H_norm rows,
+   lin = z @ M -- the same function with lin applied after the aggregation,
+   so each edge gathers one D-float row, not heads*D -- and the block then
+   forms C_norm = LN(SiLU(lin + bias) + H_norm) in one pass,
+   gat_silu_add_layernorm, without storing C_gat.)
     T^k    = P^k [H_norm | C_norm], k in order_set          multihop_csr_pipeline
     alpha  = softmax(hop_gate_mlp([H+C | |H-C|]))           hop_gate (fused)
     G_raw  = Clifford pack(H_norm, C_norm, T, alpha)        fused_clifford_*
@@ -37,7 +39,8 @@ import torch.nn.functional as F
 
 from . import fused_clifford_cign_generic, fused_clifford_cign_pack, fused_clifford_pack
 from .collapsed_gat import (attention_logits_through_weight, collapsed_gat_aggregate_first,
-                            collapsed_gat_mean_bias_silu)
+                            collapsed_gat_aggregate_first_lin, collapsed_gat_mean_bias_silu,
+                            gat_silu_add_layernorm)
 from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, fused_dropout_layernorm
 from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
@@ -91,6 +94,27 @@ class GATContext(nn.Module):
         _glorot_(self.lin.weight)
         _glorot_(self.att_src)
         _glorot_(self.att_dst)
+
+    def forward_lin(self, x: torch.Tensor, gat_graph):
+        """The head-mean GAT output before its bias and SiLU ([N, C]) when the
+        aggregate-first form applies, else None; the block then evaluates
+        bias + SiLU + add-LayerNorm in one op (gat_silu_add_layernorm)."""
+        H, C = self.heads, self.out_channels
+        if not (self.aggregate_first and x.size(1) % 4 == 0 and C % 4 == 0):
+            return None
+        drop = self.dropout if self.training else 0.0
+        if hasattr(gat_graph, "halo"):  # cign_b200.distributed.DistGatGraph
+            csr, csc, perm = gat_graph.csr, gat_graph.csc, gat_graph.perm
+            x_src = gat_graph.halo(x)
+        else:
+            csr, csc, perm = gat_graph
+            x_src = x
+        alpha = attention_logits_through_weight(x_src, self.lin.weight, self.att_src,
+                                                self.att_dst, H)
+        return collapsed_gat_aggregate_first_lin(
+            x_src, attn_row=alpha[:x.size(0), H:].contiguous(),
+            attn_col=alpha[:, :H].contiguous(), weight=self.lin.weight, csr=csr, csc=csc,
+            perm=perm, negative_slope=self.negative_slope, attn_drop=drop)
 
     def forward(self, x: torch.Tensor, gat_graph) -> torch.Tensor:
         H, C = self.heads, self.out_channels
@@ -170,9 +194,15 @@ class GraphCliffordBlock(nn.Module):
     def forward(self, H, graph_operator, gat_graph):
         p = self.dropout if self.training else 0.0
         H_norm = fused_dropout_layernorm(H, self.h_norm.weight, self.h_norm.bias, p, self.h_norm.eps)
-        C_gat = self.context_gat(H_norm, gat_graph)
-        C_norm = fused_add_layernorm(C_gat, H_norm, self.c_norm.weight, self.c_norm.bias,
-                                     self.c_norm.eps)
+        lin = self.context_gat.forward_lin(H_norm, gat_graph)
+        if lin is not None:
+            # GAT bias + SiLU and the add-LayerNorm in one pass (forward and backward)
+            C_norm = gat_silu_add_layernorm(lin, self.context_gat.bias, H_norm, self.c_norm.weight,
+                                            self.c_norm.bias, self.c_norm.eps)
+        else:
+            C_gat = self.context_gat(H_norm, gat_graph)
+            C_norm = fused_add_layernorm(C_gat, H_norm, self.c_norm.weight, self.c_norm.bias,
+                                         self.c_norm.eps)
         plan = native_spmm_plan(graph_operator)
         if (plan is not None and self.interaction_mode == "new" and self.outer_nonlinearity == "none"
                 and self.alpha_weighting_mode == "old" and self.alpha_score_mode in ("new", "old")

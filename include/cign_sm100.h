@@ -492,6 +492,26 @@ CIGN_API int cign_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const fl
                     float* grad_b, void* ws, size_t ws_bytes,
                     cign_stream_t stream);
 
+/* GAT side ops and the block's add-LayerNorm in one pass (replaces the
+ * head-mean + bias + SiLU epilogue of collapsed_gat_cuda.cu:167-173 followed by
+ * fused_add_layernorm, fused_block_ops.py:112 / model_cign.py:767-787):
+ *   pre = lin + bias;  y = LayerNorm(SiLU(pre) + h) * w + b.
+ * lin [n,d] is the head-mean GAT output before its bias; writes pre, y and
+ * the row mean / rstd; SiLU(pre) itself is not stored. */
+CIGN_API int cign_silu_add_ln_fwd(int64_t n, int64_t d, const float* lin, const float* bias,
+                         const float* h, const float* w, const float* b, float eps,
+                         float* pre, float* y, float* mean, float* rstd,
+                         cign_stream_t stream);
+CIGN_API size_t cign_silu_add_ln_bwd_workspace_bytes(int64_t n, int64_t d);
+/* Backward of cign_silu_add_ln_fwd: grad_z = d LN / d(SiLU(pre) + h) (the
+ * gradient of h), grad_pre = grad_z * SiLU'(pre) (the gradient of lin), and
+ * the LN weight / bias and GAT bias gradients (fixed-order sums). */
+CIGN_API int cign_silu_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* pre,
+                         const float* h, const float* w, const float* mean,
+                         const float* rstd, float* grad_z, float* grad_pre,
+                         float* grad_w, float* grad_b, float* grad_bias, void* ws,
+                         size_t ws_bytes, cign_stream_t stream);
+
 /* y = h + gamma * dropout(g). */
 CIGN_API int cign_gamma_residual_fwd(int64_t n, int64_t d, const float* h,
                             const float* g, const float* gamma, float p,

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from cign_b200 import synth
-from cign_b200.collapsed_gat import _AggregateFirstGATFn, gat_agg_forward_raw
+from cign_b200.collapsed_gat import aggregate_first_with_plan, gat_agg_forward_raw
 from cign_b200.graph_operator import prepare_gat_edge_index, to_graph_format
 from cign_b200.plans import gat_plan_for
 from oracle import ops
@@ -39,7 +39,7 @@ def _case(dev, edge, n, H, D, C, p, seed, slope=0.2):
     grads_o = torch.autograd.grad(out_o, leaves, gy)
     # native, aggregate first
     ins = [t.to(dev).requires_grad_(True) for t in (x, a_dst, a_src, W, bias)]
-    out = _AggregateFirstGATFn.apply(ins[0], ins[1], ins[2], ins[3], ins[4], plan, H, slope, p,
+    out = aggregate_first_with_plan(ins[0], ins[1], ins[2], ins[3], ins[4], plan, H, slope, p,
                                      seed)
     grads = torch.autograd.grad(out, ins, gy.to(dev))
     tag = f"n={n} H={H} D={D} C={C} p={p}"

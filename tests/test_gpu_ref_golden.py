@@ -89,7 +89,7 @@ def test_aggregate_first_gat_vs_reference_kernel(cuda, gat, tag, p):
     a_row, a_col, bias = g("attn_row"), g("attn_col"), g("bias")
     x = _d(z, "in_feat", cuda).reshape(n, H * C).clone().requires_grad_(True)
     weight = torch.eye(H * C, device=cuda)
-    out = collapsed_gat._AggregateFirstGATFn.apply(x, a_row, a_col, weight, bias, plan, H,
+    out = collapsed_gat.aggregate_first_with_plan(x, a_row, a_col, weight, bias, plan, H,
                                                    float(z["negative_slope"]), p, seed)
     assert_parity(out, z[f"out_{tag}"], what=f"out {tag}")
     out.backward(_d(z, "grad_y", cuda))
