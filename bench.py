@@ -678,6 +678,62 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
 
 
 # ------------------------------------------------------------------ sweep
+def sweep_bf16(device, emit):
+    """fp32 against bf16 feature storage (fp32 accumulation) for the two
+    gathers of the path -- one k-hop SpMM hop at F = 1024 and the
+    aggregate-first GAT forward at D = 512 -- on the cfg2 graph and on one
+    eighth of the cfg5 graph (an RMAT graph of 1.25M nodes and 40M edges,
+    the row block one of 8 GPUs owns, with the same degree law), each run
+    as a square operator.  Device times from CUDA events."""
+    from cign_b200 import collapsed_gat, synth
+    from cign_b200.graph_operator import (build_sparse_normalized_adjacency,
+                                          prepare_fixed_csr_operator, prepare_gat_edge_index,
+                                          to_graph_format)
+    from cign_b200.multihop_csr_pipeline import _csr_parts_int32
+    from cign_b200.plans import SpmmPlan, gat_plan_for
+    stream = torch.cuda.current_stream(device)
+    g = torch.Generator(device=device).manual_seed(5)
+    cfg5 = synth.CONFIGS["cfg5"]
+    graphs = [("cfg2_powerlaw24492", lambda: synth.make_edges(synth.CONFIGS["cfg2"]).to(device),
+               synth.CONFIGS["cfg2"].num_nodes),
+              ("cfg5_rmat_shard1250000", lambda: synth.rmat_graph(
+                  cfg5.num_nodes // 8, cfg5.num_edges // 8, seed=cfg5.seed, device=device).to(device),
+               cfg5.num_nodes // 8)]
+    for name, make, n in graphs:
+        edge = make()
+        ei, adj = build_sparse_normalized_adjacency(edge, n)
+        base = prepare_fixed_csr_operator(adj)
+        plan = SpmmPlan(*_csr_parts_int32(base.csr))
+        nnz = int(base.nnz)
+        del adj
+        F = 1024
+        X = torch.randn(n, F, device=device, generator=g)
+        Xb = X.to(torch.bfloat16)
+        t32 = time_launches(lambda: plan.spmm(X), 5, stream)
+        t16 = time_launches(lambda: plan.spmm_bf16(Xb, torch.bfloat16), 5, stream)
+        emit({"op": "spmm_hop_storage", "storage_graph": name, "storage_nodes": n,
+              "storage_nnz_P": nnz, "F": F,
+              "fp32_ms": round(t32 * 1e3, 4), "bf16_ms": round(t16 * 1e3, 4),
+              "gather_tbs_fp32": round(4 * nnz * F / t32 / 1e12, 2),
+              "gather_tbs_bf16": round(2 * nnz * F / t16 / 1e12, 2)})
+        del X, Xb
+        (rp, c), (r, cp), perm = to_graph_format(prepare_gat_edge_index(ei, n).flip(0), n)
+        gplan = gat_plan_for(rp, c, r, cp, perm)
+        H, D = 8, 512
+        x = torch.randn(n, D, device=device, generator=g)
+        xb = x.to(torch.bfloat16)
+        a = torch.randn(n, H, device=device, generator=g)
+        t32 = time_launches(lambda: collapsed_gat.gat_agg_forward_raw(gplan, a, a, x, H, 0.2, 0.5, 7),
+                            3, stream)
+        t16 = time_launches(lambda: collapsed_gat.gat_agg_forward_raw(gplan, a, a, xb, H, 0.2, 0.5,
+                                                                      7), 3, stream)
+        emit({"op": "gat_agg_fwd_storage", "storage_graph": name, "storage_nodes": n,
+              "storage_nnz_gat": int(c.numel()),
+              "heads": H, "D": D, "fp32_ms": round(t32 * 1e3, 4), "bf16_ms": round(t16 * 1e3, 4)})
+        del x, xb, gplan, plan, base, ei, edge
+        torch.cuda.empty_cache()
+
+
 def run_sweep(args, device):
     """isolated kernel sweep on the cfg2 graph.  One JSON line per
     case: k-hop SpMM (hops 1..8, F in {64, 128, 512}; forward chain and its
@@ -701,6 +757,8 @@ def run_sweep(args, device):
         print(json.dumps(d), flush=True)
 
     ops = set(args.sweep_ops.split(",")) if args.sweep_ops else {"spmm", "gat", "pack"}
+    if "bf16" in ops:
+        sweep_bf16(device, emit)
     for F in ((64, 128, 512) if "spmm" in ops else ()):
         X = torch.randn(N, F, device=device, generator=g)
         for K in range(1, 9):
@@ -849,7 +907,8 @@ def main():
                     help="block pack + proj: tcgen05 pack-prologue GEMM (fused), pack kernel + "
                          "cuBLAS (separate), or fused only when G_raw is recomputed (auto)")
     ap.add_argument("--sweep-ops", default="",
-                    help="comma-separated subset of the sweep: spmm,gat,pack (default all)")
+                    help="comma-separated subset of the sweep: spmm,gat,pack (default all), "
+                         "bf16 (fp32 against bf16 feature storage, cfg2 and a cfg5 shard)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the workload's number of CIGN blocks (0: the config's)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",

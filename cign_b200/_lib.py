@@ -77,6 +77,10 @@ SIGNATURES = {
     "cign_multihop_workspace_bytes": (c_size_t, [_P, c_int, c_int64]),
     "cign_multihop_fwd": (c_int, [_P, c_int, _P, c_int64, _PP, _P, c_size_t, _P]),
     "cign_multihop_bwd": (c_int, [_P, c_int, _PP, c_int64, _P, _P, c_size_t, _P]),
+    "cign_spmm_bf16": (c_int, [_P, c_int, _P, c_int64, _P, c_int, _P, c_size_t, _P]),
+    "cign_multihop_fwd_bf16": (c_int, [_P, c_int, _P, c_int64, _PP, _P, c_size_t, _P]),
+    "cign_gat_agg_fwd_bf16": (c_int, [_P, c_int32, c_int64, _P, _P, _P, c_float, c_float, c_uint64,
+                                      _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_gat_plan_create": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, POINTER(c_void_p)]),
     "cign_gat_plan_create_rect": (c_int, [c_int64, c_int64, c_int64, _P, _P, _P, _P, _P,
                                           POINTER(c_void_p)]),

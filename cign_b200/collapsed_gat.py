@@ -176,7 +176,9 @@ def collapsed_gat_mean_bias_silu(
 
 # ---------------------------------------------------------------- aggregate-first
 def gat_agg_forward_raw(plan, attn_row, attn_col, x, heads, negative_slope, attn_drop, seed):
-    """z [N,H,D] = per-head attention-weighted sums of x rows; returns (z, emax, esum)."""
+    """z [N,H,D] fp32 = per-head attention-weighted sums of x rows; returns
+    (z, emax, esum).  x may be float32 or bfloat16 (bf16 storage, widened to
+    fp32 as it is gathered: cign_gat_agg_fwd_bf16, D % 8 == 0)."""
     lib = ensure_collapsed_gat_loaded()
     D = int(x.size(1))
     n = int(plan.n)  # destination rows (x has plan.n_cols rows)
@@ -185,12 +187,13 @@ def gat_agg_forward_raw(plan, attn_row, attn_col, x, heads, negative_slope, attn
     emax = torch.empty((n, H), dtype=torch.float32, device=x.device)
     esum = torch.empty_like(emax)
     ws = _lib.workspace(lib.cign_gat_agg_workspace_bytes(plan.handle, H, D, D), x.device)
+    fn, name = ((lib.cign_gat_agg_fwd_bf16, "cign_gat_agg_fwd_bf16") if x.dtype == torch.bfloat16
+                else (lib.cign_gat_agg_fwd, "cign_gat_agg_fwd"))
     with _lib.DeviceGuard(x.device):
-        rc = lib.cign_gat_agg_fwd(plan.handle, H, D, _lib.ptr(attn_row), _lib.ptr(attn_col),
-                                  _lib.ptr(x), float(negative_slope), float(attn_drop),
-                                  *_lib.seed_args(seed), _lib.ptr(z), _lib.ptr(emax),
-                                  _lib.ptr(esum), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
-    _lib.check(rc, "cign_gat_agg_fwd")
+        rc = fn(plan.handle, H, D, _lib.ptr(attn_row), _lib.ptr(attn_col), _lib.ptr(x),
+                float(negative_slope), float(attn_drop), *_lib.seed_args(seed), _lib.ptr(z),
+                _lib.ptr(emax), _lib.ptr(esum), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+    _lib.check(rc, name)
     return z, emax, esum
 
 

@@ -34,6 +34,8 @@
 //      grad_attn_col[j,h] = sum_{i->j} grad_logit[e,h] -- gathers, so no
 //      atomics anywhere.
 //   grad_bias = column sums of g_pre (two-stage, fixed order).
+#include <cuda_bf16.h>
+
 #include <algorithm>
 #include <initializer_list>
 #include <map>
@@ -2139,6 +2141,141 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
   }
 }
 
+// Forward aggregation over bf16 layer inputs (storage precision of the
+// large-graph configuration): Z [N, H, D] fp32 = sum_j w_ijh x_j with x
+// stored as bf16 and widened to fp32 as it is used; weights, edge order and
+// fp32 FMA order as gat_agg_kernel<.., 0, ..>, so Z equals that kernel's
+// result on the widened inputs.  Lane l copies 16 bytes = 8 bf16 per ring
+// slot; a tile is 32 * VPL * 8 features.
+template <int VPL>
+__global__ void __launch_bounds__(kThreads)
+gat_agg_fwd_bf16_kernel(int n, int H, int64_t D, const int* __restrict__ ptr,
+                        const int* __restrict__ idx, const int* __restrict__ seg_row,
+                        const int* __restrict__ seg_begin, const int* __restrict__ seg_end,
+                        int n_seg, int seg_blocks, const float* __restrict__ attn_row,
+                        const float* __restrict__ attn_col, float* __restrict__ emax,
+                        float* __restrict__ esum, const __nv_bfloat16* __restrict__ src,
+                        float slope, float p, Seed seed_in, float* __restrict__ out,
+                        float* __restrict__ partial) {
+  extern __shared__ uint4 aggb_ring[];
+  const uint64_t seed = seed_in;
+  constexpr int kTile = 32 * VPL * 8;
+  const int lane = threadIdx.x & 31;
+  const int group = threadIdx.x >> 5;
+  const int64_t f0 = static_cast<int64_t>(blockIdx.y) * kTile;
+  const uint32_t my_ring =
+      smem_u32(aggb_ring) + static_cast<uint32_t>((group * kAggStages * VPL * 32 + lane) * 16);
+  int64_t item, target;
+  int e0, e1;
+  bool seg;
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    item = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + group;
+    if (item >= n_seg) return;
+    target = seg_row[item];
+    e0 = seg_begin[item];
+    e1 = seg_end[item];
+    seg = true;
+  } else {
+    target = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
+    if (target >= n) return;
+    e0 = ptr[target];
+    e1 = ptr[target + 1];
+    if (e1 - e0 > kSegLen) return;
+    item = target;
+    seg = false;
+  }
+  const int k = e0 + lane;
+  const bool valid = k < e1;
+  const int cnt = e1 - e0;
+  const int other = valid ? __ldg(idx + k) : 0;
+  auto issue = [&](int t) {
+    const __nv_bfloat16* xr = src + static_cast<int64_t>(__shfl_sync(kFullMask, other, t)) * D;
+    const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 8;
+      if (fi < D) cp_async16_s(slot + q * 32 * 16, xr + fi);
+    }
+  };
+  const int64_t HD = static_cast<int64_t>(H) * D;
+  for (int h0 = 0; h0 < H; h0 += kAggHB) {
+#pragma unroll
+    for (int t = 0; t < kAggStages; ++t) {
+      if (t < cnt) issue(t);
+      cp_async_commit();
+    }
+    float w[kAggHB];
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh) {
+      const int h = h0 + hh;
+      w[hh] = 0.0f;
+      if (h >= H) continue;
+      const float ad = __ldg(attn_row + target * H + h);
+      const float ac = valid ? __ldg(attn_col + static_cast<int64_t>(other) * H + h) : 0.0f;
+      float m, ssum;
+      if (seg) {
+        m = emax[target * H + h];
+        ssum = esum[target * H + h];
+      } else {
+        m = group_max<32>(valid ? fmaxf(kNegInit, leaky_f(ad + ac, slope)) : kNegInit, kFullMask);
+        ssum = group_sum<32>(valid ? expf(leaky_f(ad + ac, slope) - m) : 0.0f, kFullMask);
+        if (blockIdx.y == 0 && lane == 0) {
+          emax[target * H + h] = m;
+          esum[target * H + h] = ssum;
+        }
+      }
+      if (valid) w[hh] = edge_weight(ad, ac, m, ssum, slope, p, seed, static_cast<uint64_t>(k) * H + h);
+    }
+    float acc[kAggHB][VPL][8];
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh)
+#pragma unroll
+      for (int q = 0; q < VPL; ++q)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[hh][q][j] = 0.0f;
+    for (int t = 0; t < cnt; ++t) {
+      cp_async_wait<kAggStages - 1>();
+      const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
+      float xf[VPL][8];
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const float4 raw = lds_f4(slot + q * 32 * 16);
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f2 = __bfloat1622float2(b[i]);
+          xf[q][2 * i] = f2.x;
+          xf[q][2 * i + 1] = f2.y;
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) {
+        const float wv = __shfl_sync(kFullMask, w[hh], t);
+#pragma unroll
+        for (int q = 0; q < VPL; ++q)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[hh][q][j] = fmaf(wv, xf[q][j], acc[hh][q][j]);
+      }
+      if (t + kAggStages < cnt) issue(t + kAggStages);
+      cp_async_commit();
+    }
+    cp_async_wait<0>();
+    float* dst = seg ? partial + item * HD : out + target * HD;
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh) {
+      if (h0 + hh >= H) break;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 8;
+        if (fi >= D) continue;
+        float* o = dst + static_cast<int64_t>(h0 + hh) * D + fi;
+        st_vec(o, make_float4(acc[hh][q][0], acc[hh][q][1], acc[hh][q][2], acc[hh][q][3]));
+        st_vec(o + 4, make_float4(acc[hh][q][4], acc[hh][q][5], acc[hh][q][6], acc[hh][q][7]));
+      }
+    }
+  }
+}
+
 // Backward K1 of the aggregate-first form (CSR rows): dots(e,h) =
 // U[i,h,:] . X[j,:] over D in 256-float chunks (the row's U chunk in
 // registers, the neighbour's X chunk loaded once for all heads), reduced
@@ -2601,6 +2738,44 @@ int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const 
   return launch_agg<2, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
                           attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
                           partial, nullptr, nullptr, nullptr, s);
+}
+
+int cign_gat_agg_fwd_bf16(const cign_gat_plan* pl, int32_t heads, int64_t dim,
+                          const float* attn_row, const float* attn_col, const void* x,
+                          float negative_slope, float attn_drop, uint64_t seed_value,
+                          const uint64_t* seed_ptr, float* z, float* edge_max, float* edge_sum,
+                          void* ws, size_t ws_bytes, cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
+  int rc = check_agg(pl, heads, dim, {x, z, ws}, "gat_agg_fwd_bf16");
+  if (rc) return rc;
+  CIGN_REQUIRE(dim % 8 == 0, CIGN_ERR_UNSUPPORTED, "gat_agg_fwd_bf16: D must be a multiple of 8");
+  CIGN_REQUIRE(attn_drop >= 0.0f && attn_drop < 1.0f, CIGN_ERR_INVALID_ARGUMENT,
+               "gat_agg_fwd_bf16: attn_drop must be in [0,1)");
+  CIGN_REQUIRE(attn_row && attn_col && edge_max && edge_sum, CIGN_ERR_NULL_POINTER,
+               "gat_agg_fwd_bf16: NULL tensor argument");
+  const AggLayout L = agg_layout(pl, heads, dim, dim);
+  CIGN_REQUIRE(ws_bytes >= L.total, CIGN_ERR_INVALID_ARGUMENT,
+               "gat_agg_fwd_bf16: workspace too small (%zu < %zu bytes)", ws_bytes, L.total);
+  if (pl->n == 0) return CIGN_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + L.partial);
+  rc = launch_hub_stats(pl, heads, attn_row, attn_col, negative_slope, edge_max, edge_sum, s);
+  if (rc) return rc;
+  const SegList& sl = pl->rows;
+  const int64_t seg_blocks = (sl.n_seg + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t grid = seg_blocks + (pl->n + kThreads / 32 - 1) / (kThreads / 32);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  // 256-feature tiles (512 bytes of bf16 per edge): the 4-head fp32
+  // accumulator of a 512-feature tile would need ~120 registers
+  constexpr int VPL = 1;
+  const size_t smem = static_cast<size_t>(kThreads / 32) * kAggStages * VPL * 32 * 16;
+  const dim3 g(static_cast<unsigned>(grid), static_cast<unsigned>((dim + 255) / 256));
+  gat_agg_fwd_bf16_kernel<VPL><<<g, kThreads, smem, s>>>(
+      static_cast<int>(pl->n), heads, dim, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
+      sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
+      edge_max, edge_sum, xb, negative_slope, attn_drop, seed, z, partial);
+  CIGN_CHECK_LAUNCH("gat_agg_fwd_bf16_kernel");
+  return launch_seg_combine(sl, heads, dim, partial, nullptr, z, nullptr, s);
 }
 
 int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_t channels,

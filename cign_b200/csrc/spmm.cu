@@ -23,6 +23,8 @@
 //   * The backward "+ g" of the hop chain is the SpMM epilogue (addend).
 //   * Reference: MultiHopCsrPlan (multihop_csr_ext/multihop_csr_pipeline_cuda.cu
 //     :113-322) drives three cuSPARSE SpMMs plus two add kernels per call.
+#include <cuda_bf16.h>
+
 #include <algorithm>
 #include <vector>
 
@@ -171,11 +173,12 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
 constexpr int kCombineThreads = 64;
 constexpr int kCombineWays = 4;
 
-template <int VEC>
+// OUT_BF16: Y is bf16 (VEC == 4), each sum rounded to nearest even.
+template <int VEC, bool OUT_BF16 = false>
 __global__ void __launch_bounds__(kCombineThreads * kCombineWays)
 spmm_combine_kernel(const int* __restrict__ heavy_row, const int* __restrict__ heavy_first,
                     const float* __restrict__ partial, int64_t F,
-                    const float* __restrict__ addend, float* __restrict__ Y) {
+                    const float* __restrict__ addend, void* __restrict__ Y) {
   using V = typename VecT<VEC>::type;
   __shared__ V part[kCombineWays - 1][kCombineThreads];
   const int h = blockIdx.x;
@@ -194,21 +197,181 @@ spmm_combine_kernel(const int* __restrict__ heavy_row, const int* __restrict__ h
   for (int w = 0; w < kCombineWays - 1; ++w) vadd(acc, part[w][tx]);
   const int64_t row = heavy_row[h];
   if (addend != nullptr) vadd(acc, ld_vec<VEC>(addend + row * F + f));
-  st_vec(Y + row * F + f, acc);
+  if constexpr (OUT_BF16) {
+    static_assert(VEC == 4, "bf16 combine stores 4 values per thread");
+    __nv_bfloat162* y = reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(Y) + row * F + f);
+    y[0] = __floats2bfloat162_rn(vel(acc, 0), vel(acc, 1));
+    y[1] = __floats2bfloat162_rn(vel(acc, 2), vel(acc, 3));
+  } else {
+    st_vec(static_cast<float*>(Y) + row * F + f, acc);
+  }
 }
 
-template <int VEC>
+template <int VEC, bool OUT_BF16 = false>
 int launch_spmm_combine(const SegList& sl, const float* partial, int64_t F, const float* addend,
-                        float* Y, cudaStream_t stream) {
+                        void* Y, cudaStream_t stream) {
   if (sl.n_heavy == 0) return CIGN_OK;
   const int64_t per_block = static_cast<int64_t>(kCombineThreads) * VEC;
   const int64_t chunks = (F / VEC * VEC + per_block - 1) / per_block;
   CIGN_REQUIRE(chunks < 65536, CIGN_ERR_UNSUPPORTED, "spmm: F too large for the hub combine");
   const dim3 grid(static_cast<unsigned>(sl.n_heavy), static_cast<unsigned>(chunks));
-  spmm_combine_kernel<VEC><<<grid, kCombineThreads * kCombineWays, 0, stream>>>(
+  spmm_combine_kernel<VEC, OUT_BF16><<<grid, kCombineThreads * kCombineWays, 0, stream>>>(
       sl.heavy_row(), sl.heavy_first(), partial, F, addend, Y);
   CIGN_CHECK_LAUNCH("spmm_combine_kernel");
   return CIGN_OK;
+}
+
+// ------------------------------------------------------ bf16 storage
+// The same row-split gather over bf16 feature rows (storage precision of
+// the large-graph configuration: bf16 features, fp32 accumulation).  Lane l
+// loads 16 bytes = 8 bf16 per vector, widens them to fp32 and accumulates
+// in fp32 in the same edge order as the fp32 kernel; the output row is
+// stored as fp32 or rounded (to nearest even) to bf16.  A warp owns one
+// row's tile of 32 * VPL * 8 features (1 KB of bf16 per edge at VPL = 2),
+// UNROLL edges' loads in flight.  Hub segments write fp32 partials that the
+// fp32 path's combine sums (in its order) and stores as fp32 or bf16.
+__device__ __forceinline__ void bf8_to_f32(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(b[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 f32_to_bf8(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* b = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) b[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+template <int VPL, bool OUT_BF16, int UNROLL>
+__global__ void __launch_bounds__(kThreads)
+spmm_rows_bf16_kernel(int rows, const int* __restrict__ crow, const int* __restrict__ col,
+                      const float* __restrict__ val, const int* __restrict__ seg_begin,
+                      const int* __restrict__ seg_end, int n_seg, int seg_blocks,
+                      const __nv_bfloat16* __restrict__ X, int64_t F, void* __restrict__ Y,
+                      float* __restrict__ partial) {
+  constexpr int kTile = 32 * VPL * 8;
+  const int lane = threadIdx.x & 31;
+  const int group = threadIdx.x >> 5;
+  const int64_t f0 = static_cast<int64_t>(blockIdx.y) * kTile;
+  int64_t item;
+  int e0, e1;
+  bool seg;
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    item = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + group;
+    if (item >= n_seg) return;
+    e0 = seg_begin[item];
+    e1 = seg_end[item];
+    seg = true;
+  } else {
+    item = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
+    if (item >= rows) return;
+    e0 = crow[item];
+    e1 = crow[item + 1];
+    if (e1 - e0 > kSegLen) return;  // a hub row: done by segments + combine
+    seg = false;
+  }
+  float acc[VPL][8];
+#pragma unroll
+  for (int q = 0; q < VPL; ++q)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[q][j] = 0.0f;
+  for (int base = e0; base < e1; base += 32) {
+    const int my = base + lane;
+    int c = 0;
+    float v = 0.0f;
+    if (my < e1) {
+      c = __ldg(col + my);
+      v = __ldg(val + my);
+    }
+    const int cnt = min(32, e1 - base);
+    for (int t = 0; t < cnt; t += UNROLL) {
+      uint4 xv[UNROLL][VPL];
+      float vv[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const bool on = t + u < cnt;
+        // (t, u and cnt are warp-uniform: every lane takes the same branch)
+        const int cc = __shfl_sync(kFullMask, c, on ? t + u : 0);
+        const float vu = __shfl_sync(kFullMask, v, on ? t + u : 0);
+        vv[u] = on ? vu : 0.0f;
+        const __nv_bfloat16* xr = X + static_cast<int64_t>(cc) * F;
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) {
+          const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 8;
+          xv[u][q] = (on && fi < F) ? __ldg(reinterpret_cast<const uint4*>(xr + fi))
+                                    : make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        if (t + u >= cnt) break;
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) {
+          float xf[8];
+          bf8_to_f32(xv[u][q], xf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[q][j] = fmaf(vv[u], xf[j], acc[q][j]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < VPL; ++q) {
+    const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 8;
+    if (fi >= F) continue;
+    if (seg) {
+      float* pr = partial + item * F + fi;
+      st_vec(pr, make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]));
+      st_vec(pr + 4, make_float4(acc[q][4], acc[q][5], acc[q][6], acc[q][7]));
+    } else if (OUT_BF16) {
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(Y) + item * F + fi) =
+          f32_to_bf8(acc[q]);
+    } else {
+      float* yr = static_cast<float*>(Y) + item * F + fi;
+      st_vec(yr, make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]));
+      st_vec(yr + 4, make_float4(acc[q][4], acc[q][5], acc[q][6], acc[q][7]));
+    }
+  }
+}
+
+template <int VPL, bool OUT_BF16, int UNROLL = 4>
+int launch_spmm_bf16_cfg(const cign_csr_f32& m, const SegList& sl, const __nv_bfloat16* X,
+                         int64_t F, void* Y, float* partial, cudaStream_t stream) {
+  constexpr int kTile = 32 * VPL * 8;
+  const int64_t seg_blocks = (sl.n_seg + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t grid = seg_blocks + (m.rows + kThreads / 32 - 1) / (kThreads / 32);
+  if (grid == 0) return CIGN_OK;
+  const int64_t tiles = (F + kTile - 1) / kTile;
+  CIGN_REQUIRE(grid < (1ll << 31) && tiles <= 65535, CIGN_ERR_UNSUPPORTED,
+               "spmm_bf16: grid too large");
+  spmm_rows_bf16_kernel<VPL, OUT_BF16, UNROLL>
+      <<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(tiles)), kThreads, 0, stream>>>(
+          static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
+          static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, Y, partial);
+  CIGN_CHECK_LAUNCH("spmm_rows_bf16_kernel");
+  // hub rows: the fp32 path's combine (same segment sums, same order)
+  return launch_spmm_combine<4, OUT_BF16>(sl, partial, F, nullptr, Y, stream);
+}
+
+int run_spmm_bf16(const cign_spmm_plan* plan, int transpose, const __nv_bfloat16* X, int64_t F,
+                  void* Y, bool y_bf16, float* partial, cudaStream_t s) {
+  const bool use_t = transpose != 0 && !plan->pt_is_p;
+  const cign_csr_f32& m = use_t ? plan->pt : plan->p;
+  const SegList& sl = use_t ? plan->seg_pt : plan->seg_p;
+  if (F <= 256) {
+    return y_bf16 ? launch_spmm_bf16_cfg<1, true>(m, sl, X, F, Y, partial, s)
+                  : launch_spmm_bf16_cfg<1, false>(m, sl, X, F, Y, partial, s);
+  }
+  // 512-feature tiles (1 KB per edge), two edges' loads in flight (48
+  // registers): measured faster than four in flight (80 registers), 256- and
+  // 1024-feature tiles on the cfg2 graph and on a cfg5 row block
+  return y_bf16 ? launch_spmm_bf16_cfg<2, true, 2>(m, sl, X, F, Y, partial, s)
+                : launch_spmm_bf16_cfg<2, false, 2>(m, sl, X, F, Y, partial, s);
 }
 
 // Plan-time validation of a CSR: crow monotone with crow[0]=0, crow[rows]=nnz,
@@ -428,6 +591,41 @@ int cign_spmm(const cign_spmm_plan* plan, int transpose, const float* X, int64_t
                "spmm: workspace too small (%zu < %zu bytes)", ws_bytes, need);
   return run_spmm(plan, transpose, X, F, addend, Y, static_cast<float*>(ws),
                   static_cast<cudaStream_t>(stream));
+}
+
+int cign_spmm_bf16(const cign_spmm_plan* plan, int transpose, const void* X, int64_t F, void* Y,
+                   int y_bf16, void* ws, size_t ws_bytes, cign_stream_t stream) {
+  int rc = check_dense(plan, static_cast<const float*>(X), F, Y, "spmm_bf16", false);
+  if (rc) return rc;
+  CIGN_REQUIRE(!(transpose && plan->pt_is_p && plan->p.rows != plan->p.cols),
+               CIGN_ERR_INVALID_ARGUMENT,
+               "spmm_bf16: a rectangular P needs its transpose at plan creation");
+  CIGN_REQUIRE(F % 8 == 0, CIGN_ERR_UNSUPPORTED, "spmm_bf16: F must be a multiple of 8");
+  CIGN_REQUIRE(aligned16(X) && aligned16(Y) && aligned16(ws), CIGN_ERR_ALIGNMENT,
+               "spmm_bf16: X, Y and ws must be 16-byte aligned");
+  CIGN_REQUIRE(X != Y || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
+               "spmm_bf16: Y must not alias X");
+  const size_t need = partial_bytes(plan, F);
+  CIGN_REQUIRE(ws_bytes >= need && (need == 0 || ws != nullptr), CIGN_ERR_INVALID_ARGUMENT,
+               "spmm_bf16: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  return run_spmm_bf16(plan, transpose, static_cast<const __nv_bfloat16*>(X), F, Y, y_bf16 != 0,
+                       static_cast<float*>(ws), static_cast<cudaStream_t>(stream));
+}
+
+int cign_multihop_fwd_bf16(const cign_spmm_plan* plan, int max_power, const void* X, int64_t F,
+                           void* const* Y, void* ws, size_t ws_bytes, cign_stream_t stream) {
+  CIGN_REQUIRE(max_power >= 1, CIGN_ERR_INVALID_ARGUMENT,
+               "multihop_fwd_bf16: max_power must be >= 1");
+  CIGN_REQUIRE(Y != nullptr, CIGN_ERR_NULL_POINTER, "multihop_fwd_bf16: Y is NULL");
+  const void* src = X;
+  for (int p = 0; p < max_power; ++p) {
+    CIGN_REQUIRE(Y[p] != src || plan == nullptr || plan->p.rows == 0, CIGN_ERR_INVALID_ARGUMENT,
+                 "multihop_fwd_bf16: Y[%d] aliases its input", p);
+    const int rc = cign_spmm_bf16(plan, 0, src, F, Y[p], 1, ws, ws_bytes, stream);
+    if (rc) return rc;
+    src = Y[p];
+  }
+  return CIGN_OK;
 }
 
 size_t cign_multihop_workspace_bytes(const cign_spmm_plan* plan, int max_power, int64_t F) {

@@ -164,6 +164,47 @@ class SpmmPlan:
         _lib.check(rc, "cign_multihop_fwd")
         return ys
 
+    def spmm_bf16(self, x: torch.Tensor, out_dtype=torch.bfloat16,
+                  transpose: bool = False) -> torch.Tensor:
+        """P x (or P^T x) for bf16-stored features: fp32 accumulation, output
+        fp32 or rounded to bf16 (cign_spmm_bf16); F % 8 == 0."""
+        if x.dtype != torch.bfloat16:
+            raise TypeError("spmm_bf16 needs a bfloat16 x")
+        if out_dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError("out_dtype must be bfloat16 or float32")
+        rows_in = self.rows if transpose else self.cols
+        if x.device != self.device or x.dim() != 2 or x.size(0) != rows_in:
+            raise ValueError(f"spmm_bf16: expected [{rows_in}, F] on {self.device}")
+        x = x.contiguous()
+        F = int(x.size(1))
+        y = torch.empty((self.cols if transpose else self.rows, F), dtype=out_dtype,
+                        device=x.device)
+        ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, F), self.device)
+        with _lib.DeviceGuard(self.device):
+            rc = self.lib.cign_spmm_bf16(self.handle, 1 if transpose else 0, _lib.ptr(x), F,
+                                         _lib.ptr(y), 1 if out_dtype == torch.bfloat16 else 0,
+                                         _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+        _lib.check(rc, "cign_spmm_bf16")
+        return y
+
+    def forward_bf16(self, x: torch.Tensor, max_power: int) -> List[torch.Tensor]:
+        """[P^1 x, ..., P^max_power x] with every hop stored as bf16 (fp32
+        accumulation inside each hop; cign_multihop_fwd_bf16)."""
+        if x.dtype != torch.bfloat16:
+            raise TypeError("forward_bf16 needs a bfloat16 x")
+        if x.device != self.device or x.dim() != 2 or x.size(0) != self.rows:
+            raise ValueError(f"forward_bf16: expected [{self.rows}, F] on {self.device}")
+        x = x.contiguous()
+        ys = [torch.empty_like(x) for _ in range(int(max_power))]
+        F = int(x.size(1))
+        ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, F), self.device)
+        with _lib.DeviceGuard(self.device):
+            rc = self.lib.cign_multihop_fwd_bf16(self.handle, int(max_power), _lib.ptr(x), F,
+                                                 _lib.ptr_array(ys), _lib.ptr(ws), ws.numel(),
+                                                 _lib.stream_of(x))
+        _lib.check(rc, "cign_multihop_fwd_bf16")
+        return ys
+
     def backward(self, grads: Sequence[Optional[torch.Tensor]], F: int) -> torch.Tensor:
         """grads[p-1] = dL/d(P^p x) or None; returns dL/dx."""
         ref = next((g for g in grads if g is not None), None)

@@ -175,6 +175,11 @@ CONFIGS = {
                            4, 2, 0.5, 0.5, seed=42),
     "cfg4": WorkloadConfig("cfg4_rmat2450000", 2450000, 61900000, "rmat", 100, 47, 512, (1, 2), 4, 1,
                            0.5, 0.5, seed=7),
+    # the stress configuration: 10M-node RMAT, average degree 32, features
+    # [N, 128] stored as bf16, D = 512 (32 channels x 16 blades), K = 3,
+    # 8 heads; one block (its depth is not specified), 47 classes as cfg4
+    "cfg5": WorkloadConfig("cfg5_rmat10000000", 10_000_000, 320_000_000, "rmat", 128, 47, 512,
+                           (1, 2, 3), 8, 1, 0.5, 0.5, seed=11),
 }
 
 

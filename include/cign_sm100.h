@@ -145,6 +145,19 @@ CIGN_API int cign_multihop_bwd(const cign_spmm_plan* plan, int max_power,
                       const float* const* G, int64_t F, float* GX, void* ws,
                       size_t ws_bytes, cign_stream_t stream);
 
+/* bf16 feature storage (the large-graph configuration stores node features
+ * as bf16 with fp32 accumulation; the reference's sparse path is fp32 only,
+ * multihop_csr_pipeline_cuda.cu:63).  X is bf16 [rows, F] (F % 8 == 0, 16-byte
+ * aligned); products accumulate in fp32 in the edge order of cign_spmm, so a
+ * float32 Y (y_bf16 == 0) equals cign_spmm on the widened X; with y_bf16 != 0
+ * Y is bf16, rounded to nearest even.  Workspace: cign_spmm_workspace_bytes. */
+CIGN_API int cign_spmm_bf16(const cign_spmm_plan* plan, int transpose, const void* X, int64_t F,
+                   void* Y, int y_bf16, void* ws, size_t ws_bytes, cign_stream_t stream);
+/* Y[p-1] = P^p X for p = 1..max_power, every hop stored as bf16. */
+CIGN_API int cign_multihop_fwd_bf16(const cign_spmm_plan* plan, int max_power, const void* X,
+                           int64_t F, void* const* Y, void* ws, size_t ws_bytes,
+                           cign_stream_t stream);
+
 /* ------------------------------------------------------------------ GAT
  * Collapsed multi-head GAT (concat=False) over a fixed graph.
  *
@@ -245,6 +258,15 @@ CIGN_API int cign_gat_agg_fwd(const cign_gat_plan* plan, int32_t heads, int64_t 
                               const uint64_t* seed_ptr, float* z,
                               float* edge_max, float* edge_sum, void* ws, size_t ws_bytes,
                               cign_stream_t stream);
+/* cign_gat_agg_fwd over a bf16 layer input x [n_cols, dim] (dim % 8 == 0):
+ * z [n, H, dim] fp32, equal to cign_gat_agg_fwd on the widened x (same
+ * weights, edge order and fp32 FMA order); workspace as cign_gat_agg_fwd. */
+CIGN_API int cign_gat_agg_fwd_bf16(const cign_gat_plan* plan, int32_t heads, int64_t dim,
+                          const float* attn_row, const float* attn_col, const void* x,
+                          float negative_slope, float attn_drop, uint64_t seed_value,
+                          const uint64_t* seed_ptr, float* z, float* edge_max, float* edge_sum,
+                          void* ws, size_t ws_bytes, cign_stream_t stream);
+
 CIGN_API int cign_gat_agg_bwd(const cign_gat_plan* plan, int32_t heads, int64_t dim,
                               int64_t channels, const float* attn_row, const float* attn_col,
                               const float* x, const float* edge_max, const float* edge_sum,
