@@ -1976,6 +1976,8 @@ BwdLayout bwd_layout(const cign_gat_plan* pl, int H, int64_t C) {
 // 128*VPL floats run over the grid's second dimension.
 
 constexpr int kAggHB = 4;      // heads per pass over a work item's edges
+constexpr int kDotsSlots = 8;  // edges in the backward-K1 ring (two 4-edge groups)
+constexpr size_t kDotsSmem = static_cast<size_t>(kThreads / 32) * kDotsSlots * 2 * 32 * 16;
 constexpr int kAggStages = 4;  // neighbour rows in flight per warp (cp.async ring)
 
 template <int VPL>
@@ -2282,7 +2284,7 @@ gat_agg_fwd_bf16_kernel(int n, int H, int64_t D, const int* __restrict__ ptr,
 // across the warp; the lane owning edge e keeps its dots.  Light rows then
 // run the softmax/dropout/LeakyReLU backward in registers and write glog and
 // grad_attn_row; hub segments write their dots to glog for the hub-row kernel.
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)  // <= 80 registers: 3 CTAs (64 KB ring each) / SM
 gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
                     const int* __restrict__ col, const int* __restrict__ seg_row,
                     const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
@@ -2291,10 +2293,16 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
                     const float* __restrict__ esum, const float* __restrict__ U,
                     const float* __restrict__ X, float slope, float p, Seed seed_in,
                     float* __restrict__ glog, float* __restrict__ grad_attn_row) {
+  extern __shared__ float4 dots_ring[];
   const uint64_t seed = seed_in;
   constexpr int kChunk = 256;  // floats of D per pass: 2 float4 per lane
   const int lane = threadIdx.x & 31;
   const int group = threadIdx.x >> 5;
+  // lane-private ring of kDotsSlots edges x 2 float4 (this lane's slices of
+  // the neighbour's 256-float chunk), filled by cp.async two 4-edge groups
+  // ahead; shared address of slot t, vector q: my_ring + (t * 2 + q) * 512
+  const uint32_t my_ring =
+      smem_u32(dots_ring) + static_cast<uint32_t>((group * kDotsSlots * 2 * 32 + lane) * 16);
   int64_t row;
   int e0, e1;
   bool seg;
@@ -2333,38 +2341,56 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
                          ? ld_vec<4>(U + row * HD + static_cast<int64_t>(h0 + hh) * D + fi)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-      // 4 edges per pass: their X loads are in flight together, and the 16
-      // (edge, head) partial dots are reduced across the warp by a transposed
-      // butterfly (each level halves the values a lane carries), leaving the
-      // total of value m = 4*edge + head on lanes 2m and 2m+1.
-      for (int t0 = 0; t0 < cnt; t0 += 4) {
-        float4 x[4][2];
+      // 4 edges per pass (their neighbour chunks copied two passes ahead),
+      // and the 16 (edge, head) partial dots are reduced across the warp by a
+      // transposed butterfly (each level halves the values a lane carries),
+      // leaving the total of value m = 4*edge + head on lanes 2m and 2m+1.
+      auto issue = [&](int t0i) {  // copies of the 4-edge group starting at t0i
 #pragma unroll
         for (int e4 = 0; e4 < 4; ++e4) {
-          const int t = t0 + e4;
+          const int t = t0i + e4;
           const int ct = __shfl_sync(kFullMask, c, t < 32 ? t : 31);
+          if (t >= cnt) continue;
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
-            x[e4][q] = (t < cnt && fi < D) ? ldg_vec<4>(X + static_cast<int64_t>(ct) * D + fi)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (fi < D)
+              cp_async16_s(my_ring + static_cast<uint32_t>(((t % kDotsSlots) * 2 + q) * 512),
+                           X + static_cast<int64_t>(ct) * D + fi);
           }
         }
+        cp_async_commit();
+      };
+      issue(0);
+      issue(4);
+      for (int t0 = 0; t0 < cnt; t0 += 4) {
+        cp_async_wait<1>();  // this group's copies have landed (the next may be in flight)
         float v[16];
 #pragma unroll
-        for (int e4 = 0; e4 < 4; ++e4)
+        for (int e4 = 0; e4 < 4; ++e4) {  // one edge's slices in registers at a time
+          const int t = t0 + e4;
+          float4 x[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+            const float4 xv =
+                lds_f4(my_ring + static_cast<uint32_t>(((t % kDotsSlots) * 2 + q) * 512));
+            x[q] = (t < cnt && fi < D) ? xv : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
 #pragma unroll
           for (int hh = 0; hh < kAggHB; ++hh) {
             float d = 0.0f;
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-              d = fmaf(u[hh][q].x, x[e4][q].x, d);
-              d = fmaf(u[hh][q].y, x[e4][q].y, d);
-              d = fmaf(u[hh][q].z, x[e4][q].z, d);
-              d = fmaf(u[hh][q].w, x[e4][q].w, d);
+              d = fmaf(u[hh][q].x, x[q].x, d);
+              d = fmaf(u[hh][q].y, x[q].y, d);
+              d = fmaf(u[hh][q].z, x[q].z, d);
+              d = fmaf(u[hh][q].w, x[q].w, d);
             }
             v[e4 * 4 + hh] = d;
           }
+        }
+        issue(t0 + 8);  // into the slots just read
 #pragma unroll
         for (int level = 0; level < 4; ++level) {
           const int half = 8 >> level;                 // values kept after this level
@@ -2388,6 +2414,7 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
           if (owner) mine[hh] += d;
         }
       }
+      cp_async_wait<0>();  // the ring is reused by the next chunk
     }
 #pragma unroll
     for (int hh = 0; hh < kAggHB; ++hh) {
@@ -2807,7 +2834,21 @@ int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_
   const int64_t seg_blocks = (rs.n_seg + kThreads / 32 - 1) / (kThreads / 32);
   const int64_t grid = seg_blocks + (pl->n + kThreads / 32 - 1) / (kThreads / 32);
   CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "gat_agg_bwd: grid too large");
-  gat_agg_dots_kernel<<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+  {  // 64 KB of dynamic shared memory: opt in once per device
+    static std::mutex mu;
+    static bool set[64] = {false};
+    int dev = 0;
+    CIGN_CHECK_CUDA(cudaGetDevice(&dev), "gat_agg_bwd: cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !set[dev]) {
+      CIGN_CHECK_CUDA(cudaFuncSetAttribute(gat_agg_dots_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kDotsSmem)),
+                      "gat_agg_bwd: shared-memory opt-in");
+      if (dev >= 0 && dev < 64) set[dev] = true;
+    }
+  }
+  gat_agg_dots_kernel<<<static_cast<unsigned>(grid), kThreads, kDotsSmem, s>>>(
       static_cast<int>(pl->n), heads, dim, pl->rowptr, pl->col, rs.seg_row(), rs.seg_begin(),
       rs.seg_end(), static_cast<int>(rs.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
       edge_max, edge_sum, grad_z, x, negative_slope, attn_drop, seed, glog, grad_attn_row);
