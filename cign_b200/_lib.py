@@ -129,6 +129,8 @@ SIGNATURES = {
     "cign_pack_proj_gemm_tf32": (c_int, [c_int64, c_int64, c_int32, c_int64, _P, _P, _PP, c_int64,
                                          _P, _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_pack_proj_status": (c_int, [_P, c_int64, c_int32, c_int64, _P]),
+    "cign_gate_pack_fwd": (c_int, [c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                   _P, _P, _PP, c_int64, _P, _P, _P, _P, _P]),
     "cign_pack_bwd": (c_int, [c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, _P, _P, _P,
                               _PP, c_int64, _P, _P, _P, _PP, c_int64, c_int32, _P, _P]),
     "cign_dropout_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, c_float, c_float, c_uint64, _P,

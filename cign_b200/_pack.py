@@ -32,6 +32,34 @@ def pack_forward(H, C, props: Sequence[torch.Tensor], alpha: Optional[torch.Tens
     return out
 
 
+def gate_pack_supported(H, C, props: Sequence[torch.Tensor]) -> bool:
+    """Whether cign_gate_pack_fwd (hop gate inside the pack forward) takes
+    these operands: D % 4 == 0, D <= 1024, 1 <= K <= 8, 16-byte aligned."""
+    D, K = int(H.size(1)), len(props)
+    return (D % 4 == 0 and D <= 1024 and 1 <= K <= 8
+            and all(t.data_ptr() % 16 == 0 for t in (H, C, *props)))
+
+
+def gate_pack_forward(H, C, props: Sequence[torch.Tensor], gate_w, gate_b, gate_mode: int,
+                      interaction: int, outer: int, weighting: int):
+    """(G, alpha): the hop gate's alpha [N, K] and the pack that uses it, in
+    one pass over H and C (cign_gate_pack_fwd)."""
+    lib = _lib.load_library()
+    n, D = (int(s) for s in H.shape)
+    K = len(props)
+    out_cols = 2 * K * D if weighting == 0 else 2 * D
+    out = torch.empty((n, out_cols), dtype=torch.float32, device=H.device)
+    alpha = torch.empty((n, K), dtype=torch.float32, device=H.device)
+    with _lib.DeviceGuard(H.device):
+        rc = lib.cign_gate_pack_fwd(n, D, K, int(gate_mode), int(interaction), int(outer),
+                                    int(weighting), _lib.ptr(H), _lib.ptr(C),
+                                    _lib.ptr_array(props), 2 * D, _lib.ptr(gate_w.contiguous()),
+                                    _lib.ptr(gate_b.contiguous()), _lib.ptr(alpha),
+                                    _lib.ptr(out), _lib.stream_of(H))
+    _lib.check(rc, "cign_gate_pack_fwd")
+    return out, alpha
+
+
 def pack_proj_supported(D: int, K: int, dout: int) -> bool:
     """Shapes the tcgen05 pack + proj GEMM (cign_pack_proj_gemm_tf32) takes."""
     return D % 32 == 0 and 1 <= K <= 8 and dout % 32 == 0 and 32 <= dout <= 512

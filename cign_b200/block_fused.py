@@ -4,6 +4,8 @@
     T^p    = P^p HC,  p in order_set                 (k-hop propagation)
     alpha  = softmax(hop_gate([H+C, |H-C|]))         (hop gate)
     G_raw  = Clifford pack(H_norm, C_norm, T, alpha)
+(the hop gate and the pack run as one kernel in the forward,
+cign_gate_pack_fwd)
 
 (generic_engine/model_cign.py:781-925, production switches: interaction
 "new", outer nonlinearity "none", alpha weighting "old").  Run op by op,
@@ -55,8 +57,7 @@ class _PropagateGatePackFn(torch.autograd.Function):
         C = C.contiguous()
         D = H.size(1)
         props = _propagate(H, C, plan, order_set)
-        alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
-        G = _pack.pack_forward(H, C, props, alpha, *PACK_MODES)
+        G, alpha = _gate_pack(H, C, props, gate_w, gate_b, gate_mode)
         ctx.save_for_backward(H, C, gate_w, alpha, *props)
         ctx.plan, ctx.order_set, ctx.gate_mode, ctx.D = plan, tuple(order_set), gate_mode, D
         return G
@@ -66,6 +67,15 @@ class _PropagateGatePackFn(torch.autograd.Function):
         H, C, gate_w, alpha, *props = ctx.saved_tensors
         gH, gC, gw, gb = _gate_pack_backward(ctx, gG, H, C, gate_w, alpha, props)
         return gH, gC, gw, gb, None, None, None
+
+
+def _gate_pack(H, C, props, gate_w, gate_b, gate_mode):
+    """(G, alpha): hop gate and pack in one pass over H and C where the shape
+    allows, else the two kernels."""
+    if _pack.gate_pack_supported(H, C, props):
+        return _pack.gate_pack_forward(H, C, props, gate_w, gate_b, gate_mode, *PACK_MODES)
+    alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
+    return _pack.pack_forward(H, C, props, alpha, *PACK_MODES), alpha
 
 
 def _propagate(H, C, plan, order_set):
@@ -109,14 +119,14 @@ class _PropagateGatePackProjFn(torch.autograd.Function):
         H = H.contiguous()
         C = C.contiguous()
         props = _propagate(H, C, plan, order_set)
-        alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
         D, K = H.size(1), len(props)
         fused = (not keep_g) if USE_TCGEN05_PACK_PROJ is None else USE_TCGEN05_PACK_PROJ
         if (fused and torch.backends.cuda.matmul.allow_tf32
                 and _pack.pack_proj_supported(D, K, proj_w.size(0))):
+            alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
             out, G = _pack.pack_proj_forward(H, C, props, alpha, proj_w, proj_b, keep_g)
         else:
-            G = _pack.pack_forward(H, C, props, alpha, *PACK_MODES)
+            G, alpha = _gate_pack(H, C, props, gate_w, gate_b, gate_mode)
             out = torch.addmm(proj_b, G, proj_w.t())
             if not keep_g:
                 G = None

@@ -108,6 +108,150 @@ pack_fwd_kernel(int64_t n, int64_t D, int K, int interaction, int outer, int wei
   }
 }
 
+// The block's hop gate evaluated inside the pack forward
+// (generic_engine/model_cign.py:721-749 feeding :817-925):
+//   alpha = softmax_k([H + C | |H - C|] @ W^T + b)   (score mode "new"; [H | C] for "old")
+// then the pack with that alpha; alpha [N, K] is also written for the
+// backward.  One warp per node row holds the row's H / C slices (float4,
+// lane l owns columns 4l + 128q) for both steps, so H and C are read once.
+// The gate dots run in the order of hop_gate_fwd_kernel (columns
+// increasing, x/y/z/w, the sum half before the difference half, then one
+// warp sum) and the pack in the order of pack_fwd_kernel: alpha and the
+// packed output equal those kernels' bit for bit.
+template <int K, int VPL>
+__global__ void __launch_bounds__(kThreads)
+gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int outer,
+                     int weighting, const float* __restrict__ Hn, const float* __restrict__ Cn,
+                     CPtrs P, int64_t ldp, const float* __restrict__ W,
+                     const float* __restrict__ b, float* __restrict__ alpha_out,
+                     float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (row >= n) return;
+  const int64_t D2 = 2 * D;
+  float4 h[VPL], c[VPL];
+  float dot[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) dot[k] = 0.0f;
+#pragma unroll
+  for (int q = 0; q < VPL; ++q) {
+    const int64_t d = static_cast<int64_t>(lane + q * 32) * 4;
+    if (d < D) {
+      h[q] = ld_vec<4>(Hn + row * D + d);
+      c[q] = ld_vec<4>(Cn + row * D + d);
+      float4 g0, g1;
+      if (gate_mode == 1) {
+        g0 = make_float4(h[q].x + c[q].x, h[q].y + c[q].y, h[q].z + c[q].z, h[q].w + c[q].w);
+        g1 = make_float4(fabsf(h[q].x - c[q].x), fabsf(h[q].y - c[q].y), fabsf(h[q].z - c[q].z),
+                         fabsf(h[q].w - c[q].w));
+      } else {
+        g0 = h[q];
+        g1 = c[q];
+      }
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const float4 w0 = ldg_vec<4>(W + k * D2 + d);
+        const float4 w1 = ldg_vec<4>(W + k * D2 + D + d);
+        float t = dot[k];
+        t = fmaf(g0.x, w0.x, t); t = fmaf(g0.y, w0.y, t); t = fmaf(g0.z, w0.z, t); t = fmaf(g0.w, w0.w, t);
+        t = fmaf(g1.x, w1.x, t); t = fmaf(g1.y, w1.y, t); t = fmaf(g1.z, w1.z, t); t = fmaf(g1.w, w1.w, t);
+        dot[k] = t;
+      }
+    } else {
+      vzero(h[q]);
+      vzero(c[q]);
+    }
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    dot[k] = warp_sum(dot[k]) + __ldg(b + k);
+    m = fmaxf(m, dot[k]);
+  }
+  float ssum = 0.0f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    dot[k] = expf(dot[k] - m);
+    ssum += dot[k];
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    dot[k] = dot[k] / ssum;  // alpha_k, on every lane
+    if (lane == k) alpha_out[row * K + k] = dot[k];
+  }
+  const int64_t ow = weighting == 0 ? 2 * D * K : 2 * D;
+  float4 accD[VPL], accW[VPL];
+#pragma unroll
+  for (int q = 0; q < VPL; ++q) {
+    vzero(accD[q]);
+    vzero(accW[q]);
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float a = dot[k];
+    const float* pk = P.p[k] + row * ldp;
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t d = static_cast<int64_t>(lane + q * 32) * 4;
+      if (d >= D) continue;
+      const float4 th = ldg_vec<4>(pk + d);
+      const float4 tc = ldg_vec<4>(pk + D + d);
+      float4 ow_, od_;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float Dv, Wv;
+        interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer, Dv,
+                     Wv);
+        vel(ow_, j) = a * Wv;
+        vel(od_, j) = a * Dv;
+      }
+      if (weighting == 0) {
+        float* o = out + row * ow + static_cast<int64_t>(k) * 2 * D + d;
+        st_vec(o, ow_);
+        st_vec(o + D, od_);
+      } else {
+        vadd(accD[q], od_);
+        vadd(accW[q], ow_);
+      }
+    }
+  }
+  if (weighting == 1) {
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int64_t d = static_cast<int64_t>(lane + q * 32) * 4;
+      if (d < D) {
+        st_vec(out + row * ow + d, accD[q]);
+        st_vec(out + row * ow + D + d, accW[q]);
+      }
+    }
+  }
+}
+
+template <int K, int VPL>
+int launch_gate_pack(int64_t n, int64_t D, int gate_mode, int interaction, int outer,
+                     int weighting, const float* H, const float* C, const CPtrs& pl, int64_t ldp,
+                     const float* W, const float* b, float* alpha, float* out, cudaStream_t s) {
+  const int64_t grid = (n + kThreads / 32 - 1) / (kThreads / 32);
+  gate_pack_fwd_kernel<K, VPL><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      n, D, gate_mode, interaction, outer, weighting, H, C, pl, ldp, W, b, alpha, out);
+  CIGN_CHECK_LAUNCH("gate_pack_fwd_kernel");
+  return CIGN_OK;
+}
+
+template <int K>
+int launch_gate_pack_k(int64_t n, int64_t D, int gate_mode, int interaction, int outer,
+                       int weighting, const float* H, const float* C, const CPtrs& pl,
+                       int64_t ldp, const float* W, const float* b, float* alpha, float* out,
+                       cudaStream_t s) {
+  if (D <= 128)
+    return launch_gate_pack<K, 1>(n, D, gate_mode, interaction, outer, weighting, H, C, pl, ldp, W, b, alpha, out, s);
+  if (D <= 256)
+    return launch_gate_pack<K, 2>(n, D, gate_mode, interaction, outer, weighting, H, C, pl, ldp, W, b, alpha, out, s);
+  if (D <= 512)
+    return launch_gate_pack<K, 4>(n, D, gate_mode, interaction, outer, weighting, H, C, pl, ldp, W, b, alpha, out, s);
+  return launch_gate_pack<K, 8>(n, D, gate_mode, interaction, outer, weighting, H, C, pl, ldp, W, b, alpha, out, s);
+}
+
 template <int VEC, int VPL, int LPR>
 __global__ void __launch_bounds__(kThreads)
 pack_bwd_kernel(int64_t n, int64_t D, int K, int interaction, int outer, int weighting,
@@ -294,6 +438,40 @@ int cign_pack_fwd(int64_t n, int64_t d, int32_t k, int32_t interaction, int32_t 
     CIGN_PACK_DISPATCH(4, d / 4, return (launch_fwd<V_, P_, L_>(n, d, k, interaction, outer, weighting, H, C, pl, ldp, alpha, out, s)));
   }
   CIGN_PACK_DISPATCH(1, d, return (launch_fwd<V_, P_, L_>(n, d, k, interaction, outer, weighting, H, C, pl, ldp, alpha, out, s)));
+  return CIGN_OK;
+}
+
+int cign_gate_pack_fwd(int64_t n, int64_t d, int32_t k, int32_t gate_mode,
+                       int32_t interaction, int32_t outer, int32_t weighting, const float* H,
+                       const float* C, const float* const* P, int64_t ldp, const float* gate_w,
+                       const float* gate_b, float* alpha, float* out, cign_stream_t stream) {
+  int rc = check_modes(n, d, k, interaction, outer, weighting, "gate_pack_fwd");
+  if (rc) return rc;
+  CIGN_REQUIRE(k >= 1 && k <= 8 && (gate_mode == 0 || gate_mode == 1), CIGN_ERR_UNSUPPORTED,
+               "gate_pack_fwd: needs 1 <= K <= 8 and gate mode 0 or 1");
+  CIGN_REQUIRE(d % 4 == 0 && d <= 1024 && ldp % 4 == 0, CIGN_ERR_UNSUPPORTED,
+               "gate_pack_fwd: needs D %% 4 == 0, D <= 1024 and ldp %% 4 == 0");
+  if (n == 0) return CIGN_OK;
+  CIGN_REQUIRE(H && C && P && gate_w && gate_b && alpha && out, CIGN_ERR_NULL_POINTER,
+               "gate_pack_fwd: NULL argument");
+  CIGN_REQUIRE(ldp >= 2 * d, CIGN_ERR_INVALID_ARGUMENT, "gate_pack_fwd: ldp < 2D");
+  CIGN_REQUIRE(aligned16(H) && aligned16(C) && aligned16(out) && aligned16(gate_w),
+               CIGN_ERR_ALIGNMENT, "gate_pack_fwd: H, C, out and gate_w must be 16-byte aligned");
+  CPtrs pl{};
+  for (int i = 0; i < k; ++i) {
+    CIGN_REQUIRE(P[i] != nullptr, CIGN_ERR_NULL_POINTER, "gate_pack_fwd: P[%d] is NULL", i);
+    CIGN_REQUIRE(aligned16(P[i]), CIGN_ERR_ALIGNMENT, "gate_pack_fwd: P[%d] not 16-byte aligned",
+                 i);
+    pl.p[i] = P[i];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (k) {
+#define CIGN_GATE_PACK_K(KK) \
+    case KK: return launch_gate_pack_k<KK>(n, d, gate_mode, interaction, outer, weighting, H, C, pl, ldp, gate_w, gate_b, alpha, out, s);
+    CIGN_GATE_PACK_K(1) CIGN_GATE_PACK_K(2) CIGN_GATE_PACK_K(3) CIGN_GATE_PACK_K(4)
+    CIGN_GATE_PACK_K(5) CIGN_GATE_PACK_K(6) CIGN_GATE_PACK_K(7) CIGN_GATE_PACK_K(8)
+#undef CIGN_GATE_PACK_K
+  }
   return CIGN_OK;
 }
 

@@ -333,6 +333,19 @@ CIGN_API int cign_pack_fwd(int64_t n, int64_t d, int32_t k, int32_t interaction,
                   const float* C, const float* const* P, int64_t ldp,
                   const float* alpha, float* out, cign_stream_t stream);
 
+/* The block's hop gate evaluated inside the pack forward
+ * (generic_engine/model_cign.py:721-749 followed by :817-925): alpha =
+ * softmax_k(gate_input @ gate_w^T + gate_b) with gate_input = [H + C | |H - C|]
+ * (gate_mode 1, score mode "new") or [H | C] (0), gate_w [K, 2D], gate_b [K];
+ * alpha [n, K] is written and the pack (modes as cign_pack_fwd) uses it.
+ * H and C are read once for both.  alpha and out equal cign_hop_gate_fwd
+ * followed by cign_pack_fwd bit for bit.  1 <= K <= 8, D % 4 == 0,
+ * D <= 1024, 16-byte aligned tensors. */
+CIGN_API int cign_gate_pack_fwd(int64_t n, int64_t d, int32_t k, int32_t gate_mode,
+                       int32_t interaction, int32_t outer, int32_t weighting, const float* H,
+                       const float* C, const float* const* P, int64_t ldp,
+                       const float* gate_w, const float* gate_b, float* alpha, float* out,
+                       cign_stream_t stream);
 /* Backward: grad_H, grad_C [N,D]; grad_P: host array of K device pointers
  * ([N,2D], stride ldgp); grad_alpha [N,K] or NULL.
  * accumulate_p != 0 adds into grad_P instead of overwriting it.
