@@ -516,7 +516,8 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
     base = prepare_fixed_csr_operator(adj)
     (rp, c), _, _ = to_graph_format(prepare_gat_edge_index(ei, n).flip(0), n)
     bounds, hplan, exch, dop, dgat = partition_graph(
-        base.csr, rp, c, world, rank, device, transport=None if args.exchange == "nccl" else "peer")
+        base.csr, rp, c, world, rank, device,
+        transport={"nccl": None, "peer": "peer", "peer-copy": "peer-copy"}[args.exchange])
     r0, r1 = bounds[rank], bounds[rank + 1]
     nnz = int(base.nnz)
     x_all, y_all, train_all, _, _ = synth.make_features(gcfg)
@@ -646,9 +647,12 @@ def run_partitioned(args, cfg, metric, world, rank, local_rank, device):
                        "layers": cfg.layers, "dropout": cfg.dropout,
                        "parallelism": f"row-partition x{world}",
                        "exchange": ("halo rows per hop and per GAT layer: " +
-                                    ("NCCL point-to-point" if args.exchange == "nccl" else
-                                     "stored into the peers' IPC-mapped buffers over NVLink "
-                                     "(cign_halo_push)") +
+                                    {"nccl": "NCCL point-to-point",
+                                     "peer": "stored into the peers' IPC-mapped buffers over "
+                                             "NVLink by SM stores (cign_halo_push)",
+                                     "peer-copy": "copied into the peers' IPC-mapped buffers "
+                                                  "over NVLink by the copy engines "
+                                                  "(cign_halo_push_copy)"}[args.exchange] +
                                     "; one gradient all-reduce per step"),
                        "halo_rows_total": int(halo.item()),
                        "halo_rows_max_per_rank": int(halo_max.item()),
@@ -911,7 +915,7 @@ def main():
                          "bf16 (fp32 against bf16 feature storage, cfg2 and a cfg5 shard)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the workload's number of CIGN blocks (0: the config's)")
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--exchange", choices=["peer", "peer-copy", "nccl"], default="peer",
                     help="halo exchange of the multi-GPU run")
     ap.add_argument("--eager", action="store_true",
                     help="launch every op from Python each step (default: replay one CUDA graph)")

@@ -99,6 +99,7 @@ SIGNATURES = {
     "cign_ipc_open": (c_int, [_P, POINTER(c_void_p)]),
     "cign_ipc_close": (c_int, [_P]),
     "cign_halo_push": (c_int, [c_int32, _P, c_int64, _P, _P, _P, c_int64, _P]),
+    "cign_halo_push_copy": (c_int, [c_int32, _P, c_int64, _P, _P, _P, c_int64, _P, _P]),
     "cign_colsum_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "cign_colsum_f32": (c_int, [c_int64, c_int64, _P, _P, _P, c_size_t, _P]),
     "cign_seed_table_step": (c_int, [c_uint64, c_int32, _P, _P, c_int32, c_int32, _P, _P]),
@@ -115,6 +116,10 @@ SIGNATURES = {
     "cign_attn_logits_bwd_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
     "cign_attn_logits_bwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
                                      c_int32, _P, c_size_t, _P]),
+    "cign_row_dots_fwd": (c_int, [c_int64, c_int64, c_int32, _P, _P, _P, _P]),
+    "cign_row_dots_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int32]),
+    "cign_row_dots_bwd": (c_int, [c_int64, c_int64, c_int32, _P, _P, _P, _P, c_int32, _P, _P,
+                                  c_size_t, _P]),
     "cign_head_mean_bias_silu_fwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P]),
     "cign_head_mean_bias_silu_bwd_workspace_bytes": (c_size_t, [c_int64, c_int32]),
     "cign_head_mean_bias_silu_bwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P,

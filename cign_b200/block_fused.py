@@ -19,7 +19,7 @@ forward values are those of the op-by-op composition.
 """
 from __future__ import annotations
 
-from typing import Optional, Sequence
+from typing import Sequence
 
 import torch
 
@@ -38,9 +38,13 @@ PACK_MODES = (1, 0, 0)  # interaction "new", outer none, weighting "old"
 USE_TCGEN05_PACK_PROJ = None
 
 
-def native_spmm_plan(operator) -> Optional[SpmmPlan]:
-    """The SpmmPlan behind a k-hop operator of multihop_csr_pipeline (None for
-    other operators, e.g. a row-partitioned one)."""
+def native_spmm_plan(operator):
+    """The propagator behind a k-hop operator: the SpmmPlan of a
+    multihop_csr_pipeline operator, or the row-partitioned operator itself
+    (cign_b200.distributed.DistMultiHop, which has the same forward(x, K) /
+    backward(grads, F) pair); None for other operators."""
+    if getattr(operator, "is_row_partitioned", False):
+        return operator
     if isinstance(operator, MultiHopCSR3GraphOperator):
         return operator.plan.spmm
     if isinstance(operator, HybridNative3TailCSRGraphOperator):

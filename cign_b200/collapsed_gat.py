@@ -401,53 +401,161 @@ def _full_fp32_matmul():
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-class _LogitsThroughWeightFn(torch.autograd.Function):
-    """alpha [N, 2H] = x @ V^T, V = [W_h^T att_src[h] ; W_h^T att_dst[h]]: the
-    attention logits of lin(x) (the attention-logit side op on
-    lin(x).view(N, H, C), fused_gat_sideops.py:50-71) without forming lin(x).
+def row_dots_forward(x: torch.Tensor, V: torch.Tensor) -> torch.Tensor:
+    """out [N, K] = x [N, D] @ V[K, D]^T in fp32 (cign_row_dots_fwd)."""
+    lib = ensure_collapsed_gat_loaded()
+    n, D = (int(s) for s in x.shape)
+    K = int(V.size(0))
+    out = torch.empty((n, K), dtype=torch.float32, device=x.device)
+    with _lib.DeviceGuard(x.device):
+        rc = lib.cign_row_dots_fwd(n, D, K, _lib.ptr(x), _lib.ptr(V), _lib.ptr(out),
+                                   _lib.stream_of(x))
+    _lib.check(rc, "cign_row_dots_fwd")
+    return out
 
-    Always full fp32, whatever the TF32 setting: the parameter gradients of
-    att_src / att_dst are sums over every node of terms that largely cancel,
-    and TF32-rounded operands there cost percent-level relative error; the
-    products are N*D*2H multiply-adds, a negligible share of the step."""
+
+def row_dots_backward(x: torch.Tensor, V: torch.Tensor, g: torch.Tensor, grad_x: torch.Tensor,
+                      accumulate: bool) -> torch.Tensor:
+    """grad_x (+)= g @ V in place; returns grad_V = g^T @ x (cign_row_dots_bwd)."""
+    lib = ensure_collapsed_gat_loaded()
+    n, D = (int(s) for s in x.shape)
+    K = int(V.size(0))
+    gV = torch.empty_like(V)
+    ws = _lib.workspace(lib.cign_row_dots_bwd_workspace_bytes(n, D, K), x.device)
+    with _lib.DeviceGuard(x.device):
+        rc = lib.cign_row_dots_bwd(n, D, K, _lib.ptr(x), _lib.ptr(V), _lib.ptr(g),
+                                   _lib.ptr(grad_x), 1 if accumulate else 0, _lib.ptr(gV),
+                                   _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+    _lib.check(rc, "cign_row_dots_bwd")
+    return gV
+
+
+def _logit_vectors(weight: torch.Tensor, att_src: torch.Tensor, att_dst: torch.Tensor,
+                   heads: int):
+    """(V [2H, D], A [H, 2, C]): V[h] = W_h^T att_src[h], V[H + h] = W_h^T att_dst[h]
+    (W_h = weight[h*C:(h+1)*C]), in full fp32."""
+    HC, D = (int(s) for s in weight.shape)
+    H = int(heads)
+    C = HC // H
+    A = torch.cat([att_src.reshape(H, 1, C), att_dst.reshape(H, 1, C)], 1)
+    with _full_fp32_matmul():
+        V2 = torch.bmm(A, weight.view(H, C, D))                                  # [H, 2, D]
+    return V2.transpose(0, 1).reshape(2 * H, D), A
+
+
+class _GatContextLinFn(torch.autograd.Function):
+    """The GAT context of a CIGN block up to its bias: lin(x) -> attention
+    logits (fused_gat_sideops.py:50-71) -> collapsed GAT head mean
+    (collapsed_gat_cuda.cu:52-174) without its bias, as one node, evaluated
+    aggregate-first (_AggregateFirstLinFn) with the logits as row dots of x
+    with V = [W_h^T att_src[h] ; W_h^T att_dst[h]] (cign_row_dots_fwd): x is
+    read once for all 2H logits and no [N, H*C] tensor is formed.  Rows
+    [0, n_dst) of x are the destination rows (all of them unless the graph is
+    a row-partitioned block with halo columns).
+
+    Backward: the aggregation's gradients (gat_agg_backward_raw), then
+    grad_x = gfeat W + g_alpha V with the second term added in place by
+    cign_row_dots_bwd (no separate add), and grad W = gfeat^T x + the logit
+    vectors' share.  The logits and their gradients stay in full fp32
+    whatever the TF32 setting: the att_src / att_dst gradients are sums over
+    every node of nearly cancelling terms."""
 
     @staticmethod
-    def forward(ctx, x, weight, att_src, att_dst, heads):
+    def forward(ctx, x, weight, att_src, att_dst, plan, heads, n_dst, negative_slope, attn_drop,
+                seed):
         H = int(heads)
-        HC, D = (int(s) for s in weight.shape)
-        C = HC // H
-        Wv = weight.view(H, C, D)
-        V = torch.cat([(Wv * att_src.reshape(H, C, 1)).sum(1),
-                       (Wv * att_dst.reshape(H, C, 1)).sum(1)], 0)           # [2H, D]
-        with _full_fp32_matmul():
-            alpha = x.mm(V.t())
-        ctx.save_for_backward(x, weight, att_src, att_dst, V)
-        ctx.heads = H
-        return alpha
+        V, A = _logit_vectors(weight, att_src, att_dst, H)
+        alpha = row_dots_forward(x, V)                                              # [N, 2H]
+        attn_col = alpha[:, :H].contiguous()
+        attn_row = alpha[:n_dst, H:].contiguous()
+        n, D = int(plan.n), int(x.size(1))
+        z, emax, esum = gat_agg_forward_raw(plan, attn_row, attn_col, x, H, negative_slope,
+                                            attn_drop, seed)
+        M = _head_projection(weight, H)
+        lin = z.view(n, H * D).mm(M)
+        del z
+        ctx.save_for_backward(x, weight, attn_row, attn_col, emax, esum, V, A)
+        ctx.plan, ctx.heads, ctx.n_dst, ctx.att_shape = plan, H, int(n_dst), att_src.shape
+        ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), seed
+        return lin
 
     @staticmethod
-    def backward(ctx, g):
-        x, weight, att_src, att_dst, V = ctx.saved_tensors
-        H = ctx.heads
-        HC, D = (int(s) for s in weight.shape)
+    def backward(ctx, g_lin):
+        x, weight, attn_row, attn_col, emax, esum, V, A = ctx.saved_tensors
+        H, n_dst = ctx.heads, ctx.n_dst
+        n_src, D = (int(s) for s in x.shape)
+        HC = int(weight.size(0))
         C = HC // H
-        g = g.contiguous()
+        g_pre = g_lin.contiguous()
+        M = _head_projection(weight, H)
+        grad_z = g_pre.mm(M.t())                                                    # [N, H*D]
+        gfeat, grow, gcol = gat_agg_backward_raw(ctx.plan, attn_row, attn_col, x, emax, esum,
+                                                 grad_z, g_pre, ctx.negative_slope,
+                                                 ctx.attn_drop, ctx.seed)
+        del grad_z
+        gfeat2 = gfeat.view(n_src, HC)
+        grad_x = gfeat2.mm(weight)                                                  # [N_src, D]
+        g_alpha = torch.zeros((n_src, 2 * H), dtype=torch.float32, device=x.device)
+        g_alpha[:, :H] = gcol
+        g_alpha[:n_dst, H:] = grow
+        gV = row_dots_backward(x, V, g_alpha, grad_x, accumulate=True)              # [2H, D]
+        gV2 = gV.view(2, H, D).transpose(0, 1)                                      # [H, 2, D]
         with _full_fp32_matmul():
-            gx = g.mm(V) if ctx.needs_input_grad[0] else None
-            gV = g.t().mm(x)                                                 # [2H, D]
-        gVs, gVd = gV[:H].reshape(H, 1, D), gV[H:].reshape(H, 1, D)
-        Wv = weight.view(H, C, D)
-        gW = (att_src.reshape(H, C, 1) * gVs + att_dst.reshape(H, C, 1) * gVd).reshape(HC, D)
-        gas = (Wv * gVs).sum(2).reshape(att_src.shape)
-        gad = (Wv * gVd).sum(2).reshape(att_dst.shape)
-        return gx, gW, gas, gad, None
+            g_att = torch.bmm(weight.view(H, C, D), gV2.transpose(1, 2))             # [H, C, 2]
+            g_w_att = torch.bmm(A.transpose(1, 2), gV2)                              # [H, C, D]
+        grad_w = torch.addmm(g_w_att.reshape(HC, D), gfeat2.t(), x)                 # [H*C, D]
+        g_src = g_att[:, :, 0].reshape(ctx.att_shape)
+        g_dst = g_att[:, :, 1].reshape(ctx.att_shape)
+        return grad_x, grad_w, g_src, g_dst, None, None, None, None, None, None
 
 
-def attention_logits_through_weight(x: torch.Tensor, weight: torch.Tensor, att_src: torch.Tensor,
-                                    att_dst: torch.Tensor, heads: int) -> torch.Tensor:
-    """[alpha_src | alpha_dst] [N, 2H] of lin(x).view(N, H, C) with
-    lin.weight = weight [H*C, D] and att_* [1, H, C], in full fp32."""
-    return _LogitsThroughWeightFn.apply(x.contiguous(), weight, att_src, att_dst, int(heads))
+def _gat_context_args(x, weight, att_src, att_dst, csr, csc, perm, attn_drop, n_dst):
+    if x.dtype != torch.float32 or x.device.type != "cuda" or x.dim() != 2:
+        raise TypeError("aggregate-first GAT requires CUDA float32 x [N,D]")
+    if att_src.dim() < 2:
+        raise ValueError("att_src / att_dst must be [1, H, C]")
+    H = int(att_src.size(-2))
+    if not (1 <= H <= MAX_HEADS):
+        raise ValueError(f"collapsed GAT requires 1<=H<={MAX_HEADS}; got H={H}")
+    if weight.dim() != 2 or weight.size(0) % H != 0 or weight.size(1) != x.size(1):
+        raise ValueError("weight must be [H*C, D]")
+    C = weight.size(0) // H
+    if att_src.numel() != H * C or att_dst.numel() != H * C:
+        raise ValueError("att_src / att_dst must be [1, H, C]")
+    if not (0.0 <= float(attn_drop) < 1.0):
+        raise ValueError("attn_drop must be in [0,1)")
+    (rowptr, col), (row, colptr) = csr, csc
+    plan = gat_plan_for(rowptr, col, row, colptr, perm)
+    n_dst = int(plan.n) if n_dst is None else int(n_dst)
+    if plan.n_cols != x.size(0) or plan.n != n_dst:
+        raise RuntimeError(f"graph is {plan.n} x {plan.n_cols} but x has {x.size(0)} rows "
+                           f"({n_dst} destination rows)")
+    return plan, H, n_dst
+
+
+def gat_context_lin(x: torch.Tensor, weight: torch.Tensor, att_src: torch.Tensor,
+                    att_dst: torch.Tensor, csr, csc, perm: torch.Tensor, negative_slope: float,
+                    attn_drop: float, n_dst=None) -> torch.Tensor:
+    """The head-mean GAT output before its bias ([n_dst, C]) of GATConv(x) with
+    lin.weight = weight [H*C, D] and att_src / att_dst [1, H, C]: the logits,
+    the segment softmax and the aggregation in one node (_GatContextLinFn).
+    Pair it with gat_silu_add_layernorm or _BiasSiLUFn.  Same dropout stream
+    (call counter and keep bits) as collapsed_gat_mean_bias_silu."""
+    plan, H, n_dst = _gat_context_args(x, weight, att_src, att_dst, csr, csc, perm, attn_drop,
+                                       n_dst)
+    seed = gat_call_seed(attn_drop)
+    return _GatContextLinFn.apply(x.contiguous(), weight, att_src, att_dst, plan, H, n_dst,
+                                  float(negative_slope), float(attn_drop), seed)
+
+
+def gat_context(x: torch.Tensor, weight: torch.Tensor, att_src: torch.Tensor,
+                att_dst: torch.Tensor, bias: torch.Tensor, csr, csc, perm: torch.Tensor,
+                negative_slope: float, attn_drop: float, n_dst=None) -> torch.Tensor:
+    """SiLU(gat_context_lin(...) + bias): GATConv(concat=False) + bias + SiLU as
+    collapsed_gat_mean_bias_silu computes it on lin(x)."""
+    lin = gat_context_lin(x, weight, att_src, att_dst, csr, csc, perm, negative_slope, attn_drop,
+                          n_dst)
+    return _BiasSiLUFn.apply(lin, bias)
 
 
 def collapsed_gat_aggregate_first(x: torch.Tensor, attn_row: torch.Tensor, attn_col: torch.Tensor,

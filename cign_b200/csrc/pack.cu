@@ -117,7 +117,9 @@ pack_fwd_kernel(int64_t n, int64_t D, int K, int interaction, int outer, int wei
 // The gate dots run in the order of hop_gate_fwd_kernel (columns
 // increasing, x/y/z/w, the sum half before the difference half, then one
 // warp sum) and the pack in the order of pack_fwd_kernel: alpha and the
-// packed output equal those kernels' bit for bit.
+// packed output equal those kernels' bit for bit.  Hop 0's propagated rows
+// are read together with H and C and its interaction terms formed before
+// the gate's reductions, so that load's latency hides behind the gate.
 template <int K, int VPL>
 __global__ void __launch_bounds__(kThreads)
 gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int outer,
@@ -130,15 +132,29 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
   if (row >= n) return;
   const int64_t D2 = 2 * D;
   float4 h[VPL], c[VPL];
+  // hop 0's interaction terms (before the alpha scaling): its propagated
+  // rows are loaded with H and C and combined while the gate reduces
+  float4 w0[VPL], d0[VPL];
   float dot[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) dot[k] = 0.0f;
+  const float* p0 = P.p[0] + row * ldp;
 #pragma unroll
   for (int q = 0; q < VPL; ++q) {
     const int64_t d = static_cast<int64_t>(lane + q * 32) * 4;
     if (d < D) {
       h[q] = ld_vec<4>(Hn + row * D + d);
       c[q] = ld_vec<4>(Cn + row * D + d);
+      const float4 th = ldg_vec<4>(p0 + d);
+      const float4 tc = ldg_vec<4>(p0 + D + d);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float Dv, Wv;
+        interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer, Dv,
+                     Wv);
+        vel(w0[q], j) = Wv;
+        vel(d0[q], j) = Dv;
+      }
       float4 g0, g1;
       if (gate_mode == 1) {
         g0 = make_float4(h[q].x + c[q].x, h[q].y + c[q].y, h[q].z + c[q].z, h[q].w + c[q].w);
@@ -150,16 +166,18 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
       }
 #pragma unroll
       for (int k = 0; k < K; ++k) {
-        const float4 w0 = ldg_vec<4>(W + k * D2 + d);
-        const float4 w1 = ldg_vec<4>(W + k * D2 + D + d);
+        const float4 wa = ldg_vec<4>(W + k * D2 + d);
+        const float4 wb = ldg_vec<4>(W + k * D2 + D + d);
         float t = dot[k];
-        t = fmaf(g0.x, w0.x, t); t = fmaf(g0.y, w0.y, t); t = fmaf(g0.z, w0.z, t); t = fmaf(g0.w, w0.w, t);
-        t = fmaf(g1.x, w1.x, t); t = fmaf(g1.y, w1.y, t); t = fmaf(g1.z, w1.z, t); t = fmaf(g1.w, w1.w, t);
+        t = fmaf(g0.x, wa.x, t); t = fmaf(g0.y, wa.y, t); t = fmaf(g0.z, wa.z, t); t = fmaf(g0.w, wa.w, t);
+        t = fmaf(g1.x, wb.x, t); t = fmaf(g1.y, wb.y, t); t = fmaf(g1.z, wb.z, t); t = fmaf(g1.w, wb.w, t);
         dot[k] = t;
       }
     } else {
       vzero(h[q]);
       vzero(c[q]);
+      vzero(w0[q]);
+      vzero(d0[q]);
     }
   }
   float m = -INFINITY;
@@ -194,16 +212,24 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
     for (int q = 0; q < VPL; ++q) {
       const int64_t d = static_cast<int64_t>(lane + q * 32) * 4;
       if (d >= D) continue;
-      const float4 th = ldg_vec<4>(pk + d);
-      const float4 tc = ldg_vec<4>(pk + D + d);
       float4 ow_, od_;
+      if (k == 0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float Dv, Wv;
-        interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer, Dv,
-                     Wv);
-        vel(ow_, j) = a * Wv;
-        vel(od_, j) = a * Dv;
+        for (int j = 0; j < 4; ++j) {
+          vel(ow_, j) = a * vel(w0[q], j);
+          vel(od_, j) = a * vel(d0[q], j);
+        }
+      } else {
+        const float4 th = ldg_vec<4>(pk + d);
+        const float4 tc = ldg_vec<4>(pk + D + d);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float Dv, Wv;
+          interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer,
+                       Dv, Wv);
+          vel(ow_, j) = a * Wv;
+          vel(od_, j) = a * Dv;
+        }
       }
       if (weighting == 0) {
         float* o = out + row * ow + static_cast<int64_t>(k) * 2 * D + d;

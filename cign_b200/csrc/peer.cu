@@ -9,6 +9,11 @@
 // The stores are plain st.global to peer addresses (no multicast); the
 // caller orders the copies against the peers' reads with a collective
 // issued after the launch on the same stream.
+//
+// cign_halo_push_copy moves the same rows with the copy engines instead of
+// SM stores: the send rows are gathered into a local staging buffer and
+// each peer's block goes over NVLink as one cudaMemcpyAsync, so the
+// transfer takes no SM time from the kernels it overlaps.
 #include <algorithm>
 #include <cstring>
 
@@ -32,6 +37,22 @@ halo_push_kernel(int n_peers, const float* __restrict__ src, int64_t F,
     const int64_t row = idx != nullptr ? idx[k] : k;
     const float4* s4 = reinterpret_cast<const float4*>(src + row * F);
     float4* d4 = reinterpret_cast<float4*>(peer_dst[p] + (k - peer_begin[p]) * F);
+    for (int64_t q = lane; q < F / 4; q += 32) d4[q] = __ldg(s4 + q);
+  }
+}
+
+// Gathers the send rows into a contiguous staging buffer in this GPU's own
+// memory (warp per row, 16-byte copies), so that each peer's share is one
+// contiguous block the copy engine can move.
+__global__ void __launch_bounds__(kPushThreads)
+halo_gather_kernel(const float* __restrict__ src, int64_t F, const int64_t* __restrict__ idx,
+                   int64_t total, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kPushThreads / 32);
+  for (int64_t k = static_cast<int64_t>(blockIdx.x) * (kPushThreads / 32) + (threadIdx.x >> 5);
+       k < total; k += warps) {
+    const float4* s4 = reinterpret_cast<const float4*>(src + idx[k] * F);
+    float4* d4 = reinterpret_cast<float4*>(out + k * F);
     for (int64_t q = lane; q < F / 4; q += 32) d4[q] = __ldg(s4 + q);
   }
 }
@@ -95,6 +116,43 @@ int cign_halo_push(int32_t n_peers, const float* src, int64_t F, const int64_t* 
                      static_cast<cudaStream_t>(stream)>>>(n_peers, src, F, idx, peer_begin,
                                                           peer_dst, total);
   CIGN_CHECK_LAUNCH("halo_push_kernel");
+  return CIGN_OK;
+}
+
+int cign_halo_push_copy(int32_t n_peers, const float* src, int64_t F, const int64_t* idx,
+                        const int64_t* peer_begin_host, float* const* peer_dst_host,
+                        int64_t total, float* staging, cign_stream_t stream) {
+  CIGN_REQUIRE(n_peers >= 1 && F > 0 && total >= 0, CIGN_ERR_INVALID_ARGUMENT,
+               "halo_push_copy: bad sizes");
+  if (total == 0) return CIGN_OK;
+  CIGN_REQUIRE(src != nullptr && peer_begin_host != nullptr && peer_dst_host != nullptr,
+               CIGN_ERR_NULL_POINTER, "halo_push_copy: NULL argument");
+  CIGN_REQUIRE(peer_begin_host[0] == 0 && peer_begin_host[n_peers] == total,
+               CIGN_ERR_INVALID_ARGUMENT, "halo_push_copy: peer_begin must run from 0 to total");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float* rows = src;
+  if (idx != nullptr) {
+    CIGN_REQUIRE(staging != nullptr, CIGN_ERR_NULL_POINTER,
+                 "halo_push_copy: a gathered push needs a staging buffer of total * F floats");
+    CIGN_REQUIRE(F % 4 == 0 && aligned16(src) && aligned16(staging), CIGN_ERR_ALIGNMENT,
+                 "halo_push_copy: rows must be float4-aligned (F %% 4 == 0)");
+    const int64_t blocks = std::min<int64_t>((total + 7) / 8, 4 * 148 * 8);
+    halo_gather_kernel<<<static_cast<unsigned>(blocks), kPushThreads, 0, s>>>(src, F, idx, total,
+                                                                              staging);
+    CIGN_CHECK_LAUNCH("halo_gather_kernel");
+    rows = staging;
+  }
+  for (int p = 0; p < n_peers; ++p) {
+    const int64_t b = peer_begin_host[p], e = peer_begin_host[p + 1];
+    CIGN_REQUIRE(b <= e, CIGN_ERR_INVALID_ARGUMENT, "halo_push_copy: peer_begin not sorted");
+    if (e == b) continue;
+    CIGN_REQUIRE(peer_dst_host[p] != nullptr, CIGN_ERR_NULL_POINTER,
+                 "halo_push_copy: NULL destination for peer %d", p);
+    CIGN_CHECK_CUDA(cudaMemcpyAsync(peer_dst_host[p], rows + b * F,
+                                    static_cast<size_t>(e - b) * F * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, s),
+                    "halo_push_copy: cudaMemcpyAsync");
+  }
   return CIGN_OK;
 }
 

@@ -27,7 +27,7 @@ summed over ranks with one all-reduce (allreduce_gradients).
 """
 from __future__ import annotations
 
-from typing import Dict, List, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -291,12 +291,15 @@ class PeerHaloExchange(HaloExchange):
     previous step's reads.  Call begin_step() at the start of every step.
     """
 
-    def __init__(self, plan: HaloPlan, device, group=None):
+    def __init__(self, plan: HaloPlan, device, group=None, copy: str = "kernel"):
         super().__init__(plan, device, TorchP2P(group))
         from . import _lib
+        if copy not in ("kernel", "engine"):
+            raise ValueError("copy must be 'kernel' (SM stores) or 'engine' (copy engines)")
         self.lib = _lib.load_library()
         self._lib = _lib
         self.group = group
+        self.copy = copy
         w = plan.world
         # every rank's counts, so each rank can address its slots on the peers
         mine = torch.tensor([plan.n_own] + plan.recv_counts + plan.send_counts,
@@ -311,6 +314,11 @@ class PeerHaloExchange(HaloExchange):
                                        dtype=torch.int64, device=self.device)
         self.recv_begin = torch.tensor(_offsets(plan.recv_counts) + [sum(plan.recv_counts)],
                                        dtype=torch.int64, device=self.device)
+        self._begin_host = {  # the same offsets as host arrays (copy-engine pushes)
+            "send": (_lib.ctypes.c_int64 * (w + 1))(*(_offsets(plan.send_counts)
+                                                       + [sum(plan.send_counts)])),
+            "recv": (_lib.ctypes.c_int64 * (w + 1))(*(_offsets(plan.recv_counts)
+                                                       + [sum(plan.recv_counts)]))}
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._slots: List[dict] = []
         self._call = 0
@@ -389,20 +397,34 @@ class PeerHaloExchange(HaloExchange):
             ptr, view, bases = self._alloc_shared(int(self.send_all.numel()), F)
             dst = [bases[p] + self.send_off_of[p][me] * F * 4 for p in range(w)]
         slot = {"kind": kind, "F": F, "ptr": ptr, "view": view, "bases": bases,
-                "dst": torch.tensor(dst, dtype=torch.int64, device=self.device)}
+                "dst": torch.tensor(dst, dtype=torch.int64, device=self.device),
+                "dst_host": (self._lib.ctypes.c_void_p * w)(*dst),
+                # copy engines: the gathered send rows, contiguous per peer
+                "staging": (torch.empty((int(self.send_all.numel()), F), dtype=torch.float32,
+                                        device=self.device)
+                            if self.copy == "engine" and kind != "scatter" else None)}
         self._slots.append(slot)
         return slot
 
-    def _push(self, src, F, idx, begin, dst, total):
+    def _push(self, src, F, idx, slot, total):
         stream = torch.cuda.current_stream(self.device)
         if self.timer is not None:
             t0 = torch.cuda.Event(enable_timing=True)
             t0.record(stream)
-        rc = self.lib.cign_halo_push(self.plan.world, self._lib.ptr(src), F,
-                                     self._lib.ptr(idx) if idx is not None else None,
-                                     self._lib.ptr(begin), self._lib.ptr(dst), int(total),
-                                     self._lib.stream_of(src))
-        self._lib.check(rc, "cign_halo_push")
+        gathered = idx is not None  # send rows of x (gather) or halo-row gradients (scatter)
+        if self.copy == "engine":
+            rc = self.lib.cign_halo_push_copy(
+                self.plan.world, self._lib.ptr(src), F, self._lib.ptr(idx) if gathered else None,
+                self._begin_host["send" if gathered else "recv"], slot["dst_host"], int(total),
+                self._lib.ptr(slot["staging"]) if gathered else None, self._lib.stream_of(src))
+            self._lib.check(rc, "cign_halo_push_copy")
+        else:
+            begin = self.send_begin if gathered else self.recv_begin
+            rc = self.lib.cign_halo_push(self.plan.world, self._lib.ptr(src), F,
+                                         self._lib.ptr(idx) if gathered else None,
+                                         self._lib.ptr(begin), self._lib.ptr(slot["dst"]),
+                                         int(total), self._lib.stream_of(src))
+            self._lib.check(rc, "cign_halo_push")
         if self.timer is not None:
             t1 = torch.cuda.Event(enable_timing=True)
             t1.record(stream)
@@ -417,14 +439,14 @@ class PeerHaloExchange(HaloExchange):
             self._stream = torch.cuda.Stream(self.device)
         return self._stream
 
-    def _push_async(self, src, F, idx, begin, dst, total):
+    def _push_async(self, src, F, idx, slot, total):
         """The push and its ordering collective on the side stream, after the
         current stream's work so far; returns the event that ends them."""
         cur = torch.cuda.current_stream(self.device)
         side = self._side()
         side.wait_stream(cur)
         with torch.cuda.stream(side):
-            self._push(src, F, idx, begin, dst, total)
+            self._push(src, F, idx, slot, total)
             ev = torch.cuda.Event()
             ev.record(side)
         return ev
@@ -433,15 +455,14 @@ class PeerHaloExchange(HaloExchange):
         x_own = x_own.contiguous()
         F = int(x_own.size(1))
         slot = self._slot("halo", F)
-        ev = self._push_async(x_own, F, self.send_all, self.send_begin, slot["dst"],
-                              int(self.send_all.numel()))
+        ev = self._push_async(x_own, F, self.send_all, slot, int(self.send_all.numel()))
         return slot["view"], ev
 
     def return_halo(self, g_halo: torch.Tensor):
         g_halo = g_halo.contiguous()
         F = int(g_halo.size(1))
         slot = self._slot("scatter", F)
-        ev = self._push_async(g_halo, F, None, self.recv_begin, slot["dst"], self.n_halo)
+        ev = self._push_async(g_halo, F, None, slot, self.n_halo)
         return slot["view"], ev
 
     def gather(self, x_own: torch.Tensor) -> torch.Tensor:
@@ -450,8 +471,7 @@ class PeerHaloExchange(HaloExchange):
         slot = self._slot("gather", F)
         x_ext = slot["view"]
         x_ext[:self.n_own].copy_(x_own)
-        self._push(x_own, F, self.send_all, self.send_begin, slot["dst"],
-                   int(self.send_all.numel()))
+        self._push(x_own, F, self.send_all, slot, int(self.send_all.numel()))
         return x_ext
 
     def scatter_add(self, g_ext: torch.Tensor) -> torch.Tensor:
@@ -459,7 +479,7 @@ class PeerHaloExchange(HaloExchange):
         F = int(g_ext.size(1))
         slot = self._slot("scatter", F)
         g_own = g_ext[:self.n_own].clone()
-        self._push(g_ext[self.n_own:], F, None, self.recv_begin, slot["dst"], self.n_halo)
+        self._push(g_ext[self.n_own:], F, None, slot, self.n_halo)
         recv = slot["view"]
         for p in range(self.plan.world):
             c = self.plan.send_counts[p]
@@ -527,42 +547,28 @@ def _csr_plan(rows_of_edges, cols, vals, n_rows: int, n_cols: int, dev) -> SpmmP
 
 
 class _DistHopFn(torch.autograd.Function):
-    """One hop y = P_r x over the rank's row block, split by column owner:
-    y = P_own x_own + P_halo halo(x).  The halo push runs on a side stream
-    while P_own x_own is computed; the backward returns P_halo^T g to the
-    owners the same way while P_own^T g is computed."""
+    """One hop y = P_r x over the rank's row block as an autograd node
+    (DistMultiHop.hop_forward / hop_backward)."""
 
     @staticmethod
     def forward(ctx, x_own, hop: "DistMultiHop"):
         ctx.hop = hop
-        x_own = x_own.contiguous()
-        halo, ev = hop.exchange.gather_halo(x_own)
-        y = hop.own.spmm(x_own)
-        if ev is not None:
-            torch.cuda.current_stream(x_own.device).wait_event(ev)
-        if hop.halo is None:
-            return y
-        return hop.halo.spmm(halo, addend=y)
+        return hop.hop_forward(x_own)
 
     @staticmethod
     def backward(ctx, g):
-        hop = ctx.hop
-        g = g.contiguous()
-        # a rank without halo columns returns nothing but still takes the
-        # exchange's steps (its collective) like every other rank
-        g_halo = (g.new_zeros((0, g.size(1))) if hop.halo is None
-                  else hop.halo.spmm(g, transpose=True))
-        recv, ev = hop.exchange.return_halo(g_halo)
-        g_own = hop.own.spmm(g, transpose=True)
-        if ev is not None:
-            torch.cuda.current_stream(g.device).wait_event(ev)
-        hop.exchange.add_returned(g_own, recv)
-        return g_own, None
+        return ctx.hop.hop_backward(g), None
 
 
 class DistMultiHop:
     """k-hop propagation P^p x over the row-partitioned operator; each hop
-    overlaps the halo exchange with the own-column part of the SpMM."""
+    overlaps the halo exchange with the own-column part of the SpMM.
+
+    Besides the autograd form (powers), it offers the raw forward/backward
+    pair of a native SpmmPlan (forward(x, K), backward(grads, F)), so the
+    block's fused propagate + hop gate + pack node runs on it unchanged."""
+
+    is_row_partitioned = True
 
     def __init__(self, csr_global: torch.Tensor, plan: HaloPlan, exchange: HaloExchange):
         crow = csr_global.crow_indices().cpu()
@@ -580,6 +586,35 @@ class DistMultiHop:
         self.exchange = exchange
         self.nnz_local = int(lcol.numel())
 
+    def hop_forward(self, x_own: torch.Tensor) -> torch.Tensor:
+        """y = P_own x_own + P_halo halo(x): the owners push this rank's halo
+        rows on a side stream while P_own x_own is computed."""
+        x_own = x_own.contiguous()
+        halo, ev = self.exchange.gather_halo(x_own)
+        y = self.own.spmm(x_own)
+        if ev is not None:
+            torch.cuda.current_stream(x_own.device).wait_event(ev)
+        if self.halo is None:
+            return y
+        return self.halo.spmm(halo, addend=y)
+
+    def hop_backward(self, g: torch.Tensor,
+                     addend: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """P_r^T g (+ addend): P_halo^T g goes back to the owners on the side
+        stream while P_own^T g (+ addend) is computed; the rows the peers
+        returned are added in a fixed peer order."""
+        g = g.contiguous()
+        # a rank without halo columns returns nothing but still takes the
+        # exchange's steps (its collective) like every other rank
+        g_halo = (g.new_zeros((0, g.size(1))) if self.halo is None
+                  else self.halo.spmm(g, transpose=True))
+        recv, ev = self.exchange.return_halo(g_halo)
+        g_own = self.own.spmm(g, transpose=True, addend=addend)
+        if ev is not None:
+            torch.cuda.current_stream(g.device).wait_event(ev)
+        self.exchange.add_returned(g_own, recv)
+        return g_own
+
     def powers(self, x_own: torch.Tensor, powers: Sequence[int]) -> Dict[int, torch.Tensor]:
         wanted = sorted(set(int(p) for p in powers))
         out: Dict[int, torch.Tensor] = {}
@@ -591,6 +626,25 @@ class DistMultiHop:
             if p in wanted:
                 out[p] = cur
         return out
+
+    def forward(self, x_own: torch.Tensor, max_power: int) -> List[torch.Tensor]:
+        """[P^1 x, ..., P^max_power x] over the rank's rows (no autograd)."""
+        ys, cur = [], x_own
+        for _ in range(int(max_power)):
+            cur = self.hop_forward(cur)
+            ys.append(cur)
+        return ys
+
+    def backward(self, grads: Sequence[Optional[torch.Tensor]], F: int) -> torch.Tensor:
+        """grads[p-1] = dL/d(P^p x) or None (the last one given); returns
+        dL/dx = sum_p (P^T)^p grads[p-1], accumulated from the highest hop down
+        with each lower hop's gradient added inside the SpMM."""
+        if grads[-1] is None:
+            raise ValueError("the highest hop's gradient must be given")
+        acc = grads[-1]
+        for p in range(len(grads) - 1, 0, -1):
+            acc = self.hop_backward(acc, grads[p - 1])
+        return self.hop_backward(acc)
 
 
 class DistGatGraph:
@@ -626,13 +680,15 @@ def partition_graph(csr_global: torch.Tensor, gat_rowptr: torch.Tensor, gat_col:
     """Everything one rank needs: (bounds, HaloPlan, HaloExchange, DistMultiHop,
     DistGatGraph).  csr_global: P as a sparse CSR tensor; gat_rowptr/gat_col:
     the destination-major CSR of the GAT graph (same sparsity pattern).
-    transport: None (NCCL point-to-point), "peer" (NVLink peer-memory stores,
-    PeerHaloExchange), or a transport object (TorchP2P, StagedGlooP2P, ...).
+    transport: None (NCCL point-to-point), "peer" (NVLink peer-memory stores
+    by a kernel, PeerHaloExchange), "peer-copy" (the same buffers filled by
+    the copy engines), or a transport object (TorchP2P, StagedGlooP2P, ...).
     row_weight: cost of an own row in units of one non-zero (partition_rows)."""
     bounds = partition_rows(csr_global.crow_indices(), world, row_weight)
     plan = HaloPlan(csr_global.crow_indices(), csr_global.col_indices(), bounds, rank)
-    if transport == "peer":
-        exchange = PeerHaloExchange(plan, device)
+    if transport in ("peer", "peer-copy"):
+        exchange = PeerHaloExchange(plan, device, copy="engine" if transport == "peer-copy"
+                                    else "kernel")
     else:
         exchange = HaloExchange(plan, device, transport)
     op = DistMultiHop(csr_global, plan, exchange)

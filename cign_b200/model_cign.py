@@ -38,8 +38,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import fused_clifford_cign_generic, fused_clifford_cign_pack, fused_clifford_pack
-from .collapsed_gat import (attention_logits_through_weight, collapsed_gat_aggregate_first,
-                            collapsed_gat_aggregate_first_lin, collapsed_gat_mean_bias_silu,
+from .collapsed_gat import (collapsed_gat_mean_bias_silu, gat_context, gat_context_lin,
                             gat_silu_add_layernorm)
 from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, fused_dropout_layernorm
 from .fused_gat_sideops import fused_attention_logits
@@ -109,12 +108,8 @@ class GATContext(nn.Module):
         else:
             csr, csc, perm = gat_graph
             x_src = x
-        alpha = attention_logits_through_weight(x_src, self.lin.weight, self.att_src,
-                                                self.att_dst, H)
-        return collapsed_gat_aggregate_first_lin(
-            x_src, attn_row=alpha[:x.size(0), H:].contiguous(),
-            attn_col=alpha[:, :H].contiguous(), weight=self.lin.weight, csr=csr, csc=csc,
-            perm=perm, negative_slope=self.negative_slope, attn_drop=drop)
+        return gat_context_lin(x_src, self.lin.weight, self.att_src, self.att_dst, csr, csc, perm,
+                               self.negative_slope, drop, n_dst=x.size(0))
 
     def forward(self, x: torch.Tensor, gat_graph) -> torch.Tensor:
         H, C = self.heads, self.out_channels
@@ -127,15 +122,10 @@ class GATContext(nn.Module):
             csr, csc, perm = gat_graph
             x_src = x
         if self.aggregate_first and x.size(1) % 4 == 0 and C % 4 == 0:
-            # lin is linear: aggregate x per head, apply lin.weight afterwards.
+            # lin is linear: aggregate x per head, apply lin.weight afterwards;
             # alpha_src[n,h] = <W_h x_n, att_src[h]> = <x_n, W_h^T att_src[h]>.
-            alpha = attention_logits_through_weight(x_src, self.lin.weight, self.att_src,
-                                                    self.att_dst, H)
-            a_src = alpha[:, :H].contiguous()
-            a_dst = alpha[:x.size(0), H:].contiguous()
-            return collapsed_gat_aggregate_first(
-                x_src, attn_row=a_dst, attn_col=a_src, weight=self.lin.weight, bias=self.bias,
-                csr=csr, csc=csc, perm=perm, negative_slope=self.negative_slope, attn_drop=drop)
+            return gat_context(x_src, self.lin.weight, self.att_src, self.att_dst, self.bias, csr,
+                               csc, perm, self.negative_slope, drop, n_dst=x.size(0))
         if partitioned:
             raise NotImplementedError("a partitioned graph needs the aggregate-first GAT form")
         xh = self.lin(x).view(-1, H, C)

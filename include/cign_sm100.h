@@ -298,6 +298,24 @@ CIGN_API int cign_attn_logits_bwd(int64_t n, int32_t heads, int32_t channels,
                          int32_t accumulate, void* ws, size_t ws_bytes,
                          cign_stream_t stream);
 
+/* Attention logits of lin(x) without forming lin(x) (the side op of
+ * fused_gat_sideops.py:50-71 applied to lin(x).view(N, H, C),
+ * generic_engine/model_cign.py:551-567): out[n, j] = <x[n, :], V[j, :]>
+ * for K <= 16 vectors V [K, D] (V = [W_h^T att_src[h] ; W_h^T att_dst[h]]
+ * gives the 2H logits).  fp32, fixed summation order.  D % 4 == 0, x and V
+ * 16-byte aligned.  One read of x. */
+CIGN_API int cign_row_dots_fwd(int64_t n, int64_t d, int32_t k, const float* x,
+                      const float* V, float* out, cign_stream_t stream);
+
+CIGN_API size_t cign_row_dots_bwd_workspace_bytes(int64_t n, int64_t d, int32_t k);
+
+/* grad_x = (accumulate ? grad_x : 0) + grad_out V;  grad_V = grad_out^T x
+ * (chunk partials summed in a fixed order).  grad_out [n, K]. */
+CIGN_API int cign_row_dots_bwd(int64_t n, int64_t d, int32_t k, const float* x,
+                      const float* V, const float* grad_out, float* grad_x,
+                      int32_t accumulate, float* grad_V, void* ws, size_t ws_bytes,
+                      cign_stream_t stream);
+
 /* y = SiLU(mean_h out[n,h,:] + bias).  Replaces head_silu_forward_cuda
  * (fused_gat_sideops_cuda.cu:301-316). */
 CIGN_API int cign_head_mean_bias_silu_fwd(int64_t n, int32_t heads, int32_t channels,
@@ -424,6 +442,15 @@ CIGN_API int cign_ipc_close(void* ptr);
 CIGN_API int cign_halo_push(int32_t n_peers, const float* src, int64_t F, const int64_t* idx,
                             const int64_t* peer_begin, float* const* peer_dst, int64_t total,
                             cign_stream_t stream);
+/* The same copies by the copy engines: with idx, the send rows are first
+ * gathered into `staging` (this GPU's memory, total * F floats); then each
+ * peer's contiguous block goes to peer_dst_host[p] as one cudaMemcpyAsync
+ * on `stream`.  peer_begin_host / peer_dst_host are HOST arrays here.  No SM
+ * time is spent on the transfer itself. */
+CIGN_API int cign_halo_push_copy(int32_t n_peers, const float* src, int64_t F,
+                                 const int64_t* idx, const int64_t* peer_begin_host,
+                                 float* const* peer_dst_host, int64_t total, float* staging,
+                                 cign_stream_t stream);
 
 /* ------------------------------------------------------------ column sum
  * out[j] = sum_i a[i, j] for a row-major [n, c] matrix, in a fixed order

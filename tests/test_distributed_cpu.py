@@ -199,6 +199,14 @@ def _khop_worker(rank, world, port, errors):
                 g = Pt @ g
             want_grad += g
         assert torch.allclose(x_own.grad, want_grad[me.r0:me.r1], atol=1e-5)
+        # the raw forward/backward pair the fused block node calls
+        ys = hop.forward(X[me.r0:me.r1].contiguous(), 3)
+        Y = X
+        for p in (1, 2, 3):
+            Y = P @ Y
+            assert torch.allclose(ys[p - 1], Y[me.r0:me.r1], atol=1e-5), p
+        gx = hop.backward([Gs[p][me.r0:me.r1].contiguous() for p in (1, 2, 3)], 4)
+        assert torch.allclose(gx, want_grad[me.r0:me.r1], atol=1e-5)
         # every rank took the same exchange steps in the same order
         seqs = [None] * world
         dist.all_gather_object(seqs, ex.calls)
@@ -212,7 +220,8 @@ def _khop_worker(rank, world, port, errors):
 
 def test_partitioned_khop_with_a_halo_free_rank_gloo():
     """k-hop forward and backward over three ranks, one of which has no halo
-    columns: results equal the global P^p X and its gradient, and all ranks
+    columns, in the autograd form and as the raw forward/backward pair:
+    results equal the global P^p X and its gradient, and all ranks
     take the same sequence of exchange steps (one collective each on the
     peer-memory transport)."""
     ctx = mp.get_context("spawn")

@@ -17,14 +17,19 @@ Tolerances: with TF32 off, the reference's own model thresholds
 gradients rtol 5e-4 / atol 5e-5) elementwise.  With TF32 on (the bench's
 setting, and the reference's default, train_cign.py:755-768): logits and
 loss within 2e-3 relative (rel-L2).  Parameter gradients within 2e-3, or,
-where TF32 itself moves a gradient further than that, no further from the
-fp32 oracle than the reference's own order of computation under TF32 moves
-it (x 1.5): lin(x) as a TF32 GEMM, the attention logits and the collapsed
-GAT in fp32 (CompatibleCollapsedFusedGATConv.forward, model_cign.py:524-570),
-i.e. this model with GATContext.aggregate_first off, same parameters and
-seeds.  The GAT parameters' gradients are sums over all nodes of nearly
-cancelling terms (the softmax backward), so TF32-rounded operands anywhere
-upstream move them by about 1e-2 in either order.
+where TF32 itself moves a gradient further than that, within 2.5x of how far
+the reference's own order of computation under TF32 moves it from the fp32
+oracle: lin(x) as a TF32 GEMM, the attention logits and the collapsed GAT in
+fp32 (CompatibleCollapsedFusedGATConv.forward, model_cign.py:524-570), i.e.
+this model with GATContext.aggregate_first off, same parameters and seeds.
+The GAT parameters' gradients are sums over all nodes of nearly cancelling
+terms (the softmax backward), so TF32-rounded operands anywhere upstream
+move them by 1e-2 to 3e-2 in either order, and which order lands closer
+depends on the parameter state: over five parameter states (three initial,
+two after warm-up steps) the ratio of this model's error to the reference
+order's ranged from 0.39 to 1.88 for these gradients, with identical errors
+from the graph-captured and the eager step.  A wrong gradient is off by
+order 1.
 """
 import copy
 
@@ -144,7 +149,7 @@ def test_cfg2_graphed_training_step_vs_oracle(cuda, monkeypatch, tf32):
                            for k, (a, b) in sorted(errs.items(), key=lambda kv: -kv[1][0]))
         assert rel_l2(logits, ref_logits) <= 2e-3, (rel_l2(logits, ref_logits), report)
         assert abs(loss - float(ref_loss)) <= 2e-3 * abs(float(ref_loss)), report
-        bad = {k: a for k, (a, b) in errs.items() if a > max(2e-3, 1.5 * b)}
+        bad = {k: a for k, (a, b) in errs.items() if a > max(2e-3, 2.5 * b)}
         assert not bad, report
     else:
         torch.testing.assert_close(logits, ref_logits.detach(), rtol=2e-4, atol=2e-5)

@@ -1,5 +1,6 @@
 """PeerHaloExchange (halo rows stored into the peers' IPC-mapped buffers by
-cign_halo_push) against the NCCL point-to-point exchange: the same extended
+cign_halo_push, or copied there by the copy engines with
+cign_halo_push_copy) against the NCCL point-to-point exchange: the same extended
 tensors forward and the same gathered gradients backward, and the same
 halo rows / returned gradients through the asynchronous halo-only path
 (side-stream pushes), over three steps (buffers reused per step).  Needs 2
@@ -23,7 +24,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, errors):
+def _worker(rank, world, port, errors, copy):
     try:
         from cign_b200 import synth
         from cign_b200.distributed import (HaloExchange, HaloPlan, PeerHaloExchange, halo_gather,
@@ -42,7 +43,7 @@ def _worker(rank, world, port, errors):
         b = partition_rows(crow, world)
         plan = HaloPlan(crow, col, b, rank)
         ref = HaloExchange(plan, dev)
-        peer = PeerHaloExchange(plan, dev)
+        peer = PeerHaloExchange(plan, dev, copy=copy)
         for step in range(3):
             peer.begin_step()
             for F in (64, 1024):
@@ -79,11 +80,12 @@ def _worker(rank, world, port, errors):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_exchange_matches_nccl_p2p(cuda):
+@pytest.mark.parametrize("copy", ["kernel", "engine"])
+def test_peer_exchange_matches_nccl_p2p(cuda, copy):
     ctx = mp.get_context("spawn")
     errors = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, errors)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, errors, copy)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
