@@ -107,14 +107,13 @@ def step_roofline_items(cfg, nnz, nnz_g):
     add("input SiLU mix", 1, 12 * N * D)
     # forward, per block
     add("dropout-LN fwd", L, 8 * N * D + 8 * N)
-    add("GAT logits (fp32 GEMM)", L, *gemm(N, 2 * H, D))
+    add("GAT logits (row dots of x with W_h^T att)", L, gemm(N, 2 * H, D)[0])
     add("GAT aggregate fwd", L, algorithmic_bytes("gat_agg_fwd", N, nnz, H=H, D=D, nnz_g=nnz_g))
     add("GAT z.M (GEMM)", L, *gemm(N, D, HD))
     add("GAT bias+SiLU + add-LN fwd", L, 16 * N * D + 8 * N)
     add("[H|C] concat", L, 16 * N * D)
     add("k-hop SpMM fwd hop", L * K, algorithmic_bytes("spmm", N, nnz, F=F2))
-    add("hop gate fwd", L, 8 * N * D + 4 * N * K)
-    add("pack fwd", L, algorithmic_bytes("pack_fwd", N, nnz, K=K, D=D))
+    add("hop gate + pack fwd", L, algorithmic_bytes("gate_pack_fwd", N, nnz, K=K, D=D))
     add("proj (GEMM)", L, *gemm(N, D, 2 * K * D))
     add("dropout-gamma-residual fwd", L, 12 * N * D)
     # forward, net output and loss
@@ -143,8 +142,8 @@ def step_roofline_items(cfg, nnz, nnz_g):
                                                    nnz_g=nnz_g))
     add("GAT lin wgrad (GEMM)", L, *gemm(HD, D, N))
     add("GAT input dgrad (GEMM)", L, *gemm(N, D, HD))
-    add("GAT logits bwd (fp32 GEMMs)", L, 2 * gemm(N, D, 2 * H)[0], 2 * gemm(N, D, 2 * H)[1])
-    add("H_norm gradient sums", 3 * L, 12 * N * D)
+    add("GAT logits bwd (row dots, added into grad x)", L, 12 * N * D + 8 * N * H)
+    add("H_norm gradient sums", 2 * L, 12 * N * D)
     add("dropout-LN bwd", L, 12 * N * D + 8 * N)
     # backward, net input
     add("input SiLU mix bwd", 1, 20 * N * D)
@@ -360,6 +359,8 @@ def algorithmic_bytes(kind, N, nnz, F=0, H=0, C=0, K=0, D=0, nnz_g=0):
                 + 4 * N * C + 4 * C)
     if kind == "pack_fwd":
         return 8 * N * D + 8 * K * N * D + 4 * N * K + 8 * K * N * D
+    if kind == "gate_pack_fwd":  # pack_fwd with alpha written instead of read, + gate W and b
+        return 8 * N * D + 8 * K * N * D + 4 * N * K + 8 * K * N * D + 8 * K * D + 4 * K
     if kind == "pack_bwd":
         return 8 * K * N * D + 8 * N * D + 8 * K * N * D + 4 * N * K + 8 * N * D + 8 * K * N * D + 4 * N * K
     raise ValueError(kind)
@@ -410,7 +411,10 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device, pack_proj_in_step=F
     Cn = torch.randn(N, D, device=device, generator=g)
     props = [torch.randn(N, 2 * D, device=device, generator=g) for _ in range(K)]
     alpha = torch.softmax(torch.randn(N, K, device=device, generator=g), -1)
-    t_pack_f = time_launches(lambda: _pack.pack_forward(Hn, Cn, props, alpha, 1, 0, 0), 20, stream)
+    gw = torch.randn(K, 2 * D, device=device, generator=g) / (2 * D) ** 0.5
+    gb = torch.zeros(K, device=device)
+    t_pack_f = time_launches(lambda: _pack.gate_pack_forward(Hn, Cn, props, gw, gb, 1, 1, 0, 0), 20,
+                             stream)
     go = torch.randn(N, 2 * K * D, device=device, generator=g)
     t_pack_b = time_launches(lambda: _pack.pack_backward(go, Hn, Cn, props, alpha, 1, 0, 0, True),
                              20, stream)
@@ -431,7 +435,7 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device, pack_proj_in_step=F
                                                         nnz_g=nnz_g)),
         "pack_proj_tcgen05_fwd": (t_pp, L if pack_proj_in_step else 0,
                                   algorithmic_bytes("pack_proj", N, nnz, K=K, D=D, C=D)),
-        "pack_fwd": (t_pack_f, L, algorithmic_bytes("pack_fwd", N, nnz, K=K, D=D)),
+        "gate_pack_fwd": (t_pack_f, L, algorithmic_bytes("gate_pack_fwd", N, nnz, K=K, D=D)),
         "pack_bwd": (t_pack_b, L, algorithmic_bytes("pack_bwd", N, nnz, K=K, D=D)),
     }
     out = {}

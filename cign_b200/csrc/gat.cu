@@ -1988,14 +1988,114 @@ struct AggCfg {
   static constexpr size_t kSmem = static_cast<size_t>(kGroups) * kAggStages * kTile * 4;
 };
 
-// MODE 0 (forward, CSR rows of `ptr`/`idx`): out = Z [N, H, D] from X = src.
-//   Light rows compute their per-head max / exp-sum inline (written by the
-//   blockIdx.y == 0 tile); hub-row segments read them from emax/esum and
-//   write partials [n_seg, H, D].
+// Edge weights w[e, h] of the aggregate-first form (edge id e in CSR order),
+// computed once per edge and head and read by the aggregation kernels for
+// every feature tile.  Work items as in gat_agg_kernel's forward (one warp
+// per row of at most kSegLen edges or per hub-row segment, lane k = edge k).
+// STATS (forward): light rows compute their per-head max / exp-sum here with
+// the warp reductions and write emax / esum; hub-row segments read them
+// (gat_hub_stats_kernel ran first).  !STATS (backward): every row reads the
+// forward's emax / esum.  The weights equal the ones the aggregation used to
+// form inline, bit for bit (same reductions, same edge_weight).
+template <bool STATS>
+__global__ void __launch_bounds__(kThreads)
+gat_edge_weights_kernel(int n, int H, const int* __restrict__ rowptr, const int* __restrict__ col,
+                        const int* __restrict__ seg_row, const int* __restrict__ seg_begin,
+                        const int* __restrict__ seg_end, int n_seg, int seg_blocks,
+                        const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                        float* __restrict__ emax, float* __restrict__ esum, float slope, float p,
+                        Seed seed_in, float* __restrict__ wts) {
+  const uint64_t seed = seed_in;
+  const int lane = threadIdx.x & 31;
+  const int group = threadIdx.x >> 5;
+  int64_t target;
+  int e0, e1;
+  bool seg;
+  if (static_cast<int>(blockIdx.x) < seg_blocks) {
+    const int64_t item = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + group;
+    if (item >= n_seg) return;
+    target = seg_row[item];
+    e0 = seg_begin[item];
+    e1 = seg_end[item];
+    seg = true;
+  } else {
+    target = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
+    if (target >= n) return;
+    e0 = rowptr[target];
+    e1 = rowptr[target + 1];
+    if (e1 - e0 > kSegLen) return;  // hub: done by its segments
+    seg = false;
+  }
+  const int k = e0 + lane;
+  const bool valid = k < e1;
+  const int other = valid ? __ldg(col + k) : 0;
+  // kAggHB heads per pass, their reductions interleaved (each head's butterfly
+  // is the one group_max / group_sum runs, so the values are the same)
+  for (int h0 = 0; h0 < H; h0 += kAggHB) {
+    float ad[kAggHB], lg[kAggHB], m[kAggHB], sm[kAggHB];
+#pragma unroll
+    for (int hh = 0; hh < kAggHB; ++hh) {
+      const int h = h0 + hh < H ? h0 + hh : H - 1;
+      ad[hh] = __ldg(attn_row + target * H + h);
+      const float ac = valid ? __ldg(attn_col + static_cast<int64_t>(other) * H + h) : 0.0f;
+      lg[hh] = leaky_f(ad[hh] + ac, slope);
+    }
+    if (seg || !STATS) {
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) {
+        const int h = h0 + hh < H ? h0 + hh : H - 1;
+        m[hh] = emax[target * H + h];
+        sm[hh] = esum[target * H + h];
+      }
+    } else {
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) m[hh] = valid ? fmaxf(kNegInit, lg[hh]) : kNegInit;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int hh = 0; hh < kAggHB; ++hh)
+          m[hh] = fmaxf(m[hh], __shfl_xor_sync(kFullMask, m[hh], o, 32));
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) sm[hh] = valid ? expf(lg[hh] - m[hh]) : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int hh = 0; hh < kAggHB; ++hh) sm[hh] += __shfl_xor_sync(kFullMask, sm[hh], o, 32);
+      if (lane == 0) {
+#pragma unroll
+        for (int hh = 0; hh < kAggHB; ++hh) {
+          if (h0 + hh >= H) break;
+          emax[target * H + h0 + hh] = m[hh];
+          esum[target * H + h0 + hh] = sm[hh];
+        }
+      }
+    }
+    if (valid) {
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) {
+        const int h = h0 + hh;
+        if (h >= H) break;
+        const uint64_t idx = static_cast<uint64_t>(k) * H + h;
+        const bool keep = (p <= 0.0f) || gat_keep(seed, idx, p);
+        float w = 0.0f;
+        if (keep && sm[hh] > 0.0f) {  // edge_weight's expression
+          w = expf(lg[hh] - m[hh]) / sm[hh];
+          if (p > 0.0f) w /= (1.0f - p);
+        }
+        wts[static_cast<int64_t>(k) * H + h] = w;
+      }
+    }
+  }
+}
+
+// MODE 0 (forward, CSR rows of `ptr`/`idx`): out = Z [N, H, D] from X = src;
+//   hub-row segments write partials [n_seg, H, D].
 // MODE 1 (backward K2, CSC columns: ptr = colptr, idx = row, perm):
 //   out = grad_feat [N, H, D] from src = g_pre [N, D], scaled by 1/H; the
 //   y == 0 tile also sums glog over the column into gcol (hub segments:
 //   into pcol).
+// Both read the edge weights from wts [nnz, H] (gat_edge_weights_kernel),
+// indexed by the CSR edge id (perm[k] for a CSC position k).
 // The neighbour rows are gathered by cp.async into a lane-private ring of
 // kAggStages shared-memory slots per warp: lane l copies, and later reads,
 // only its own 16-byte slices, so no warp synchronisation is needed, and
@@ -2009,14 +2109,11 @@ __global__ void __launch_bounds__(kThreads, ONE_PASS ? 4 : 1)  // <= 64 register
 gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* __restrict__ idx,
                const int* __restrict__ perm, const int* __restrict__ seg_row,
                const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
-               int seg_blocks, const float* __restrict__ attn_row,
-               const float* __restrict__ attn_col, float* __restrict__ emax,
-               float* __restrict__ esum, const float* __restrict__ src, float slope, float p,
-               Seed seed_in, float* __restrict__ out, float* __restrict__ partial,
+               int seg_blocks, const float* __restrict__ wts, const float* __restrict__ src,
+               float* __restrict__ out, float* __restrict__ partial,
                const float* __restrict__ glog, float* __restrict__ gcol,
                float* __restrict__ pcol) {
   extern __shared__ float4 agg_ring[];
-  const uint64_t seed = seed_in;
   using Cfg = AggCfg<VPL>;
   const int lane = threadIdx.x & 31;
   const int group = threadIdx.x >> 5;
@@ -2053,15 +2150,21 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
     other = __ldg(idx + k);
     if (MODE == 1) e = __ldg(perm + k);
   }
-  // copies of edge t's tile slices (lanes past D copy nothing and store nothing)
-  auto issue = [&](int t) {
-    const float* xr = src + static_cast<int64_t>(__shfl_sync(kFullMask, other, t)) * D;
-    const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
+  // this lane's feature offsets in the tile (lanes past D copy and store nothing)
+  int64_t foff[VPL];
+  bool fin[VPL];
 #pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
-      if (fi < D) cp_async16_s(slot + q * 32 * 16, xr + fi);
-    }
+  for (int q = 0; q < VPL; ++q) {
+    foff[q] = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+    fin[q] = foff[q] < D;
+  }
+  // copies of edge t's tile slices into ring stage `stage`
+  auto issue = [&](int t, int stage) {
+    const float* xr = src + static_cast<int64_t>(__shfl_sync(kFullMask, other, t)) * D;
+    const uint32_t slot = my_ring + static_cast<uint32_t>(stage * VPL * 32 * 16);
+#pragma unroll
+    for (int q = 0; q < VPL; ++q)
+      if (fin[q]) cp_async16_s(slot + q * 32 * 16, xr + foff[q]);
   };
   const float scale = MODE == 1 ? 1.0f / static_cast<float>(H) : 1.0f;
   const int64_t HD = static_cast<int64_t>(H) * D;
@@ -2069,7 +2172,7 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
   for (int h0 = 0; h0 < (ONE_PASS ? 1 : H); h0 += kAggHB) {
 #pragma unroll
     for (int t = 0; t < kAggStages; ++t) {
-      if (t < cnt) issue(t);
+      if (t < cnt) issue(t, t);
       cp_async_commit();
     }
     float w[kAggHB];
@@ -2078,28 +2181,8 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
       const int h = h0 + hh;
       w[hh] = 0.0f;
       if (h >= H) continue;
-      if (MODE == 0) {
-        const float ad = __ldg(attn_row + target * H + h);
-        const float ac = valid ? __ldg(attn_col + static_cast<int64_t>(other) * H + h) : 0.0f;
-        float m, ssum;
-        if (seg) {
-          m = emax[target * H + h];
-          ssum = esum[target * H + h];
-        } else {
-          m = group_max<32>(valid ? fmaxf(kNegInit, leaky_f(ad + ac, slope)) : kNegInit, kFullMask);
-          ssum = group_sum<32>(valid ? expf(leaky_f(ad + ac, slope) - m) : 0.0f, kFullMask);
-          if (blockIdx.y == 0 && lane == 0) {
-            emax[target * H + h] = m;
-            esum[target * H + h] = ssum;
-          }
-        }
-        if (valid) w[hh] = edge_weight(ad, ac, m, ssum, slope, p, seed, static_cast<uint64_t>(e) * H + h);
-      } else {
-        if (valid) {
-          const int64_t ih = static_cast<int64_t>(other) * H + h;
-          w[hh] = edge_weight(__ldg(attn_row + ih), __ldg(attn_col + target * H + h), emax[ih],
-                              esum[ih], slope, p, seed, static_cast<uint64_t>(e) * H + h) * scale;
-        }
+      if (valid) w[hh] = __ldg(wts + e * H + h) * scale;
+      if (MODE == 1) {
         if (blockIdx.y == 0) {
           const float gsum = group_sum<32>(valid ? glog[e * H + h] : 0.0f, kFullMask);
           if (lane == 0) {
@@ -2114,20 +2197,27 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
     for (int hh = 0; hh < kAggHB; ++hh)
 #pragma unroll
       for (int q = 0; q < VPL; ++q) acc[hh][q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int t = 0; t < cnt; ++t) {
-      cp_async_wait<kAggStages - 1>();  // edge t's copies have landed
-      const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
-      float4 xv[VPL];
+    // edge t sits in ring stage t % kAggStages: the loop runs kAggStages
+    // edges per pass so that every stage's shared address is a constant
+    for (int t0 = 0; t0 < cnt; t0 += kAggStages) {
 #pragma unroll
-      for (int q = 0; q < VPL; ++q) xv[q] = lds_f4(slot + q * 32 * 16);
+      for (int u = 0; u < kAggStages; ++u) {
+        const int t = t0 + u;
+        if (t >= cnt) break;
+        cp_async_wait<kAggStages - 1>();  // edge t's copies have landed
+        const uint32_t slot = my_ring + static_cast<uint32_t>(u * VPL * 32 * 16);
+        float4 xv[VPL];
 #pragma unroll
-      for (int hh = 0; hh < kAggHB; ++hh) {
-        const float wv = __shfl_sync(kFullMask, w[hh], t);
+        for (int q = 0; q < VPL; ++q) xv[q] = lds_f4(slot + q * 32 * 16);
 #pragma unroll
-        for (int q = 0; q < VPL; ++q) vfma(acc[hh][q], wv, xv[q]);
+        for (int hh = 0; hh < kAggHB; ++hh) {
+          const float wv = __shfl_sync(kFullMask, w[hh], t);
+#pragma unroll
+          for (int q = 0; q < VPL; ++q) vfma(acc[hh][q], wv, xv[q]);
+        }
+        if (t + kAggStages < cnt) issue(t + kAggStages, u);  // into the stage just read
+        cp_async_commit();
       }
-      if (t + kAggStages < cnt) issue(t + kAggStages);  // into the slot just read
-      cp_async_commit();
     }
     cp_async_wait<0>();
     float* dst = seg ? partial + item * HD : out + target * HD;
@@ -2135,10 +2225,8 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
     for (int hh = 0; hh < kAggHB; ++hh) {
       if (h0 + hh >= H) break;
 #pragma unroll
-      for (int q = 0; q < VPL; ++q) {
-        const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
-        if (fi < D) st_vec(dst + static_cast<int64_t>(h0 + hh) * D + fi, acc[hh][q]);
-      }
+      for (int q = 0; q < VPL; ++q)
+        if (fin[q]) st_vec(dst + static_cast<int64_t>(h0 + hh) * D + foff[q], acc[hh][q]);
     }
   }
 }
@@ -2444,10 +2532,26 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
   }
 }
 
+// The edge weights [nnz, H] (CSR edge order) of every row item of the plan.
+template <bool STATS>
+int launch_edge_weights(const cign_gat_plan* pl, int H, const float* attn_row,
+                        const float* attn_col, float* emax, float* esum, float slope, float p,
+                        Seed seed, float* wts, cudaStream_t s) {
+  const SegList& rs = pl->rows;
+  const int64_t seg_blocks = (rs.n_seg + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t grid = seg_blocks + (pl->n + kThreads / 32 - 1) / (kThreads / 32);
+  CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "gat edge weights: grid too large");
+  gat_edge_weights_kernel<STATS><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+      static_cast<int>(pl->n), H, pl->rowptr, pl->col, rs.seg_row(), rs.seg_begin(),
+      rs.seg_end(), static_cast<int>(rs.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
+      emax, esum, slope, p, seed, wts);
+  CIGN_CHECK_LAUNCH("gat_edge_weights_kernel");
+  return CIGN_OK;
+}
+
 template <int VPL, int MODE>
 int launch_agg(const cign_gat_plan* pl, const SegList& sl, int H, int64_t D, const int* ptr,
-               const int* idx, const int* perm, const float* attn_row, const float* attn_col,
-               float* emax, float* esum, const float* src, float slope, float p, Seed seed,
+               const int* idx, const int* perm, const float* wts, const float* src,
                float* out, float* partial, const float* glog, float* gcol, float* pcol,
                cudaStream_t s) {
   using Cfg = AggCfg<VPL>;
@@ -2461,13 +2565,13 @@ int launch_agg(const cign_gat_plan* pl, const SegList& sl, int H, int64_t D, con
   if (H <= kAggHB)
     gat_agg_kernel<VPL, MODE, true><<<g, kThreads, Cfg::kSmem, s>>>(
         static_cast<int>(targets), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(),
-        sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row,
-        attn_col, emax, esum, src, slope, p, seed, out, partial, glog, gcol, pcol);
+        sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), wts, src, out,
+        partial, glog, gcol, pcol);
   else
     gat_agg_kernel<VPL, MODE, false><<<g, kThreads, Cfg::kSmem, s>>>(
         static_cast<int>(targets), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(),
-        sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row,
-        attn_col, emax, esum, src, slope, p, seed, out, partial, glog, gcol, pcol);
+        sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), wts, src, out,
+        partial, glog, gcol, pcol);
   CIGN_CHECK_LAUNCH("gat_agg_kernel");
   return launch_seg_combine(sl, H, D, partial, MODE == 1 ? pcol : nullptr, out,
                             MODE == 1 ? gcol : nullptr, s);
@@ -2476,7 +2580,7 @@ int launch_agg(const cign_gat_plan* pl, const SegList& sl, int H, int64_t D, con
 // aggregate-first workspace: hub partials [max(n_seg rows, n_seg cols), H*D]
 // | column-hub logit partials [n_seg cols, H] | grad_logit [nnz, H]
 struct AggLayout {
-  size_t partial, pcol, glog, total;
+  size_t partial, pcol, glog, wts, total;
 };
 AggLayout agg_layout(const cign_gat_plan* pl, int H, int64_t D, int64_t C) {
   AggLayout L;
@@ -2485,7 +2589,8 @@ AggLayout agg_layout(const cign_gat_plan* pl, int H, int64_t D, int64_t C) {
   L.partial = 0;
   L.pcol = rnd(part * H * sizeof(float));
   L.glog = L.pcol + rnd(static_cast<size_t>(pl->cols.n_seg) * H * sizeof(float));
-  L.total = L.glog + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float)) + 256;
+  L.wts = L.glog + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float));
+  L.total = L.wts + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float)) + 256;
   return L;
 }
 
@@ -2756,14 +2861,16 @@ int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const 
   if (pl->n == 0) return CIGN_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + L.partial);
+  float* wts = reinterpret_cast<float*>(static_cast<char*>(ws) + L.wts);
   rc = launch_hub_stats(pl, heads, attn_row, attn_col, negative_slope, edge_max, edge_sum, s);
   if (rc) return rc;
+  rc = launch_edge_weights<true>(pl, heads, attn_row, attn_col, edge_max, edge_sum,
+                                 negative_slope, attn_drop, seed, wts, s);
+  if (rc) return rc;
   if (dim <= 128)
-    return launch_agg<1, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
-                            attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
+    return launch_agg<1, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, wts, x, z,
                             partial, nullptr, nullptr, nullptr, s);
-  return launch_agg<2, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, attn_row,
-                          attn_col, edge_max, edge_sum, x, negative_slope, attn_drop, seed, z,
+  return launch_agg<2, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, wts, x, z,
                           partial, nullptr, nullptr, nullptr, s);
 }
 
@@ -2857,16 +2964,18 @@ int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_
                            nullptr, negative_slope, attn_drop, seed, nullptr, glog, grad_attn_row,
                            s);
   if (rc) return rc;
-  // K2: grad_feat[j,h,:] = sum_i w g_pre[i,:] / H and grad_attn_col (columns)
-  float* emax = const_cast<float*>(edge_max);
-  float* esum = const_cast<float*>(edge_sum);
+  // K2: grad_feat[j,h,:] = sum_i w g_pre[i,:] / H and grad_attn_col (columns),
+  // with the edge weights formed once per edge from the forward's statistics
+  float* wts = reinterpret_cast<float*>(w + L.wts);
+  rc = launch_edge_weights<false>(pl, heads, attn_row, attn_col, const_cast<float*>(edge_max),
+                                  const_cast<float*>(edge_sum), negative_slope, attn_drop, seed,
+                                  wts, s);
+  if (rc) return rc;
   if (channels <= 128)
-    return launch_agg<1, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm,
-                            attn_row, attn_col, emax, esum, grad_pre, negative_slope, attn_drop,
-                            seed, grad_feat, partial, glog, grad_attn_col, pcol, s);
-  return launch_agg<2, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm, attn_row,
-                          attn_col, emax, esum, grad_pre, negative_slope, attn_drop, seed,
-                          grad_feat, partial, glog, grad_attn_col, pcol, s);
+    return launch_agg<1, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
+                            grad_pre, grad_feat, partial, glog, grad_attn_col, pcol, s);
+  return launch_agg<2, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
+                          grad_pre, grad_feat, partial, glog, grad_attn_col, pcol, s);
 }
 
 }  // extern "C"

@@ -72,22 +72,36 @@ row_dots_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
   const int64_t r1 = r0 + rpc < n ? r0 + rpc : n;
   if (cv) {
-    for (int64_t row = r0 + warp; row < r1; row += kThreads / 32) {
-      const float4 xv = ld_vec<4>(x + row * D + c);
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    // kRowBatch rows per pass with all their loads issued first: the rows
+    // a warp walks are independent, so their latencies overlap; partials
+    // still accumulate row by row in increasing order.
+    constexpr int kRowBatch = 4;
+    constexpr int64_t kStride = kThreads / 32;
+    for (int64_t base = r0 + warp; base < r1; base += kRowBatch * kStride) {
+      float4 xv[kRowBatch], t[kRowBatch];
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const float gk = __ldg(g + row * K + k);
-        vfma(o, gk, v[k]);
-        vfma(a[k], gk, xv);
+      for (int b = 0; b < kRowBatch; ++b) {
+        const int64_t row = base + b * kStride;
+        if (row < r1) {
+          xv[b] = ld_vec<4>(x + row * D + c);
+          t[b] = accumulate ? ld_vec<4>(gx + row * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
-      // existing gradient first, then this op's part
-      if (accumulate) {
-        float4 t = ld_vec<4>(gx + row * D + c);
-        vadd(t, o);
-        o = t;
+#pragma unroll
+      for (int b = 0; b < kRowBatch; ++b) {
+        const int64_t row = base + b * kStride;
+        if (row >= r1) break;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const float gk = __ldg(g + row * K + k);
+          vfma(o, gk, v[k]);
+          vfma(a[k], gk, xv[b]);
+        }
+        // existing gradient first, then this op's part
+        vadd(t[b], o);
+        st_vec(gx + row * D + c, t[b]);
       }
-      st_vec(gx + row * D + c, o);
     }
   }
   // fixed-order sum of the warps' partials, one k at a time
