@@ -43,16 +43,16 @@ __device__ __forceinline__ float gsum(float v, unsigned gmask) {
   return v;
 }
 
-// Rows per chunk of the parameter-gradient reductions: a multiple of 32
-// (so every group layout divides it) giving at most ~4 chunks per SM.
-// Row chunks of the parameter-gradient reduction: at most this many (four
-// per SM), each a multiple of 32 rows.
-constexpr int64_t kLnChunkTarget = 592;
+// Row chunks of the parameter-gradient reductions (one CTA each): at most
+// this many -- two per SM, the residency of the ~128-register backward
+// kernels, so that all chunks run in one wave (a second, partial wave left
+// most SMs idle) -- each a multiple of 8 rows.
+constexpr int64_t kLnChunkTarget = 296;
 int64_t rows_per_chunk(int64_t n) {
   const int64_t target = kLnChunkTarget;
   int64_t r = (n + target - 1) / target;
-  r = std::max<int64_t>(r, 32);
-  return (r + 31) / 32 * 32;
+  r = std::max<int64_t>(r, 8);
+  return (r + 7) / 8 * 8;
 }
 int64_t num_chunks(int64_t n) { return (n + rows_per_chunk(n) - 1) / rows_per_chunk(n); }
 
@@ -154,9 +154,11 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
   }
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
   const int64_t r1 = (r0 + rpc < n) ? (r0 + rpc) : n;
+  static_assert(VPL * VEC <= 32, "one keep bit per element of a lane's row slice");
   for (int64_t row = r0 + group; row < r1; row += Cfg::kGroups) {
     const float mu = mean[row], rs = rstd[row];
     V xh[VPL], dn[VPL];
+    uint32_t keep_bits = 0;  // MODE 0: the dropout keep bits, hashed once per element
     float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
@@ -174,6 +176,7 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
           float qv;
           if (MODE == 0) {
             const bool keep = block_keep(seed, static_cast<uint64_t>(row * D + d + j), p);
+            keep_bits |= static_cast<uint32_t>(keep) << (k * VEC + j);
             qv = keep ? vel(xv, j) * scale : 0.0f;
           } else {
             qv = vel(xv, j) + vel(x2v, j);
@@ -200,7 +203,7 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
         for (int j = 0; j < VEC; ++j) {
           const float dq = (rs / Df) * (Df * vel(dn[k], j) - s1 - vel(xh[k], j) * s2);
           if (MODE == 0) {
-            const bool keep = block_keep(seed, static_cast<uint64_t>(row * D + d + j), p);
+            const bool keep = (keep_bits >> (k * VEC + j)) & 1u;
             vel(o, j) = keep ? dq * scale : 0.0f;
           } else {
             vel(o, j) = dq;
@@ -804,9 +807,9 @@ int cign_block_dropout_mask(int64_t count, float p, uint64_t seed_value, const u
 // parameter-gradient reduction lives in the fixed array below instead of a
 // caller-provided buffer.
 //
-// The array holds 592 row chunks x 1024 columns x 2 partial sums (4.6 MiB);
+// The array holds 296 row chunks x 1024 columns x 2 partial sums (2.3 MiB);
 // every GPU on which this library is loaded keeps it for the life of the
-// process.  592 is the largest chunk count rows_per_chunk() can produce, so
+// process.  296 is the largest chunk count rows_per_chunk() can produce, so
 // the limit is the hidden width: D <= 1024 (D <= 256 unless D % 4 == 0 and
 // the tensors are 16-byte aligned), the same as the workspace version.
 //
@@ -819,7 +822,7 @@ int cign_block_dropout_mask(int64_t count, float p, uint64_t seed_value, const u
 // stream capture.  The dropout seed is a host value only (no device seed
 // slot, unlike cign_dropout_ln_bwd): a captured graph that replays this call
 // replays the same mask.
-constexpr int64_t kStaticLnChunks = 592;
+constexpr int64_t kStaticLnChunks = 296;
 constexpr int64_t kStaticLnMaxD = 1024;
 static_assert(kStaticLnChunks == kLnChunkTarget,
               "the static scratch must hold the largest chunk count rows_per_chunk() gives");

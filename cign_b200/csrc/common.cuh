@@ -141,13 +141,16 @@ __host__ __device__ __forceinline__ bool gat_keep(uint64_t seed, uint64_t idx,
   return u > p;
 }
 // Block-op dropout (53-bit double uniform): keep iff (r >> 11) * 2^-53 >= p.
-// (fused_block_ops.py:15, dropout_keep)
+// (fused_block_ops.py:15, dropout_keep)  t = r >> 11 < 2^53, so t * 2^-53 is
+// exact in double and so is double(p) * 2^53: the test is the integer
+// comparison t >= ceil(double(p) * 2^53), with the threshold loop-invariant.
+__host__ __device__ __forceinline__ uint64_t block_keep_threshold(float p) {
+  return static_cast<uint64_t>(ceil(static_cast<double>(p) * 9007199254740992.0));
+}
 __host__ __device__ __forceinline__ bool block_keep(uint64_t seed, uint64_t idx,
                                                     float p) {
   if (p <= 0.0f) return true;
-  const uint64_t r = dropout_hash(seed, idx);
-  const double u = static_cast<double>(r >> 11) * (1.0 / 9007199254740992.0);
-  return u >= static_cast<double>(p);
+  return (dropout_hash(seed, idx) >> 11) >= block_keep_threshold(p);
 }
 
 // ---------------------------------------------------------------- warp

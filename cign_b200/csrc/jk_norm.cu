@@ -27,6 +27,31 @@ constexpr int kJkRowsPerChunk = 64;
 struct SegPtrs { const float* p[kJkMaxSeg]; };
 struct SegOut { float* p[kJkMaxSeg]; };
 
+// Segment `seg`'s base pointer by a chain of selects: indexing the parameter
+// array with a run-time index would copy it to local memory.
+template <typename P>
+__device__ __forceinline__ auto seg_base(const P& s, int seg) -> decltype(s.p[0]) {
+  auto q = s.p[0];
+#pragma unroll
+  for (int i = 1; i < kJkMaxSeg; ++i)
+    if (seg == i) q = s.p[i];
+  return q;
+}
+
+// Walks a lane's float4 columns c = lane, lane + 32, ... of the row as
+// (segment, column within the segment) without dividing by the segment width.
+struct SegCursor {
+  int seg;
+  int cs;
+  __device__ __forceinline__ SegCursor(int lane, int wq) : seg(0), cs(lane) {
+    while (cs >= wq) { cs -= wq; ++seg; }
+  }
+  __device__ __forceinline__ void next(int wq) {
+    cs += 32;
+    while (cs >= wq) { cs -= wq; ++seg; }
+  }
+};
+
 template <int NCH>
 __global__ void __launch_bounds__(kJkThreads)
 jk_ln_fwd_kernel(int64_t n, int64_t W, int64_t D, SegPtrs segs, const float* __restrict__ w,
@@ -35,19 +60,20 @@ jk_ln_fwd_kernel(int64_t n, int64_t W, int64_t D, SegPtrs segs, const float* __r
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kJkWarps + (threadIdx.x >> 5);
   if (row >= n) return;
-  const int64_t wq = W / 4;  // float4 chunks per segment
+  const int wq = static_cast<int>(W / 4);  // float4 chunks per segment
   const int64_t dq = D / 4;
   float4 x[NCH];
   float s = 0.0f;
+  SegCursor cur(lane, wq);
 #pragma unroll
   for (int k = 0; k < NCH; ++k) {
     const int64_t c = lane + 32 * k;
     x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (c < dq) {
-      const int seg = static_cast<int>(c / wq);
-      x[k] = __ldg(reinterpret_cast<const float4*>(segs.p[seg] + row * W) + (c - seg * wq));
+      x[k] = __ldg(reinterpret_cast<const float4*>(seg_base(segs, cur.seg) + row * W) + cur.cs);
       s += (x[k].x + x[k].y) + (x[k].z + x[k].w);
     }
+    cur.next(wq);
   }
   const float mu = warp_sum(s) / static_cast<float>(D);
   float v = 0.0f;
@@ -91,17 +117,17 @@ jk_ln_bwd_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy, 
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kJkWarps + (threadIdx.x >> 5);
   if (row >= n) return;
-  const int64_t wq = W / 4;
+  const int wq = static_cast<int>(W / 4);
   const int64_t dq = D / 4;
   const float mu = mean[row], rs = rstd[row];
   float s1 = 0.0f, s2 = 0.0f;
+  SegCursor cur(lane, wq);
 #pragma unroll 4
-  for (int k = 0; k < NCH; ++k) {
+  for (int k = 0; k < NCH; ++k, cur.next(wq)) {
     const int64_t c = lane + 32 * k;
     if (c < dq) {
-      const int seg = static_cast<int>(c / wq);
       const float4 xv =
-          __ldg(reinterpret_cast<const float4*>(segs.p[seg] + row * W) + (c - seg * wq));
+          __ldg(reinterpret_cast<const float4*>(seg_base(segs, cur.seg) + row * W) + cur.cs);
       const float4 gv = __ldg(reinterpret_cast<const float4*>(gy + row * D) + c);
       const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + c);
       const float d0 = gv.x * wv.x, d1 = gv.y * wv.y, d2 = gv.z * wv.z, d3 = gv.w * wv.w;
@@ -114,13 +140,13 @@ jk_ln_bwd_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy, 
   s1 = warp_sum(s1);
   s2 = warp_sum(s2);
   const float f = rs / Df;
+  SegCursor cur2(lane, wq);
 #pragma unroll 4
-  for (int k = 0; k < NCH; ++k) {
+  for (int k = 0; k < NCH; ++k, cur2.next(wq)) {
     const int64_t c = lane + 32 * k;
     if (c < dq) {
-      const int seg = static_cast<int>(c / wq);
       const float4 xv =
-          __ldg(reinterpret_cast<const float4*>(segs.p[seg] + row * W) + (c - seg * wq));
+          __ldg(reinterpret_cast<const float4*>(seg_base(segs, cur2.seg) + row * W) + cur2.cs);
       const float4 gv = __ldg(reinterpret_cast<const float4*>(gy + row * D) + c);
       const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + c);
       float4 o;
@@ -128,7 +154,7 @@ jk_ln_bwd_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy, 
       o.y = f * (Df * (gv.y * wv.y) - s1 - ((xv.y - mu) * rs) * s2);
       o.z = f * (Df * (gv.z * wv.z) - s1 - ((xv.z - mu) * rs) * s2);
       o.w = f * (Df * (gv.w * wv.w) - s1 - ((xv.w - mu) * rs) * s2);
-      reinterpret_cast<float4*>(gsegs.p[seg] + row * W)[c - seg * wq] = o;
+      reinterpret_cast<float4*>(seg_base(gsegs, cur2.seg) + row * W)[cur2.cs] = o;
     }
   }
 }
@@ -144,7 +170,7 @@ jk_ln_param_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy
   if (c >= dq) return;
   const int64_t wq = W / 4;
   const int seg = static_cast<int>(c / wq);
-  const float4* xs = reinterpret_cast<const float4*>(segs.p[seg]) + (c - seg * wq);
+  const float4* xs = reinterpret_cast<const float4*>(seg_base(segs, seg)) + (c - seg * wq);
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kJkRowsPerChunk;
   const int64_t r1 = r0 + kJkRowsPerChunk < n ? r0 + kJkRowsPerChunk : n;
   float4 aw = make_float4(0.f, 0.f, 0.f, 0.f), ab = aw;
