@@ -13,7 +13,9 @@
 // cign_halo_push_copy moves the same rows with the copy engines instead of
 // SM stores: the send rows are gathered into a local staging buffer and
 // each peer's block goes over NVLink as one cudaMemcpyAsync, so the
-// transfer takes no SM time from the kernels it overlaps.
+// transfer takes no SM time from the kernels it overlaps.  The peers are
+// served in turn from `first_peer` (rank + 1 on the caller's side), so the
+// ranks' copies form a permutation instead of all targeting one peer.
 #include <algorithm>
 #include <cstring>
 
@@ -24,14 +26,19 @@ namespace {
 
 constexpr int kPushThreads = 256;
 
+// Warp j copies send-list row order[j] (row j without an order): an order
+// that interleaves the peers keeps every peer's inbound links busy at once
+// instead of all ranks storing into the same peer first.
 __global__ void __launch_bounds__(kPushThreads)
 halo_push_kernel(int n_peers, const float* __restrict__ src, int64_t F,
                  const int64_t* __restrict__ idx, const int64_t* __restrict__ peer_begin,
-                 float* const* __restrict__ peer_dst, int64_t total) {
+                 float* const* __restrict__ peer_dst, int64_t total,
+                 const int64_t* __restrict__ order) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kPushThreads / 32);
-  for (int64_t k = static_cast<int64_t>(blockIdx.x) * (kPushThreads / 32) + (threadIdx.x >> 5);
-       k < total; k += warps) {
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * (kPushThreads / 32) + (threadIdx.x >> 5);
+       j < total; j += warps) {
+    const int64_t k = order != nullptr ? order[j] : j;
     int p = 0;
     while (p + 1 < n_peers && peer_begin[p + 1] <= k) ++p;  // few peers: linear scan
     const int64_t row = idx != nullptr ? idx[k] : k;
@@ -103,7 +110,7 @@ int cign_ipc_close(void* ptr) {
 
 int cign_halo_push(int32_t n_peers, const float* src, int64_t F, const int64_t* idx,
                    const int64_t* peer_begin, float* const* peer_dst, int64_t total,
-                   cign_stream_t stream) {
+                   const int64_t* order, cign_stream_t stream) {
   CIGN_REQUIRE(n_peers >= 1 && F > 0 && total >= 0, CIGN_ERR_INVALID_ARGUMENT,
                "halo_push: bad sizes");
   if (total == 0) return CIGN_OK;
@@ -114,14 +121,15 @@ int cign_halo_push(int32_t n_peers, const float* src, int64_t F, const int64_t* 
   const int64_t blocks = std::min<int64_t>((total + 7) / 8, 4 * 148 * 8);
   halo_push_kernel<<<static_cast<unsigned>(blocks), kPushThreads, 0,
                      static_cast<cudaStream_t>(stream)>>>(n_peers, src, F, idx, peer_begin,
-                                                          peer_dst, total);
+                                                          peer_dst, total, order);
   CIGN_CHECK_LAUNCH("halo_push_kernel");
   return CIGN_OK;
 }
 
 int cign_halo_push_copy(int32_t n_peers, const float* src, int64_t F, const int64_t* idx,
                         const int64_t* peer_begin_host, float* const* peer_dst_host,
-                        int64_t total, float* staging, cign_stream_t stream) {
+                        int64_t total, float* staging, int32_t first_peer,
+                        cign_stream_t stream) {
   CIGN_REQUIRE(n_peers >= 1 && F > 0 && total >= 0, CIGN_ERR_INVALID_ARGUMENT,
                "halo_push_copy: bad sizes");
   if (total == 0) return CIGN_OK;
@@ -142,7 +150,10 @@ int cign_halo_push_copy(int32_t n_peers, const float* src, int64_t F, const int6
     CIGN_CHECK_LAUNCH("halo_gather_kernel");
     rows = staging;
   }
-  for (int p = 0; p < n_peers; ++p) {
+  CIGN_REQUIRE(first_peer >= 0 && first_peer < n_peers, CIGN_ERR_INVALID_ARGUMENT,
+               "halo_push_copy: first_peer out of range");
+  for (int i = 0; i < n_peers; ++i) {  // peers in turn from first_peer
+    const int p = (first_peer + i) % n_peers;
     const int64_t b = peer_begin_host[p], e = peer_begin_host[p + 1];
     CIGN_REQUIRE(b <= e, CIGN_ERR_INVALID_ARGUMENT, "halo_push_copy: peer_begin not sorted");
     if (e == b) continue;

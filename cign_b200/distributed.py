@@ -314,6 +314,11 @@ class PeerHaloExchange(HaloExchange):
                                        dtype=torch.int64, device=self.device)
         self.recv_begin = torch.tensor(_offsets(plan.recv_counts) + [sum(plan.recv_counts)],
                                        dtype=torch.int64, device=self.device)
+        first = (plan.rank + 1) % w
+        self._order = {  # kernel pushes: rows interleaved over the peers
+            "send": interleaved_order(plan.send_counts, first).to(self.device),
+            "recv": interleaved_order(plan.recv_counts, first).to(self.device)}
+        self._first_peer = first  # copy-engine pushes: peers in turn from rank + 1
         self._begin_host = {  # the same offsets as host arrays (copy-engine pushes)
             "send": (_lib.ctypes.c_int64 * (w + 1))(*(_offsets(plan.send_counts)
                                                        + [sum(plan.send_counts)])),
@@ -416,14 +421,17 @@ class PeerHaloExchange(HaloExchange):
             rc = self.lib.cign_halo_push_copy(
                 self.plan.world, self._lib.ptr(src), F, self._lib.ptr(idx) if gathered else None,
                 self._begin_host["send" if gathered else "recv"], slot["dst_host"], int(total),
-                self._lib.ptr(slot["staging"]) if gathered else None, self._lib.stream_of(src))
+                self._lib.ptr(slot["staging"]) if gathered else None, self._first_peer,
+                self._lib.stream_of(src))
             self._lib.check(rc, "cign_halo_push_copy")
         else:
             begin = self.send_begin if gathered else self.recv_begin
+            order = self._order["send" if gathered else "recv"]
             rc = self.lib.cign_halo_push(self.plan.world, self._lib.ptr(src), F,
                                          self._lib.ptr(idx) if gathered else None,
                                          self._lib.ptr(begin), self._lib.ptr(slot["dst"]),
-                                         int(total), self._lib.stream_of(src))
+                                         int(total), self._lib.ptr(order) if order.numel() else None,
+                                         self._lib.stream_of(src))
             self._lib.check(rc, "cign_halo_push")
         if self.timer is not None:
             t1 = torch.cuda.Event(enable_timing=True)
@@ -499,6 +507,27 @@ class PeerHaloExchange(HaloExchange):
         for slot in self._slots:
             self.lib.cign_device_free(slot["ptr"])
         self._slots = []
+
+
+def interleaved_order(counts: Sequence[int], first: int) -> torch.Tensor:
+    """Flat indices of a list made of consecutive per-peer blocks (block p
+    holds counts[p] rows), visited round-robin over the peers starting at
+    peer `first`: row 0 of every peer, then row 1 of every peer, ...  Pushed
+    in this order, every rank's stores spread over all its peers' links at
+    once instead of all ranks storing into the same peer first."""
+    w = len(counts)
+    offs = _offsets(counts)
+    keys, flat = [], []
+    for p, c in enumerate(counts):
+        if c == 0:
+            continue
+        j = torch.arange(int(c), dtype=torch.int64)
+        keys.append(j * w + (p - first) % w)
+        flat.append(offs[p] + j)
+    if not keys:
+        return torch.zeros(0, dtype=torch.int64)
+    keys, flat = torch.cat(keys), torch.cat(flat)
+    return flat[torch.argsort(keys)]
 
 
 def _offsets(counts: Sequence[int]) -> List[int]:

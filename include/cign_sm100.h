@@ -431,6 +431,9 @@ CIGN_API int cign_pack_proj_status(const void* ws, int64_t d, int32_t k, int64_t
  * n_peers+1 entries), copy row idx[k] of src (row k when idx is NULL) to
  * peer_dst[p] + (k - peer_begin[p]) * F -- peer_dst is a device array of
  * n_peers (usually IPC-mapped) pointers.  F % 4 == 0, 16-byte aligned rows.
+ * order (device, optional): the rows are copied in the sequence order[0..total)
+ * -- a sequence that interleaves the peers spreads the stores over every
+ * peer's links at once. 
  * The copies are ordinary stores; order them against the readers with a
  * collective (or event) after the launch. */
 #define CIGN_IPC_HANDLE_BYTES 64
@@ -441,16 +444,16 @@ CIGN_API int cign_ipc_open(const void* handle, void** ptr);
 CIGN_API int cign_ipc_close(void* ptr);
 CIGN_API int cign_halo_push(int32_t n_peers, const float* src, int64_t F, const int64_t* idx,
                             const int64_t* peer_begin, float* const* peer_dst, int64_t total,
-                            cign_stream_t stream);
+                            const int64_t* order, cign_stream_t stream);
 /* The same copies by the copy engines: with idx, the send rows are first
  * gathered into `staging` (this GPU's memory, total * F floats); then each
  * peer's contiguous block goes to peer_dst_host[p] as one cudaMemcpyAsync
- * on `stream`.  peer_begin_host / peer_dst_host are HOST arrays here.  No SM
- * time is spent on the transfer itself. */
+ * on `stream`, peers in turn from first_peer.  peer_begin_host / peer_dst_host
+ * are HOST arrays here.  No SM time is spent on the transfer itself. */
 CIGN_API int cign_halo_push_copy(int32_t n_peers, const float* src, int64_t F,
                                  const int64_t* idx, const int64_t* peer_begin_host,
                                  float* const* peer_dst_host, int64_t total, float* staging,
-                                 cign_stream_t stream);
+                                 int32_t first_peer, cign_stream_t stream);
 
 /* ------------------------------------------------------------ column sum
  * out[j] = sum_i a[i, j] for a row-major [n, c] matrix, in a fixed order

@@ -240,3 +240,16 @@ def test_partitioned_khop_with_a_halo_free_rank_gloo():
         msgs.append(errors.get())
     assert not msgs, msgs
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+def test_interleaved_push_order():
+    """The push order visits the per-peer blocks round-robin from the given
+    peer and is a permutation of the whole send list."""
+    counts = [3, 0, 2, 4]
+    order = distributed.interleaved_order(counts, first=2)
+    assert order.tolist() == [3, 5, 0, 4, 6, 1, 7, 2, 8]
+    g = torch.Generator().manual_seed(5)
+    for w in (2, 3, 8):
+        for first in range(w):
+            counts = torch.randint(0, 50, (w,), generator=g).tolist()
+            order = distributed.interleaved_order(counts, first)
+            assert sorted(order.tolist()) == list(range(sum(counts)))
