@@ -82,8 +82,10 @@ pack_fwd_kernel(int64_t n, int64_t D, int K, int interaction, int outer, int wei
           float Dv, Wv;
           interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer,
                        Dv, Wv);
-          vel(ow_, j) = a * Wv;
-          vel(od_, j) = a * Dv;
+          // explicit rounded products: never contracted into the hop sum
+          // below, so every kernel forming the pack gives the same bits
+          vel(ow_, j) = __fmul_rn(a, Wv);
+          vel(od_, j) = __fmul_rn(a, Dv);
         }
         if (weighting == 0) {
           float* o = out + row * ow + static_cast<int64_t>(k) * 2 * D + d;
@@ -112,18 +114,22 @@ pack_fwd_kernel(int64_t n, int64_t D, int K, int interaction, int outer, int wei
 // (generic_engine/model_cign.py:721-749 feeding :817-925):
 //   alpha = softmax_k([H + C | |H - C|] @ W^T + b)   (score mode "new"; [H | C] for "old")
 // then the pack with that alpha; alpha [N, K] is also written for the
-// backward.  One warp per node row holds the row's H / C slices (float4,
-// lane l owns columns 4l + 128q) for both steps, so H and C are read once.
+// backward.  One warp per node row (float4 slices, lane l owns columns
+// 4l + 128q); H and C come from HBM once for both steps.
 // The gate dots run in the order of hop_gate_fwd_kernel (columns
 // increasing, x/y/z/w, the sum half before the difference half, then one
 // warp sum) and the pack in the order of pack_fwd_kernel: alpha and the
 // packed output equal those kernels' bit for bit.  Hop 0's propagated rows
 // are read together with H and C and its interaction terms formed before
-// the gate's reductions, so that load's latency hides behind the gate.
-template <int K, int VPL>
-__global__ void __launch_bounds__(kThreads)
+// the gate's reductions, so that load's latency hides behind the gate; the
+// later hops re-read H and C (L1 hits) instead of holding them, which keeps
+// the kernel at three CTAs per SM.
+template <int K, int VPL, int WEIGHTING>
+// D <= 512: <= 85 registers, 3 CTAs (24 rows) per SM; wider rows keep their
+// registers (capping them would spill)
+__global__ void __launch_bounds__(kThreads, VPL <= 4 ? 3 : 1)
 gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int outer,
-                     int weighting, const float* __restrict__ Hn, const float* __restrict__ Cn,
+                     const float* __restrict__ Hn, const float* __restrict__ Cn,
                      CPtrs P, int64_t ldp, const float* __restrict__ W,
                      const float* __restrict__ b, float* __restrict__ alpha_out,
                      float* __restrict__ out) {
@@ -131,7 +137,8 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
   if (row >= n) return;
   const int64_t D2 = 2 * D;
-  float4 h[VPL], c[VPL];
+  const float* hr = Hn + row * D;
+  const float* cr = Cn + row * D;
   // hop 0's interaction terms (before the alpha scaling): its propagated
   // rows are loaded with H and C and combined while the gate reduces
   float4 w0[VPL], d0[VPL];
@@ -143,26 +150,24 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
   for (int q = 0; q < VPL; ++q) {
     const int64_t d = static_cast<int64_t>(lane + q * 32) * 4;
     if (d < D) {
-      h[q] = ld_vec<4>(Hn + row * D + d);
-      c[q] = ld_vec<4>(Cn + row * D + d);
+      const float4 h = ldg_vec<4>(hr + d);
+      const float4 c = ldg_vec<4>(cr + d);
       const float4 th = ldg_vec<4>(p0 + d);
       const float4 tc = ldg_vec<4>(p0 + D + d);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float Dv, Wv;
-        interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer, Dv,
-                     Wv);
+        interact_fwd(vel(h, j) * vel(tc, j), vel(c, j) * vel(th, j), interaction, outer, Dv, Wv);
         vel(w0[q], j) = Wv;
         vel(d0[q], j) = Dv;
       }
       float4 g0, g1;
       if (gate_mode == 1) {
-        g0 = make_float4(h[q].x + c[q].x, h[q].y + c[q].y, h[q].z + c[q].z, h[q].w + c[q].w);
-        g1 = make_float4(fabsf(h[q].x - c[q].x), fabsf(h[q].y - c[q].y), fabsf(h[q].z - c[q].z),
-                         fabsf(h[q].w - c[q].w));
+        g0 = make_float4(h.x + c.x, h.y + c.y, h.z + c.z, h.w + c.w);
+        g1 = make_float4(fabsf(h.x - c.x), fabsf(h.y - c.y), fabsf(h.z - c.z), fabsf(h.w - c.w));
       } else {
-        g0 = h[q];
-        g1 = c[q];
+        g0 = h;
+        g1 = c;
       }
 #pragma unroll
       for (int k = 0; k < K; ++k) {
@@ -174,8 +179,6 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
         dot[k] = t;
       }
     } else {
-      vzero(h[q]);
-      vzero(c[q]);
       vzero(w0[q]);
       vzero(d0[q]);
     }
@@ -197,10 +200,10 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
     dot[k] = dot[k] / ssum;  // alpha_k, on every lane
     if (lane == k) alpha_out[row * K + k] = dot[k];
   }
-  const int64_t ow = weighting == 0 ? 2 * D * K : 2 * D;
-  float4 accD[VPL], accW[VPL];
+  const int64_t ow = WEIGHTING == 0 ? 2 * D * K : 2 * D;
+  float4 accD[WEIGHTING == 1 ? VPL : 1], accW[WEIGHTING == 1 ? VPL : 1];
 #pragma unroll
-  for (int q = 0; q < VPL; ++q) {
+  for (int q = 0; q < (WEIGHTING == 1 ? VPL : 1); ++q) {
     vzero(accD[q]);
     vzero(accW[q]);
   }
@@ -216,22 +219,26 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
       if (k == 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          vel(ow_, j) = a * vel(w0[q], j);
-          vel(od_, j) = a * vel(d0[q], j);
+          vel(ow_, j) = __fmul_rn(a, vel(w0[q], j));
+          vel(od_, j) = __fmul_rn(a, vel(d0[q], j));
         }
       } else {
+        // H and C again (this warp read them above: L1 hits), so a lane keeps
+        // no copy of them across the gate
+        const float4 h = ldg_vec<4>(hr + d);
+        const float4 c = ldg_vec<4>(cr + d);
         const float4 th = ldg_vec<4>(pk + d);
         const float4 tc = ldg_vec<4>(pk + D + d);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           float Dv, Wv;
-          interact_fwd(vel(h[q], j) * vel(tc, j), vel(c[q], j) * vel(th, j), interaction, outer,
+          interact_fwd(vel(h, j) * vel(tc, j), vel(c, j) * vel(th, j), interaction, outer,
                        Dv, Wv);
-          vel(ow_, j) = a * Wv;
-          vel(od_, j) = a * Dv;
+          vel(ow_, j) = __fmul_rn(a, Wv);
+          vel(od_, j) = __fmul_rn(a, Dv);
         }
       }
-      if (weighting == 0) {
+      if constexpr (WEIGHTING == 0) {
         float* o = out + row * ow + static_cast<int64_t>(k) * 2 * D + d;
         st_vec(o, ow_);
         st_vec(o + D, od_);
@@ -241,7 +248,7 @@ gate_pack_fwd_kernel(int64_t n, int64_t D, int gate_mode, int interaction, int o
       }
     }
   }
-  if (weighting == 1) {
+  if constexpr (WEIGHTING == 1) {
 #pragma unroll
     for (int q = 0; q < VPL; ++q) {
       const int64_t d = static_cast<int64_t>(lane + q * 32) * 4;
@@ -258,8 +265,12 @@ int launch_gate_pack(int64_t n, int64_t D, int gate_mode, int interaction, int o
                      int weighting, const float* H, const float* C, const CPtrs& pl, int64_t ldp,
                      const float* W, const float* b, float* alpha, float* out, cudaStream_t s) {
   const int64_t grid = (n + kThreads / 32 - 1) / (kThreads / 32);
-  gate_pack_fwd_kernel<K, VPL><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
-      n, D, gate_mode, interaction, outer, weighting, H, C, pl, ldp, W, b, alpha, out);
+  if (weighting == 0)
+    gate_pack_fwd_kernel<K, VPL, 0><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+        n, D, gate_mode, interaction, outer, H, C, pl, ldp, W, b, alpha, out);
+  else
+    gate_pack_fwd_kernel<K, VPL, 1><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
+        n, D, gate_mode, interaction, outer, H, C, pl, ldp, W, b, alpha, out);
   CIGN_CHECK_LAUNCH("gate_pack_fwd_kernel");
   return CIGN_OK;
 }
