@@ -2105,7 +2105,8 @@ gat_edge_weights_kernel(int n, int H, const int* __restrict__ rowptr, const int*
 // Measured at cfg2 (D=512, H=4): forward 194 us against 217 us for the same
 // gather from registers (two rows in flight), K2 185 us against 251 us.
 template <int VPL, int MODE, bool ONE_PASS>
-__global__ void __launch_bounds__(kThreads, ONE_PASS ? 4 : 1)  // <= 64 registers: 4 CTAs / SM
+// <= 64 registers (1024 threads of 64 registers per SM):
+__global__ void __launch_bounds__(kThreads, ONE_PASS ? 1024 / kThreads : 1)
 gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* __restrict__ idx,
                const int* __restrict__ perm, const int* __restrict__ seg_row,
                const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
@@ -2372,7 +2373,8 @@ gat_agg_fwd_bf16_kernel(int n, int H, int64_t D, const int* __restrict__ ptr,
 // across the warp; the lane owning edge e keeps its dots.  Light rows then
 // run the softmax/dropout/LeakyReLU backward in registers and write glog and
 // grad_attn_row; hub segments write their dots to glog for the hub-row kernel.
-__global__ void __launch_bounds__(kThreads, 3)  // <= 80 registers: 3 CTAs (64 KB ring each) / SM
+// <= 80 registers (768 threads of 80 registers per SM):
+__global__ void __launch_bounds__(kThreads, 768 / kThreads)
 gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
                     const int* __restrict__ col, const int* __restrict__ seg_row,
                     const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,

@@ -42,7 +42,11 @@ struct cign_spmm_plan {
 namespace cign {
 namespace {
 
-constexpr int kThreads = 256;
+// 4 warps (rows) per CTA: a CTA holds its SM slot until its longest row is
+// done, and the power-law row lengths leave fewer idle warp slots behind
+// with small CTAs (measured on the cfg2 graph: 118 us per F=1024 hop
+// against 125 us at 8 warps per CTA; 2 warps gave the same as 4).
+constexpr int kThreads = 128;
 constexpr int kSegLen = 64;  // edges per work item of a hub row
 
 template <int VEC, int VPL, int LPR>
