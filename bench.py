@@ -103,7 +103,7 @@ def step_roofline_items(cfg, nnz, nnz_g):
 
     # forward, net input
     add("input dropout", 1, 9 * N * I)
-    add("input projections (GEMM)", 2, *gemm(N, D, I))
+    add("input projections (one stacked GEMM)", 1, *gemm(N, 2 * D, I))
     add("input SiLU mix", 1, 12 * N * D)
     # forward, per block
     add("dropout-LN fwd", L, 8 * N * D + 8 * N)
@@ -147,8 +147,8 @@ def step_roofline_items(cfg, nnz, nnz_g):
     add("dropout-LN bwd", L, 12 * N * D + 8 * N)
     # backward, net input
     add("input SiLU mix bwd", 1, 20 * N * D)
-    add("input projections wgrad (GEMM)", 2, *gemm(D, I, N))
-    add("input projections bias colsum", 2, 4 * N * D)
+    add("input projections wgrad (one GEMM)", 1, *gemm(2 * D, I, N))
+    add("input projections bias colsum", 1, 8 * N * D)
     # optimizer: fused Adam reads param, grad, exp_avg, exp_avg_sq, writes three
     params = (2 * (I * D + D) + 1 + L * (4 * D + HD * D + 2 * H * D + D + 2 * K * D * D + D
                                      + 2 * D * K + K + D) + 2 * S * D + S * D * Cls + Cls)

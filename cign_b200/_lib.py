@@ -98,6 +98,9 @@ SIGNATURES = {
     "cign_ipc_handle": (c_int, [_P, _P]),
     "cign_ipc_open": (c_int, [_P, POINTER(c_void_p)]),
     "cign_ipc_close": (c_int, [_P]),
+    "cign_silu_mix_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P]),
+    "cign_silu_mix_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "cign_silu_mix_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_halo_push": (c_int, [c_int32, _P, c_int64, _P, _P, _P, c_int64, _P, _P]),
     "cign_halo_push_copy": (c_int, [c_int32, _P, c_int64, _P, _P, _P, c_int64, _P, c_int32,
                                     _P]),

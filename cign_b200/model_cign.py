@@ -43,6 +43,7 @@ from .collapsed_gat import (collapsed_gat_mean_bias_silu, gat_context, gat_conte
 from .fused_block_ops import fused_add_layernorm, fused_dropout_gamma_residual, fused_dropout_layernorm
 from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
+from .input_proj import dual_input_projection
 from .block_fused import native_spmm_plan, propagate_gate_pack_proj
 from .jk_norm import jk_layer_norm, jk_norm_supported
 from .hop_gate import fused_hop_gate
@@ -267,9 +268,15 @@ class GraphCliffordNet(nn.Module):
             raise RuntimeError("call prepare_fused_gat_graph(...) once before training")
         x = x.float()
         H_in = F.dropout(x, p=self.dropout, training=self.training)
-        H = self.input_act(linear(H_in, self.input_proj_0.weight, self.input_proj_0.bias)) + \
-            self.input_eta * self.input_act(linear(H_in, self.input_proj_1.weight,
-                                                   self.input_proj_1.bias))
+        if H_in.is_cuda and self.hidden_dim % 4 == 0 and not H_in.requires_grad:
+            # both projections in one GEMM, SiLU and the eta mix in one pass
+            H = dual_input_projection(H_in, self.input_proj_0.weight, self.input_proj_0.bias,
+                                      self.input_proj_1.weight, self.input_proj_1.bias,
+                                      self.input_eta)
+        else:
+            H = self.input_act(linear(H_in, self.input_proj_0.weight, self.input_proj_0.bias)) + \
+                self.input_eta * self.input_act(linear(H_in, self.input_proj_1.weight,
+                                                       self.input_proj_1.bias))
         states = [H]
         for block in self.blocks:
             H = block(H, graph_operator, self._gat_graph)

@@ -419,6 +419,20 @@ CIGN_API int cign_pack_proj_gemm_tf32(int64_t n, int64_t d, int32_t k, int64_t d
 CIGN_API int cign_pack_proj_status(const void* ws, int64_t d, int32_t k, int64_t dout,
                           cign_stream_t stream);
 
+/* ------------------------------------------------------------ input projection
+ * The net's dual input projection after one GEMM has formed both halves
+ * z = [x W0^T + b0 | x W1^T + b1] ([n, 2d]) (generic_engine/model_cign.py:
+ * 1162-1170, H = SiLU(z0) + eta * SiLU(z1)).  eta is a device scalar.
+ * cign_silu_mix_fwd: out [n, d].  cign_silu_mix_bwd: grad_z [n, 2d] and
+ * grad_eta (a device scalar, summed in a fixed order).  d % 4 == 0,
+ * 16-byte aligned tensors. */
+CIGN_API int cign_silu_mix_fwd(int64_t n, int64_t d, const float* z, const float* eta,
+                               float* out, cign_stream_t stream);
+CIGN_API size_t cign_silu_mix_bwd_workspace_bytes(int64_t n, int64_t d);
+CIGN_API int cign_silu_mix_bwd(int64_t n, int64_t d, const float* grad_out, const float* z,
+                               const float* eta, float* grad_z, float* grad_eta, void* ws,
+                               size_t ws_bytes, cign_stream_t stream);
+
 /* ------------------------------------------------------------ peer memory
  * Halo exchange of the row-partitioned path over NVLink peer memory
  * (the reference trains on one GPU: these entry points have no reference
