@@ -44,17 +44,21 @@ __device__ __forceinline__ float gsum(float v, unsigned gmask) {
 }
 
 // Row chunks of the parameter-gradient reductions (one CTA each): at most
-// this many -- two per SM, the residency of the ~128-register backward
+// this many -- three per SM, the residency of the 80-register backward
 // kernels, so that all chunks run in one wave (a second, partial wave left
 // most SMs idle) -- each a multiple of 8 rows.
-constexpr int64_t kLnChunkTarget = 296;
-int64_t rows_per_chunk(int64_t n) {
-  const int64_t target = kLnChunkTarget;
+constexpr int64_t kLnChunkTarget = 444;
+// silu_add_ln_bwd_kernel keeps three parameter partials and its row in
+// registers (~128): two CTAs per SM, so its chunks target two per SM.
+constexpr int64_t kSiluLnChunkTarget = 296;
+int64_t rows_per_chunk(int64_t n, int64_t target = kLnChunkTarget) {
   int64_t r = (n + target - 1) / target;
   r = std::max<int64_t>(r, 8);
   return (r + 7) / 8 * 8;
 }
-int64_t num_chunks(int64_t n) { return (n + rows_per_chunk(n) - 1) / rows_per_chunk(n); }
+int64_t num_chunks(int64_t n, int64_t target = kLnChunkTarget) {
+  return (n + rows_per_chunk(n, target) - 1) / rows_per_chunk(n, target);
+}
 
 // ---------------------------------------------------------------- forward
 // MODE 0: dropout-LN (x, seed, p);  MODE 1: add-LN (a + b).
@@ -131,7 +135,7 @@ ln_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ x, const float* __
 // grad wrt the normalised input (dq) plus per-chunk partials of
 // sum(gy * xhat) and sum(gy) for the LN weight and bias.
 template <int MODE, int VEC, int VPL, int LPR>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, VPL <= 4 ? 3 : 1)
 ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
               const float* __restrict__ x, const float* __restrict__ x2,
               const float* __restrict__ w, const float* __restrict__ mean,
@@ -155,16 +159,17 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
   const int64_t r1 = (r0 + rpc < n) ? (r0 + rpc) : n;
   static_assert(VPL * VEC <= 32, "one keep bit per element of a lane's row slice");
+  // Two passes over each row: the first forms the row sums and the parameter
+  // partials, the second re-reads x (and x2), gy (this warp's own recent
+  // loads: L1 hits) and writes grad x, so a lane keeps no row arrays (only
+  // the dropout keep bits, hashed once per element).
   for (int64_t row = r0 + group; row < r1; row += Cfg::kGroups) {
     const float mu = mean[row], rs = rstd[row];
-    V xh[VPL], dn[VPL];
-    uint32_t keep_bits = 0;  // MODE 0: the dropout keep bits, hashed once per element
+    uint32_t keep_bits = 0;  // MODE 0: the dropout keep bits
     float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
       const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
-      vzero(xh[k]);
-      vzero(dn[k]);
       if (d < D) {
         const V xv = ld_vec<VEC>(x + row * D + d);
         const V gv = ld_vec<VEC>(gy + row * D + d);
@@ -183,8 +188,6 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
           }
           const float xhat = (qv - mu) * rs;
           const float dnorm = vel(gv, j) * vel(wv, j);
-          vel(xh[k], j) = xhat;
-          vel(dn[k], j) = dnorm;
           s1 += dnorm;
           s2 += dnorm * xhat;
           vel(aw[k], j) += vel(gv, j) * xhat;
@@ -198,16 +201,20 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
     for (int k = 0; k < VPL; ++k) {
       const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
       if (d < D) {
+        const V xv = ld_vec<VEC>(x + row * D + d);
+        const V gv = ld_vec<VEC>(gy + row * D + d);
+        const V wv = ldg_vec<VEC>(w + d);
+        V x2v;
+        if (MODE == 1) x2v = ld_vec<VEC>(x2 + row * D + d);
         V o;
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const float dq = (rs / Df) * (Df * vel(dn[k], j) - s1 - vel(xh[k], j) * s2);
-          if (MODE == 0) {
-            const bool keep = (keep_bits >> (k * VEC + j)) & 1u;
-            vel(o, j) = keep ? dq * scale : 0.0f;
-          } else {
-            vel(o, j) = dq;
-          }
+          const bool keep = MODE == 0 ? ((keep_bits >> (k * VEC + j)) & 1u) != 0 : true;
+          const float qv = MODE == 0 ? (keep ? vel(xv, j) * scale : 0.0f) : vel(xv, j) + vel(x2v, j);
+          const float xhat = (qv - mu) * rs;
+          const float dnorm = vel(gv, j) * vel(wv, j);
+          const float dq = (rs / Df) * (Df * dnorm - s1 - xhat * s2);
+          vel(o, j) = MODE == 0 ? (keep ? dq * scale : 0.0f) : dq;
         }
         st_vec(gx + row * D + d, o);
       }
@@ -549,8 +556,8 @@ int launch_silu_add_ln_bwd(int64_t n, int64_t D, const float* gy, const float* p
                            const float* h, const float* w, const float* mean, const float* rstd,
                            float* gz, float* gpre, float* gw, float* gb, float* gbias, float* ws,
                            cudaStream_t s) {
-  const int64_t rpc = rows_per_chunk(n);
-  const int64_t chunks = num_chunks(n);
+  const int64_t rpc = rows_per_chunk(n, kSiluLnChunkTarget);
+  const int64_t chunks = num_chunks(n, kSiluLnChunkTarget);
   float* pw = ws;
   float* pb = ws + chunks * D;
   float* pbias = ws + 2 * chunks * D;
@@ -749,7 +756,7 @@ int cign_silu_add_ln_fwd(int64_t n, int64_t d, const float* lin, const float* bi
 
 size_t cign_silu_add_ln_bwd_workspace_bytes(int64_t n, int64_t d) {
   if (n <= 0) return 0;
-  return static_cast<size_t>(num_chunks(n)) * d * 3 * sizeof(float);
+  return static_cast<size_t>(num_chunks(n, kSiluLnChunkTarget)) * d * 3 * sizeof(float);
 }
 
 int cign_silu_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* pre,
@@ -807,9 +814,9 @@ int cign_block_dropout_mask(int64_t count, float p, uint64_t seed_value, const u
 // parameter-gradient reduction lives in the fixed array below instead of a
 // caller-provided buffer.
 //
-// The array holds 296 row chunks x 1024 columns x 2 partial sums (2.3 MiB);
+// The array holds 444 row chunks x 1024 columns x 2 partial sums (3.5 MiB);
 // every GPU on which this library is loaded keeps it for the life of the
-// process.  296 is the largest chunk count rows_per_chunk() can produce, so
+// process.  444 is the largest chunk count rows_per_chunk() can produce, so
 // the limit is the hidden width: D <= 1024 (D <= 256 unless D % 4 == 0 and
 // the tensors are 16-byte aligned), the same as the workspace version.
 //
@@ -822,7 +829,7 @@ int cign_block_dropout_mask(int64_t count, float p, uint64_t seed_value, const u
 // stream capture.  The dropout seed is a host value only (no device seed
 // slot, unlike cign_dropout_ln_bwd): a captured graph that replays this call
 // replays the same mask.
-constexpr int64_t kStaticLnChunks = 296;
+constexpr int64_t kStaticLnChunks = 444;
 constexpr int64_t kStaticLnMaxD = 1024;
 static_assert(kStaticLnChunks == kLnChunkTarget,
               "the static scratch must hold the largest chunk count rows_per_chunk() gives");

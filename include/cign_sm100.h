@@ -542,7 +542,7 @@ CIGN_API int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y,
  * counterpart in the reference).  For callers that cannot allocate device
  * memory -- e.g. a plugin inside a host framework that owns all device memory
  * through its own pool and passes kernels only their inputs and outputs --
- * the reduction scratch is a fixed 2.3 MiB array inside the library (296 row
+ * the reduction scratch is a fixed 3.5 MiB array inside the library (444 row
  * chunks x 1024 columns x 2 floats), held on every GPU that loads the
  * library until the process exits.  Limit: D <= 1024 (the same as the
  * workspace version); larger shapes return CIGN_ERR_UNSUPPORTED.  No
