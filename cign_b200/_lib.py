@@ -76,6 +76,7 @@ SIGNATURES = {
     "cign_spmm": (c_int, [_P, c_int, _P, c_int64, _P, _P, _P, c_size_t, _P]),
     "cign_multihop_workspace_bytes": (c_size_t, [_P, c_int, c_int64]),
     "cign_multihop_fwd": (c_int, [_P, c_int, _P, c_int64, _PP, _P, c_size_t, _P]),
+    "cign_multihop_fwd_split": (c_int, [_P, c_int, _P, _P, c_int64, _PP, _P, c_size_t, _P]),
     "cign_multihop_bwd": (c_int, [_P, c_int, _PP, c_int64, _P, _P, c_size_t, _P]),
     "cign_spmm_bf16": (c_int, [_P, c_int, _P, c_int64, _P, c_int, _P, c_size_t, _P]),
     "cign_multihop_fwd_bf16": (c_int, [_P, c_int, _P, c_int64, _PP, _P, c_size_t, _P]),

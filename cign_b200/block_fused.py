@@ -83,7 +83,11 @@ def _gate_pack(H, C, props, gate_w, gate_b, gate_mode):
 
 
 def _propagate(H, C, plan, order_set):
-    ys = plan.forward(torch.cat([H, C], 1), max(order_set))
+    if (isinstance(plan, SpmmPlan) and H.size(1) % 256 == 0
+            and H.data_ptr() % 16 == 0 and C.data_ptr() % 16 == 0):
+        ys = plan.forward_split(H, C, max(order_set))  # no [H | C] copy
+    else:
+        ys = plan.forward(torch.cat([H, C], 1), max(order_set))
     return [ys[p - 1] for p in order_set]
 
 

@@ -57,13 +57,15 @@ struct SpmmCfg {
 };
 
 // acc[q] += sum over edges e in {start, start+step, ...} < e1 of
-//           val[e] * X[col[e], f0 + (lig + q*LPR)*VEC ...]
-// Edges are fetched LPR at a time (one per lane) and broadcast.
+//           val[e] * X[col[e] * ldx + xf0 + (lig + q*LPR)*VEC ...]
+// (feature f0 + (lig + q*LPR)*VEC < F of the F-wide row; ldx = F and
+// xf0 = f0 for a plain [*, F] X).  Edges are fetched LPR at a time (one per
+// lane) and broadcast.
 template <int VEC, int VPL, int LPR>
 __device__ __forceinline__ void gather_edges(
     const int* __restrict__ col, const float* __restrict__ val, int start,
-    int e1, int step, const float* __restrict__ X, int64_t F, int64_t f0,
-    int lig, unsigned gmask, typename VecT<VEC>::type (&acc)[VPL]) {
+    int e1, int step, const float* __restrict__ X, int64_t ldx, int64_t xf0, int64_t F,
+    int64_t f0, int lig, unsigned gmask, typename VecT<VEC>::type (&acc)[VPL]) {
   using V = typename VecT<VEC>::type;
   using Cfg = SpmmCfg<VEC, VPL, LPR>;
   for (int base = start; base < e1; base += step) {
@@ -87,7 +89,7 @@ __device__ __forceinline__ void gather_edges(
       V xv[Cfg::kUnroll][VPL];
 #pragma unroll
       for (int u = 0; u < Cfg::kUnroll; ++u) {
-        const float* xr = X + static_cast<int64_t>(cc[u]) * F + f0;
+        const float* xr = X + static_cast<int64_t>(cc[u]) * ldx + xf0;
 #pragma unroll
         for (int q = 0; q < VPL; ++q) {
           const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
@@ -103,7 +105,7 @@ __device__ __forceinline__ void gather_edges(
     for (; t < cnt; ++t) {
       const int c0 = __shfl_sync(gmask, c, t, LPR);
       const float v0 = __shfl_sync(gmask, v, t, LPR);
-      const float* xr = X + static_cast<int64_t>(c0) * F + f0;
+      const float* xr = X + static_cast<int64_t>(c0) * ldx + xf0;
 #pragma unroll
       for (int q = 0; q < VPL; ++q) {
         const int64_t fi = static_cast<int64_t>(lig + q * LPR) * VEC;
@@ -115,13 +117,16 @@ __device__ __forceinline__ void gather_edges(
 
 // Blocks [0, seg_blocks) process hub-row segments (one group each) into
 // `partial`; the remaining blocks process whole rows of at most kSegLen
-// non-zeros.
-template <int VEC, int VPL, int LPR>
+// non-zeros.  X is [rows of X, F] -- or, with X1 != NULL, the two column
+// blocks [X | X1] of widths split and F - split held as separate row-major
+// matrices (split a multiple of the tile width, so a tile lies in one).
+template <int VEC, int VPL, int LPR, bool SPLIT = false>
 __global__ void __launch_bounds__(kThreads)
 spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__ col,
                  const float* __restrict__ val, const int* __restrict__ seg_begin,
                  const int* __restrict__ seg_end, int n_seg, int seg_blocks,
-                 const float* __restrict__ X, int64_t F, const float* __restrict__ addend,
+                 const float* __restrict__ X, int64_t F, const float* __restrict__ X1,
+                 int64_t split, const float* __restrict__ addend,
                  float* __restrict__ Y, float* __restrict__ partial) {
   using V = typename VecT<VEC>::type;
   using Cfg = SpmmCfg<VEC, VPL, LPR>;
@@ -133,14 +138,23 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
 
   // one feature tile per block row of the grid (gridDim.y * kTile >= F)
   const int64_t f0 = static_cast<int64_t>(blockIdx.y) * Cfg::kTile;
+  // the gathered matrix, its row stride and this tile's first column in it
+  const float* Xg = X;
+  int64_t ldx = F, xf0 = f0;
+  if constexpr (SPLIT) {
+    const bool second = f0 >= split;
+    Xg = second ? X1 : X;
+    ldx = second ? F - split : split;
+    xf0 = second ? f0 - split : f0;
+  }
   V acc[VPL];
 #pragma unroll
   for (int q = 0; q < VPL; ++q) vzero(acc[q]);
   if (static_cast<int>(blockIdx.x) < seg_blocks) {
     const int64_t sidx = static_cast<int64_t>(blockIdx.x) * Cfg::kGroups + group;
     if (sidx >= n_seg) return;
-    gather_edges<VEC, VPL, LPR>(col, val, seg_begin[sidx], seg_end[sidx], LPR, X, F, f0, lig,
-                                gmask, acc);
+    gather_edges<VEC, VPL, LPR>(col, val, seg_begin[sidx], seg_end[sidx], LPR, Xg, ldx, xf0, F,
+                                f0, lig, gmask, acc);
     float* pr = partial + sidx * F;
 #pragma unroll
     for (int q = 0; q < VPL; ++q) {
@@ -156,7 +170,7 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
   const int e0 = crow[row64];
   const int e1 = crow[row64 + 1];
   if (e1 - e0 > kSegLen) return;  // a hub row: done by segments + combine
-  gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, X, F, f0, lig, gmask, acc);
+  gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, Xg, ldx, xf0, F, f0, lig, gmask, acc);
   float* yr = Y + row64 * F + f0;
   const float* ar = addend != nullptr ? addend + row64 * F + f0 : nullptr;
 #pragma unroll
@@ -402,7 +416,8 @@ __global__ void csr_validate_kernel(int64_t rows, int64_t cols, int64_t nnz,
 
 template <int VEC, int VPL, int LPR>
 int launch_spmm_cfg(const cign_csr_f32& m, const SegList& sl, const float* X, int64_t F,
-                    const float* addend, float* Y, float* partial, cudaStream_t stream) {
+                    const float* addend, float* Y, float* partial, cudaStream_t stream,
+                    const float* X1 = nullptr, int64_t split = 0) {
   using Cfg = SpmmCfg<VEC, VPL, LPR>;
   const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
   const int64_t light_blocks = (m.rows + Cfg::kGroups - 1) / Cfg::kGroups;
@@ -413,10 +428,17 @@ int launch_spmm_cfg(const cign_csr_f32& m, const SegList& sl, const float* X, in
   const int64_t tiles = (F + Cfg::kTile - 1) / Cfg::kTile;
   CIGN_REQUIRE(tiles <= 65535, CIGN_ERR_UNSUPPORTED, "spmm: F too large (%lld tiles)",
                static_cast<long long>(tiles));
-  spmm_rows_kernel<VEC, VPL, LPR><<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(tiles)),
-                                    kThreads, 0, stream>>>(
-      static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
-      static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, addend, Y, partial);
+  const dim3 g(static_cast<unsigned>(grid), static_cast<unsigned>(tiles));
+  if (X1 != nullptr)
+    spmm_rows_kernel<VEC, VPL, LPR, true><<<g, kThreads, 0, stream>>>(
+        static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
+        static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, X1, split, addend, Y,
+        partial);
+  else
+    spmm_rows_kernel<VEC, VPL, LPR, false><<<g, kThreads, 0, stream>>>(
+        static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
+        static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, nullptr, 0, addend, Y,
+        partial);
   CIGN_CHECK_LAUNCH("spmm_rows_kernel");
   return launch_spmm_combine<VEC>(sl, partial, F, addend, Y, stream);
 }
@@ -666,6 +688,44 @@ int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power, const float* X,
     rc = run_spmm(plan, 0, src, F, nullptr, Y[p], partial, s);
     if (rc) return rc;
     src = Y[p];
+  }
+  return CIGN_OK;
+}
+
+int cign_multihop_fwd_split(const cign_spmm_plan* plan, int max_power, const float* X0,
+                            const float* X1, int64_t d, float* const* Y, void* ws,
+                            size_t ws_bytes, cign_stream_t stream) {
+  CIGN_REQUIRE(max_power >= 1, CIGN_ERR_INVALID_ARGUMENT,
+               "multihop_fwd_split: max_power must be >= 1");
+  CIGN_REQUIRE(Y != nullptr && X1 != nullptr, CIGN_ERR_NULL_POINTER,
+               "multihop_fwd_split: NULL argument");
+  const int64_t F = 2 * d;
+  int rc = check_dense(plan, X0, F, Y[0], "multihop_fwd_split");
+  if (rc) return rc;
+  // the 256-float tiles of the float4 path for rows wider than 256 floats
+  CIGN_REQUIRE(d % 256 == 0, CIGN_ERR_UNSUPPORTED,
+               "multihop_fwd_split: d must be a multiple of 256 (got %lld)",
+               static_cast<long long>(d));
+  for (int p = 0; p < max_power; ++p) {
+    CIGN_REQUIRE(Y[p] != nullptr || plan->p.rows == 0, CIGN_ERR_NULL_POINTER,
+                 "multihop_fwd_split: Y[%d] is NULL", p);
+    CIGN_REQUIRE(plan->p.rows == 0 || aligned16(Y[p]), CIGN_ERR_ALIGNMENT,
+                 "multihop_fwd_split: Y[%d] must be 16-byte aligned", p);
+  }
+  CIGN_REQUIRE(plan->p.rows == 0 || (aligned16(X0) && aligned16(X1)), CIGN_ERR_ALIGNMENT,
+               "multihop_fwd_split: X0 and X1 must be 16-byte aligned");
+  const size_t need = partial_bytes(plan, F);
+  CIGN_REQUIRE(ws_bytes >= need && (need == 0 || ws != nullptr), CIGN_ERR_INVALID_ARGUMENT,
+               "multihop_fwd_split: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* partial = static_cast<float*>(ws);
+  CIGN_REQUIRE(partial == nullptr || aligned16(partial), CIGN_ERR_ALIGNMENT,
+               "multihop_fwd_split: workspace must be 16-byte aligned");
+  rc = launch_spmm_cfg<4, 2, 32>(plan->p, plan->seg_p, X0, F, nullptr, Y[0], partial, s, X1, d);
+  if (rc) return rc;
+  for (int p = 1; p < max_power; ++p) {
+    rc = run_spmm(plan, 0, Y[p - 1], F, nullptr, Y[p], partial, s);
+    if (rc) return rc;
   }
   return CIGN_OK;
 }

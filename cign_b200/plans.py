@@ -164,6 +164,31 @@ class SpmmPlan:
         _lib.check(rc, "cign_multihop_fwd")
         return ys
 
+    def forward_split(self, x0: torch.Tensor, x1: torch.Tensor,
+                      max_power: int) -> List[torch.Tensor]:
+        """forward(torch.cat([x0, x1], 1), max_power) without forming the
+        concatenation: hop 1 reads the two [rows, d] blocks directly
+        (cign_multihop_fwd_split; d % 256 == 0)."""
+        x0 = self._check_dense(x0, "multihop forward (first block)")
+        x1 = self._check_dense(x1, "multihop forward (second block)")
+        d = int(x0.size(1))
+        if x1.shape != x0.shape:
+            raise ValueError("forward_split: the two column blocks must have the same shape")
+        ys = [torch.empty((self.rows, 2 * d), dtype=torch.float32, device=self.device)
+              for _ in range(int(max_power))]
+        ws = _lib.workspace(self.lib.cign_spmm_workspace_bytes(self.handle, 2 * d), self.device)
+        timer = SpmmPlan.hop_timer
+        with _lib.DeviceGuard(self.device):
+            t0 = timer.begin(torch.cuda.current_stream(self.device)) if timer else None
+            rc = self.lib.cign_multihop_fwd_split(self.handle, int(max_power), _lib.ptr(x0),
+                                                  _lib.ptr(x1), d, _lib.ptr_array(ys),
+                                                  _lib.ptr(ws), ws.numel(), _lib.stream_of(x0))
+            if timer:
+                timer.end(torch.cuda.current_stream(self.device), t0, "fwd", int(max_power), 0,
+                          2 * d)
+        _lib.check(rc, "cign_multihop_fwd_split")
+        return ys
+
     def spmm_bf16(self, x: torch.Tensor, out_dtype=torch.bfloat16,
                   transpose: bool = False) -> torch.Tensor:
         """P x (or P^T x) for bf16-stored features: fp32 accumulation, output

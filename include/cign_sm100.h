@@ -134,6 +134,15 @@ CIGN_API int cign_multihop_fwd(const cign_spmm_plan* plan, int max_power,
                       const float* X, int64_t F, float* const* Y, void* ws,
                       size_t ws_bytes, cign_stream_t stream);
 
+/* cign_multihop_fwd with hop 1's input given as its two column blocks
+ * X = [X0 | X1], each [rows, d] row-major (the block's H_norm and C_norm), so
+ * the [rows, 2d] concatenation is never written; Y[p] as cign_multihop_fwd
+ * (F = 2d).  d % 256 == 0, 16-byte aligned tensors. */
+CIGN_API int cign_multihop_fwd_split(const cign_spmm_plan* plan, int max_power,
+                                     const float* X0, const float* X1, int64_t d,
+                                     float* const* Y, void* ws, size_t ws_bytes,
+                                     cign_stream_t stream);
+
 /* k-hop transposed backward: acc = 0; for p = max_power..1:
  *   acc = P^T (acc + G[p-1]);   GX = acc.
  * G: host array of max_power device pointers ([rows, F]) or NULL entries

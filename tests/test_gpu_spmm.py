@@ -177,3 +177,20 @@ def test_cfg2_scale_properties(cuda):
     assert_parity(px.cpu()[sample], ref, what="cfg2 row sample")
     y1, y2, y3 = op.plan.forward3(x)
     assert_parity(y2.cpu()[sample], torch.sparse.mm(P, y1.cpu())[sample], what="hop 2")
+
+
+@pytest.mark.parametrize("d", [256, 512])
+def test_multihop_split_input_equals_concatenated(cuda, d):
+    """cign_multihop_fwd_split (hop 1 reads [H | C] as two matrices) gives the
+    hops of the concatenated input bit for bit, hub rows included."""
+    n = 4000
+    base, _ = _powerlaw_operator(n, 30000, 13, cuda)
+    plan = SpmmPlan(base.csr.crow_indices(), base.csr.col_indices(), base.csr.values())
+    assert plan.info()["heavy_rows"] > 0
+    g = torch.Generator().manual_seed(d)
+    h = torch.randn(n, d, generator=g).to(cuda)
+    c = torch.randn(n, d, generator=g).to(cuda)
+    ys = plan.forward_split(h, c, 3)
+    ref = plan.forward(torch.cat([h, c], 1), 3)
+    for p in range(3):
+        assert torch.equal(ys[p], ref[p]), p
