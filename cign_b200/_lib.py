@@ -148,13 +148,15 @@ SIGNATURES = {
     "cign_ln_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "cign_dropout_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, c_uint64, _P, _P,
                                     _P, _P, _P, c_size_t, _P]),
+    "cign_dropout_ln_bwd_add": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, c_uint64,
+                                        _P, _P, _P, _P, _P, _P, c_size_t, _P]),
     "cign_dropout_ln_bwd_static": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, c_uint64,
                                            _P, _P, _P, _P]),
     "cign_silu_add_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, c_float, _P, _P, _P, _P,
                                      _P]),
     "cign_silu_add_ln_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
-    "cign_silu_add_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                     _P, c_size_t, _P]),
+    "cign_silu_add_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, _P, c_int32, _P, _P,
+                                     _P, _P, _P, _P, c_size_t, _P]),
     "cign_add_ln_fwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, c_float, _P, _P, _P, _P]),
     "cign_add_ln_bwd": (c_int, [c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                 c_size_t, _P]),

@@ -111,6 +111,55 @@ def _gate_pack_backward(ctx, gG, H, C, gate_w, alpha, props):
     return gH, gC, gw, gb
 
 
+def propagate_gate_pack_proj_forward_raw(H, C, gate_w, gate_b, proj_w, proj_b, plan, order_set,
+                                         gate_mode, keep_g):
+    """Forward of _PropagateGatePackProjFn on contiguous H, C: (out, saved) with
+    saved = [H, C, gate_w, alpha, proj_w, *props] (+ [G] when kept), the
+    tensors propagate_gate_pack_proj_backward_raw reads."""
+    props = _propagate(H, C, plan, order_set)
+    D, K = H.size(1), len(props)
+    fused = (not keep_g) if USE_TCGEN05_PACK_PROJ is None else USE_TCGEN05_PACK_PROJ
+    if (fused and torch.backends.cuda.matmul.allow_tf32
+            and _pack.pack_proj_supported(D, K, proj_w.size(0))):
+        alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
+        out, G = _pack.pack_proj_forward(H, C, props, alpha, proj_w, proj_b, keep_g)
+    else:
+        G, alpha = _gate_pack(H, C, props, gate_w, gate_b, gate_mode)
+        out = torch.addmm(proj_b, G, proj_w.t())
+        if not keep_g:
+            G = None
+    saved = [H, C, gate_w, alpha, proj_w, *props]
+    if G is not None:
+        saved.append(G)
+    return out, saved
+
+
+class _NodeState:
+    """The non-tensor state a propagate/gate/pack backward reads (the ctx
+    attributes of the autograd nodes that run it)."""
+
+    def __init__(self, plan, order_set, gate_mode, D):
+        self.plan, self.order_set, self.gate_mode, self.D = plan, tuple(order_set), gate_mode, D
+
+
+def propagate_gate_pack_proj_backward_raw(saved, g, plan, order_set, gate_mode):
+    """Backward of _PropagateGatePackProjFn from its saved tensors:
+    (gH, gC, g_gate_w, g_gate_b, g_proj_w, g_proj_b).  gH is a fresh tensor
+    written by the hop-gate backward (callers may accumulate into it)."""
+    H, C, gate_w, alpha, proj_w, *rest = saved
+    K = len(order_set)
+    props = rest[:K]
+    g = g.contiguous()
+    G = rest[K] if len(rest) > K else _pack.pack_forward(H, C, props, alpha, *PACK_MODES)
+    g_proj_w = _weight_grad(g, G)
+    del G
+    g_proj_b = colsum(g)
+    gG = g.mm(proj_w)
+    state = _NodeState(plan, order_set, gate_mode, H.size(1))
+    gH, gC, gw, gb = _gate_pack_backward(state, gG, H, C, gate_w, alpha, props)
+    return gH, gC, gw, gb, g_proj_w, g_proj_b
+
+
 class _PropagateGatePackProjFn(torch.autograd.Function):
     """The same node followed by the block's proj linear layer.
 
@@ -124,40 +173,17 @@ class _PropagateGatePackProjFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, H, C, gate_w, gate_b, proj_w, proj_b, plan, order_set, gate_mode, keep_g):
-        H = H.contiguous()
-        C = C.contiguous()
-        props = _propagate(H, C, plan, order_set)
-        D, K = H.size(1), len(props)
-        fused = (not keep_g) if USE_TCGEN05_PACK_PROJ is None else USE_TCGEN05_PACK_PROJ
-        if (fused and torch.backends.cuda.matmul.allow_tf32
-                and _pack.pack_proj_supported(D, K, proj_w.size(0))):
-            alpha = hop_gate_forward_raw(H, C, gate_w, gate_b, gate_mode)
-            out, G = _pack.pack_proj_forward(H, C, props, alpha, proj_w, proj_b, keep_g)
-        else:
-            G, alpha = _gate_pack(H, C, props, gate_w, gate_b, gate_mode)
-            out = torch.addmm(proj_b, G, proj_w.t())
-            if not keep_g:
-                G = None
-        saved = [H, C, gate_w, alpha, proj_w, *props]
-        ctx.keep_g = G is not None
-        if ctx.keep_g:
-            saved.append(G)
+        out, saved = propagate_gate_pack_proj_forward_raw(
+            H.contiguous(), C.contiguous(), gate_w, gate_b, proj_w, proj_b, plan, order_set,
+            gate_mode, keep_g)
         ctx.save_for_backward(*saved)
-        ctx.plan, ctx.order_set, ctx.gate_mode, ctx.D = plan, tuple(order_set), gate_mode, D
+        ctx.plan, ctx.order_set, ctx.gate_mode = plan, tuple(order_set), gate_mode
         return out
 
     @staticmethod
     def backward(ctx, g):
-        H, C, gate_w, alpha, proj_w, *rest = ctx.saved_tensors
-        K = len(ctx.order_set)
-        props = rest[:K]
-        g = g.contiguous()
-        G = rest[K] if ctx.keep_g else _pack.pack_forward(H, C, props, alpha, *PACK_MODES)
-        g_proj_w = _weight_grad(g, G)
-        del G
-        g_proj_b = colsum(g)
-        gG = g.mm(proj_w)
-        gH, gC, gw, gb = _gate_pack_backward(ctx, gG, H, C, gate_w, alpha, props)
+        gH, gC, gw, gb, g_proj_w, g_proj_b = propagate_gate_pack_proj_backward_raw(
+            list(ctx.saved_tensors), g, ctx.plan, ctx.order_set, ctx.gate_mode)
         return gH, gC, gw, gb, g_proj_w, g_proj_b, None, None, None, None
 
 

@@ -342,11 +342,16 @@ def silu_add_ln_forward(lin, bias, h, weight, ln_bias, eps):
     return y, pre, mean, rstd
 
 
-def silu_add_ln_backward(grad_y, pre, h, weight, mean, rstd):
-    """(grad_z, grad_pre, grad_w, grad_b, grad_bias) of cign_silu_add_ln_bwd."""
+def silu_add_ln_backward(grad_y, pre, h, weight, mean, rstd, grad_h=None):
+    """(grad_z, grad_pre, grad_w, grad_b, grad_bias) of cign_silu_add_ln_bwd.
+    With grad_h given (h's gradient from its other consumers, [N, D]), grad_z
+    is added into it in place and grad_h is returned as grad_z."""
     lib = ensure_collapsed_gat_loaded()
     n, D = (int(v) for v in pre.shape)
-    gz = torch.empty_like(pre)
+    acc = grad_h is not None
+    if acc and (grad_h.shape != pre.shape or not grad_h.is_contiguous()):
+        raise ValueError("grad_h must be a contiguous [N, D] tensor")
+    gz = grad_h if acc else torch.empty_like(pre)
     gpre = torch.empty_like(pre)
     gw = torch.empty((D,), dtype=torch.float32, device=pre.device)
     gb = torch.empty_like(gw)
@@ -355,7 +360,8 @@ def silu_add_ln_backward(grad_y, pre, h, weight, mean, rstd):
     with _lib.DeviceGuard(pre.device):
         rc = lib.cign_silu_add_ln_bwd(n, D, _lib.ptr(grad_y), _lib.ptr(pre), _lib.ptr(h),
                                       _lib.ptr(weight), _lib.ptr(mean), _lib.ptr(rstd),
-                                      _lib.ptr(gz), _lib.ptr(gpre), _lib.ptr(gw), _lib.ptr(gb),
+                                      int(acc), _lib.ptr(gz), _lib.ptr(gpre), _lib.ptr(gw),
+                                      _lib.ptr(gb),
                                       _lib.ptr(gbias), _lib.ptr(ws), ws.numel(),
                                       _lib.stream_of(pre))
     _lib.check(rc, "cign_silu_add_ln_bwd")
@@ -443,6 +449,60 @@ def _logit_vectors(weight: torch.Tensor, att_src: torch.Tensor, att_dst: torch.T
     return V2.transpose(0, 1).reshape(2 * H, D), A
 
 
+def gat_context_lin_forward_raw(x, weight, att_src, att_dst, plan, heads, n_dst, negative_slope,
+                                attn_drop, seed):
+    """Forward of _GatContextLinFn: (lin [n_dst, C], saved) with saved the
+    tensors its backward needs besides x and weight."""
+    H = int(heads)
+    V, A = _logit_vectors(weight, att_src, att_dst, H)
+    alpha = row_dots_forward(x, V)                                                  # [N, 2H]
+    attn_col = alpha[:, :H].contiguous()
+    attn_row = alpha[:n_dst, H:].contiguous()
+    n, D = int(plan.n), int(x.size(1))
+    z, emax, esum = gat_agg_forward_raw(plan, attn_row, attn_col, x, H, negative_slope,
+                                        attn_drop, seed)
+    M = _head_projection(weight, H)
+    lin = z.view(n, H * D).mm(M)
+    del z
+    return lin, (attn_row, attn_col, emax, esum, V, A)
+
+
+def gat_context_lin_backward_raw(x, weight, saved, g_lin, plan, heads, n_dst, att_shape,
+                                 negative_slope, attn_drop, seed, grad_x=None):
+    """Backward of _GatContextLinFn: (grad_x, grad_w, grad_att_src, grad_att_dst).
+    With grad_x given ([N_src, D], x's gradient from its other consumers) the
+    GAT's share is added into it in place (beta = 1 GEMM, then the logit
+    term), with no separate add."""
+    attn_row, attn_col, emax, esum, V, A = saved
+    H = int(heads)
+    n_src, D = (int(s) for s in x.shape)
+    HC = int(weight.size(0))
+    C = HC // H
+    g_pre = g_lin.contiguous()
+    M = _head_projection(weight, H)
+    grad_z = g_pre.mm(M.t())                                                        # [N, H*D]
+    gfeat, grow, gcol = gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z,
+                                             g_pre, negative_slope, attn_drop, seed)
+    del grad_z
+    gfeat2 = gfeat.view(n_src, HC)
+    if grad_x is None:
+        grad_x = gfeat2.mm(weight)                                                  # [N_src, D]
+    else:
+        grad_x.addmm_(gfeat2, weight)
+    g_alpha = torch.zeros((n_src, 2 * H), dtype=torch.float32, device=x.device)
+    g_alpha[:, :H] = gcol
+    g_alpha[:n_dst, H:] = grow
+    gV = row_dots_backward(x, V, g_alpha, grad_x, accumulate=True)                  # [2H, D]
+    gV2 = gV.view(2, H, D).transpose(0, 1)                                          # [H, 2, D]
+    with _full_fp32_matmul():
+        g_att = torch.bmm(weight.view(H, C, D), gV2.transpose(1, 2))                 # [H, C, 2]
+        g_w_att = torch.bmm(A.transpose(1, 2), gV2)                                  # [H, C, D]
+    grad_w = torch.addmm(g_w_att.reshape(HC, D), gfeat2.t(), x)                     # [H*C, D]
+    g_src = g_att[:, :, 0].reshape(att_shape)
+    g_dst = g_att[:, :, 1].reshape(att_shape)
+    return grad_x, grad_w, g_src, g_dst
+
+
 class _GatContextLinFn(torch.autograd.Function):
     """The GAT context of a CIGN block up to its bias: lin(x) -> attention
     logits (fused_gat_sideops.py:50-71) -> collapsed GAT head mean
@@ -463,49 +523,19 @@ class _GatContextLinFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, att_src, att_dst, plan, heads, n_dst, negative_slope, attn_drop,
                 seed):
-        H = int(heads)
-        V, A = _logit_vectors(weight, att_src, att_dst, H)
-        alpha = row_dots_forward(x, V)                                              # [N, 2H]
-        attn_col = alpha[:, :H].contiguous()
-        attn_row = alpha[:n_dst, H:].contiguous()
-        n, D = int(plan.n), int(x.size(1))
-        z, emax, esum = gat_agg_forward_raw(plan, attn_row, attn_col, x, H, negative_slope,
-                                            attn_drop, seed)
-        M = _head_projection(weight, H)
-        lin = z.view(n, H * D).mm(M)
-        del z
-        ctx.save_for_backward(x, weight, attn_row, attn_col, emax, esum, V, A)
-        ctx.plan, ctx.heads, ctx.n_dst, ctx.att_shape = plan, H, int(n_dst), att_src.shape
+        lin, saved = gat_context_lin_forward_raw(x, weight, att_src, att_dst, plan, heads, n_dst,
+                                                 negative_slope, attn_drop, seed)
+        ctx.save_for_backward(x, weight, *saved)
+        ctx.plan, ctx.heads, ctx.n_dst, ctx.att_shape = plan, int(heads), int(n_dst), att_src.shape
         ctx.negative_slope, ctx.attn_drop, ctx.seed = float(negative_slope), float(attn_drop), seed
         return lin
 
     @staticmethod
     def backward(ctx, g_lin):
-        x, weight, attn_row, attn_col, emax, esum, V, A = ctx.saved_tensors
-        H, n_dst = ctx.heads, ctx.n_dst
-        n_src, D = (int(s) for s in x.shape)
-        HC = int(weight.size(0))
-        C = HC // H
-        g_pre = g_lin.contiguous()
-        M = _head_projection(weight, H)
-        grad_z = g_pre.mm(M.t())                                                    # [N, H*D]
-        gfeat, grow, gcol = gat_agg_backward_raw(ctx.plan, attn_row, attn_col, x, emax, esum,
-                                                 grad_z, g_pre, ctx.negative_slope,
-                                                 ctx.attn_drop, ctx.seed)
-        del grad_z
-        gfeat2 = gfeat.view(n_src, HC)
-        grad_x = gfeat2.mm(weight)                                                  # [N_src, D]
-        g_alpha = torch.zeros((n_src, 2 * H), dtype=torch.float32, device=x.device)
-        g_alpha[:, :H] = gcol
-        g_alpha[:n_dst, H:] = grow
-        gV = row_dots_backward(x, V, g_alpha, grad_x, accumulate=True)              # [2H, D]
-        gV2 = gV.view(2, H, D).transpose(0, 1)                                      # [H, 2, D]
-        with _full_fp32_matmul():
-            g_att = torch.bmm(weight.view(H, C, D), gV2.transpose(1, 2))             # [H, C, 2]
-            g_w_att = torch.bmm(A.transpose(1, 2), gV2)                              # [H, C, D]
-        grad_w = torch.addmm(g_w_att.reshape(HC, D), gfeat2.t(), x)                 # [H*C, D]
-        g_src = g_att[:, :, 0].reshape(ctx.att_shape)
-        g_dst = g_att[:, :, 1].reshape(ctx.att_shape)
+        x, weight, *saved = ctx.saved_tensors
+        grad_x, grad_w, g_src, g_dst = gat_context_lin_backward_raw(
+            x, weight, saved, g_lin, ctx.plan, ctx.heads, ctx.n_dst, ctx.att_shape,
+            ctx.negative_slope, ctx.attn_drop, ctx.seed)
         return grad_x, grad_w, g_src, g_dst, None, None, None, None, None, None
 
 

@@ -52,19 +52,30 @@ int sm_count() {
 int build_segments(const int32_t* ptr_dev, int64_t rows, int seg_len, SegList* out) {
   *out = SegList();
   out->seg_len = seg_len;
+  if (rows <= 0) return CIGN_OK;
   std::vector<int32_t> ptr(static_cast<size_t>(rows) + 1);
   CIGN_CHECK_CUDA(cudaMemcpy(ptr.data(), ptr_dev, ptr.size() * sizeof(int32_t),
                              cudaMemcpyDeviceToHost),
                   "plan: copy row pointers");
   std::vector<std::pair<int32_t, int32_t>> heavy;  // (length, row)
+  // light rows bucketed by length (counting sort: longest first, ties in row order)
+  std::vector<int64_t> bucket(static_cast<size_t>(seg_len) + 2, 0);
   int32_t max_len = 0;
   for (int64_t r = 0; r < rows; ++r) {
     const int32_t len = ptr[r + 1] - ptr[r];
     max_len = std::max(max_len, len);
     if (len > seg_len) heavy.emplace_back(len, static_cast<int32_t>(r));
+    else ++bucket[static_cast<size_t>(seg_len - len) + 1];
   }
   out->max_len = max_len;
-  if (heavy.empty()) return CIGN_OK;
+  for (size_t b = 1; b < bucket.size(); ++b) bucket[b] += bucket[b - 1];
+  const int64_t n_light = bucket.back();
+  std::vector<int32_t> light(static_cast<size_t>(n_light));
+  for (int64_t r = 0; r < rows; ++r) {
+    const int32_t len = ptr[r + 1] - ptr[r];
+    if (len <= seg_len) light[static_cast<size_t>(bucket[static_cast<size_t>(seg_len - len)]++)] =
+        static_cast<int32_t>(r);
+  }
   std::stable_sort(heavy.begin(), heavy.end(),
                    [](const std::pair<int32_t, int32_t>& a,
                       const std::pair<int32_t, int32_t>& b) { return a.first > b.first; });
@@ -83,12 +94,13 @@ int build_segments(const int32_t* ptr_dev, int64_t rows, int seg_len, SegList* o
   const int64_t n_seg = static_cast<int64_t>(srow.size());
   const int64_t n_heavy = static_cast<int64_t>(hrow.size());
   std::vector<int32_t> host;
-  host.reserve(3 * n_seg + 2 * n_heavy + 1);
+  host.reserve(3 * n_seg + 2 * n_heavy + 1 + n_light);
   host.insert(host.end(), srow.begin(), srow.end());
   host.insert(host.end(), sbeg.begin(), sbeg.end());
   host.insert(host.end(), send.begin(), send.end());
   host.insert(host.end(), hrow.begin(), hrow.end());
   host.insert(host.end(), hfirst.begin(), hfirst.end());
+  host.insert(host.end(), light.begin(), light.end());
   int32_t* d = nullptr;
   CIGN_CHECK_CUDA(cudaMalloc(&d, host.size() * sizeof(int32_t)), "plan: cudaMalloc segments");
   cudaError_t e = cudaMemcpy(d, host.data(), host.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
@@ -99,6 +111,7 @@ int build_segments(const int32_t* ptr_dev, int64_t rows, int seg_len, SegList* o
   out->buf = d;
   out->n_seg = n_seg;
   out->n_heavy = n_heavy;
+  out->n_light = n_light;
   return CIGN_OK;
 }
 

@@ -133,14 +133,17 @@ ln_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ x, const float* __
 
 // ---------------------------------------------------------------- backward
 // grad wrt the normalised input (dq) plus per-chunk partials of
-// sum(gy * xhat) and sum(gy) for the LN weight and bias.
+// sum(gy * xhat) and sum(gy) for the LN weight and bias.  With addend !=
+// NULL the row's addend [n, D] is added to the written gradient (a second
+// consumer's gradient of the same input, e.g. a residual branch).
 template <int MODE, int VEC, int VPL, int LPR>
 __global__ void __launch_bounds__(kThreads, VPL <= 4 ? 3 : 1)
 ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
               const float* __restrict__ x, const float* __restrict__ x2,
               const float* __restrict__ w, const float* __restrict__ mean,
               const float* __restrict__ rstd, float p, Seed seed_in,
-              float* __restrict__ gx, float* __restrict__ pw, float* __restrict__ pb) {
+              const float* __restrict__ addend, float* __restrict__ gx,
+              float* __restrict__ pw, float* __restrict__ pb) {
   const uint64_t seed = seed_in;
   using V = typename VecT<VEC>::type;
   using Cfg = RowCfg<VEC, VPL, LPR>;
@@ -216,6 +219,7 @@ ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
           const float dq = (rs / Df) * (Df * dnorm - s1 - xhat * s2);
           vel(o, j) = MODE == 0 ? (keep ? dq * scale : 0.0f) : dq;
         }
+        if (addend != nullptr) vadd(o, ld_vec<VEC>(addend + row * D + d));
         st_vec(gx + row * D + d, o);
       }
     }
@@ -400,7 +404,7 @@ __global__ void __launch_bounds__(kThreads)
 silu_add_ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
                        const float* __restrict__ pre, const float* __restrict__ h,
                        const float* __restrict__ w, const float* __restrict__ mean,
-                       const float* __restrict__ rstd, float* __restrict__ gz,
+                       const float* __restrict__ rstd, bool acc_z, float* __restrict__ gz,
                        float* __restrict__ gpre, float* __restrict__ pw,
                        float* __restrict__ pb, float* __restrict__ pbias) {
   using V = typename VecT<VEC>::type;
@@ -462,6 +466,7 @@ silu_add_ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restric
           vel(op, j) = dq * silu_grad_f(vel(pv[k], j));
           vel(ag[k], j) += vel(op, j);
         }
+        if (acc_z) vadd(oz, ld_vec<VEC>(gz + row * D + d));
         st_vec(gz + row * D + d, oz);
         st_vec(gpre + row * D + d, op);
       }
@@ -528,13 +533,14 @@ int launch_ln_fwd(int64_t n, int64_t D, const float* x, const float* x2, const f
 template <int MODE, int VEC, int VPL, int LPR>
 int launch_ln_bwd(int64_t n, int64_t D, const float* gy, const float* x, const float* x2,
                   const float* w, const float* mean, const float* rstd, float p, Seed seed,
-                  float* gx, float* gw, float* gb, float* ws, cudaStream_t s) {
+                  float* gx, float* gw, float* gb, float* ws, cudaStream_t s,
+                  const float* addend = nullptr) {
   const int64_t rpc = rows_per_chunk(n);
   const int64_t chunks = num_chunks(n);
   float* pw = ws;
   float* pb = ws + chunks * D;
   ln_bwd_kernel<MODE, VEC, VPL, LPR><<<static_cast<unsigned>(chunks), kThreads, 0, s>>>(
-      n, D, rpc, gy, x, x2, w, mean, rstd, p, seed, gx, pw, pb);
+      n, D, rpc, gy, x, x2, w, mean, rstd, p, seed, addend, gx, pw, pb);
   CIGN_CHECK_LAUNCH("ln_bwd_kernel");
   return colsum_rows(pw, gw, pb, gb, chunks, D, D, s);
 }
@@ -554,15 +560,15 @@ int launch_silu_add_ln_fwd(int64_t n, int64_t D, const float* lin, const float* 
 template <int VEC, int VPL, int LPR>
 int launch_silu_add_ln_bwd(int64_t n, int64_t D, const float* gy, const float* pre,
                            const float* h, const float* w, const float* mean, const float* rstd,
-                           float* gz, float* gpre, float* gw, float* gb, float* gbias, float* ws,
-                           cudaStream_t s) {
+                           bool acc_z, float* gz, float* gpre, float* gw, float* gb, float* gbias,
+                           float* ws, cudaStream_t s) {
   const int64_t rpc = rows_per_chunk(n, kSiluLnChunkTarget);
   const int64_t chunks = num_chunks(n, kSiluLnChunkTarget);
   float* pw = ws;
   float* pb = ws + chunks * D;
   float* pbias = ws + 2 * chunks * D;
   silu_add_ln_bwd_kernel<VEC, VPL, LPR><<<static_cast<unsigned>(chunks), kThreads, 0, s>>>(
-      n, D, rpc, gy, pre, h, w, mean, rstd, gz, gpre, pw, pb, pbias);
+      n, D, rpc, gy, pre, h, w, mean, rstd, acc_z, gz, gpre, pw, pb, pbias);
   CIGN_CHECK_LAUNCH("silu_add_ln_bwd_kernel");
   int rc = colsum_rows(pw, gw, pb, gb, chunks, D, D, s);
   if (rc) return rc;
@@ -638,6 +644,37 @@ int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* 
     CIGN_ROW_DISPATCH(4, d / 4, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s)));
   }
   CIGN_ROW_DISPATCH(1, d, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s)));
+  return CIGN_OK;
+}
+
+int cign_dropout_ln_bwd_add(int64_t n, int64_t d, const float* grad_y, const float* x,
+                            const float* w, const float* mean, const float* rstd, float p,
+                            uint64_t seed_value, const uint64_t* seed_ptr, const float* addend,
+                            float* grad_x, float* grad_w, float* grad_b, void* ws,
+                            size_t ws_bytes, cign_stream_t stream) {
+  const Seed seed{seed_value, seed_ptr};
+  const bool v4 = d % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(grad_y) &&
+                  aligned16(grad_x) && aligned16(addend);
+  int rc = check_rows(n, d, v4, "dropout_ln_bwd_add");
+  if (rc) return rc;
+  CIGN_REQUIRE(grad_w && grad_b, CIGN_ERR_NULL_POINTER, "dropout_ln_bwd_add: NULL param grad");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_w, 0, d * sizeof(float), s), "memset");
+    CIGN_CHECK_CUDA(cudaMemsetAsync(grad_b, 0, d * sizeof(float), s), "memset");
+    return CIGN_OK;
+  }
+  CIGN_REQUIRE(grad_y && x && w && mean && rstd && grad_x && addend, CIGN_ERR_NULL_POINTER,
+               "dropout_ln_bwd_add: NULL");
+  CIGN_REQUIRE(addend != grad_x, CIGN_ERR_INVALID_ARGUMENT,
+               "dropout_ln_bwd_add: addend must not alias grad_x");
+  CIGN_REQUIRE(ws && ws_bytes >= cign_ln_bwd_workspace_bytes(n, d), CIGN_ERR_INVALID_ARGUMENT,
+               "dropout_ln_bwd_add: workspace too small");
+  float* wsf = static_cast<float*>(ws);
+  if (v4) {
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s, addend)));
+  }
+  CIGN_ROW_DISPATCH(1, d, return (launch_ln_bwd<0, V_, P_, L_>(n, d, grad_y, x, nullptr, w, mean, rstd, p, seed, grad_x, grad_w, grad_b, wsf, s, addend)));
   return CIGN_OK;
 }
 
@@ -761,8 +798,9 @@ size_t cign_silu_add_ln_bwd_workspace_bytes(int64_t n, int64_t d) {
 
 int cign_silu_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* pre,
                          const float* h, const float* w, const float* mean, const float* rstd,
-                         float* grad_z, float* grad_pre, float* grad_w, float* grad_b,
-                         float* grad_bias, void* ws, size_t ws_bytes, cign_stream_t stream) {
+                         int accumulate_z, float* grad_z, float* grad_pre, float* grad_w,
+                         float* grad_b, float* grad_bias, void* ws, size_t ws_bytes,
+                         cign_stream_t stream) {
   const bool v4 = d % 4 == 0 && aligned16(grad_y) && aligned16(pre) && aligned16(h) &&
                   aligned16(w) && aligned16(grad_z) && aligned16(grad_pre);
   int rc = check_rows(n, d, v4, "silu_add_ln_bwd");
@@ -782,9 +820,9 @@ int cign_silu_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float*
                CIGN_ERR_INVALID_ARGUMENT, "silu_add_ln_bwd: workspace too small");
   float* wsf = static_cast<float*>(ws);
   if (v4) {
-    CIGN_ROW_DISPATCH(4, d / 4, return (launch_silu_add_ln_bwd<V_, P_, L_>(n, d, grad_y, pre, h, w, mean, rstd, grad_z, grad_pre, grad_w, grad_b, grad_bias, wsf, s)));
+    CIGN_ROW_DISPATCH(4, d / 4, return (launch_silu_add_ln_bwd<V_, P_, L_>(n, d, grad_y, pre, h, w, mean, rstd, accumulate_z != 0, grad_z, grad_pre, grad_w, grad_b, grad_bias, wsf, s)));
   }
-  CIGN_ROW_DISPATCH(1, d, return (launch_silu_add_ln_bwd<V_, P_, L_>(n, d, grad_y, pre, h, w, mean, rstd, grad_z, grad_pre, grad_w, grad_b, grad_bias, wsf, s)));
+  CIGN_ROW_DISPATCH(1, d, return (launch_silu_add_ln_bwd<V_, P_, L_>(n, d, grad_y, pre, h, w, mean, rstd, accumulate_z != 0, grad_z, grad_pre, grad_w, grad_b, grad_bias, wsf, s)));
   return CIGN_OK;
 }
 

@@ -58,12 +58,20 @@ int sm_count();
 // which keeps the sum order fixed (deterministic).  Rows of at most seg_len
 // entries are processed whole.  One device buffer holds
 //   seg_row[n_seg] | seg_begin[n_seg] | seg_end[n_seg] |
-//   heavy_row[n_heavy] | heavy_first[n_heavy + 1]
+//   heavy_row[n_heavy] | heavy_first[n_heavy + 1] | light_row[n_light]
 // (segments of heavy row h are heavy_first[h] .. heavy_first[h+1]-1).
+// light_row lists the other rows (at most seg_len entries, empty rows
+// included) by length, longest first, ties in row order.  Kernels that
+// take whole rows from it give the warps of one CTA rows of (nearly) the
+// same length, so a CTA does not hold its SM slot with most of its warps
+// finished while one long row completes, and the longest rows start first.
+// The order only decides which warp computes a row, not how: every row's
+// result is the same as with rows taken in index order.
 struct SegList {
   int32_t* buf = nullptr;  // device
   int64_t n_seg = 0;
   int64_t n_heavy = 0;
+  int64_t n_light = 0;
   int32_t max_len = 0;
   int32_t seg_len = 0;
   const int32_t* seg_row() const { return buf; }
@@ -71,10 +79,12 @@ struct SegList {
   const int32_t* seg_end() const { return buf + 2 * n_seg; }
   const int32_t* heavy_row() const { return buf + 3 * n_seg; }
   const int32_t* heavy_first() const { return buf + 3 * n_seg + n_heavy; }
+  const int32_t* light_row() const { return buf + 3 * n_seg + 2 * n_heavy + 1; }
 };
 
 // Reads the device pointer array (int32 [rows+1]) to the host and builds the
-// segment list (heavy rows ordered by length, longest first).  Plan time only.
+// segment list (heavy rows ordered by length, longest first) and the
+// length-ordered light-row list.  Plan time only.
 int build_segments(const int32_t* ptr_dev, int64_t rows, int seg_len, SegList* out);
 void free_segments(SegList* s);
 

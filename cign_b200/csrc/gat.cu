@@ -1999,7 +1999,8 @@ struct AggCfg {
 // form inline, bit for bit (same reductions, same edge_weight).
 template <bool STATS>
 __global__ void __launch_bounds__(kThreads)
-gat_edge_weights_kernel(int n, int H, const int* __restrict__ rowptr, const int* __restrict__ col,
+gat_edge_weights_kernel(int n_light, const int* __restrict__ light, int H,
+                        const int* __restrict__ rowptr, const int* __restrict__ col,
                         const int* __restrict__ seg_row, const int* __restrict__ seg_begin,
                         const int* __restrict__ seg_end, int n_seg, int seg_blocks,
                         const float* __restrict__ attn_row, const float* __restrict__ attn_col,
@@ -2018,12 +2019,12 @@ gat_edge_weights_kernel(int n, int H, const int* __restrict__ rowptr, const int*
     e0 = seg_begin[item];
     e1 = seg_end[item];
     seg = true;
-  } else {
-    target = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
-    if (target >= n) return;
+  } else {  // light rows in the plan's length order
+    const int64_t li = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
+    if (li >= n_light) return;
+    target = light[li];
     e0 = rowptr[target];
     e1 = rowptr[target + 1];
-    if (e1 - e0 > kSegLen) return;  // hub: done by its segments
     seg = false;
   }
   const int k = e0 + lane;
@@ -2107,7 +2108,8 @@ gat_edge_weights_kernel(int n, int H, const int* __restrict__ rowptr, const int*
 template <int VPL, int MODE, bool ONE_PASS>
 // <= 64 registers (1024 threads of 64 registers per SM):
 __global__ void __launch_bounds__(kThreads, ONE_PASS ? 1024 / kThreads : 1)
-gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* __restrict__ idx,
+gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
+               const int* __restrict__ ptr, const int* __restrict__ idx,
                const int* __restrict__ perm, const int* __restrict__ seg_row,
                const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
                int seg_blocks, const float* __restrict__ wts, const float* __restrict__ src,
@@ -2133,12 +2135,12 @@ gat_agg_kernel(int n, int H, int64_t D, const int* __restrict__ ptr, const int* 
     e0 = seg_begin[item];
     e1 = seg_end[item];
     seg = true;
-  } else {
-    target = static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
-    if (target >= n) return;
+  } else {  // light rows (columns) in the plan's length order
+    const int64_t li = static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
+    if (li >= n_light) return;
+    target = light[li];
     e0 = ptr[target];
     e1 = ptr[target + 1];
-    if (e1 - e0 > kSegLen) return;  // hub: done by its segments + combine
     item = target;
     seg = false;
   }
@@ -2375,7 +2377,8 @@ gat_agg_fwd_bf16_kernel(int n, int H, int64_t D, const int* __restrict__ ptr,
 // grad_attn_row; hub segments write their dots to glog for the hub-row kernel.
 // <= 80 registers (768 threads of 80 registers per SM):
 __global__ void __launch_bounds__(kThreads, 768 / kThreads)
-gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
+gat_agg_dots_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
+                    const int* __restrict__ rowptr,
                     const int* __restrict__ col, const int* __restrict__ seg_row,
                     const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
                     int seg_blocks, const float* __restrict__ attn_row,
@@ -2403,12 +2406,12 @@ gat_agg_dots_kernel(int n, int H, int64_t D, const int* __restrict__ rowptr,
     e0 = seg_begin[sidx];
     e1 = seg_end[sidx];
     seg = true;
-  } else {
-    row = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
-    if (row >= n) return;
+  } else {  // light rows in the plan's length order
+    const int64_t li = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
+    if (li >= n_light) return;
+    row = light[li];
     e0 = rowptr[row];
     e1 = rowptr[row + 1];
-    if (e1 - e0 > kSegLen) return;
     seg = false;
   }
   const int k = e0 + lane;
@@ -2541,10 +2544,10 @@ int launch_edge_weights(const cign_gat_plan* pl, int H, const float* attn_row,
                         Seed seed, float* wts, cudaStream_t s) {
   const SegList& rs = pl->rows;
   const int64_t seg_blocks = (rs.n_seg + kThreads / 32 - 1) / (kThreads / 32);
-  const int64_t grid = seg_blocks + (pl->n + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t grid = seg_blocks + (rs.n_light + kThreads / 32 - 1) / (kThreads / 32);
   CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "gat edge weights: grid too large");
   gat_edge_weights_kernel<STATS><<<static_cast<unsigned>(grid), kThreads, 0, s>>>(
-      static_cast<int>(pl->n), H, pl->rowptr, pl->col, rs.seg_row(), rs.seg_begin(),
+      static_cast<int>(rs.n_light), rs.light_row(), H, pl->rowptr, pl->col, rs.seg_row(), rs.seg_begin(),
       rs.seg_end(), static_cast<int>(rs.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
       emax, esum, slope, p, seed, wts);
   CIGN_CHECK_LAUNCH("gat_edge_weights_kernel");
@@ -2557,21 +2560,20 @@ int launch_agg(const cign_gat_plan* pl, const SegList& sl, int H, int64_t D, con
                float* out, float* partial, const float* glog, float* gcol, float* pcol,
                cudaStream_t s) {
   using Cfg = AggCfg<VPL>;
-  const int64_t targets = MODE == 0 ? pl->n : pl->n_cols;
   const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
-  const int64_t grid = seg_blocks + (targets + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t grid = seg_blocks + (sl.n_light + Cfg::kGroups - 1) / Cfg::kGroups;
   const int64_t tiles = (D + Cfg::kTile - 1) / Cfg::kTile;
   CIGN_REQUIRE(grid < (1ll << 31) && tiles < 65536, CIGN_ERR_UNSUPPORTED, "gat_agg: grid too large");
   static_assert(Cfg::kSmem <= 48 * 1024, "aggregation ring exceeds the default shared memory");
   const dim3 g(static_cast<unsigned>(grid), static_cast<unsigned>(tiles));
   if (H <= kAggHB)
     gat_agg_kernel<VPL, MODE, true><<<g, kThreads, Cfg::kSmem, s>>>(
-        static_cast<int>(targets), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(),
+        static_cast<int>(sl.n_light), sl.light_row(), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(),
         sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), wts, src, out,
         partial, glog, gcol, pcol);
   else
     gat_agg_kernel<VPL, MODE, false><<<g, kThreads, Cfg::kSmem, s>>>(
-        static_cast<int>(targets), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(),
+        static_cast<int>(sl.n_light), sl.light_row(), H, D, ptr, idx, perm, sl.seg_row(), sl.seg_begin(),
         sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), wts, src, out,
         partial, glog, gcol, pcol);
   CIGN_CHECK_LAUNCH("gat_agg_kernel");
@@ -2941,7 +2943,7 @@ int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_
   // K1: dots U[i,h,:].X[j,:] and the softmax backward (rows)
   const SegList& rs = pl->rows;
   const int64_t seg_blocks = (rs.n_seg + kThreads / 32 - 1) / (kThreads / 32);
-  const int64_t grid = seg_blocks + (pl->n + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t grid = seg_blocks + (rs.n_light + kThreads / 32 - 1) / (kThreads / 32);
   CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "gat_agg_bwd: grid too large");
   {  // 64 KB of dynamic shared memory: opt in once per device
     static std::mutex mu;
@@ -2958,7 +2960,7 @@ int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_
     }
   }
   gat_agg_dots_kernel<<<static_cast<unsigned>(grid), kThreads, kDotsSmem, s>>>(
-      static_cast<int>(pl->n), heads, dim, pl->rowptr, pl->col, rs.seg_row(), rs.seg_begin(),
+      static_cast<int>(rs.n_light), rs.light_row(), heads, dim, pl->rowptr, pl->col, rs.seg_row(), rs.seg_begin(),
       rs.seg_end(), static_cast<int>(rs.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
       edge_max, edge_sum, grad_z, x, negative_slope, attn_drop, seed, glog, grad_attn_row);
   CIGN_CHECK_LAUNCH("gat_agg_dots_kernel");

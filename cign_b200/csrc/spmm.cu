@@ -116,16 +116,18 @@ __device__ __forceinline__ void gather_edges(
 }
 
 // Blocks [0, seg_blocks) process hub-row segments (one group each) into
-// `partial`; the remaining blocks process whole rows of at most kSegLen
-// non-zeros.  X is [rows of X, F] -- or, with X1 != NULL, the two column
+// `partial`; the remaining blocks process the whole rows of at most kSegLen
+// non-zeros, taken from the plan's length-ordered list `light` (n_light
+// entries, longest first).  X is [rows of X, F] -- or, with X1 != NULL, the two column
 // blocks [X | X1] of widths split and F - split held as separate row-major
 // matrices (split a multiple of the tile width, so a tile lies in one).
 template <int VEC, int VPL, int LPR, bool SPLIT = false>
 __global__ void __launch_bounds__(kThreads)
-spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__ col,
-                 const float* __restrict__ val, const int* __restrict__ seg_begin,
-                 const int* __restrict__ seg_end, int n_seg, int seg_blocks,
-                 const float* __restrict__ X, int64_t F, const float* __restrict__ X1,
+spmm_rows_kernel(int n_light, const int* __restrict__ light, const int* __restrict__ crow,
+                 const int* __restrict__ col, const float* __restrict__ val,
+                 const int* __restrict__ seg_begin, const int* __restrict__ seg_end, int n_seg,
+                 int seg_blocks, const float* __restrict__ X, int64_t F,
+                 const float* __restrict__ X1,
                  int64_t split, const float* __restrict__ addend,
                  float* __restrict__ Y, float* __restrict__ partial) {
   using V = typename VecT<VEC>::type;
@@ -164,12 +166,11 @@ spmm_rows_kernel(int rows, const int* __restrict__ crow, const int* __restrict__
     return;
   }
 
-  const int64_t row64 =
-      static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
-  if (row64 >= rows) return;
+  const int64_t item = static_cast<int64_t>(blockIdx.x - seg_blocks) * Cfg::kGroups + group;
+  if (item >= n_light) return;
+  const int64_t row64 = light[item];  // at most kSegLen non-zeros
   const int e0 = crow[row64];
   const int e1 = crow[row64 + 1];
-  if (e1 - e0 > kSegLen) return;  // a hub row: done by segments + combine
   gather_edges<VEC, VPL, LPR>(col, val, e0, e1, LPR, Xg, ldx, xf0, F, f0, lig, gmask, acc);
   float* yr = Y + row64 * F + f0;
   const float* ar = addend != nullptr ? addend + row64 * F + f0 : nullptr;
@@ -420,7 +421,7 @@ int launch_spmm_cfg(const cign_csr_f32& m, const SegList& sl, const float* X, in
                     const float* X1 = nullptr, int64_t split = 0) {
   using Cfg = SpmmCfg<VEC, VPL, LPR>;
   const int64_t seg_blocks = (sl.n_seg + Cfg::kGroups - 1) / Cfg::kGroups;
-  const int64_t light_blocks = (m.rows + Cfg::kGroups - 1) / Cfg::kGroups;
+  const int64_t light_blocks = (sl.n_light + Cfg::kGroups - 1) / Cfg::kGroups;
   const int64_t grid = seg_blocks + light_blocks;
   if (grid == 0) return CIGN_OK;
   CIGN_REQUIRE(grid < (1ll << 31), CIGN_ERR_UNSUPPORTED, "spmm: grid too large");
@@ -431,14 +432,14 @@ int launch_spmm_cfg(const cign_csr_f32& m, const SegList& sl, const float* X, in
   const dim3 g(static_cast<unsigned>(grid), static_cast<unsigned>(tiles));
   if (X1 != nullptr)
     spmm_rows_kernel<VEC, VPL, LPR, true><<<g, kThreads, 0, stream>>>(
-        static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
-        static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, X1, split, addend, Y,
-        partial);
+        static_cast<int>(sl.n_light), sl.light_row(), m.crow, m.col, m.val, sl.seg_begin(),
+        sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, X1, split,
+        addend, Y, partial);
   else
     spmm_rows_kernel<VEC, VPL, LPR, false><<<g, kThreads, 0, stream>>>(
-        static_cast<int>(m.rows), m.crow, m.col, m.val, sl.seg_begin(), sl.seg_end(),
-        static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, nullptr, 0, addend, Y,
-        partial);
+        static_cast<int>(sl.n_light), sl.light_row(), m.crow, m.col, m.val, sl.seg_begin(),
+        sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), X, F, nullptr, 0,
+        addend, Y, partial);
   CIGN_CHECK_LAUNCH("spmm_rows_kernel");
   return launch_spmm_combine<VEC>(sl, partial, F, addend, Y, stream);
 }

@@ -68,7 +68,9 @@ def dropout_ln_forward(x, w, b, p, eps, seed):
     return y, mean, rstd
 
 
-def dropout_ln_backward(gy, x, w, mean, rstd, p, seed):
+def dropout_ln_backward(gy, x, w, mean, rstd, p, seed, addend=None):
+    """(grad_x, grad_w, grad_b); with addend ([N, D], x's gradient from another
+    consumer) grad_x includes it (cign_dropout_ln_bwd_add, no separate add)."""
     lib = ensure_fused_block_ops_loaded()
     n, D = (int(s) for s in x.shape)
     gx = torch.empty_like(x)
@@ -76,11 +78,23 @@ def dropout_ln_backward(gy, x, w, mean, rstd, p, seed):
     gb = torch.empty_like(gw)
     ws = _lib.workspace(lib.cign_ln_bwd_workspace_bytes(n, D), x.device)
     with _lib.DeviceGuard(x.device):
-        rc = lib.cign_dropout_ln_bwd(n, D, _lib.ptr(gy), _lib.ptr(x), _lib.ptr(w), _lib.ptr(mean),
-                                     _lib.ptr(rstd), float(p), *_lib.seed_args(seed), _lib.ptr(gx),
-                                     _lib.ptr(gw), _lib.ptr(gb), _lib.ptr(ws), ws.numel(),
-                                     _lib.stream_of(x))
-    _lib.check(rc, "cign_dropout_ln_bwd")
+        if addend is None:
+            rc = lib.cign_dropout_ln_bwd(n, D, _lib.ptr(gy), _lib.ptr(x), _lib.ptr(w),
+                                         _lib.ptr(mean), _lib.ptr(rstd), float(p),
+                                         *_lib.seed_args(seed), _lib.ptr(gx), _lib.ptr(gw),
+                                         _lib.ptr(gb), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+            name = "cign_dropout_ln_bwd"
+        else:
+            addend = addend.contiguous()
+            if addend.shape != x.shape or addend.dtype != torch.float32:
+                raise ValueError("addend must be a float32 tensor shaped like x")
+            rc = lib.cign_dropout_ln_bwd_add(n, D, _lib.ptr(gy), _lib.ptr(x), _lib.ptr(w),
+                                             _lib.ptr(mean), _lib.ptr(rstd), float(p),
+                                             *_lib.seed_args(seed), _lib.ptr(addend),
+                                             _lib.ptr(gx), _lib.ptr(gw), _lib.ptr(gb),
+                                             _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+            name = "cign_dropout_ln_bwd_add"
+    _lib.check(rc, name)
     return gx, gw, gb
 
 

@@ -26,6 +26,9 @@ outer nonlinearity "none"):
     alpha  = softmax(hop_gate_mlp([H+C | |H-C|]))           hop_gate (fused)
     G_raw  = Clifford pack(H_norm, C_norm, T, alpha)        fused_clifford_*
     H'     = H + gamma * dropout(proj(G_raw))               fused_block_ops
+On an unpartitioned graph with these switches the whole block runs as one
+autograd node (block_node.cign_block), whose backward accumulates the
+gradients of H_norm and H in-kernel instead of with separate add passes.
 Net (model_cign.py:1160-1212): dropout, dual input projection + SiLU, L
 blocks, JK concat, LayerNorm, dropout, classifier.
 """
@@ -45,6 +48,7 @@ from .fused_gat_sideops import fused_attention_logits
 from .graph_operator import selected_sparse_powers
 from .input_proj import dual_input_projection
 from .block_fused import native_spmm_plan, propagate_gate_pack_proj
+from .block_node import block_node_applies, cign_block
 from .jk_norm import jk_layer_norm, jk_norm_supported
 from .hop_gate import fused_hop_gate
 from .linear import linear
@@ -182,7 +186,14 @@ class GraphCliffordBlock(nn.Module):
             gate_input = torch.cat([H_norm + C_norm, torch.abs(H_norm - C_norm)], dim=-1)
         return F.softmax(self.hop_gate_mlp(gate_input), dim=-1).unsqueeze(-1)
 
+    # run the whole block as one autograd node where it applies
+    # (cign_b200.block_node: gradients accumulated in-kernel, no add passes)
+    use_block_node = True
+
     def forward(self, H, graph_operator, gat_graph):
+        if (self.use_block_node and native_spmm_plan(graph_operator) is not None
+                and block_node_applies(self, H, graph_operator, gat_graph)):
+            return cign_block(self, H, graph_operator, gat_graph)
         p = self.dropout if self.training else 0.0
         H_norm = fused_dropout_layernorm(H, self.h_norm.weight, self.h_norm.bias, p, self.h_norm.eps)
         lin = self.context_gat.forward_lin(H_norm, gat_graph)

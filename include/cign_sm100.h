@@ -547,6 +547,18 @@ CIGN_API int cign_dropout_ln_bwd(int64_t n, int64_t d, const float* grad_y,
                         float* grad_x, float* grad_w, float* grad_b, void* ws,
                         size_t ws_bytes, cign_stream_t stream);
 
+/* cign_dropout_ln_bwd with the gradient of a second consumer of x added:
+ * grad_x = d LN(dropout(x)) / dx + addend (addend [n, d], not aliasing
+ * grad_x).  A CIGN block's input H feeds both its dropout-LayerNorm and its
+ * residual (model_cign.py:781 and :929); this writes H's whole gradient in
+ * the LayerNorm backward's own pass instead of a separate add. */
+CIGN_API int cign_dropout_ln_bwd_add(int64_t n, int64_t d, const float* grad_y,
+                        const float* x, const float* w, const float* mean,
+                        const float* rstd, float p, uint64_t seed,
+                              const uint64_t* seed_ptr, const float* addend,
+                        float* grad_x, float* grad_w, float* grad_b, void* ws,
+                        size_t ws_bytes, cign_stream_t stream);
+
 /* Allocation-free variant of cign_dropout_ln_bwd (this entry point has no
  * counterpart in the reference).  For callers that cannot allocate device
  * memory -- e.g. a plugin inside a host framework that owns all device memory
@@ -593,10 +605,12 @@ CIGN_API int cign_silu_add_ln_fwd(int64_t n, int64_t d, const float* lin, const 
 CIGN_API size_t cign_silu_add_ln_bwd_workspace_bytes(int64_t n, int64_t d);
 /* Backward of cign_silu_add_ln_fwd: grad_z = d LN / d(SiLU(pre) + h) (the
  * gradient of h), grad_pre = grad_z * SiLU'(pre) (the gradient of lin), and
- * the LN weight / bias and GAT bias gradients (fixed-order sums). */
+ * the LN weight / bias and GAT bias gradients (fixed-order sums).  With
+ * accumulate_z != 0, grad_z is added to what grad_z holds (h's gradient from
+ * its other consumers) instead of overwriting it. */
 CIGN_API int cign_silu_add_ln_bwd(int64_t n, int64_t d, const float* grad_y, const float* pre,
                          const float* h, const float* w, const float* mean,
-                         const float* rstd, float* grad_z, float* grad_pre,
+                         const float* rstd, int accumulate_z, float* grad_z, float* grad_pre,
                          float* grad_w, float* grad_b, float* grad_bias, void* ws,
                          size_t ws_bytes, cign_stream_t stream);
 

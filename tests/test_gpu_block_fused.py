@@ -19,11 +19,15 @@ from tests.helpers import assert_parity
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("block_node", [False, True])
 @pytest.mark.parametrize("recompute", [False, True])
 @pytest.mark.parametrize("hops,score", [((1, 2, 3), "new"), ((1, 3), "old"), ((2,), "new")])
-def test_fused_block_matches_op_by_op(cuda, monkeypatch, hops, score, recompute):
+def test_fused_block_matches_op_by_op(cuda, monkeypatch, hops, score, recompute, block_node):
     """recompute=True runs the node that also applies proj and recomputes
-    G_raw in the backward instead of keeping it."""
+    G_raw in the backward instead of keeping it; block_node=True runs the
+    whole block as one node (block_node.cign_block: in-kernel gradient
+    accumulation), block_node=False the fused propagate/gate/pack/proj node
+    inside the op-by-op block."""
     torch.backends.cuda.matmul.allow_tf32 = False
     n, in_dim, hidden = 800, 24, 64
     edge = synth.powerlaw_graph(n, 6000, seed=2).to(cuda)
@@ -39,6 +43,7 @@ def test_fused_block_matches_op_by_op(cuda, monkeypatch, hops, score, recompute)
     other = copy.deepcopy(model)
     for block in model.blocks:
         block.recompute_pack = recompute
+        block.use_block_node = block_node
     x = torch.randn(n, in_dim, device=cuda)
     y = torch.randint(0, 4, (n,), device=cuda)
     out = model(x, op)
@@ -89,3 +94,37 @@ def test_tcgen05_pack_proj_in_model(cuda, monkeypatch):
                 assert_parity(g, r, tol=2e-3, atol=1e-4, what=f"grad {name}")
     finally:
         torch.backends.cuda.matmul.allow_tf32 = False
+
+
+def test_block_node_with_dropout_matches_op_by_op(cuda):
+    """The whole-block node against the op-by-op block with every dropout on
+    (block dropout 0.5, attention dropout 0.3): the same seed draws in the
+    same order, so the same masks, logits and gradients."""
+    from cign_b200 import seeds
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n, in_dim, hidden, hops = 700, 20, 64, (1, 2, 3)
+    edge = synth.powerlaw_graph(n, 5000, seed=9).to(cuda)
+    ei, adj = build_sparse_normalized_adjacency(edge, n)
+    op = prepare_multihop_csr_operator(prepare_fixed_csr_operator(adj), dense_cols=2 * hidden,
+                                       powers=hops)
+    gat = to_graph_format(prepare_gat_edge_index(ei, n).flip(0), n)
+    torch.manual_seed(0)
+    model = mc.build_model(in_dim=in_dim, hidden_dim=hidden, out_dim=4, num_layers=2,
+                           dropout=0.5, hop_scales=hops, gat_heads=2, gat_dropout=0.3).to(cuda)
+    model.prepare_fused_gat_graph(gat)
+    other = copy.deepcopy(model)
+    for block in other.blocks:
+        block.use_block_node = False
+    x = torch.randn(n, in_dim, device=cuda)
+    y = torch.randint(0, 4, (n,), device=cuda)
+    counters = seeds.host_counters()
+    torch.manual_seed(1)  # the net's torch dropout on x and on the JK output
+    out = model(x, op)
+    F.cross_entropy(out, y).backward()
+    seeds.set_host_counters(*counters)
+    torch.manual_seed(1)
+    ref = other(x, op)
+    F.cross_entropy(ref, y).backward()
+    assert_parity(out.detach(), ref.detach(), what="logits")
+    for (name, p), (_, q) in zip(model.named_parameters(), other.named_parameters()):
+        assert_parity(p.grad, q.grad, what=f"grad {name}")
