@@ -399,8 +399,14 @@ silu_add_ln_fwd_kernel(int64_t n, int64_t D, const float* __restrict__ lin,
 // of the SiLU output c), grad_pre = grad_z * SiLU'(pre) (the gradient of lin),
 // and per-chunk partials of sum(gy * xhat), sum(gy) (LN weight and bias) and
 // sum(grad_pre) (the GAT bias), reduced in a fixed order like ln_bwd_kernel.
+// With acc_z the row's previous grad_z is added (h's gradient from its other
+// consumers).  Two passes over each row, as in ln_bwd_kernel: the first forms
+// the row sums and the LN parameter partials, the second re-reads pre, h and
+// gy (this warp's own recent loads) and writes grad_z and grad_pre, so a lane
+// keeps only the three parameter partials (<= 128 registers: two CTAs per
+// SM, the residency kSiluLnChunkTarget assumes).
 template <int VEC, int VPL, int LPR>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
 silu_add_ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restrict__ gy,
                        const float* __restrict__ pre, const float* __restrict__ h,
                        const float* __restrict__ w, const float* __restrict__ mean,
@@ -425,26 +431,20 @@ silu_add_ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restric
   const int64_t r1 = (r0 + rpc < n) ? (r0 + rpc) : n;
   for (int64_t row = r0 + group; row < r1; row += Cfg::kGroups) {
     const float mu = mean[row], rs = rstd[row];
-    V xh[VPL], dn[VPL], pv[VPL];
     float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
       const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
-      vzero(xh[k]);
-      vzero(dn[k]);
-      vzero(pv[k]);
       if (d < D) {
-        pv[k] = ld_vec<VEC>(pre + row * D + d);
+        const V pv = ld_vec<VEC>(pre + row * D + d);
         const V hv = ld_vec<VEC>(h + row * D + d);
         const V gv = ld_vec<VEC>(gy + row * D + d);
         const V wv = ldg_vec<VEC>(w + d);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const float qv = silu_f(vel(pv[k], j)) + vel(hv, j);
+          const float qv = silu_f(vel(pv, j)) + vel(hv, j);
           const float xhat = (qv - mu) * rs;
           const float dnorm = vel(gv, j) * vel(wv, j);
-          vel(xh[k], j) = xhat;
-          vel(dn[k], j) = dnorm;
           s1 += dnorm;
           s2 += dnorm * xhat;
           vel(aw[k], j) += vel(gv, j) * xhat;
@@ -458,15 +458,23 @@ silu_add_ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restric
     for (int k = 0; k < VPL; ++k) {
       const int64_t d = static_cast<int64_t>(lig + k * LPR) * VEC;
       if (d < D) {
+        const V pv = ld_vec<VEC>(pre + row * D + d);
+        const V hv = ld_vec<VEC>(h + row * D + d);
+        const V gv = ld_vec<VEC>(gy + row * D + d);
+        const V wv = ldg_vec<VEC>(w + d);
         V oz, op;
+        if (acc_z) oz = ld_vec<VEC>(gz + row * D + d);
+        else vzero(oz);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const float dq = (rs / Df) * (Df * vel(dn[k], j) - s1 - vel(xh[k], j) * s2);
-          vel(oz, j) = dq;
-          vel(op, j) = dq * silu_grad_f(vel(pv[k], j));
+          const float qv = silu_f(vel(pv, j)) + vel(hv, j);
+          const float xhat = (qv - mu) * rs;
+          const float dnorm = vel(gv, j) * vel(wv, j);
+          const float dq = (rs / Df) * (Df * dnorm - s1 - xhat * s2);
+          vel(oz, j) += dq;
+          vel(op, j) = dq * silu_grad_f(vel(pv, j));
           vel(ag[k], j) += vel(op, j);
         }
-        if (acc_z) vadd(oz, ld_vec<VEC>(gz + row * D + d));
         st_vec(gz + row * D + d, oz);
         st_vec(gpre + row * D + d, op);
       }

@@ -94,6 +94,7 @@ __device__ __forceinline__ unsigned group_mask() {
 }
 
 // Block-wide reductions over kThreads threads (all threads must call).
+template <int NT = kThreads>
 __device__ __forceinline__ float block_sum(float v, float* scratch) {
   v = warp_sum(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -102,9 +103,10 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   __syncthreads();
   float r = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kThreads / 32; ++i) r += scratch[i];
+  for (int i = 0; i < NT / 32; ++i) r += scratch[i];
   return r;
 }
+template <int NT = kThreads>
 __device__ __forceinline__ float block_max(float v, float* scratch) {
   v = warp_max(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -113,7 +115,7 @@ __device__ __forceinline__ float block_max(float v, float* scratch) {
   __syncthreads();
   float r = scratch[0];
 #pragma unroll
-  for (int i = 1; i < kThreads / 32; ++i) r = fmaxf(r, scratch[i]);
+  for (int i = 1; i < NT / 32; ++i) r = fmaxf(r, scratch[i]);
   return r;
 }
 
@@ -193,8 +195,13 @@ __device__ __forceinline__ void gat_gather(
 }
 
 // ------------------------------------------------------------ forward
-// Hub rows: CTA (hub, head) computes that head's max / exp-sum of the row.
-__global__ void __launch_bounds__(kThreads)
+// Hub rows: CTA (hub, head) of kHubThreads threads computes that head's
+// max / exp-sum of the row.  The largest hub of a power-law graph (thousands
+// of edges) sets these kernels' time: measured on the cfg2 graph, two-warp
+// CTAs took 2.8x longer than eight-warp ones despite fitting every hub in
+// one wave.
+constexpr int kHubThreads = kThreads;
+__global__ void __launch_bounds__(kHubThreads)
 gat_hub_stats_kernel(int H, const int* __restrict__ rowptr, const int* __restrict__ col,
                      const int* __restrict__ hub_row, const float* __restrict__ attn_row,
                      const float* __restrict__ attn_col, float slope,
@@ -205,13 +212,13 @@ gat_hub_stats_kernel(int H, const int* __restrict__ rowptr, const int* __restric
   const int e0 = rowptr[row], e1 = rowptr[row + 1];
   const float ad = attn_row[row * H + h];
   float m = kNegInit;
-  for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
+  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads)
     m = fmaxf(m, leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope));
-  m = block_max(m, scratch);
+  m = block_max<kHubThreads>(m, scratch);
   float s = 0.0f;
-  for (int e = e0 + threadIdx.x; e < e1; e += kThreads)
+  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads)
     s += expf(leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope) - m);
-  s = block_sum(s, scratch);
+  s = block_sum<kHubThreads>(s, scratch);
   if (threadIdx.x == 0) {
     emax[row * H + h] = m;
     esum[row * H + h] = s;
@@ -526,7 +533,7 @@ gat_bwd_rows_kernel(int n, int H, int64_t C, const int* __restrict__ rowptr,
 // Hub rows, CTA (hub, head): the softmax backward of that head over the
 // row's edges (dots already in glog from the segment groups); the head-0 CTA
 // also writes the row's g_pre.
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kHubThreads)
 gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
                         const int* __restrict__ col, const int* __restrict__ hub_row,
                         const float* __restrict__ attn_row, const float* __restrict__ attn_col,
@@ -539,22 +546,22 @@ gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
   const int64_t row = hub_row[blockIdx.x];
   const int h = blockIdx.y;
   if (h == 0 && grad_y != nullptr) {
-    for (int64_t c = threadIdx.x; c < C; c += kThreads)
+    for (int64_t c = threadIdx.x; c < C; c += kHubThreads)
       gpre[row * C + c] = grad_y[row * C + c] * silu_grad_f(pre[row * C + c]);
   }
   const int e0 = rowptr[row], e1 = rowptr[row + 1];
   const float ad = attn_row[row * H + h];
   const float m = emax[row * H + h], s = esum[row * H + h];
   float wsum = 0.0f;
-  for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
+  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads) {
     const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
                                   p, seed, static_cast<uint64_t>(e) * H + h,
                                   glog[static_cast<int64_t>(e) * H + h]);
     wsum += es.soft * es.ge;
   }
-  wsum = block_sum(wsum, scratch);
+  wsum = block_sum<kHubThreads>(wsum, scratch);
   float grow = 0.0f;
-  for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
+  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads) {
     const int64_t o = static_cast<int64_t>(e) * H + h;
     const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
                                   p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
@@ -563,7 +570,7 @@ gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
     glog[o] = gout;
     grow += gout;
   }
-  grow = block_sum(grow, scratch);
+  grow = block_sum<kHubThreads>(grow, scratch);
   if (threadIdx.x == 0) grad_attn_row[row * H + h] = grow;
 }
 
@@ -732,21 +739,47 @@ gat_bwd_cols_kernel(int n, int H, int64_t C, const int* __restrict__ colptr,
 // Hub-column combine: grad_feat[j] / grad_attn_col[j] = sums of the
 // column's segment partials in segment order.  Block (hub, chunk) covers
 // kCombineThreads * VEC of the H*C features; chunk 0 also does the H logits.
+// Its kSegCombineWays thread rows each sum a contiguous share of the
+// segments (the largest hub of a power-law graph has over a hundred), and
+// way 0 then adds the shares in way order: a fixed order, with a critical
+// path a share long instead of the whole segment list.
+constexpr int kSegCombineWays = 4;
 template <int VEC>
-__global__ void __launch_bounds__(kCombineThreads)
+__global__ void __launch_bounds__(kCombineThreads * kSegCombineWays)
 gat_bwd_cols_combine_kernel(int H, int64_t C, const int* __restrict__ hub_col,
                             const int* __restrict__ hub_first, const float* __restrict__ pfeat,
                             const float* __restrict__ pcol, float* __restrict__ grad_feat,
                             float* __restrict__ grad_attn_col) {
+  using V = typename VecT<VEC>::type;
+  __shared__ V part[kSegCombineWays - 1][kCombineThreads];
+  __shared__ float lpart[kSegCombineWays - 1][kCombineThreads];
+  const int tx = threadIdx.x % kCombineThreads, way = threadIdx.x / kCombineThreads;
   const int64_t j = hub_col[blockIdx.x];
   const int s0 = hub_first[blockIdx.x], s1 = hub_first[blockIdx.x + 1];
+  const int per = (s1 - s0 + kSegCombineWays - 1) / kSegCombineWays;
+  const int a = min(s1, s0 + way * per), b = min(s1, a + per);
   const int64_t HC = static_cast<int64_t>(H) * C;
-  const int64_t k = (static_cast<int64_t>(blockIdx.y) * kCombineThreads + threadIdx.x) * VEC;
-  if (k < HC) st_vec(grad_feat + j * HC + k, ordered_sum<VEC>(pfeat + k, HC, s0, s1));
-  if (blockIdx.y == 0 && pcol != nullptr) {
-    for (int h = threadIdx.x; h < H; h += kCombineThreads)
-      grad_attn_col[j * H + h] = ordered_sum<1>(pcol + h, H, s0, s1);
+  const int64_t k = (static_cast<int64_t>(blockIdx.y) * kCombineThreads + tx) * VEC;
+  const bool logits = blockIdx.y == 0 && pcol != nullptr;
+  V acc;
+  vzero(acc);
+  if (k < HC) acc = ordered_sum<VEC>(pfeat + k, HC, a, b);
+  // the H logit sums (H <= kCombineThreads), in the same shares
+  float lacc = 0.0f;
+  if (logits && tx < H) lacc = ordered_sum<1>(pcol + tx, H, a, b);
+  if (way > 0) {
+    part[way - 1][tx] = acc;
+    lpart[way - 1][tx] = lacc;
   }
+  __syncthreads();
+  if (way > 0) return;
+#pragma unroll
+  for (int w = 0; w < kSegCombineWays - 1; ++w) {
+    vadd(acc, part[w][tx]);
+    lacc += lpart[w][tx];
+  }
+  if (k < HC) st_vec(grad_feat + j * HC + k, acc);
+  if (logits && tx < H) grad_attn_col[j * H + tx] = lacc;
 }
 
 // ------------------------------------------------------------ misc kernels
@@ -1203,7 +1236,7 @@ int launch_hub_stats(const cign_gat_plan* pl, int H, const float* attn_row, cons
                      float slope, float* emax, float* esum, cudaStream_t s) {
   const SegList& sl = pl->rows;
   if (sl.n_heavy == 0) return CIGN_OK;
-  gat_hub_stats_kernel<<<dim3(static_cast<unsigned>(sl.n_heavy), H), kThreads, 0, s>>>(
+  gat_hub_stats_kernel<<<dim3(static_cast<unsigned>(sl.n_heavy), H), kHubThreads, 0, s>>>(
       H, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, slope, emax, esum);
   CIGN_CHECK_LAUNCH("gat_hub_stats_kernel");
   return CIGN_OK;
@@ -1247,7 +1280,7 @@ int launch_bwd_hub_rows(const cign_gat_plan* pl, int H, int64_t C, const float* 
                         float* gpre, float* glog, float* grow, cudaStream_t s) {
   const SegList& sl = pl->rows;
   if (sl.n_heavy == 0) return CIGN_OK;
-  gat_bwd_hub_rows_kernel<<<dim3(static_cast<unsigned>(sl.n_heavy), H), kThreads, 0, s>>>(
+  gat_bwd_hub_rows_kernel<<<dim3(static_cast<unsigned>(sl.n_heavy), H), kHubThreads, 0, s>>>(
       H, C, pl->rowptr, pl->col, sl.heavy_row(), attn_row, attn_col, pre, emax, esum, gy, slope,
       p, seed, gpre, glog, grow);
   CIGN_CHECK_LAUNCH("gat_bwd_hub_rows_kernel");
@@ -1271,11 +1304,13 @@ int launch_seg_combine(const SegList& sl, int H, int64_t C, const float* pfeat, 
   const bool v4 = combine_v4(HC, {pfeat, gfeat});
   const dim3 grid(static_cast<unsigned>(sl.n_heavy), combine_chunks(HC, v4 ? 4 : 1));
   CIGN_REQUIRE(grid.y < 65536, CIGN_ERR_UNSUPPORTED, "gat: H*C too large for the hub combine");
+  CIGN_REQUIRE(pcol == nullptr || H <= kCombineThreads, CIGN_ERR_UNSUPPORTED,
+               "gat: too many heads for the hub combine");
   if (v4)
-    gat_bwd_cols_combine_kernel<4><<<grid, kCombineThreads, 0, s>>>(
+    gat_bwd_cols_combine_kernel<4><<<grid, kCombineThreads * kSegCombineWays, 0, s>>>(
         H, C, sl.heavy_row(), sl.heavy_first(), pfeat, pcol, gfeat, gcol);
   else
-    gat_bwd_cols_combine_kernel<1><<<grid, kCombineThreads, 0, s>>>(
+    gat_bwd_cols_combine_kernel<1><<<grid, kCombineThreads * kSegCombineWays, 0, s>>>(
         H, C, sl.heavy_row(), sl.heavy_first(), pfeat, pcol, gfeat, gcol);
   CIGN_CHECK_LAUNCH("gat_bwd_cols_combine_kernel");
   return CIGN_OK;
