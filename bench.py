@@ -111,7 +111,6 @@ def step_roofline_items(cfg, nnz, nnz_g):
     add("GAT aggregate fwd", L, algorithmic_bytes("gat_agg_fwd", N, nnz, H=H, D=D, nnz_g=nnz_g))
     add("GAT z.M (GEMM)", L, *gemm(N, D, HD))
     add("GAT bias+SiLU + add-LN fwd", L, 16 * N * D + 8 * N)
-    add("[H|C] concat", L, 16 * N * D)
     add("k-hop SpMM fwd hop", L * K, algorithmic_bytes("spmm", N, nnz, F=F2))
     add("hop gate + pack fwd", L, algorithmic_bytes("gate_pack_fwd", N, nnz, K=K, D=D))
     add("proj (GEMM)", L, *gemm(N, D, 2 * K * D))
@@ -127,7 +126,9 @@ def step_roofline_items(cfg, nnz, nnz_g):
     add("output dropout bwd", 1, 9 * N * S * D)
     add("JK LayerNorm bwd (+ parameter pass)", 1, 20 * N * S * D + 8 * N)
     # backward, per block
-    add("block-state gradient sums", 2 * L, 12 * N * D)
+    # block states H_0 .. H_{L-1}: the JK LayerNorm's gradient meets the next
+    # block's (the block node adds its own residual share in-kernel)
+    add("block-state gradient sums", L, 12 * N * D)
     add("dropout-gamma-residual bwd", L, 12 * N * D)
     add("proj dgrad (GEMM)", L, *gemm(N, 2 * K * D, D))
     add("proj wgrad (GEMM)", L, *gemm(D, 2 * K * D, N))
@@ -136,15 +137,16 @@ def step_roofline_items(cfg, nnz, nnz_g):
     add("k-hop SpMM bwd hop (+g fused)", L * (K - 1), algorithmic_bytes("spmm_add", N, nnz, F=F2))
     add("k-hop SpMM bwd hop", L, algorithmic_bytes("spmm", N, nnz, F=F2))
     add("hop gate bwd (+ gradient adds)", L, 24 * N * D + 8 * N * K)
-    add("GAT bias+SiLU + add-LN bwd (+ parameter sums)", L, 20 * N * D + 8 * N)
+    add("GAT bias+SiLU + add-LN bwd (+ parameter sums, grad H_norm += in place)", L,
+        24 * N * D + 8 * N)
     add("GAT grad z (GEMM)", L, *gemm(N, HD, D))
     add("GAT aggregate bwd", L, algorithmic_bytes("gat_agg_bwd", N, nnz, H=H, C=D, D=D,
                                                    nnz_g=nnz_g))
     add("GAT lin wgrad (GEMM)", L, *gemm(HD, D, N))
-    add("GAT input dgrad (GEMM)", L, *gemm(N, D, HD))
+    g_in = gemm(N, D, HD)
+    add("GAT input dgrad (GEMM, beta = 1 into grad H_norm)", L, g_in[0] + 4 * N * D, g_in[1])
     add("GAT logits bwd (row dots, added into grad x)", L, 12 * N * D + 8 * N * H)
-    add("H_norm gradient sums", 2 * L, 12 * N * D)
-    add("dropout-LN bwd", L, 12 * N * D + 8 * N)
+    add("dropout-LN bwd (+ the residual's gradient)", L, 16 * N * D + 8 * N)
     # backward, net input
     add("input SiLU mix bwd", 1, 20 * N * D)
     add("input projections wgrad (one GEMM)", 1, *gemm(2 * D, I, N))
