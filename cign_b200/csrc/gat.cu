@@ -201,6 +201,7 @@ __device__ __forceinline__ void gat_gather(
 // CTAs took 2.8x longer than eight-warp ones despite fitting every hub in
 // one wave.
 constexpr int kHubThreads = kThreads;
+constexpr int kHubBatch = 4;  // edges per thread whose loads are in flight together
 __global__ void __launch_bounds__(kHubThreads)
 gat_hub_stats_kernel(int H, const int* __restrict__ rowptr, const int* __restrict__ col,
                      const int* __restrict__ hub_row, const float* __restrict__ attn_row,
@@ -211,13 +212,33 @@ gat_hub_stats_kernel(int H, const int* __restrict__ rowptr, const int* __restric
   const int h = blockIdx.y;
   const int e0 = rowptr[row], e1 = rowptr[row + 1];
   const float ad = attn_row[row * H + h];
+  // edges in groups of kHubBatch per thread with their loads issued
+  // together; the per-thread max and sum still run over the edges in order
   float m = kNegInit;
-  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads)
-    m = fmaxf(m, leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope));
+  for (int eb = e0 + threadIdx.x; eb < e1; eb += kHubBatch * kHubThreads) {
+    float ac[kHubBatch];
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u) {
+      const int e = eb + u * kHubThreads;
+      ac[u] = e < e1 ? attn_col[static_cast<int64_t>(col[e]) * H + h] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u)
+      if (eb + u * kHubThreads < e1) m = fmaxf(m, leaky_f(ad + ac[u], slope));
+  }
   m = block_max<kHubThreads>(m, scratch);
   float s = 0.0f;
-  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads)
-    s += expf(leaky_f(ad + attn_col[static_cast<int64_t>(col[e]) * H + h], slope) - m);
+  for (int eb = e0 + threadIdx.x; eb < e1; eb += kHubBatch * kHubThreads) {
+    float ac[kHubBatch];
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u) {
+      const int e = eb + u * kHubThreads;
+      ac[u] = e < e1 ? attn_col[static_cast<int64_t>(col[e]) * H + h] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u)
+      if (eb + u * kHubThreads < e1) s += expf(leaky_f(ad + ac[u], slope) - m);
+  }
   s = block_sum<kHubThreads>(s, scratch);
   if (threadIdx.x == 0) {
     emax[row * H + h] = m;
@@ -552,23 +573,52 @@ gat_bwd_hub_rows_kernel(int H, int64_t C, const int* __restrict__ rowptr,
   const int e0 = rowptr[row], e1 = rowptr[row + 1];
   const float ad = attn_row[row * H + h];
   const float m = emax[row * H + h], s = esum[row * H + h];
+  // A thread's edges e0 + tid, + kHubThreads, ... in groups of kHubBatch
+  // whose col / attn_col / glog loads are issued together (the largest hub
+  // row of a power-law graph gives each thread a few dozen edges); the
+  // per-thread sums still run over the edges in order.
   float wsum = 0.0f;
-  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads) {
-    const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
-                                  p, seed, static_cast<uint64_t>(e) * H + h,
-                                  glog[static_cast<int64_t>(e) * H + h]);
-    wsum += es.soft * es.ge;
+  for (int eb = e0 + threadIdx.x; eb < e1; eb += kHubBatch * kHubThreads) {
+    float ac[kHubBatch], gl[kHubBatch];
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u) {
+      const int e = eb + u * kHubThreads;
+      const int cc = e < e1 ? col[e] : 0;
+      ac[u] = e < e1 ? attn_col[static_cast<int64_t>(cc) * H + h] : 0.0f;
+      gl[u] = e < e1 ? glog[static_cast<int64_t>(e) * H + h] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u) {
+      const int e = eb + u * kHubThreads;
+      if (e >= e1) break;
+      const EdgeSoft es = edge_soft(ad, ac[u], m, s, slope, p, seed,
+                                    static_cast<uint64_t>(e) * H + h, gl[u]);
+      wsum += es.soft * es.ge;
+    }
   }
   wsum = block_sum<kHubThreads>(wsum, scratch);
   float grow = 0.0f;
-  for (int e = e0 + threadIdx.x; e < e1; e += kHubThreads) {
-    const int64_t o = static_cast<int64_t>(e) * H + h;
-    const EdgeSoft es = edge_soft(ad, attn_col[static_cast<int64_t>(col[e]) * H + h], m, s, slope,
-                                  p, seed, static_cast<uint64_t>(e) * H + h, glog[o]);
-    float gout = es.soft * (es.ge - wsum);
-    if (es.neg) gout *= slope;
-    glog[o] = gout;
-    grow += gout;
+  for (int eb = e0 + threadIdx.x; eb < e1; eb += kHubBatch * kHubThreads) {
+    float ac[kHubBatch], gl[kHubBatch];
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u) {
+      const int e = eb + u * kHubThreads;
+      const int cc = e < e1 ? col[e] : 0;
+      ac[u] = e < e1 ? attn_col[static_cast<int64_t>(cc) * H + h] : 0.0f;
+      gl[u] = e < e1 ? glog[static_cast<int64_t>(e) * H + h] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kHubBatch; ++u) {
+      const int e = eb + u * kHubThreads;
+      if (e >= e1) break;
+      const int64_t o = static_cast<int64_t>(e) * H + h;
+      const EdgeSoft es = edge_soft(ad, ac[u], m, s, slope, p, seed,
+                                    static_cast<uint64_t>(e) * H + h, gl[u]);
+      float gout = es.soft * (es.ge - wsum);
+      if (es.neg) gout *= slope;
+      glog[o] = gout;
+      grow += gout;
+    }
   }
   grow = block_sum<kHubThreads>(grow, scratch);
   if (threadIdx.x == 0) grad_attn_row[row * H + h] = grow;

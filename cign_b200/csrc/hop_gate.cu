@@ -87,7 +87,9 @@ hop_gate_fwd_kernel(int64_t n, int64_t D, int mode, const float* __restrict__ H,
 // partial layout: pw [chunks, K, 2D] (this tile's columns), pb [chunks, K]
 // (tile 0 only).
 template <int K>
-__global__ void __launch_bounds__(kThreads)
+// two CTAs per SM (<= 128 registers) up to K = 3 hops; more hops keep their
+// per-lane partials in registers at one CTA per SM instead of spilling
+__global__ void __launch_bounds__(kThreads, K <= 3 ? 2 : 1)
 hop_gate_bwd_kernel(int64_t n, int64_t D, int64_t rpc, int mode, const float* __restrict__ H,
                     const float* __restrict__ C, const float* __restrict__ W,
                     const float* __restrict__ alpha, const float* __restrict__ g_alpha,
@@ -96,39 +98,66 @@ hop_gate_bwd_kernel(int64_t n, int64_t D, int64_t rpc, int mode, const float* __
                     int64_t add_ld, float* __restrict__ pw, float* __restrict__ pb) {
   __shared__ float4 red[kThreads / 32][2][32];
   __shared__ float redb[kThreads / 32][K];
+  __shared__ float4 wt[2][K][32];  // this tile's columns of W's two halves
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t c = static_cast<int64_t>(blockIdx.y) * kTileCols + lane * 4;
   const bool cv = c < D;
   const int64_t D2 = 2 * D;
-  float4 w0[K], w1[K], a0[K], a1[K];
+  float4 a0[K], a1[K];
   float ab[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
-    w0[k] = cv ? ldg_vec<4>(W + k * D2 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    w1[k] = cv ? ldg_vec<4>(W + k * D2 + D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     a0[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     a1[k] = a0[k];
     ab[k] = 0.0f;
   }
+  for (int i = threadIdx.x; i < 2 * K * 32; i += kThreads) {
+    const int half = i / (K * 32), k = (i / 32) % K, l = i % 32;
+    const int64_t cc = static_cast<int64_t>(blockIdx.y) * kTileCols + l * 4;
+    wt[half][k][l] = cc < D ? ldg_vec<4>(W + k * D2 + half * D + cc)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
   const int64_t r1 = r0 + rpc < n ? r0 + rpc : n;
-  for (int64_t row = r0 + warp; row < r1; row += kThreads / 32) {
-    float al[K], gl[K];
+  // Two of the warp's rows per iteration (row, then row + kThreads/32: the
+  // order of the single-row loop), with both rows' loads issued before
+  // either is used, so twice the bytes are in flight per warp.
+  struct RowIn {
+    float al[K], ga[K];
+    float4 h, x, th, tc;
+  };
+  auto load = [&](int64_t row, RowIn& in) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      in.al[k] = __ldg(alpha + row * K + k);
+      in.ga[k] = __ldg(g_alpha + row * K + k);
+    }
+    if (!cv) return;
+    in.h = ld_vec<4>(H + row * D + c);
+    in.x = ld_vec<4>(C + row * D + c);
+    // existing gradient first, then the extra addend, then this op's part
+    in.th = make_float4(0.f, 0.f, 0.f, 0.f);
+    in.tc = in.th;
+    if (accumulate) {
+      in.th = ld_vec<4>(gH + row * D + c);
+      in.tc = ld_vec<4>(gC + row * D + c);
+    }
+    if (add_h != nullptr) vadd(in.th, ld_vec<4>(add_h + row * add_ld + c));
+    if (add_c != nullptr) vadd(in.tc, ld_vec<4>(add_c + row * add_ld + c));
+  };
+  auto apply = [&](int64_t row, RowIn& in) {
+    float gl[K];
     float dotp = 0.0f;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      al[k] = __ldg(alpha + row * K + k);
-      gl[k] = __ldg(g_alpha + row * K + k);
-      dotp = fmaf(al[k], gl[k], dotp);
-    }
+    for (int k = 0; k < K; ++k) dotp = fmaf(in.al[k], in.ga[k], dotp);
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      gl[k] = al[k] * (gl[k] - dotp);
+      gl[k] = in.al[k] * (in.ga[k] - dotp);
       ab[k] += gl[k];
     }
-    if (!cv) continue;
-    const float4 h = ld_vec<4>(H + row * D + c);
-    const float4 x = ld_vec<4>(C + row * D + c);
+    if (!cv) return;
+    const float4 h = in.h, x = in.x;
     float4 s0, s1;
     if (mode == 1) {
       s0 = make_float4(h.x + x.x, h.y + x.y, h.z + x.z, h.w + x.w);
@@ -140,8 +169,8 @@ hop_gate_bwd_kernel(int64_t n, int64_t D, int64_t rpc, int mode, const float* __
     float4 gi0 = make_float4(0.f, 0.f, 0.f, 0.f), gi1 = gi0;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      vfma(gi0, gl[k], w0[k]);
-      vfma(gi1, gl[k], w1[k]);
+      vfma(gi0, gl[k], wt[0][k][lane]);
+      vfma(gi1, gl[k], wt[1][k][lane]);
       vfma(a0[k], gl[k], s0);
       vfma(a1[k], gl[k], s1);
     }
@@ -155,18 +184,19 @@ hop_gate_bwd_kernel(int64_t n, int64_t D, int64_t rpc, int mode, const float* __
       oh = gi0;
       oc = gi1;
     }
-    // existing gradient first, then the extra addend, then this op's part
-    float4 th = make_float4(0.f, 0.f, 0.f, 0.f), tc = th;
-    if (accumulate) {
-      th = ld_vec<4>(gH + row * D + c);
-      tc = ld_vec<4>(gC + row * D + c);
-    }
-    if (add_h != nullptr) vadd(th, ld_vec<4>(add_h + row * add_ld + c));
-    if (add_c != nullptr) vadd(tc, ld_vec<4>(add_c + row * add_ld + c));
-    vadd(th, oh);
-    vadd(tc, oc);
-    st_vec(gH + row * D + c, th);
-    st_vec(gC + row * D + c, tc);
+    vadd(in.th, oh);
+    vadd(in.tc, oc);
+    st_vec(gH + row * D + c, in.th);
+    st_vec(gC + row * D + c, in.tc);
+  };
+  constexpr int kW = kThreads / 32;
+  for (int64_t row = r0 + warp; row < r1; row += 2 * kW) {
+    const bool two = row + kW < r1;
+    RowIn a, b;
+    load(row, a);
+    if (two) load(row + kW, b);
+    apply(row, a);
+    if (two) apply(row + kW, b);
   }
   // fixed-order reduction of the warps' parameter partials, one k at a time
 #pragma unroll
