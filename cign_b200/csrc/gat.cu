@@ -55,6 +55,10 @@ struct cign_gat_plan {
   const int32_t* perm;
   cign::SegList rows;  // hub destination rows (CSR)
   cign::SegList cols;  // hub source columns (CSC)
+  // the same with kAggSegLen-edge work items, for the aggregate-first
+  // aggregation kernels (gat_agg_kernel walks an item in 32-edge chunks)
+  cign::SegList agg_rows;
+  cign::SegList agg_cols;
   int device;
 };
 
@@ -2061,6 +2065,12 @@ BwdLayout bwd_layout(const cign_gat_plan* pl, int H, int64_t C) {
 // 128*VPL floats run over the grid's second dimension.
 
 constexpr int kAggHB = 4;      // heads per pass over a work item's edges
+// edges per work item of the aggregation kernels: rows (columns) of up to
+// this many edges are one item, longer ones are cut into items of this
+// length whose partials a combine sums.  Longer items than the 32 of the
+// other GAT kernels leave fewer hub partials ([items, H, D] written and read
+// back) on power-law graphs.
+constexpr int kAggSegLen = 128;
 constexpr int kDotsSlots = 8;  // edges in the backward-K1 ring (two 4-edge groups)
 constexpr size_t kDotsSmem = static_cast<size_t>(kThreads / 32) * kDotsSlots * 2 * 32 * 16;
 constexpr int kAggStages = 4;  // neighbour rows in flight per warp (cp.async ring)
@@ -2229,15 +2239,6 @@ gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
     item = target;
     seg = false;
   }
-  const int k = e0 + lane;
-  const bool valid = k < e1;
-  const int cnt = e1 - e0;
-  int other = 0;     // MODE 0: source column j; MODE 1: destination row i
-  int64_t e = k;     // CSR edge id (dropout index)
-  if (valid) {
-    other = __ldg(idx + k);
-    if (MODE == 1) e = __ldg(perm + k);
-  }
   // this lane's feature offsets in the tile (lanes past D copy and store nothing)
   int64_t foff[VPL];
   bool fin[VPL];
@@ -2246,69 +2247,84 @@ gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
     foff[q] = f0 + static_cast<int64_t>(lane + q * 32) * 4;
     fin[q] = foff[q] < D;
   }
-  // copies of edge t's tile slices into ring stage `stage`
-  auto issue = [&](int t, int stage) {
-    const float* xr = src + static_cast<int64_t>(__shfl_sync(kFullMask, other, t)) * D;
-    const uint32_t slot = my_ring + static_cast<uint32_t>(stage * VPL * 32 * 16);
-#pragma unroll
-    for (int q = 0; q < VPL; ++q)
-      if (fin[q]) cp_async16_s(slot + q * 32 * 16, xr + foff[q]);
-  };
   const float scale = MODE == 1 ? 1.0f / static_cast<float>(H) : 1.0f;
   const int64_t HD = static_cast<int64_t>(H) * D;
+  // the item's output row and (MODE 1) logit-gradient slots, fixed before
+  // the edge loop so that no item bookkeeping stays live across it
+  float* const dst = seg ? partial + item * HD : out + target * HD;
+  float* const gdst = MODE == 1 ? (seg ? pcol + item * H : gcol + target * H) : nullptr;
   // ONE_PASS (H <= kAggHB): a single head pass with h0 = 0 known to the compiler
   for (int h0 = 0; h0 < (ONE_PASS ? 1 : H); h0 += kAggHB) {
-#pragma unroll
-    for (int t = 0; t < kAggStages; ++t) {
-      if (t < cnt) issue(t, t);
-      cp_async_commit();
-    }
-    float w[kAggHB];
-#pragma unroll
-    for (int hh = 0; hh < kAggHB; ++hh) {
-      const int h = h0 + hh;
-      w[hh] = 0.0f;
-      if (h >= H) continue;
-      if (valid) w[hh] = __ldg(wts + e * H + h) * scale;
-      if (MODE == 1) {
-        if (blockIdx.y == 0) {
-          const float gsum = group_sum<32>(valid ? glog[e * H + h] : 0.0f, kFullMask);
-          if (lane == 0) {
-            if (seg) pcol[item * H + h] = gsum;
-            else gcol[target * H + h] = gsum;
-          }
-        }
-      }
-    }
     float4 acc[kAggHB][VPL];
 #pragma unroll
     for (int hh = 0; hh < kAggHB; ++hh)
 #pragma unroll
       for (int q = 0; q < VPL; ++q) acc[hh][q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    // edge t sits in ring stage t % kAggStages: the loop runs kAggStages
-    // edges per pass so that every stage's shared address is a constant
-    for (int t0 = 0; t0 < cnt; t0 += kAggStages) {
+    // MODE 1: the item's logit-gradient sum of head h0 + lane (lanes < kAggHB),
+    // accumulated chunk by chunk
+    float gs = 0.0f;
+    // the item's edges in chunks of 32 (lane k owns edge c0 + k of a chunk)
+    for (int c0 = e0; c0 < e1; c0 += 32) {
+      const int k = c0 + lane;
+      const bool valid = k < e1;
+      const int cnt = min(32, e1 - c0);
+      int other = 0;  // MODE 0: source column j; MODE 1: destination row i
+      int64_t e = k;  // CSR edge id (dropout index)
+      if (valid) {
+        other = __ldg(idx + k);
+        if (MODE == 1) e = __ldg(perm + k);
+      }
+      // copies of chunk edge t's tile slices into ring stage `stage`
+      auto issue = [&](int t, int stage) {
+        const float* xr = src + static_cast<int64_t>(__shfl_sync(kFullMask, other, t)) * D;
+        const uint32_t slot = my_ring + static_cast<uint32_t>(stage * VPL * 32 * 16);
 #pragma unroll
-      for (int u = 0; u < kAggStages; ++u) {
-        const int t = t0 + u;
-        if (t >= cnt) break;
-        cp_async_wait<kAggStages - 1>();  // edge t's copies have landed
-        const uint32_t slot = my_ring + static_cast<uint32_t>(u * VPL * 32 * 16);
-        float4 xv[VPL];
+        for (int q = 0; q < VPL; ++q)
+          if (fin[q]) cp_async16_s(slot + q * 32 * 16, xr + foff[q]);
+      };
 #pragma unroll
-        for (int q = 0; q < VPL; ++q) xv[q] = lds_f4(slot + q * 32 * 16);
-#pragma unroll
-        for (int hh = 0; hh < kAggHB; ++hh) {
-          const float wv = __shfl_sync(kFullMask, w[hh], t);
-#pragma unroll
-          for (int q = 0; q < VPL; ++q) vfma(acc[hh][q], wv, xv[q]);
-        }
-        if (t + kAggStages < cnt) issue(t + kAggStages, u);  // into the stage just read
+      for (int t = 0; t < kAggStages; ++t) {
+        if (t < cnt) issue(t, t);
         cp_async_commit();
       }
+      float w[kAggHB];
+#pragma unroll
+      for (int hh = 0; hh < kAggHB; ++hh) {
+        const int h = h0 + hh;
+        w[hh] = 0.0f;
+        if (h >= H) continue;
+        if (valid) w[hh] = __ldg(wts + e * H + h) * scale;
+        if (MODE == 1 && blockIdx.y == 0) {
+          const float t = group_sum<32>(valid ? glog[e * H + h] : 0.0f, kFullMask);
+          if (lane == hh) gs += t;
+        }
+      }
+      // chunk edge t sits in ring stage t % kAggStages: the loop runs
+      // kAggStages edges per pass so that every stage's shared address is a
+      // constant
+      for (int t0 = 0; t0 < cnt; t0 += kAggStages) {
+#pragma unroll
+        for (int u = 0; u < kAggStages; ++u) {
+          const int t = t0 + u;
+          if (t >= cnt) break;
+          cp_async_wait<kAggStages - 1>();  // edge t's copies have landed
+          const uint32_t slot = my_ring + static_cast<uint32_t>(u * VPL * 32 * 16);
+          float4 xv[VPL];
+#pragma unroll
+          for (int q = 0; q < VPL; ++q) xv[q] = lds_f4(slot + q * 32 * 16);
+#pragma unroll
+          for (int hh = 0; hh < kAggHB; ++hh) {
+            const float wv = __shfl_sync(kFullMask, w[hh], t);
+#pragma unroll
+            for (int q = 0; q < VPL; ++q) vfma(acc[hh][q], wv, xv[q]);
+          }
+          if (t + kAggStages < cnt) issue(t + kAggStages, u);  // into the stage just read
+          cp_async_commit();
+        }
+      }
+      cp_async_wait<0>();  // the ring is reused by the next chunk
     }
-    cp_async_wait<0>();
-    float* dst = seg ? partial + item * HD : out + target * HD;
+    if (MODE == 1 && blockIdx.y == 0 && lane < kAggHB && h0 + lane < H) gdst[h0 + lane] = gs;
 #pragma unroll
     for (int hh = 0; hh < kAggHB; ++hh) {
       if (h0 + hh >= H) break;
@@ -2327,14 +2343,14 @@ gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
 // slot; a tile is 32 * VPL * 8 features.
 template <int VPL>
 __global__ void __launch_bounds__(kThreads)
-gat_agg_fwd_bf16_kernel(int n, int H, int64_t D, const int* __restrict__ ptr,
-                        const int* __restrict__ idx, const int* __restrict__ seg_row,
-                        const int* __restrict__ seg_begin, const int* __restrict__ seg_end,
-                        int n_seg, int seg_blocks, const float* __restrict__ attn_row,
-                        const float* __restrict__ attn_col, float* __restrict__ emax,
-                        float* __restrict__ esum, const __nv_bfloat16* __restrict__ src,
-                        float slope, float p, Seed seed_in, float* __restrict__ out,
-                        float* __restrict__ partial) {
+gat_agg_fwd_bf16_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
+                        const int* __restrict__ ptr, const int* __restrict__ idx,
+                        const int* __restrict__ seg_row, const int* __restrict__ seg_begin,
+                        const int* __restrict__ seg_end, int n_seg, int seg_blocks,
+                        const float* __restrict__ attn_row, const float* __restrict__ attn_col,
+                        float* __restrict__ emax, float* __restrict__ esum,
+                        const __nv_bfloat16* __restrict__ src, float slope, float p,
+                        Seed seed_in, float* __restrict__ out, float* __restrict__ partial) {
   extern __shared__ uint4 aggb_ring[];
   const uint64_t seed = seed_in;
   constexpr int kTile = 32 * VPL * 8;
@@ -2353,57 +2369,22 @@ gat_agg_fwd_bf16_kernel(int n, int H, int64_t D, const int* __restrict__ ptr,
     e0 = seg_begin[item];
     e1 = seg_end[item];
     seg = true;
-  } else {
-    target = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
-    if (target >= n) return;
+  } else {  // light rows in the plan's length order
+    const int64_t li = static_cast<int64_t>(blockIdx.x - seg_blocks) * (kThreads / 32) + group;
+    if (li >= n_light) return;
+    target = light[li];
     e0 = ptr[target];
     e1 = ptr[target + 1];
-    if (e1 - e0 > kSegLen) return;
     item = target;
     seg = false;
   }
-  const int k = e0 + lane;
-  const bool valid = k < e1;
-  const int cnt = e1 - e0;
-  const int other = valid ? __ldg(idx + k) : 0;
-  auto issue = [&](int t) {
-    const __nv_bfloat16* xr = src + static_cast<int64_t>(__shfl_sync(kFullMask, other, t)) * D;
-    const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
-#pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 8;
-      if (fi < D) cp_async16_s(slot + q * 32 * 16, xr + fi);
-    }
-  };
+  // rows of at most 32 edges form their max / exp-sum here (warp
+  // reductions, as gat_edge_weights_kernel<true> does); longer rows read the
+  // hub statistics (gat_hub_stats_kernel ran first)
+  const bool own_stats = !seg && e1 - e0 <= 32;
   const int64_t HD = static_cast<int64_t>(H) * D;
+  float* const dst = seg ? partial + item * HD : out + target * HD;
   for (int h0 = 0; h0 < H; h0 += kAggHB) {
-#pragma unroll
-    for (int t = 0; t < kAggStages; ++t) {
-      if (t < cnt) issue(t);
-      cp_async_commit();
-    }
-    float w[kAggHB];
-#pragma unroll
-    for (int hh = 0; hh < kAggHB; ++hh) {
-      const int h = h0 + hh;
-      w[hh] = 0.0f;
-      if (h >= H) continue;
-      const float ad = __ldg(attn_row + target * H + h);
-      const float ac = valid ? __ldg(attn_col + static_cast<int64_t>(other) * H + h) : 0.0f;
-      float m, ssum;
-      if (seg) {
-        m = emax[target * H + h];
-        ssum = esum[target * H + h];
-      } else {
-        m = group_max<32>(valid ? fmaxf(kNegInit, leaky_f(ad + ac, slope)) : kNegInit, kFullMask);
-        ssum = group_sum<32>(valid ? expf(leaky_f(ad + ac, slope) - m) : 0.0f, kFullMask);
-        if (blockIdx.y == 0 && lane == 0) {
-          emax[target * H + h] = m;
-          esum[target * H + h] = ssum;
-        }
-      }
-      if (valid) w[hh] = edge_weight(ad, ac, m, ssum, slope, p, seed, static_cast<uint64_t>(k) * H + h);
-    }
     float acc[kAggHB][VPL][8];
 #pragma unroll
     for (int hh = 0; hh < kAggHB; ++hh)
@@ -2411,34 +2392,79 @@ gat_agg_fwd_bf16_kernel(int n, int H, int64_t D, const int* __restrict__ ptr,
       for (int q = 0; q < VPL; ++q)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[hh][q][j] = 0.0f;
-    for (int t = 0; t < cnt; ++t) {
-      cp_async_wait<kAggStages - 1>();
-      const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
-      float xf[VPL][8];
+    // the item's edges in chunks of 32 (lane k owns edge c0 + k of a chunk)
+    for (int c0 = e0; c0 < e1; c0 += 32) {
+      const int k = c0 + lane;
+      const bool valid = k < e1;
+      const int cnt = min(32, e1 - c0);
+      const int other = valid ? __ldg(idx + k) : 0;
+      auto issue = [&](int t) {
+        const __nv_bfloat16* xr =
+            src + static_cast<int64_t>(__shfl_sync(kFullMask, other, t)) * D;
+        const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
 #pragma unroll
-      for (int q = 0; q < VPL; ++q) {
-        const float4 raw = lds_f4(slot + q * 32 * 16);
-        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f2 = __bfloat1622float2(b[i]);
-          xf[q][2 * i] = f2.x;
-          xf[q][2 * i + 1] = f2.y;
+        for (int q = 0; q < VPL; ++q) {
+          const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 8;
+          if (fi < D) cp_async16_s(slot + q * 32 * 16, xr + fi);
         }
+      };
+#pragma unroll
+      for (int t = 0; t < kAggStages; ++t) {
+        if (t < cnt) issue(t);
+        cp_async_commit();
       }
+      float w[kAggHB];
 #pragma unroll
       for (int hh = 0; hh < kAggHB; ++hh) {
-        const float wv = __shfl_sync(kFullMask, w[hh], t);
-#pragma unroll
-        for (int q = 0; q < VPL; ++q)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[hh][q][j] = fmaf(wv, xf[q][j], acc[hh][q][j]);
+        const int h = h0 + hh;
+        w[hh] = 0.0f;
+        if (h >= H) continue;
+        const float ad = __ldg(attn_row + target * H + h);
+        const float ac = valid ? __ldg(attn_col + static_cast<int64_t>(other) * H + h) : 0.0f;
+        float m, ssum;
+        if (!own_stats) {
+          m = emax[target * H + h];
+          ssum = esum[target * H + h];
+        } else {
+          m = group_max<32>(valid ? fmaxf(kNegInit, leaky_f(ad + ac, slope)) : kNegInit,
+                            kFullMask);
+          ssum = group_sum<32>(valid ? expf(leaky_f(ad + ac, slope) - m) : 0.0f, kFullMask);
+          if (blockIdx.y == 0 && lane == 0) {
+            emax[target * H + h] = m;
+            esum[target * H + h] = ssum;
+          }
+        }
+        if (valid)
+          w[hh] = edge_weight(ad, ac, m, ssum, slope, p, seed, static_cast<uint64_t>(k) * H + h);
       }
-      if (t + kAggStages < cnt) issue(t + kAggStages);
-      cp_async_commit();
+      for (int t = 0; t < cnt; ++t) {
+        cp_async_wait<kAggStages - 1>();
+        const uint32_t slot = my_ring + static_cast<uint32_t>((t % kAggStages) * VPL * 32 * 16);
+        float xf[VPL][8];
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) {
+          const float4 raw = lds_f4(slot + q * 32 * 16);
+          const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f2 = __bfloat1622float2(b[i]);
+            xf[q][2 * i] = f2.x;
+            xf[q][2 * i + 1] = f2.y;
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < kAggHB; ++hh) {
+          const float wv = __shfl_sync(kFullMask, w[hh], t);
+#pragma unroll
+          for (int q = 0; q < VPL; ++q)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[hh][q][j] = fmaf(wv, xf[q][j], acc[hh][q][j]);
+        }
+        if (t + kAggStages < cnt) issue(t + kAggStages);
+        cp_async_commit();
+      }
+      cp_async_wait<0>();  // the ring is reused by the next chunk
     }
-    cp_async_wait<0>();
-    float* dst = seg ? partial + item * HD : out + target * HD;
 #pragma unroll
     for (int hh = 0; hh < kAggHB; ++hh) {
       if (h0 + hh >= H) break;
@@ -2749,9 +2775,13 @@ int cign_gat_plan_create_rect(int64_t n, int64_t n_cols, int64_t nnz, const int3
   cudaGetDevice(&pl->device);
   int rc = build_segments(rowptr, n, kSegLen, &pl->rows);
   if (rc == CIGN_OK) rc = build_segments(colptr, n_cols, kSegLen, &pl->cols);
+  if (rc == CIGN_OK) rc = build_segments(rowptr, n, kAggSegLen, &pl->agg_rows);
+  if (rc == CIGN_OK) rc = build_segments(colptr, n_cols, kAggSegLen, &pl->agg_cols);
   if (rc != CIGN_OK) {
     free_segments(&pl->rows);
     free_segments(&pl->cols);
+    free_segments(&pl->agg_rows);
+    free_segments(&pl->agg_cols);
     delete pl;
     return rc;
   }
@@ -2767,6 +2797,8 @@ int cign_gat_plan_destroy(cign_gat_plan* pl) {
   cudaSetDevice(pl->device);
   free_segments(&pl->rows);
   free_segments(&pl->cols);
+  free_segments(&pl->agg_rows);
+  free_segments(&pl->agg_cols);
   cudaSetDevice(prev);
   delete pl;
   return CIGN_OK;
@@ -2957,9 +2989,9 @@ int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const 
                                  negative_slope, attn_drop, seed, wts, s);
   if (rc) return rc;
   if (dim <= 128)
-    return launch_agg<1, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, wts, x, z,
+    return launch_agg<1, 0>(pl, pl->agg_rows, heads, dim, pl->rowptr, pl->col, nullptr, wts, x, z,
                             partial, nullptr, nullptr, nullptr, s);
-  return launch_agg<2, 0>(pl, pl->rows, heads, dim, pl->rowptr, pl->col, nullptr, wts, x, z,
+  return launch_agg<2, 0>(pl, pl->agg_rows, heads, dim, pl->rowptr, pl->col, nullptr, wts, x, z,
                           partial, nullptr, nullptr, nullptr, s);
 }
 
@@ -2984,9 +3016,9 @@ int cign_gat_agg_fwd_bf16(const cign_gat_plan* pl, int32_t heads, int64_t dim,
   float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + L.partial);
   rc = launch_hub_stats(pl, heads, attn_row, attn_col, negative_slope, edge_max, edge_sum, s);
   if (rc) return rc;
-  const SegList& sl = pl->rows;
+  const SegList& sl = pl->agg_rows;  // the fp32 aggregation's items: same sums
   const int64_t seg_blocks = (sl.n_seg + kThreads / 32 - 1) / (kThreads / 32);
-  const int64_t grid = seg_blocks + (pl->n + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t grid = seg_blocks + (sl.n_light + kThreads / 32 - 1) / (kThreads / 32);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   // 256-feature tiles (512 bytes of bf16 per edge): the 4-head fp32
   // accumulator of a 512-feature tile would need ~120 registers
@@ -2994,8 +3026,9 @@ int cign_gat_agg_fwd_bf16(const cign_gat_plan* pl, int32_t heads, int64_t dim,
   const size_t smem = static_cast<size_t>(kThreads / 32) * kAggStages * VPL * 32 * 16;
   const dim3 g(static_cast<unsigned>(grid), static_cast<unsigned>((dim + 255) / 256));
   gat_agg_fwd_bf16_kernel<VPL><<<g, kThreads, smem, s>>>(
-      static_cast<int>(pl->n), heads, dim, pl->rowptr, pl->col, sl.seg_row(), sl.seg_begin(),
-      sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks), attn_row, attn_col,
+      static_cast<int>(sl.n_light), sl.light_row(), heads, dim, pl->rowptr, pl->col, sl.seg_row(),
+      sl.seg_begin(), sl.seg_end(), static_cast<int>(sl.n_seg), static_cast<int>(seg_blocks),
+      attn_row, attn_col,
       edge_max, edge_sum, xb, negative_slope, attn_drop, seed, z, partial);
   CIGN_CHECK_LAUNCH("gat_agg_fwd_bf16_kernel");
   return launch_seg_combine(sl, heads, dim, partial, nullptr, z, nullptr, s);
@@ -3061,9 +3094,9 @@ int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_
                                   wts, s);
   if (rc) return rc;
   if (channels <= 128)
-    return launch_agg<1, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
+    return launch_agg<1, 1>(pl, pl->agg_cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
                             grad_pre, grad_feat, partial, glog, grad_attn_col, pcol, s);
-  return launch_agg<2, 1>(pl, pl->cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
+  return launch_agg<2, 1>(pl, pl->agg_cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
                           grad_pre, grad_feat, partial, glog, grad_attn_col, pcol, s);
 }
 
