@@ -47,7 +47,7 @@ namespace {
 // with small CTAs (measured on the cfg2 graph: 118 us per F=1024 hop
 // against 125 us at 8 warps per CTA; 2 warps gave the same as 4).
 constexpr int kThreads = 128;
-constexpr int kSegLen = 64;  // edges per work item of a hub row
+constexpr int kSegLen = 128;  // edges per work item of a hub row
 
 template <int VEC, int VPL, int LPR>
 struct SpmmCfg {

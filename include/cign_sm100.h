@@ -75,8 +75,8 @@ typedef struct cign_csr_f32 {
 } cign_csr_f32;
 
 /* SpMM plan over P (and P^T).  Validates the CSR on the device and cuts rows
- * with more than 64 non-zeros ("hub" rows of power-law graphs) into 64-edge
- * segments processed in parallel and combined in a fixed order.  The CSR
+ * with more than 128 non-zeros ("hub" rows of power-law graphs) into
+ * 128-edge segments processed in parallel and combined in a fixed order.  The CSR
  * arrays stay owned by the caller and must outlive the plan.  Immutable
  * after creation: one plan may be used from several streams at once.
  * Replaces MultiHopCsrPlan (multihop_csr_ext/multihop_csr_pipeline_cuda.cu:
