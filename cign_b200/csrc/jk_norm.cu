@@ -160,12 +160,16 @@ jk_ln_bwd_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy, 
 }
 
 // Column partials over one chunk of kJkRowsPerChunk rows: pw[chunk][d] =
-// sum gy*xhat, pb[chunk][d] = sum gy, rows in order.
-__global__ void __launch_bounds__(kJkThreads)
+// sum gy*xhat, pb[chunk][d] = sum gy, rows in order.  Eight rows' loads
+// are issued together per thread (the sums still add the rows in order),
+// and 128-thread blocks leave no idle threads at the 384 float4 columns of a
+// 3 x 512 JK row.
+constexpr int kJkParamThreads = 128;
+__global__ void __launch_bounds__(kJkParamThreads)
 jk_ln_param_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy, SegPtrs segs,
                    const float* __restrict__ mean, const float* __restrict__ rstd,
                    float* __restrict__ pw, float* __restrict__ pb) {
-  const int64_t c = static_cast<int64_t>(blockIdx.y) * kJkThreads + threadIdx.x;  // float4 col
+  const int64_t c = static_cast<int64_t>(blockIdx.y) * kJkParamThreads + threadIdx.x;  // float4 col
   const int64_t dq = D / 4;
   if (c >= dq) return;
   const int64_t wq = W / 4;
@@ -174,18 +178,30 @@ jk_ln_param_kernel(int64_t n, int64_t W, int64_t D, const float* __restrict__ gy
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kJkRowsPerChunk;
   const int64_t r1 = r0 + kJkRowsPerChunk < n ? r0 + kJkRowsPerChunk : n;
   float4 aw = make_float4(0.f, 0.f, 0.f, 0.f), ab = aw;
-  for (int64_t r = r0; r < r1; ++r) {
-    const float mu = __ldg(mean + r), rs = __ldg(rstd + r);
-    const float4 xv = __ldg(xs + r * wq);
-    const float4 gv = __ldg(reinterpret_cast<const float4*>(gy + r * D) + c);
-    aw.x += gv.x * ((xv.x - mu) * rs);
-    aw.y += gv.y * ((xv.y - mu) * rs);
-    aw.z += gv.z * ((xv.z - mu) * rs);
-    aw.w += gv.w * ((xv.w - mu) * rs);
-    ab.x += gv.x;
-    ab.y += gv.y;
-    ab.z += gv.z;
-    ab.w += gv.w;
+  constexpr int kG = 8;  // rows whose loads are issued together
+  for (int64_t rb = r0; rb < r1; rb += kG) {
+    float4 xv[kG], gv[kG];
+    float mu[kG], rs[kG];
+#pragma unroll
+    for (int u = 0; u < kG; ++u) {
+      const int64_t r = rb + u < r1 ? rb + u : r1 - 1;  // clamped: loaded, not added
+      mu[u] = __ldg(mean + r);
+      rs[u] = __ldg(rstd + r);
+      xv[u] = __ldg(xs + r * wq);
+      gv[u] = __ldg(reinterpret_cast<const float4*>(gy + r * D) + c);
+    }
+#pragma unroll
+    for (int u = 0; u < kG; ++u) {
+      if (rb + u >= r1) break;
+      aw.x += gv[u].x * ((xv[u].x - mu[u]) * rs[u]);
+      aw.y += gv[u].y * ((xv[u].y - mu[u]) * rs[u]);
+      aw.z += gv[u].z * ((xv[u].z - mu[u]) * rs[u]);
+      aw.w += gv[u].w * ((xv[u].w - mu[u]) * rs[u]);
+      ab.x += gv[u].x;
+      ab.y += gv[u].y;
+      ab.z += gv[u].z;
+      ab.w += gv[u].w;
+    }
   }
   reinterpret_cast<float4*>(pw + static_cast<int64_t>(blockIdx.x) * D)[c] = aw;
   reinterpret_cast<float4*>(pb + static_cast<int64_t>(blockIdx.x) * D)[c] = ab;
@@ -288,9 +304,9 @@ int cign_jk_ln_bwd(int64_t n, int32_t n_seg, int64_t seg_width, const float* gra
   float* pw = static_cast<float*>(ws);
   float* pb = pw + chunks * D;
   const dim3 pgrid(static_cast<unsigned>(chunks),
-                   static_cast<unsigned>((D / 4 + kJkThreads - 1) / kJkThreads));
-  jk_ln_param_kernel<<<pgrid, kJkThreads, 0, s>>>(n, seg_width, D, grad_y, P, mean, rstd, pw,
-                                                   pb);
+                   static_cast<unsigned>((D / 4 + kJkParamThreads - 1) / kJkParamThreads));
+  jk_ln_param_kernel<<<pgrid, kJkParamThreads, 0, s>>>(n, seg_width, D, grad_y, P, mean, rstd,
+                                                        pw, pb);
   CIGN_CHECK_LAUNCH("jk_ln_param_kernel");
   return colsum_rows(pw, grad_w, pb, grad_b, chunks, D, D, s);
 }
