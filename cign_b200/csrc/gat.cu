@@ -2545,6 +2545,20 @@ gat_agg_dots_kernel(int n_light, const int* __restrict__ light, int H, int64_t D
                          ? ld_vec<4>(U + row * HD + static_cast<int64_t>(h0 + hh) * D + fi)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+      // slices past D get no copies: zero this lane's slots for them once
+      // per chunk, so that every edge's slices are read without a select (a
+      // ring slot of an edge past the item's end keeps stale values, but its
+      // dots are reduced separately from every other edge's and never used)
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
+        if (fi >= D) {
+#pragma unroll
+          for (int t = 0; t < kDotsSlots; ++t)
+            dots_ring[(group * kDotsSlots * 2 + t * 2 + q) * 32 + lane] =
+                make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
       // 4 edges per pass (their neighbour chunks copied two passes ahead),
       // and the 16 (edge, head) partial dots are reduced across the warp by a
       // transposed butterfly (each level halves the values a lane carries),
@@ -2575,12 +2589,8 @@ gat_agg_dots_kernel(int n_light, const int* __restrict__ light, int H, int64_t D
           const int t = t0 + e4;
           float4 x[2];
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int64_t fi = f0 + static_cast<int64_t>(lane + q * 32) * 4;
-            const float4 xv =
-                lds_f4(my_ring + static_cast<uint32_t>(((t % kDotsSlots) * 2 + q) * 512));
-            x[q] = (t < cnt && fi < D) ? xv : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
+          for (int q = 0; q < 2; ++q)
+            x[q] = lds_f4(my_ring + static_cast<uint32_t>(((t % kDotsSlots) * 2 + q) * 512));
 #pragma unroll
           for (int hh = 0; hh < kAggHB; ++hh) {
             float d = 0.0f;
