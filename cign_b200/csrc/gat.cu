@@ -2079,8 +2079,11 @@ template <int VPL>
 struct AggCfg {
   static constexpr int kGroups = kThreads / 32;  // one warp per work item
   static constexpr int kTile = 128 * VPL;        // floats per feature tile
-  // dynamic shared memory: per warp, kAggStages slots of one tile
-  static constexpr size_t kSmem = static_cast<size_t>(kGroups) * kAggStages * kTile * 4;
+  // dynamic shared memory: per warp, kAggStages slots of one tile, then per
+  // warp the kAggHB head weights of the current chunk's 32 edges (one float4
+  // per edge, read back as a broadcast)
+  static constexpr size_t kRing = static_cast<size_t>(kGroups) * kAggStages * kTile * 4;
+  static constexpr size_t kSmem = kRing + static_cast<size_t>(kGroups) * 32 * 16;
 };
 
 // Edge weights w[e, h] of the aggregate-first form (edge id e in CSR order),
@@ -2220,6 +2223,8 @@ gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
   // agg_ring[((group * S + s) * VPL + q) * 32 + lane]
   const uint32_t my_ring =
       smem_u32(agg_ring) + static_cast<uint32_t>((group * kAggStages * VPL * 32 + lane) * 16);
+  static_assert(kAggHB == 4, "one float4 of head weights per edge");
+  float4* const wsm = agg_ring + Cfg::kRing / 16 + group * 32;  // this warp's weights
   int64_t item, target;
   int e0, e1;
   bool seg;
@@ -2299,6 +2304,10 @@ gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
           if (lane == hh) gs += t;
         }
       }
+      // lane k's head weights, broadcast to the warp from shared memory (one
+      // 16-byte read per edge instead of kAggHB shuffles)
+      wsm[lane] = make_float4(w[0], w[1], w[2], w[3]);
+      __syncwarp();
       // chunk edge t sits in ring stage t % kAggStages: the loop runs
       // kAggStages edges per pass so that every stage's shared address is a
       // constant
@@ -2312,9 +2321,10 @@ gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
           float4 xv[VPL];
 #pragma unroll
           for (int q = 0; q < VPL; ++q) xv[q] = lds_f4(slot + q * 32 * 16);
+          const float4 wt = wsm[t];
 #pragma unroll
           for (int hh = 0; hh < kAggHB; ++hh) {
-            const float wv = __shfl_sync(kFullMask, w[hh], t);
+            const float wv = vel(wt, hh);
 #pragma unroll
             for (int q = 0; q < VPL; ++q) vfma(acc[hh][q], wv, xv[q]);
           }
@@ -2323,6 +2333,7 @@ gat_agg_kernel(int n_light, const int* __restrict__ light, int H, int64_t D,
         }
       }
       cp_async_wait<0>();  // the ring is reused by the next chunk
+      __syncwarp();        // and the weights
     }
     if (MODE == 1 && blockIdx.y == 0 && lane < kAggHB && h0 + lane < H) gdst[h0 + lane] = gs;
 #pragma unroll
