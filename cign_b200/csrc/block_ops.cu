@@ -467,12 +467,16 @@ silu_add_ln_bwd_kernel(int64_t n, int64_t D, int64_t rpc, const float* __restric
         else vzero(oz);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const float qv = silu_f(vel(pv, j)) + vel(hv, j);
+          // SiLU and its derivative from one sigmoid (the values silu_f and
+          // silu_grad_f give, without evaluating the sigmoid twice)
+          const float x = vel(pv, j);
+          const float sg = sigmoid_f(x);
+          const float qv = x * sg + vel(hv, j);
           const float xhat = (qv - mu) * rs;
           const float dnorm = vel(gv, j) * vel(wv, j);
           const float dq = (rs / Df) * (Df * dnorm - s1 - xhat * s2);
           vel(oz, j) += dq;
-          vel(op, j) = dq * silu_grad_f(vel(pv, j));
+          vel(op, j) = dq * (sg * (1.0f + x * (1.0f - sg)));
           vel(ag[k], j) += vel(op, j);
         }
         st_vec(gz + row * D + d, oz);
