@@ -48,6 +48,13 @@ class _BlockConfig:
 
 
 class _CignBlockFn(torch.autograd.Function):
+    """The block's tensors for the backward are kept as attributes of ctx,
+    not through save_for_backward, so that the backward can drop each group
+    as soon as its last consumer has run (the propagation's hop outputs, for
+    instance, before the GAT backward allocates its workspace) instead of
+    holding all of them until the node returns.  None of them is an output
+    of this node, so no reference cycle arises."""
+
     @staticmethod
     def forward(ctx, H, ln_w, ln_b, gat_w, att_src, att_dst, gat_bias, cn_w, cn_b, gate_w,
                 gate_b, proj_w, proj_b, gamma, cfg):
@@ -64,40 +71,45 @@ class _CignBlockFn(torch.autograd.Function):
             H_norm, C_norm, gate_w, gate_b, proj_w, proj_b, cfg.spmm_plan, cfg.order_set,
             cfg.gate_mode, cfg.keep_g)
         out = _blk.gamma_residual_forward(H, G_feat, gamma, cfg.p, cfg.res_seed)
-        # prop_saved starts with (H_norm, C_norm, gate_w): saved once through it
-        ctx.save_for_backward(H, ln_w, ln_mean, ln_rstd, gat_w, *gat_saved, pre, cn_w, cn_mean,
-                              cn_rstd, G_feat, gamma, *prop_saved)
         ctx.cfg = cfg
-        ctx.n_gat = len(gat_saved)
+        ctx.ln = (H, ln_w, ln_mean, ln_rstd)
+        ctx.gat = (gat_w, gat_saved)
+        ctx.cn = (pre, cn_w, cn_mean, cn_rstd)
+        ctx.res = (G_feat, gamma)
+        ctx.prop = prop_saved  # starts with (H_norm, C_norm, gate_w)
         return out
 
     @staticmethod
     def backward(ctx, g_out):
         cfg = ctx.cfg
-        t = list(ctx.saved_tensors)
-        H, ln_w, ln_mean, ln_rstd, gat_w = t[:5]
-        gat_saved = t[5:5 + ctx.n_gat]
-        pre, cn_w, cn_mean, cn_rstd, G_feat, gamma = t[5 + ctx.n_gat:11 + ctx.n_gat]
-        prop_saved = t[11 + ctx.n_gat:]
-        del t
-        H_norm = prop_saved[0]
         g_out = g_out.to(torch.float32).contiguous()
+        G_feat, gamma = ctx.res
+        del ctx.res
         gG, g_gamma = _blk.gamma_residual_backward(g_out, G_feat, gamma, cfg.p, cfg.res_seed)
         del G_feat
+        prop_saved = ctx.prop
+        del ctx.prop
+        H_norm = prop_saved[0]
         gH_norm, gC_norm, g_gate_w, g_gate_b, g_proj_w, g_proj_b = \
             propagate_gate_pack_proj_backward_raw(prop_saved, gG, cfg.spmm_plan, cfg.order_set,
                                                   cfg.gate_mode)
         del prop_saved, gG
         # the add-LayerNorm's share of grad H_norm, added in place
+        pre, cn_w, cn_mean, cn_rstd = ctx.cn
+        del ctx.cn
         _, g_lin, g_cn_w, g_cn_b, g_gat_bias = _gat.silu_add_ln_backward(
             gC_norm, pre, H_norm, cn_w, cn_mean, cn_rstd, grad_h=gH_norm)
         del gC_norm, pre
         # the GAT context's share, added in place
+        gat_w, gat_saved = ctx.gat
+        del ctx.gat
         _, g_gat_w, g_att_src, g_att_dst = _gat.gat_context_lin_backward_raw(
             H_norm, gat_w, gat_saved, g_lin, cfg.gat_plan, cfg.heads, cfg.n_dst, cfg.att_shape,
             cfg.slope, cfg.attn_drop, cfg.gat_seed, grad_x=gH_norm)
-        del g_lin, gat_saved
+        del g_lin, gat_saved, H_norm
         # grad H = LayerNorm backward + the residual branch's g_out, one pass
+        H, ln_w, ln_mean, ln_rstd = ctx.ln
+        del ctx.ln
         g_H, g_ln_w, g_ln_b = _blk.dropout_ln_backward(gH_norm, H, ln_w, ln_mean, ln_rstd, cfg.p,
                                                        cfg.ln_seed, addend=g_out)
         return (g_H, g_ln_w, g_ln_b, g_gat_w, g_att_src, g_att_dst, g_gat_bias, g_cn_w, g_cn_b,

@@ -2720,11 +2720,12 @@ struct AggLayout {
 };
 AggLayout agg_layout(const cign_gat_plan* pl, int H, int64_t D, int64_t C) {
   AggLayout L;
-  const size_t part = std::max(static_cast<size_t>(pl->rows.n_seg) * D,
-                               static_cast<size_t>(pl->cols.n_seg) * C);
+  // the aggregation kernels' own (kAggSegLen-edge) items: their hub partials
+  const size_t part = std::max(static_cast<size_t>(pl->agg_rows.n_seg) * D,
+                               static_cast<size_t>(pl->agg_cols.n_seg) * C);
   L.partial = 0;
   L.pcol = rnd(part * H * sizeof(float));
-  L.glog = L.pcol + rnd(static_cast<size_t>(pl->cols.n_seg) * H * sizeof(float));
+  L.glog = L.pcol + rnd(static_cast<size_t>(pl->agg_cols.n_seg) * H * sizeof(float));
   L.wts = L.glog + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float));
   L.total = L.wts + rnd(static_cast<size_t>(pl->nnz) * H * sizeof(float)) + 256;
   return L;
