@@ -188,3 +188,34 @@ def test_step_roofline_model_at_cfg2():
     assert abs(r["t_roof_ms"] - round(manual, 4)) < 1e-3
     assert abs(r["epoch_frac"] - round(manual / 10.0, 4)) < 1e-4
     assert r["hbm_bound_ms"] <= r["t_roof_ms"] <= r["hbm_bound_ms"] + r["tensor_bound_ms"]
+
+
+def test_block_node_gate():
+    """The whole-block node takes CUDA fp32 inputs on an unpartitioned GAT
+    graph only; CPU tensors, a partitioned graph (an object with a halo
+    exchange) or a non-production pack switch fall back to the op-by-op
+    block."""
+    from cign_b200.block_node import block_node_applies
+    from cign_b200.model_cign import GraphCliffordBlock
+
+    block = GraphCliffordBlock(64, (1, 2, 3), gat_heads=2)
+    H = torch.zeros(10, 64)
+    triple = ((None, None), (None, None), None)
+    assert not block_node_applies(block, H, object(), triple)  # CPU tensor
+
+    class _Partitioned:
+        halo = None
+
+    class _FakeCuda:
+        is_cuda = True
+        dtype = torch.float32
+
+        def dim(self):
+            return 2
+
+        def size(self, i):
+            return (10, 64)[i]
+
+    assert not block_node_applies(block, _FakeCuda(), object(), _Partitioned())
+    block.interaction_mode = "old"
+    assert not block_node_applies(block, _FakeCuda(), object(), triple)
