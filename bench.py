@@ -400,14 +400,16 @@ def kernel_breakdown(cfg, op, gat_graph, nnz, nnz_g, device, pack_proj_in_step=F
     gplan = gat_plan_for(rp, c, r, cp, perm)
     x = torch.randn(N, D, device=device, generator=g)
     a = torch.randn(N, H, device=device, generator=g)
-    fwd = lambda: collapsed_gat.gat_agg_forward_raw(gplan, a, a, x, H, 0.2, cfg.gat_dropout, 7)
+    # the model's calls: the forward keeps the edge weights for the backward
+    fwd = lambda: collapsed_gat.gat_agg_forward_keep_raw(gplan, a, a, x, H, 0.2,  # noqa: E731
+                                                         cfg.gat_dropout, 7)
     t_gat_fwd = time_launches(fwd, 10, stream)
-    z, emax, esum = fwd()
+    z, emax, esum, wts = fwd()
     del z
     gz = torch.randn(N, H * D, device=device, generator=g)
     gpre = torch.randn(N, D, device=device, generator=g)
     t_gat_bwd = time_launches(lambda: collapsed_gat.gat_agg_backward_raw(
-        gplan, a, a, x, emax, esum, gz, gpre, 0.2, cfg.gat_dropout, 7), 10, stream)
+        gplan, a, a, x, emax, esum, gz, gpre, 0.2, cfg.gat_dropout, 7, wts=wts), 10, stream)
     del gz, gpre
     Hn = torch.randn(N, D, device=device, generator=g)
     Cn = torch.randn(N, D, device=device, generator=g)

@@ -117,6 +117,11 @@ SIGNATURES = {
                                  _P, _P, _P, _P, c_size_t, _P]),
     "cign_gat_agg_bwd": (c_int, [_P, c_int32, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P,
                                  c_float, c_float, c_uint64, _P, _P, _P, _P, _P, c_size_t, _P]),
+    "cign_gat_agg_fwd_w": (c_int, [_P, c_int32, c_int64, _P, _P, _P, c_float, c_float, c_uint64,
+                                   _P, _P, _P, _P, _P, _P, c_size_t, _P]),
+    "cign_gat_agg_bwd_w": (c_int, [_P, c_int32, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P,
+                                   _P, c_float, c_float, c_uint64, _P, _P, _P, _P, _P, c_size_t,
+                                   _P]),
     "cign_attn_logits_fwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P]),
     "cign_attn_logits_bwd_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
     "cign_attn_logits_bwd": (c_int, [c_int64, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,

@@ -197,9 +197,35 @@ def gat_agg_forward_raw(plan, attn_row, attn_col, x, heads, negative_slope, attn
     return z, emax, esum
 
 
+def gat_agg_forward_keep_raw(plan, attn_row, attn_col, x, heads, negative_slope, attn_drop,
+                             seed):
+    """gat_agg_forward_raw on fp32 x that also returns the edge weights
+    [nnz, H] (cign_gat_agg_fwd_w): (z, emax, esum, wts), wts to be handed to
+    gat_agg_backward_raw so that the backward does not form them again."""
+    lib = ensure_collapsed_gat_loaded()
+    D = int(x.size(1))
+    n = int(plan.n)
+    H = int(heads)
+    z = torch.empty((n, H, D), dtype=torch.float32, device=x.device)
+    emax = torch.empty((n, H), dtype=torch.float32, device=x.device)
+    esum = torch.empty_like(emax)
+    wts = torch.empty((max(int(plan.nnz), 1), H), dtype=torch.float32, device=x.device)
+    ws = _lib.workspace(lib.cign_gat_agg_workspace_bytes(plan.handle, H, D, D), x.device)
+    with _lib.DeviceGuard(x.device):
+        rc = lib.cign_gat_agg_fwd_w(plan.handle, H, D, _lib.ptr(attn_row), _lib.ptr(attn_col),
+                                    _lib.ptr(x), float(negative_slope), float(attn_drop),
+                                    *_lib.seed_args(seed), _lib.ptr(z), _lib.ptr(emax),
+                                    _lib.ptr(esum), _lib.ptr(wts), _lib.ptr(ws), ws.numel(),
+                                    _lib.stream_of(x))
+    _lib.check(rc, "cign_gat_agg_fwd_w")
+    return z, emax, esum, wts
+
+
 def gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z, grad_pre, negative_slope,
-                         attn_drop, seed):
-    """Returns (grad_feat [N,H,C], grad_attn_row [N,H], grad_attn_col [N,H])."""
+                         attn_drop, seed, wts=None):
+    """Returns (grad_feat [N,H,C], grad_attn_row [N,H], grad_attn_col [N,H]).
+    With wts (the forward's edge weights, gat_agg_forward_keep_raw) the
+    backward reads them instead of forming them again."""
     lib = ensure_collapsed_gat_loaded()
     n_cols, D = (int(s) for s in x.shape)
     n = int(plan.n)
@@ -211,12 +237,24 @@ def gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z, grad_p
     gcol = torch.empty((n_cols, H), dtype=torch.float32, device=dev)
     ws = _lib.workspace(lib.cign_gat_agg_workspace_bytes(plan.handle, H, D, C), dev)
     with _lib.DeviceGuard(dev):
-        rc = lib.cign_gat_agg_bwd(plan.handle, H, D, C, _lib.ptr(attn_row), _lib.ptr(attn_col),
-                                  _lib.ptr(x), _lib.ptr(emax), _lib.ptr(esum), _lib.ptr(grad_z),
-                                  _lib.ptr(grad_pre), float(negative_slope), float(attn_drop),
-                                  *_lib.seed_args(seed), _lib.ptr(gfeat), _lib.ptr(grow),
-                                  _lib.ptr(gcol), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
-    _lib.check(rc, "cign_gat_agg_bwd")
+        if wts is None:
+            rc = lib.cign_gat_agg_bwd(plan.handle, H, D, C, _lib.ptr(attn_row),
+                                      _lib.ptr(attn_col), _lib.ptr(x), _lib.ptr(emax),
+                                      _lib.ptr(esum), _lib.ptr(grad_z), _lib.ptr(grad_pre),
+                                      float(negative_slope), float(attn_drop),
+                                      *_lib.seed_args(seed), _lib.ptr(gfeat), _lib.ptr(grow),
+                                      _lib.ptr(gcol), _lib.ptr(ws), ws.numel(), _lib.stream_of(x))
+            name = "cign_gat_agg_bwd"
+        else:
+            rc = lib.cign_gat_agg_bwd_w(plan.handle, H, D, C, _lib.ptr(attn_row),
+                                        _lib.ptr(attn_col), _lib.ptr(x), _lib.ptr(emax),
+                                        _lib.ptr(esum), _lib.ptr(grad_z), _lib.ptr(grad_pre),
+                                        _lib.ptr(wts), float(negative_slope), float(attn_drop),
+                                        *_lib.seed_args(seed), _lib.ptr(gfeat), _lib.ptr(grow),
+                                        _lib.ptr(gcol), _lib.ptr(ws), ws.numel(),
+                                        _lib.stream_of(x))
+            name = "cign_gat_agg_bwd_w"
+    _lib.check(rc, name)
     return gfeat, grow, gcol
 
 
@@ -459,12 +497,12 @@ def gat_context_lin_forward_raw(x, weight, att_src, att_dst, plan, heads, n_dst,
     attn_col = alpha[:, :H].contiguous()
     attn_row = alpha[:n_dst, H:].contiguous()
     n, D = int(plan.n), int(x.size(1))
-    z, emax, esum = gat_agg_forward_raw(plan, attn_row, attn_col, x, H, negative_slope,
-                                        attn_drop, seed)
+    z, emax, esum, wts = gat_agg_forward_keep_raw(plan, attn_row, attn_col, x, H, negative_slope,
+                                                  attn_drop, seed)
     M = _head_projection(weight, H)
     lin = z.view(n, H * D).mm(M)
     del z
-    return lin, (attn_row, attn_col, emax, esum, V, A)
+    return lin, (attn_row, attn_col, emax, esum, V, A, wts)
 
 
 def gat_context_lin_backward_raw(x, weight, saved, g_lin, plan, heads, n_dst, att_shape,
@@ -473,7 +511,7 @@ def gat_context_lin_backward_raw(x, weight, saved, g_lin, plan, heads, n_dst, at
     With grad_x given ([N_src, D], x's gradient from its other consumers) the
     GAT's share is added into it in place (beta = 1 GEMM, then the logit
     term), with no separate add."""
-    attn_row, attn_col, emax, esum, V, A = saved
+    attn_row, attn_col, emax, esum, V, A, wts = saved
     H = int(heads)
     n_src, D = (int(s) for s in x.shape)
     HC = int(weight.size(0))
@@ -482,7 +520,7 @@ def gat_context_lin_backward_raw(x, weight, saved, g_lin, plan, heads, n_dst, at
     M = _head_projection(weight, H)
     grad_z = g_pre.mm(M.t())                                                        # [N, H*D]
     gfeat, grow, gcol = gat_agg_backward_raw(plan, attn_row, attn_col, x, emax, esum, grad_z,
-                                             g_pre, negative_slope, attn_drop, seed)
+                                             g_pre, negative_slope, attn_drop, seed, wts=wts)
     del grad_z
     gfeat2 = gfeat.view(n_src, HC)
     if grad_x is None:

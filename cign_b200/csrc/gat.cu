@@ -2986,11 +2986,14 @@ size_t cign_gat_agg_workspace_bytes(const cign_gat_plan* pl, int32_t heads, int6
   return agg_layout(pl, heads, dim, channels).total;
 }
 
-int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const float* attn_row,
-                     const float* attn_col, const float* x, float negative_slope, float attn_drop,
-                     uint64_t seed_value, const uint64_t* seed_ptr,
-                     float* z, float* edge_max, float* edge_sum, void* ws,
-                     size_t ws_bytes, cign_stream_t stream) {
+// Body of cign_gat_agg_fwd / cign_gat_agg_fwd_w: the edge weights go to
+// wts_out when it is given (kept by the caller for the backward), else to
+// the workspace.
+static int gat_agg_fwd_impl(const cign_gat_plan* pl, int32_t heads, int64_t dim,
+                            const float* attn_row, const float* attn_col, const float* x,
+                            float negative_slope, float attn_drop, uint64_t seed_value,
+                            const uint64_t* seed_ptr, float* z, float* edge_max, float* edge_sum,
+                            float* wts_out, void* ws, size_t ws_bytes, cign_stream_t stream) {
   const Seed seed{seed_value, seed_ptr};
   int rc = check_agg(pl, heads, dim, {x, z, ws}, "gat_agg_fwd");
   if (rc) return rc;
@@ -3004,7 +3007,8 @@ int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const 
   if (pl->n == 0) return CIGN_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + L.partial);
-  float* wts = reinterpret_cast<float*>(static_cast<char*>(ws) + L.wts);
+  float* wts = wts_out != nullptr ? wts_out
+                                  : reinterpret_cast<float*>(static_cast<char*>(ws) + L.wts);
   rc = launch_hub_stats(pl, heads, attn_row, attn_col, negative_slope, edge_max, edge_sum, s);
   if (rc) return rc;
   rc = launch_edge_weights<true>(pl, heads, attn_row, attn_col, edge_max, edge_sum,
@@ -3015,6 +3019,27 @@ int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const 
                             partial, nullptr, nullptr, nullptr, s);
   return launch_agg<2, 0>(pl, pl->agg_rows, heads, dim, pl->rowptr, pl->col, nullptr, wts, x, z,
                           partial, nullptr, nullptr, nullptr, s);
+}
+
+int cign_gat_agg_fwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, const float* attn_row,
+                     const float* attn_col, const float* x, float negative_slope, float attn_drop,
+                     uint64_t seed_value, const uint64_t* seed_ptr,
+                     float* z, float* edge_max, float* edge_sum, void* ws,
+                     size_t ws_bytes, cign_stream_t stream) {
+  return gat_agg_fwd_impl(pl, heads, dim, attn_row, attn_col, x, negative_slope, attn_drop,
+                          seed_value, seed_ptr, z, edge_max, edge_sum, nullptr, ws, ws_bytes,
+                          stream);
+}
+
+int cign_gat_agg_fwd_w(const cign_gat_plan* pl, int32_t heads, int64_t dim,
+                       const float* attn_row, const float* attn_col, const float* x,
+                       float negative_slope, float attn_drop, uint64_t seed_value,
+                       const uint64_t* seed_ptr, float* z, float* edge_max, float* edge_sum,
+                       float* wts, void* ws, size_t ws_bytes, cign_stream_t stream) {
+  CIGN_REQUIRE(wts != nullptr || pl == nullptr || pl->nnz == 0, CIGN_ERR_NULL_POINTER,
+               "gat_agg_fwd_w: NULL edge-weight buffer");
+  return gat_agg_fwd_impl(pl, heads, dim, attn_row, attn_col, x, negative_slope, attn_drop,
+                          seed_value, seed_ptr, z, edge_max, edge_sum, wts, ws, ws_bytes, stream);
 }
 
 int cign_gat_agg_fwd_bf16(const cign_gat_plan* pl, int32_t heads, int64_t dim,
@@ -3056,12 +3081,16 @@ int cign_gat_agg_fwd_bf16(const cign_gat_plan* pl, int32_t heads, int64_t dim,
   return launch_seg_combine(sl, heads, dim, partial, nullptr, z, nullptr, s);
 }
 
-int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_t channels,
-                     const float* attn_row, const float* attn_col, const float* x,
-                     const float* edge_max, const float* edge_sum, const float* grad_z,
-                     const float* grad_pre, float negative_slope, float attn_drop, uint64_t seed_value, const uint64_t* seed_ptr,
-                     float* grad_feat, float* grad_attn_row, float* grad_attn_col, void* ws,
-                     size_t ws_bytes, cign_stream_t stream) {
+// Body of cign_gat_agg_bwd / cign_gat_agg_bwd_w: with wts_in (the forward's
+// edge weights) K2 reads them instead of forming them again.
+static int gat_agg_bwd_impl(const cign_gat_plan* pl, int32_t heads, int64_t dim,
+                            int64_t channels, const float* attn_row, const float* attn_col,
+                            const float* x, const float* edge_max, const float* edge_sum,
+                            const float* grad_z, const float* grad_pre, float negative_slope,
+                            float attn_drop, uint64_t seed_value, const uint64_t* seed_ptr,
+                            const float* wts_in, float* grad_feat, float* grad_attn_row,
+                            float* grad_attn_col, void* ws, size_t ws_bytes,
+                            cign_stream_t stream) {
   const Seed seed{seed_value, seed_ptr};
   int rc = check_agg(pl, heads, dim, {x, grad_z, ws}, "gat_agg_bwd");
   if (rc) return rc;
@@ -3109,17 +3138,47 @@ int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_
                            s);
   if (rc) return rc;
   // K2: grad_feat[j,h,:] = sum_i w g_pre[i,:] / H and grad_attn_col (columns),
-  // with the edge weights formed once per edge from the forward's statistics
-  float* wts = reinterpret_cast<float*>(w + L.wts);
-  rc = launch_edge_weights<false>(pl, heads, attn_row, attn_col, const_cast<float*>(edge_max),
-                                  const_cast<float*>(edge_sum), negative_slope, attn_drop, seed,
-                                  wts, s);
-  if (rc) return rc;
+  // with the forward's edge weights or ones formed again from its statistics
+  const float* wts = wts_in;
+  if (wts == nullptr) {
+    float* wk = reinterpret_cast<float*>(w + L.wts);
+    rc = launch_edge_weights<false>(pl, heads, attn_row, attn_col, const_cast<float*>(edge_max),
+                                    const_cast<float*>(edge_sum), negative_slope, attn_drop, seed,
+                                    wk, s);
+    if (rc) return rc;
+    wts = wk;
+  }
   if (channels <= 128)
     return launch_agg<1, 1>(pl, pl->agg_cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
                             grad_pre, grad_feat, partial, glog, grad_attn_col, pcol, s);
   return launch_agg<2, 1>(pl, pl->agg_cols, heads, channels, pl->colptr, pl->row, pl->perm, wts,
                           grad_pre, grad_feat, partial, glog, grad_attn_col, pcol, s);
+}
+
+int cign_gat_agg_bwd(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_t channels,
+                     const float* attn_row, const float* attn_col, const float* x,
+                     const float* edge_max, const float* edge_sum, const float* grad_z,
+                     const float* grad_pre, float negative_slope, float attn_drop,
+                     uint64_t seed_value, const uint64_t* seed_ptr, float* grad_feat,
+                     float* grad_attn_row, float* grad_attn_col, void* ws, size_t ws_bytes,
+                     cign_stream_t stream) {
+  return gat_agg_bwd_impl(pl, heads, dim, channels, attn_row, attn_col, x, edge_max, edge_sum,
+                          grad_z, grad_pre, negative_slope, attn_drop, seed_value, seed_ptr,
+                          nullptr, grad_feat, grad_attn_row, grad_attn_col, ws, ws_bytes, stream);
+}
+
+int cign_gat_agg_bwd_w(const cign_gat_plan* pl, int32_t heads, int64_t dim, int64_t channels,
+                       const float* attn_row, const float* attn_col, const float* x,
+                       const float* edge_max, const float* edge_sum, const float* grad_z,
+                       const float* grad_pre, const float* wts, float negative_slope,
+                       float attn_drop, uint64_t seed_value, const uint64_t* seed_ptr,
+                       float* grad_feat, float* grad_attn_row, float* grad_attn_col, void* ws,
+                       size_t ws_bytes, cign_stream_t stream) {
+  CIGN_REQUIRE(wts != nullptr || pl == nullptr || pl->nnz == 0, CIGN_ERR_NULL_POINTER,
+               "gat_agg_bwd_w: NULL edge-weight buffer");
+  return gat_agg_bwd_impl(pl, heads, dim, channels, attn_row, attn_col, x, edge_max, edge_sum,
+                          grad_z, grad_pre, negative_slope, attn_drop, seed_value, seed_ptr, wts,
+                          grad_feat, grad_attn_row, grad_attn_col, ws, ws_bytes, stream);
 }
 
 }  // extern "C"

@@ -285,6 +285,27 @@ CIGN_API int cign_gat_agg_bwd(const cign_gat_plan* plan, int32_t heads, int64_t 
                               float* grad_attn_row, float* grad_attn_col, void* ws,
                               size_t ws_bytes, cign_stream_t stream);
 
+/* cign_gat_agg_fwd / cign_gat_agg_bwd with the edge weights [nnz, H] (CSR
+ * edge order) kept between them: the forward writes them to `wts` and the
+ * backward reads them there instead of forming them again from
+ * edge_max / edge_sum (the same values, bit for bit).  The caller keeps
+ * `wts` (16-byte aligned, nnz * H floats) alive from the forward to the
+ * backward of the same call; workspace as cign_gat_agg_fwd / _bwd. */
+CIGN_API int cign_gat_agg_fwd_w(const cign_gat_plan* plan, int32_t heads, int64_t dim,
+                                const float* attn_row, const float* attn_col, const float* x,
+                                float negative_slope, float attn_drop, uint64_t seed,
+                                const uint64_t* seed_ptr, float* z, float* edge_max,
+                                float* edge_sum, float* wts, void* ws, size_t ws_bytes,
+                                cign_stream_t stream);
+CIGN_API int cign_gat_agg_bwd_w(const cign_gat_plan* plan, int32_t heads, int64_t dim,
+                                int64_t channels, const float* attn_row, const float* attn_col,
+                                const float* x, const float* edge_max, const float* edge_sum,
+                                const float* grad_z, const float* grad_pre, const float* wts,
+                                float negative_slope, float attn_drop, uint64_t seed,
+                                const uint64_t* seed_ptr, float* grad_feat,
+                                float* grad_attn_row, float* grad_attn_col, void* ws,
+                                size_t ws_bytes, cign_stream_t stream);
+
 /* ------------------------------------------------------------ side ops
  * alpha_src[n,h] = sum_c x[n,h,c] att_src[h,c];  same for dst.
  * Replaces attention_forward_cuda (fused_gat_sideops_cuda.cu:243-260). */

@@ -94,3 +94,26 @@ def test_agg_gat_deterministic(cuda):
     z1, _, _ = gat_agg_forward_raw(plan, a, a, x, 4, 0.2, 0.4, 5)
     z2, _, _ = gat_agg_forward_raw(plan, a, a, x, 4, 0.2, 0.4, 5)
     assert torch.equal(z1, z2)
+
+
+def test_agg_gat_kept_edge_weights_equal_recomputed(cuda):
+    """The forward's edge weights handed to the backward (cign_gat_agg_fwd_w /
+    _bwd_w) give the backward of the recomputing entry points bit for bit,
+    with attention dropout and hub rows and columns."""
+    from cign_b200.collapsed_gat import gat_agg_backward_raw, gat_agg_forward_keep_raw
+    n, H, D = 1500, 4, 128
+    edge = prepare_gat_edge_index(synth.powerlaw_graph(n, 12000, seed=21), n)
+    plan, _, _ = _plan(edge, n, cuda)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn(n, D, device=cuda, generator=g)
+    a_row = torch.randn(n, H, device=cuda, generator=g)
+    a_col = torch.randn(n, H, device=cuda, generator=g)
+    z1, m1, s1 = gat_agg_forward_raw(plan, a_row, a_col, x, H, 0.2, 0.4, 11)
+    z2, m2, s2, wts = gat_agg_forward_keep_raw(plan, a_row, a_col, x, H, 0.2, 0.4, 11)
+    assert torch.equal(z1, z2) and torch.equal(m1, m2) and torch.equal(s1, s2)
+    gz = torch.randn(n, H * D, device=cuda, generator=g)
+    gp = torch.randn(n, D, device=cuda, generator=g)
+    ref = gat_agg_backward_raw(plan, a_row, a_col, x, m1, s1, gz, gp, 0.2, 0.4, 11)
+    got = gat_agg_backward_raw(plan, a_row, a_col, x, m1, s1, gz, gp, 0.2, 0.4, 11, wts=wts)
+    for r, o in zip(ref, got):
+        assert torch.equal(r, o)
