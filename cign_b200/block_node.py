@@ -53,7 +53,11 @@ class _CignBlockFn(torch.autograd.Function):
     as soon as its last consumer has run (the propagation's hop outputs, for
     instance, before the GAT backward allocates its workspace) instead of
     holding all of them until the node returns.  None of them is an output
-    of this node, so no reference cycle arises."""
+    of this node, so no reference cycle arises.  Unlike save_for_backward,
+    this does not detect an in-place change of the block input or of a
+    parameter between the forward and the backward (a training step makes
+    none: the optimizer runs after the backward); such a change would give
+    wrong gradients instead of an error."""
 
     @staticmethod
     def forward(ctx, H, ln_w, ln_b, gat_w, att_src, att_dst, gat_bias, cn_w, cn_b, gate_w,
